@@ -1,0 +1,217 @@
+/*
+ * b2.h -- C ABI of libxdna_b200.so, the sm_100a kernel library behind the
+ * `xdna` PyTorch device of this package.
+ *
+ * Plain pointers and sizes only: no torch types, no CUDA types.  Streams are
+ * passed as `void*` (a cudaStream_t; NULL is the legacy default stream).  All
+ * pointers except the explicitly host-side ones are device (HBM) pointers.
+ *
+ * Error convention (mirrors the reference's C shims, which return NULL or
+ * nonzero and keep the message in a thread-local string --
+ * xdna_train/_vendor/xrt_shim/xrt_shim.h:2-3, xrt_shim.cpp:235-238):
+ * every call returns B2_OK (0) or a nonzero b2_status; the message of the
+ * last failure on the calling thread is b2_last_error().  Launches are
+ * asynchronous: a kernel that detects a problem on the device (a pipeline
+ * wait that ran out of its time limit) records a code in a per-device status
+ * word read by b2_device_status().
+ *
+ * Layouts (the reference's conv3x3w host layouts, xdna_train/_designs/
+ * conv3x3w_host.py:15-47, without the NPU's group/halo duplication):
+ *   padded-grid rows  : X_rows[B*(H+2)*(W+2)][chunks*64] bf16.  Pixel (b,y,x)
+ *                       is row (b*(H+2)+y+1)*(W+2)+x+1; the border rows and
+ *                       the channels >= C are zero.  Output pixel (b,y,x) of a
+ *                       3x3/s1/p1 conv is row p=(b*(H+2)+y)*(W+2)+x and its tap
+ *                       (dy,dx) reads row p + dy*(W+2) + dx.
+ *   conv weights      : Wk[Cout][chunks*9*64] bf16 with K order
+ *                       (chunk, dy, dx, c) (conv3x3w_host.py:66-78); the
+ *                       dgrad copy reads w'[ci][co][dy][dx] = w[co][ci][2-dy][2-dx]
+ *                       (xdna_train/_native/conv_pack.cpp:470-473).
+ */
+#ifndef XDNA_B200_B2_H
+#define XDNA_B200_B2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int b2_status;
+
+enum {
+  B2_OK = 0,
+  B2_ERR_INVALID = 1,      /* bad argument (shape, alignment, null pointer) */
+  B2_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+  B2_ERR_UNSUPPORTED = 3,  /* valid request this library does not serve */
+  B2_ERR_TIMEOUT = 4,      /* device-side wait ran out of its limit */
+  B2_ERR_WORKSPACE = 5     /* workspace too small */
+};
+
+/* dtype codes used where a pointer can hold more than one element type */
+enum { B2_BF16 = 0, B2_F32 = 1 };
+
+/* ---- runtime ------------------------------------------------------------ */
+
+/* Thread-local message of the last failed call on this thread ("" if none).
+ * Replaces shim_last_error() (xdna_train/_vendor/xrt_shim/xrt_shim.h:157). */
+const char* b2_last_error(void);
+
+/* Library ABI version (increments on any signature change). */
+int b2_abi_version(void);
+
+/* Reads and clears the device-side status word of `device` (0 = no error,
+ * else a b2_status recorded by a kernel).  Synchronizes the device.
+ * Replaces the dispatch-deadline check of shim_run_wait
+ * (xdna_train/_vendor/xrt_shim/xrt_shim.cpp:174-233). */
+b2_status b2_device_status(int device, int* code);
+
+/* ---- layout packers (replace xdna_train/_native/conv_pack.cpp) ---------- */
+
+/* Strided bf16 activation x (element strides sn, sc, sh, sw; NCHW and NHWC
+ * are both strided views) -> padded-grid rows [B*(H+2)*(W+2)][chunks*64].
+ * Writes every row (borders and padded channels zero), so `rows` needs no
+ * prior memset.  chunks >= ceil(C/64).
+ * Replaces xdna_conv3x3w_pack_input_bf16 / _strips_range_bf16
+ * (conv_pack.cpp:352-392, 632-700). */
+b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh,
+                            int64_t sw, int B, int C, int H, int W, int chunks,
+                            void* rows, void* stream);
+
+/* OIHW bf16 weight [Cout][Cin][3][3] -> Wk[Cout][chunks*9*64], K order
+ * (chunk, dy, dx, c), zero for c >= Cin.  chunks >= ceil(Cin/64).
+ * Replaces the K ordering of xdna_conv3x3w_pack_weights_bfp16
+ * (conv_pack.cpp:398-443) without the NPU's BFP16 encode. */
+b2_status b2_pack_weight_fwd_bf16(const void* w, int Cout, int Cin, int chunks,
+                                  void* wk, void* stream);
+
+/* dgrad weights: Wk'[Cin][chunks_o*9*64] with w'[ci][co][dy][dx] =
+ * w[co][ci][2-dy][2-dx], chunks_o >= ceil(Cout/64).
+ * Replaces xdna_conv3x3w_pack_weights_dx_bfp16 (conv_pack.cpp:474-519). */
+b2_status b2_pack_weight_dgrad_bf16(const void* w, int Cout, int Cin,
+                                    int chunks_o, void* wk, void* stream);
+
+/* Dense bf16 NCHW [B][C][H*W] <-> NHWC [B][H*W][C] transposes.
+ * Replace xdna_pack_conv3x3_halo_padded_bf16 / xdna_yxbc_to_channels_last_bf16
+ * (conv_pack.cpp:19-112) for the channels-last boundary. */
+b2_status b2_nchw_to_nhwc_bf16(const void* src, void* dst, int B, int C,
+                               int HW, void* stream);
+b2_status b2_nhwc_to_nchw_bf16(const void* src, void* dst, int B, int C,
+                               int HW, void* stream);
+
+/* ---- 3x3 / stride 1 / pad 1 convolution (tcgen05 implicit GEMM) ---------- */
+
+/* y[b][co][y][x] (strided bf16, element strides ysn..ysw) =
+ *   bias[co] + sum_{ci,dy,dx} x[b][ci][y+dy-1][x+dx-1] * w[co][ci][dy][dx]
+ * from padded-grid rows of x (chunks = ceil(Cin/64)) and Wk from
+ * b2_pack_weight_fwd_bf16.  bias may be NULL (bf16 [Cout]); relu != 0 clamps
+ * at zero.  FP32 accumulation in tensor memory, one bf16 rounding.
+ * Replaces XdnaConv3x3wRuntime::run (xdna_train/_native/
+ * torch_xdna_device.cpp:2317-2483) and the unpack of conv_pack.cpp:447-466. */
+b2_status b2_conv3x3_fwd(const void* x_rows, const void* wk, const void* bias,
+                         void* y, int64_t ysn, int64_t ysc, int64_t ysh,
+                         int64_t ysw, int B, int Cin, int H, int W, int Cout,
+                         int relu, void* stream);
+
+/* dgrad: dx = conv3x3(dy, w') from padded-grid rows of dy (chunks =
+ * ceil(Cout/64)) and Wk' from b2_pack_weight_dgrad_bf16; dx strided bf16.
+ * Replaces XdnaConv3x3wRuntime::input_grad (torch_xdna_device.cpp:2515-2522). */
+b2_status b2_conv3x3_dgrad(const void* dy_rows, const void* wk_dgrad, void* dx,
+                           int64_t sn, int64_t sc, int64_t sh, int64_t sw,
+                           int B, int Cout, int H, int W, int Cin, void* stream);
+
+/* Workspace bytes b2_conv3x3_wgrad needs for this shape (fp32 split-K
+ * partial sums; 0 is never returned). */
+size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout);
+
+/* wgrad: dw[co][ci][dy][dx] = sum_{b,y,x} dy[b][co][y][x] *
+ * x[b][ci][y+dy-1][x+dx-1], from the padded-grid rows of dy (chunks_o =
+ * ceil(Cout/64)) and of x (chunks_i = ceil(Cin/64)), the same buffers the
+ * forward and dgrad read.  dw is OIHW, dtype B2_BF16 or B2_F32.  FP32
+ * accumulation; the split-K reduction is deterministic (fixed order).
+ * Replaces XdnaConv3x3wDwRuntime::compute (torch_xdna_device.cpp:2683-2751). */
+b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw,
+                           int dw_dtype, int B, int Cin, int H, int W, int Cout,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* ---- dense GEMM (tcgen05) ------------------------------------------------ */
+
+/* For each batch index i < batch:
+ *   D_i[m][n] = alpha * sum_k opA(A_i)[m][k] * opB(B_i)[k][n] + beta * C_i[m][n]
+ * A, B, D bf16 row-major with leading dims lda, ldb, ldd and batch strides;
+ * opA(A) = A ([M][K]) if transA == 0 else A^T (A stored [K][M]); likewise B
+ * ([K][N], or [N][K] when transB).  C (may be NULL when beta == 0) is read
+ * through element strides c_sm, c_sn, c_sb (0 broadcasts, e.g. a bias row)
+ * with dtype c_dtype.  lda/ldb (in elements) must be multiples of 8 and the
+ * operand base addresses 16-byte aligned (B2_ERR_UNSUPPORTED otherwise).
+ * Replaces XdnaGemmRuntime (torch_xdna_device.cpp:1320-1458), which served
+ * three fixed shapes; this serves any shape. */
+b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
+                       const void* A, int64_t lda, int64_t strideA,
+                       const void* B, int64_t ldb, int64_t strideB, float beta,
+                       const void* C, int c_dtype, int64_t c_sm, int64_t c_sn,
+                       int64_t c_sb, void* D, int64_t ldd, int64_t strideD,
+                       int batch, void* stream);
+
+/* ---- multi-tensor fused Adam / AdamW ---------------------------------- */
+
+/* One parameter tensor of a fused step (device pointers; host struct). */
+typedef struct b2_adam_tensor {
+  void* param;           /* param_dtype */
+  const void* grad;      /* param_dtype */
+  void* exp_avg;         /* state_dtype */
+  void* exp_avg_sq;      /* state_dtype */
+  void* max_exp_avg_sq;  /* state_dtype, NULL unless amsgrad */
+  const float* step;     /* device fp32 scalar (already incremented) */
+  int64_t numel;
+} b2_adam_tensor;
+
+typedef struct b2_adam_hparams {
+  double lr, beta1, beta2, weight_decay, eps;
+  int amsgrad, maximize, adamw;
+  int param_dtype;        /* B2_BF16 or B2_F32 */
+  int state_dtype;        /* B2_BF16 or B2_F32 */
+  const float* lr_tensor; /* device fp32 scalar overriding lr, or NULL */
+  const float* grad_scale;/* device fp32 scalar, or NULL */
+  const float* found_inf; /* device fp32 scalar, or NULL (nonzero skips) */
+} b2_adam_hparams;
+
+/* In-place fused Adam/AdamW over n tensors, one pass per element in FP32
+ * (opmath) arithmetic.  Replaces the reference's CPU _fused_adam_ reached
+ * through the boxed fallback (torch_xdna_device.cpp:5124-5260). */
+b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n,
+                        const b2_adam_hparams* hp, void* stream);
+
+/* ---- fused region kernels (replace xdna_train/_native/region_kernels.cpp) */
+
+/* *out (device double) = sum (a[i]-b[i])^2 over n bf16 elements.
+ * region_kernels.cpp:52-71 */
+b2_status b2_region_sqdiff_sum_bf16(const void* a, const void* b, int64_t n,
+                                    double* out, void* stream);
+/* r = relu(a), NaN kept.  region_kernels.cpp:74-87 */
+b2_status b2_region_relu_bf16(const void* a, void* r, int64_t n, void* stream);
+/* r = relu(a); p = 2x2/2 max-pool of r over [planes][H][W].
+ * region_kernels.cpp:150-184 */
+b2_status b2_region_relu_maxpool2_bf16(const void* a, void* r, void* p,
+                                       int64_t planes, int64_t H, int64_t W,
+                                       void* stream);
+/* out = bf16(base + scale*(a-b)), base may be NULL.  region_kernels.cpp:187-205 */
+b2_status b2_region_addtap_bf16(const void* base, const void* a, const void* b,
+                                void* out, int64_t n, float scale, void* stream);
+/* out = (r <= 0) ? 0 : bf16(base + scale*(a-b)); base, a/b may be NULL.
+ * region_kernels.cpp:212-246 */
+b2_status b2_region_relu_bwd_bf16(const void* r, const void* base,
+                                  const void* a, const void* b, void* out,
+                                  int64_t n, float scale, void* stream);
+/* out[argmax of each 2x2 window of x] = g, 0 elsewhere.
+ * region_kernels.cpp:248-307 */
+b2_status b2_region_maxpool2_bwd_bf16(const void* x, const void* g, void* out,
+                                      int64_t planes, int64_t H, int64_t W,
+                                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XDNA_B200_B2_H */

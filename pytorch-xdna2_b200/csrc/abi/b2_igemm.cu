@@ -1,0 +1,701 @@
+// tcgen05 implicit-GEMM kernels for sm_100a: 3x3/s1/p1 convolution forward
+// and dgrad, convolution wgrad, and dense (batched) bf16 GEMM.
+//
+// One persistent, warp-specialized kernel template serves all of them:
+//   warp 0      TMA producer: fills a STAGES-deep ring of shared-memory
+//               operand tiles (A: 128 x 64, B: BN x 64 bf16, 128-byte swizzle)
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16)
+//               into a double-buffered fp32 accumulator in tensor memory
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator, fused bias / ReLU /
+//               alpha-beta, bf16 rounding and the store in the caller's layout
+// The epilogue of tile i overlaps the mainloop of tile i+1.
+//
+// The convolution is the reference's conv3x3w formulation
+// (xdna_train/_designs/conv3x3w.py:1-38): output rows are padded-grid pixels,
+// so tap (dy,dx) of output row p is input row p + dy*(W+2) + dx and the im2col
+// is nothing but a row offset in the TMA coordinate of the A tile.  K order is
+// (chunk, dy, dx, c) as in conv3x3w_host.py:66-78.  Wgrad reduces over the
+// padded rows with both operands M/N-major, so the same packed buffers serve
+// forward, dgrad and wgrad (the reference's dW also reuses the packed X and dY,
+// torch_xdna_device.cpp:1968-1985, 2660-2679).
+#include <algorithm>
+#include <cstdio>
+
+#include "b2_common.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kABytes = BM * BK * 2;
+
+enum Kind : int { kConv = 0, kWgrad = 1, kGemm = 2 };
+
+struct Params {
+  // tile space
+  int tiles_m, tiles_n, splits, batch;
+  int num_kb;        // k-blocks of a full reduction
+  int kb_per_split;  // wgrad split-K
+  // conv geometry (padded grid)
+  int wp, hp, H, W, m_total;
+  int a_row_shift;   // wgrad: dY rows are read shifted by W+3
+  int ci_blocks;     // wgrad: BN-wide input-channel blocks per tap
+  // output
+  int M, N;                      // valid output extents
+  void* out;
+  long long osn, osc, osh, osw;  // conv: element strides; gemm: osn = batch stride, osh = ldd
+  const uint16_t* bias;
+  int relu;
+  float alpha, beta;
+  const void* cin;
+  int cin_dtype;
+  long long c_sm, c_sn, c_sb;
+  float* partial;                // wgrad partial sums [splits][9][M][N]
+  int* status;
+};
+
+template <int BN>
+struct Smem {
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+};
+
+__device__ __forceinline__ void decode_tile(int kind, const Params& p, int t, int& mt, int& nt,
+                                            int& bz, int& tap, int& kb0, int& kb1) {
+  tap = 0;
+  bz = 0;
+  if (kind == kConv) {
+    nt = t % p.tiles_n;
+    mt = t / p.tiles_n;
+    kb0 = 0;
+    kb1 = p.num_kb;
+  } else if (kind == kWgrad) {
+    nt = t % p.ci_blocks;
+    t /= p.ci_blocks;
+    tap = t % 9;
+    t /= 9;
+    mt = t % p.tiles_m;
+    int s = t / p.tiles_m;
+    bz = s;
+    kb0 = s * p.kb_per_split;
+    kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+  } else {
+    nt = t % p.tiles_n;
+    t /= p.tiles_n;
+    mt = t % p.tiles_m;
+    bz = t / p.tiles_m;
+    kb0 = 0;
+    kb1 = p.num_kb;
+  }
+}
+
+__device__ __forceinline__ int total_tiles(int kind, const Params& p) {
+  if (kind == kConv) return p.tiles_m * p.tiles_n;
+  if (kind == kWgrad) return p.splits * p.tiles_m * 9 * p.ci_blocks;
+  return p.batch * p.tiles_m * p.tiles_n;
+}
+
+// ---------------------------------------------------------------------------
+// epilogues: thread owns accumulator row `row` of the tile; r[] holds columns
+// [col0, col0+32) as fp32 bit patterns.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void epi_conv(const Params& p, int mt, int col0, int row,
+                                         const uint32_t (&r)[32]) {
+  const int prow = mt * BM + row;
+  if (prow >= p.m_total) return;
+  const int plane = p.hp * p.wp;
+  const int b = prow / plane;
+  const int rem = prow - b * plane;
+  const int y = rem / p.wp;
+  const int x = rem - y * p.wp;
+  if (y >= p.H || x >= p.W) return;
+  uint16_t* base = static_cast<uint16_t*>(p.out) + b * p.osn + y * p.osh + x * p.osw;
+  float v[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    float a = __uint_as_float(r[c]);
+    const int co = col0 + c;
+    if (p.bias && co < p.N) a += bf2f(p.bias[co]);
+    if (p.relu) a = a > 0.f ? a : 0.f;
+    v[c] = a;
+  }
+  if (p.osc == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
+    uint4* dst = reinterpret_cast<uint4*>(base + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf2(v[q * 8 + 6], v[q * 8 + 7]);
+      dst[q] = w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const int co = col0 + c;
+    if (co < p.N) base[(long long)co * p.osc] = f2bf(v[c]);
+  }
+}
+
+__device__ __forceinline__ void epi_wgrad(const Params& p, int split, int tap, int mt, int col0,
+                                          int row, const uint32_t (&r)[32]) {
+  const int co = mt * BM + row;
+  if (co >= p.M) return;
+  float* dst = p.partial + ((((long long)split * 9 + tap) * p.M + co) * p.N);
+  if (col0 + 32 <= p.N && (p.N % 4) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      d4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                          __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (col0 + c < p.N) dst[col0 + c] = __uint_as_float(r[c]);
+}
+
+__device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int col0, int row,
+                                         const uint32_t (&r)[32]) {
+  const int m = mt * BM + row;
+  if (m >= p.M) return;
+  float v[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    float a = p.alpha * __uint_as_float(r[c]);
+    const int n = col0 + c;
+    if (p.beta != 0.f && n < p.N) {
+      const long long ci = bz * p.c_sb + (long long)m * p.c_sm + (long long)n * p.c_sn;
+      const float cv = p.cin_dtype == B2_F32 ? static_cast<const float*>(p.cin)[ci]
+                                             : bf2f(static_cast<const uint16_t*>(p.cin)[ci]);
+      a += p.beta * cv;
+    }
+    v[c] = a;
+  }
+  uint16_t* base = static_cast<uint16_t*>(p.out) + bz * p.osn + (long long)m * p.osh;
+  if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
+    uint4* dst = reinterpret_cast<uint4*>(base + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf2(v[q * 8 + 6], v[q * 8 + 7]);
+      dst[q] = w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (col0 + c < p.N) base[col0 + c] = f2bf(v[c]);
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    igemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                 const __grid_constant__ CUtensorMap tma_b, const Params p) {
+  constexpr int kStageBytes = Smem<BN>::kStageBytes;
+  constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+  constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int ntiles = total_tiles(KIND, p);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ producer ------------------------------
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int mt, nt, bz, tap, kb0, kb1;
+        decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, kStageBytes);
+          last_par[stage] = int(phase);
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+          if constexpr (KIND == kConv) {
+            const int chunk = kb / 9, tp = kb - chunk * 9;
+            const int dy = tp / 3, dx = tp - dy * 3;
+            tma_load_3d(sa, &tma_a, fb, chunk * BK, mt * BM + dy * p.wp + dx, 0);
+            tma_load_3d(sb, &tma_b, fb, kb * BK, nt * BN, 0);
+          } else if constexpr (KIND == kWgrad) {
+            const int dy = tap / 3, dx = tap - dy * 3;
+            tma_load_3d(sa, &tma_a, fb, mt * BM, kb * BK + p.a_row_shift, 0);
+            tma_load_3d(sa + 8192, &tma_a, fb, mt * BM + 64, kb * BK + p.a_row_shift, 0);
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h)
+              tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK + dy * p.wp + dx, 0);
+          } else {
+            if constexpr (A_MN) {
+              tma_load_3d(sa, &tma_a, fb, mt * BM, kb * BK, bz);
+              tma_load_3d(sa + 8192, &tma_a, fb, mt * BM + 64, kb * BK, bz);
+            } else {
+              tma_load_3d(sa, &tma_a, fb, kb * BK, mt * BM, bz);
+            }
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int h = 0; h < BN / 64; ++h)
+                tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK, bz);
+            } else {
+              tma_load_3d(sb, &tma_b, fb, kb * BK, nt * BN, bz);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA can exit.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(smem_u32(&full[s]), uint32_t(last_par[s]), p.status, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer ----------------------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        int mt, nt, bz, tap, kb0, kb1;
+        decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma_f16(d_tmem, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(smem_u32(&tfull[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // All MMAs of this CTA have completed once mma_done flips.
+      tc_commit(smem_u32(mma_done));
+      mbar_wait(smem_u32(mma_done), 0, p.status, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------- epilogue ------------------------------
+    const int quarter = warp & 3;  // tensor-memory lane quarter this warp may read
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      int mt, nt, bz, tap, kb0, kb1;
+      decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
+      bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+#pragma unroll 1
+      for (int j = 0; j < BN / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld32(taddr + j * 32, r);
+        tc_wait_ld();
+        if constexpr (KIND == kConv) {
+          epi_conv(p, mt, nt * BN + j * 32, row, r);
+        } else if constexpr (KIND == kWgrad) {
+          epi_wgrad(p, bz, tap, mt, nt * BN + j * 32, row, r);
+        } else {
+          epi_gemm(p, bz, mt, nt * BN + j * 32, row, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
+__global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw, int dtype,
+                                    int splits, int Cout, int Cin) {
+  const long long total = (long long)Cout * Cin * 9;
+  const long long plane = (long long)9 * Cout * Cin;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int tap = int(i % 9);
+    const long long oc = i / 9;
+    const int ci = int(oc % Cin);
+    const int co = int(oc / Cin);
+    const float* src = partial + ((long long)tap * Cout + co) * Cin + ci;
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += src[k * plane];
+    if (dtype == B2_F32)
+      static_cast<float*>(dw)[i] = s;
+    else
+      static_cast<uint16_t*>(dw)[i] = f2bf(s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES>
+constexpr size_t smem_bytes() {
+  return size_t(STAGES) * Smem<BN>::kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+}
+
+template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
+b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles,
+                 cudaStream_t st) {
+  auto kern = igemm_kernel<BN, STAGES, KIND, A_MN, B_MN>;
+  constexpr size_t smem = smem_bytes<BN, STAGES>();
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[dev]) {
+    B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                      "cudaFuncSetAttribute(smem)"));
+    configured[dev] = true;
+  }
+  if (tiles <= 0) return B2_OK;
+  const int grid = std::min(tiles, sm_count(dev));
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  return check_cuda(cudaGetLastError(), "igemm launch");
+}
+
+constexpr int kStages128 = 6;
+constexpr int kStages256 = 4;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, void* y, int64_t sn,
+                      int64_t sc, int64_t sh, int64_t sw, int B, int Cin, int H, int W, int Cout,
+                      int relu, cudaStream_t st, const char* name) {
+  if (!rows || !wk || !y) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
+  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
+    return set_error(B2_ERR_INVALID, "%s: bad shape B=%d C=%d H=%d W=%d Cout=%d", name, B, Cin, H, W, Cout);
+  if (!aligned16(rows) || !aligned16(wk)) return set_error(B2_ERR_INVALID, "%s: operands must be 16-byte aligned", name);
+  const long long m_total = (long long)B * (H + 2) * (W + 2);
+  if (m_total + 2LL * (W + 2) + 2 + BM >= (1LL << 31))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: %lld padded rows exceed the 32-bit TMA coordinate range", name, m_total);
+  const int chunks = (Cin + 63) / 64;
+  const int cpad = chunks * 64;
+  const int ktot = chunks * 9 * 64;
+  const bool wide = Cout > 128 && (Cout % 256 == 0 || Cout % 256 > 128);
+  const int BN = wide ? 256 : 128;
+
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
+    const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
+    const uint32_t box[3] = {64, BM, 1};
+    B2_TRY(encode_tmap(&ta, rows, 3, dims, strides, box, true));
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(ktot), uint64_t(Cout), 1};
+    const uint64_t strides[2] = {uint64_t(ktot) * 2, uint64_t(ktot) * 2 * Cout};
+    const uint32_t box[3] = {64, uint32_t(BN), 1};
+    B2_TRY(encode_tmap(&tb, wk, 3, dims, strides, box, true));
+  }
+  Params p{};
+  p.tiles_m = int((m_total + BM - 1) / BM);
+  p.tiles_n = (Cout + BN - 1) / BN;
+  p.splits = 1;
+  p.batch = 1;
+  p.num_kb = chunks * 9;
+  p.kb_per_split = p.num_kb;
+  p.wp = W + 2;
+  p.hp = H + 2;
+  p.H = H;
+  p.W = W;
+  p.m_total = int(m_total);
+  p.M = int(m_total);
+  p.N = Cout;
+  p.out = y;
+  p.osn = sn;
+  p.osc = sc;
+  p.osh = sh;
+  p.osw = sw;
+  p.bias = bias;
+  p.relu = relu;
+  p.alpha = 1.f;
+  p.status = device_status_ptr();
+  const int tiles = p.tiles_m * p.tiles_n;
+  if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
+  return launch<128, kStages128, kConv, false, false>(ta, tb, p, tiles, st);
+}
+
+struct WgradPlan {
+  int BN, ci_blocks, tiles_m, num_kb, splits, kb_per_split;
+  long long m_total;
+  size_t workspace;
+};
+
+WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms) {
+  WgradPlan w{};
+  w.m_total = (long long)B * (H + 2) * (W + 2);
+  w.BN = Cin > 128 ? 256 : 128;
+  w.ci_blocks = (Cin + w.BN - 1) / w.BN;
+  w.tiles_m = (Cout + BM - 1) / BM;
+  w.num_kb = int((w.m_total + BK - 1) / BK);
+  const int base = w.tiles_m * 9 * w.ci_blocks;
+  int splits = std::max(1, (2 * sms + base - 1) / base);
+  splits = std::min(splits, std::max(1, w.num_kb / 16));
+  w.kb_per_split = (w.num_kb + splits - 1) / splits;
+  w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
+  w.workspace = size_t(w.splits) * 9 * size_t(Cout) * size_t(Cin) * sizeof(float);
+  return w;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+b2_status b2_conv3x3_fwd(const void* x_rows, const void* wk, const void* bias, void* y, int64_t ysn,
+                         int64_t ysc, int64_t ysh, int64_t ysw, int B, int Cin, int H, int W,
+                         int Cout, int relu, void* stream) {
+  return conv_common(x_rows, wk, static_cast<const uint16_t*>(bias), y, ysn, ysc, ysh, ysw, B, Cin,
+                     H, W, Cout, relu, static_cast<cudaStream_t>(stream), "b2_conv3x3_fwd");
+}
+
+b2_status b2_conv3x3_dgrad(const void* dy_rows, const void* wk_dgrad, void* dx, int64_t sn,
+                           int64_t sc, int64_t sh, int64_t sw, int B, int Cout, int H, int W,
+                           int Cin, void* stream) {
+  return conv_common(dy_rows, wk_dgrad, nullptr, dx, sn, sc, sh, sw, B, Cout, H, W, Cin, 0,
+                     static_cast<cudaStream_t>(stream), "b2_conv3x3_dgrad");
+}
+
+size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout) {
+  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return 16;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return std::max<size_t>(16, wgrad_plan(B, Cin, H, W, Cout, sm_count(dev)).workspace);
+}
+
+b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, int dw_dtype, int B,
+                           int Cin, int H, int W, int Cout, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!dy_rows || !x_rows || !dw || !workspace) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: null pointer");
+  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
+    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: bad shape");
+  if (dw_dtype != B2_BF16 && dw_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: dtype");
+  if (!aligned16(dy_rows) || !aligned16(x_rows) || !aligned16(workspace))
+    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: operands must be 16-byte aligned");
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
+    return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
+  if (workspace_bytes < w.workspace)
+    return set_error(B2_ERR_WORKSPACE, "b2_conv3x3_wgrad: workspace %zu < %zu bytes", workspace_bytes, w.workspace);
+  const int cpo = ((Cout + 63) / 64) * 64;
+  const int cpi = ((Cin + 63) / 64) * 64;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[3] = {uint64_t(cpo), uint64_t(w.m_total), 1};
+    const uint64_t strides[2] = {uint64_t(cpo) * 2, uint64_t(cpo) * 2 * w.m_total};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&ta, dy_rows, 3, dims, strides, box, true));
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(cpi), uint64_t(w.m_total), 1};
+    const uint64_t strides[2] = {uint64_t(cpi) * 2, uint64_t(cpi) * 2 * w.m_total};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&tb, x_rows, 3, dims, strides, box, true));
+  }
+  Params p{};
+  p.tiles_m = w.tiles_m;
+  p.tiles_n = 1;
+  p.splits = w.splits;
+  p.batch = 1;
+  p.num_kb = w.num_kb;
+  p.kb_per_split = w.kb_per_split;
+  p.wp = W + 2;
+  p.hp = H + 2;
+  p.H = H;
+  p.W = W;
+  p.m_total = int(w.m_total);
+  p.a_row_shift = W + 3;
+  p.ci_blocks = w.ci_blocks;
+  p.M = Cout;
+  p.N = Cin;
+  p.partial = static_cast<float*>(workspace);
+  p.alpha = 1.f;
+  p.status = device_status_ptr();
+  const int tiles = w.splits * w.tiles_m * 9 * w.ci_blocks;
+  if (w.BN == 256)
+    B2_TRY((launch<256, kStages256, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  else
+    B2_TRY((launch<128, kStages128, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  const long long total = (long long)Cout * Cin * 9;
+  const int threads = 256;
+  const int blocks = int(std::min<long long>((total + threads - 1) / threads, 148LL * 16));
+  wgrad_reduce_kernel<<<blocks, threads, 0, st>>>(static_cast<const float*>(workspace), dw, dw_dtype,
+                                                  w.splits, Cout, Cin);
+  return check_cuda(cudaGetLastError(), "wgrad reduce launch");
+}
+
+b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha, const void* A,
+                       int64_t lda, int64_t strideA, const void* Bm, int64_t ldb, int64_t strideB,
+                       float beta, const void* C, int c_dtype, int64_t c_sm, int64_t c_sn,
+                       int64_t c_sb, void* D, int64_t ldd, int64_t strideD, int batch,
+                       void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M < 0 || N < 0 || K < 0 || batch < 0) return set_error(B2_ERR_INVALID, "b2_gemm_bf16: negative size");
+  if (M == 0 || N == 0 || batch == 0) return B2_OK;
+  if (!A || !Bm || !D) return set_error(B2_ERR_INVALID, "b2_gemm_bf16: null pointer");
+  if (beta != 0.f && !C) return set_error(B2_ERR_INVALID, "b2_gemm_bf16: beta != 0 needs C");
+  if (c_dtype != B2_BF16 && c_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_gemm_bf16: c dtype");
+  if (K == 0) return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_bf16: K == 0");
+  if (!aligned16(A) || !aligned16(Bm) || lda % 8 || ldb % 8 || (batch > 1 && (strideA % 8 || strideB % 8)))
+    return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_bf16: operands need 16-byte aligned rows");
+  const int BN = N > 128 ? 256 : 128;
+  const uint64_t bt = uint64_t(batch);
+  CUtensorMap ta, tb;
+  if (!transA) {  // A [M][K], K contiguous -> K-major
+    const uint64_t dims[3] = {uint64_t(K), uint64_t(M), bt};
+    const uint64_t strides[2] = {uint64_t(lda) * 2, uint64_t(batch > 1 ? strideA : lda * M) * 2};
+    const uint32_t box[3] = {64, BM, 1};
+    B2_TRY(encode_tmap(&ta, A, 3, dims, strides, box, true));
+  } else {  // A stored [K][M], M contiguous -> MN-major
+    const uint64_t dims[3] = {uint64_t(M), uint64_t(K), bt};
+    const uint64_t strides[2] = {uint64_t(lda) * 2, uint64_t(batch > 1 ? strideA : lda * K) * 2};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&ta, A, 3, dims, strides, box, true));
+  }
+  if (transB) {  // B stored [N][K] -> K-major
+    const uint64_t dims[3] = {uint64_t(K), uint64_t(N), bt};
+    const uint64_t strides[2] = {uint64_t(ldb) * 2, uint64_t(batch > 1 ? strideB : ldb * N) * 2};
+    const uint32_t box[3] = {64, uint32_t(BN), 1};
+    B2_TRY(encode_tmap(&tb, Bm, 3, dims, strides, box, true));
+  } else {  // B [K][N], N contiguous -> MN-major
+    const uint64_t dims[3] = {uint64_t(N), uint64_t(K), bt};
+    const uint64_t strides[2] = {uint64_t(ldb) * 2, uint64_t(batch > 1 ? strideB : ldb * K) * 2};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&tb, Bm, 3, dims, strides, box, true));
+  }
+  Params p{};
+  p.tiles_m = (M + BM - 1) / BM;
+  p.tiles_n = (N + BN - 1) / BN;
+  p.splits = 1;
+  p.batch = batch;
+  p.num_kb = (K + BK - 1) / BK;
+  p.kb_per_split = p.num_kb;
+  p.M = M;
+  p.N = N;
+  p.out = D;
+  p.osn = strideD;
+  p.osh = ldd;
+  p.alpha = alpha;
+  p.beta = beta;
+  p.cin = C;
+  p.cin_dtype = c_dtype;
+  p.c_sm = c_sm;
+  p.c_sn = c_sn;
+  p.c_sb = c_sb;
+  p.status = device_status_ptr();
+  const int tiles = batch * p.tiles_m * p.tiles_n;
+  const bool amn = transA != 0, bmn = transB == 0;
+  if (BN == 256) {
+    if (!amn && !bmn) return launch<256, kStages256, kGemm, false, false>(ta, tb, p, tiles, st);
+    if (!amn && bmn) return launch<256, kStages256, kGemm, false, true>(ta, tb, p, tiles, st);
+    if (amn && !bmn) return launch<256, kStages256, kGemm, true, false>(ta, tb, p, tiles, st);
+    return launch<256, kStages256, kGemm, true, true>(ta, tb, p, tiles, st);
+  }
+  if (!amn && !bmn) return launch<128, kStages128, kGemm, false, false>(ta, tb, p, tiles, st);
+  if (!amn && bmn) return launch<128, kStages128, kGemm, false, true>(ta, tb, p, tiles, st);
+  if (amn && !bmn) return launch<128, kStages128, kGemm, true, false>(ta, tb, p, tiles, st);
+  return launch<128, kStages128, kGemm, true, true>(ta, tb, p, tiles, st);
+}
+
+}  // extern "C"

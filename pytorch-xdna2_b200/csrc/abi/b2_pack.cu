@@ -1,0 +1,197 @@
+// Layout packers: strided bf16 activations -> padded-grid rows, OIHW weights
+// -> K-ordered GEMM operands (forward and dgrad), and dense NCHW <-> NHWC.
+// All of them move bf16 bit patterns unchanged (bit-exact copies), staged
+// through shared memory so that both the global reads and the 16-byte global
+// writes are coalesced.
+//
+// Reference layouts: xdna_train/_designs/conv3x3w_host.py:32-78 and
+// xdna_train/_native/conv_pack.cpp:352-443, 470-519.
+#include <algorithm>
+
+#include "b2_common.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kPix = 64;  // pixels per tile
+constexpr int kCh = 64;   // channels per tile (one chunk)
+
+// One CTA writes one padded grid row (b, yp) for one 64-channel chunk:
+// (W+2) pixels x 64 channels, 128 bytes per pixel.
+__global__ void __launch_bounds__(256) pack_rows_kernel(const uint16_t* __restrict__ x, long long sn,
+                                                        long long sc, long long sh, long long sw,
+                                                        int B, int C, int H, int W, int chunks,
+                                                        uint16_t* __restrict__ rows) {
+  __shared__ uint16_t tile[kCh][kPix + 2];
+  const int chunk = blockIdx.x % chunks;
+  const int yp = (blockIdx.x / chunks) % (H + 2);
+  const int b = blockIdx.x / (chunks * (H + 2));
+  const int wp = W + 2;
+  const long long cpad = (long long)chunks * kCh;
+  uint16_t* dst_row = rows + ((long long)(b * (H + 2) + yp) * wp) * cpad + chunk * kCh;
+  const int tid = threadIdx.x;
+  if (yp == 0 || yp == H + 1) {
+    // border row: all zeros
+    for (int e = tid; e < wp * 8; e += 256) {
+      const int px = e >> 3, v = e & 7;
+      *reinterpret_cast<uint4*>(dst_row + px * cpad + v * 8) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const int y = yp - 1;
+  if (tid < 16) {  // left and right border pixels
+    const int px = (tid < 8) ? 0 : W + 1;
+    *reinterpret_cast<uint4*>(dst_row + px * cpad + (tid & 7) * 8) = make_uint4(0, 0, 0, 0);
+  }
+  const uint16_t* src = x + b * sn + y * sh + (long long)(chunk * kCh) * sc;
+  const bool x_fast = (sw == 1);  // NCHW-like: pixels contiguous
+  for (int x0 = 0; x0 < W; x0 += kPix) {
+    __syncthreads();
+    // load [64 ch][64 px]
+    for (int i = 0; i < (kCh * kPix) / 256; ++i) {
+      const int e = i * 256 + tid;
+      int c, px;
+      if (x_fast) {
+        c = e / kPix;
+        px = e % kPix;
+      } else {
+        px = e / kCh;
+        c = e % kCh;
+      }
+      const int xx = x0 + px;
+      const int cc = chunk * kCh + c;
+      uint16_t v = 0;
+      if (xx < W && cc < C) v = src[(long long)c * sc + (long long)xx * sw];
+      tile[c][px] = v;
+    }
+    __syncthreads();
+    // store: pixel-major, 8 x 16 B per pixel
+    for (int i = 0; i < (kCh * kPix / 8) / 256; ++i) {
+      const int e = i * 256 + tid;
+      const int px = e >> 3, v = e & 7;
+      const int xx = x0 + px;
+      if (xx >= W) continue;
+      uint4 w;
+      w.x = uint32_t(tile[v * 8 + 0][px]) | (uint32_t(tile[v * 8 + 1][px]) << 16);
+      w.y = uint32_t(tile[v * 8 + 2][px]) | (uint32_t(tile[v * 8 + 3][px]) << 16);
+      w.z = uint32_t(tile[v * 8 + 4][px]) | (uint32_t(tile[v * 8 + 5][px]) << 16);
+      w.w = uint32_t(tile[v * 8 + 6][px]) | (uint32_t(tile[v * 8 + 7][px]) << 16);
+      *reinterpret_cast<uint4*>(dst_row + (long long)(xx + 1) * cpad + v * 8) = w;
+    }
+  }
+}
+
+// Wk[n][chunk*576 + tap*64 + c]; forward: n = co, source w[co][chunk*64+c][tap];
+// dgrad: n = ci, source w[chunk*64+c][ci][8-tap] (spatial flip + in/out swap).
+__global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int Cout, int Cin, int chunks,
+                                   int dgrad, uint16_t* __restrict__ wk) {
+  const int ktot = chunks * 576;
+  const int nrows = dgrad ? Cin : Cout;
+  const int kred = dgrad ? Cout : Cin;  // channels reduced over
+  const long long total = (long long)nrows * ktot;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = int(i / ktot);
+    const int k = int(i % ktot);
+    const int chunk = k / 576;
+    const int tap = (k % 576) / 64;
+    const int c = chunk * 64 + (k % 64);
+    uint16_t v = 0;
+    if (c < kred) {
+      if (!dgrad)
+        v = w[((long long)n * Cin + c) * 9 + tap];
+      else
+        v = w[((long long)c * Cin + n) * 9 + (8 - tap)];
+    }
+    wk[i] = v;
+  }
+}
+
+// [B][R][S] -> [B][S][R] bf16 tile transpose (R, S arbitrary).
+__global__ void __launch_bounds__(256) transpose_kernel(const uint16_t* __restrict__ src,
+                                                        uint16_t* __restrict__ dst, int R, int S) {
+  __shared__ uint16_t tile[64][64 + 2];
+  const int tiles_s = (S + 63) / 64;
+  const int tiles_r = (R + 63) / 64;
+  const int ts = blockIdx.x % tiles_s;
+  const int tr = (blockIdx.x / tiles_s) % tiles_r;
+  const int b = blockIdx.x / (tiles_s * tiles_r);
+  const uint16_t* s = src + (long long)b * R * S;
+  uint16_t* d = dst + (long long)b * R * S;
+  const int tid = threadIdx.x;
+  for (int i = 0; i < 16; ++i) {
+    const int e = i * 256 + tid;
+    const int r = e / 64, c = e % 64;
+    const int rr = tr * 64 + r, cc = ts * 64 + c;
+    tile[r][c] = (rr < R && cc < S) ? s[(long long)rr * S + cc] : uint16_t(0);
+  }
+  __syncthreads();
+  for (int i = 0; i < 16; ++i) {
+    const int e = i * 256 + tid;
+    const int c = e / 64, r = e % 64;
+    const int rr = tr * 64 + r, cc = ts * 64 + c;
+    if (rr < R && cc < S) d[(long long)cc * R + rr] = tile[r][c];
+  }
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B,
+                            int C, int H, int W, int chunks, void* rows, void* stream) {
+  if (!x || !rows) return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: null pointer");
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || chunks < (C + 63) / 64)
+    return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: bad shape B=%d C=%d H=%d W=%d chunks=%d", B, C,
+                     H, W, chunks);
+  if (reinterpret_cast<uintptr_t>(rows) & 15) return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: rows not 16-byte aligned");
+  const long long blocks = (long long)B * (H + 2) * chunks;
+  if (blocks >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "b2_pack_rows_bf16: too large");
+  pack_rows_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), sn, sc, sh, sw, B, C, H, W, chunks, static_cast<uint16_t*>(rows));
+  return check_cuda(cudaGetLastError(), "pack_rows launch");
+}
+
+static b2_status pack_weight(const void* w, int Cout, int Cin, int chunks, int dgrad, void* wk,
+                             void* stream, const char* name) {
+  if (!w || !wk) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
+  const int kred = dgrad ? Cout : Cin;
+  if (Cout <= 0 || Cin <= 0 || chunks < (kred + 63) / 64) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
+  const long long total = (long long)(dgrad ? Cin : Cout) * chunks * 576;
+  const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 8));
+  pack_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(w), Cout, Cin, chunks, dgrad, static_cast<uint16_t*>(wk));
+  return check_cuda(cudaGetLastError(), "pack_weight launch");
+}
+
+b2_status b2_pack_weight_fwd_bf16(const void* w, int Cout, int Cin, int chunks, void* wk, void* stream) {
+  return pack_weight(w, Cout, Cin, chunks, 0, wk, stream, "b2_pack_weight_fwd_bf16");
+}
+
+b2_status b2_pack_weight_dgrad_bf16(const void* w, int Cout, int Cin, int chunks_o, void* wk,
+                                    void* stream) {
+  return pack_weight(w, Cout, Cin, chunks_o, 1, wk, stream, "b2_pack_weight_dgrad_bf16");
+}
+
+static b2_status transpose(const void* src, void* dst, int B, int R, int S, void* stream, const char* name) {
+  if (!src || !dst) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
+  if (B <= 0 || R <= 0 || S <= 0) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
+  const long long blocks = (long long)B * ((R + 63) / 64) * ((S + 63) / 64);
+  if (blocks >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "%s: too large", name);
+  transpose_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), R, S);
+  return check_cuda(cudaGetLastError(), name);
+}
+
+b2_status b2_nchw_to_nhwc_bf16(const void* src, void* dst, int B, int C, int HW, void* stream) {
+  return transpose(src, dst, B, C, HW, stream, "b2_nchw_to_nhwc_bf16");
+}
+
+b2_status b2_nhwc_to_nchw_bf16(const void* src, void* dst, int B, int C, int HW, void* stream) {
+  return transpose(src, dst, B, HW, C, stream, "b2_nhwc_to_nchw_bf16");
+}
+
+}  // extern "C"

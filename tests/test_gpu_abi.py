@@ -1,0 +1,343 @@
+"""Parity of libxdna_b200's sm_100a kernels, called through the C ABI, with
+the CPU oracle (oracle/, pinned to the reference) and with an FP32 PyTorch
+reference of the same op.
+
+Tolerances: layouts and region kernels bit-exact; conv / GEMM
+max|out - ref| <= 2e-2 * max|ref| and relative L2 error
+<= 5e-3 (what fp32 accumulation + one bf16 rounding gives); Adam within 1e-6
+(fp32) or one bf16 ulp.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from xdna_train import _abi
+
+pytestmark = pytest.mark.gpu
+
+
+def st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def close(got: torch.Tensor, ref: torch.Tensor, tol=2e-2, l2=5e-3):
+    got = got.detach().float().cpu()
+    ref = ref.detach().float().cpu()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    rel = ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item()
+    assert err <= tol * scale, f"max abs err {err} > {tol} * {scale}"
+    assert rel <= l2, f"rel L2 {rel}"
+
+
+def rows_of(x: torch.Tensor) -> torch.Tensor:
+    B, Cc, H, W = x.shape
+    chunks = -(-Cc // 64)
+    rows = torch.empty(B * (H + 2) * (W + 2), chunks * 64, dtype=torch.bfloat16, device=x.device)
+    s = x.stride()
+    _abi.call("b2_pack_rows_bf16", x.data_ptr(), s[0], s[1], s[2], s[3], B, Cc, H, W, chunks, rows.data_ptr(),
+              st())
+    return rows
+
+
+def wk_of(w: torch.Tensor, dgrad=False) -> torch.Tensor:
+    Cout, Cin = w.shape[:2]
+    kred = Cout if dgrad else Cin
+    chunks = -(-kred // 64)
+    wk = torch.empty((Cin if dgrad else Cout), chunks * 576, dtype=torch.bfloat16, device=w.device)
+    name = "b2_pack_weight_dgrad_bf16" if dgrad else "b2_pack_weight_fwd_bf16"
+    _abi.call(name, w.data_ptr(), Cout, Cin, chunks, wk.data_ptr(), st())
+    return wk
+
+
+# --------------------------------------------------------------------- packers
+
+@pytest.mark.parametrize("shape", [(2, 70, 5, 7), (1, 3, 4, 4), (3, 64, 6, 9), (2, 130, 3, 11), (1, 64, 2, 150)])
+@pytest.mark.parametrize("channels_last", [False, True])
+def test_pack_rows_bit_exact(cuda, shape, channels_last):
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(*shape, generator=g).bfloat16()
+    xd = x.to(cuda)
+    if channels_last:
+        xd = xd.contiguous(memory_format=torch.channels_last)
+    got = bits(rows_of(xd))
+    want = oracle.pack_rows(bits(x))
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("co_ci", [(128, 70), (100, 64), (3, 10), (256, 130)])
+def test_pack_weights_bit_exact(cuda, co_ci):
+    Cout, Cin = co_ci
+    w = torch.randn(Cout, Cin, 3, 3).bfloat16()
+    wd = w.to(cuda)
+    assert np.array_equal(bits(wk_of(wd)), oracle.pack_weight(bits(w)))
+    assert np.array_equal(bits(wk_of(wd, dgrad=True)), oracle.pack_weight(bits(w), dgrad=True))
+
+
+def test_nchw_nhwc_roundtrip_bit_exact(cuda):
+    x = torch.randn(3, 70, 9, 13, device=cuda).bfloat16()
+    y = torch.empty(3, 9 * 13, 70, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_nchw_to_nhwc_bf16", x.data_ptr(), y.data_ptr(), 3, 70, 117, st())
+    assert torch.equal(y.view(3, 9, 13, 70).permute(0, 3, 1, 2), x)
+    z = torch.empty_like(x)
+    _abi.call("b2_nhwc_to_nchw_bf16", y.data_ptr(), z.data_ptr(), 3, 70, 117, st())
+    assert torch.equal(z, x)
+
+
+# ------------------------------------------------------------------------ conv
+
+SMALL = [  # B, Cin, H, W, Cout, bias  (oracle-checked)
+    (2, 64, 8, 8, 64, True),
+    (3, 3, 5, 7, 10, True),
+    (2, 70, 12, 37, 70, False),
+    (1, 130, 6, 6, 200, True),
+]
+LARGE = [  # the reference's run_conv3x3w_torch.py shapes (:22-35) and the README conv
+    (40, 256, 36, 36, 128, False),
+    (40, 64, 36, 36, 64, True),
+    (4, 195, 36, 36, 70, False),
+    (40, 128, 9, 9, 128, False),
+    (40, 256, 18, 18, 256, False),
+    (2, 128, 14, 112, 128, False),
+    (1, 64, 8, 224, 64, False),
+    (16, 128, 36, 36, 128, True),
+    (8, 512, 18, 18, 512, False),
+]
+
+
+def _conv_inputs(cuda, B, Cin, H, W, Cout, bias, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, Cin, H, W, generator=g).bfloat16()
+    w = ((torch.rand(Cout, Cin, 3, 3, generator=g) * 2 - 1) * (1.0 / (9 * Cin)) ** 0.5).bfloat16()
+    b = torch.randn(Cout, generator=g).bfloat16() if bias else None
+    dy = torch.randn(B, Cout, H, W, generator=g).bfloat16()
+    return x, w, b, dy
+
+
+def _gpu_conv(cuda, x, w, b, dy, out_channels_last=False):
+    B, Cin, H, W = x.shape
+    Cout = w.shape[0]
+    xd, wd, dyd = x.to(cuda), w.to(cuda), dy.to(cuda)
+    bd = b.to(cuda) if b is not None else None
+    xr, dyr = rows_of(xd), rows_of(dyd)
+    mf = torch.channels_last if out_channels_last else torch.contiguous_format
+    y = torch.empty(B, Cout, H, W, dtype=torch.bfloat16, device=cuda, memory_format=mf)
+    s = y.stride()
+    _abi.call("b2_conv3x3_fwd", xr.data_ptr(), wk_of(wd).data_ptr(), 0 if bd is None else bd.data_ptr(),
+              y.data_ptr(), s[0], s[1], s[2], s[3], B, Cin, H, W, Cout, 0, st())
+    dx = torch.empty(B, Cin, H, W, dtype=torch.bfloat16, device=cuda, memory_format=mf)
+    s = dx.stride()
+    _abi.call("b2_conv3x3_dgrad", dyr.data_ptr(), wk_of(wd, dgrad=True).data_ptr(), dx.data_ptr(), s[0], s[1],
+              s[2], s[3], B, Cout, H, W, Cin, st())
+    ws_bytes = _abi.lib().b2_conv3x3_wgrad_workspace_bytes(B, Cin, H, W, Cout)
+    ws = torch.empty(ws_bytes // 4 + 4, dtype=torch.float32, device=cuda)
+    dw = torch.empty(Cout, Cin, 3, 3, dtype=torch.float32, device=cuda)
+    _abi.call("b2_conv3x3_wgrad", dyr.data_ptr(), xr.data_ptr(), dw.data_ptr(), _abi.B2_F32, B, Cin, H, W, Cout,
+              ws.data_ptr(), ws.numel() * 4, st())
+    torch.cuda.synchronize()
+    return y, dx, dw
+
+
+@pytest.mark.parametrize("shape", SMALL)
+def test_conv_vs_oracle(cuda, shape):
+    x, w, b, dy = _conv_inputs(cuda, *shape)
+    y, dx, dw = _gpu_conv(cuda, x, w, b, dy)
+    close(y, torch.from_numpy(oracle.conv_fwd(bits(x), bits(w), None if b is None else bits(b))))
+    close(dx, torch.from_numpy(oracle.conv_dgrad(bits(dy), bits(w))))
+    close(dw, torch.from_numpy(oracle.conv_wgrad(bits(dy), bits(x))))
+
+
+@pytest.mark.parametrize("shape", LARGE)
+def test_conv_vs_fp32_reference(cuda, shape):
+    x, w, b, dy = _conv_inputs(cuda, *shape, seed=1)
+    y, dx, dw = _gpu_conv(cuda, x, w, b, dy, out_channels_last=(shape[0] % 2 == 0))
+    xf, wf, dyf = x.float().to(cuda), w.float().to(cuda), dy.float().to(cuda)
+    bf = b.float().to(cuda) if b is not None else None
+    with torch.no_grad():
+        torch.backends.cudnn.allow_tf32 = False
+        y_ref = torch.nn.functional.conv2d(xf, wf, bf, padding=1)
+        dx_ref, dw_ref, _ = torch.ops.aten.convolution_backward(dyf, xf, wf, None, [1, 1], [1, 1], [1, 1], False,
+                                                                [0, 0], 1, [True, True, False])
+    close(y, y_ref)
+    close(dx, dx_ref)
+    close(dw, dw_ref)
+
+
+def test_conv_relu_epilogue_and_bf16_wgrad(cuda):
+    x, w, b, dy = _conv_inputs(cuda, 2, 64, 9, 9, 96, True, seed=3)
+    xd, wd, bd = x.to(cuda), w.to(cuda), b.to(cuda)
+    y = torch.empty(2, 96, 9, 9, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_conv3x3_fwd", rows_of(xd).data_ptr(), wk_of(wd).data_ptr(), bd.data_ptr(), y.data_ptr(),
+              *y.stride(), 2, 64, 9, 9, 96, 1, st())
+    ref = torch.from_numpy(oracle.conv_fwd(bits(x), bits(w), bits(b), relu=True))
+    close(y, ref)
+    assert (y >= 0).all()
+    # bf16 dW output = fp32 result rounded once
+    dyd = dy.to(cuda)
+    ws_bytes = _abi.lib().b2_conv3x3_wgrad_workspace_bytes(2, 64, 9, 9, 96)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
+    dw32 = torch.empty(96, 64, 3, 3, dtype=torch.float32, device=cuda)
+    dw16 = torch.empty(96, 64, 3, 3, dtype=torch.bfloat16, device=cuda)
+    xr, dyr = rows_of(xd), rows_of(dyd)
+    for out, dt in ((dw32, _abi.B2_F32), (dw16, _abi.B2_BF16)):
+        _abi.call("b2_conv3x3_wgrad", dyr.data_ptr(), xr.data_ptr(), out.data_ptr(), dt, 2, 64, 9, 9, 96,
+                  ws.data_ptr(), ws_bytes, st())
+    assert torch.equal(dw16, dw32.bfloat16())
+
+
+def test_wgrad_rejects_small_workspace(cuda):
+    ws = torch.empty(16, dtype=torch.uint8, device=cuda)
+    t = torch.empty(1 << 16, dtype=torch.bfloat16, device=cuda)
+    st_ = _abi.lib().b2_conv3x3_wgrad(t.data_ptr(), t.data_ptr(), t.data_ptr(), 0, 1, 64, 8, 8, 64, ws.data_ptr(),
+                                      16, st())
+    assert st_ == 5
+
+
+def test_device_status_clean(cuda):
+    code = ctypes.c_int(-1)
+    _abi.check(_abi.lib().b2_device_status(0, ctypes.byref(code)))
+    assert code.value == 0
+
+
+# ------------------------------------------------------------------------ GEMM
+
+@pytest.mark.parametrize("ta", [0, 1])
+@pytest.mark.parametrize("tb", [0, 1])
+@pytest.mark.parametrize("mnk", [(512, 1024, 4096), (300, 200, 136), (64, 520, 72), (1, 256, 64)])
+def test_gemm_transposes(cuda, ta, tb, mnk):
+    M, N, K = mnk
+    g = torch.Generator().manual_seed(M + N + K)
+    A = torch.randn(M, K, generator=g).bfloat16()
+    Bm = torch.randn(K, N, generator=g).bfloat16()
+    a_store = (A.t().contiguous() if ta else A).to(cuda)
+    b_store = (Bm.t().contiguous() if tb else Bm).to(cuda)
+    lda, ldb = a_store.shape[1], b_store.shape[1]
+    if lda % 8 or ldb % 8:
+        pytest.skip("TMA needs 16-byte aligned rows")
+    D = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_gemm_bf16", ta, tb, M, N, K, 1.0, a_store.data_ptr(), lda, 0, b_store.data_ptr(), ldb, 0, 0.0,
+              None, _abi.B2_BF16, 0, 0, 0, D.data_ptr(), N, 0, 1, st())
+    torch.cuda.synchronize()
+    close(D, A.float() @ Bm.float())
+
+
+def test_gemm_batched_bias_alpha_beta(cuda):
+    g = torch.Generator().manual_seed(7)
+    bt, M, N, K = 3, 200, 136, 256
+    A = torch.randn(bt, M, K, generator=g).bfloat16()
+    Bm = torch.randn(bt, N, K, generator=g).bfloat16()  # transB storage
+    bias = torch.randn(N, generator=g).bfloat16()
+    Ad, Bd, biasd = A.to(cuda), Bm.to(cuda), bias.to(cuda)
+    D = torch.empty(bt, M, N, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_gemm_bf16", 0, 1, M, N, K, 0.5, Ad.data_ptr(), K, M * K, Bd.data_ptr(), K, N * K, 2.0,
+              biasd.data_ptr(), _abi.B2_BF16, 0, 1, 0, D.data_ptr(), N, M * N, bt, st())
+    torch.cuda.synchronize()
+    ref = 0.5 * torch.bmm(A.float(), Bm.float().transpose(1, 2)) + 2.0 * bias.float()
+    close(D, ref)
+    # and against the oracle for one batch entry
+    o = oracle.gemm(bits(A[1]), bits(Bm[1].t().contiguous()), np.broadcast_to(bias.float().numpy(), (M, N)),
+                    alpha=0.5, beta=2.0)
+    close(D[1], torch.from_numpy(o))
+
+
+# ------------------------------------------------------------------------ Adam
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("adamw,amsgrad,wd", [(False, False, 0.0), (True, False, 0.01), (False, True, 0.1)])
+def test_fused_adam_matches_cpu(cuda, dtype, adamw, amsgrad, wd):
+    g = torch.Generator().manual_seed(5)
+    sizes = [1, 7, 4096, 70001, 3 * 16384 + 5]
+    ps = [torch.randn(n, generator=g).to(dtype) for n in sizes]
+    gs = [torch.randn(n, generator=g).to(dtype) for n in sizes]
+    ms = [(torch.randn(n, generator=g) * 0.1).to(dtype) for n in sizes]
+    vs = [(torch.rand(n, generator=g) * 0.1).to(dtype) for n in sizes]
+    xs = [(torch.rand(n, generator=g) * 0.1).to(dtype) for n in sizes] if amsgrad else []
+    steps = [torch.tensor(float(i + 2)) for i in range(len(sizes))]
+    dev = lambda L: [t.to(cuda) for t in L]  # noqa: E731
+    P, G, M, V, X, S = dev(ps), dev(gs), dev(ms), dev(vs), dev(xs), dev(steps)
+    fn = torch._fused_adamw_ if adamw else torch._fused_adam_
+    fn(ps, gs, ms, vs, xs, steps, lr=1e-2, beta1=0.9, beta2=0.99, weight_decay=wd, eps=1e-8, amsgrad=amsgrad,
+       maximize=False)
+    arr = (_abi.AdamTensor * len(sizes))()
+    for i, n in enumerate(sizes):
+        arr[i] = _abi.AdamTensor(P[i].data_ptr(), G[i].data_ptr(), M[i].data_ptr(), V[i].data_ptr(),
+                                 X[i].data_ptr() if amsgrad else None, S[i].data_ptr(), n)
+    code = _abi.B2_F32 if dtype == torch.float32 else _abi.B2_BF16
+    hp = _abi.AdamHparams(1e-2, 0.9, 0.99, wd, 1e-8, int(amsgrad), 0, int(adamw), code, code, None, None, None)
+    _abi.check(_abi.lib().b2_fused_adam(arr, len(sizes), ctypes.byref(hp), st()))
+    torch.cuda.synchronize()
+    for got, ref in zip(P + M + V, ps + ms + vs):
+        got = got.cpu().float()
+        ref = ref.float()
+        if dtype == torch.float32:
+            assert (got - ref).abs().max().item() <= 1e-6 * max(1.0, ref.abs().max().item())
+        else:  # at most one bf16 ulp apart
+            ulp = ref.abs().clamp_min(1e-30) * 2.0 ** -7
+            assert ((got - ref).abs() <= ulp + 1e-30).all()
+
+
+# --------------------------------------------------------------------- regions
+
+@pytest.fixture(scope="module")
+def reg():
+    from pathlib import Path
+    return np.load(Path(__file__).resolve().parent / "golden" / "regions.npz")
+
+
+def _dev(a: np.ndarray, cuda):
+    return torch.from_numpy(a.view(np.int16).copy()).to(cuda).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("tag", ["even", "odd"])
+def test_regions_bit_exact_vs_reference(cuda, reg, tag):
+    a, b, base = (_dev(reg[f"{tag}_{k}"], cuda) for k in ("a", "b", "base"))
+    shape = reg[f"{tag}_a"].shape
+    planes, H, W = shape[0] * shape[1], shape[2], shape[3]
+    n = a.numel()
+    out = torch.empty_like(a)
+    _abi.call("b2_region_relu_bf16", a.data_ptr(), out.data_ptr(), n, st())
+    assert np.array_equal(bits(out), reg[f"{tag}_relu"])
+    r = torch.empty_like(a)
+    p = torch.empty(shape[0], shape[1], H // 2, W // 2, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_region_relu_maxpool2_bf16", a.data_ptr(), r.data_ptr(), p.data_ptr(), planes, H, W, st())
+    assert np.array_equal(bits(r), reg[f"{tag}_relu_r"])
+    assert np.array_equal(bits(p), reg[f"{tag}_pool"])
+    _abi.call("b2_region_addtap_bf16", base.data_ptr(), a.data_ptr(), b.data_ptr(), out.data_ptr(), n,
+              ctypes.c_float(0.37), st())
+    assert np.array_equal(bits(out), reg[f"{tag}_addtap"])
+    _abi.call("b2_region_addtap_bf16", None, a.data_ptr(), b.data_ptr(), out.data_ptr(), n, ctypes.c_float(-1.5),
+              st())
+    assert np.array_equal(bits(out), reg[f"{tag}_addtap_nobase"])
+    rr = _dev(reg[f"{tag}_relu"], cuda)
+    _abi.call("b2_region_relu_bwd_bf16", rr.data_ptr(), base.data_ptr(), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+              n, ctypes.c_float(0.25), st())
+    assert np.array_equal(bits(out), reg[f"{tag}_relu_bwd"])
+    _abi.call("b2_region_relu_bwd_bf16", rr.data_ptr(), base.data_ptr(), None, None, out.data_ptr(), n,
+              ctypes.c_float(0.25), st())
+    assert np.array_equal(bits(out), reg[f"{tag}_relu_bwd_notap"])
+    gg = _dev(reg[f"{tag}_g"], cuda)
+    _abi.call("b2_region_maxpool2_bwd_bf16", a.data_ptr(), gg.data_ptr(), out.data_ptr(), planes, H, W, st())
+    assert np.array_equal(bits(out), reg[f"{tag}_maxpool_bwd"])
+    fa, fb = _dev(reg[f"{tag}_fin_a"], cuda), _dev(reg[f"{tag}_fin_b"], cuda)
+    acc = torch.zeros(1, dtype=torch.float64, device=cuda)
+    _abi.call("b2_region_sqdiff_sum_bf16", fa.data_ptr(), fb.data_ptr(), n, acc.data_ptr(), st())
+    want = reg[f"{tag}_sqdiff"][0]
+    assert abs(acc.item() - want) <= 1e-5 * abs(want)
+
+
+def test_regions_large_sqdiff(cuda):
+    g = torch.Generator().manual_seed(11)
+    a = torch.randn(40, 256, 18, 18, generator=g).bfloat16()
+    b = torch.randn(40, 256, 18, 18, generator=g).bfloat16()
+    acc = torch.zeros(1, dtype=torch.float64, device=cuda)
+    ad, bd = a.to(cuda), b.to(cuda)
+    _abi.call("b2_region_sqdiff_sum_bf16", ad.data_ptr(), bd.data_ptr(), a.numel(), acc.data_ptr(), st())
+    want = oracle.sqdiff_sum(bits(a), bits(b))
+    assert abs(acc.item() - want) <= 1e-5 * want
