@@ -216,27 +216,40 @@ void oracle_maxpool2_bwd(const uint16_t* x, const uint16_t* g, uint16_t* out, lo
       }
 }
 
-/* ---- Adam / AdamW, PyTorch's definition (torch.optim.Adam docs), fp32 ---- */
+/* ---- Adam / AdamW, fp32 ----------------------------------------------------
+ * PyTorch's Adam/AdamW definition in the operation order of its CPU
+ * _fused_adam_ kernel (the reference's path, torch_xdna_device.cpp:5196-5198):
+ * m = fma(1-b1, g-m, m); v = fma((1-b2)g, g, b2 v); AdamW decay p *= 1-lr*wd;
+ * coefficients formed in double, rounded to float once. */
 void oracle_adam_f32(float* p, const float* g_in, float* m, float* v, float* vmax, long long n, float step,
                      float lr, float beta1, float beta2, float wd, float eps, int amsgrad, int maximize,
                      int adamw) {
-  const double bc1 = 1.0 - pow(beta1, step), bc2 = 1.0 - pow(beta2, step);
-  const float step_size = (float)(lr / bc1), bc2_sqrt = (float)sqrt(bc2);
+  const double bc1 = 1.0 - pow((double)beta1, (double)step), bc2 = 1.0 - pow((double)beta2, (double)step);
+  const float step_size = (float)((double)lr / bc1), bc2_sqrt = (float)sqrt(bc2);
+  const float omb1 = (float)(1.0 - (double)beta1), omb2 = (float)(1.0 - (double)beta2);
+  const float decay = (float)(1.0 - (double)lr * (double)wd);
   for (long long i = 0; i < n; ++i) {
     float g = maximize ? -g_in[i] : g_in[i];
     float pp = p[i];
     if (wd != 0.0f) {
-      if (adamw) pp -= lr * wd * pp;
-      else g += wd * pp;
+      if (adamw) pp = pp * decay;
+      else g = fmaf(wd, pp, g);
     }
-    m[i] = m[i] + (1.0f - beta1) * (g - m[i]);
-    v[i] = beta2 * v[i] + (1.0f - beta2) * g * g;
+    m[i] = fmaf(omb1, g - m[i], m[i]);
+    {
+      const float gs = omb2 * g, bv = beta2 * v[i];
+      v[i] = fmaf(gs, g, bv);
+    }
     float vv = v[i];
     if (amsgrad) {
       vv = vmax[i] > v[i] ? vmax[i] : v[i];
       vmax[i] = vv;
     }
-    pp -= step_size * m[i] / (sqrtf(vv) / bc2_sqrt + eps);
+    {
+      const float denom = sqrtf(vv) / bc2_sqrt + eps;
+      const float upd = step_size * m[i];
+      pp = pp - upd / denom;
+    }
     p[i] = pp;
   }
 }

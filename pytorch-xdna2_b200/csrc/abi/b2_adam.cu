@@ -8,10 +8,14 @@
 // `_fused_adam_` CPU path runs (reached through the boxed fallback,
 // xdna_train/_native/torch_xdna_device.cpp:5124-5260):
 //   g = grad / grad_scale; g = maximize ? -g : g
-//   AdamW: p *= 1 - lr*wd         Adam: g += wd * p
-//   m = lerp(m, g, 1-beta1);  v = beta2*v + (1-beta2)*g*g
+//   AdamW: p *= 1 - lr*wd         Adam: g = fma(wd, p, g)
+//   m = fma(1-beta1, g-m, m)      v = fma((1-beta2)*g, g, beta2*v)
 //   denom = sqrt(amsgrad ? max(vmax, v) : v) / sqrt(1 - beta2^t) + eps
-//   p -= lr / (1 - beta1^t) * m / denom
+//   p -= (lr / (1 - beta1^t)) * m / denom
+// with the scalar coefficients formed in double and rounded to fp32 once.
+// This operation order reproduces torch's CPU _fused_adam_ bit for bit on
+// bf16 parameters (checked in tests/test_gpu_abi.py); the explicit __f*_rn /
+// __fmaf_rn intrinsics keep nvcc from contracting it differently.
 #include <algorithm>
 #include <cmath>
 
@@ -38,7 +42,7 @@ struct AdamArgs {
 };
 
 struct AdamScalars {
-  float lr, beta1, beta2, wd, eps;
+  double lr, beta1, beta2, wd, eps;
   int amsgrad, maximize, adamw;
   const float* lr_tensor;
   const float* grad_scale;
@@ -67,13 +71,16 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
   const int t = a.block_tensor[blockIdx.x];
   const long long begin = (long long)a.block_chunk[blockIdx.x] * kChunk;
   const long long end = min(begin + kChunk, a.numel[t]);
-  const float step = *a.step[t];
-  const float lr = s.lr_tensor ? *s.lr_tensor : s.lr;
-  const double bc1 = 1.0 - pow(double(s.beta1), double(step));
-  const double bc2 = 1.0 - pow(double(s.beta2), double(step));
-  const float step_size = float(double(lr) / bc1);
+  const double step = double(*a.step[t]);
+  const double lr = s.lr_tensor ? double(*s.lr_tensor) : s.lr;
+  const double bc1 = 1.0 - pow(s.beta1, step);
+  const double bc2 = 1.0 - pow(s.beta2, step);
+  const float step_size = float(lr / bc1);
   const float bc2_sqrt = float(sqrt(bc2));
-  const float inv_scale = s.grad_scale ? 1.f / *s.grad_scale : 1.f;
+  const float omb1 = float(1.0 - s.beta1), omb2 = float(1.0 - s.beta2), b2 = float(s.beta2);
+  const float wd = float(s.wd), eps = float(s.eps);
+  const float decay = float(1.0 - lr * s.wd);
+  const float gscale = s.grad_scale ? *s.grad_scale : 1.f;
   void* P_ = a.param[t];
   const void* G_ = a.grad[t];
   void* M_ = a.m[t];
@@ -81,26 +88,26 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
   void* X_ = a.vmax[t];
   for (long long i = begin + threadIdx.x; i < end; i += kThreads) {
     float g = ld<P>(G_, i);
-    if (s.grad_scale) g *= inv_scale;
+    if (s.grad_scale) g = __fdiv_rn(g, gscale);
     if (s.maximize) g = -g;
     float p = ld<P>(P_, i);
-    if (s.wd != 0.f) {
+    if (s.wd != 0.0) {
       if (s.adamw)
-        p -= lr * s.wd * p;
+        p = __fmul_rn(p, decay);
       else
-        g += s.wd * p;
+        g = __fmaf_rn(wd, p, g);
     }
     float m = ld<S>(M_, i);
     float v = ld<S>(V_, i);
-    m = m + (1.f - s.beta1) * (g - m);
-    v = s.beta2 * v + (1.f - s.beta2) * g * g;
+    m = __fmaf_rn(omb1, __fsub_rn(g, m), m);
+    v = __fmaf_rn(__fmul_rn(omb2, g), g, __fmul_rn(b2, v));
     float vv = v;
     if (s.amsgrad) {
       vv = fmaxf(ld<S>(X_, i), v);
       st<S>(X_, i, vv);
     }
-    const float denom = sqrtf(vv) / bc2_sqrt + s.eps;
-    p -= step_size * m / denom;
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vv), bc2_sqrt), eps);
+    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(step_size, m), denom));
     st<P>(P_, i, p);
     st<S>(M_, i, m);
     st<S>(V_, i, v);
@@ -120,11 +127,11 @@ extern "C" b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n, const b
     return set_error(B2_ERR_INVALID, "b2_fused_adam: dtype");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   AdamScalars sc{};
-  sc.lr = float(hp->lr);
-  sc.beta1 = float(hp->beta1);
-  sc.beta2 = float(hp->beta2);
-  sc.wd = float(hp->weight_decay);
-  sc.eps = float(hp->eps);
+  sc.lr = hp->lr;
+  sc.beta1 = hp->beta1;
+  sc.beta2 = hp->beta2;
+  sc.wd = hp->weight_decay;
+  sc.eps = hp->eps;
   sc.amsgrad = hp->amsgrad;
   sc.maximize = hp->maximize;
   sc.adamw = hp->adamw;

@@ -29,8 +29,8 @@ __global__ void sqdiff_kernel(const uint16_t* __restrict__ a, const uint16_t* __
   float acc = 0.f;
   for (long long i = blockIdx.x * (long long)kThreads + threadIdx.x; i < n;
        i += (long long)gridDim.x * kThreads) {
-    const float d = bf2f(a[i]) - bf2f(b[i]);
-    acc += d * d;
+    const float d = __fsub_rn(bf2f(a[i]), bf2f(b[i]));
+    acc = __fmaf_rn(d, d, acc);
   }
   double dacc = acc;
 #pragma unroll
@@ -110,8 +110,9 @@ __global__ void addtap_kernel(const uint16_t* __restrict__ base, const uint16_t*
                               long long n, float scale) {
   for (long long i = blockIdx.x * (long long)kThreads + threadIdx.x; i < n;
        i += (long long)gridDim.x * kThreads) {
-    const float t = scale * (bf2f(a[i]) - bf2f(b[i]));
-    out[i] = f2bf(base ? bf2f(base[i]) + t : t);
+    // no fma contraction: the reference rounds the product and the sum apart
+    const float t = __fmul_rn(scale, __fsub_rn(bf2f(a[i]), bf2f(b[i])));
+    out[i] = f2bf(base ? __fadd_rn(bf2f(base[i]), t) : t);
   }
 }
 
@@ -122,7 +123,7 @@ __global__ void relu_bwd_kernel(const uint16_t* __restrict__ r, const uint16_t* 
        i += (long long)gridDim.x * kThreads) {
     float g = 0.0f;
     if (base) g = bf2f(base[i]);
-    if (a) g += scale * (bf2f(a[i]) - bf2f(b[i]));
+    if (a) g = __fadd_rn(g, __fmul_rn(scale, __fsub_rn(bf2f(a[i]), bf2f(b[i]))));
     out[i] = (bf2f(r[i]) <= 0.0f) ? uint16_t(0) : f2bf(g);
   }
 }

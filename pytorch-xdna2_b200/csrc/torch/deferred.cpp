@@ -1,0 +1,185 @@
+// Deferred weight gradients and packed-operand attachments.
+//
+// Semantics of the reference's DeferredHostJob / AsyncDwPolicy
+// (torch_xdna_device.cpp:299-482, 550-656, 1212-1250): convolution_backward
+// returns the weight gradient before computing it; the storage carries the
+// pending job; the first reader (the optimizer, a copy, any op) runs it; a
+// gradient freed unread drops its job without ever running it.  The job owns
+// snapshots of its operands (the packed X and dY rows), so later in-place
+// changes of x or dy do not leak into dW.
+//
+// On B200 "running" a job means enqueueing its wgrad kernel on the current
+// stream, so a reader never blocks the host; stream order makes every later
+// kernel see the finished gradient.  With XDNA_ASYNC_DW=1 (default) the
+// policy learns K = dX calls per optimizer step and, once two steps agree,
+// launches all pending jobs right after the K-th dX of a step instead of
+// waiting for a reader.
+#include <algorithm>
+#include <cstdlib>
+#include <unordered_map>
+#include <vector>
+
+#include "xdna.h"
+
+namespace xdna {
+
+std::atomic<int64_t> g_pending_jobs{0};
+
+namespace {
+
+struct Job {
+  std::function<void()> fn;
+  int64_t order = 0;
+};
+
+struct Attachment {
+  at::Tensor rows;
+  int64_t version = 0;
+  std::vector<int64_t> sizes, strides;
+  int64_t offset = 0;
+};
+
+std::mutex g_mu;
+std::unordered_map<void*, Job> g_jobs;               // storage data ptr -> pending job
+std::unordered_map<void*, Attachment> g_attach;      // storage data ptr -> packed rows
+int64_t g_order = 0;
+int64_t g_started = 0, g_dropped = 0, g_kicks = 0, g_deferred = 0;
+int64_t g_dx_this_step = 0, g_k_prev = -1, g_k_learned = 0;
+
+bool async_enabled() {
+  static const bool on = [] {
+    const char* s = std::getenv("XDNA_ASYNC_DW");
+    return !s || std::string(s) != "0";
+  }();
+  return on;
+}
+
+void run_job(std::function<void()>& fn) {
+  fn();
+}
+
+}  // namespace
+
+// Entries are always moved out of the tables before they are destroyed:
+// destroying a job or an attachment frees tensors, and the allocator's release
+// hook (on_release) takes g_mu again.
+void defer_write(const at::Tensor& target, std::function<void()> job) {
+  void* key = target.storage().mutable_data();
+  Job old;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_jobs.find(key);
+    if (it != g_jobs.end()) old = std::move(it->second);
+    g_jobs[key] = Job{std::move(job), g_order++};
+    ++g_deferred;
+    g_pending_jobs.store(int64_t(g_jobs.size()));
+  }
+}
+
+void materialize(const at::Tensor& t) {
+  if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
+  void* key = t.storage().mutable_data();
+  std::function<void()> fn;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_jobs.find(key);
+    if (it == g_jobs.end()) return;
+    fn = std::move(it->second.fn);
+    g_jobs.erase(it);
+    ++g_started;
+    g_pending_jobs.store(int64_t(g_jobs.size()));
+  }
+  run_job(fn);
+}
+
+bool has_pending(const at::Tensor& t) {
+  if (g_pending_jobs.load() == 0 || !t.defined() || !t.has_storage()) return false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_jobs.count(t.storage().mutable_data()) != 0;
+}
+
+void materialize_all() {
+  std::vector<std::pair<int64_t, std::function<void()>>> fns;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto& kv : g_jobs) fns.emplace_back(kv.second.order, std::move(kv.second.fn));
+    g_started += int64_t(g_jobs.size());
+    g_jobs.clear();
+    g_pending_jobs.store(0);
+  }
+  std::sort(fns.begin(), fns.end(), [](auto& a, auto& b) { return a.first < b.first; });
+  for (auto& f : fns) run_job(f.second);
+}
+
+void on_release(void* ptr) {
+  if (!ptr) return;
+  Job dropped;
+  Attachment att;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_jobs.find(ptr);
+    if (it != g_jobs.end()) {
+      dropped = std::move(it->second);
+      g_jobs.erase(it);
+      ++g_dropped;
+      g_pending_jobs.store(int64_t(g_jobs.size()));
+    }
+    auto at = g_attach.find(ptr);
+    if (at != g_attach.end()) {
+      att = std::move(at->second);
+      g_attach.erase(at);
+    }
+  }
+}
+
+void note_dgrad() {
+  bool kick = false;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    ++g_dx_this_step;
+    kick = async_enabled() && g_k_learned > 0 && g_dx_this_step == g_k_learned && !g_jobs.empty();
+    if (kick) ++g_kicks;
+  }
+  if (kick) materialize_all();
+}
+
+void note_optimizer_step() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_dx_this_step > 0) {
+    if (g_dx_this_step == g_k_prev) g_k_learned = g_dx_this_step;
+    g_k_prev = g_dx_this_step;
+  }
+  g_dx_this_step = 0;
+}
+
+std::map<std::string, int64_t> deferred_stats() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  return {{"pending", int64_t(g_jobs.size())}, {"deferred", g_deferred}, {"started", g_started},
+          {"dropped", g_dropped},          {"kicks", g_kicks},       {"k_learned", g_k_learned},
+          {"attached_rows", int64_t(g_attach.size())}};
+}
+
+void attach_rows(const at::Tensor& input, const at::Tensor& rows) {
+  if (!input.has_storage()) return;
+  Attachment old;
+  Attachment fresh{rows, int64_t(input._version()), input.sizes().vec(), input.strides().vec(),
+                   input.storage_offset()};
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto& slot = g_attach[input.storage().mutable_data()];
+  old = std::move(slot);
+  slot = std::move(fresh);
+}
+
+at::Tensor find_rows(const at::Tensor& input) {
+  if (!input.has_storage()) return {};
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_attach.find(input.storage().mutable_data());
+  if (it == g_attach.end()) return {};
+  const Attachment& a = it->second;
+  if (a.version != int64_t(input._version()) || a.sizes != input.sizes().vec() ||
+      a.strides != input.strides().vec() || a.offset != input.storage_offset())
+    return {};
+  return a.rows;
+}
+
+}  // namespace xdna

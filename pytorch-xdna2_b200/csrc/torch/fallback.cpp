@@ -1,0 +1,184 @@
+// Boxed fallback for every aten op without an `xdna` kernel.
+//
+// The reference runs such ops as stock ATen CPU kernels on zero-copy CPU
+// aliases of its host-mapped buffers (zero_copy_cpu_fallback,
+// torch_xdna_device.cpp:5124-5260).  Here xdna memory is HBM, so the same idea
+// maps every xdna tensor argument to a zero-copy CUDA alias and redispatches to
+// ATen's CUDA kernel: non-hot ops (BatchNorm, activations, pooling, losses,
+// elementwise, reductions, factories) stay on the GPU with no copies.
+//   * pending deferred writes of every xdna argument are materialized first;
+//   * mutated arguments (in-place / out=) are written through the alias; if the
+//     op re-allocated an out= tensor, the new memory is adopted back;
+//   * returns that alias an argument come back as views of the original xdna
+//     storage; fresh results are adopted (xdna storage over the CUDA block).
+// Every call is counted per op (fallback_stats); the hot-path ops never come
+// here (tests assert their counters stay zero).
+#include <ATen/core/dispatch/Dispatcher.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <unordered_map>
+
+#include "xdna.h"
+
+namespace xdna {
+namespace {
+
+struct ArgMap {
+  // CUDA alias storage impl -> original xdna tensor (for view/alias returns)
+  std::vector<std::pair<c10::StorageImpl*, at::Tensor>> storages;
+};
+
+c10::IValue convert_in(const c10::IValue& v, ArgMap& map, c10::DeviceIndex& dev) {
+  if (v.isTensor()) {
+    const at::Tensor& t = v.toTensor();
+    if (t.defined() && t.device().type() == kXdna) {
+      dev = t.device().index();
+      at::Tensor c = to_cuda(t);
+      map.storages.emplace_back(c.storage().unsafeGetStorageImpl(), t);
+      return c;
+    }
+    return v;
+  }
+  if (v.isTensorList()) {
+    auto list = v.toTensorList();
+    c10::List<at::Tensor> out;
+    out.reserve(list.size());
+    for (const at::Tensor& t : list) {
+      if (t.defined() && t.device().type() == kXdna) {
+        dev = t.device().index();
+        at::Tensor c = to_cuda(t);
+        map.storages.emplace_back(c.storage().unsafeGetStorageImpl(), t);
+        out.push_back(c);
+      } else {
+        out.push_back(t);
+      }
+    }
+    return out;
+  }
+  if (v.isOptionalTensorList()) {
+    auto list = v.toOptionalTensorList();
+    c10::List<std::optional<at::Tensor>> out;
+    for (const std::optional<at::Tensor>& ot : list) {
+      if (ot.has_value() && ot->defined() && ot->device().type() == kXdna) {
+        dev = ot->device().index();
+        out.push_back(std::optional<at::Tensor>(to_cuda(*ot)));
+      } else {
+        out.push_back(ot);
+      }
+    }
+    return out;
+  }
+  if (v.isDevice()) {
+    c10::Device d = v.toDevice();
+    if (d.type() == kXdna) {
+      if (d.has_index()) dev = d.index();
+      return c10::Device(c10::DeviceType::CUDA, d.has_index() ? d.index() : dev);
+    }
+    return v;
+  }
+  return v;
+}
+
+at::Tensor convert_out(const at::Tensor& r, const ArgMap& map) {
+  if (!r.defined() || r.device().type() != c10::DeviceType::CUDA) return r;
+  c10::StorageImpl* si = r.storage().unsafeGetStorageImpl();
+  for (const auto& kv : map.storages) {
+    if (kv.first == si) {
+      // a view of an argument: same xdna storage, the result's geometry
+      at::Tensor v = at::detail::make_tensor<c10::TensorImpl>(c10::Storage(kv.second.storage()),
+                                                              kv.second.key_set(), r.dtype());
+      v.unsafeGetTensorImpl()->set_sizes_and_strides(r.sizes(), r.strides(), r.storage_offset());
+      return v;
+    }
+  }
+  return adopt(r);
+}
+
+// After an op wrote through the alias of `orig`: if the alias was resized or
+// re-pointed (out= resize), carry that back to the xdna tensor.
+void sync_back(const at::Tensor& orig, const at::Tensor& alias) {
+  auto* oi = orig.unsafeGetTensorImpl();
+  if (alias.storage().mutable_data() != orig.storage().mutable_data() ||
+      alias.storage().nbytes() != orig.storage().nbytes()) {
+    at::Tensor adopted = adopt(alias);
+    oi->set_storage_keep_dtype(adopted.storage());
+  }
+  if (alias.sizes() != orig.sizes() || alias.strides() != orig.strides() ||
+      alias.storage_offset() != orig.storage_offset())
+    oi->set_sizes_and_strides(alias.sizes(), alias.strides(), alias.storage_offset());
+}
+
+void cuda_alias_fallback(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
+  const auto& schema = op.schema();
+  const size_t nargs = schema.arguments().size();
+  const size_t nret = schema.returns().size();
+  count_fallback(schema.operator_name().name + (schema.overload_name().empty() ? "" : "." + schema.overload_name()));
+
+  ArgMap map;
+  c10::DeviceIndex dev = -1;
+  auto args_begin = stack->end() - nargs;
+  std::vector<c10::IValue> originals(args_begin, stack->end());
+  for (size_t i = 0; i < nargs; ++i) args_begin[i] = convert_in(args_begin[i], map, dev);
+  // aliases of mutated arguments, to sync back after the call
+  std::vector<std::pair<size_t, c10::IValue>> written;
+  for (size_t i = 0; i < nargs; ++i) {
+    const auto* ai = schema.arguments()[i].alias_info();
+    if (ai && ai->isWrite()) written.emplace_back(i, args_begin[i]);
+  }
+
+  {
+    c10::cuda::OptionalCUDAGuard g;
+    if (dev >= 0) g.set_index(dev);
+    op.callBoxed(stack);
+  }
+
+  for (auto& w : written) {
+    const c10::IValue& o = originals[w.first];
+    if (o.isTensor() && o.toTensor().defined() && o.toTensor().device().type() == kXdna)
+      sync_back(o.toTensor(), w.second.toTensor());
+    else if (o.isTensorList()) {
+      auto ol = o.toTensorList();
+      auto al = w.second.toTensorList();
+      for (size_t k = 0; k < ol.size(); ++k) {
+        const at::Tensor& ot = ol[k];
+        if (ot.defined() && ot.device().type() == kXdna) sync_back(ot, al[k]);
+      }
+    }
+  }
+
+  auto rets_begin = stack->end() - nret;
+  for (size_t i = 0; i < nret; ++i) {
+    const auto* ai = schema.returns()[i].alias_info();
+    c10::IValue& r = rets_begin[i];
+    if (ai && ai->isWrite()) {
+      // in-place / out=: return the original argument with the same alias set
+      bool done = false;
+      for (size_t a = 0; a < nargs && !done; ++a) {
+        const auto* aa = schema.arguments()[a].alias_info();
+        if (aa && aa->beforeSets() == ai->beforeSets()) {
+          r = originals[a];
+          done = true;
+        }
+      }
+      if (done) continue;
+    }
+    if (r.isTensor()) {
+      r = convert_out(r.toTensor(), map);
+    } else if (r.isTensorList()) {
+      auto list = r.toTensorList();
+      c10::List<at::Tensor> out;
+      out.reserve(list.size());
+      for (const at::Tensor& t : list) out.push_back(convert_out(t, map));
+      r = out;
+    }
+  }
+}
+
+}  // namespace
+
+TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {
+  m.fallback(torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>());
+}
+
+}  // namespace xdna

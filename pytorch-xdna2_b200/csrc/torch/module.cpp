@@ -1,0 +1,207 @@
+// Python module `xdna_train._C`: device queries, modes, statistics, the
+// deferred-gradient controls, CUDA aliases for NCCL, and the region kernels.
+// Mirrors the reference's pybind surface (torch_xdna_device.cpp:5346-5767) for
+// the functions the hot path and xdna_train's Python API use.
+#include <c10/cuda/CUDACachingAllocator.h>
+#include <c10/cuda/CUDAFunctions.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstdlib>
+
+#include "xdna.h"
+
+namespace xdna {
+
+void register_hooks();  // guard.cpp
+
+std::atomic<int> g_mode{[] {
+  const char* s = std::getenv("XDNA_NPU_MODE");
+  return s ? std::atoi(s) : 2;
+}()};
+
+namespace {
+std::mutex g_stat_mu;
+std::map<std::string, int64_t> g_launches, g_fallbacks;
+}  // namespace
+
+void count_launch(const char* what, int64_t n) {
+  std::lock_guard<std::mutex> lk(g_stat_mu);
+  g_launches[what] += n;
+}
+void count_fallback(const std::string& op) {
+  std::lock_guard<std::mutex> lk(g_stat_mu);
+  g_fallbacks[op] += 1;
+}
+std::map<std::string, int64_t> launch_stats() {
+  std::lock_guard<std::mutex> lk(g_stat_mu);
+  return g_launches;
+}
+std::map<std::string, int64_t> fallback_stats() {
+  std::lock_guard<std::mutex> lk(g_stat_mu);
+  return g_fallbacks;
+}
+void reset_stats() {
+  std::lock_guard<std::mutex> lk(g_stat_mu);
+  g_launches.clear();
+  g_fallbacks.clear();
+}
+
+namespace {
+
+void check_bf16(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.device().type() == kXdna && t.scalar_type() == at::kBFloat16 && t.is_contiguous(),
+              "xdna region kernel: ", what, " must be a contiguous bf16 xdna tensor");
+}
+const void* opt_ptr(const std::optional<at::Tensor>& t, const char* what) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  check_bf16(*t, what);
+  materialize(*t);
+  return t->data_ptr();
+}
+
+double region_sqdiff_sum(const at::Tensor& a, const at::Tensor& b) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  TORCH_CHECK(a.numel() == b.numel(), "region_sqdiff_sum: size mismatch");
+  materialize(a);
+  materialize(b);
+  c10::cuda::CUDAGuard g(a.device().index());
+  at::Tensor acc = empty({1}, at::kDouble, a.device().index());
+  XDNA_B2(b2_region_sqdiff_sum_bf16(a.data_ptr(), b.data_ptr(), a.numel(), acc.data_ptr<double>(),
+                                    stream(a.device().index())));
+  count_launch("region.sqdiff_sum");
+  return to_cuda(acc).item<double>();
+}
+
+void region_relu(const at::Tensor& a, const at::Tensor& r) {
+  check_bf16(a, "a");
+  check_bf16(r, "r");
+  materialize(a);
+  c10::cuda::CUDAGuard g(a.device().index());
+  XDNA_B2(b2_region_relu_bf16(a.data_ptr(), r.data_ptr(), a.numel(), stream(a.device().index())));
+  count_launch("region.relu");
+}
+
+void region_relu_maxpool2(const at::Tensor& a, const at::Tensor& r, const at::Tensor& p) {
+  check_bf16(a, "a");
+  check_bf16(r, "r");
+  check_bf16(p, "p");
+  TORCH_CHECK(a.dim() == 4, "region_relu_maxpool2: NCHW input expected");
+  materialize(a);
+  c10::cuda::CUDAGuard g(a.device().index());
+  XDNA_B2(b2_region_relu_maxpool2_bf16(a.data_ptr(), r.data_ptr(), p.data_ptr(), a.size(0) * a.size(1), a.size(2),
+                                       a.size(3), stream(a.device().index())));
+  count_launch("region.relu_maxpool2");
+}
+
+void region_addtap(const std::optional<at::Tensor>& base, const at::Tensor& a, const at::Tensor& b,
+                   const at::Tensor& out, double scale) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  check_bf16(out, "out");
+  materialize(a);
+  materialize(b);
+  c10::cuda::CUDAGuard g(a.device().index());
+  XDNA_B2(b2_region_addtap_bf16(opt_ptr(base, "base"), a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(),
+                                float(scale), stream(a.device().index())));
+  count_launch("region.addtap");
+}
+
+void region_relu_bwd(const at::Tensor& r, const std::optional<at::Tensor>& base, const std::optional<at::Tensor>& a,
+                     const std::optional<at::Tensor>& b, const at::Tensor& out, double scale) {
+  check_bf16(r, "r");
+  check_bf16(out, "out");
+  materialize(r);
+  c10::cuda::CUDAGuard g(r.device().index());
+  XDNA_B2(b2_region_relu_bwd_bf16(r.data_ptr(), opt_ptr(base, "base"), opt_ptr(a, "a"), opt_ptr(b, "b"),
+                                  out.data_ptr(), r.numel(), float(scale), stream(r.device().index())));
+  count_launch("region.relu_bwd");
+}
+
+void region_maxpool2_bwd(const at::Tensor& x, const at::Tensor& gr, const at::Tensor& out) {
+  check_bf16(x, "x");
+  check_bf16(gr, "g");
+  check_bf16(out, "out");
+  TORCH_CHECK(x.dim() == 4, "region_maxpool2_bwd: NCHW input expected");
+  materialize(x);
+  materialize(gr);
+  c10::cuda::CUDAGuard g(x.device().index());
+  XDNA_B2(b2_region_maxpool2_bwd_bf16(x.data_ptr(), gr.data_ptr(), out.data_ptr(), x.size(0) * x.size(1), x.size(2),
+                                      x.size(3), stream(x.device().index())));
+  count_launch("region.maxpool2_bwd");
+}
+
+py::dict to_dict(const std::map<std::string, int64_t>& m) {
+  py::dict d;
+  for (auto& kv : m) d[py::str(kv.first)] = kv.second;
+  return d;
+}
+
+}  // namespace
+}  // namespace xdna
+
+PYBIND11_MODULE(_C, m) {
+  using namespace xdna;
+  register_hooks();
+  m.doc() = "xdna device on NVIDIA B200 (PrivateUse1 over CUDA, sm_100a kernels in libxdna_b200.so)";
+  m.def("abi_version", [] { return b2_abi_version(); });
+  m.def("is_available", [] { return c10::cuda::device_count() > 0; });
+  m.def("device_count", [] { return int(c10::cuda::device_count()); });
+  m.def("current_device", [] { return int(c10::cuda::current_device()); });
+  m.def("set_device", [](int d) { c10::cuda::set_device(c10::DeviceIndex(d)); });
+  m.def(
+      "synchronize",
+      [](int d) {
+        py::gil_scoped_release nogil;
+        if (d < 0) d = c10::cuda::current_device();
+        c10::cuda::CUDAGuard g(c10::DeviceIndex(d));
+        XDNA_CUDA(cudaDeviceSynchronize());
+      },
+      py::arg("device") = -1);
+  m.def("empty_cache", [] {
+    empty_cache();
+    c10::cuda::CUDACachingAllocator::emptyCache();
+  });
+  m.def("allocator_stats", [] { return to_dict(allocator_stats()); });
+  m.def("fallback_stats", [] {
+    py::dict d;
+    for (auto& kv : fallback_stats()) {
+      py::dict e;
+      e["calls"] = kv.second;
+      d[py::str(kv.first)] = e;
+    }
+    return d;
+  });
+  m.def("launch_stats", [] { return to_dict(launch_stats()); });
+  m.def("reset_stats", [] { reset_stats(); });
+  m.def("set_npu_mode", [](int mode) {
+    TORCH_CHECK(mode >= 0 && mode <= 2, "npu mode must be 0, 1 or 2");
+    g_mode.store(mode);
+  });
+  m.def("npu_mode", [] { return g_mode.load(); });
+  m.def("async_dw_stats", [] { return to_dict(deferred_stats()); });
+  m.def("materialize", [](const at::Tensor& t) { materialize(t); });
+  m.def("materialize_all", [] { materialize_all(); });
+  m.def("has_pending", [](const at::Tensor& t) { return has_pending(t); });
+  m.def("optimizer_step_boundary", [] { note_optimizer_step(); });
+  m.def("as_cuda", [](const at::Tensor& t) {
+    TORCH_CHECK(t.device().type() == kXdna, "as_cuda: expected an xdna tensor");
+    return to_cuda(t);
+  });
+  m.def("adopt", [](const at::Tensor& t) {
+    TORCH_CHECK(t.device().type() == c10::DeviceType::CUDA, "adopt: expected a CUDA tensor");
+    return adopt(t);
+  });
+  m.def("device_status", [](int d) {
+    int code = 0;
+    XDNA_B2(b2_device_status(d, &code));
+    return code;
+  });
+  m.def("region_sqdiff_sum", &region_sqdiff_sum);
+  m.def("region_relu", &region_relu);
+  m.def("region_relu_maxpool2", &region_relu_maxpool2);
+  m.def("region_addtap", &region_addtap);
+  m.def("region_relu_bwd", &region_relu_bwd);
+  m.def("region_maxpool2_bwd", &region_maxpool2_bwd);
+}

@@ -1,0 +1,92 @@
+// Shared declarations of the `xdna` PrivateUse1 backend (B200 edition).
+//
+// The device is a CUDA device under another name: `xdna:i` is `cuda:i`, its
+// streams and events are CUDA streams and events, its storage is HBM from a
+// stream-ordered caching allocator, and the hot ops run the sm_100a kernels of
+// libxdna_b200.so (include/b2.h).  Everything else runs ATen's CUDA kernels on
+// zero-copy CUDA aliases of the same memory (the B200 counterpart of the
+// reference's zero-copy CPU fallback, torch_xdna_device.cpp:5117-5260).
+#pragma once
+
+#include <ATen/ATen.h>
+#include <c10/core/Allocator.h>
+#include <c10/cuda/CUDAStream.h>
+#include <cuda_runtime_api.h>
+
+#include <atomic>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+
+#include "b2.h"
+
+namespace xdna {
+
+constexpr c10::DeviceType kXdna = c10::DeviceType::PrivateUse1;
+
+// ---- errors ------------------------------------------------------------
+#define XDNA_B2(call)                                                              \
+  do {                                                                             \
+    b2_status _st = (call);                                                        \
+    TORCH_CHECK(_st == B2_OK, "xdna: ", #call, " failed (", _st, "): ", b2_last_error()); \
+  } while (0)
+
+#define XDNA_CUDA(call)                                                            \
+  do {                                                                             \
+    cudaError_t _e = (call);                                                       \
+    TORCH_CHECK(_e == cudaSuccess, "xdna: ", #call, ": ", cudaGetErrorString(_e)); \
+  } while (0)
+
+// ---- allocator (allocator.cpp) -------------------------------------------
+c10::Allocator* allocator();
+void record_stream(const c10::DataPtr& ptr, cudaStream_t stream);
+void empty_cache();
+std::map<std::string, int64_t> allocator_stats();
+// Called by the allocator when a block is released; drops deferred work and
+// packed-operand attachments keyed on that address.
+void on_release(void* ptr);
+
+// ---- tensors / streams (tensor_ops.cpp) -----------------------------------
+cudaStream_t stream(c10::DeviceIndex device);  // current CUDA stream of xdna:device
+at::Tensor empty(at::IntArrayRef size, at::ScalarType dtype, c10::DeviceIndex device,
+                 c10::MemoryFormat mf = c10::MemoryFormat::Contiguous);
+// Zero-copy CUDA view of an xdna tensor (same bytes, sizes, strides, offset).
+// Materializes deferred writes into that storage first.
+at::Tensor to_cuda(const at::Tensor& t);
+at::Tensor to_cuda_nosync(const at::Tensor& t);
+// xdna tensor over the memory of a CUDA tensor (the xdna storage keeps the
+// CUDA storage alive).
+at::Tensor adopt(const at::Tensor& cuda_tensor);
+
+// ---- deferred weight gradients (deferred.cpp) -----------------------------
+// A job produces the contents of one storage.  Readers run it first; freeing
+// the storage before anyone read it drops it unrun (reference semantics,
+// torch_xdna_device.cpp:299-482, 550-656).
+void defer_write(const at::Tensor& target, std::function<void()> job);
+void materialize(const at::Tensor& t);  // no-op unless t's storage has a pending job
+void materialize_all();
+bool has_pending(const at::Tensor& t);
+void note_dgrad();           // one dX computed (async policy bookkeeping)
+void note_optimizer_step();  // step boundary
+std::map<std::string, int64_t> deferred_stats();
+extern std::atomic<int64_t> g_pending_jobs;
+
+// Packed padded-grid rows of a conv input, attached to the input's storage by
+// the forward so the weight gradient reuses them (reference: packed X attached
+// to the allocation, torch_xdna_device.cpp:1968-1985).
+void attach_rows(const at::Tensor& input, const at::Tensor& rows);
+at::Tensor find_rows(const at::Tensor& input);
+
+// ---- modes and counters (module.cpp) --------------------------------------
+// 2: all hot-path kernels; 1: weight gradients through the CUDA-alias path;
+// 0: every hot op through the CUDA-alias path (A/B switch, set_npu_mode).
+extern std::atomic<int> g_mode;
+void count_launch(const char* what, int64_t n = 1);
+void count_fallback(const std::string& op);
+std::map<std::string, int64_t> launch_stats();
+std::map<std::string, int64_t> fallback_stats();
+void reset_stats();
+
+}  // namespace xdna

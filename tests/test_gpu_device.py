@@ -1,0 +1,340 @@
+"""The `xdna` device end to end on a B200: registration, tensor semantics, the
+hot ops through the dispatcher (checked against the reference's CPU BF16
+path: stock PyTorch CPU ops on the same seeded inputs), deferred weight
+gradients, autocast, the fused optimizer and the perceptual-loss region.
+
+Every hot-path test also asserts that the native kernels ran (launch
+counters) and that the op never took the CUDA-alias fallback -- the
+reference's "cannot pass vacuously" rule (its tests check mapped_cpu_stats).
+"""
+import copy
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import xdna_train
+from xdna_train import regions
+
+pytestmark = pytest.mark.gpu
+
+X = torch.device("xdna")
+
+
+@pytest.fixture(autouse=True)
+def _fresh_stats(cuda):
+    xdna_train.register_xdna_device()
+    xdna_train.set_npu_mode(2)
+    xdna_train.reset_fallback_stats()
+    yield
+
+
+def close(got, ref, tol=2e-2):
+    got, ref = got.detach().float().cpu(), ref.detach().float().cpu()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    assert err <= tol * scale + 1e-6, f"max abs err {err} vs scale {scale}"
+
+
+def launched(kind):
+    return xdna_train.kernel_stats().get(kind, 0)
+
+
+def no_fallback(*ops):
+    fb = xdna_train.fallback_stats()
+    for op in ops:
+        assert op not in fb, f"{op} took the CUDA-alias fallback: {fb}"
+
+
+# ------------------------------------------------------------- tensor semantics
+
+def test_registration_and_module():
+    assert torch._C._get_privateuse1_backend_name() == "xdna"
+    assert torch.xdna.is_available() and torch.xdna.device_count() >= 1
+    t = torch.ones(3, device="xdna")
+    assert t.device.type == "xdna" and t.is_xdna
+    assert xdna_train.is_xrt_backed(t)
+
+
+def test_copies_views_resize_set():
+    a = torch.arange(24, dtype=torch.float32).reshape(2, 3, 4)
+    x = a.to(X)
+    assert torch.equal(x.cpu(), a)
+    assert torch.equal(x.transpose(0, 2).cpu(), a.transpose(0, 2))
+    assert torch.equal(x[:, 1:, ::2].cpu(), a[:, 1:, ::2])
+    assert torch.equal(x.view(6, 4).cpu(), a.view(6, 4))
+    assert torch.equal(x.to(torch.bfloat16).cpu(), a.to(torch.bfloat16))
+    y = x.clone()
+    y.add_(1)
+    assert torch.equal(y.cpu(), a + 1) and torch.equal(x.cpu(), a)
+    y.resize_(50)
+    assert y.numel() == 50 and torch.equal(y[:24].cpu(), (a + 1).reshape(-1))
+    z = torch.empty(0, device=X)
+    z.set_(x)
+    assert torch.equal(z.cpu(), a)
+    assert x.sum().item() == a.sum().item()
+    cl = x.reshape(1, 2, 3, 4).contiguous(memory_format=torch.channels_last)
+    assert torch.equal(cl.cpu(), a.reshape(1, 2, 3, 4))
+    s = torch.randn(5, 5, device=X)
+    assert "xdna" in repr(s)
+
+
+def test_factories_and_random_ops():
+    torch.manual_seed(0)
+    r = torch.randn(1000, device=X)
+    assert r.device.type == "xdna" and 0.8 < r.std().item() < 1.2
+    z = torch.zeros(4, 5, device=X, dtype=torch.bfloat16)
+    assert z.dtype == torch.bfloat16 and z.abs().sum().item() == 0
+    assert torch.equal(torch.arange(7, device=X).cpu(), torch.arange(7))
+
+
+# ------------------------------------------------------------------ conv3x3
+
+def _conv_case(B, Cin, H, W, Cout, bias, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, Cin, H, W, generator=g).bfloat16()
+    conv = nn.Conv2d(Cin, Cout, 3, padding=1, bias=bias)
+    with torch.no_grad():
+        conv.weight.copy_((torch.rand(Cout, Cin, 3, 3, generator=g) * 2 - 1) * (1.0 / (9 * Cin)) ** 0.5)
+        if bias:
+            conv.bias.copy_(torch.randn(Cout, generator=g) * 0.1)
+    dy = torch.randn(B, Cout, H, W, generator=g).bfloat16()
+    return x, conv.bfloat16(), dy
+
+
+@pytest.mark.parametrize("shape", [(16, 128, 36, 36, 128, True), (4, 70, 12, 37, 64, False),
+                                   (2, 256, 18, 18, 512, True), (3, 3, 5, 7, 10, True)])
+@pytest.mark.parametrize("channels_last", [False, True])
+def test_conv_fwd_bwd_vs_reference_cpu_path(shape, channels_last):
+    x, conv, dy = _conv_case(*shape)
+    # the reference's CPU BF16 path: stock ATen CPU kernels on the same values
+    xc = x.clone().requires_grad_()
+    cc = copy.deepcopy(conv)
+    yc = cc(xc)
+    yc.backward(dy)
+    # xdna
+    cx = copy.deepcopy(conv).to(X)
+    xx = x.to(X)
+    if channels_last:
+        xx = xx.contiguous(memory_format=torch.channels_last)
+    xx.requires_grad_()
+    y = cx(xx)
+    if channels_last:
+        assert y.is_contiguous(memory_format=torch.channels_last)
+    y.backward(dy.to(X))
+    close(y, yc)
+    close(xx.grad, xc.grad)
+    close(cx.weight.grad, cc.weight.grad)
+    if shape[5]:
+        close(cx.bias.grad, cc.bias.grad)
+    assert launched("conv3x3.fwd") >= 1 and launched("conv3x3.dgrad") >= 1 and launched("conv3x3.wgrad") >= 1
+    no_fallback("convolution_overrideable", "convolution_backward_overrideable")
+
+
+def test_non3x3_conv_takes_cuda_path():
+    conv = nn.Conv2d(8, 16, 1).bfloat16().to(X)
+    x = torch.randn(2, 8, 5, 5, dtype=torch.bfloat16, device=X)
+    y = conv(x)
+    ref = F.conv2d(x.cpu().float(), conv.weight.cpu().float(), conv.bias.cpu().float())
+    close(y, ref)
+    assert "convolution_overrideable" in xdna_train.fallback_stats()
+
+
+def test_readme_training_step_matches_cpu():
+    """README example (shortened): losses of the xdna run
+    and the reference's CPU BF16 run from the same seed stay within 1 %."""
+    def run(device, steps=8):
+        torch.manual_seed(0)
+        model = nn.Conv2d(128, 128, 3, padding=1).bfloat16().to(device)
+        opt = torch.optim.Adam(model.parameters(), lr=1e-3)
+        g = torch.Generator().manual_seed(1)
+        x = torch.randn(16, 128, 36, 36, generator=g).bfloat16().to(device)
+        target = torch.zeros_like(x)
+        losses = []
+        for _ in range(steps):
+            opt.zero_grad(set_to_none=True)
+            loss = F.mse_loss(model(x).float(), target.float())
+            loss.backward()
+            opt.step()
+            losses.append(loss.item())
+        return losses, model
+    lc, mc = run("cpu")
+    lx, mx = run(X)
+    for a, b in zip(lx, lc):
+        assert abs(a - b) <= 0.01 * abs(b), (lx, lc)
+    close(mx.weight, mc.weight, tol=2e-2)
+    assert launched("fused_adam") >= 1
+    no_fallback("convolution_overrideable", "convolution_backward_overrideable", "_fused_adam_")
+
+
+# ------------------------------------------------------- deferred weight gradient
+
+def test_deferred_dw_semantics():
+    x, conv, dy = _conv_case(2, 64, 9, 9, 64, False, seed=4)
+    cx = copy.deepcopy(conv).to(X)
+    xx = x.to(X).requires_grad_()
+    dyx = dy.to(X)
+    before = xdna_train.async_dw_stats()
+    y = cx(xx)
+    y.backward(dyx)
+    st = xdna_train.async_dw_stats()
+    assert st["deferred"] == before["deferred"] + 1
+    # mutating the operands after backward must not change the deferred dW
+    with torch.no_grad():
+        xx.mul_(3.0)
+        dyx.zero_()
+    xc = x.clone().requires_grad_()
+    cc = copy.deepcopy(conv)
+    cc(xc).backward(dy)
+    close(cx.weight.grad, cc.weight.grad)  # reading materializes
+    # an unread gradient that is freed is dropped, never computed
+    cx.weight.grad = None
+    y = cx(x.to(X).requires_grad_())
+    y.backward(dy.to(X))
+    d0 = xdna_train.async_dw_stats()["dropped"]
+    cx.weight.grad = None
+    assert xdna_train.async_dw_stats()["dropped"] == d0 + 1
+
+
+def test_deferred_dw_materialized_by_optimizer_and_accumulation():
+    x, conv, dy = _conv_case(2, 64, 8, 8, 64, True, seed=5)
+    cx = copy.deepcopy(conv).to(X)
+    opt = torch.optim.SGD(cx.parameters(), lr=0.1)
+    for _ in range(2):  # two backward passes accumulate into .grad
+        cx(x.to(X).requires_grad_()).backward(dy.to(X))
+    cc = copy.deepcopy(conv)
+    for _ in range(2):
+        cc(x.clone().requires_grad_()).backward(dy)
+    close(cx.weight.grad, cc.weight.grad)
+    opt.step()
+    assert xdna_train.async_dw_stats()["pending"] == 0
+
+
+# ------------------------------------------------------------------- GEMMs
+
+def test_linear_mlp_mm_addmm_vs_cpu():
+    torch.manual_seed(0)
+    mlp = nn.Sequential(nn.Linear(256, 512), nn.GELU(), nn.Linear(512, 128)).bfloat16()
+    x = torch.randn(64, 256).bfloat16()
+    xc = x.clone().requires_grad_()
+    mc = copy.deepcopy(mlp)
+    yc = mc(xc)
+    yc.float().square().mean().backward()
+    mx = copy.deepcopy(mlp).to(X)
+    xx = x.to(X).requires_grad_()
+    y = mx(xx)
+    y.float().square().mean().backward()
+    close(y, yc)
+    close(xx.grad, xc.grad)
+    close(mx[0].weight.grad, mc[0].weight.grad)
+    close(mx[2].bias.grad, mc[2].bias.grad)
+    assert launched("gemm") >= 5
+    no_fallback("mm", "addmm", "addmm.out")
+
+
+def test_bmm_gram_matrix():
+    f = torch.randn(4, 64, 200).bfloat16()
+    gram_c = torch.bmm(f, f.transpose(1, 2))
+    fx = f.to(X)
+    gram = torch.bmm(fx, fx.transpose(1, 2))
+    close(gram, gram_c)
+    no_fallback("bmm", "bmm.out")
+
+
+# --------------------------------------------------------------- autocast
+
+def test_autocast_bf16_conv_linear():
+    torch.manual_seed(0)
+    conv = nn.Conv2d(64, 64, 3, padding=1)
+    lin = nn.Linear(64, 32)
+    x = torch.randn(2, 64, 8, 8)
+    with torch.autocast("cpu", dtype=torch.bfloat16):
+        yc = lin(conv(x).mean((2, 3)))
+    cx, lx = copy.deepcopy(conv).to(X), copy.deepcopy(lin).to(X)
+    with torch.autocast("xdna"):
+        h = cx(x.to(X))
+        assert h.dtype == torch.bfloat16
+        y = lx(h.mean((2, 3)))
+        assert y.dtype == torch.bfloat16
+    close(y, yc, tol=3e-2)
+    assert cx.weight.dtype == torch.float32
+    assert launched("conv3x3.fwd") >= 1 and launched("gemm") >= 1
+
+
+# ------------------------------------------------------------------ optimizer
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("cls", [torch.optim.Adam, torch.optim.AdamW])
+def test_fused_adam_through_torch_optim(dtype, cls):
+    torch.manual_seed(3)
+    ps = [torch.randn(n).to(dtype) for n in (10, 1000, 70000)]
+    gs = [torch.randn(n).to(dtype) for n in (10, 1000, 70000)]
+    pc = [nn.Parameter(p.clone()) for p in ps]
+    px = [nn.Parameter(p.clone().to(X)) for p in ps]
+    oc = cls(pc, lr=1e-2, weight_decay=0.01, fused=True)
+    ox = cls(px, lr=1e-2, weight_decay=0.01)  # the pre-hook turns fused on
+    for step in range(3):
+        for a, b, g in zip(pc, px, gs):
+            a.grad = (g * (step + 1)).clone()
+            b.grad = (g * (step + 1)).clone().to(X)
+        oc.step()
+        ox.step()
+    assert ox.param_groups[0]["fused"] is True
+    for a, b in zip(pc, px):
+        if dtype == torch.bfloat16:
+            assert torch.equal(a.detach(), b.detach().cpu())
+        else:
+            assert (a.detach() - b.detach().cpu()).abs().max().item() <= 1e-6
+    no_fallback("_fused_adam_", "_fused_adamw_")
+
+
+# -------------------------------------------------------------------- regions
+
+class _Feat(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.model = nn.Module()
+        self.model.features = nn.Sequential(
+            nn.Conv2d(3, 16, 3, padding=1), nn.ReLU(), nn.Conv2d(16, 16, 3, padding=1), nn.ReLU(),
+            nn.MaxPool2d(2), nn.Conv2d(16, 32, 3, padding=1), nn.ReLU())
+        self.feature_layers = (1, 3, 6)
+        self.use_norm = False
+
+
+class _Loss(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.perceptual_vgg = _Feat()
+
+    def compute_perceptual_loss(self, x, t):
+        feats_x, feats_t, h, g = [], [], x, t
+        for i, m in enumerate(self.perceptual_vgg.model.features):
+            h, g = m(h), m(g)
+            if i in self.perceptual_vgg.feature_layers:
+                feats_x.append(h.reshape(-1))
+                feats_t.append(g.reshape(-1))
+            if i >= max(self.perceptual_vgg.feature_layers):
+                break
+        return F.mse_loss(torch.cat(feats_x), torch.cat(feats_t))
+
+
+def test_fuse_perceptual_loss_matches_eager():
+    torch.manual_seed(0)
+    loss_mod = _Loss().bfloat16().to(X)
+    for p in loss_mod.parameters():
+        p.requires_grad_(False)
+    x = torch.rand(4, 3, 16, 16, dtype=torch.bfloat16, device=X)
+    t = torch.rand(4, 3, 16, 16, dtype=torch.bfloat16, device=X)
+    xe = x.clone().requires_grad_()
+    le = loss_mod.compute_perceptual_loss(xe, t)
+    le.backward()
+    fused = copy.deepcopy(loss_mod)
+    assert regions.fuse_perceptual_loss(fused)
+    xf = x.clone().requires_grad_()
+    lf = fused.compute_perceptual_loss(xf, t)
+    lf.backward()
+    assert abs(lf.item() - le.item()) <= 0.02 * abs(le.item())
+    close(xf.grad, xe.grad, tol=5e-2)
+    assert launched("region.relu_maxpool2") >= 1 and launched("region.sqdiff_sum") >= 1
+    assert launched("region.maxpool2_bwd") >= 1 and launched("region.relu_bwd") >= 1
