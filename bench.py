@@ -257,7 +257,7 @@ def kernel_times(x, dy, conv, local, iters=10):
     L = _abi.lib()
     X = x.device
     st = torch.cuda.current_stream().cuda_stream
-    B = x.shape[0]
+    B, C, HW = x.shape[0], x.shape[1], x.shape[2]
     ch = (C + 63) // 64
     rows = torch.empty(B * (HW + 2) * (HW + 2), ch * 64, dtype=torch.bfloat16, device=X)
     drows = torch.empty_like(rows)
@@ -284,7 +284,7 @@ def kernel_times(x, dy, conv, local, iters=10):
     }
     out = {}
     for name, fn in fns.items():
-        for _ in range(3):
+        for _ in range(2):
             _abi.check(fn(), name)
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -355,14 +355,44 @@ def run_reference(args):
     }
 
 
+def kernel_probe(args):
+    """Per-kernel device times of one conv shape (``--kernel-probe``): used for
+    sweeps and as the small case of ncu captures."""
+    import torch.nn as nn
+
+    import xdna_train
+    xdna_train.register_xdna_device()
+    torch.cuda.set_device(0)
+    X = torch.device("xdna", 0)
+    b, c, hw = args.batch, args.channels, args.hw
+    conv = nn.Conv2d(c, c, 3, padding=1).bfloat16().to(X)
+    x = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
+    dy = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
+    kt = kernel_times(x, dy, conv, 0, iters=args.iters)
+    fl = 2.0 * b * hw * hw * c * c * 9
+    out = {k: {"ms": round(v, 4)} for k, v in kt.items()}
+    for k in ("fwd", "dgrad", "wgrad"):
+        out[k]["tflops"] = round(fl / (kt[k] * 1e-3) / 1e12, 1)
+    out["pack_rows"]["gbs"] = round(2 * (x.numel() + b * (hw + 2) ** 2 * ((c + 63) // 64) * 64) / (kt["pack_rows"] * 1e-3) / 1e9, 1)
+    print(json.dumps({"probe": f"B{b} C{c} HW{hw}", **out}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel-probe", action="store_true")
+    ap.add_argument("--batch", type=int, default=B_PER_GPU)
+    ap.add_argument("--channels", type=int, default=C)
+    ap.add_argument("--hw", type=int, default=HW)
+    ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.kernel_probe:
+        kernel_probe(args)
+        return
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
         line = run_reference(args)

@@ -81,6 +81,97 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const uint16_t* __restri
   }
 }
 
+// Fast path for NCHW-like inputs (pixels contiguous, W % 8 == 0, 16-byte
+// aligned rows): one CTA writes padded row (b, yp) for one 64-channel chunk.
+// Global reads are 16-byte vectors along x; the tile is transposed through
+// shared memory as 32-bit pixel pairs (row pitch chosen so the 8 channel rows a
+// thread gathers fall in different banks), and each thread writes two 16-byte
+// channel vectors, one per pixel of its pair.
+constexpr int kVecThreads = 256;
+constexpr int kMaxSeg = 256;  // pixels per pass
+
+__global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
+    const uint16_t* __restrict__ x, long long sn, long long sc, long long sh, int C, int H, int W, int chunks,
+    int pitch_words, uint16_t* __restrict__ rows) {
+  extern __shared__ uint32_t tw[];  // [64][pitch_words]
+  const int chunk = blockIdx.x % chunks;
+  const int yp = (blockIdx.x / chunks) % (H + 2);
+  const int b = blockIdx.x / (chunks * (H + 2));
+  const int wp = W + 2;
+  const long long cpad = (long long)chunks * kCh;
+  uint16_t* dst_row = rows + ((long long)(b * (H + 2) + yp) * wp) * cpad + chunk * kCh;
+  const int tid = threadIdx.x;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  if (yp == 0 || yp == H + 1) {
+    for (int e = tid; e < wp * 8; e += kVecThreads)
+      *reinterpret_cast<uint4*>(dst_row + (long long)(e >> 3) * cpad + (e & 7) * 8) = zero;
+    return;
+  }
+  if (tid < 16) {
+    const int px = (tid < 8) ? 0 : W + 1;
+    *reinterpret_cast<uint4*>(dst_row + (long long)px * cpad + (tid & 7) * 8) = zero;
+  }
+  const uint16_t* src = x + b * sn + (long long)(yp - 1) * sh + (long long)(chunk * kCh) * sc;
+  const int cvalid = min(kCh, C - chunk * kCh);
+  for (int x0 = 0; x0 < W; x0 += kMaxSeg) {
+    const int seg = min(kMaxSeg, W - x0);  // multiple of 8
+    const int nvec = seg >> 3;
+    if (x0) __syncthreads();
+    for (int e = tid; e < kCh * nvec; e += kVecThreads) {
+      const int c = e / nvec, v = e - c * nvec;
+      uint4 val = zero;
+      if (c < cvalid) val = *reinterpret_cast<const uint4*>(src + (long long)c * sc + x0 + v * 8);
+      uint32_t* t = tw + c * pitch_words + v * 4;
+      t[0] = val.x;
+      t[1] = val.y;
+      t[2] = val.z;
+      t[3] = val.w;
+    }
+    __syncthreads();
+    const int npairs = seg >> 1;
+    for (int e = tid; e < npairs * 8; e += kVecThreads) {
+      const int pp = e >> 3, v = e & 7;
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = tw[(v * 8 + k) * pitch_words + pp];
+      uint4 lo, hi;
+      lo.x = __byte_perm(w[0], w[1], 0x5410);
+      lo.y = __byte_perm(w[2], w[3], 0x5410);
+      lo.z = __byte_perm(w[4], w[5], 0x5410);
+      lo.w = __byte_perm(w[6], w[7], 0x5410);
+      hi.x = __byte_perm(w[0], w[1], 0x7632);
+      hi.y = __byte_perm(w[2], w[3], 0x7632);
+      hi.z = __byte_perm(w[4], w[5], 0x7632);
+      hi.w = __byte_perm(w[6], w[7], 0x7632);
+      const long long px = x0 + 2 * pp + 1;  // padded column of the pair's first pixel
+      *reinterpret_cast<uint4*>(dst_row + px * cpad + v * 8) = lo;
+      *reinterpret_cast<uint4*>(dst_row + (px + 1) * cpad + v * 8) = hi;
+    }
+  }
+}
+
+// Channels-last inputs (channels contiguous, C % 8 == 0): a padded 16-byte copy.
+__global__ void pack_rows_nhwc_vec_kernel(const uint16_t* __restrict__ x, long long sn, long long sh, long long sw,
+                                          int B, int C, int H, int W, int chunks, uint16_t* __restrict__ rows) {
+  const int wp = W + 2, hp = H + 2;
+  const int vpr = chunks * 8;  // 16-byte vectors per padded row (pixel)
+  const long long total = (long long)B * hp * wp * vpr;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int v = int(i % vpr);
+    const long long p = i / vpr;
+    const int xp = int(p % wp);
+    const long long r = p / wp;
+    const int yp = int(r % hp);
+    const int b = int(r / hp);
+    uint4 val = make_uint4(0, 0, 0, 0);
+    const int c = v * 8;
+    if (yp >= 1 && yp <= H && xp >= 1 && xp <= W && c < C)
+      val = *reinterpret_cast<const uint4*>(x + b * sn + (long long)(yp - 1) * sh + (long long)(xp - 1) * sw + c);
+    *reinterpret_cast<uint4*>(rows + p * (long long)(chunks * kCh) + c) = val;
+  }
+}
+
 // Wk[n][chunk*576 + tap*64 + c]; forward: n = co, source w[co][chunk*64+c][tap];
 // dgrad: n = ci, source w[chunk*64+c][ci][8-tap] (spatial flip + in/out swap).
 __global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int Cout, int Cin, int chunks,
@@ -150,7 +241,25 @@ b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, i
   if (reinterpret_cast<uintptr_t>(rows) & 15) return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: rows not 16-byte aligned");
   const long long blocks = (long long)B * (H + 2) * chunks;
   if (blocks >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "b2_pack_rows_bf16: too large");
-  pack_rows_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+  if (sw == 1 && W % 8 == 0 && sh % 8 == 0 && sc % 8 == 0 && sn % 8 == 0 && (xa & 15) == 0) {
+    const int seg = std::min(W, kMaxSeg);
+    int pitch = seg / 2;
+    while (pitch % 4 != 1) ++pitch;  // pitch = 1 mod 4 words: conflict-light gathers
+    const size_t smem = size_t(kCh) * pitch * 4;
+    pack_rows_nchw_vec_kernel<<<unsigned(blocks), kVecThreads, smem, st>>>(
+        static_cast<const uint16_t*>(x), sn, sc, sh, C, H, W, chunks, pitch, static_cast<uint16_t*>(rows));
+    return check_cuda(cudaGetLastError(), "pack_rows(nchw) launch");
+  }
+  if (sc == 1 && C % 8 == 0 && sw % 8 == 0 && sh % 8 == 0 && sn % 8 == 0 && (xa & 15) == 0) {
+    const long long total = (long long)B * (H + 2) * (W + 2) * chunks * 8;
+    const int grid = int(std::min<long long>((total + 255) / 256, 148LL * 16));
+    pack_rows_nhwc_vec_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), sn, sh, sw, B, C, H, W, chunks,
+                                                    static_cast<uint16_t*>(rows));
+    return check_cuda(cudaGetLastError(), "pack_rows(nhwc) launch");
+  }
+  pack_rows_kernel<<<unsigned(blocks), 256, 0, st>>>(
       static_cast<const uint16_t*>(x), sn, sc, sh, sw, B, C, H, W, chunks, static_cast<uint16_t*>(rows));
   return check_cuda(cudaGetLastError(), "pack_rows launch");
 }

@@ -15,6 +15,20 @@ constexpr int kThreads = 256;
 
 __device__ __forceinline__ bool nan_or_gt(float v, float m) { return (v > m) || (v != v); }
 
+// NaN results follow x86 SSE propagation (first NaN operand, quieted; an
+// invalid operation gives the default NaN 0xFFC00000), the arithmetic of the
+// reference's host build.  With it even NaN payloads match bit for bit.
+__device__ __forceinline__ float x86_nan(float r, float x, float y) {
+  const uint32_t xu = __float_as_uint(x), yu = __float_as_uint(y), ru = __float_as_uint(r);
+  if ((xu & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(xu | 0x00400000u);
+  if ((yu & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(yu | 0x00400000u);
+  if ((ru & 0x7fffffffu) > 0x7f800000u) return __uint_as_float(0xFFC00000u);
+  return r;
+}
+__device__ __forceinline__ float xsub(float a, float b) { return x86_nan(__fsub_rn(a, b), a, b); }
+__device__ __forceinline__ float xmul(float a, float b) { return x86_nan(__fmul_rn(a, b), a, b); }
+__device__ __forceinline__ float xadd(float a, float b) { return x86_nan(__fadd_rn(a, b), a, b); }
+
 __device__ __forceinline__ uint16_t relu_bits(uint16_t a) {
   return (bf2f(a) <= 0.0f) ? uint16_t(0) : a;
 }
@@ -111,8 +125,8 @@ __global__ void addtap_kernel(const uint16_t* __restrict__ base, const uint16_t*
   for (long long i = blockIdx.x * (long long)kThreads + threadIdx.x; i < n;
        i += (long long)gridDim.x * kThreads) {
     // no fma contraction: the reference rounds the product and the sum apart
-    const float t = __fmul_rn(scale, __fsub_rn(bf2f(a[i]), bf2f(b[i])));
-    out[i] = f2bf(base ? __fadd_rn(bf2f(base[i]), t) : t);
+    const float t = xmul(scale, xsub(bf2f(a[i]), bf2f(b[i])));
+    out[i] = f2bf(base ? xadd(bf2f(base[i]), t) : t);
   }
 }
 
@@ -123,7 +137,7 @@ __global__ void relu_bwd_kernel(const uint16_t* __restrict__ r, const uint16_t* 
        i += (long long)gridDim.x * kThreads) {
     float g = 0.0f;
     if (base) g = bf2f(base[i]);
-    if (a) g = __fadd_rn(g, __fmul_rn(scale, __fsub_rn(bf2f(a[i]), bf2f(b[i]))));
+    if (a) g = xadd(g, xmul(scale, xsub(bf2f(a[i]), bf2f(b[i]))));
     out[i] = (bf2f(r[i]) <= 0.0f) ? uint16_t(0) : f2bf(g);
   }
 }

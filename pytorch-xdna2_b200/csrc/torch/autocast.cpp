@@ -25,6 +25,9 @@ using c10::IntArrayRef;
 using at::Dimname;
 using at::DimnameList;
 
+// ops without an autocast policy pass straight through
+TORCH_LIBRARY_IMPL(_, AutocastPrivateUse1, m) { m.fallback(torch::CppFunction::makeFallthrough()); }
+
 TORCH_LIBRARY_IMPL(aten, AutocastPrivateUse1, m) {
   AT_FORALL_LOWER_PRECISION_FP(XDNA_AUTOCAST_LOWER_PRECISION_FP)
   AT_FORALL_FP32(XDNA_AUTOCAST_FP32)
