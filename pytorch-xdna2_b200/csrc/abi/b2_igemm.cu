@@ -20,6 +20,7 @@
 // torch_xdna_device.cpp:1968-1985, 2660-2679).
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "b2_common.cuh"
 
@@ -28,7 +29,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue
+constexpr int kEpiWarps = 8;
 constexpr int kABytes = BM * BK * 2;
 
 enum Kind : int { kConv = 0, kWgrad = 1, kGemm = 2 };
@@ -98,46 +100,68 @@ __device__ __forceinline__ int total_tiles(int kind, const Params& p) {
 }
 
 // ---------------------------------------------------------------------------
-// epilogues: thread owns accumulator row `row` of the tile; r[] holds columns
-// [col0, col0+32) as fp32 bit patterns.
+// epilogues.  Thread owns accumulator row `row` of the tile; r[] holds columns
+// [col0, col0+32) as fp32 bit patterns.  bf16 rounding uses the hardware
+// round-to-nearest-even conversion (cvt.rn.bf16x2.f32).  Per-column vectors
+// (bias) are read once per chunk by the warp and broadcast with shuffles.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void epi_conv(const Params& p, int mt, int col0, int row,
-                                         const uint32_t (&r)[32]) {
+__device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint16_t cvt1(float v) {
+  __nv_bfloat16 h = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+// Output row of a conv tile: base pointer of pixel (b, y, x), or null when the
+// padded-grid row is a border / tail row that produces nothing.
+__device__ __forceinline__ uint16_t* conv_row_base(const Params& p, int mt, int row) {
   const int prow = mt * BM + row;
-  if (prow >= p.m_total) return;
+  if (prow >= p.m_total) return nullptr;
   const int plane = p.hp * p.wp;
   const int b = prow / plane;
   const int rem = prow - b * plane;
   const int y = rem / p.wp;
   const int x = rem - y * p.wp;
-  if (y >= p.H || x >= p.W) return;
-  uint16_t* base = static_cast<uint16_t*>(p.out) + b * p.osn + y * p.osh + x * p.osw;
+  if (y >= p.H || x >= p.W) return nullptr;
+  return static_cast<uint16_t*>(p.out) + b * p.osn + y * p.osh + x * p.osw;
+}
+
+__device__ __forceinline__ void epi_conv(const Params& p, uint16_t* base, int col0, int lane,
+                                         const uint32_t (&r)[32]) {
+  const bool full = col0 + 32 <= p.N;
+  float bl = 0.f;
+  if (p.bias && col0 + lane < p.N) bl = bf2f(p.bias[col0 + lane]);
   float v[32];
 #pragma unroll
   for (int c = 0; c < 32; ++c) {
-    float a = __uint_as_float(r[c]);
-    const int co = col0 + c;
-    if (p.bias && co < p.N) a += bf2f(p.bias[co]);
-    if (p.relu) a = a > 0.f ? a : 0.f;
+    float a = __uint_as_float(r[c]) + __shfl_sync(0xffffffffu, bl, c);
+    if (p.relu) a = fmaxf(a, 0.f);
     v[c] = a;
   }
-  if (p.osc == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
+  if (!base) return;
+  if (p.osc == 1 && full && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
     uint4* dst = reinterpret_cast<uint4*>(base + col0);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack_bf2(v[q * 8 + 0], v[q * 8 + 1]);
-      w.y = pack_bf2(v[q * 8 + 2], v[q * 8 + 3]);
-      w.z = pack_bf2(v[q * 8 + 4], v[q * 8 + 5]);
-      w.w = pack_bf2(v[q * 8 + 6], v[q * 8 + 7]);
-      dst[q] = w;
-    }
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(cvt2(v[q * 8 + 0], v[q * 8 + 1]), cvt2(v[q * 8 + 2], v[q * 8 + 3]),
+                          cvt2(v[q * 8 + 4], v[q * 8 + 5]), cvt2(v[q * 8 + 6], v[q * 8 + 7]));
     return;
   }
+  uint16_t* q = base + (long long)col0 * p.osc;
+  if (full) {
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const int co = col0 + c;
-    if (co < p.N) base[(long long)co * p.osc] = f2bf(v[c]);
+    for (int c = 0; c < 32; ++c) {
+      *q = cvt1(v[c]);
+      q += p.osc;
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      if (col0 + c < p.N) *q = cvt1(v[c]);
+      q += p.osc;
+    }
   }
 }
 
@@ -159,40 +183,44 @@ __device__ __forceinline__ void epi_wgrad(const Params& p, int split, int tap, i
     if (col0 + c < p.N) dst[col0 + c] = __uint_as_float(r[c]);
 }
 
-__device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int col0, int row,
+__device__ __forceinline__ float load_c(const Params& p, long long i) {
+  return p.cin_dtype == B2_F32 ? static_cast<const float*>(p.cin)[i]
+                               : bf2f(static_cast<const uint16_t*>(p.cin)[i]);
+}
+
+__device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int col0, int row, int lane,
                                          const uint32_t (&r)[32]) {
   const int m = mt * BM + row;
-  if (m >= p.M) return;
   float v[32];
+  if (p.beta != 0.f && p.c_sm == 0) {
+    // C broadcast along rows (a bias vector): one load per lane, shuffled
+    float cl = 0.f;
+    if (col0 + lane < p.N) cl = load_c(p, bz * p.c_sb + (long long)(col0 + lane) * p.c_sn);
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    float a = p.alpha * __uint_as_float(r[c]);
-    const int n = col0 + c;
-    if (p.beta != 0.f && n < p.N) {
-      const long long ci = bz * p.c_sb + (long long)m * p.c_sm + (long long)n * p.c_sn;
-      const float cv = p.cin_dtype == B2_F32 ? static_cast<const float*>(p.cin)[ci]
-                                             : bf2f(static_cast<const uint16_t*>(p.cin)[ci]);
-      a += p.beta * cv;
+    for (int c = 0; c < 32; ++c)
+      v[c] = p.alpha * __uint_as_float(r[c]) + p.beta * __shfl_sync(0xffffffffu, cl, c);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      float a = p.alpha * __uint_as_float(r[c]);
+      if (p.beta != 0.f && m < p.M && col0 + c < p.N)
+        a += p.beta * load_c(p, bz * p.c_sb + (long long)m * p.c_sm + (long long)(col0 + c) * p.c_sn);
+      v[c] = a;
     }
-    v[c] = a;
   }
+  if (m >= p.M) return;
   uint16_t* base = static_cast<uint16_t*>(p.out) + bz * p.osn + (long long)m * p.osh;
   if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
     uint4* dst = reinterpret_cast<uint4*>(base + col0);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      w.x = pack_bf2(v[q * 8 + 0], v[q * 8 + 1]);
-      w.y = pack_bf2(v[q * 8 + 2], v[q * 8 + 3]);
-      w.z = pack_bf2(v[q * 8 + 4], v[q * 8 + 5]);
-      w.w = pack_bf2(v[q * 8 + 6], v[q * 8 + 7]);
-      dst[q] = w;
-    }
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(cvt2(v[q * 8 + 0], v[q * 8 + 1]), cvt2(v[q * 8 + 2], v[q * 8 + 3]),
+                          cvt2(v[q * 8 + 4], v[q * 8 + 5]), cvt2(v[q * 8 + 6], v[q * 8 + 7]));
     return;
   }
 #pragma unroll
   for (int c = 0; c < 32; ++c)
-    if (col0 + c < p.N) base[col0 + c] = f2bf(v[c]);
+    if (col0 + c < p.N) base[col0 + c] = cvt1(v[c]);
 }
 
 // ---------------------------------------------------------------------------
@@ -228,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
-      mbar_init(smem_u32(&tempty[a]), 4);
+      mbar_init(smem_u32(&tempty[a]), kEpiWarps);
     }
     mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
@@ -359,29 +387,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // -------------------------------- epilogue ------------------------------
+    // 8 warps: two per tensor-memory lane quarter, each draining half of the
+    // accumulator's columns.
     const int quarter = warp & 3;  // tensor-memory lane quarter this warp may read
+    const int half = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
+    constexpr int kChunks = BN / 64;  // 32-column chunks per half
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       int mt, nt, bz, tap, kb0, kb1;
       decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
+      uint16_t* obase = nullptr;
+      if constexpr (KIND == kConv) obase = conv_row_base(p, mt, row);
       bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN);
+      const uint32_t taddr =
+          tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
 #pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
+      for (int j = 0; j < kChunks; ++j) {
         uint32_t r[32];
         tmem_ld32(taddr + j * 32, r);
         tc_wait_ld();
+        const int col0 = nt * BN + half * (BN / 2) + j * 32;
         if constexpr (KIND == kConv) {
-          epi_conv(p, mt, nt * BN + j * 32, row, r);
+          epi_conv(p, obase, col0, lane, r);
         } else if constexpr (KIND == kWgrad) {
-          epi_wgrad(p, bz, tap, mt, nt * BN + j * 32, row, r);
+          epi_wgrad(p, bz, tap, mt, col0, row, r);
         } else {
-          epi_gemm(p, bz, mt, nt * BN + j * 32, row, r);
+          epi_gemm(p, bz, mt, col0, row, lane, r);
         }
       }
       tc_fence_before();
@@ -524,9 +560,12 @@ WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms) {
   w.ci_blocks = (Cin + w.BN - 1) / w.BN;
   w.tiles_m = (Cout + BM - 1) / BM;
   w.num_kb = int((w.m_total + BK - 1) / BK);
+  // Split-K so that the tiles fill the SMs in whole waves: tiles are long
+  // (thousands of k-blocks), so a partial last wave would idle SMs for a
+  // whole tile's duration.
   const int base = w.tiles_m * 9 * w.ci_blocks;
-  int splits = std::max(1, (2 * sms + base - 1) / base);
-  splits = std::min(splits, std::max(1, w.num_kb / 16));
+  int splits = base >= sms ? 1 : sms / base;
+  splits = std::max(1, std::min(splits, w.num_kb / 16));
   w.kb_per_split = (w.num_kb + splits - 1) / splits;
   w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
   w.workspace = size_t(w.splits) * 9 * size_t(Cout) * size_t(Cin) * sizeof(float);

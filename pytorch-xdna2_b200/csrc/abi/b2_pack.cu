@@ -81,15 +81,16 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(const uint16_t* __restri
   }
 }
 
-// Fast path for NCHW-like inputs (pixels contiguous, W % 8 == 0, 16-byte
-// aligned rows): one CTA writes padded row (b, yp) for one 64-channel chunk.
-// Global reads are 16-byte vectors along x; the tile is transposed through
+// Fast path for NCHW-like inputs (pixels contiguous, W even, rows aligned to
+// the vector width): one CTA writes padded row (b, yp) for one 64-channel chunk.
+// Global reads are 16-, 8- or 4-byte vectors along x; the tile is transposed through
 // shared memory as 32-bit pixel pairs (row pitch chosen so the 8 channel rows a
 // thread gathers fall in different banks), and each thread writes two 16-byte
 // channel vectors, one per pixel of its pair.
 constexpr int kVecThreads = 256;
 constexpr int kMaxSeg = 256;  // pixels per pass
 
+template <int VW>  // elements per global load: 8 (16 B), 4 (8 B) or 2 (4 B)
 __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
     const uint16_t* __restrict__ x, long long sn, long long sc, long long sh, int C, int H, int W, int chunks,
     int pitch_words, uint16_t* __restrict__ rows) {
@@ -114,18 +115,28 @@ __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
   const uint16_t* src = x + b * sn + (long long)(yp - 1) * sh + (long long)(chunk * kCh) * sc;
   const int cvalid = min(kCh, C - chunk * kCh);
   for (int x0 = 0; x0 < W; x0 += kMaxSeg) {
-    const int seg = min(kMaxSeg, W - x0);  // multiple of 8
-    const int nvec = seg >> 3;
+    const int seg = min(kMaxSeg, W - x0);  // multiple of VW
+    const int nvec = seg / VW;
     if (x0) __syncthreads();
     for (int e = tid; e < kCh * nvec; e += kVecThreads) {
       const int c = e / nvec, v = e - c * nvec;
-      uint4 val = zero;
-      if (c < cvalid) val = *reinterpret_cast<const uint4*>(src + (long long)c * sc + x0 + v * 8);
-      uint32_t* t = tw + c * pitch_words + v * 4;
-      t[0] = val.x;
-      t[1] = val.y;
-      t[2] = val.z;
-      t[3] = val.w;
+      const uint16_t* g = src + (long long)c * sc + x0 + v * VW;
+      uint32_t* t = tw + c * pitch_words + v * (VW / 2);
+      if constexpr (VW == 8) {
+        uint4 val = zero;
+        if (c < cvalid) val = *reinterpret_cast<const uint4*>(g);
+        t[0] = val.x;
+        t[1] = val.y;
+        t[2] = val.z;
+        t[3] = val.w;
+      } else if constexpr (VW == 4) {
+        uint2 val = make_uint2(0, 0);
+        if (c < cvalid) val = *reinterpret_cast<const uint2*>(g);
+        t[0] = val.x;
+        t[1] = val.y;
+      } else {
+        t[0] = c < cvalid ? *reinterpret_cast<const uint32_t*>(g) : 0u;
+      }
     }
     __syncthreads();
     const int npairs = seg >> 1;
@@ -243,13 +254,30 @@ b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, i
   if (blocks >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "b2_pack_rows_bf16: too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
-  if (sw == 1 && W % 8 == 0 && sh % 8 == 0 && sc % 8 == 0 && sn % 8 == 0 && (xa & 15) == 0) {
+  int vw = 0;  // widest vector the strides and the base address allow
+  for (int cand : {8, 4, 2}) {
+    if (sw == 1 && W % cand == 0 && sh % cand == 0 && sc % cand == 0 && sn % cand == 0 &&
+        (xa % (2 * cand)) == 0) {
+      vw = cand;
+      break;
+    }
+  }
+  if (vw) {
     const int seg = std::min(W, kMaxSeg);
     int pitch = seg / 2;
     while (pitch % 4 != 1) ++pitch;  // pitch = 1 mod 4 words: conflict-light gathers
     const size_t smem = size_t(kCh) * pitch * 4;
-    pack_rows_nchw_vec_kernel<<<unsigned(blocks), kVecThreads, smem, st>>>(
-        static_cast<const uint16_t*>(x), sn, sc, sh, C, H, W, chunks, pitch, static_cast<uint16_t*>(rows));
+    auto* xs = static_cast<const uint16_t*>(x);
+    auto* rs = static_cast<uint16_t*>(rows);
+    if (vw == 8)
+      pack_rows_nchw_vec_kernel<8><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
+                                                                               pitch, rs);
+    else if (vw == 4)
+      pack_rows_nchw_vec_kernel<4><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
+                                                                               pitch, rs);
+    else
+      pack_rows_nchw_vec_kernel<2><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
+                                                                               pitch, rs);
     return check_cuda(cudaGetLastError(), "pack_rows(nchw) launch");
   }
   if (sc == 1 && C % 8 == 0 && sw % 8 == 0 && sh % 8 == 0 && sn % 8 == 0 && (xa & 15) == 0) {

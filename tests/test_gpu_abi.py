@@ -59,7 +59,8 @@ def wk_of(w: torch.Tensor, dgrad=False) -> torch.Tensor:
 
 # --------------------------------------------------------------------- packers
 
-@pytest.mark.parametrize("shape", [(2, 70, 5, 7), (1, 3, 4, 4), (3, 64, 6, 9), (2, 130, 3, 11), (1, 64, 2, 150)])
+@pytest.mark.parametrize("shape", [(2, 70, 5, 7), (1, 3, 4, 4), (3, 64, 6, 9), (2, 130, 3, 11), (1, 64, 2, 150),
+                                   (2, 64, 5, 36), (2, 96, 3, 18), (1, 70, 3, 264), (2, 128, 4, 72)])
 @pytest.mark.parametrize("channels_last", [False, True])
 def test_pack_rows_bit_exact(cuda, shape, channels_last):
     g = torch.Generator().manual_seed(0)
