@@ -135,6 +135,23 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw,
                            void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* Weight gradient that allocates nothing (no counterpart in the reference).
+ * Same result as b2_conv3x3_wgrad, but the split-K partial sums live in one
+ * fixed device array inside this library instead of a caller workspace, for
+ * callers that cannot allocate device memory (a framework that reserved the
+ * GPU's memory for its own pool, a loop that must never reach cudaMalloc).
+ * The array holds b2_conv3x3_wgrad_noalloc_max_bytes() (16 MiB) on every GPU
+ * that loads the library, until exit.  If the usual split plan needs more,
+ * fewer splits are used; shapes with 9*Cout*Cin*4 bytes above the limit fail
+ * with B2_ERR_WORKSPACE.  The first call on a device looks the array's
+ * address up (make it before any stream capture).  Calls share the array:
+ * calls that overlap on the GPU race and must be serialized by the caller.
+ * Calls no cudaMalloc / cudaFree. */
+b2_status b2_conv3x3_wgrad_noalloc(const void* dy_rows, const void* x_rows,
+                                   void* dw, int dw_dtype, int B, int Cin,
+                                   int H, int W, int Cout, void* stream);
+size_t b2_conv3x3_wgrad_noalloc_max_bytes(void);
+
 /* ---- dense GEMM (tcgen05) ------------------------------------------------ */
 
 /* For each batch index i < batch:

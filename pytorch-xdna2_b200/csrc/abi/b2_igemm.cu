@@ -738,3 +738,130 @@ b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Weight gradient without any allocation.
+//
+// b2_conv3x3_wgrad needs a caller-provided workspace for its split-K partial
+// sums.  Some callers cannot provide one: a host framework that has already
+// reserved all device memory for its own pool, or a latency-critical loop that
+// must never reach cudaMalloc (which can synchronize the whole device).  For
+// them this variant keeps the partial sums in one fixed device array that
+// lives as long as the library is loaded on each GPU.
+//   * Limit: kNoAllocScratchBytes (16 MiB).  If the usual split-K plan needs
+//     more, fewer splits are used; if even one split (9*Cout*Cin floats) does
+//     not fit, the call fails with B2_ERR_WORKSPACE.
+//   * The array's device address is looked up once per device, on the first
+//     call made with that device current (cudaGetSymbolAddress); make that
+//     first call before any stream capture.
+//   * Every call reuses the same array.  Each call overwrites every partial
+//     sum it later reads, so nothing has to be cleared between calls, but two
+//     calls that overlap on the GPU (different streams, or different host
+//     threads) race on it: serialize them.
+// ---------------------------------------------------------------------------
+namespace b2 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+b2_status noalloc_scratch(float** out) {
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    B2_TRY(check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)"));
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return B2_OK;
+}
+
+}  // namespace
+}  // namespace b2
+
+extern "C" {
+
+size_t b2_conv3x3_wgrad_noalloc_max_bytes(void) { return b2::kNoAllocScratchBytes; }
+
+b2_status b2_conv3x3_wgrad_noalloc(const void* dy_rows, const void* x_rows, void* dw, int dw_dtype, int B, int Cin,
+                                   int H, int W, int Cout, void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!dy_rows || !x_rows || !dw) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad_noalloc: null pointer");
+  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
+    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad_noalloc: bad shape");
+  if (dw_dtype != B2_BF16 && dw_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad_noalloc: dtype");
+  if (!aligned16(dy_rows) || !aligned16(x_rows))
+    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad_noalloc: operands must be 16-byte aligned");
+  const size_t per_split = size_t(9) * size_t(Cout) * size_t(Cin) * sizeof(float);
+  if (per_split > kNoAllocScratchBytes)
+    return set_error(B2_ERR_WORKSPACE,
+                     "b2_conv3x3_wgrad_noalloc: Cout*Cin = %d*%d needs %zu bytes of partial sums, more than the "
+                     "fixed %zu-byte scratch; use b2_conv3x3_wgrad with a workspace",
+                     Cout, Cin, per_split, kNoAllocScratchBytes);
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
+    return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad_noalloc: too many padded rows");
+  if (w.workspace > kNoAllocScratchBytes) {  // fewer splits, same result up to fp32 summation order
+    const int max_splits = int(kNoAllocScratchBytes / per_split);
+    w.kb_per_split = (w.num_kb + max_splits - 1) / max_splits;
+    w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
+    w.workspace = size_t(w.splits) * per_split;
+  }
+  float* scratch = nullptr;
+  B2_TRY(noalloc_scratch(&scratch));
+  const int cpo = ((Cout + 63) / 64) * 64;
+  const int cpi = ((Cin + 63) / 64) * 64;
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[3] = {uint64_t(cpo), uint64_t(w.m_total), 1};
+    const uint64_t strides[2] = {uint64_t(cpo) * 2, uint64_t(cpo) * 2 * w.m_total};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&ta, dy_rows, 3, dims, strides, box, true));
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(cpi), uint64_t(w.m_total), 1};
+    const uint64_t strides[2] = {uint64_t(cpi) * 2, uint64_t(cpi) * 2 * w.m_total};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&tb, x_rows, 3, dims, strides, box, true));
+  }
+  Params p{};
+  p.tiles_m = w.tiles_m;
+  p.tiles_n = 1;
+  p.splits = w.splits;
+  p.batch = 1;
+  p.num_kb = w.num_kb;
+  p.kb_per_split = w.kb_per_split;
+  p.wp = W + 2;
+  p.hp = H + 2;
+  p.H = H;
+  p.W = W;
+  p.m_total = int(w.m_total);
+  p.a_row_shift = W + 3;
+  p.ci_blocks = w.ci_blocks;
+  p.M = Cout;
+  p.N = Cin;
+  p.partial = scratch;
+  p.alpha = 1.f;
+  p.status = device_status_ptr();
+  const int tiles = w.splits * w.tiles_m * 9 * w.ci_blocks;
+  if (w.BN == 256)
+    B2_TRY((launch<256, kStages256, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  else
+    B2_TRY((launch<128, kStages128, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  const long long total = (long long)Cout * Cin * 9;
+  const int threads = 256;
+  const int blocks = int(std::min<long long>((total + threads - 1) / threads, 148LL * 16));
+  wgrad_reduce_kernel<<<blocks, threads, 0, st>>>(scratch, dw, dw_dtype, w.splits, Cout, Cin);
+  return check_cuda(cudaGetLastError(), "wgrad reduce launch (no-alloc)");
+}
+
+}  // extern "C"

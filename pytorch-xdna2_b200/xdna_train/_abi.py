@@ -43,6 +43,8 @@ SIGNATURES = {
     "b2_conv3x3_dgrad": [vp, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp],
     "b2_conv3x3_wgrad_workspace_bytes": [i32, i32, i32, i32, i32],
     "b2_conv3x3_wgrad": [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, sz, vp],
+    "b2_conv3x3_wgrad_noalloc": [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp],
+    "b2_conv3x3_wgrad_noalloc_max_bytes": [],
     "b2_gemm_bf16": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
                      i64, i64, i64, vp, i64, i64, i32, vp],
     "b2_fused_adam": [C.POINTER(AdamTensor), i32, C.POINTER(AdamHparams), vp],
@@ -53,7 +55,8 @@ SIGNATURES = {
     "b2_region_relu_bwd_bf16": [vp, vp, vp, vp, vp, i64, f32, vp],
     "b2_region_maxpool2_bwd_bf16": [vp, vp, vp, i64, i64, i64, vp],
 }
-_RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz}
+_RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
+             "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 
 class B2Error(RuntimeError):
