@@ -42,6 +42,17 @@ def conv_flops(b: int) -> float:
     return 2.0 * b * HW * HW * C * C * 9  # one direction (fwd, dgrad or wgrad)
 
 
+def conv_traffic_bytes():
+    """DRAM bytes of one fwd+dgrad+wgrad launch set at the bench shape, from the
+    committed ncu summary (captured at batch 64, scaled by the batch)."""
+    import re
+    f = REPO / "profiles" / "conv3x3_igemm_B64_C256_HW72.md"
+    if not f.is_file():
+        return None
+    m = re.search(r"traffic_fwd_dgrad_wgrad_bytes_B128:\s*(\d+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.is_file():
@@ -237,7 +248,8 @@ def run_ours(args):
                 "h2d_bytes_per_step": int(x_host.numel() * 2 + dy_host.numel() * 2),
                 "d2h_bytes_per_step": int(w_host.numel() * 2)},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / bf16_peak, 4), "traffic": None,
+                     "frac": round(achieved / bf16_peak, 4), "traffic": conv_traffic_bytes(),
+                     "traffic_source": "ncu dram__bytes_read+write of the three kernels at B64, x2 (profiles/)",
                      "kernel": "conv3x3 implicit GEMM fwd+dgrad+wgrad (tcgen05)",
                      "per_launch_ms": {k: round(v, 4) for k, v in kt.items()},
                      "flops_per_launch": flops_dir, "peak_kind": peak_kind},
