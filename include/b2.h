@@ -78,6 +78,19 @@ b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh,
                             int64_t sw, int B, int C, int H, int W, int chunks,
                             void* rows, void* stream);
 
+/* b2_pack_rows_bf16 of dY that also produces the conv bias gradient
+ * dbias[c] = sum over (b, y, x) of x[b][c][y][x] (dtype B2_BF16 or B2_F32),
+ * taken from the tile the packer already holds (no second pass over dY on the
+ * NCHW path), reduced in a fixed order: deterministic.  Workspace:
+ * b2_pack_rows_dbias_workspace_bytes().  Replaces the reference's CPU dbias
+ * (mask[2] of convolution_backward, torch_xdna_device.cpp:4828-4878). */
+size_t b2_pack_rows_dbias_workspace_bytes(int B, int C, int H, int W);
+b2_status b2_pack_rows_dbias_bf16(const void* x, int64_t sn, int64_t sc,
+                                  int64_t sh, int64_t sw, int B, int C, int H,
+                                  int W, int chunks, void* rows, void* dbias,
+                                  int dbias_dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* OIHW bf16 weight [Cout][Cin][3][3] -> Wk[Cout][chunks*9*64], K order
  * (chunk, dy, dx, c), zero for c >= Cin.  chunks >= ceil(Cin/64).
  * Replaces the K ordering of xdna_conv3x3w_pack_weights_bfp16

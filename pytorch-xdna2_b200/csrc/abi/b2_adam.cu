@@ -1,8 +1,10 @@
 // Multi-tensor fused Adam / AdamW.  One pass per element: read grad, param,
 // exp_avg, exp_avg_sq (and max_exp_avg_sq), write param and the moments, all
 // arithmetic in fp32.  Tensor metadata travels in the kernel parameter block
-// (no device allocation); a launch covers up to kMaxTensors tensors and
-// kMaxBlocks chunks of kChunk elements, larger lists take several launches.
+// (no device allocation); a launch covers up to kMaxTensors tensors, split into
+// kChunk-element chunks that a grid of at most 4 CTAs per SM walks with a
+// grid stride (each thread updates 4 consecutive elements per step, with
+// vector loads when the tensor's arrays are aligned).
 //
 // The update follows PyTorch's Adam/AdamW definition that the reference's
 // `_fused_adam_` CPU path runs (reached through the boxed fallback,
@@ -25,8 +27,7 @@ namespace b2 {
 namespace {
 
 constexpr int kMaxTensors = 64;
-constexpr int kMaxBlocks = 320;
-constexpr int kChunk = 16384;
+constexpr int kChunk = 4096;
 constexpr int kThreads = 256;
 
 struct AdamArgs {
@@ -37,8 +38,9 @@ struct AdamArgs {
   void* vmax[kMaxTensors];
   const float* step[kMaxTensors];
   long long numel[kMaxTensors];
-  unsigned short block_tensor[kMaxBlocks];
-  int block_chunk[kMaxBlocks];
+  int chunk_begin[kMaxTensors + 1];  // prefix sums of chunks per tensor
+  unsigned char vec[kMaxTensors];    // all arrays aligned for 4-element vectors
+  int ntensors;
 };
 
 struct AdamScalars {
@@ -47,6 +49,10 @@ struct AdamScalars {
   const float* lr_tensor;
   const float* grad_scale;
   const float* found_inf;
+};
+
+struct Coef {
+  float step_size, bc2_sqrt, omb1, omb2, b2, wd, eps, decay, gscale;
 };
 
 template <typename T>
@@ -63,54 +69,129 @@ __device__ __forceinline__ void st(void* p, long long i, float v) {
   else
     static_cast<float*>(p)[i] = v;
 }
+// 4 consecutive elements (i % 4 == 0, arrays aligned for it)
+template <typename T>
+__device__ __forceinline__ void ld4(const void* p, long long i, float (&o)[4]) {
+  if constexpr (sizeof(T) == 2) {
+    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
+    o[0] = __uint_as_float(u.x << 16);
+    o[1] = __uint_as_float(u.x & 0xffff0000u);
+    o[2] = __uint_as_float(u.y << 16);
+    o[3] = __uint_as_float(u.y & 0xffff0000u);
+  } else {
+    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    o[0] = f.x;
+    o[1] = f.y;
+    o[2] = f.z;
+    o[3] = f.w;
+  }
+}
+template <typename T>
+__device__ __forceinline__ void st4(void* p, long long i, const float (&v)[4]) {
+  if constexpr (sizeof(T) == 2) {
+    uint2 u;
+    u.x = uint32_t(f2bf(v[0])) | (uint32_t(f2bf(v[1])) << 16);
+    u.y = uint32_t(f2bf(v[2])) | (uint32_t(f2bf(v[3])) << 16);
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p) + i) = u;
+  } else {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+__device__ __forceinline__ void update(const AdamScalars& s, const Coef& c, float g, float& p, float& m, float& v,
+                                       float& vx) {
+  if (s.grad_scale) g = __fdiv_rn(g, c.gscale);
+  if (s.maximize) g = -g;
+  if (s.wd != 0.0) {
+    if (s.adamw)
+      p = __fmul_rn(p, c.decay);
+    else
+      g = __fmaf_rn(c.wd, p, g);
+  }
+  m = __fmaf_rn(c.omb1, __fsub_rn(g, m), m);
+  v = __fmaf_rn(__fmul_rn(c.omb2, g), g, __fmul_rn(c.b2, v));
+  float vv = v;
+  if (s.amsgrad) {
+    vv = fmaxf(vx, v);
+    vx = vv;
+  }
+  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vv), c.bc2_sqrt), c.eps);
+  p = __fsub_rn(p, __fdiv_rn(__fmul_rn(c.step_size, m), denom));
+}
 
 template <typename P, typename S>
-__global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ AdamArgs a,
-                                                        const AdamScalars s) {
+__global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ AdamArgs a, const AdamScalars s) {
   if (s.found_inf && *s.found_inf != 0.f) return;
-  const int t = a.block_tensor[blockIdx.x];
-  const long long begin = (long long)a.block_chunk[blockIdx.x] * kChunk;
-  const long long end = min(begin + kChunk, a.numel[t]);
-  const double step = double(*a.step[t]);
-  const double lr = s.lr_tensor ? double(*s.lr_tensor) : s.lr;
-  const double bc1 = 1.0 - pow(s.beta1, step);
-  const double bc2 = 1.0 - pow(s.beta2, step);
-  const float step_size = float(lr / bc1);
-  const float bc2_sqrt = float(sqrt(bc2));
-  const float omb1 = float(1.0 - s.beta1), omb2 = float(1.0 - s.beta2), b2 = float(s.beta2);
-  const float wd = float(s.wd), eps = float(s.eps);
-  const float decay = float(1.0 - lr * s.wd);
-  const float gscale = s.grad_scale ? *s.grad_scale : 1.f;
-  void* P_ = a.param[t];
-  const void* G_ = a.grad[t];
-  void* M_ = a.m[t];
-  void* V_ = a.v[t];
-  void* X_ = a.vmax[t];
-  for (long long i = begin + threadIdx.x; i < end; i += kThreads) {
-    float g = ld<P>(G_, i);
-    if (s.grad_scale) g = __fdiv_rn(g, gscale);
-    if (s.maximize) g = -g;
-    float p = ld<P>(P_, i);
-    if (s.wd != 0.0) {
-      if (s.adamw)
-        p = __fmul_rn(p, decay);
-      else
-        g = __fmaf_rn(wd, p, g);
+  __shared__ Coef sc;
+  const int total = a.chunk_begin[a.ntensors];
+  int t = 0;
+  int cur = -1;
+  for (int chunk = blockIdx.x; chunk < total; chunk += gridDim.x) {
+    while (chunk >= a.chunk_begin[t + 1]) ++t;
+    if (t != cur) {
+      __syncthreads();  // everyone is done with the previous coefficients
+      if (threadIdx.x == 0) {
+        const double step = double(*a.step[t]);
+        const double lr = s.lr_tensor ? double(*s.lr_tensor) : s.lr;
+        const double bc1 = 1.0 - pow(s.beta1, step);
+        const double bc2 = 1.0 - pow(s.beta2, step);
+        sc.step_size = float(lr / bc1);
+        sc.bc2_sqrt = float(sqrt(bc2));
+        sc.omb1 = float(1.0 - s.beta1);
+        sc.omb2 = float(1.0 - s.beta2);
+        sc.b2 = float(s.beta2);
+        sc.wd = float(s.wd);
+        sc.eps = float(s.eps);
+        sc.decay = float(1.0 - lr * s.wd);
+        sc.gscale = s.grad_scale ? *s.grad_scale : 1.f;
+      }
+      __syncthreads();
+      cur = t;
     }
-    float m = ld<S>(M_, i);
-    float v = ld<S>(V_, i);
-    m = __fmaf_rn(omb1, __fsub_rn(g, m), m);
-    v = __fmaf_rn(__fmul_rn(omb2, g), g, __fmul_rn(b2, v));
-    float vv = v;
-    if (s.amsgrad) {
-      vv = fmaxf(ld<S>(X_, i), v);
-      st<S>(X_, i, vv);
+    const Coef c = sc;
+    const long long begin = (long long)(chunk - a.chunk_begin[t]) * kChunk;
+    const long long end = min(begin + kChunk, a.numel[t]);
+    void* P_ = a.param[t];
+    const void* G_ = a.grad[t];
+    void* M_ = a.m[t];
+    void* V_ = a.v[t];
+    void* X_ = a.vmax[t];
+    if (a.vec[t]) {
+      for (long long i = begin + 4 * threadIdx.x; i < end; i += 4 * kThreads) {
+        if (i + 4 <= end) {
+          float g[4], p[4], m[4], v[4], x[4] = {0.f, 0.f, 0.f, 0.f};
+          ld4<P>(G_, i, g);
+          ld4<P>(P_, i, p);
+          ld4<S>(M_, i, m);
+          ld4<S>(V_, i, v);
+          if (s.amsgrad) ld4<S>(X_, i, x);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) update(s, c, g[k], p[k], m[k], v[k], x[k]);
+          st4<P>(P_, i, p);
+          st4<S>(M_, i, m);
+          st4<S>(V_, i, v);
+          if (s.amsgrad) st4<S>(X_, i, x);
+        } else {
+          for (long long j = i; j < end; ++j) {
+            float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
+            update(s, c, ld<P>(G_, j), p, m, v, x);
+            st<P>(P_, j, p);
+            st<S>(M_, j, m);
+            st<S>(V_, j, v);
+            if (s.amsgrad) st<S>(X_, j, x);
+          }
+        }
+      }
+    } else {
+      for (long long j = begin + threadIdx.x; j < end; j += kThreads) {
+        float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
+        update(s, c, ld<P>(G_, j), p, m, v, x);
+        st<P>(P_, j, p);
+        st<S>(M_, j, m);
+        st<S>(V_, j, v);
+        if (s.amsgrad) st<S>(X_, j, x);
+      }
     }
-    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(vv), bc2_sqrt), eps);
-    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(step_size, m), denom));
-    st<P>(P_, i, p);
-    st<S>(M_, i, m);
-    st<S>(V_, i, v);
   }
 }
 
@@ -141,39 +222,44 @@ extern "C" b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n, const b
   auto kern = hp->param_dtype == B2_F32
                   ? (hp->state_dtype == B2_F32 ? adam_kernel<float, float> : adam_kernel<float, uint16_t>)
                   : (hp->state_dtype == B2_F32 ? adam_kernel<uint16_t, float> : adam_kernel<uint16_t, uint16_t>);
+  const int psz = hp->param_dtype == B2_F32 ? 4 : 2, ssz = hp->state_dtype == B2_F32 ? 4 : 2;
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const int max_grid = 4 * sm_count(dev);
   AdamArgs args;
-  int nt = 0, nb = 0;
+  args.ntensors = 0;
+  args.chunk_begin[0] = 0;
   auto flush = [&]() -> b2_status {
-    if (nb == 0) return B2_OK;
-    kern<<<nb, kThreads, 0, st>>>(args, sc);
-    nt = 0;
-    nb = 0;
-    return check_cuda(cudaGetLastError(), "fused adam launch");
+    const int total = args.chunk_begin[args.ntensors];
+    if (total > 0) {
+      kern<<<std::min(total, max_grid), kThreads, 0, st>>>(args, sc);
+      B2_TRY(check_cuda(cudaGetLastError(), "fused adam launch"));
+    }
+    args.ntensors = 0;
+    args.chunk_begin[0] = 0;
+    return B2_OK;
   };
+  auto al = [](const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; };
   for (int i = 0; i < n; ++i) {
     const b2_adam_tensor& t = tensors[i];
     if (t.numel <= 0) continue;
     if (!t.param || !t.grad || !t.exp_avg || !t.exp_avg_sq || !t.step || (hp->amsgrad && !t.max_exp_avg_sq))
       return set_error(B2_ERR_INVALID, "b2_fused_adam: null pointer in tensor %d", i);
     const long long chunks = (t.numel + kChunk - 1) / kChunk;
-    long long c = 0;
-    while (c < chunks) {
-      if (nt == kMaxTensors || nb == kMaxBlocks) B2_TRY(flush());
-      args.param[nt] = t.param;
-      args.grad[nt] = t.grad;
-      args.m[nt] = t.exp_avg;
-      args.v[nt] = t.exp_avg_sq;
-      args.vmax[nt] = t.max_exp_avg_sq;
-      args.step[nt] = t.step;
-      args.numel[nt] = t.numel;
-      while (c < chunks && nb < kMaxBlocks) {
-        args.block_tensor[nb] = (unsigned short)nt;
-        args.block_chunk[nb] = int(c);
-        ++nb;
-        ++c;
-      }
-      ++nt;
-    }
+    if (chunks > (1LL << 30)) return set_error(B2_ERR_UNSUPPORTED, "b2_fused_adam: tensor %d too large", i);
+    if (args.ntensors == kMaxTensors || args.chunk_begin[args.ntensors] + chunks > (1LL << 30)) B2_TRY(flush());
+    const int k = args.ntensors;
+    args.param[k] = t.param;
+    args.grad[k] = t.grad;
+    args.m[k] = t.exp_avg;
+    args.v[k] = t.exp_avg_sq;
+    args.vmax[k] = t.max_exp_avg_sq;
+    args.step[k] = t.step;
+    args.numel[k] = t.numel;
+    args.vec[k] = al(t.param, 4 * psz) && al(t.grad, 4 * psz) && al(t.exp_avg, 4 * ssz) &&
+                  al(t.exp_avg_sq, 4 * ssz) && (!hp->amsgrad || al(t.max_exp_avg_sq, 4 * ssz));
+    args.chunk_begin[k + 1] = args.chunk_begin[k] + int(chunks);
+    args.ntensors = k + 1;
   }
   return flush();
 }

@@ -93,7 +93,7 @@ constexpr int kMaxSeg = 256;  // pixels per pass
 template <int VW>  // elements per global load: 8 (16 B), 4 (8 B) or 2 (4 B)
 __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
     const uint16_t* __restrict__ x, long long sn, long long sc, long long sh, int C, int H, int W, int chunks,
-    int pitch_words, uint16_t* __restrict__ rows) {
+    int pitch_words, uint16_t* __restrict__ rows, float* __restrict__ rowsum) {
   extern __shared__ uint32_t tw[];  // [64][pitch_words]
   const int chunk = blockIdx.x % chunks;
   const int yp = (blockIdx.x / chunks) % (H + 2);
@@ -103,11 +103,15 @@ __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
   uint16_t* dst_row = rows + ((long long)(b * (H + 2) + yp) * wp) * cpad + chunk * kCh;
   const int tid = threadIdx.x;
   const uint4 zero = make_uint4(0, 0, 0, 0);
+  // rowsum (optional): per padded row, the sum over x of each channel (border rows 0)
+  float* rsum = rowsum ? rowsum + (long long)(b * (H + 2) + yp) * cpad + chunk * kCh : nullptr;
   if (yp == 0 || yp == H + 1) {
     for (int e = tid; e < wp * 8; e += kVecThreads)
       *reinterpret_cast<uint4*>(dst_row + (long long)(e >> 3) * cpad + (e & 7) * 8) = zero;
+    if (rsum && tid < kCh) rsum[tid] = 0.f;
     return;
   }
+  float csum = 0.f;
   if (tid < 16) {
     const int px = (tid < 8) ? 0 : W + 1;
     *reinterpret_cast<uint4*>(dst_row + (long long)px * cpad + (tid & 7) * 8) = zero;
@@ -139,6 +143,14 @@ __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
       }
     }
     __syncthreads();
+    if (rsum && tid < kCh) {  // channel tid of this row segment, in x order
+      const uint32_t* t = tw + tid * pitch_words;
+      for (int w = 0; w < (seg >> 1); ++w) {
+        const uint32_t v = t[w];
+        csum += __uint_as_float(v << 16);
+        csum += __uint_as_float(v & 0xffff0000u);
+      }
+    }
     const int npairs = seg >> 1;
     for (int e = tid; e < npairs * 8; e += kVecThreads) {
       const int pp = e >> 3, v = e & 7;
@@ -159,6 +171,38 @@ __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
       *reinterpret_cast<uint4*>(dst_row + (px + 1) * cpad + v * 8) = hi;
     }
   }
+  if (rsum && tid < kCh) rsum[tid] = csum;
+}
+
+// Channel sums, stage 1: out[g][c] = sum of rows [64g, 64g+64) of in[.][c]
+// (in = per-row sums from the packer, or the packed rows themselves).
+template <typename T>
+__global__ void chsum_stage1_kernel(const T* __restrict__ in, long long nrows, int ld, int C,
+                                    float* __restrict__ out) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const long long r0 = (long long)blockIdx.x * 64;
+  const long long r1 = r0 + 64 < nrows ? r0 + 64 : nrows;
+  float s = 0.f;
+  for (long long r = r0; r < r1; ++r) {
+    if constexpr (sizeof(T) == 2)
+      s += bf2f(in[r * ld + c]);
+    else
+      s += in[r * ld + c];
+  }
+  out[(long long)blockIdx.x * C + c] = s;
+}
+
+// Stage 2: dbias[c] = sum over groups, fixed order, rounded once.
+__global__ void chsum_stage2_kernel(const float* __restrict__ in, int ngroups, int C, void* out, int dtype) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double s = 0.0;
+  for (int g = 0; g < ngroups; ++g) s += in[(long long)g * C + c];
+  if (dtype == B2_F32)
+    static_cast<float*>(out)[c] = float(s);
+  else
+    static_cast<uint16_t*>(out)[c] = f2bf(float(s));
 }
 
 // Channels-last inputs (channels contiguous, C % 8 == 0): a padded 16-byte copy.
@@ -243,8 +287,70 @@ using namespace b2;
 
 extern "C" {
 
+// Returns the vector width of the NCHW fast path (0: not eligible).
+static int nchw_vec_width(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int W) {
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+  for (int cand : {8, 4, 2})
+    if (sw == 1 && W % cand == 0 && sh % cand == 0 && sc % cand == 0 && sn % cand == 0 && (xa % (2 * cand)) == 0)
+      return cand;
+  return 0;
+}
+
+static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B, int C, int H,
+                                int W, int chunks, void* rows, float* rowsum, void* stream);
+
 b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B,
                             int C, int H, int W, int chunks, void* rows, void* stream) {
+  return pack_rows_impl(x, sn, sc, sh, sw, B, C, H, W, chunks, rows, nullptr, stream);
+}
+
+size_t b2_pack_rows_dbias_workspace_bytes(int B, int C, int H, int W) {
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0) return 256;
+  const long long cpad = ((C + 63) / 64) * 64;
+  const long long prow = (long long)B * (H + 2);
+  const long long m_total = prow * (W + 2);
+  const long long fused = prow * cpad + ((prow + 63) / 64) * C;
+  const long long generic = ((m_total + 63) / 64) * C;
+  const long long floats = fused > generic ? fused : generic;
+  return size_t((floats * 4 + 255) / 256 * 256);
+}
+
+b2_status b2_pack_rows_dbias_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B, int C, int H,
+                                  int W, int chunks, void* rows, void* dbias, int dbias_dtype, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (!dbias || !workspace) return set_error(B2_ERR_INVALID, "b2_pack_rows_dbias_bf16: null pointer");
+  if (dbias_dtype != B2_BF16 && dbias_dtype != B2_F32)
+    return set_error(B2_ERR_INVALID, "b2_pack_rows_dbias_bf16: dtype");
+  if (workspace_bytes < b2_pack_rows_dbias_workspace_bytes(B, C, H, W))
+    return set_error(B2_ERR_WORKSPACE, "b2_pack_rows_dbias_bf16: workspace %zu < %zu bytes", workspace_bytes,
+                     b2_pack_rows_dbias_workspace_bytes(B, C, H, W));
+  if (reinterpret_cast<uintptr_t>(workspace) & 15) return set_error(B2_ERR_INVALID, "b2_pack_rows_dbias_bf16: workspace alignment");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long cpad = (long long)chunks * kCh;
+  const long long prow = (long long)B * (H + 2);
+  float* ws = static_cast<float*>(workspace);
+  if (nchw_vec_width(x, sn, sc, sh, sw, W)) {
+    // the packer itself leaves per-row channel sums: no second pass over dY
+    float* rowsum = ws;
+    float* groups = ws + prow * cpad;
+    B2_TRY(pack_rows_impl(x, sn, sc, sh, sw, B, C, H, W, chunks, rows, rowsum, stream));
+    const long long ng = (prow + 63) / 64;
+    chsum_stage1_kernel<float><<<dim3(unsigned(ng), unsigned((C + 255) / 256)), 256, 0, st>>>(rowsum, prow,
+                                                                                          int(cpad), C, groups);
+    chsum_stage2_kernel<<<(C + 255) / 256, 256, 0, st>>>(groups, int(ng), C, dbias, dbias_dtype);
+  } else {
+    B2_TRY(pack_rows_impl(x, sn, sc, sh, sw, B, C, H, W, chunks, rows, nullptr, stream));
+    const long long m_total = prow * (W + 2);
+    const long long ng = (m_total + 63) / 64;
+    chsum_stage1_kernel<uint16_t><<<dim3(unsigned(ng), unsigned((C + 255) / 256)), 256, 0, st>>>(
+        static_cast<const uint16_t*>(rows), m_total, int(cpad), C, ws);
+    chsum_stage2_kernel<<<(C + 255) / 256, 256, 0, st>>>(ws, int(ng), C, dbias, dbias_dtype);
+  }
+  return check_cuda(cudaGetLastError(), "channel-sum launch");
+}
+
+static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B, int C, int H,
+                                int W, int chunks, void* rows, float* rowsum, void* stream) {
   if (!x || !rows) return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: null pointer");
   if (B <= 0 || C <= 0 || H <= 0 || W <= 0 || chunks < (C + 63) / 64)
     return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: bad shape B=%d C=%d H=%d W=%d chunks=%d", B, C,
@@ -254,14 +360,7 @@ b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, i
   if (blocks >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "b2_pack_rows_bf16: too large");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
-  int vw = 0;  // widest vector the strides and the base address allow
-  for (int cand : {8, 4, 2}) {
-    if (sw == 1 && W % cand == 0 && sh % cand == 0 && sc % cand == 0 && sn % cand == 0 &&
-        (xa % (2 * cand)) == 0) {
-      vw = cand;
-      break;
-    }
-  }
+  const int vw = nchw_vec_width(x, sn, sc, sh, sw, W);  // widest vector the strides and base allow
   if (vw) {
     const int seg = std::min(W, kMaxSeg);
     int pitch = seg / 2;
@@ -271,13 +370,13 @@ b2_status b2_pack_rows_bf16(const void* x, int64_t sn, int64_t sc, int64_t sh, i
     auto* rs = static_cast<uint16_t*>(rows);
     if (vw == 8)
       pack_rows_nchw_vec_kernel<8><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
-                                                                               pitch, rs);
+                                                                               pitch, rs, rowsum);
     else if (vw == 4)
       pack_rows_nchw_vec_kernel<4><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
-                                                                               pitch, rs);
+                                                                               pitch, rs, rowsum);
     else
       pack_rows_nchw_vec_kernel<2><<<unsigned(blocks), kVecThreads, smem, st>>>(xs, sn, sc, sh, C, H, W, chunks,
-                                                                               pitch, rs);
+                                                                               pitch, rs, rowsum);
     return check_cuda(cudaGetLastError(), "pack_rows(nchw) launch");
   }
   if (sc == 1 && C % 8 == 0 && sw % 8 == 0 && sh % 8 == 0 && sn % 8 == 0 && (xa & 15) == 0) {

@@ -136,8 +136,23 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
   const int B = int(input.size(0)), Cin = int(input.size(1)), H = int(input.size(2)), W = int(input.size(3));
   const int Cout = int(weight.size(0));
   const c10::DeviceIndex dev = input.device().index();
-  at::Tensor dy_rows = pack_rows(grad_output);
   at::Tensor dx, dw, db;
+  at::Tensor dy_rows;
+  if (output_mask[2]) {
+    // the dY packer also reduces dbias (one pass over dY, deterministic order)
+    const int ch = chunks_of(Cout);
+    dy_rows = empty({int64_t(B) * (H + 2) * (W + 2), int64_t(ch) * 64}, at::kBFloat16, dev);
+    db = empty({Cout}, grad_output.scalar_type(), dev);
+    const size_t ws_bytes = b2_pack_rows_dbias_workspace_bytes(B, Cout, H, W);
+    at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
+    materialize(grad_output);
+    XDNA_B2(b2_pack_rows_dbias_bf16(grad_output.data_ptr(), grad_output.stride(0), grad_output.stride(1),
+                                    grad_output.stride(2), grad_output.stride(3), B, Cout, H, W, ch, dy_rows.data_ptr(),
+                                    db.data_ptr(), B2_BF16, ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
+    count_launch("pack_rows_dbias");
+  } else {
+    dy_rows = pack_rows(grad_output);
+  }
   if (output_mask[0]) {
     at::Tensor wkd = pack_weight(weight, true);
     dx = empty({B, Cin, H, W}, at::kBFloat16, dev, out_format(input));
@@ -164,9 +179,6 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
                                         padding, dilation, transposed, output_padding, groups, {false, true, false});
       to_cuda_nosync(dw).copy_(std::get<1>(r));
     }
-  }
-  if (output_mask[2]) {
-    db = adopt(to_cuda(grad_output).sum(at::IntArrayRef{0, 2, 3}));
   }
   if (output_mask[0]) note_dgrad();
   return {dx, dw, db};

@@ -35,6 +35,8 @@ SIGNATURES = {
     "b2_abi_version": [],
     "b2_device_status": [i32, C.POINTER(i32)],
     "b2_pack_rows_bf16": [vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp, vp],
+    "b2_pack_rows_dbias_workspace_bytes": [i32, i32, i32, i32],
+    "b2_pack_rows_dbias_bf16": [vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp, vp, i32, vp, sz, vp],
     "b2_pack_weight_fwd_bf16": [vp, i32, i32, i32, vp, vp],
     "b2_pack_weight_dgrad_bf16": [vp, i32, i32, i32, vp, vp],
     "b2_nchw_to_nhwc_bf16": [vp, vp, i32, i32, i32, vp],
@@ -56,6 +58,7 @@ SIGNATURES = {
     "b2_region_maxpool2_bwd_bf16": [vp, vp, vp, i64, i64, i64, vp],
 }
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
+             "b2_pack_rows_dbias_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 

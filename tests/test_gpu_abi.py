@@ -73,6 +73,32 @@ def test_pack_rows_bit_exact(cuda, shape, channels_last):
     assert np.array_equal(got, want)
 
 
+@pytest.mark.parametrize("shape", [(4, 256, 9, 72), (2, 70, 5, 36), (3, 64, 6, 9), (2, 130, 7, 18)])
+@pytest.mark.parametrize("channels_last", [False, True])
+def test_pack_rows_dbias(cuda, shape, channels_last):
+    """Packed rows bit-exact, plus dbias = sum over (b, y, x) (fixed-order fp32 sums)."""
+    B, Cc, H, W = shape
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(*shape, generator=g).bfloat16()
+    xd = x.to(cuda)
+    if channels_last:
+        xd = xd.contiguous(memory_format=torch.channels_last)
+    ch = -(-Cc // 64)
+    rows = torch.empty(B * (H + 2) * (W + 2), ch * 64, dtype=torch.bfloat16, device=cuda)
+    ws_bytes = _abi.lib().b2_pack_rows_dbias_workspace_bytes(B, Cc, H, W)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
+    db = torch.empty(Cc, dtype=torch.float32, device=cuda)
+    db16 = torch.empty(Cc, dtype=torch.bfloat16, device=cuda)
+    for out, dt in ((db, _abi.B2_F32), (db16, _abi.B2_BF16)):
+        _abi.call("b2_pack_rows_dbias_bf16", xd.data_ptr(), *xd.stride(), B, Cc, H, W, ch, rows.data_ptr(),
+                  out.data_ptr(), dt, ws.data_ptr(), ws_bytes, st())
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(rows), oracle.pack_rows(bits(x)))
+    ref = x.double().sum((0, 2, 3))
+    assert (db.double().cpu() - ref).abs().max().item() <= 1e-4 * max(1.0, ref.abs().max().item())
+    assert torch.equal(db16.cpu(), db.cpu().bfloat16())
+
+
 @pytest.mark.parametrize("co_ci", [(128, 70), (100, 64), (3, 10), (256, 130)])
 def test_pack_weights_bit_exact(cuda, co_ci):
     Cout, Cin = co_ci
