@@ -20,6 +20,7 @@
 // torch_xdna_device.cpp:1968-1985, 2660-2679).
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "b2_common.cuh"
@@ -116,8 +117,7 @@ __device__ __forceinline__ uint16_t cvt1(float v) {
 
 // Output row of a conv tile: base pointer of pixel (b, y, x), or null when the
 // padded-grid row is a border / tail row that produces nothing.
-__device__ __forceinline__ uint16_t* conv_row_base(const Params& p, int mt, int row) {
-  const int prow = mt * BM + row;
+__device__ __forceinline__ uint16_t* conv_row_base_at(const Params& p, int prow) {
   if (prow >= p.m_total) return nullptr;
   const int plane = p.hp * p.wp;
   const int b = prow / plane;
@@ -126,6 +126,9 @@ __device__ __forceinline__ uint16_t* conv_row_base(const Params& p, int mt, int 
   const int x = rem - y * p.wp;
   if (y >= p.H || x >= p.W) return nullptr;
   return static_cast<uint16_t*>(p.out) + b * p.osn + y * p.osh + x * p.osw;
+}
+__device__ __forceinline__ uint16_t* conv_row_base(const Params& p, int mt, int row) {
+  return conv_row_base_at(p, mt * BM + row);
 }
 
 __device__ __forceinline__ void epi_conv(const Params& p, uint16_t* base, int col0, int lane,
@@ -436,6 +439,204 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// The SM-pair variant for the conv (fwd / dgrad) with Cout > 128: a cluster of
+// two CTAs computes a 256-pixel x 256-channel tile with tcgen05.mma
+// .cta_group::2 (M=256, N=256).  Each CTA TMA-loads its own 128 A rows and its
+// own 128-row half of the B tile (no multicast; the loads signal the leader
+// CTA's "full" barrier, which expects both CTAs' bytes), so per k-block each
+// SM stages 32 KB instead of 48 KB and the ring is 6 stages deep.  The leader's
+// single MMA thread issues for both SMs and commits to the "empty" / "tmem full"
+// barriers of both CTAs at once; each CTA drains its own 128 accumulator rows
+// (all 256 columns) and releases the accumulator buffer through the leader's
+// "tmem empty" barrier.  Same bounded waits as the single-CTA kernel.
+// ---------------------------------------------------------------------------
+template <int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    igemm_pair_conv_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                           const Params p) {
+  constexpr int BN = 256;        // output channels per pair tile
+  constexpr int kBHalf = 128;    // B rows each CTA loads
+  constexpr int kStageBytes = kABytes + kBHalf * BK * 2;
+  constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, false, false);
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 2 * kEpiWarps);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialized before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int tiles_m = (p.m_total + 255) / 256;
+  const int ntiles = tiles_m * p.tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ producer (both CTAs) -----------------
+      tma_prefetch_desc(&tma_a);
+      tma_prefetch_desc(&tma_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_par[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        const int nt = t % p.tiles_n, mt = t / p.tiles_n;
+        const int row0 = mt * 256 + int(rank) * 128;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb_local, 2 * kStageBytes);
+          last_par[stage] = int(phase);
+          const uint32_t fb = mapa_shared(fb_local, 0);
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+          const int chunk = kb / 9, tp = kb - chunk * 9;
+          const int dy = tp / 3, dx = tp - dy * 3;
+          tma_load_3d_pair(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, 0);
+          tma_load_3d_pair(sb, &tma_b, fb, kb * BK, nt * BN + int(rank) * kBHalf, 0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && leader) {
+        for (int s = 0; s < STAGES; ++s)
+          if (last_par[s] >= 0) mbar_wait(smem_u32(&full[s]), uint32_t(last_par[s]), p.status, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------ MMA issuer (leader CTA) --------------
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, p.status, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
+          const uint32_t sb = sa + kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma_pair(d_tmem, ad, bd, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit_pair_mc(smem_u32(&empty[stage]), uint16_t(0x3));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(smem_u32(&tfull[acc]), uint16_t(0x3));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      tc_commit_pair(smem_u32(mma_done));
+      mbar_wait(smem_u32(mma_done), 0, p.status, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------- epilogue (both CTAs) ------------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    constexpr int kChunks = BN / 64;
+    const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty[0]), 0), mapa_shared(smem_u32(&tempty[1]), 0)};
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster; t < ntiles; t += nclusters) {
+      const int nt = t % p.tiles_n, mt = t / p.tiles_n;
+      uint16_t* obase = conv_row_base_at(p, mt * 256 + int(rank) * 128 + row);
+      bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
+#pragma unroll 1
+      for (int j = 0; j < kChunks; ++j) {
+        uint32_t r[32];
+        tmem_ld32(taddr + j * 32, r);
+        tc_wait_ld();
+        epi_conv(p, obase, nt * BN + half * (BN / 2) + j * 32, lane, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(smem_u32(&tempty[acc]));
+        else
+          mbar_arrive_remote(tempty_leader[acc]);
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its pair may still signal or read it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw, int dtype,
                                     int splits, int Cout, int Cin) {
@@ -487,6 +688,35 @@ b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
 
 constexpr int kStages128 = 6;
 constexpr int kStages256 = 4;
+constexpr int kStagesPair = 6;
+
+b2_status launch_pair_conv(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  auto kern = igemm_pair_conv_kernel<kStagesPair>;
+  constexpr size_t smem = size_t(kStagesPair) * (kABytes + 128 * BK * 2) + 1024 + 256;
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[dev]) {
+    B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                      "cudaFuncSetAttribute(smem, pair)"));
+    configured[dev] = true;
+  }
+  const int tiles = ((p.m_total + 255) / 256) * p.tiles_n;
+  if (tiles <= 0) return B2_OK;
+  const int clusters = std::min(tiles, sm_count(dev) / 2);
+  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, p);
+  return check_cuda(cudaGetLastError(), "igemm pair launch");
+}
+
+// SM-pair MMA for wide convolutions unless B2_PAIR_MMA=0 (A/B switch).
+bool pair_mma_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_PAIR_MMA");
+    return !e || e[0] != '0';
+  }();
+  return on;
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -504,7 +734,9 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   const int cpad = chunks * 64;
   const int ktot = chunks * 9 * 64;
   const bool wide = Cout > 128 && (Cout % 256 == 0 || Cout % 256 > 128);
+  const bool pair = wide && pair_mma_enabled();
   const int BN = wide ? 256 : 128;
+  const uint32_t b_box = pair ? 128u : uint32_t(BN);  // the pair kernel loads half of B per CTA
 
   CUtensorMap ta, tb;
   {
@@ -516,7 +748,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   {
     const uint64_t dims[3] = {uint64_t(ktot), uint64_t(Cout), 1};
     const uint64_t strides[2] = {uint64_t(ktot) * 2, uint64_t(ktot) * 2 * Cout};
-    const uint32_t box[3] = {64, uint32_t(BN), 1};
+    const uint32_t box[3] = {64, b_box, 1};
     B2_TRY(encode_tmap(&tb, wk, 3, dims, strides, box, true));
   }
   Params p{};
@@ -543,6 +775,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   p.alpha = 1.f;
   p.status = device_status_ptr();
   const int tiles = p.tiles_m * p.tiles_n;
+  if (pair) return launch_pair_conv(ta, tb, p, st);
   if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
   return launch<128, kStages128, kConv, false, false>(ta, tb, p, tiles, st);
 }

@@ -368,3 +368,26 @@ def test_regions_large_sqdiff(cuda):
     _abi.call("b2_region_sqdiff_sum_bf16", ad.data_ptr(), bd.data_ptr(), a.numel(), acc.data_ptr(), st())
     want = oracle.sqdiff_sum(bits(a), bits(b))
     assert abs(acc.item() - want) <= 1e-5 * want
+
+
+def test_single_cta_conv_path_still_matches(cuda):
+    """Wide convolutions run the SM-pair kernel by default; B2_PAIR_MMA=0 keeps
+    the single-CTA kernel.  Check that one too, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    code = (
+        "import sys; sys.path[:0] = [%r, %r]\n"
+        "import torch\n"
+        "from tests.test_gpu_abi import _conv_inputs, _gpu_conv, close\n"
+        "x, w, b, dy = _conv_inputs(None, 4, 256, 18, 18, 320, True, seed=9)\n"
+        "y, dx, dw = _gpu_conv(torch.device('cuda', 0), x, w, b, dy)\n"
+        "with torch.no_grad():\n"
+        "    y_ref = torch.nn.functional.conv2d(x.float(), w.float(), b.float(), padding=1)\n"
+        "close(y, y_ref)\n"
+        "print('ok')\n" % (str(root), str(root / "pytorch-xdna2_b200")))
+    env = dict(os.environ, B2_PAIR_MMA="0")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
