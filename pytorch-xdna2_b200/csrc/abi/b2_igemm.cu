@@ -168,9 +168,8 @@ __device__ __forceinline__ void epi_conv(const Params& p, uint16_t* base, int co
   }
 }
 
-__device__ __forceinline__ void epi_wgrad(const Params& p, int split, int tap, int mt, int col0,
-                                          int row, const uint32_t (&r)[32]) {
-  const int co = mt * BM + row;
+__device__ __forceinline__ void epi_wgrad_co(const Params& p, int split, int tap, int co, int col0,
+                                             const uint32_t (&r)[32]) {
   if (co >= p.M) return;
   float* dst = p.partial + ((((long long)split * 9 + tap) * p.M + co) * p.N);
   if (col0 + 32 <= p.N && (p.N % 4) == 0) {
@@ -184,6 +183,10 @@ __device__ __forceinline__ void epi_wgrad(const Params& p, int split, int tap, i
 #pragma unroll
   for (int c = 0; c < 32; ++c)
     if (col0 + c < p.N) dst[col0 + c] = __uint_as_float(r[c]);
+}
+__device__ __forceinline__ void epi_wgrad(const Params& p, int split, int tap, int mt, int col0, int row,
+                                          const uint32_t (&r)[32]) {
+  epi_wgrad_co(p, split, tap, mt * BM + row, col0, r);
 }
 
 __device__ __forceinline__ float load_c(const Params& p, long long i) {
@@ -451,14 +454,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (all 256 columns) and releases the accumulator buffer through the leader's
 // "tmem empty" barrier.  Same bounded waits as the single-CTA kernel.
 // ---------------------------------------------------------------------------
-template <int STAGES>
+template <int STAGES, int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    igemm_pair_conv_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                           const Params p) {
-  constexpr int BN = 256;        // output channels per pair tile
+    igemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                      const Params p) {
+  static_assert(KIND == kConv || KIND == kWgrad, "pair kernel: conv or wgrad");
+  constexpr bool MN = KIND == kWgrad;  // wgrad: both operands M/N-major
+  constexpr int BN = 256;        // N per pair tile
   constexpr int kBHalf = 128;    // B rows each CTA loads
   constexpr int kStageBytes = kABytes + kBHalf * BK * 2;
-  constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, false, false);
+  constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, MN, MN);
   constexpr uint32_t kTmemCols = 2 * BN;
 
   extern __shared__ uint8_t smem_raw[];
@@ -502,8 +507,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // both CTAs' barriers initialized before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int tiles_m = (p.m_total + 255) / 256;
-  const int ntiles = tiles_m * p.tiles_n;
+  // conv: tiles (256-pixel block, 256-channel block); wgrad: (split, 256-co
+  // block, tap, 256-ci block), as in decode_tile with M tiles of 256
+  const int ntiles = KIND == kConv ? p.tiles_m * p.tiles_n : p.splits * p.tiles_m * 9 * p.ci_blocks;
+  auto decode = [&](int t, int& mt, int& nt, int& split, int& tap, int& kb0, int& kb1) {
+    if (KIND == kConv) {
+      nt = t % p.tiles_n;
+      mt = t / p.tiles_n;
+      split = 0;
+      tap = 0;
+      kb0 = 0;
+      kb1 = p.num_kb;
+    } else {
+      nt = t % p.ci_blocks;
+      t /= p.ci_blocks;
+      tap = t % 9;
+      t /= 9;
+      mt = t % p.tiles_m;
+      split = t / p.tiles_m;
+      kb0 = split * p.kb_per_split;
+      kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+    }
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -517,9 +542,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int s = 0; s < STAGES; ++s) last_par[s] = -1;
       bool ok = true;
       for (int t = cluster; t < ntiles && ok; t += nclusters) {
-        const int nt = t % p.tiles_n, mt = t / p.tiles_n;
+        int mt, nt, split, tap, kb0, kb1;
+        decode(t, mt, nt, split, tap, kb0, kb1);
         const int row0 = mt * 256 + int(rank) * 128;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, p.status, abort_flag)) {
             ok = false;
             break;
@@ -530,10 +556,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t fb = mapa_shared(fb_local, 0);
           const uint32_t sa = smem_u32(smem + stage * kStageBytes);
           const uint32_t sb = sa + kABytes;
-          const int chunk = kb / 9, tp = kb - chunk * 9;
-          const int dy = tp / 3, dx = tp - dy * 3;
-          tma_load_3d_pair(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, 0);
-          tma_load_3d_pair(sb, &tma_b, fb, kb * BK, nt * BN + int(rank) * kBHalf, 0);
+          if constexpr (KIND == kConv) {
+            const int chunk = kb / 9, tp = kb - chunk * 9;
+            const int dy = tp / 3, dx = tp - dy * 3;
+            tma_load_3d_pair(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, 0);
+            tma_load_3d_pair(sb, &tma_b, fb, kb * BK, nt * BN + int(rank) * kBHalf, 0);
+          } else {
+            // A = dY rows (co contiguous), this CTA's 128 co; B = X rows shifted by the tap
+            const int dy = tap / 3, dx = tap - dy * 3;
+            const int ci0 = nt * BN + int(rank) * kBHalf;
+            tma_load_3d_pair(sa, &tma_a, fb, row0, kb * BK + p.a_row_shift, 0);
+            tma_load_3d_pair(sa + 8192, &tma_a, fb, row0 + 64, kb * BK + p.a_row_shift, 0);
+            tma_load_3d_pair(sb, &tma_b, fb, ci0, kb * BK + dy * p.wp + dx, 0);
+            tma_load_3d_pair(sb + 8192, &tma_b, fb, ci0 + 64, kb * BK + dy * p.wp + dx, 0);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -555,13 +591,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = cluster; t < ntiles && ok; t += nclusters) {
+        int mt, nt, split, tap, kb0, kb1;
+        decode(t, mt, nt, split, tap, kb0, kb1);
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(smem_u32(&full[stage]), phase, p.status, abort_flag)) {
             ok = false;
             break;
@@ -571,9 +609,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + kABytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
-            tc_mma_pair(d_tmem, ad, bd, kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+            const uint64_t ad = MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024) : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024) : smem_desc_sw128(sb + k * 32, 16, 1024);
+            tc_mma_pair(d_tmem, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(smem_u32(&empty[stage]), uint16_t(0x3));
           if (++stage == STAGES) {
@@ -600,8 +638,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = cluster; t < ntiles; t += nclusters) {
-      const int nt = t % p.tiles_n, mt = t / p.tiles_n;
-      uint16_t* obase = conv_row_base_at(p, mt * 256 + int(rank) * 128 + row);
+      int mt, nt, split, tap, kb0, kb1;
+      decode(t, mt, nt, split, tap, kb0, kb1);
+      const int grow = mt * 256 + int(rank) * 128 + row;  // pixel (conv) or co (wgrad) of this thread
+      uint16_t* obase = nullptr;
+      if constexpr (KIND == kConv) obase = conv_row_base_at(p, grow);
       bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -613,7 +654,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         uint32_t r[32];
         tmem_ld32(taddr + j * 32, r);
         tc_wait_ld();
-        epi_conv(p, obase, nt * BN + half * (BN / 2) + j * 32, lane, r);
+        const int col0 = nt * BN + half * (BN / 2) + j * 32;
+        if constexpr (KIND == kConv)
+          epi_conv(p, obase, col0, lane, r);
+        else
+          epi_wgrad_co(p, split, tap, grow, col0, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -690,8 +735,9 @@ constexpr int kStages128 = 6;
 constexpr int kStages256 = 4;
 constexpr int kStagesPair = 6;
 
-b2_status launch_pair_conv(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
-  auto kern = igemm_pair_conv_kernel<kStagesPair>;
+template <int KIND>
+b2_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles, cudaStream_t st) {
+  auto kern = igemm_pair_kernel<kStagesPair, KIND>;
   constexpr size_t smem = size_t(kStagesPair) * (kABytes + 128 * BK * 2) + 1024 + 256;
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
@@ -702,7 +748,6 @@ b2_status launch_pair_conv(const CUtensorMap& ta, const CUtensorMap& tb, const P
                       "cudaFuncSetAttribute(smem, pair)"));
     configured[dev] = true;
   }
-  const int tiles = ((p.m_total + 255) / 256) * p.tiles_n;
   if (tiles <= 0) return B2_OK;
   const int clusters = std::min(tiles, sm_count(dev) / 2);
   kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, p);
@@ -775,29 +820,36 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   p.alpha = 1.f;
   p.status = device_status_ptr();
   const int tiles = p.tiles_m * p.tiles_n;
-  if (pair) return launch_pair_conv(ta, tb, p, st);
+  if (pair) {
+    Params pp = p;
+    pp.tiles_m = int((m_total + 255) / 256);  // 256-pixel tiles
+    return launch_pair<kConv>(ta, tb, pp, pp.tiles_m * pp.tiles_n, st);
+  }
   if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
   return launch<128, kStages128, kConv, false, false>(ta, tb, p, tiles, st);
 }
 
 struct WgradPlan {
   int BN, ci_blocks, tiles_m, num_kb, splits, kb_per_split;
+  bool pair;  // SM-pair kernel: 256-co x 256-ci tiles per cluster of two CTAs
   long long m_total;
   size_t workspace;
 };
 
-WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms) {
+WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow_pair) {
   WgradPlan w{};
   w.m_total = (long long)B * (H + 2) * (W + 2);
+  w.pair = allow_pair && Cin > 128 && Cout > 128;
   w.BN = Cin > 128 ? 256 : 128;
   w.ci_blocks = (Cin + w.BN - 1) / w.BN;
-  w.tiles_m = (Cout + BM - 1) / BM;
+  w.tiles_m = (Cout + (w.pair ? 255 : BM - 1)) / (w.pair ? 256 : BM);
   w.num_kb = int((w.m_total + BK - 1) / BK);
-  // Split-K so that the tiles fill the SMs in whole waves: tiles are long
-  // (thousands of k-blocks), so a partial last wave would idle SMs for a
-  // whole tile's duration.
+  // Split-K so that the tiles fill the SMs (pairs of SMs for the pair kernel)
+  // in whole waves: tiles are long (thousands of k-blocks), so a partial last
+  // wave would idle SMs for a whole tile's duration.
+  const int units = w.pair ? sms / 2 : sms;
   const int base = w.tiles_m * 9 * w.ci_blocks;
-  int splits = base >= sms ? 1 : sms / base;
+  int splits = base >= units ? 1 : units / base;
   splits = std::max(1, std::min(splits, w.num_kb / 16));
   w.kb_per_split = (w.num_kb + splits - 1) / splits;
   w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
@@ -830,7 +882,7 @@ size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout) 
   if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return 16;
   int dev = 0;
   cudaGetDevice(&dev);
-  return std::max<size_t>(16, wgrad_plan(B, Cin, H, W, Cout, sm_count(dev)).workspace);
+  return std::max<size_t>(16, wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled()).workspace);
 }
 
 b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, int dw_dtype, int B,
@@ -845,7 +897,7 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
     return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: operands must be 16-byte aligned");
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled());
   if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
     return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
   if (workspace_bytes < w.workspace)
@@ -885,7 +937,9 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
   p.alpha = 1.f;
   p.status = device_status_ptr();
   const int tiles = w.splits * w.tiles_m * 9 * w.ci_blocks;
-  if (w.BN == 256)
+  if (w.pair)
+    B2_TRY(launch_pair<kWgrad>(ta, tb, p, tiles, st));
+  else if (w.BN == 256)
     B2_TRY((launch<256, kStages256, kWgrad, true, true>(ta, tb, p, tiles, st)));
   else
     B2_TRY((launch<128, kStages128, kWgrad, true, true>(ta, tb, p, tiles, st)));
@@ -1040,7 +1094,7 @@ b2_status b2_conv3x3_wgrad_noalloc(const void* dy_rows, const void* x_rows, void
                      Cout, Cin, per_split, kNoAllocScratchBytes);
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), /*allow_pair=*/false);
   if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
     return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad_noalloc: too many padded rows");
   if (w.workspace > kNoAllocScratchBytes) {  // fewer splits, same result up to fp32 summation order

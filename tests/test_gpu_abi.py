@@ -385,8 +385,11 @@ def test_single_cta_conv_path_still_matches(cuda):
         "x, w, b, dy = _conv_inputs(None, 4, 256, 18, 18, 320, True, seed=9)\n"
         "y, dx, dw = _gpu_conv(torch.device('cuda', 0), x, w, b, dy)\n"
         "with torch.no_grad():\n"
-        "    y_ref = torch.nn.functional.conv2d(x.float(), w.float(), b.float(), padding=1)\n"
-        "close(y, y_ref)\n"
+        "    xf, wf, dyf = x.float(), w.float(), dy.float()\n"
+        "    y_ref = torch.nn.functional.conv2d(xf, wf, b.float(), padding=1)\n"
+        "    dx_ref, dw_ref, _ = torch.ops.aten.convolution_backward(dyf, xf, wf, None, [1, 1], [1, 1], [1, 1],"
+        " False, [0, 0], 1, [True, True, False])\n"
+        "close(y, y_ref); close(dx, dx_ref); close(dw, dw_ref)\n"
         "print('ok')\n" % (str(root), str(root / "pytorch-xdna2_b200")))
     env = dict(os.environ, B2_PAIR_MMA="0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
