@@ -250,7 +250,7 @@ def run_ours(args):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
                      "frac": round(achieved / bf16_peak, 4), "traffic": conv_traffic_bytes(),
                      "traffic_source": "ncu dram__bytes_read+write of the three kernels at B64, x2 (profiles/)",
-                     "kernel": "conv3x3 implicit GEMM fwd+dgrad+wgrad (tcgen05)",
+                     "kernel": "conv3x3 implicit GEMM fwd+dgrad+wgrad (tcgen05 cta_group::2 SM-pair kernel)",
                      "per_launch_ms": {k: round(v, 4) for k, v in kt.items()},
                      "flops_per_launch": flops_dir, "peak_kind": peak_kind},
         "gpu_launches": launches,

@@ -79,7 +79,7 @@ void launch_wgrad(const at::Tensor& dy_rows, const at::Tensor& x_rows, void* gw,
   const int dt = dtype == at::kFloat ? B2_F32 : B2_BF16;
   XDNA_B2(b2_conv3x3_wgrad(dy_rows.data_ptr(), x_rows.data_ptr(), gw, dt, B, Cin, H, W, Cout, ws.data_ptr(),
                            size_t(ws.numel()) * 4, stream(dev)));
-  count_launch("conv3x3.wgrad");
+  count_launch("conv3x3.wgrad", 2);  // igemm + split-K reduce
 }
 
 bool deferral_enabled() {
@@ -149,7 +149,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     XDNA_B2(b2_pack_rows_dbias_bf16(grad_output.data_ptr(), grad_output.stride(0), grad_output.stride(1),
                                     grad_output.stride(2), grad_output.stride(3), B, Cout, H, W, ch, dy_rows.data_ptr(),
                                     db.data_ptr(), B2_BF16, ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
-    count_launch("pack_rows_dbias");
+    count_launch("pack_rows_dbias", 3);  // pack + two channel-sum stages
   } else {
     dy_rows = pack_rows(grad_output);
   }
