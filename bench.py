@@ -73,10 +73,19 @@ class Clocks:
         self.proc = None
 
     def __enter__(self):
+        self.first = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # nvidia-smi takes a moment to start: wait for its first sample (taken
+            # before the timed region, so it is not counted) before timing starts
+            import threading
+            box = []
+            t = threading.Thread(target=lambda: box.append(self.proc.stdout.readline()), daemon=True)
+            t.start()
+            t.join(timeout=5.0)
+            self.first = box[0] if box else None
         except OSError:
             self.proc = None
         return self
@@ -397,7 +406,7 @@ def main():
     ap.add_argument("--hw", type=int, default=HW)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
