@@ -376,6 +376,243 @@ def run_reference(args):
     }
 
 
+# ------------------------------------------------- the other BASELINE configs
+# Model definitions written from BASELINE.json's config descriptions; used by
+# `--workload` and by the GPU parity tests (tests/test_gpu_workloads.py).
+
+def make_mlp():
+    """Config 3: Linear 1024-4096-4096-4096-1024 with GELU between."""
+    import torch.nn as nn
+    return nn.Sequential(nn.Linear(1024, 4096), nn.GELU(), nn.Linear(4096, 4096), nn.GELU(),
+                         nn.Linear(4096, 4096), nn.GELU(), nn.Linear(4096, 1024))
+
+
+def make_style_generator():
+    """Config 4 generator: 9x9 conv 3->32, stride-2 3x3 convs to 64 and 128, 5
+    residual blocks (3x3 conv-BN-ReLU, 128 ch), two (nearest 2x upsample + 3x3
+    conv) stages back to 32, 9x9 conv to 3."""
+    import torch.nn as nn
+
+    def cbr(ci, co, k, s=1):
+        return [nn.Conv2d(ci, co, k, stride=s, padding=k // 2, bias=False), nn.BatchNorm2d(co), nn.ReLU()]
+
+    class Res(nn.Module):
+        def __init__(self, c):
+            super().__init__()
+            self.body = nn.Sequential(*cbr(c, c, 3), nn.Conv2d(c, c, 3, padding=1, bias=False), nn.BatchNorm2d(c))
+
+        def forward(self, x):
+            return torch.relu(self.body(x) + x)
+
+    layers = cbr(3, 32, 9) + cbr(32, 64, 3, 2) + cbr(64, 128, 3, 2) + [Res(128) for _ in range(5)]
+    layers += [nn.Upsample(scale_factor=2, mode="nearest")] + cbr(128, 64, 3)
+    layers += [nn.Upsample(scale_factor=2, mode="nearest")] + cbr(64, 32, 3)
+    layers += [nn.Conv2d(32, 3, 9, padding=4)]
+    return nn.Sequential(*layers)
+
+
+
+
+class StyleLoss(torch.nn.Module):
+    """Config 4 loss: frozen random-init VGG19 features; content MSE over the
+    concatenated taps plus Gram-matrix style MSE.  Follows the module pattern
+    `fuse_perceptual_loss` accepts (perceptual_vgg.model.features,
+    feature_layers, compute_perceptual_loss)."""
+
+    def __init__(self, taps=(3, 8, 17), style_weight=1e-2):
+        super().__init__()
+        from torchvision.models import vgg19
+        self.perceptual_vgg = torch.nn.Module()
+        self.perceptual_vgg.model = vgg19(weights=None)
+        self.perceptual_vgg.feature_layers = tuple(taps)
+        self.perceptual_vgg.use_norm = False
+        for q in self.perceptual_vgg.parameters():
+            q.requires_grad_(False)
+        self.style_weight = style_weight
+
+    def features(self, x):
+        maps, y = [], x
+        for i in range(max(self.perceptual_vgg.feature_layers) + 1):
+            y = self.perceptual_vgg.model.features[i](y)
+            if i in self.perceptual_vgg.feature_layers:
+                maps.append(y)
+        return maps
+
+    def compute_perceptual_loss(self, x, t):
+        fx, ft = self.features(x), self.features(t)
+        return torch.nn.functional.mse_loss(torch.cat([a.reshape(-1) for a in fx]),
+                                            torch.cat([b.reshape(-1) for b in ft]))
+
+    @staticmethod
+    def gram(f):
+        b, c, h, w = f.shape
+        f = f.reshape(b, c, h * w)
+        return torch.bmm(f, f.transpose(1, 2)) / (c * h * w)
+
+    def forward(self, out, target, style):
+        content = self.compute_perceptual_loss(out, target)
+        with torch.no_grad():
+            gs = [self.gram(f) for f in self.features(style)]
+        go = [self.gram(f) for f in self.features(out)]
+        sl = sum(torch.nn.functional.mse_loss(a.float(), b.float()) for a, b in zip(go, gs))
+        return content.float() + self.style_weight * sl
+
+
+def _timed(fn, steps, warmup, device_sync):
+    for _ in range(warmup):
+        fn()
+    device_sync()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        fn()
+    device_sync()
+    return (time.perf_counter() - t0) / steps
+
+
+def run_workload(args):
+    """One JSON line for a non-headline BASELINE config (1, 3, 4 or 5)."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    import xdna_train
+    xdna_train.register_xdna_device()
+    world, rank, local = setup_dist(args)
+    X = torch.device("xdna", local)
+    sync = lambda: torch.xdna.synchronize()  # noqa: E731
+    cpu = lambda: None  # noqa: E731
+    w = args.workload
+    out = {"workload": w, "n_gpus": world, "dtype": "bf16", "data": "synthetic", "steps": args.steps,
+           "warmup": args.warmup}
+
+    def cpu_rate(make_step, steps=2, warmup=1):
+        if rank != 0 or world != 1 or args.no_cpu_baseline:
+            return None
+        return _timed(make_step(), steps, warmup, cpu)
+
+    if w == "readme":
+        # config 1: Conv2d(128,128,3,pad=1) BF16, x [16,128,36,36], target 0, Adam 1e-3
+        def make(dev):
+            torch.manual_seed(0)
+            model = nn.Conv2d(128, 128, 3, padding=1).bfloat16().to(dev)
+            opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
+            x = torch.randn(16, 128, 36, 36, dtype=torch.bfloat16).to(dev)
+            tgt = torch.zeros_like(x)
+
+            def step():
+                opt.zero_grad(set_to_none=True)
+                loss = F.mse_loss(model(x).float(), tgt.float())
+                loss.backward()
+                opt.step()
+            return step
+        dt = _timed(make(X), args.steps, args.warmup, sync)
+        out.update(metric="README Conv2d training step it/s (BASELINE config 1)", value=round(1 / dt, 2),
+                   unit="it/s", ms_per_step=round(dt * 1e3, 4),
+                   tflops=round(18.35e9 / dt / 1e12, 1))
+        c = cpu_rate(lambda: make("cpu"), steps=5, warmup=1)
+    elif w == "mlp":
+        # config 3: MLP B512, autocast BF16 over FP32 params (FP32 master state), Adam 1e-4
+        def make(dev):
+            torch.manual_seed(0)
+            model = make_mlp().to(dev)
+            opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True)
+            x = torch.randn(512, 1024).to(dev)
+            tgt = torch.randn(512, 1024).to(dev)
+            dtype = "xdna" if torch.device(dev).type == "xdna" else "cpu"
+
+            def step():
+                opt.zero_grad(set_to_none=True)
+                with torch.autocast(dtype, dtype=torch.bfloat16):
+                    loss = F.mse_loss(model(x).float(), tgt)
+                loss.backward()
+                opt.step()
+            return step
+        dt = _timed(make(X), args.steps, args.warmup, sync)
+        out.update(metric="MLP training TFLOP/s (BASELINE config 3)", value=round(128.85e9 / dt / 1e12, 2),
+                   unit="TFLOP/s", ms_per_step=round(dt * 1e3, 4))
+        c = cpu_rate(lambda: make("cpu"))
+        if c:
+            c = c  # seconds per step
+    elif w == "style":
+        # config 4: B40 36x36 style transfer, Adam 1e-3, with and without the region
+        from xdna_train import regions
+
+        def make(dev, fused):
+            torch.manual_seed(0)
+            gen = make_style_generator().bfloat16().to(dev)
+            crit = StyleLoss().bfloat16().to(dev)
+            if fused:
+                assert regions.fuse_perceptual_loss(crit)
+            opt = torch.optim.Adam(gen.parameters(), lr=1e-3, fused=True)
+            g = torch.Generator().manual_seed(1)
+            x = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
+            tgt = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
+            sty = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
+
+            def step():
+                opt.zero_grad(set_to_none=True)
+                loss = crit(gen(x), tgt, sty)
+                loss.backward()
+                opt.step()
+            return step
+        dt = _timed(make(X, False), args.steps, args.warmup, sync)
+        dtf = _timed(make(X, True), args.steps, args.warmup, sync)
+        out.update(metric="style-transfer training it/s (BASELINE config 4)", value=round(1 / dt, 2), unit="it/s",
+                   ms_per_step=round(dt * 1e3, 4), fused_perceptual_loss_it_s=round(1 / dtf, 2))
+        c = cpu_rate(lambda: make("cpu", False))
+    elif w == "resnet50":
+        # config 5: ResNet-50 224x224, per-GPU batch 128, SGD momentum 0.9, DP over NCCL
+        from torchvision.models import resnet50
+
+        from xdna_train.ddp import GradAllReduce
+        bsz = args.batch if args.batch != B_PER_GPU else 128
+
+        def make(dev, b):
+            torch.manual_seed(0)
+            model = resnet50(num_classes=1000).bfloat16().to(dev).to(memory_format=torch.channels_last)
+            on_x = torch.device(dev).type == "xdna"
+            # the CPU side keeps the single-tensor SGD: torch 2.11's CPU _fused_sgd_
+            # leaves bf16 parameters unchanged
+            opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True if on_x else None)
+            ar = GradAllReduce(model) if (world > 1 and torch.device(dev).type == "xdna") else None
+            g = torch.Generator().manual_seed(rank)
+            x = torch.randn(b, 3, 224, 224, generator=g).bfloat16().to(dev).contiguous(
+                memory_format=torch.channels_last)
+            y = torch.randint(0, 1000, (b,), generator=g).to(dev)
+
+            def step():
+                opt.zero_grad(set_to_none=True)
+                loss = F.cross_entropy(model(x).float(), y)
+                loss.backward()
+                if ar is not None:
+                    ar.synchronize()
+                opt.step()
+            return step
+        dt = _timed(make(X, bsz), args.steps, args.warmup, sync)
+        out.update(metric="ResNet-50 training images/s (BASELINE config 5)", value=round(world * bsz / dt, 1),
+                   unit="images/s", ms_per_step=round(dt * 1e3, 4), per_gpu_batch=bsz, scaling="weak")
+        c = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            c = _timed(make("cpu", 4), 2, 1, cpu) / 4 * bsz  # seconds per bsz images, from a 4-image sample
+    else:
+        raise SystemExit(f"unknown workload {w}")
+    if c:
+        if w == "readme":
+            unit_scale = 1 / c
+        elif w == "mlp":
+            unit_scale = 128.85e9 / c / 1e12
+        elif w == "style":
+            unit_scale = 1 / c
+        else:
+            unit_scale = bsz / c
+        out["cpu_baseline"] = {"value": round(unit_scale, 3), "unit": out["unit"], "cores": torch.get_num_threads(),
+                               "kind": "reference", "sample": "same step on the reference's CPU BF16 path "
+                                                              "(stock PyTorch CPU ops), few steps"}
+    fb = xdna_train.fallback_stats()
+    out["fallback_ops_top"] = dict(sorted(((k, v["calls"]) for k, v in fb.items()), key=lambda kv: -kv[1])[:8])
+    out["kernel_launches"] = xdna_train.kernel_stats()
+    return out if rank == 0 else None
+
+
 def kernel_probe(args):
     """Per-kernel device times of one conv shape (``--kernel-probe``): used for
     sweeps and as the small case of ncu captures."""
@@ -401,6 +638,8 @@ def kernel_probe(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
+    ap.add_argument("--workload", default="conv", choices=["conv", "readme", "mlp", "style", "resnet50"],
+                    help="conv (default, the headline) or another BASELINE config")
     ap.add_argument("--batch", type=int, default=B_PER_GPU)
     ap.add_argument("--channels", type=int, default=C)
     ap.add_argument("--hw", type=int, default=HW)
@@ -413,6 +652,15 @@ def main():
     args = ap.parse_args()
     if args.kernel_probe:
         kernel_probe(args)
+        return
+    if args.workload != "conv":
+        line = run_workload(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup
     if args.impl == "reference":

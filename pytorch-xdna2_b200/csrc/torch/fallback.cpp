@@ -181,4 +181,14 @@ TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {
   m.fallback(torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>());
 }
 
+// Structured ops reach a backend without kernels through a generic wrapper that
+// allocates the output from the meta function and then calls the out= variant.
+// For mse_loss with a reduction that wrapper hands the CUDA out= kernel a 0-dim
+// output which the kernel resizes (a deprecation warning on every call); the
+// functional form on the CUDA alias allocates its own output and needs one
+// dispatch instead of two.
+TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
+  m.impl("mse_loss", torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>());
+}
+
 }  // namespace xdna

@@ -74,6 +74,22 @@ double region_sqdiff_sum(const at::Tensor& a, const at::Tensor& b) {
   return to_cuda(acc).item<double>();
 }
 
+// Same sum as region_sqdiff_sum, left on the device (0-dim double xdna tensor):
+// no host synchronization inside a training step.
+at::Tensor region_sqdiff_sum_tensor(const at::Tensor& a, const at::Tensor& b) {
+  check_bf16(a, "a");
+  check_bf16(b, "b");
+  TORCH_CHECK(a.numel() == b.numel(), "region_sqdiff_sum: size mismatch");
+  materialize(a);
+  materialize(b);
+  c10::cuda::CUDAGuard g(a.device().index());
+  at::Tensor acc = empty({}, at::kDouble, a.device().index());
+  XDNA_B2(b2_region_sqdiff_sum_bf16(a.data_ptr(), b.data_ptr(), a.numel(), acc.data_ptr<double>(),
+                                    stream(a.device().index())));
+  count_launch("region.sqdiff_sum");
+  return acc;
+}
+
 void region_relu(const at::Tensor& a, const at::Tensor& r) {
   check_bf16(a, "a");
   check_bf16(r, "r");
@@ -199,6 +215,7 @@ PYBIND11_MODULE(_C, m) {
     return code;
   });
   m.def("region_sqdiff_sum", &region_sqdiff_sum);
+  m.def("region_sqdiff_sum_tensor", &region_sqdiff_sum_tensor);
   m.def("region_relu", &region_relu);
   m.def("region_relu_maxpool2", &region_relu_maxpool2);
   m.def("region_addtap", &region_addtap);

@@ -18,7 +18,8 @@ Contract (unchanged from the reference)
   * output: a bf16 scalar, the mean over the concatenated tap elements.
   * backward produces dX only; not double-differentiable; retain_graph works.
   * numerics: bf16 storage, fp32 arithmetic in the fused kernels rounded once
-    to bf16, the squared-difference sum accumulated in double.
+    to bf16, the squared-difference sum accumulated in double on the device
+    (no host synchronization; the incoming gradient scales dX at the end).
   * eligibility is semantic (layer types, dtype, device, requires_grad);
     anything else takes the module's own method.  ``XDNA_REGIONS=0`` disables.
 
@@ -189,16 +190,19 @@ class _FrozenFeatureMSE(torch.autograd.Function):
         with torch.no_grad():
             g_outs = _forward_pass(chain, x, keep_all=True)
             t_outs = _forward_pass(chain, target, keep_all=False)
-            total, sq = 0, 0.0
+            total = 0
+            parts = []
             for k in chain.taps:
                 total += g_outs[k].numel()
-                sq += C.region_sqdiff_sum(g_outs[k], t_outs[k])
+                # per-tap sums stay on the device: no host synchronization
+                parts.append(C.region_sqdiff_sum_tensor(g_outs[k], t_outs[k]))
+            sq = torch.stack(parts).sum()
         gi = [i for i, t in enumerate(g_outs) if t is not None]
         ti = [i for i, t in enumerate(t_outs) if t is not None]
         weights = [op.weight for op in chain.ops if op.kind == "conv"]
         ctx.save_for_backward(x, *[g_outs[i] for i in gi], *[t_outs[i] for i in ti], *weights)
         ctx.meta = (chain, gi, ti, total)
-        return torch.full((), sq / total, dtype=torch.bfloat16, device=x.device)
+        return (sq / total).to(torch.bfloat16)
 
     @staticmethod
     @once_differentiable
@@ -215,7 +219,10 @@ class _FrozenFeatureMSE(torch.autograd.Function):
             t_outs[i] = saved[1 + len(gi) + n]
         weights = iter(saved[1 + len(gi) + len(ti):])
         w_of = {k: next(weights) for k, o in enumerate(chain.ops) if o.kind == "conv"}
-        scale = 2.0 * float(go) / total
+        # The backward is linear in the incoming gradient `go`: run it for go = 1
+        # and scale dX by go at the end, so that no device value is read on the
+        # host (the reference folds float(go) into the scale, regions.py:313).
+        scale = 2.0 / total
         G = None  # gradient w.r.t. the output of the op being processed
         for k in range(chain.taps[-1], -1, -1):
             op = chain.ops[k]
@@ -244,7 +251,7 @@ class _FrozenFeatureMSE(torch.autograd.Function):
                 G = torch.ops.aten.convolution_backward(G, src, w_of[k], None, list(op.stride), list(op.padding),
                                                         list(op.dilation), False, [0, 0], op.groups,
                                                         [True, False, False])[0]
-        return None, G, None
+        return None, G * go.to(G.dtype), None
 
 
 def frozen_feature_mse(chain: FrozenFeatureChain, x: torch.Tensor, target: torch.Tensor):

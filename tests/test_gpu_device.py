@@ -147,7 +147,7 @@ def test_readme_training_step_matches_cpu():
     def run(device, steps=8):
         torch.manual_seed(0)
         model = nn.Conv2d(128, 128, 3, padding=1).bfloat16().to(device)
-        opt = torch.optim.Adam(model.parameters(), lr=1e-3)
+        opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
         g = torch.Generator().manual_seed(1)
         x = torch.randn(16, 128, 36, 36, generator=g).bfloat16().to(device)
         target = torch.zeros_like(x)
