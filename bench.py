@@ -536,12 +536,19 @@ def run_workload(args):
         # config 4: B40 36x36 style transfer, Adam 1e-3, with and without the region
         from xdna_train import regions
 
-        def make(dev, fused):
+        def make(dev, fused, fuse_norm=False):
             torch.manual_seed(0)
             gen = make_style_generator().bfloat16().to(dev)
             crit = StyleLoss().bfloat16().to(dev)
             if fused:
                 assert regions.fuse_perceptual_loss(crit)
+            if fuse_norm:
+                # every BatchNorm2d directly followed by its ReLU in a Sequential
+                for seq in [m for m in gen.modules() if isinstance(m, nn.Sequential)]:
+                    mods = list(seq)
+                    for a, b in zip(mods, mods[1:]):
+                        if isinstance(a, nn.BatchNorm2d) and isinstance(b, nn.ReLU):
+                            assert regions.fuse_norm_activation(a, b)
             opt = torch.optim.Adam(gen.parameters(), lr=1e-3, fused=True)
             g = torch.Generator().manual_seed(1)
             x = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
@@ -556,8 +563,10 @@ def run_workload(args):
             return step
         dt = _timed(make(X, False), args.steps, args.warmup, sync)
         dtf = _timed(make(X, True), args.steps, args.warmup, sync)
+        dtn = _timed(make(X, True, True), args.steps, args.warmup, sync)
         out.update(metric="style-transfer training it/s (BASELINE config 4)", value=round(1 / dt, 2), unit="it/s",
-                   ms_per_step=round(dt * 1e3, 4), fused_perceptual_loss_it_s=round(1 / dtf, 2))
+                   ms_per_step=round(dt * 1e3, 4), fused_perceptual_loss_it_s=round(1 / dtf, 2),
+                   fused_perceptual_and_norm_act_it_s=round(1 / dtn, 2))
         c = cpu_rate(lambda: make("cpu", False))
     elif w == "resnet50":
         # config 5: ResNet-50 224x224, per-GPU batch 128, SGD momentum 0.9, DP over NCCL

@@ -240,6 +240,36 @@ b2_status b2_region_maxpool2_bwd_bf16(const void* x, const void* g, void* out,
                                       int64_t planes, int64_t H, int64_t W,
                                       void* stream);
 
+/* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
+ * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,
+ * region_kernels.cpp:309-460; used by regions.fuse_norm_activation,
+ * regions.py:426-548).  Statistics: each (n, c) plane reduced in fp32 (mean,
+ * then the sum of squared deviations), the N planes of a channel merged in
+ * double in plane order with Chan's formula.  Workspace: at least
+ * b2_region_bn_workspace_bytes(N, C) bytes of device memory, 16-byte aligned.
+ *
+ * Forward: w, b may be NULL (affine=False); if update != 0 the bf16 running
+ * statistics rm, rv move by `factor` towards the batch mean and the unbiased
+ * batch variance.  mean_out / invstd_out: fp32 [C].  y = act(x*scale + shift)
+ * with scale = w*invstd, shift = b - mean*scale, act(z) = z > 0 ? z : z*slope,
+ * rounded once to bf16. */
+size_t b2_region_bn_workspace_bytes(int64_t N, int64_t C);
+b2_status b2_region_bn_fwd_bf16(const void* x, const void* w, const void* b,
+                                void* rm, void* rv, void* y, float* mean_out,
+                                float* invstd_out, int64_t N, int64_t C,
+                                int64_t HW, float eps, float slope, float factor,
+                                int update, void* workspace,
+                                size_t workspace_bytes, void* stream);
+/* Backward: dz = (y > 0 or (relu and y is NaN)) ? dy : dy*slope; dw, db (bf16
+ * [C], each may be NULL) get sum(dz*xhat) and sum(dz); dx (may be NULL) gets
+ * w*invstd*(dz - mean(dz) - xhat*mean(dz*xhat)). */
+b2_status b2_region_bn_bwd_bf16(const void* dy, const void* y, const void* x,
+                                const void* w, const float* mean,
+                                const float* invstd, void* dx, void* dw,
+                                void* db, int64_t N, int64_t C, int64_t HW,
+                                float slope, int relu, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,6 +12,7 @@
  *                                row offsets dy*(W+2)+dx), unpack conv3x3w_host.py:81-87
  *   - wgrad                      xdna_train/_designs/conv3x3w_dw.py:1-21
  *   - region kernels             xdna_train/_native/region_kernels.cpp:52-307
+ *   - BatchNorm + activation     region_kernels.cpp:309-460
  * Parity pins: tests/test_oracle_golden.py checks the packers against vectors
  * generated from conv3x3w_host.py itself (tests/golden/make_golden.py) and the
  * region kernels bit-exactly against the reference's region_kernels.cpp built
@@ -251,5 +252,90 @@ void oracle_adam_f32(float* p, const float* g_in, float* m, float* v, float* vma
       pp = pp - upd / denom;
     }
     p[i] = pp;
+  }
+}
+
+/* ---- training BatchNorm2d + LeakyReLU/ReLU: region_kernels.cpp:309-460 -----
+ * Contiguous NCHW bf16 [N, C, HW].  Statistics over (N, HW) per channel in
+ * double (two passes: mean, then squared deviations), so the oracle is tighter
+ * than the reference's fp32 plane sums merged with Chan's formula; invstd =
+ * 1/sqrt(var + eps); running statistics (bf16) move by `factor` towards the
+ * mean and the unbiased variance.  The elementwise expressions are the
+ * reference's, in fp32 with one rounding each and no contraction:
+ *   y  = act(x*scale + shift), scale = w*invstd, shift = b - mean*scale,
+ *        act(z) = z > 0 ? z : z*slope
+ *   dz = (y > 0 or (relu and y is NaN)) ? dy : dy*slope
+ *   dx = (w*invstd) * ((dz - sum(dz)/M) - xhat*(sum(dz*xhat)/M)),
+ *        xhat = (x - mean)*invstd. */
+#if defined(__FP_FAST_FMAF)
+#error "the BN oracle needs fp32 expressions without FMA contraction"
+#endif
+
+void oracle_bn_fwd(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* rm, uint16_t* rv,
+                   uint16_t* y, float* mean_out, float* invstd_out, long long N, long long C, long long HW,
+                   float eps, float slope, float factor, int update) {
+  const double M = (double)N * (double)HW;
+  for (long long c = 0; c < C; ++c) {
+    double s = 0.0;
+    for (long long n = 0; n < N; ++n)
+      for (long long i = 0; i < HW; ++i) s += (double)bf2f(x[(n * C + c) * HW + i]);
+    const double mean = s / M;
+    double q = 0.0;
+    for (long long n = 0; n < N; ++n)
+      for (long long i = 0; i < HW; ++i) {
+        const double d = (double)bf2f(x[(n * C + c) * HW + i]) - mean;
+        q += d * d;
+      }
+    const double var = q / M;
+    mean_out[c] = (float)mean;
+    invstd_out[c] = (float)(1.0 / sqrt(var + (double)eps));
+    if (update) {
+      const double unbiased = M > 1.0 ? var * M / (M - 1.0) : var;
+      const double f = (double)factor;
+      rm[c] = f2bf((float)((1.0 - f) * (double)bf2f(rm[c]) + f * mean));
+      rv[c] = f2bf((float)((1.0 - f) * (double)bf2f(rv[c]) + f * unbiased));
+    }
+    const float scale = (w ? bf2f(w[c]) : 1.0f) * invstd_out[c];
+    const float shift = (b ? bf2f(b[c]) : 0.0f) - mean_out[c] * scale;
+    for (long long n = 0; n < N; ++n)
+      for (long long i = 0; i < HW; ++i) {
+        const long long o = (n * C + c) * HW + i;
+        const float z = bf2f(x[o]) * scale + shift;
+        y[o] = f2bf(z > 0.0f ? z : z * slope);
+      }
+  }
+}
+
+static float bn_dz(float g, float yv, float slope, int relu) {
+  return ((yv > 0.0f) || (relu && yv != yv)) ? g : g * slope;
+}
+
+void oracle_bn_bwd(const uint16_t* dy, const uint16_t* y, const uint16_t* x, const uint16_t* w,
+                   const float* mean, const float* invstd, uint16_t* dx, uint16_t* dw, uint16_t* db,
+                   long long N, long long C, long long HW, float slope, int relu) {
+  const double M = (double)N * (double)HW;
+  for (long long c = 0; c < C; ++c) {
+    const float mc = mean[c], is = invstd[c];
+    double a = 0.0, bs = 0.0;
+    for (long long n = 0; n < N; ++n)
+      for (long long i = 0; i < HW; ++i) {
+        const long long o = (n * C + c) * HW + i;
+        const float dz = bn_dz(bf2f(dy[o]), bf2f(y[o]), slope, relu);
+        const float xhat = (bf2f(x[o]) - mc) * is;
+        a += (double)dz;
+        bs += (double)dz * (double)xhat;
+      }
+    if (db) db[c] = f2bf((float)a);
+    if (dw) dw[c] = f2bf((float)bs);
+    if (!dx) continue;
+    const float k1 = (float)(a / M), k2 = (float)(bs / M);
+    const float ws = (w ? bf2f(w[c]) : 1.0f) * is;
+    for (long long n = 0; n < N; ++n)
+      for (long long i = 0; i < HW; ++i) {
+        const long long o = (n * C + c) * HW + i;
+        const float dz = bn_dz(bf2f(dy[o]), bf2f(y[o]), slope, relu);
+        const float xhat = (bf2f(x[o]) - mc) * is;
+        dx[o] = f2bf(ws * ((dz - k1) - xhat * k2));
+      }
   }
 }

@@ -56,6 +56,8 @@ def native():
         L.oracle_maxpool2_bwd.argtypes = [u16p, u16p, u16p, i64, i64, i64]
         L.oracle_adam_f32.argtypes = [f32p, f32p, f32p, f32p, f32p, i64, f32, f32, f32, f32, f32, f32,
                                       i32, i32, i32]
+        L.oracle_bn_fwd.argtypes = [u16p, vp, vp, vp, vp, u16p, f32p, f32p, i64, i64, i64, f32, f32, f32, i32]
+        L.oracle_bn_bwd.argtypes = [u16p, u16p, u16p, vp, f32p, f32p, vp, vp, vp, i64, i64, i64, f32, i32]
         _native = L
     return _native
 
@@ -73,6 +75,10 @@ def reference():
         L.xdna_region_addtap_bf16.argtypes = [vp, u16p, u16p, u16p, i64, f32, i32]
         L.xdna_region_relu_bwd_bf16.argtypes = [u16p, vp, vp, vp, u16p, i64, f32, i32]
         L.xdna_region_maxpool2_bwd_bf16.argtypes = [u16p, u16p, u16p, i64, i64, i64, i32]
+        L.xdna_region_bn_fwd_bf16.argtypes = [u16p, vp, vp, vp, vp, u16p, f32p, f32p, i64, i64, i64, f32, f32,
+                                              f32, i32, i32]
+        L.xdna_region_bn_bwd_bf16.argtypes = [u16p, u16p, u16p, vp, f32p, f32p, vp, vp, vp, i64, i64, i64, f32,
+                                              i32, i32]
         _ref = L
     return _ref
 
@@ -197,3 +203,47 @@ def adam_f32(p, g, m, v, vmax, step, lr, beta1, beta2, wd, eps, amsgrad=False, m
     """In-place on float32 arrays."""
     native().oracle_adam_f32(p, g, m, v, vmax, p.size, step, lr, beta1, beta2, wd, eps, int(amsgrad),
                              int(maximize), int(adamw))
+
+
+# ---- training BatchNorm2d + activation (region_kernels.cpp:309-460) ----------
+
+def _bn_call(fn, x, w, b, rm, rv, eps, slope, factor, update, extra=()):
+    N, Cc = x.shape[:2]
+    HW = int(np.prod(x.shape[2:]))
+    x = np.ascontiguousarray(x, np.uint16)
+    y = np.empty_like(x)
+    mean = np.empty(Cc, np.float32)
+    invstd = np.empty(Cc, np.float32)
+    rm = None if rm is None else np.array(rm, np.uint16)
+    rv = None if rv is None else np.array(rv, np.uint16)
+    w = None if w is None else np.ascontiguousarray(w, np.uint16)
+    b = None if b is None else np.ascontiguousarray(b, np.uint16)
+    fn(x, _ptr(w), _ptr(b), _ptr(rm), _ptr(rv), y, mean, invstd, N, Cc, HW, eps, slope, factor, int(update), *extra)
+    return y, mean, invstd, rm, rv
+
+
+def bn_fwd(x, w, b, rm, rv, eps=1e-5, slope=0.0, factor=0.1, update=True, reference_impl=False):
+    """Fused BN + activation forward on bf16 bits [N, C, ...]: (y, mean, invstd, rm', rv').
+
+    reference_impl=True runs the reference's own compiled host kernel."""
+    if reference_impl:
+        return _bn_call(reference().xdna_region_bn_fwd_bf16, x, w, b, rm, rv, eps, slope, factor, update, (2,))
+    return _bn_call(native().oracle_bn_fwd, x, w, b, rm, rv, eps, slope, factor, update)
+
+
+def bn_bwd(dy, y, x, w, mean, invstd, slope=0.0, relu=True, need=(True, True, True), reference_impl=False):
+    """Backward of the fused pair: (dx, dw, db) as bf16 bits (None where not needed)."""
+    N, Cc = x.shape[:2]
+    HW = int(np.prod(x.shape[2:]))
+    dx = np.empty_like(x) if need[0] else None
+    dw = np.empty(Cc, np.uint16) if need[1] else None
+    db = np.empty(Cc, np.uint16) if need[2] else None
+    w = None if w is None else np.ascontiguousarray(w, np.uint16)
+    args = [np.ascontiguousarray(dy, np.uint16), np.ascontiguousarray(y, np.uint16),
+            np.ascontiguousarray(x, np.uint16), _ptr(w), np.ascontiguousarray(mean, np.float32),
+            np.ascontiguousarray(invstd, np.float32), _ptr(dx), _ptr(dw), _ptr(db), N, Cc, HW, slope, int(relu)]
+    if reference_impl:
+        reference().xdna_region_bn_bwd_bf16(*args, 2)
+    else:
+        native().oracle_bn_bwd(*args)
+    return dx, dw, db

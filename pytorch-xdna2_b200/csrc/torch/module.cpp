@@ -148,6 +148,110 @@ void region_maxpool2_bwd(const at::Tensor& x, const at::Tensor& gr, const at::Te
   count_launch("region.maxpool2_bwd");
 }
 
+void check_f32(const at::Tensor& t, int64_t n, const char* what) {
+  TORCH_CHECK(t.device().type() == kXdna && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() == n,
+              "xdna region kernel: ", what, " must be a contiguous fp32 xdna tensor of ", n, " elements");
+}
+
+at::Tensor bn_workspace(int64_t N, int64_t C, c10::DeviceIndex dev) {
+  const int64_t bytes = int64_t(b2_region_bn_workspace_bytes(N, C));
+  return empty({std::max<int64_t>(bytes, 16)}, at::kByte, dev);
+}
+
+// Fused training BatchNorm2d + LeakyReLU/ReLU forward on contiguous NCHW bf16
+// (the reference's region_bn_fwd binding, torch_xdna_device.cpp:5521-5550).
+void region_bn_fwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const std::optional<at::Tensor>& b,
+                   const std::optional<at::Tensor>& rm, const std::optional<at::Tensor>& rv, const at::Tensor& y,
+                   const at::Tensor& mean, const at::Tensor& invstd, double eps, double slope, double factor,
+                   bool update) {
+  check_bf16(x, "x");
+  check_bf16(y, "y");
+  TORCH_CHECK(x.dim() >= 2 && y.sizes() == x.sizes(), "region_bn_fwd: x and y must be [N, C, ...] of one shape");
+  const int64_t N = x.size(0), C = x.size(1), HW = C ? x.numel() / std::max<int64_t>(1, N * C) : 0;
+  check_f32(mean, C, "mean");
+  check_f32(invstd, C, "invstd");
+  for (const auto* t : {&w, &b, &rm, &rv})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->numel() == C, "region_bn_fwd: per-channel tensors must have C elements");
+  TORCH_CHECK(!update || (rm.has_value() && rv.has_value()), "region_bn_fwd: update needs running statistics");
+  materialize(x);
+  const auto dev = x.device().index();
+  c10::cuda::CUDAGuard g(dev);
+  at::Tensor ws = bn_workspace(N, C, dev);
+  XDNA_B2(b2_region_bn_fwd_bf16(x.data_ptr(), opt_ptr(w, "weight"), opt_ptr(b, "bias"),
+                                const_cast<void*>(opt_ptr(rm, "running_mean")),
+                                const_cast<void*>(opt_ptr(rv, "running_var")), y.data_ptr(),
+                                mean.data_ptr<float>(), invstd.data_ptr<float>(), N, C, HW, float(eps), float(slope),
+                                float(factor), update ? 1 : 0, ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+  count_launch("region.bn_fwd", 3);
+}
+
+// Backward of the fused pair: dx, dw, db each optional (region_bn_bwd,
+// torch_xdna_device.cpp:5552-5580).
+void region_bn_bwd(const at::Tensor& dy, const at::Tensor& y, const at::Tensor& x, const std::optional<at::Tensor>& w,
+                   const at::Tensor& mean, const at::Tensor& invstd, const std::optional<at::Tensor>& dx,
+                   const std::optional<at::Tensor>& dw, const std::optional<at::Tensor>& db, double slope,
+                   bool relu) {
+  check_bf16(dy, "dy");
+  check_bf16(y, "y");
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() >= 2 && dy.sizes() == x.sizes() && y.sizes() == x.sizes(),
+              "region_bn_bwd: dy, y and x must be [N, C, ...] of one shape");
+  const int64_t N = x.size(0), C = x.size(1), HW = C ? x.numel() / std::max<int64_t>(1, N * C) : 0;
+  check_f32(mean, C, "mean");
+  check_f32(invstd, C, "invstd");
+  auto out_ptr = [&](const std::optional<at::Tensor>& t, int64_t n, const char* what) -> void* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    check_bf16(*t, what);
+    TORCH_CHECK(t->numel() == n, "region_bn_bwd: ", what, " has the wrong size");
+    return t->data_ptr();
+  };
+  void* pdx = out_ptr(dx, x.numel(), "dx");
+  void* pdw = out_ptr(dw, C, "dw");
+  void* pdb = out_ptr(db, C, "db");
+  materialize(dy);
+  materialize(y);
+  materialize(x);
+  const auto dev = x.device().index();
+  c10::cuda::CUDAGuard g(dev);
+  at::Tensor ws = bn_workspace(N, C, dev);
+  XDNA_B2(b2_region_bn_bwd_bf16(dy.data_ptr(), y.data_ptr(), x.data_ptr(), opt_ptr(w, "weight"),
+                                mean.data_ptr<float>(), invstd.data_ptr<float>(), pdx, pdw, pdb, N, C, HW,
+                                float(slope), relu ? 1 : 0, ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+  count_launch("region.bn_bwd", pdx ? 3 : 2);
+}
+
+// Allocating forms used by regions._BatchNormAct: one binding call per
+// direction.  region_bn_forward returns (y, stats) with stats = [mean; invstd]
+// as fp32 [2, C]; region_bn_backward returns (dx, dw, db), None where not
+// requested.
+std::tuple<at::Tensor, at::Tensor> region_bn_forward(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b,
+                                                     const at::Tensor& rm, const at::Tensor& rv, double eps,
+                                                     double slope, double factor) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() >= 2, "region_bn_forward: x must be [N, C, ...]");
+  const auto dev = x.device().index();
+  at::Tensor y = empty(x.sizes(), at::kBFloat16, dev);
+  at::Tensor stats = empty({2, x.size(1)}, at::kFloat, dev);
+  region_bn_fwd(x, w, b, rm, rv, y, stats[0], stats[1], eps, slope, factor, true);
+  return {y, stats};
+}
+
+py::tuple region_bn_backward(const at::Tensor& dy, const at::Tensor& y, const at::Tensor& x, const at::Tensor& w,
+                             const at::Tensor& stats, bool want_x, bool want_w, bool want_b, double slope,
+                             bool relu) {
+  const auto dev = x.device().index();
+  const int64_t C = x.dim() >= 2 ? x.size(1) : 0;
+  std::optional<at::Tensor> dx, dw, db;
+  if (want_x) dx = empty(x.sizes(), at::kBFloat16, dev);
+  if (want_w) dw = empty({C}, at::kBFloat16, dev);
+  if (want_b) db = empty({C}, at::kBFloat16, dev);
+  const at::Tensor g = dy.is_contiguous() ? dy : dy.contiguous();
+  region_bn_bwd(g, y, x, w, stats[0], stats[1], dx, dw, db, slope, relu);
+  auto as_py = [](const std::optional<at::Tensor>& t) { return t ? py::cast(*t) : py::none(); };
+  return py::make_tuple(as_py(dx), as_py(dw), as_py(db));
+}
+
 py::dict to_dict(const std::map<std::string, int64_t>& m) {
   py::dict d;
   for (auto& kv : m) d[py::str(kv.first)] = kv.second;
@@ -221,4 +325,8 @@ PYBIND11_MODULE(_C, m) {
   m.def("region_addtap", &region_addtap);
   m.def("region_relu_bwd", &region_relu_bwd);
   m.def("region_maxpool2_bwd", &region_maxpool2_bwd);
+  m.def("region_bn_fwd", &region_bn_fwd);
+  m.def("region_bn_bwd", &region_bn_bwd);
+  m.def("region_bn_forward", &region_bn_forward);
+  m.def("region_bn_backward", &region_bn_backward);
 }

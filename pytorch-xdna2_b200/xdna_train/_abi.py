@@ -56,9 +56,12 @@ SIGNATURES = {
     "b2_region_addtap_bf16": [vp, vp, vp, vp, i64, f32, vp],
     "b2_region_relu_bwd_bf16": [vp, vp, vp, vp, vp, i64, f32, vp],
     "b2_region_maxpool2_bwd_bf16": [vp, vp, vp, i64, i64, i64, vp],
+    "b2_region_bn_workspace_bytes": [i64, i64],
+    "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
+    "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
 }
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
-             "b2_pack_rows_dbias_workspace_bytes": sz,
+             "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 

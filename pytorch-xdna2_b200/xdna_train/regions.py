@@ -23,6 +23,12 @@ Contract (unchanged from the reference)
   * eligibility is semantic (layer types, dtype, device, requires_grad);
     anything else takes the module's own method.  ``XDNA_REGIONS=0`` disables.
 
+``fuse_norm_activation`` runs a training ``BatchNorm2d`` and the ``ReLU`` /
+``LeakyReLU`` applied directly to its output as one op (the reference's
+``regions.py:426-548`` contract): statistics and the activated output in two
+passes over the input, the backward's parameter sums and input gradient in
+two more (``b2_region_bn_*``).
+
 The reference also times CPU vs NPU placement per convolution (its
 ``_Placer``); on B200 every convolution runs on the GPU, so there is nothing to
 place.
@@ -31,6 +37,7 @@ from __future__ import annotations
 
 import os
 import types
+import weakref
 from dataclasses import dataclass, field
 
 import torch
@@ -41,10 +48,16 @@ from torch.nn.utils import parametrize
 import torch.nn.functional as F
 
 
+_C_MOD = None
+
+
 def _native():
-    from . import device
-    device.register_xdna_device()
-    return device._C
+    global _C_MOD
+    if _C_MOD is None:
+        from . import device
+        device.register_xdna_device()
+        _C_MOD = device._C
+    return _C_MOD
 
 
 def enabled() -> bool:
@@ -319,4 +332,129 @@ def fuse_perceptual_loss(loss_module, features_attr: str = "perceptual_vgg") -> 
             return False
     loss_module.__dict__["_xdna_region_cfg"] = {"features_attr": features_attr}
     loss_module.compute_perceptual_loss = types.MethodType(_fused_compute_perceptual_loss, loss_module)
+    return True
+
+
+
+# ---------------------------------------------------------------------------
+# fuse_norm_activation: training BatchNorm2d + ReLU / LeakyReLU as one op
+# ---------------------------------------------------------------------------
+
+#: Inputs smaller than this many bytes keep the eager pair.  The reference
+#: fuses only from 4 MB up (its host kernel loses to eager on small tensors);
+#: on the GPU the fused op saves launches and passes at every size, so the
+#: default is 0.  ``XDNA_REGION_NORM_ACT_MIN_BYTES`` overrides it.
+_NORM_ACT_MIN_BYTES = int(os.environ.get("XDNA_REGION_NORM_ACT_MIN_BYTES", "0"))
+
+
+class _BatchNormAct(torch.autograd.Function):
+    """act(batch_norm(x)) in training mode on contiguous NCHW bf16 xdna tensors.
+
+    Statistics over (N, H, W) per channel; the biased variance normalizes, the
+    unbiased one moves the running variance (once per call, by ``factor``);
+    affine weight and bias.  Backward reads x, the activated output y (its sign
+    is the activation mask), the weight and the fp32 per-channel mean and
+    inverse std saved by the forward; it returns the input, weight and bias
+    gradients that autograd asks for.  Not double differentiable."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, running_mean, running_var, eps, slope, factor, relu):
+        # outputs allocated by the binding: one native call per direction
+        y, stats = _native().region_bn_forward(x, weight, bias, running_mean, running_var, eps, slope, factor)
+        ctx.save_for_backward(x, y, weight, stats)
+        ctx.slope, ctx.relu = slope, relu
+        return y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dy):
+        x, y, weight, stats = ctx.saved_tensors
+        want_x, want_w, want_b = ctx.needs_input_grad[:3]
+        if not (want_x or want_w or want_b):
+            return (None,) * 9
+        dx, dw, db = _native().region_bn_backward(dy, y, x, weight, stats, want_x, want_w, want_b, ctx.slope,
+                                                  ctx.relu)
+        return dx, dw, db, None, None, None, None, None, None
+
+
+def _bf16_xdna(t, n) -> bool:
+    return (isinstance(t, torch.Tensor) and t.device.type == "xdna" and t.dtype == torch.bfloat16
+            and t.is_contiguous() and t.numel() == n)
+
+
+def _norm_act_eligible(bn: nn.BatchNorm2d, x) -> bool:
+    """The fused op applies to training-mode statistics of an affine norm with
+    tracked running statistics and a float momentum, on a contiguous 4-D bf16
+    xdna input with more than one value per channel, at least
+    ``_NORM_ACT_MIN_BYTES`` large, with bf16 xdna parameters and buffers."""
+    if not (enabled() and bn.training and bn.track_running_stats and bn.affine) or bn.momentum is None:
+        return False
+    if not isinstance(x, torch.Tensor) or x.dim() != 4 or not _bf16_xdna(x, x.numel()):
+        return False
+    channels = x.shape[1]
+    if channels == 0 or x.numel() // channels <= 1 or 2 * x.numel() < _NORM_ACT_MIN_BYTES:
+        return False
+    return all(_bf16_xdna(t, channels) for t in (bn.weight, bn.bias, bn.running_mean, bn.running_var))
+
+
+def _act_slope(act):
+    """Negative slope of a plain ReLU (0) or LeakyReLU; None for anything else
+    (subclasses included: their forward could differ)."""
+    if type(act) is nn.ReLU:
+        return 0.0
+    if type(act) is nn.LeakyReLU:
+        return float(act.negative_slope)
+    return None
+
+
+def _fused_bn_forward(self, x):
+    # Bound to the norm module itself, so copy.deepcopy rebinds it to the copy;
+    # the paired activation and its slope are looked up on every call.
+    act = self.__dict__.get("_xdna_pair")
+    slope = None if act is None else _act_slope(act)
+    # a negative slope breaks the y > 0 mask the backward relies on
+    if slope is None or slope < 0.0 or not _norm_act_eligible(self, x):
+        return type(self).forward(self, x)
+    self.num_batches_tracked.add_(1)
+    y = _BatchNormAct.apply(x, self.weight, self.bias, self.running_mean, self.running_var,
+                            float(self.eps), slope, float(self.momentum), type(act) is nn.ReLU)
+    y._xdna_act_for = weakref.ref(act)
+    return y
+
+
+def _checked_act_forward(self, x):
+    # The paired norm already activated this exact tensor: pass it through,
+    # once.  Any other input is activated normally.
+    owner = getattr(x, "_xdna_act_for", None)
+    if owner is not None and owner() is self:
+        x._xdna_act_for = None
+        return x
+    return type(self).forward(self, x)
+
+
+def fuse_norm_activation(bn: nn.BatchNorm2d, act: nn.Module) -> bool:
+    """Declare that ``act`` (an ``nn.ReLU`` or ``nn.LeakyReLU``) is applied
+    directly to the output of ``bn`` (an ``nn.BatchNorm2d``) and run the pair as
+    one fused op where eligible (reference: regions.py:508-548).
+
+    Parameters, buffers and state_dict keys are untouched; only the two
+    ``forward`` methods are replaced, by methods bound to the modules, so a
+    ``copy.deepcopy`` of a model holding both modules keeps a working pair.
+    When eligible (training mode, contiguous bf16 NCHW xdna input, affine,
+    tracked statistics with a float momentum, at least
+    ``_NORM_ACT_MIN_BYTES``), ``bn(x)`` returns the activated tensor and the
+    next call of ``act`` on that exact tensor returns it unchanged, once;
+    otherwise both modules run their own forward.  The caller vouches for the
+    dataflow: a pair with anything in between (an add, a branch) must not be
+    declared.  Returns True if the pair is installed (or already was)."""
+    if not enabled() or type(bn) is not nn.BatchNorm2d or _act_slope(act) is None:
+        return False
+    paired = bn.__dict__.get("_xdna_pair")
+    if paired is not None:
+        return paired is act
+    object.__setattr__(bn, "_xdna_pair", act)  # a plain attribute, not a submodule
+    bn.forward = types.MethodType(_fused_bn_forward, bn)
+    fwd = act.__dict__.get("forward")
+    if not (isinstance(fwd, types.MethodType) and fwd.__func__ is _checked_act_forward):
+        act.forward = types.MethodType(_checked_act_forward, act)
     return True

@@ -13,6 +13,7 @@ Files
   conv3x3w_host.npz  pack_input (rows view), pack_weights / pack_weights_dx
                      (decoded K x N matrices), unpack_output cases
   regions.npz        region kernel inputs/outputs from region_kernels.cpp
+  regions_bn.npz     fused BatchNorm + activation vectors from region_kernels.cpp:309-460
 """
 from __future__ import annotations
 
@@ -184,6 +185,42 @@ def make_regions(out: Path) -> None:
     np.savez_compressed(out, **data)
 
 
+def make_regions_bn(out: Path) -> None:
+    """Fused BatchNorm + activation vectors from the reference's own host kernels
+    (xdna_region_bn_fwd_bf16 / _bwd_bf16, region_kernels.cpp:309-460)."""
+    ref = oracle.reference()
+    if ref is None:
+        raise SystemExit("oracle/_ref/libxdna_ref.so missing: run `make -C oracle` first")
+    rng = np.random.default_rng(7)
+    data = {}
+    # (N, C, H, W, slope, relu, affine): shapes after the reference test (tests/run_regions_bn.py:43-44)
+    cases = [(2, 16, 18, 18, 0.2, 0, 1), (2, 3, 5, 7, 0.2, 0, 1), (3, 1, 4, 4, 0.2, 0, 1),
+             (4, 8, 11, 13, 0.0, 1, 1), (4, 16, 8, 8, 0.0, 1, 0)]
+    for i, (N, Cc, H, W, slope, relu, affine) in enumerate(cases):
+        x = oracle.bf16_bits((rng.standard_normal((N, Cc, H, W)) * 1.5 + 0.3).astype(np.float32))
+        w = oracle.bf16_bits(rng.uniform(0.5, 1.5, Cc).astype(np.float32)) if affine else None
+        b = oracle.bf16_bits((rng.standard_normal(Cc) * 0.3).astype(np.float32)) if affine else None
+        rm = oracle.bf16_bits((rng.standard_normal(Cc) * 0.1).astype(np.float32))
+        rv = oracle.bf16_bits(rng.uniform(0.5, 1.5, Cc).astype(np.float32))
+        y, mean, invstd, rm2, rv2 = oracle.bn_fwd(x, w, b, rm, rv, 1e-5, slope, 0.1, True, reference_impl=True)
+        dy = oracle.bf16_bits(rng.standard_normal((N, Cc, H, W)).astype(np.float32))
+        # backward on an activation with planted zeros and NaNs: pins the dz rule
+        yb = y.copy().reshape(-1)
+        idx = rng.choice(yb.size, size=max(2, yb.size // 40), replace=False)
+        yb[idx[: idx.size // 2]] = 0x0000
+        yb[idx[idx.size // 2:]] = 0x7FC0
+        yb = yb.reshape(y.shape)
+        dx, dw, db = oracle.bn_bwd(dy, yb, x, w, mean, invstd, slope, relu, reference_impl=True)
+        data.update({f"c{i}_meta": np.array([N, Cc, H, W, relu, affine]), f"c{i}_slope": np.array([slope], np.float32),
+                     f"c{i}_x": x, f"c{i}_rm": rm, f"c{i}_rv": rv, f"c{i}_y": y, f"c{i}_mean": mean,
+                     f"c{i}_invstd": invstd, f"c{i}_rm_out": rm2, f"c{i}_rv_out": rv2, f"c{i}_dy": dy,
+                     f"c{i}_ybwd": yb, f"c{i}_dx": dx, f"c{i}_dw": dw, f"c{i}_db": db})
+        if affine:
+            data.update({f"c{i}_w": w, f"c{i}_b": b})
+    data["cases"] = np.array([len(cases)])
+    np.savez_compressed(out, **data)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -193,6 +230,7 @@ def main():
     host = load_host_spec(ref)
     make_conv3x3w_host(host, HERE / "conv3x3w_host.npz")
     make_regions(HERE / "regions.npz")
+    make_regions_bn(HERE / "regions_bn.npz")
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size, "bytes")
 

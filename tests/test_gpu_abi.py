@@ -5,9 +5,13 @@ reference of the same op.
 Tolerances: layouts and region kernels bit-exact; conv / GEMM
 max|out - ref| <= 2e-2 * max|ref| and relative L2 error
 <= 5e-3 (what fp32 accumulation + one bf16 rounding gives); Adam within 1e-6
-(fp32) and bit-exact on bf16 parameters.
+(fp32) and bit-exact on bf16 parameters; fused BatchNorm + activation within
+one bf16 ulp of the reference's host kernels, or within a small absolute floor
+where cancellation leaves a near-zero result (their fp32 plane sums are added
+in another order), and bit-equal on at least 99.5 % of the elements.
 """
 import ctypes
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -394,3 +398,125 @@ def test_single_cta_conv_path_still_matches(cuda):
     env = dict(os.environ, B2_PAIR_MMA="0")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
+# ---- fused BatchNorm + activation (region_kernels.cpp:309-460) ----------------
+
+def _ulps(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    return np.abs(a.astype(np.int32) - b.astype(np.int32))
+
+
+def _bf_close(got: np.ndarray, want: np.ndarray, floor: float, exact: float = 0.995):
+    """bf16 bit arrays that agree to one bf16 ulp, or to `floor` absolutely
+    where the value is the small difference of larger terms (cancellation makes
+    ulps of a near-zero result meaningless), with at least `exact` of the
+    elements bit-equal."""
+    g, w = oracle.bf16_value(got), oracle.bf16_value(want)
+    err = np.abs(g - w)
+    bound = np.abs(w) * 2.0 ** -7 + floor
+    assert (err <= bound).all(), f"max excess {(err - bound).max()} (floor {floor})"
+    assert (got == want).mean() >= exact, f"only {(got == want).mean():.5f} bit-equal"
+
+
+def _gpu_bn(cuda, x, w, b, rm, rv, slope, relu, dy, ybwd=None, need=(True, True, True), update=True):
+    """Runs b2_region_bn_fwd_bf16 / _bwd_bf16 on bf16-bit numpy inputs."""
+    N, Cc = x.shape[:2]
+    HW = int(np.prod(x.shape[2:]))
+    dv = lambda a: None if a is None else _dev(a, cuda)  # noqa: E731
+    xd, wd, bd, rmd, rvd, dyd = dv(x), dv(w), dv(b), dv(rm), dv(rv), dv(dy)
+    y = torch.empty_like(xd)
+    mean = torch.empty(Cc, dtype=torch.float32, device=cuda)
+    invstd = torch.empty_like(mean)
+    nws = _abi.lib().b2_region_bn_workspace_bytes(N, Cc)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=cuda)
+    p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _abi.call("b2_region_bn_fwd_bf16", xd.data_ptr(), p(wd), p(bd), p(rmd), p(rvd), y.data_ptr(), mean.data_ptr(),
+              invstd.data_ptr(), N, Cc, HW, ctypes.c_float(1e-5), ctypes.c_float(slope), ctypes.c_float(0.1),
+              int(update), ws.data_ptr(), nws, st())
+    yb = y if ybwd is None else dv(ybwd)
+    dx = torch.empty_like(xd) if need[0] else None
+    dw = torch.empty(Cc, dtype=torch.bfloat16, device=cuda) if need[1] else None
+    db = torch.empty(Cc, dtype=torch.bfloat16, device=cuda) if need[2] else None
+    _abi.call("b2_region_bn_bwd_bf16", dyd.data_ptr(), yb.data_ptr(), xd.data_ptr(), p(wd), mean.data_ptr(),
+              invstd.data_ptr(), p(dx), p(dw), p(db), N, Cc, HW, ctypes.c_float(slope), int(relu), ws.data_ptr(),
+              nws, st())
+    torch.cuda.synchronize()
+    out = lambda t: None if t is None else bits(t)  # noqa: E731
+    return (bits(y), mean.cpu().numpy(), invstd.cpu().numpy(), out(rmd), out(rvd), out(dx), out(dw), out(db))
+
+
+@pytest.fixture(scope="module")
+def bn_gold():
+    return np.load(Path(__file__).resolve().parent / "golden" / "regions_bn.npz")
+
+
+def test_bn_act_vs_reference_vectors(cuda, bn_gold):
+    """Against the reference's own host kernels' outputs: the fp32 plane sums
+    are ordered differently, so a value on a bf16 rounding boundary may land one
+    ulp apart (or, for a near-zero difference of larger terms, a small absolute
+    amount); nearly every element is bit-equal."""
+    g = bn_gold
+    for i in range(int(g["cases"][0])):
+        N, Cc, H, W, relu, affine = (int(v) for v in g[f"c{i}_meta"])
+        slope = float(g[f"c{i}_slope"][0])
+        w = g[f"c{i}_w"] if affine else None
+        b = g[f"c{i}_b"] if affine else None
+        y, mean, invstd, rm, rv, dx, dw, db = _gpu_bn(cuda, g[f"c{i}_x"], w, b, g[f"c{i}_rm"], g[f"c{i}_rv"],
+                                                      slope, relu, g[f"c{i}_dy"])
+        M = N * H * W
+        _bf_close(y, g[f"c{i}_y"], 1e-5 * np.abs(oracle.bf16_value(g[f"c{i}_y"])).max())
+        np.testing.assert_allclose(mean, g[f"c{i}_mean"], rtol=0, atol=1e-6 * max(1.0, np.abs(mean).max()))
+        np.testing.assert_allclose(invstd, g[f"c{i}_invstd"], rtol=1e-6)
+        assert _ulps(rm, g[f"c{i}_rm_out"]).max() <= 1 and _ulps(rv, g[f"c{i}_rv_out"]).max() <= 1
+        # backward on the reference's activation with planted 0 / NaN (the dz rule)
+        *_, dx, dw, db = _gpu_bn(cuda, g[f"c{i}_x"], w, b, g[f"c{i}_rm"], g[f"c{i}_rv"], slope, relu,
+                                 g[f"c{i}_dy"], ybwd=g[f"c{i}_ybwd"])
+        _bf_close(dx, g[f"c{i}_dx"], 1e-5 * np.abs(oracle.bf16_value(g[f"c{i}_dx"])).max())
+        _bf_close(dw, g[f"c{i}_dw"], 2e-6 * M, exact=0.9)
+        _bf_close(db, g[f"c{i}_db"], 2e-6 * M, exact=0.9)
+
+
+# warp-per-plane (>= 32 planes per SM) and block-per-plane paths, 16-byte
+# vector and scalar (HW % 8 != 0) paths, N = 1, C = 1, no affine, no update
+@pytest.mark.parametrize("shape,slope,relu,affine", [
+    ((40, 128, 9, 9), 0.2, 0, True),      # 5120 planes, scalar
+    ((64, 96, 16, 16), 0.0, 1, True),     # 6144 planes, vector
+    ((2, 64, 56, 56), 0.0, 1, True),      # block per plane, vector
+    ((3, 5, 7, 9), 0.2, 0, True),         # block per plane, scalar
+    ((1, 32, 20, 20), 0.01, 0, False),    # N = 1, affine=False
+    ((16, 1, 12, 12), 0.0, 1, True),      # C = 1
+])
+def test_bn_act_vs_oracle(cuda, shape, slope, relu, affine):
+    rng = np.random.default_rng(sum(shape))
+    N, Cc = shape[:2]
+    x = oracle.bf16_bits((rng.standard_normal(shape) * 1.5 + 0.3).astype(np.float32))
+    w = oracle.bf16_bits(rng.uniform(0.5, 1.5, Cc).astype(np.float32)) if affine else None
+    b = oracle.bf16_bits((rng.standard_normal(Cc) * 0.3).astype(np.float32)) if affine else None
+    rm = oracle.bf16_bits((rng.standard_normal(Cc) * 0.1).astype(np.float32))
+    rv = oracle.bf16_bits(rng.uniform(0.5, 1.5, Cc).astype(np.float32))
+    dy = oracle.bf16_bits(rng.standard_normal(shape).astype(np.float32))
+    y, mean, invstd, rm2, rv2, dx, dw, db = _gpu_bn(cuda, x, w, b, rm, rv, slope, relu, dy)
+    oy, omean, oinv, orm, orv = oracle.bn_fwd(x, w, b, rm, rv, 1e-5, slope, 0.1, True)
+    np.testing.assert_allclose(mean, omean, rtol=0, atol=1e-6 * max(1.0, np.abs(omean).max()))
+    np.testing.assert_allclose(invstd, oinv, rtol=1e-6)
+    M = int(np.prod(shape)) // Cc
+    _bf_close(y, oy, 1e-5 * np.abs(oracle.bf16_value(oy)).max())
+    assert _ulps(rm2, orm).max() <= 1 and _ulps(rv2, orv).max() <= 1
+    # backward from the GPU's own statistics, so only the backward is compared
+    odx, odw, odb = oracle.bn_bwd(dy, y, x, w, mean, invstd, slope, bool(relu))
+    _bf_close(dx, odx, 1e-5 * np.abs(oracle.bf16_value(odx)).max())
+    _bf_close(dw, odw, 2e-6 * M, exact=0.9)
+    _bf_close(db, odb, 2e-6 * M, exact=0.9)
+    # only some gradients requested; no running-statistics update
+    y3, _, _, rm3, rv3, dx3, dw3, db3 = _gpu_bn(cuda, x, w, b, rm, rv, slope, relu, dy, need=(False, True, False),
+                                                update=False)
+    assert np.array_equal(y3, y) and np.array_equal(rm3, rm) and np.array_equal(rv3, rv)
+    assert dx3 is None and db3 is None and np.array_equal(dw3, dw)
+
+
+def test_bn_act_rejects_small_workspace(cuda):
+    t = torch.zeros(64, dtype=torch.float32, device=cuda)
+    rc = _abi.lib().b2_region_bn_fwd_bf16(t.data_ptr(), None, None, None, None, t.data_ptr(), t.data_ptr(),
+                                          t.data_ptr(), 2, 4, 8, ctypes.c_float(1e-5), ctypes.c_float(0.0),
+                                          ctypes.c_float(0.1), 0, t.data_ptr(), 8, st())
+    assert rc == 5 and b"workspace" in _abi.lib().b2_last_error()

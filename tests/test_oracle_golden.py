@@ -126,3 +126,45 @@ def test_oracle_gemm_and_adam():
                         eps=1e-8, amsgrad=False, maximize=False)
     assert np.abs(P - p.numpy()).max() <= 1e-6
     assert np.abs(M - m.numpy()).max() <= 1e-6
+
+
+def _ulps(a, b):
+    return np.abs(a.astype(np.int32) - b.astype(np.int32))
+
+
+def _bf_close(got, want, floor, exact=0.995):
+    """One bf16 ulp, or `floor` absolutely for near-zero differences of larger
+    terms; at least `exact` of the elements bit-equal."""
+    g, w = oracle.bf16_value(got), oracle.bf16_value(want)
+    assert (np.abs(g - w) <= np.abs(w) * 2.0 ** -7 + floor).all()
+    assert (got == want).mean() >= exact
+
+
+@pytest.fixture(scope="module")
+def bn():
+    return np.load(GOLD / "regions_bn.npz")
+
+
+def test_bn_norm_activation_matches_reference(bn):
+    """Fused BatchNorm + activation: the oracle against the reference's own host
+    kernels (region_kernels.cpp:309-460).  The oracle's statistics are summed in
+    double, the reference's plane sums in fp32, so outputs may differ by one bf16
+    ulp where a value lies on a rounding boundary, or by a small absolute amount
+    where the result is a near-zero difference of larger terms."""
+    for i in range(int(bn["cases"][0])):
+        N, Cc, H, W, relu, affine = (int(v) for v in bn[f"c{i}_meta"])
+        slope = float(bn[f"c{i}_slope"][0])
+        w = bn[f"c{i}_w"] if affine else None
+        b = bn[f"c{i}_b"] if affine else None
+        x = bn[f"c{i}_x"]
+        y, mean, invstd, rm, rv = oracle.bn_fwd(x, w, b, bn[f"c{i}_rm"], bn[f"c{i}_rv"], 1e-5, slope, 0.1, True)
+        np.testing.assert_allclose(mean, bn[f"c{i}_mean"], rtol=0, atol=2e-7 * max(1.0, np.abs(mean).max()))
+        np.testing.assert_allclose(invstd, bn[f"c{i}_invstd"], rtol=3e-7)
+        _bf_close(y, bn[f"c{i}_y"], 1e-5 * np.abs(oracle.bf16_value(bn[f"c{i}_y"])).max())
+        assert _ulps(rm, bn[f"c{i}_rm_out"]).max() <= 1 and _ulps(rv, bn[f"c{i}_rv_out"]).max() <= 1
+        # backward from the reference's own statistics, on an activation with planted 0 / NaN
+        dx, dw, db = oracle.bn_bwd(bn[f"c{i}_dy"], bn[f"c{i}_ybwd"], x, w, bn[f"c{i}_mean"], bn[f"c{i}_invstd"],
+                                   slope, bool(relu))
+        _bf_close(dx, bn[f"c{i}_dx"], 1e-5 * np.abs(oracle.bf16_value(bn[f"c{i}_dx"])).max())
+        _bf_close(dw, bn[f"c{i}_dw"], 2e-6 * N * H * W, exact=0.9)
+        _bf_close(db, bn[f"c{i}_db"], 2e-6 * N * H * W, exact=0.9)
