@@ -240,6 +240,29 @@ b2_status b2_region_maxpool2_bwd_bf16(const void* x, const void* g, void* out,
                                       int64_t planes, int64_t H, int64_t W,
                                       void* stream);
 
+/* ---- layout ops (replace the reference's host cat / nearest-2x upsample,
+ * torch_xdna_device.cpp:3796-4175; used by the xdna `cat`,
+ * `upsample_nearest2d` and `upsample_nearest2d_backward` kernels) ---------- */
+
+/* Concatenation of contiguous byte blocks: for every outer index o and source
+ * i (in order), block_bytes[i] bytes at srcs[i] + o*block_bytes[i] go to dst +
+ * o*out_block_bytes + (block_bytes[0] + ... + block_bytes[i-1]).  The blocks
+ * must add up to out_block_bytes.  Any dtype; any number of sources. */
+b2_status b2_cat_blocks(const void* const* srcs, const int64_t* block_bytes,
+                        int n, void* dst, int64_t outer,
+                        int64_t out_block_bytes, void* stream);
+/* Nearest 2x upsampling [N, C, H, W] -> [N, C, 2H, 2W] (a copy).  dtype
+ * B2_BF16 or B2_F32; layout 0 = contiguous NCHW, 1 = channels-last NHWC. */
+b2_status b2_upsample_nearest2x(const void* in, void* out, int dtype,
+                                int layout, int64_t N, int64_t C, int64_t H,
+                                int64_t W, void* stream);
+/* Its backward: each input gradient = the fp32 sum of its 2x2 block of output
+ * gradients from +0 in raster order (ATen's CPU order, x86 NaN propagation),
+ * rounded once (bf16: nearest even, NaN -> 0x7FC0). */
+b2_status b2_upsample_nearest2x_backward(const void* go, void* gi, int dtype,
+                                         int layout, int64_t N, int64_t C,
+                                         int64_t H, int64_t W, void* stream);
+
 /* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
  * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,
  * region_kernels.cpp:309-460; used by regions.fuse_norm_activation,

@@ -56,6 +56,9 @@ SIGNATURES = {
     "b2_region_addtap_bf16": [vp, vp, vp, vp, i64, f32, vp],
     "b2_region_relu_bwd_bf16": [vp, vp, vp, vp, vp, i64, f32, vp],
     "b2_region_maxpool2_bwd_bf16": [vp, vp, vp, i64, i64, i64, vp],
+    "b2_cat_blocks": [vp, vp, i32, vp, i64, i64, vp],
+    "b2_upsample_nearest2x": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
+    "b2_upsample_nearest2x_backward": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_region_bn_workspace_bytes": [i64, i64],
     "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
     "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
