@@ -263,6 +263,35 @@ b2_status b2_upsample_nearest2x_backward(const void* go, void* gi, int dtype,
                                          int layout, int64_t N, int64_t C,
                                          int64_t H, int64_t W, void* stream);
 
+/* Training-mode BatchNorm on bf16 activations [N, C, HW] (replaces the
+ * reference's native_batch_norm / native_batch_norm_backward on CPU aliases,
+ * torch_xdna_device.cpp:4214-4358).  layout 0 = contiguous NCHW; 1 =
+ * channels-last NHWC (C % 8 == 0, C <= 2048, 16-byte aligned tensors).
+ * Batch statistics as in the fused region below (NCHW: per-plane fp32, Chan
+ * merge in double; NHWC: one pass of shifted fp32 sums, merged in double);
+ * y = x*scale + shift.  w, b (dtype pdtype), rm, rv (dtype rdtype; updated with
+ * `momentum` when both are given) may be NULL; pdtype / rdtype are B2_BF16 or
+ * B2_F32.  save_mean / save_invstd: fp32 [C].  Workspace: at least
+ * b2_batch_norm_workspace_bytes(N, C, HW, layout) bytes, 16-byte aligned. */
+size_t b2_batch_norm_workspace_bytes(int64_t N, int64_t C, int64_t HW,
+                                     int layout);
+b2_status b2_batch_norm_fwd_bf16(const void* x, int layout, const void* w,
+                                 const void* b, int pdtype, void* rm, void* rv,
+                                 int rdtype, void* y, float* save_mean,
+                                 float* save_invstd, int64_t N, int64_t C,
+                                 int64_t HW, float momentum, float eps,
+                                 void* workspace, size_t workspace_bytes,
+                                 void* stream);
+/* Backward from the saved batch statistics: dx (may be NULL), dw = sum
+ * dy*xhat, db = sum dy (dtype gdtype, each may be NULL). */
+b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout,
+                                 const void* w, int pdtype,
+                                 const float* save_mean,
+                                 const float* save_invstd, void* dx, void* dw,
+                                 void* db, int gdtype, int64_t N, int64_t C,
+                                 int64_t HW, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
  * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,
  * region_kernels.cpp:309-460; used by regions.fuse_norm_activation,

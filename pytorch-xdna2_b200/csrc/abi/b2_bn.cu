@@ -1,28 +1,37 @@
-// Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16, the fused
-// pair behind xdna_train.regions.fuse_norm_activation.  Same contract as the
-// reference's host kernels (xdna_train/_native/region_kernels.cpp:309-460):
+// Training BatchNorm2d on bf16 activations, alone (the xdna
+// native_batch_norm kernels) or fused with the ReLU / LeakyReLU applied
+// directly to its output (xdna_train.regions.fuse_norm_activation).  Same
+// contract as the reference's fused host kernels
+// (xdna_train/_native/region_kernels.cpp:309-460):
 //
-//   statistics  each (n, c) plane reduced in fp32: mean = sum / HW, then the
-//               sum of squared deviations from that mean; the N planes of a
-//               channel merged in double, in plane order, with Chan's
-//               parallel-variance formula; invstd = 1 / sqrt(var + eps) in
-//               double; running statistics (bf16) updated with the unbiased
-//               variance.
 //   forward     y = act(x*scale + shift), scale = w*invstd, shift = b -
-//               mean*scale, act(z) = z > 0 ? z : z*slope, one rounding to bf16.
+//               mean*scale, act(z) = z > 0 ? z : z*slope (slope 1: plain BN),
+//               one rounding to bf16; invstd = 1/sqrt(var + eps) in double from
+//               the biased variance; running statistics move by `momentum`
+//               towards the mean and the unbiased variance.
 //   backward    dz = dy where y > 0 (or y is NaN and the activation is ReLU),
-//               else dy*slope; db = sum dz, dw = sum dz*xhat (plane sums in
-//               fp32, channel sums in double); dx = w*invstd*(dz - db/M -
-//               xhat*dw/M).
+//               else dy*slope (dz = dy without an activation); db = sum dz,
+//               dw = sum dz*xhat (fp32 partial sums, summed in double in a
+//               fixed order, see merge_partials: deterministic);
+//               dx = w*invstd*(dz - db/M - xhat*dw/M), xhat = (x - mean)*invstd.
 //
-// Every elementwise expression is evaluated with explicitly rounded fp32
-// operations in the reference's order (no FMA contraction: the reference's
-// host build has none), so the outputs differ from the reference only where
-// the fp32 plane sums do (their summation order differs).
+// Two memory layouts:
+//   NCHW  each (n, c) plane reduced in fp32 (mean, then the squared
+//         deviations from it; the second read of a plane hits L1/L2), the N
+//         planes of a channel merged in double, in plane order, with Chan's
+//         parallel-variance formula -- the reference's statistics.
+//   NHWC  (channels-last) one read of x: every thread accumulates, for 8
+//         consecutive channels, sums of x - K and (x - K)^2 with K the first
+//         pixel's value of the channel (a shift that keeps the variance free
+//         of cancellation); block partials merged in double in a fixed order.
 //
-// Memory traffic (M = N*C*HW elements): forward 6 B/elem (stats read x, apply
-// reads x and writes y), backward 14 B/elem (plane sums read dy, y, x; dx reads
-// them again and writes dx).  Second reads of tensors smaller than L2 hit L2.
+// Every elementwise expression uses explicitly rounded fp32 operations in the
+// reference's order (no FMA contraction: the reference's host build has none).
+//
+// Memory traffic (M = N*C*HW elements, algorithmic): forward 6 B/elem (x read
+// twice, y written), backward 8 B/elem for plain BN (dy and x twice, dx
+// written; the second reads of tensors smaller than L2 hit L2), 12 B/elem with
+// the activation (y read twice too).  NHWC forward: x once for the sums.
 #include <algorithm>
 
 #include "b2_common.cuh"
@@ -31,6 +40,8 @@ namespace b2 {
 namespace {
 
 constexpr int kBnThreads = 256;
+constexpr long long kMaxSumBlocks = 1024;  // NHWC partial-sum blocks (workspace bound)
+constexpr long long kMaxNhwcChannels = 2048;
 
 // Sum over the TPP threads of a plane group (a warp, or the whole block).
 template <int TPP>
@@ -59,6 +70,69 @@ __device__ __forceinline__ void unpack8(const uint4 v, float* f) {
     f[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
   }
 }
+
+__device__ __forceinline__ uint4 pack8(const float* r) {
+  uint4 o;
+  o.x = pack_bf2(r[0], r[1]);
+  o.y = pack_bf2(r[2], r[3]);
+  o.z = pack_bf2(r[4], r[5]);
+  o.w = pack_bf2(r[6], r[7]);
+  return o;
+}
+
+// Per-channel vectors are bf16 or fp32 (B2_BF16 / B2_F32); absent -> dflt.
+__device__ __forceinline__ float ld_par(const void* p, int dt, long long c, float dflt) {
+  if (!p) return dflt;
+  return dt == B2_F32 ? static_cast<const float*>(p)[c] : bf2f(static_cast<const uint16_t*>(p)[c]);
+}
+__device__ __forceinline__ void st_par(void* p, int dt, long long c, float v) {
+  if (dt == B2_F32) static_cast<float*>(p)[c] = v;
+  else static_cast<uint16_t*>(p)[c] = f2bf(v);
+}
+
+// Per-channel operands of the forward.
+struct BnChan {
+  const void* w;
+  const void* b;
+  int pdtype;  // dtype of w, b
+  void* rm;
+  void* rv;
+  int rdtype;  // dtype of rm, rv; statistics updated when both are non-null
+};
+
+__device__ __forceinline__ void finish_stats(long long c, double mean, double var, double M, float eps,
+                                             float momentum, const BnChan& ch, float* mean_out,
+                                             float* invstd_out) {
+  mean_out[c] = float(mean);
+  invstd_out[c] = float(1.0 / sqrt(var + double(eps)));
+  if (ch.rm && ch.rv) {
+    const double unbiased = M > 1.0 ? var * M / (M - 1.0) : var;
+    const double f = double(momentum);
+    st_par(ch.rm, ch.rdtype, c, float((1.0 - f) * double(ld_par(ch.rm, ch.rdtype, c, 0.f)) + f * mean));
+    st_par(ch.rv, ch.rdtype, c, float((1.0 - f) * double(ld_par(ch.rv, ch.rdtype, c, 0.f)) + f * unbiased));
+  }
+}
+
+__device__ __forceinline__ float bn_act(float xv, float scale, float shift, float slope) {
+  const float z = __fadd_rn(__fmul_rn(xv, scale), shift);
+  return z > 0.0f ? z : __fmul_rn(z, slope);
+}
+
+template <bool ACT>
+__device__ __forceinline__ float bn_dz(float g, float yv, float slope, int relu) {
+  if constexpr (!ACT) return g;
+  else return ((yv > 0.0f) || (relu && yv != yv)) ? g : __fmul_rn(g, slope);
+}
+
+template <bool ACT>
+__device__ __forceinline__ float bn_dx(float g, float yv, float xv, float mc, float is, float ws, float k1,
+                                       float k2, float slope, int relu) {
+  const float dz = bn_dz<ACT>(g, yv, slope, relu);
+  const float xhat = __fmul_rn(__fsub_rn(xv, mc), is);
+  return __fmul_rn(ws, __fsub_rn(__fsub_rn(dz, k1), __fmul_rn(xhat, k2)));
+}
+
+// ============================ NCHW ==========================================
 
 // Per-plane fp32 mean and sum of squared deviations.  TPP threads per plane:
 // a warp (many small planes) or the whole block (few large planes).  VEC:
@@ -124,9 +198,8 @@ __global__ void __launch_bounds__(kBnThreads) bn_plane_stats_kernel(
 // One thread per channel: Chan's merge of the N plane statistics in double,
 // in plane order; mean / invstd out; running statistics.
 __global__ void bn_channel_stats_kernel(const float* __restrict__ pm, const float* __restrict__ pq,
-                                        long long N, long long C, long long hw, float eps,
-                                        float factor, int update, uint16_t* rm, uint16_t* rv,
-                                        float* __restrict__ mean_out, float* __restrict__ invstd_out) {
+                                        long long N, long long C, long long hw, float eps, float momentum,
+                                        BnChan ch, float* __restrict__ mean_out, float* __restrict__ invstd_out) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   const double nb = double(hw);
@@ -139,55 +212,33 @@ __global__ void bn_channel_stats_kernel(const float* __restrict__ pm, const floa
     count = tot;
   }
   const double M = double(N) * nb;
-  const double var = m2 / M;
-  mean_out[c] = float(mean);
-  invstd_out[c] = float(1.0 / sqrt(var + double(eps)));
-  if (update) {
-    const double unbiased = M > 1.0 ? var * M / (M - 1.0) : var;
-    const double f = double(factor);
-    rm[c] = f2bf(float((1.0 - f) * double(bf2f(rm[c])) + f * mean));
-    rv[c] = f2bf(float((1.0 - f) * double(bf2f(rv[c])) + f * unbiased));
-  }
-}
-
-__device__ __forceinline__ float bn_act(float xv, float scale, float shift, float slope) {
-  const float z = __fadd_rn(__fmul_rn(xv, scale), shift);
-  return z > 0.0f ? z : __fmul_rn(z, slope);
+  finish_stats(c, mean, m2 / M, M, eps, momentum, ch, mean_out, invstd_out);
 }
 
 // y = act(x*scale + shift); one thread per 8 elements (VEC) or per element.
 template <bool VEC>
 __global__ void __launch_bounds__(kBnThreads) bn_apply_kernel(
-    const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, const uint16_t* __restrict__ b,
-    const float* __restrict__ mean, const float* __restrict__ invstd, uint16_t* __restrict__ y,
-    long long units, long long units_per_plane, long long C, float slope) {
+    const uint16_t* __restrict__ x, BnChan ch, const float* __restrict__ mean, const float* __restrict__ invstd,
+    uint16_t* __restrict__ y, long long units, long long units_per_plane, long long C, float slope) {
   for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
        u += (long long)gridDim.x * kBnThreads) {
     const long long c = (u / units_per_plane) % C;
-    const float is = __ldg(invstd + c);
-    const float scale = __fmul_rn(w ? bf2f(__ldg(w + c)) : 1.0f, is);
-    const float shift = __fsub_rn(b ? bf2f(__ldg(b + c)) : 0.0f, __fmul_rn(__ldg(mean + c), scale));
+    const float scale = __fmul_rn(ld_par(ch.w, ch.pdtype, c, 1.0f), __ldg(invstd + c));
+    const float shift = __fsub_rn(ld_par(ch.b, ch.pdtype, c, 0.0f), __fmul_rn(__ldg(mean + c), scale));
     if constexpr (VEC) {
-      float f[8];
+      float f[8], r[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), f);
-      uint4 o;
-      o.x = pack_bf2(bn_act(f[0], scale, shift, slope), bn_act(f[1], scale, shift, slope));
-      o.y = pack_bf2(bn_act(f[2], scale, shift, slope), bn_act(f[3], scale, shift, slope));
-      o.z = pack_bf2(bn_act(f[4], scale, shift, slope), bn_act(f[5], scale, shift, slope));
-      o.w = pack_bf2(bn_act(f[6], scale, shift, slope), bn_act(f[7], scale, shift, slope));
-      reinterpret_cast<uint4*>(y)[u] = o;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale, shift, slope);
+      reinterpret_cast<uint4*>(y)[u] = pack8(r);
     } else {
       y[u] = f2bf(bn_act(bf2f(x[u]), scale, shift, slope));
     }
   }
 }
 
-__device__ __forceinline__ float bn_dz(float g, float yv, float slope, int relu) {
-  return ((yv > 0.0f) || (relu && yv != yv)) ? g : __fmul_rn(g, slope);
-}
-
 // Per-plane fp32 sums of dz and dz*xhat.
-template <int TPP, bool VEC>
+template <int TPP, bool VEC, bool ACT>
 __global__ void __launch_bounds__(kBnThreads) bn_bwd_plane_kernel(
     const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y, const uint16_t* __restrict__ x,
     const float* __restrict__ mean, const float* __restrict__ invstd, long long planes, long long C,
@@ -208,23 +259,23 @@ __global__ void __launch_bounds__(kBnThreads) bn_bwd_plane_kernel(
       const long long off = pl * hw;
       if constexpr (VEC) {
         const uint4* dv = reinterpret_cast<const uint4*>(dy + off);
-        const uint4* yv = reinterpret_cast<const uint4*>(y + off);
+        const uint4* yv = reinterpret_cast<const uint4*>((ACT ? y : dy) + off);
         const uint4* xv = reinterpret_cast<const uint4*>(x + off);
         for (long long v = lane; v < hw / 8; v += TPP) {
           float fg[8], fy[8], fx[8];
           unpack8(__ldg(dv + v), fg);
-          unpack8(__ldg(yv + v), fy);
+          if constexpr (ACT) unpack8(__ldg(yv + v), fy);
           unpack8(__ldg(xv + v), fx);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const float dz = bn_dz(fg[k], fy[k], slope, relu);
+            const float dz = bn_dz<ACT>(fg[k], ACT ? fy[k] : 0.0f, slope, relu);
             s1 = __fadd_rn(s1, dz);
             s2 = __fadd_rn(s2, __fmul_rn(dz, __fmul_rn(__fsub_rn(fx[k], mc), is)));
           }
         }
       } else {
         for (long long i = lane; i < hw; i += TPP) {
-          const float dz = bn_dz(bf2f(dy[off + i]), bf2f(y[off + i]), slope, relu);
+          const float dz = bn_dz<ACT>(bf2f(dy[off + i]), ACT ? bf2f(y[off + i]) : 0.0f, slope, relu);
           s1 = __fadd_rn(s1, dz);
           s2 = __fadd_rn(s2, __fmul_rn(dz, __fmul_rn(__fsub_rn(bf2f(x[off + i]), mc), is)));
         }
@@ -239,62 +290,271 @@ __global__ void __launch_bounds__(kBnThreads) bn_bwd_plane_kernel(
   }
 }
 
-// One thread per channel: double sums over the N planes in order; db, dw and
-// the two means the dx pass needs (k[c] = db/M, k[C + c] = dw/M).
-__global__ void bn_bwd_channel_kernel(const float* __restrict__ ps, const float* __restrict__ pt,
-                                      long long N, long long C, long long hw, uint16_t* dw,
-                                      uint16_t* db, float* __restrict__ k) {
-  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  double a = 0.0, bs = 0.0;
-  for (long long n = 0; n < N; ++n) {
-    a += double(ps[n * C + c]);
-    bs += double(pt[n * C + c]);
+// Sums of `parts` partial rows (row r at pa[r*C + c]) per channel, in double,
+// in a fixed order: a block covers 32 channels (one per lane, coalesced
+// reads); warp w adds rows w, w+8, w+16, ... in order; the eight warp sums are
+// then added in warp order.  Deterministic and independent of scheduling.
+constexpr int kMergeWarps = 8;
+
+__device__ __forceinline__ bool merge_partials(const float* __restrict__ pa, const float* __restrict__ pb,
+                                               long long parts, long long C, double& a, double& b) {
+  __shared__ double ra[kMergeWarps][32], rb[kMergeWarps][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long c = (long long)blockIdx.x * 32 + lane;
+  double sa = 0.0, sb = 0.0;
+  if (c < C) {
+    for (long long r = w; r < parts; r += kMergeWarps) {
+      sa += double(pa[r * C + c]);
+      sb += double(pb[r * C + c]);
+    }
   }
-  if (db) db[c] = f2bf(float(a));
-  if (dw) dw[c] = f2bf(float(bs));
-  const double M = double(N) * double(hw);
+  ra[w][lane] = sa;
+  rb[w][lane] = sb;
+  __syncthreads();
+  if (w != 0 || c >= C) return false;
+  a = ra[0][lane];
+  b = rb[0][lane];
+#pragma unroll
+  for (int k = 1; k < kMergeWarps; ++k) {
+    a += ra[k][lane];
+    b += rb[k][lane];
+  }
+  return true;
+}
+
+// Backward: db, dw (dtype gdtype) and the two means the dx pass needs
+// (k[c] = db/M, k[C + c] = dw/M).  Grid: ceil(C/32) blocks of 256 threads.
+__global__ void __launch_bounds__(kMergeWarps * 32) bn_bwd_channel_kernel(
+    const float* __restrict__ ps, const float* __restrict__ pt, long long parts, long long C, double M, void* dw,
+    void* db, int gdtype, float* __restrict__ k) {
+  double a, bs;
+  if (!merge_partials(ps, pt, parts, C, a, bs)) return;
+  const long long c = (long long)blockIdx.x * 32 + threadIdx.x;
+  if (db) st_par(db, gdtype, c, float(a));
+  if (dw) st_par(dw, gdtype, c, float(bs));
   k[c] = float(a / M);
   k[C + c] = float(bs / M);
 }
 
-__device__ __forceinline__ float bn_dx(float g, float yv, float xv, float mc, float is, float ws,
-                                       float k1, float k2, float slope, int relu) {
-  const float dz = bn_dz(g, yv, slope, relu);
-  const float xhat = __fmul_rn(__fsub_rn(xv, mc), is);
-  return __fmul_rn(ws, __fsub_rn(__fsub_rn(dz, k1), __fmul_rn(xhat, k2)));
-}
-
-template <bool VEC>
+template <bool VEC, bool ACT>
 __global__ void __launch_bounds__(kBnThreads) bn_bwd_dx_kernel(
     const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y, const uint16_t* __restrict__ x,
-    const uint16_t* __restrict__ w, const float* __restrict__ mean, const float* __restrict__ invstd,
+    const void* w, int pdtype, const float* __restrict__ mean, const float* __restrict__ invstd,
     const float* __restrict__ k, uint16_t* __restrict__ dx, long long units, long long units_per_plane,
     long long C, float slope, int relu) {
   for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
        u += (long long)gridDim.x * kBnThreads) {
     const long long c = (u / units_per_plane) % C;
     const float mc = __ldg(mean + c), is = __ldg(invstd + c);
-    const float ws = __fmul_rn(w ? bf2f(__ldg(w + c)) : 1.0f, is);
+    const float ws = __fmul_rn(ld_par(w, pdtype, c, 1.0f), is);
     const float k1 = __ldg(k + c), k2 = __ldg(k + C + c);
     if constexpr (VEC) {
       float fg[8], fy[8], fx[8], r[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(dy) + u), fg);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
+      if constexpr (ACT) unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
       unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), fx);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) r[e] = bn_dx(fg[e], fy[e], fx[e], mc, is, ws, k1, k2, slope, relu);
-      uint4 o;
-      o.x = pack_bf2(r[0], r[1]);
-      o.y = pack_bf2(r[2], r[3]);
-      o.z = pack_bf2(r[4], r[5]);
-      o.w = pack_bf2(r[6], r[7]);
-      reinterpret_cast<uint4*>(dx)[u] = o;
+      for (int e = 0; e < 8; ++e)
+        r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc, is, ws, k1, k2, slope, relu);
+      reinterpret_cast<uint4*>(dx)[u] = pack8(r);
     } else {
-      dx[u] = f2bf(bn_dx(bf2f(dy[u]), bf2f(y[u]), bf2f(x[u]), mc, is, ws, k1, k2, slope, relu));
+      dx[u] = f2bf(bn_dx<ACT>(bf2f(dy[u]), ACT ? bf2f(y[u]) : 0.0f, bf2f(x[u]), mc, is, ws, k1, k2, slope,
+                              relu));
     }
   }
 }
+
+// ============================ NHWC ==========================================
+// x viewed as [P pixels][C], C % 8 == 0, C <= kMaxNhwcChannels, 16-byte
+// aligned.  A block is CV = C/8 channel groups wide and rpb = 256/CV pixel rows
+// deep; thread (row pr, group cg) owns channels [8cg, 8cg+8).
+
+struct NhwcShape {
+  long long P;
+  int C, CV, rpb;
+};
+
+// Sums per block and channel:  forward  a = sum(x - K), b = sum((x - K)^2)
+//                              backward a = sum(dz),    b = sum(dz * xhat)
+template <bool BWD, bool ACT>
+__global__ void __launch_bounds__(kBnThreads) bn_nhwc_sums_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y,
+    const float* __restrict__ mean, const float* __restrict__ invstd, NhwcShape sh, float slope, int relu,
+    float* __restrict__ part_a, float* __restrict__ part_b) {
+  extern __shared__ float red[];  // [2][rpb][C]
+  const int cg = threadIdx.x % sh.CV, pr = threadIdx.x / sh.CV;
+  const bool active = pr < sh.rpb;
+  float a[8], b[8], k0[8], k1[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) a[e] = b[e] = 0.0f;
+  if (active) {
+    const int c0 = cg * 8;
+    if constexpr (BWD) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        k0[e] = mean[c0 + e];
+        k1[e] = invstd[c0 + e];
+      }
+    } else {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x) + cg), k0);  // shift K: the first pixel
+    }
+    const long long step = (long long)gridDim.x * sh.rpb;
+    for (long long p = (long long)blockIdx.x * sh.rpb + pr; p < sh.P; p += step) {
+      const long long u = p * sh.CV + cg;
+      float fx[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), fx);
+      if constexpr (BWD) {
+        float fg[8], fy[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(dy) + u), fg);
+        if constexpr (ACT) unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float dz = bn_dz<ACT>(fg[e], ACT ? fy[e] : 0.0f, slope, relu);
+          a[e] = __fadd_rn(a[e], dz);
+          b[e] = __fadd_rn(b[e], __fmul_rn(dz, __fmul_rn(__fsub_rn(fx[e], k0[e]), k1[e])));
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = __fsub_rn(fx[e], k0[e]);
+          a[e] = __fadd_rn(a[e], d);
+          b[e] = __fadd_rn(b[e], __fmul_rn(d, d));
+        }
+      }
+    }
+    float* ra = red + (long long)pr * sh.C + cg * 8;
+    float* rb = red + (long long)(sh.rpb + pr) * sh.C + cg * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ra[e] = a[e];
+      rb[e] = b[e];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < sh.C; c += kBnThreads) {
+    float sa = 0.0f, sb = 0.0f;
+    for (int r = 0; r < sh.rpb; ++r) {
+      sa = __fadd_rn(sa, red[(long long)r * sh.C + c]);
+      sb = __fadd_rn(sb, red[(long long)(sh.rpb + r) * sh.C + c]);
+    }
+    part_a[(long long)blockIdx.x * sh.C + c] = sa;
+    part_b[(long long)blockIdx.x * sh.C + c] = sb;
+  }
+}
+
+// Forward merge of the block partials (merge_partials order), statistics out.
+__global__ void __launch_bounds__(kMergeWarps * 32) bn_nhwc_stats_kernel(
+    const uint16_t* __restrict__ x, const float* __restrict__ part_a, const float* __restrict__ part_b,
+    long long blocks, long long C, long long P, float eps, float momentum, BnChan ch, float* __restrict__ mean_out,
+    float* __restrict__ invstd_out) {
+  double s, q;
+  if (!merge_partials(part_a, part_b, blocks, C, s, q)) return;
+  const long long c = (long long)blockIdx.x * 32 + threadIdx.x;
+  const double M = double(P);
+  const double shift = double(bf2f(x[c]));
+  const double var = fmax(0.0, (q - s * s / M) / M);
+  finish_stats(c, shift + s / M, var, M, eps, momentum, ch, mean_out, invstd_out);
+}
+
+// y = act(x*scale + shift).  FIXED: CV divides the block size, so every
+// thread keeps one channel group through the grid-stride loop and holds its 8
+// scales and shifts in registers; otherwise they are staged in shared memory.
+template <bool FIXED>
+__global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
+    const uint16_t* __restrict__ x, BnChan ch, const float* __restrict__ mean, const float* __restrict__ invstd,
+    uint16_t* __restrict__ y, NhwcShape sh, float slope) {
+  extern __shared__ float tab[];  // scale[C], shift[C] (!FIXED)
+  float scale[8], shift[8];
+  if constexpr (FIXED) {
+    const int c0 = int(threadIdx.x % sh.CV) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      scale[e] = __fmul_rn(ld_par(ch.w, ch.pdtype, c0 + e, 1.0f), invstd[c0 + e]);
+      shift[e] = __fsub_rn(ld_par(ch.b, ch.pdtype, c0 + e, 0.0f), __fmul_rn(mean[c0 + e], scale[e]));
+    }
+  } else {
+    for (int c = threadIdx.x; c < sh.C; c += kBnThreads) {
+      const float sc = __fmul_rn(ld_par(ch.w, ch.pdtype, c, 1.0f), invstd[c]);
+      tab[c] = sc;
+      tab[sh.C + c] = __fsub_rn(ld_par(ch.b, ch.pdtype, c, 0.0f), __fmul_rn(mean[c], sc));
+    }
+    __syncthreads();
+  }
+  const long long units = sh.P * sh.CV;
+  for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
+       u += (long long)gridDim.x * kBnThreads) {
+    if constexpr (!FIXED) {
+      const int c0 = int(u % sh.CV) * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        scale[e] = tab[c0 + e];
+        shift[e] = tab[sh.C + c0 + e];
+      }
+    }
+    float f[8], r[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
+    reinterpret_cast<uint4*>(y)[u] = pack8(r);
+  }
+}
+
+template <bool ACT, bool FIXED>
+__global__ void __launch_bounds__(kBnThreads) bn_nhwc_dx_kernel(
+    const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y, const uint16_t* __restrict__ x,
+    const void* w, int pdtype, const float* __restrict__ mean, const float* __restrict__ invstd,
+    const float* __restrict__ k, uint16_t* __restrict__ dx, NhwcShape sh, float slope, int relu) {
+  extern __shared__ float tab[];  // ws[C], mean[C], invstd[C], k1[C], k2[C] (!FIXED)
+  const int C = sh.C;
+  float ws[8], mc[8], is[8], k1[8], k2[8];
+  if constexpr (FIXED) {
+    const int c0 = int(threadIdx.x % sh.CV) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = c0 + e;
+      ws[e] = __fmul_rn(ld_par(w, pdtype, c, 1.0f), invstd[c]);
+      mc[e] = mean[c];
+      is[e] = invstd[c];
+      k1[e] = k[c];
+      k2[e] = k[C + c];
+    }
+  } else {
+    for (int c = threadIdx.x; c < C; c += kBnThreads) {
+      tab[c] = __fmul_rn(ld_par(w, pdtype, c, 1.0f), invstd[c]);
+      tab[C + c] = mean[c];
+      tab[2 * C + c] = invstd[c];
+      tab[3 * C + c] = k[c];
+      tab[4 * C + c] = k[C + c];
+    }
+    __syncthreads();
+  }
+  const long long units = sh.P * sh.CV;
+  for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
+       u += (long long)gridDim.x * kBnThreads) {
+    if constexpr (!FIXED) {
+      const int c0 = int(u % sh.CV) * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = c0 + e;
+        ws[e] = tab[c];
+        mc[e] = tab[C + c];
+        is[e] = tab[2 * C + c];
+        k1[e] = tab[3 * C + c];
+        k2[e] = tab[4 * C + c];
+      }
+    }
+    float fg[8], fy[8], fx[8], r[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(dy) + u), fg);
+    if constexpr (ACT) unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
+    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), fx);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
+    reinterpret_cast<uint4*>(dx)[u] = pack8(r);
+  }
+}
+
+// ============================ launchers =====================================
 
 // Warp-per-plane when there are enough planes to fill the GPU with warps,
 // else block-per-plane.
@@ -312,12 +572,170 @@ int elem_grid(long long units, int sms) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-b2_status bn_check(int64_t N, int64_t C, int64_t HW, const void* ws, size_t ws_bytes, const char* who) {
+size_t align16(size_t b) { return (b + 15) & ~size_t(15); }
+
+NhwcShape nhwc_shape(long long N, long long C, long long HW) {
+  NhwcShape s;
+  s.P = N * HW;
+  s.C = int(C);
+  s.CV = int(C / 8);
+  s.rpb = std::max(1, kBnThreads / std::max(1, s.CV));
+  return s;
+}
+
+long long nhwc_blocks(const NhwcShape& s) {
+  // every active thread sums at least ~16 pixels
+  const long long want = (s.P + (long long)s.rpb * 16 - 1) / ((long long)s.rpb * 16);
+  return std::max<long long>(1, std::min<long long>(want, kMaxSumBlocks));
+}
+
+size_t workspace_bytes(long long N, long long C, long long HW, int layout) {
+  if (N <= 0 || C <= 0) return 0;
+  const long long parts = layout == 0 ? N : nhwc_blocks(nhwc_shape(N, C, HW));
+  // two fp32 per (part, channel), then two fp32 per channel
+  return align16(2 * size_t(parts) * size_t(C) * sizeof(float)) + align16(2 * size_t(C) * sizeof(float));
+}
+
+b2_status check_common(int64_t N, int64_t C, int64_t HW, int layout, const void* ws, size_t ws_bytes,
+                       const char* who) {
   if (N < 0 || C < 0 || HW < 0) return set_error(B2_ERR_INVALID, "%s: negative size", who);
-  if (ws_bytes < b2_region_bn_workspace_bytes(N, C) || (N * C > 0 && !ws) || !aligned16(ws))
+  if (layout != 0 && layout != 1) return set_error(B2_ERR_INVALID, "%s: layout must be 0 (NCHW) or 1 (NHWC)", who);
+  if (ws_bytes < workspace_bytes(N, C, HW, layout) || (N * C > 0 && !ws) || !aligned16(ws))
     return set_error(B2_ERR_WORKSPACE, "%s: workspace too small or misaligned", who);
   return B2_OK;
 }
+
+b2_status check_nhwc(int64_t C, std::initializer_list<const void*> ptrs, const char* who) {
+  if (C % 8 != 0 || C > kMaxNhwcChannels)
+    return set_error(B2_ERR_UNSUPPORTED, "%s: channels-last needs C %% 8 == 0 and C <= %lld", who,
+                     (long long)kMaxNhwcChannels);
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return set_error(B2_ERR_UNSUPPORTED, "%s: channels-last needs 16-byte alignment", who);
+  return B2_OK;
+}
+
+int current_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  return sm_count(dev);
+}
+
+b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* y, float* mean_out,
+                     float* invstd_out, long long N, long long C, long long HW, float eps, float slope,
+                     float momentum, void* workspace, cudaStream_t st, const char* who) {
+  const int sms = current_sms();
+  if (layout == 1) {
+    B2_TRY(check_nhwc(C, {x, y}, who));
+    const NhwcShape sh = nhwc_shape(N, C, HW);
+    const long long blocks = nhwc_blocks(sh);
+    float* pa = static_cast<float*>(workspace);
+    float* pb = pa + blocks * C;
+    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+    bn_nhwc_sums_kernel<false, false><<<int(blocks), kBnThreads, red, st>>>(x, nullptr, nullptr, nullptr, nullptr,
+                                                                            sh, 0.0f, 0, pa, pb);
+    B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc sums launch"));
+    bn_nhwc_stats_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(x, pa, pb, blocks, C, sh.P, eps,
+                                                                          momentum, ch, mean_out, invstd_out);
+    B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc stats launch"));
+    if (kBnThreads % sh.CV == 0)
+      bn_nhwc_apply_kernel<true><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out,
+                                                                                      y, sh, slope);
+    else
+      bn_nhwc_apply_kernel<false><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 2 * C * sizeof(float), st>>>(
+          x, ch, mean_out, invstd_out, y, sh, slope);
+    return check_cuda(cudaGetLastError(), "bn nhwc apply launch");
+  }
+  const long long planes = N * C;
+  float* pm = static_cast<float*>(workspace);
+  float* pq = pm + planes;
+  const bool vec = HW % 8 == 0 && aligned16(x) && aligned16(y);
+  const bool warp = warp_per_plane(planes, sms);
+  const int sg = stats_grid(planes, warp, sms);
+  if (warp && vec) bn_plane_stats_kernel<32, true><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
+  else if (warp) bn_plane_stats_kernel<32, false><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
+  else if (vec) bn_plane_stats_kernel<kBnThreads, true><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
+  else bn_plane_stats_kernel<kBnThreads, false><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn stats launch"));
+  bn_channel_stats_kernel<<<int((C + 127) / 128), 128, 0, st>>>(pm, pq, N, C, HW, eps, momentum, ch, mean_out,
+                                                                invstd_out);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn channel launch"));
+  if (vec) {
+    const long long units = planes * (HW / 8);
+    bn_apply_kernel<true><<<elem_grid(units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
+                                                                       HW / 8, C, slope);
+  } else {
+    const long long units = planes * HW;
+    bn_apply_kernel<false><<<elem_grid(units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
+                                                                        HW, C, slope);
+  }
+  return check_cuda(cudaGetLastError(), "bn apply launch");
+}
+
+template <bool ACT>
+b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx, int layout, const void* w,
+                      int pdtype, const float* mean, const float* invstd, uint16_t* dx, void* dw, void* db,
+                      int gdtype, long long N, long long C, long long HW, float slope, int relu, void* workspace,
+                      cudaStream_t st, const char* who) {
+  const int sms = current_sms();
+  const double M = double(N) * double(HW);
+  if (layout == 1) {
+    B2_TRY(check_nhwc(C, {g, yy, xx, dx}, who));
+    const NhwcShape sh = nhwc_shape(N, C, HW);
+    const long long blocks = nhwc_blocks(sh);
+    float* pa = static_cast<float*>(workspace);
+    float* pb = pa + blocks * C;
+    float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(blocks) * C * sizeof(float)));
+    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+    bn_nhwc_sums_kernel<true, ACT><<<int(blocks), kBnThreads, red, st>>>(xx, g, yy, mean, invstd, sh, slope, relu,
+                                                                         pa, pb);
+    B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd sums launch"));
+    bn_bwd_channel_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
+    B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd channel launch"));
+    if (!dx) return B2_OK;
+    if (kBnThreads % sh.CV == 0)
+      bn_nhwc_dx_kernel<ACT, true><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 0, st>>>(
+          g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu);
+    else
+      bn_nhwc_dx_kernel<ACT, false><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 5 * C * sizeof(float), st>>>(
+          g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu);
+    return check_cuda(cudaGetLastError(), "bn nhwc dx launch");
+  }
+  const long long planes = N * C;
+  float* ps = static_cast<float*>(workspace);
+  float* pt = ps + planes;
+  float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(planes) * sizeof(float)));
+  const bool vec = HW % 8 == 0 && aligned16(g) && (!ACT || aligned16(yy)) && aligned16(xx) && (!dx || aligned16(dx));
+  const bool warp = warp_per_plane(planes, sms);
+  const int sg = stats_grid(planes, warp, sms);
+  if (warp && vec)
+    bn_bwd_plane_kernel<32, true, ACT><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope,
+                                                                  relu, ps, pt);
+  else if (warp)
+    bn_bwd_plane_kernel<32, false, ACT><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope,
+                                                                   relu, ps, pt);
+  else if (vec)
+    bn_bwd_plane_kernel<kBnThreads, true, ACT><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW,
+                                                                          slope, relu, ps, pt);
+  else
+    bn_bwd_plane_kernel<kBnThreads, false, ACT><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW,
+                                                                           slope, relu, ps, pt);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn bwd plane launch"));
+  bn_bwd_channel_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(ps, pt, N, C, M, dw, db, gdtype, k);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn bwd channel launch"));
+  if (!dx) return B2_OK;
+  if (vec) {
+    const long long units = planes * (HW / 8);
+    bn_bwd_dx_kernel<true, ACT><<<elem_grid(units, sms), kBnThreads, 0, st>>>(g, yy, xx, w, pdtype, mean, invstd, k,
+                                                                             dx, units, HW / 8, C, slope, relu);
+  } else {
+    const long long units = planes * HW;
+    bn_bwd_dx_kernel<false, ACT><<<elem_grid(units, sms), kBnThreads, 0, st>>>(g, yy, xx, w, pdtype, mean, invstd,
+                                                                              k, dx, units, HW, C, slope, relu);
+  }
+  return check_cuda(cudaGetLastError(), "bn dx launch");
+}
+
+bool valid_pdtype(int dt) { return dt == B2_BF16 || dt == B2_F32; }
 
 }  // namespace
 }  // namespace b2
@@ -326,108 +744,71 @@ using namespace b2;
 
 extern "C" {
 
-size_t b2_region_bn_workspace_bytes(int64_t N, int64_t C) {
-  if (N <= 0 || C <= 0) return 0;
-  // two fp32 per plane, then two fp32 per channel, each array 16-byte aligned
-  const size_t planes = size_t(N) * size_t(C);
-  return ((2 * planes * sizeof(float) + 15) & ~size_t(15)) + ((2 * size_t(C) * sizeof(float) + 15) & ~size_t(15));
+size_t b2_region_bn_workspace_bytes(int64_t N, int64_t C) { return workspace_bytes(N, C, 1, 0); }
+
+size_t b2_batch_norm_workspace_bytes(int64_t N, int64_t C, int64_t HW, int layout) {
+  return workspace_bytes(N, C, HW, layout == 1 ? 1 : 0);
 }
 
 b2_status b2_region_bn_fwd_bf16(const void* x, const void* w, const void* b, void* rm, void* rv,
                                 void* y, float* mean_out, float* invstd_out, int64_t N, int64_t C,
                                 int64_t HW, float eps, float slope, float factor, int update,
                                 void* workspace, size_t workspace_bytes, void* stream) {
-  B2_TRY(bn_check(N, C, HW, workspace, workspace_bytes, "b2_region_bn_fwd_bf16"));
+  const char* who = "b2_region_bn_fwd_bf16";
+  B2_TRY(check_common(N, C, HW, 0, workspace, workspace_bytes, who));
   if (N * C == 0) return B2_OK;
-  if (HW == 0) return set_error(B2_ERR_INVALID, "b2_region_bn_fwd_bf16: empty planes");
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
   if (!x || !y || !mean_out || !invstd_out || (update && (!rm || !rv)))
-    return set_error(B2_ERR_INVALID, "b2_region_bn_fwd_bf16: null pointer");
-  int dev = 0;
-  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  const int sms = sm_count(dev);
-  auto st = static_cast<cudaStream_t>(stream);
-  const long long planes = N * C;
-  float* pm = static_cast<float*>(workspace);
-  float* pq = pm + planes;
-  const bool vec = HW % 8 == 0 && aligned16(x) && aligned16(y);
-  const bool warp = warp_per_plane(planes, sms);
-  const int sg = stats_grid(planes, warp, sms);
-  auto xs = static_cast<const uint16_t*>(x);
-  if (warp && vec) bn_plane_stats_kernel<32, true><<<sg, kBnThreads, 0, st>>>(xs, planes, HW, pm, pq);
-  else if (warp) bn_plane_stats_kernel<32, false><<<sg, kBnThreads, 0, st>>>(xs, planes, HW, pm, pq);
-  else if (vec) bn_plane_stats_kernel<kBnThreads, true><<<sg, kBnThreads, 0, st>>>(xs, planes, HW, pm, pq);
-  else bn_plane_stats_kernel<kBnThreads, false><<<sg, kBnThreads, 0, st>>>(xs, planes, HW, pm, pq);
-  B2_TRY(check_cuda(cudaGetLastError(), "bn stats launch"));
-  bn_channel_stats_kernel<<<int((C + 127) / 128), 128, 0, st>>>(
-      pm, pq, N, C, HW, eps, factor, update, static_cast<uint16_t*>(rm), static_cast<uint16_t*>(rv),
-      mean_out, invstd_out);
-  B2_TRY(check_cuda(cudaGetLastError(), "bn channel launch"));
-  auto wp = static_cast<const uint16_t*>(w);
-  auto bp = static_cast<const uint16_t*>(b);
-  auto yp = static_cast<uint16_t*>(y);
-  if (vec) {
-    const long long units = planes * (HW / 8);
-    bn_apply_kernel<true><<<elem_grid(units, sms), kBnThreads, 0, st>>>(xs, wp, bp, mean_out, invstd_out, yp,
-                                                                       units, HW / 8, C, slope);
-  } else {
-    const long long units = planes * HW;
-    bn_apply_kernel<false><<<elem_grid(units, sms), kBnThreads, 0, st>>>(xs, wp, bp, mean_out, invstd_out, yp,
-                                                                        units, HW, C, slope);
-  }
-  return check_cuda(cudaGetLastError(), "bn apply launch");
+    return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  const BnChan ch{w, b, B2_BF16, update ? rm : nullptr, update ? rv : nullptr, B2_BF16};
+  return bn_forward(static_cast<const uint16_t*>(x), 0, ch, static_cast<uint16_t*>(y), mean_out, invstd_out, N, C,
+                    HW, eps, slope, factor, workspace, static_cast<cudaStream_t>(stream), who);
 }
 
 b2_status b2_region_bn_bwd_bf16(const void* dy, const void* y, const void* x, const void* w,
                                 const float* mean, const float* invstd, void* dx, void* dw, void* db,
                                 int64_t N, int64_t C, int64_t HW, float slope, int relu, void* workspace,
                                 size_t workspace_bytes, void* stream) {
-  B2_TRY(bn_check(N, C, HW, workspace, workspace_bytes, "b2_region_bn_bwd_bf16"));
+  const char* who = "b2_region_bn_bwd_bf16";
+  B2_TRY(check_common(N, C, HW, 0, workspace, workspace_bytes, who));
   if (N * C == 0) return B2_OK;
-  if (HW == 0) return set_error(B2_ERR_INVALID, "b2_region_bn_bwd_bf16: empty planes");
-  if (!dy || !y || !x || !mean || !invstd)
-    return set_error(B2_ERR_INVALID, "b2_region_bn_bwd_bf16: null pointer");
-  int dev = 0;
-  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  const int sms = sm_count(dev);
-  auto st = static_cast<cudaStream_t>(stream);
-  const long long planes = N * C;
-  float* ps = static_cast<float*>(workspace);
-  float* pt = ps + planes;
-  float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                      ((2 * size_t(planes) * sizeof(float) + 15) & ~size_t(15)));
-  const bool vec = HW % 8 == 0 && aligned16(dy) && aligned16(y) && aligned16(x) && (!dx || aligned16(dx));
-  const bool warp = warp_per_plane(planes, sms);
-  const int sg = stats_grid(planes, warp, sms);
-  auto g = static_cast<const uint16_t*>(dy);
-  auto yy = static_cast<const uint16_t*>(y);
-  auto xx = static_cast<const uint16_t*>(x);
-  if (warp && vec)
-    bn_bwd_plane_kernel<32, true><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope, relu, ps, pt);
-  else if (warp)
-    bn_bwd_plane_kernel<32, false><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope, relu, ps, pt);
-  else if (vec)
-    bn_bwd_plane_kernel<kBnThreads, true><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope,
-                                                                     relu, ps, pt);
-  else
-    bn_bwd_plane_kernel<kBnThreads, false><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW, slope,
-                                                                      relu, ps, pt);
-  B2_TRY(check_cuda(cudaGetLastError(), "bn bwd plane launch"));
-  bn_bwd_channel_kernel<<<int((C + 127) / 128), 128, 0, st>>>(ps, pt, N, C, HW, static_cast<uint16_t*>(dw),
-                                                              static_cast<uint16_t*>(db), k);
-  B2_TRY(check_cuda(cudaGetLastError(), "bn bwd channel launch"));
-  if (!dx) return B2_OK;
-  auto wp = static_cast<const uint16_t*>(w);
-  auto out = static_cast<uint16_t*>(dx);
-  if (vec) {
-    const long long units = planes * (HW / 8);
-    bn_bwd_dx_kernel<true><<<elem_grid(units, sms), kBnThreads, 0, st>>>(g, yy, xx, wp, mean, invstd, k, out, units,
-                                                                        HW / 8, C, slope, relu);
-  } else {
-    const long long units = planes * HW;
-    bn_bwd_dx_kernel<false><<<elem_grid(units, sms), kBnThreads, 0, st>>>(g, yy, xx, wp, mean, invstd, k, out, units,
-                                                                         HW, C, slope, relu);
-  }
-  return check_cuda(cudaGetLastError(), "bn dx launch");
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!dy || !y || !x || !mean || !invstd) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  return bn_backward<true>(static_cast<const uint16_t*>(dy), static_cast<const uint16_t*>(y),
+                           static_cast<const uint16_t*>(x), 0, w, B2_BF16, mean, invstd,
+                           static_cast<uint16_t*>(dx), dw, db, B2_BF16, N, C, HW, slope, relu, workspace,
+                           static_cast<cudaStream_t>(stream), who);
+}
+
+b2_status b2_batch_norm_fwd_bf16(const void* x, int layout, const void* w, const void* b, int pdtype, void* rm,
+                                 void* rv, int rdtype, void* y, float* save_mean, float* save_invstd, int64_t N,
+                                 int64_t C, int64_t HW, float momentum, float eps, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_fwd_bf16";
+  B2_TRY(check_common(N, C, HW, layout, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(rdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C == 0) return B2_OK;
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!x || !y || !save_mean || !save_invstd || (!rm) != (!rv))
+    return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  const BnChan ch{w, b, pdtype, rm, rv, rdtype};
+  return bn_forward(static_cast<const uint16_t*>(x), layout, ch, static_cast<uint16_t*>(y), save_mean, save_invstd,
+                    N, C, HW, eps, 1.0f, momentum, workspace, static_cast<cudaStream_t>(stream), who);
+}
+
+b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout, const void* w, int pdtype,
+                                 const float* save_mean, const float* save_invstd, void* dx, void* dw, void* db,
+                                 int gdtype, int64_t N, int64_t C, int64_t HW, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_bwd_bf16";
+  B2_TRY(check_common(N, C, HW, layout, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(gdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C == 0) return B2_OK;
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!dy || !x || !save_mean || !save_invstd) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  return bn_backward<false>(static_cast<const uint16_t*>(dy), nullptr, static_cast<const uint16_t*>(x), layout, w,
+                            pdtype, save_mean, save_invstd, static_cast<uint16_t*>(dx), dw, db, gdtype, N, C, HW,
+                            1.0f, 0, workspace, static_cast<cudaStream_t>(stream), who);
 }
 
 }  // extern "C"

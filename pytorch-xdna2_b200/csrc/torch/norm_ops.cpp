@@ -1,0 +1,144 @@
+// Training-mode BatchNorm with xdna kernels: `native_batch_norm` and
+// `native_batch_norm_backward` (the reference runs ATen's CPU kernels on
+// aliases, torch_xdna_device.cpp:4214-4358).
+//
+// Fast path (b2_batch_norm_*): training mode, bf16 input of rank >= 2 that is
+// contiguous (NCHW order) or 4-D channels-last with C % 8 == 0 and C <= 2048;
+// weight, bias, running statistics absent or bf16 / fp32 xdna vectors of C
+// elements.  save_mean / save_invstd are fp32.  Evaluation mode and every
+// other case run ATen's CUDA kernels on zero-copy CUDA aliases.
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "xdna.h"
+
+namespace xdna {
+namespace {
+
+int vec_dtype(const std::optional<at::Tensor>& t, int64_t C) {
+  if (!t.has_value() || !t->defined()) return B2_BF16;  // absent: any
+  if (t->device().type() != kXdna || !t->is_contiguous() || t->numel() != C) return -1;
+  return t->scalar_type() == at::kBFloat16 ? B2_BF16 : t->scalar_type() == at::kFloat ? B2_F32 : -1;
+}
+
+bool defined(const std::optional<at::Tensor>& t) { return t.has_value() && t->defined(); }
+
+const void* ptr_of(const std::optional<at::Tensor>& t) {
+  if (!defined(t)) return nullptr;
+  materialize(*t);
+  return t->data_ptr();
+}
+
+// 0 = contiguous, 1 = channels-last (4-D), -1 = neither or not supported.
+int bn_layout(const at::Tensor& x) {
+  if (x.dim() == 4 && x.suggest_memory_format() == c10::MemoryFormat::ChannelsLast &&
+      x.is_contiguous(c10::MemoryFormat::ChannelsLast))
+    return (x.size(1) % 8 == 0 && x.size(1) <= 2048) ? 1 : -1;
+  return x.is_contiguous() ? 0 : -1;
+}
+
+std::vector<at::Tensor> as_cuda(const std::vector<std::optional<at::Tensor>>& ts) {
+  std::vector<at::Tensor> out;
+  for (const auto& t : ts) out.push_back(defined(t) ? to_cuda(*t) : at::Tensor());
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> bn_fwd_alias(
+    const at::Tensor& input, const std::optional<at::Tensor>& weight, const std::optional<at::Tensor>& bias,
+    const std::optional<at::Tensor>& rm, const std::optional<at::Tensor>& rv, bool training, double momentum,
+    double eps) {
+  count_fallback("aten::native_batch_norm");
+  c10::cuda::CUDAGuard g(input.device().index());
+  auto c = as_cuda({weight, bias, rm, rv});
+  auto r = at::native_batch_norm(to_cuda(input), c[0], c[1], c[2], c[3], training, momentum, eps);
+  return {adopt(std::get<0>(r)), adopt(std::get<1>(r)), adopt(std::get<2>(r))};
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
+    const at::Tensor& input, const std::optional<at::Tensor>& weight, const std::optional<at::Tensor>& bias,
+    const std::optional<at::Tensor>& running_mean, const std::optional<at::Tensor>& running_var, bool training,
+    double momentum, double eps) {
+  const int64_t C = input.dim() >= 2 ? input.size(1) : 0;
+  const int layout = input.dim() >= 2 ? bn_layout(input) : -1;
+  const int pw = vec_dtype(weight, C), pb = vec_dtype(bias, C);
+  const int rdm = vec_dtype(running_mean, C), rdv = vec_dtype(running_var, C);
+  const bool params_ok = pw >= 0 && pb >= 0 && (!defined(weight) || !defined(bias) || pw == pb);
+  const bool stats_ok = rdm >= 0 && rdv >= 0 && defined(running_mean) == defined(running_var) &&
+                        (!defined(running_mean) || rdm == rdv);
+  if (g_mode.load() == 0 || !training || input.scalar_type() != at::kBFloat16 || layout < 0 || !params_ok ||
+      !stats_ok || input.numel() == 0)
+    return bn_fwd_alias(input, weight, bias, running_mean, running_var, training, momentum, eps);
+  const auto dev = input.device().index();
+  const int64_t N = input.size(0), HW = input.numel() / (N * C);
+  const auto mf = layout == 1 ? c10::MemoryFormat::ChannelsLast : c10::MemoryFormat::Contiguous;
+  at::Tensor out = empty(input.sizes(), at::kBFloat16, dev, mf);
+  at::Tensor stats = empty({2, C}, at::kFloat, dev);
+  at::Tensor save_mean = stats[0], save_invstd = stats[1];
+  const int64_t wsb = int64_t(b2_batch_norm_workspace_bytes(N, C, HW, layout));
+  at::Tensor ws = empty({std::max<int64_t>(wsb, 16)}, at::kByte, dev);
+  materialize(input);
+  const int pdt = defined(weight) ? pw : pb;
+  c10::cuda::CUDAGuard g(dev);
+  XDNA_B2(b2_batch_norm_fwd_bf16(input.data_ptr(), layout, ptr_of(weight), ptr_of(bias), pdt,
+                                 const_cast<void*>(ptr_of(running_mean)), const_cast<void*>(ptr_of(running_var)),
+                                 rdm, out.data_ptr(), save_mean.data_ptr<float>(), save_invstd.data_ptr<float>(), N,
+                                 C, HW, float(momentum), float(eps), ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+  count_launch("batch_norm.fwd", 3);
+  return {out, save_mean, save_invstd};
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
+    const at::Tensor& grad_out, const at::Tensor& input, const std::optional<at::Tensor>& weight,
+    const std::optional<at::Tensor>& running_mean, const std::optional<at::Tensor>& running_var,
+    const std::optional<at::Tensor>& save_mean, const std::optional<at::Tensor>& save_invstd, bool train,
+    double eps, std::array<bool, 3> mask) {
+  const int64_t C = input.dim() >= 2 ? input.size(1) : 0;
+  const int layout = input.dim() >= 2 ? bn_layout(input) : -1;
+  const int pw = vec_dtype(weight, C);
+  auto f32_vec = [&](const std::optional<at::Tensor>& t) {
+    return defined(t) && t->device().type() == kXdna && t->scalar_type() == at::kFloat && t->is_contiguous() &&
+           t->numel() == C;
+  };
+  const bool fast = g_mode.load() != 0 && train && input.scalar_type() == at::kBFloat16 && layout >= 0 && pw >= 0 &&
+                    grad_out.scalar_type() == at::kBFloat16 && grad_out.sizes() == input.sizes() &&
+                    f32_vec(save_mean) && f32_vec(save_invstd) && input.numel() > 0;
+  if (!fast) {
+    count_fallback("aten::native_batch_norm_backward");
+    c10::cuda::CUDAGuard g(input.device().index());
+    auto c = as_cuda({weight, running_mean, running_var, save_mean, save_invstd});
+    auto r = at::native_batch_norm_backward(to_cuda(grad_out), to_cuda(input), c[0], c[1], c[2], c[3], c[4], train,
+                                            eps, mask);
+    return {adopt(std::get<0>(r)), adopt(std::get<1>(r)), adopt(std::get<2>(r))};
+  }
+  const auto dev = input.device().index();
+  const auto mf = layout == 1 ? c10::MemoryFormat::ChannelsLast : c10::MemoryFormat::Contiguous;
+  // the gradient in the input's memory order (a copy only when they differ)
+  at::Tensor g = grad_out.is_contiguous(mf) ? grad_out : grad_out.contiguous(mf);
+  const int64_t N = input.size(0), HW = input.numel() / (N * C);
+  const auto gdt = defined(weight) ? weight->scalar_type() : at::kFloat;
+  at::Tensor gi, gw, gb;
+  if (mask[0]) gi = empty(input.sizes(), at::kBFloat16, dev, mf);
+  if (mask[1]) gw = empty({C}, gdt, dev);
+  if (mask[2]) gb = empty({C}, gdt, dev);
+  const int64_t wsb = int64_t(b2_batch_norm_workspace_bytes(N, C, HW, layout));
+  at::Tensor ws = empty({std::max<int64_t>(wsb, 16)}, at::kByte, dev);
+  materialize(g);
+  materialize(input);
+  c10::cuda::CUDAGuard guard(dev);
+  XDNA_B2(b2_batch_norm_bwd_bf16(g.data_ptr(), input.data_ptr(), layout, ptr_of(weight), pw,
+                                 save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(),
+                                 mask[0] ? gi.data_ptr() : nullptr, mask[1] ? gw.data_ptr() : nullptr,
+                                 mask[2] ? gb.data_ptr() : nullptr, gdt == at::kFloat ? B2_F32 : B2_BF16, N, C, HW,
+                                 ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+  count_launch("batch_norm.bwd", mask[0] ? 3 : 2);
+  return {gi, gw, gb};
+}
+
+}  // namespace
+
+TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
+  m.impl("native_batch_norm", native_batch_norm);
+  m.impl("native_batch_norm_backward", native_batch_norm_backward);
+}
+
+}  // namespace xdna

@@ -60,11 +60,15 @@ SIGNATURES = {
     "b2_upsample_nearest2x": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_upsample_nearest2x_backward": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_region_bn_workspace_bytes": [i64, i64],
+    "b2_batch_norm_workspace_bytes": [i64, i64, i64, i32],
+    "b2_batch_norm_fwd_bf16": [vp, i32, vp, vp, i32, vp, vp, i32, vp, vp, vp, i64, i64, i64, f32, f32, vp, sz, vp],
+    "b2_batch_norm_bwd_bf16": [vp, vp, i32, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
     "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
     "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
 }
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
              "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
+             "b2_batch_norm_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 

@@ -1,0 +1,211 @@
+"""Training-mode BatchNorm on the xdna kernels (native_batch_norm /
+native_batch_norm_backward): the C ABI against the oracle in both memory
+layouts, and the modules against PyTorch on the CPU -- the reference's path
+for these ops (it runs ATen's CPU kernels on aliases, torch_xdna_device.cpp:
+4214-4358) -- with the cases of the reference's own test
+(tests/run_norm_backward.py: every output mask, BatchNorm1d/2d, InstanceNorm,
+bf16 rel-L2 < 0.03, fp32 < 1e-4).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+
+import xdna_train
+from oracle import oracle
+from xdna_train import _abi
+
+pytestmark = pytest.mark.gpu
+
+X = torch.device("xdna")
+
+
+@pytest.fixture(autouse=True)
+def _fresh(cuda):
+    xdna_train.register_xdna_device()
+    xdna_train.set_npu_mode(2)
+    xdna_train.reset_fallback_stats()
+    yield
+
+
+def st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def rel(a, b):
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
+    return ((a - b).norm() / (b.norm() + 1e-9)).item()
+
+
+def launched(kind):
+    return xdna_train.kernel_stats().get(kind, 0)
+
+
+# ---- C ABI vs the oracle --------------------------------------------------------
+
+@pytest.mark.parametrize("shape,layout", [((8, 64, 14, 14), 0), ((8, 64, 14, 14), 1), ((4, 256, 7, 7), 1),
+                                          ((2, 2048, 3, 3), 1), ((3, 24, 5, 7), 1), ((40, 128, 9, 9), 0),
+                                          ((64, 8, 1, 1), 0)])
+@pytest.mark.parametrize("pdtype", [0, 1])
+def test_batch_norm_abi_vs_oracle(cuda, shape, layout, pdtype):
+    N, C, H, W = shape
+    rng = np.random.default_rng(N * C + H)
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * 1.7 + 0.4).bfloat16()
+    dy = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).bfloat16()
+    pt = torch.float32 if pdtype == 1 else torch.bfloat16
+    w = torch.from_numpy(rng.uniform(0.5, 1.5, C).astype(np.float32)).to(pt)
+    b = torch.from_numpy(rng.standard_normal(C).astype(np.float32) * 0.3).to(pt)
+    rm = torch.from_numpy(rng.standard_normal(C).astype(np.float32) * 0.1).to(pt)
+    rv = torch.from_numpy(rng.uniform(0.5, 1.5, C).astype(np.float32)).to(pt)
+    mf = torch.channels_last if layout == 1 else torch.contiguous_format
+    xd, dyd = x.to(cuda).contiguous(memory_format=mf), dy.to(cuda).contiguous(memory_format=mf)
+    wd, bd, rmd, rvd = (t.to(cuda) for t in (w, b, rm, rv))
+    y = torch.empty_like(xd)
+    sm = torch.empty(C, dtype=torch.float32, device=cuda)
+    si = torch.empty_like(sm)
+    nws = _abi.lib().b2_batch_norm_workspace_bytes(N, C, H * W, layout)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=cuda)
+    _abi.call("b2_batch_norm_fwd_bf16", xd.data_ptr(), layout, wd.data_ptr(), bd.data_ptr(), pdtype, rmd.data_ptr(),
+              rvd.data_ptr(), pdtype, y.data_ptr(), sm.data_ptr(), si.data_ptr(), N, C, H * W, ctypes.c_float(0.1),
+              ctypes.c_float(1e-5), ws.data_ptr(), nws, st())
+    dx = torch.empty_like(xd)
+    dw = torch.empty(C, dtype=pt, device=cuda)
+    db = torch.empty_like(dw)
+    _abi.call("b2_batch_norm_bwd_bf16", dyd.data_ptr(), xd.data_ptr(), layout, wd.data_ptr(), pdtype, sm.data_ptr(),
+              si.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), pdtype, N, C, H * W, ws.data_ptr(), nws,
+              st())
+    torch.cuda.synchronize()
+    # oracle: the fused BN + activation with slope 1 (identity), on NCHW bf16 bits
+    wb = bits(w.bfloat16())
+    bb = bits(b.bfloat16())
+    oy, om, oi, orm, orv = oracle.bn_fwd(bits(x), wb if pdtype == 0 else None, None, bits(rm.bfloat16()),
+                                         bits(rv.bfloat16()), 1e-5, 1.0, 0.1, True)
+    np.testing.assert_allclose(sm.cpu().numpy(), om, rtol=0, atol=2e-6 * max(1.0, np.abs(om).max()))
+    np.testing.assert_allclose(si.cpu().numpy(), oi, rtol=2e-6)
+    # y against the same affine transform in fp32 from the GPU's own statistics
+    scale = w.float() * si.cpu()
+    shift = b.float() - sm.cpu() * scale
+    want_y = (x.float() * scale[None, :, None, None] + shift[None, :, None, None]).bfloat16()
+    assert rel(y, want_y) < 4e-3
+    yb = bits(y.contiguous())
+    assert (yb == bits(want_y)).mean() > 0.98
+    # running statistics (bf16 case: the oracle's update exactly, up to one ulp)
+    if pdtype == 0:
+        assert np.abs(bits(rmd).astype(int) - orm.astype(int)).max() <= 1
+        assert np.abs(bits(rvd).astype(int) - orv.astype(int)).max() <= 1
+    else:
+        M = N * H * W
+        torch.testing.assert_close(rmd.cpu(), 0.9 * rm + 0.1 * torch.from_numpy(om), rtol=1e-5, atol=1e-5)
+        var = torch.from_numpy(1.0 / oi.astype(np.float64) ** 2 - 1e-5)
+        torch.testing.assert_close(rvd.cpu().double(), 0.9 * rv.double() + 0.1 * var * M / (M - 1), rtol=1e-4,
+                                   atol=1e-5)
+    # backward from the GPU's statistics; slope 1 makes the oracle's dz = dy
+    odx, odw, odb = oracle.bn_bwd(bits(dy), bits(x), bits(x), wb if pdtype == 0 else bits(w.bfloat16()),
+                                  sm.cpu().numpy(), si.cpu().numpy(), 1.0, False)
+    if pdtype == 1:  # the oracle reads a bf16 weight; redo dx's final scale with the fp32 one
+        odx = None
+    got_dx = dx.contiguous().cpu()
+    if odx is not None:
+        assert rel(got_dx, torch.from_numpy(oracle.bf16_value(odx))) < 4e-3
+    assert rel(dw.float().cpu(), torch.from_numpy(oracle.bf16_value(odw))) < 1e-2
+    assert rel(db.float().cpu(), torch.from_numpy(oracle.bf16_value(odb))) < 1e-2
+
+
+# ---- modules vs the CPU (the reference's path) ------------------------------------
+
+def _grads(make, shape, dtype, dev, input_grad=True, channels_last=False):
+    torch.manual_seed(0)
+    model = make().to(dtype)
+    x = torch.randn(*shape, dtype=dtype)
+    torch.manual_seed(1)
+    w = torch.randn(*shape, dtype=dtype)
+    model, x, w = model.to(dev), x.to(dev), w.to(dev)
+    if channels_last:
+        x = x.contiguous(memory_format=torch.channels_last)
+    if input_grad:
+        x.requires_grad_()
+    y = model(x)
+    (y * w).float().sum().backward()
+    out = {"y": y.detach(), "x": x.grad if input_grad else None}
+    for name, p in model.named_parameters():
+        out[name] = p.grad
+    for name, b in model.named_buffers():
+        if b.is_floating_point():
+            out[name] = b.detach()
+    return out
+
+
+CASES = [
+    ("BatchNorm2d(affine=False)", lambda: nn.BatchNorm2d(4, affine=False), (8, 4, 6, 6), True),
+    ("BatchNorm1d(affine=False)", lambda: nn.BatchNorm1d(4, affine=False), (8, 4), True),
+    ("InstanceNorm2d()", lambda: nn.InstanceNorm2d(4), (8, 4, 6, 6), True),
+    ("InstanceNorm1d()", lambda: nn.InstanceNorm1d(4), (8, 4, 6), True),
+    ("InstanceNorm2d(affine=True)", lambda: nn.InstanceNorm2d(4, affine=True), (8, 4, 6, 6), True),
+    ("BatchNorm2d(no stats, affine=False)", lambda: nn.BatchNorm2d(4, affine=False, track_running_stats=False),
+     (8, 4, 6, 6), True),
+    ("BatchNorm2d(), no input grad", lambda: nn.BatchNorm2d(4), (8, 4, 6, 6), False),
+    ("BatchNorm2d()", lambda: nn.BatchNorm2d(4), (8, 4, 6, 6), True),
+    ("BatchNorm2d(64) large", lambda: nn.BatchNorm2d(64), (16, 64, 28, 28), True),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("name,make,shape,input_grad", CASES)
+def test_norm_modules_vs_cpu(dtype, name, make, shape, input_grad):
+    tol = 0.03 if dtype == torch.bfloat16 else 1e-4
+    ref = _grads(make, shape, dtype, "cpu", input_grad)
+    got = _grads(make, shape, dtype, X, input_grad)
+    for k in ref:
+        assert (got[k] is None) == (ref[k] is None), k
+        if ref[k] is not None:
+            assert rel(got[k], ref[k]) < tol, (k, rel(got[k], ref[k]))
+    if dtype == torch.bfloat16:
+        assert launched("batch_norm.fwd") >= 3 and launched("batch_norm.bwd") >= 2
+        assert "aten::native_batch_norm" not in xdna_train.fallback_stats()
+
+
+@pytest.mark.parametrize("C,hw", [(64, 28), (256, 14), (2048, 7), (24, 9)])
+def test_channels_last_batch_norm_vs_fp32(C, hw):
+    """ResNet-style channels-last BatchNorm2d: errors against an fp32 CPU
+    reference no larger than those of the CPU's own bf16 path (+ a floor)."""
+    make = lambda: nn.BatchNorm2d(C)  # noqa: E731
+    shape = (16, C, hw, hw)
+    ref32 = _grads(make, shape, torch.float32, "cpu")
+    cpu16 = _grads(make, shape, torch.bfloat16, "cpu", channels_last=True)
+    got = _grads(make, shape, torch.bfloat16, X, channels_last=True)
+    assert got["y"].is_contiguous(memory_format=torch.channels_last)
+    for k in ref32:
+        e_got, e_cpu = rel(got[k], ref32[k]), rel(cpu16[k], ref32[k])
+        assert e_got <= 1.5 * e_cpu + 4e-3, (k, e_got, e_cpu)
+    assert launched("batch_norm.fwd") >= 3 and "aten::native_batch_norm" not in xdna_train.fallback_stats()
+
+
+def test_eval_mode_and_mixed_dtypes():
+    torch.manual_seed(3)
+    bn = nn.BatchNorm2d(16)
+    x = torch.randn(4, 16, 5, 5)
+    # bf16 activations with fp32 parameters and statistics (autocast-style model)
+    ref = nn.BatchNorm2d(16)
+    ref.load_state_dict(bn.state_dict())
+    bx = bn.to(X)
+    xb = x.bfloat16().to(X).requires_grad_()
+    y = bx(xb)
+    xr = x.bfloat16().float().requires_grad_()
+    yr = ref(xr)
+    assert rel(y, yr) < 1e-2
+    g = torch.randn(4, 16, 5, 5)
+    (y.float() * g.to(X)).sum().backward()
+    (yr * g).sum().backward()
+    assert rel(bx.weight.grad, ref.weight.grad) < 1e-2 and bx.weight.grad.dtype == torch.float32
+    assert rel(bx.running_var, ref.running_var) < 1e-3
+    assert launched("batch_norm.fwd") >= 3
+    bx.eval()
+    ref.eval()
+    assert rel(bx(x.bfloat16().to(X)), ref(x.bfloat16().float())) < 1e-2
+    assert xdna_train.fallback_stats()["aten::native_batch_norm"]["calls"] == 1
