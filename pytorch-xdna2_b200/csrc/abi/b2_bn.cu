@@ -292,9 +292,11 @@ __global__ void __launch_bounds__(kBnThreads) bn_bwd_plane_kernel(
 
 // Sums of `parts` partial rows (row r at pa[r*C + c]) per channel, in double,
 // in a fixed order: a block covers 32 channels (one per lane, coalesced
-// reads); warp w adds rows w, w+8, w+16, ... in order; the eight warp sums are
-// then added in warp order.  Deterministic and independent of scheduling.
-constexpr int kMergeWarps = 8;
+// reads); warp w adds rows w, w+16, w+32, ... in order, loading eight rows
+// ahead of the additions so the loads overlap; the sixteen warp sums are then
+// added in warp order.  Deterministic and independent of scheduling.
+constexpr int kMergeWarps = 16;
+constexpr int kMergeAhead = 8;
 
 __device__ __forceinline__ bool merge_partials(const float* __restrict__ pa, const float* __restrict__ pb,
                                                long long parts, long long C, double& a, double& b) {
@@ -303,9 +305,21 @@ __device__ __forceinline__ bool merge_partials(const float* __restrict__ pa, con
   const long long c = (long long)blockIdx.x * 32 + lane;
   double sa = 0.0, sb = 0.0;
   if (c < C) {
-    for (long long r = w; r < parts; r += kMergeWarps) {
-      sa += double(pa[r * C + c]);
-      sb += double(pb[r * C + c]);
+    for (long long r0 = w; r0 < parts; r0 += (long long)kMergeWarps * kMergeAhead) {
+      float va[kMergeAhead], vb[kMergeAhead];
+#pragma unroll
+      for (int i = 0; i < kMergeAhead; ++i) {
+        const long long r = r0 + (long long)i * kMergeWarps;
+        va[i] = r < parts ? __ldg(pa + r * C + c) : 0.0f;
+        vb[i] = r < parts ? __ldg(pb + r * C + c) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < kMergeAhead; ++i) {
+        if (r0 + (long long)i * kMergeWarps < parts) {
+          sa += double(va[i]);
+          sb += double(vb[i]);
+        }
+      }
     }
   }
   ra[w][lane] = sa;
@@ -398,15 +412,13 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_sums_kernel(
     } else {
       unpack8(__ldg(reinterpret_cast<const uint4*>(x) + cg), k0);  // shift K: the first pixel
     }
-    const long long step = (long long)gridDim.x * sh.rpb;
-    for (long long p = (long long)blockIdx.x * sh.rpb + pr; p < sh.P; p += step) {
-      const long long u = p * sh.CV + cg;
+    auto accum = [&](const uint4 vx, const uint4 vg, const uint4 vy) {
       float fx[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), fx);
+      unpack8(vx, fx);
       if constexpr (BWD) {
         float fg[8], fy[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(dy) + u), fg);
-        if constexpr (ACT) unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
+        unpack8(vg, fg);
+        if constexpr (ACT) unpack8(vy, fy);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float dz = bn_dz<ACT>(fg[e], ACT ? fy[e] : 0.0f, slope, relu);
@@ -421,6 +433,29 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_sums_kernel(
           b[e] = __fadd_rn(b[e], __fmul_rn(d, d));
         }
       }
+    };
+    const uint4* x4 = reinterpret_cast<const uint4*>(x);
+    const uint4* g4 = reinterpret_cast<const uint4*>(dy);
+    const uint4* y4 = reinterpret_cast<const uint4*>(y);
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    const long long step = (long long)gridDim.x * sh.rpb;
+    long long p = (long long)blockIdx.x * sh.rpb + pr;
+    // four pixels' loads in flight before their additions (in pixel order)
+    for (; p + 3 * step < sh.P; p += 4 * step) {
+      uint4 vx[4], vg[4], vy[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const long long u = (p + i * step) * sh.CV + cg;
+        vx[i] = __ldg(x4 + u);
+        vg[i] = BWD ? __ldg(g4 + u) : zero;
+        vy[i] = ACT ? __ldg(y4 + u) : zero;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) accum(vx[i], vg[i], vy[i]);
+    }
+    for (; p < sh.P; p += step) {
+      const long long u = p * sh.CV + cg;
+      accum(__ldg(x4 + u), BWD ? __ldg(g4 + u) : zero, ACT ? __ldg(y4 + u) : zero);
     }
     float* ra = red + (long long)pr * sh.C + cg * 8;
     float* rb = red + (long long)(sh.rpb + pr) * sh.C + cg * 8;
@@ -481,8 +516,27 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
     __syncthreads();
   }
   const long long units = sh.P * sh.CV;
-  for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
-       u += (long long)gridDim.x * kBnThreads) {
+  const long long stride = (long long)gridDim.x * kBnThreads;
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  uint4* y4 = reinterpret_cast<uint4*>(y);
+  auto one = [&](const uint4 v) {
+    float f[8], r[8];
+    unpack8(v, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
+    return pack8(r);
+  };
+  long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x;
+  if constexpr (FIXED) {  // the channel group is the same for u, u + stride, ...
+    for (; u + 3 * stride < units; u += 4 * stride) {
+      uint4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __ldg(x4 + u + i * stride);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y4[u + i * stride] = one(v[i]);
+    }
+  }
+  for (; u < units; u += stride) {
     if constexpr (!FIXED) {
       const int c0 = int(u % sh.CV) * 8;
 #pragma unroll
@@ -491,11 +545,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
         shift[e] = tab[sh.C + c0 + e];
       }
     }
-    float f[8], r[8];
-    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), f);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
-    reinterpret_cast<uint4*>(y)[u] = pack8(r);
+    y4[u] = one(__ldg(x4 + u));
   }
 }
 
@@ -529,8 +579,37 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_dx_kernel(
     __syncthreads();
   }
   const long long units = sh.P * sh.CV;
-  for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
-       u += (long long)gridDim.x * kBnThreads) {
+  const long long stride = (long long)gridDim.x * kBnThreads;
+  const uint4* g4 = reinterpret_cast<const uint4*>(dy);
+  const uint4* y4 = reinterpret_cast<const uint4*>(y);
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  uint4* d4 = reinterpret_cast<uint4*>(dx);
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  auto one = [&](const uint4 vg, const uint4 vy, const uint4 vx) {
+    float fg[8], fy[8], fx[8], r[8];
+    unpack8(vg, fg);
+    if constexpr (ACT) unpack8(vy, fy);
+    unpack8(vx, fx);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
+    return pack8(r);
+  };
+  long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x;
+  if constexpr (FIXED) {  // the channel group is the same for u, u + stride, ...
+    for (; u + 3 * stride < units; u += 4 * stride) {
+      uint4 vg[4], vy[4], vx[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        vg[i] = __ldg(g4 + u + i * stride);
+        vy[i] = ACT ? __ldg(y4 + u + i * stride) : zero;
+        vx[i] = __ldg(x4 + u + i * stride);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d4[u + i * stride] = one(vg[i], vy[i], vx[i]);
+    }
+  }
+  for (; u < units; u += stride) {
     if constexpr (!FIXED) {
       const int c0 = int(u % sh.CV) * 8;
 #pragma unroll
@@ -543,14 +622,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_dx_kernel(
         k2[e] = tab[4 * C + c];
       }
     }
-    float fg[8], fy[8], fx[8], r[8];
-    unpack8(__ldg(reinterpret_cast<const uint4*>(dy) + u), fg);
-    if constexpr (ACT) unpack8(__ldg(reinterpret_cast<const uint4*>(y) + u), fy);
-    unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), fx);
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
-    reinterpret_cast<uint4*>(dx)[u] = pack8(r);
+    d4[u] = one(__ldg(g4 + u), ACT ? __ldg(y4 + u) : zero, __ldg(x4 + u));
   }
 }
 
