@@ -284,66 +284,72 @@ __global__ void __launch_bounds__(kBnThreads) bn_bwd_plane_kernel(
     s1 = group_sum<TPP>(s1, red);
     s2 = group_sum<TPP>(s2, red);
     if (live && lane == 0) {
-      ps[pl] = s1;
-      pt[pl] = s2;
+      // channel-major partials: row (channel) c holds its N plane sums
+      const long long idx = (pl % C) * (planes / C) + pl / C;
+      ps[idx] = s1;
+      pt[idx] = s2;
     }
   }
 }
 
-// Sums of `parts` partial rows (row r at pa[r*C + c]) per channel, in double,
-// in a fixed order: a block covers 32 channels (one per lane, coalesced
-// reads); warp w adds rows w, w+16, w+32, ... in order, loading eight rows
-// ahead of the additions so the loads overlap; the sixteen warp sums are then
-// added in warp order.  Deterministic and independent of scheduling.
-constexpr int kMergeWarps = 16;
-constexpr int kMergeAhead = 8;
+// Sums of the `parts` partial sums of channel c (channel-major: pa[c*parts +
+// r]) in double, in a fixed order: one block per channel; thread t adds rows
+// t, t+256, t+512, ... in order (their loads issued together, coalesced across
+// the block), then a fixed shuffle / shared-memory tree adds the 256 thread
+// sums.  Deterministic and independent of scheduling.  Returns true in thread 0.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeAhead = 4;
 
 __device__ __forceinline__ bool merge_partials(const float* __restrict__ pa, const float* __restrict__ pb,
-                                               long long parts, long long C, double& a, double& b) {
-  __shared__ double ra[kMergeWarps][32], rb[kMergeWarps][32];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const long long c = (long long)blockIdx.x * 32 + lane;
+                                               long long parts, long long c, double& a, double& b) {
+  __shared__ double ra[kMergeThreads / 32], rb[kMergeThreads / 32];
+  const float* qa = pa + c * parts;
+  const float* qb = pb + c * parts;
   double sa = 0.0, sb = 0.0;
-  if (c < C) {
-    for (long long r0 = w; r0 < parts; r0 += (long long)kMergeWarps * kMergeAhead) {
-      float va[kMergeAhead], vb[kMergeAhead];
+  for (long long r0 = threadIdx.x; r0 < parts; r0 += (long long)kMergeThreads * kMergeAhead) {
+    float va[kMergeAhead], vb[kMergeAhead];
 #pragma unroll
-      for (int i = 0; i < kMergeAhead; ++i) {
-        const long long r = r0 + (long long)i * kMergeWarps;
-        va[i] = r < parts ? __ldg(pa + r * C + c) : 0.0f;
-        vb[i] = r < parts ? __ldg(pb + r * C + c) : 0.0f;
-      }
+    for (int i = 0; i < kMergeAhead; ++i) {
+      const long long r = r0 + (long long)i * kMergeThreads;
+      va[i] = r < parts ? __ldg(qa + r) : 0.0f;
+      vb[i] = r < parts ? __ldg(qb + r) : 0.0f;
+    }
 #pragma unroll
-      for (int i = 0; i < kMergeAhead; ++i) {
-        if (r0 + (long long)i * kMergeWarps < parts) {
-          sa += double(va[i]);
-          sb += double(vb[i]);
-        }
-      }
+    for (int i = 0; i < kMergeAhead; ++i) {
+      sa += double(va[i]);
+      sb += double(vb[i]);
     }
   }
-  ra[w][lane] = sa;
-  rb[w][lane] = sb;
-  __syncthreads();
-  if (w != 0 || c >= C) return false;
-  a = ra[0][lane];
-  b = rb[0][lane];
 #pragma unroll
-  for (int k = 1; k < kMergeWarps; ++k) {
-    a += ra[k][lane];
-    b += rb[k][lane];
+  for (int o = 16; o > 0; o >>= 1) {
+    sa += __shfl_xor_sync(0xffffffffu, sa, o);
+    sb += __shfl_xor_sync(0xffffffffu, sb, o);
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    ra[w] = sa;
+    rb[w] = sb;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return false;
+  a = ra[0];
+  b = rb[0];
+#pragma unroll
+  for (int k = 1; k < kMergeThreads / 32; ++k) {
+    a += ra[k];
+    b += rb[k];
   }
   return true;
 }
 
 // Backward: db, dw (dtype gdtype) and the two means the dx pass needs
 // (k[c] = db/M, k[C + c] = dw/M).  Grid: ceil(C/32) blocks of 256 threads.
-__global__ void __launch_bounds__(kMergeWarps * 32) bn_bwd_channel_kernel(
+__global__ void __launch_bounds__(kMergeThreads) bn_bwd_channel_kernel(
     const float* __restrict__ ps, const float* __restrict__ pt, long long parts, long long C, double M, void* dw,
     void* db, int gdtype, float* __restrict__ k) {
+  const long long c = blockIdx.x;
   double a, bs;
-  if (!merge_partials(ps, pt, parts, C, a, bs)) return;
-  const long long c = (long long)blockIdx.x * 32 + threadIdx.x;
+  if (!merge_partials(ps, pt, parts, c, a, bs)) return;
   if (db) st_par(db, gdtype, c, float(a));
   if (dw) st_par(dw, gdtype, c, float(bs));
   k[c] = float(a / M);
@@ -472,19 +478,19 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_sums_kernel(
       sa = __fadd_rn(sa, red[(long long)r * sh.C + c]);
       sb = __fadd_rn(sb, red[(long long)(sh.rpb + r) * sh.C + c]);
     }
-    part_a[(long long)blockIdx.x * sh.C + c] = sa;
-    part_b[(long long)blockIdx.x * sh.C + c] = sb;
+    part_a[(long long)c * gridDim.x + blockIdx.x] = sa;  // channel-major
+    part_b[(long long)c * gridDim.x + blockIdx.x] = sb;
   }
 }
 
-// Forward merge of the block partials (merge_partials order), statistics out.
-__global__ void __launch_bounds__(kMergeWarps * 32) bn_nhwc_stats_kernel(
+// Forward merge of the block partials (one block per channel), statistics out.
+__global__ void __launch_bounds__(kMergeThreads) bn_nhwc_stats_kernel(
     const uint16_t* __restrict__ x, const float* __restrict__ part_a, const float* __restrict__ part_b,
     long long blocks, long long C, long long P, float eps, float momentum, BnChan ch, float* __restrict__ mean_out,
     float* __restrict__ invstd_out) {
+  const long long c = blockIdx.x;
   double s, q;
-  if (!merge_partials(part_a, part_b, blocks, C, s, q)) return;
-  const long long c = (long long)blockIdx.x * 32 + threadIdx.x;
+  if (!merge_partials(part_a, part_b, blocks, c, s, q)) return;
   const double M = double(P);
   const double shift = double(bf2f(x[c]));
   const double var = fmax(0.0, (q - s * s / M) / M);
@@ -706,7 +712,7 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
     bn_nhwc_sums_kernel<false, false><<<int(blocks), kBnThreads, red, st>>>(x, nullptr, nullptr, nullptr, nullptr,
                                                                             sh, 0.0f, 0, pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc sums launch"));
-    bn_nhwc_stats_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(x, pa, pb, blocks, C, sh.P, eps,
+    bn_nhwc_stats_kernel<<<int(C), kMergeThreads, 0, st>>>(x, pa, pb, blocks, C, sh.P, eps,
                                                                           momentum, ch, mean_out, invstd_out);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc stats launch"));
     if (kBnThreads % sh.CV == 0)
@@ -761,7 +767,7 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
     bn_nhwc_sums_kernel<true, ACT><<<int(blocks), kBnThreads, red, st>>>(xx, g, yy, mean, invstd, sh, slope, relu,
                                                                          pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd sums launch"));
-    bn_bwd_channel_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
+    bn_bwd_channel_kernel<<<int(C), kMergeThreads, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd channel launch"));
     if (!dx) return B2_OK;
     if (kBnThreads % sh.CV == 0)
@@ -792,7 +798,7 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
     bn_bwd_plane_kernel<kBnThreads, false, ACT><<<sg, kBnThreads, 0, st>>>(g, yy, xx, mean, invstd, planes, C, HW,
                                                                            slope, relu, ps, pt);
   B2_TRY(check_cuda(cudaGetLastError(), "bn bwd plane launch"));
-  bn_bwd_channel_kernel<<<int((C + 31) / 32), kMergeWarps * 32, 0, st>>>(ps, pt, N, C, M, dw, db, gdtype, k);
+  bn_bwd_channel_kernel<<<int(C), kMergeThreads, 0, st>>>(ps, pt, N, C, M, dw, db, gdtype, k);
   B2_TRY(check_cuda(cudaGetLastError(), "bn bwd channel launch"));
   if (!dx) return B2_OK;
   if (vec) {
