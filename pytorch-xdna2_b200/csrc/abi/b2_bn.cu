@@ -33,6 +33,8 @@
 // written; the second reads of tensors smaller than L2 hit L2), 12 B/elem with
 // the activation (y read twice too).  NHWC forward: x once for the sums.
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "b2_common.cuh"
 
@@ -643,6 +645,31 @@ int stats_grid(long long planes, bool warp, int sms) {
   return int(std::max<long long>(1, std::min<long long>(groups, (long long)sms * 8)));
 }
 
+// Blocks of `kfn` resident per SM (cached per kernel and shared-memory size).
+int resident_blocks(const void* kfn, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({kfn, smem});
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, kBnThreads, smem) != cudaSuccess || n < 1) {
+    cudaGetLastError();
+    n = 1;
+  }
+  cache[{kfn, smem}] = n;
+  return n;
+}
+
+// Grid-stride kernels: one full wave of resident blocks (no partial last
+// wave), fewer when there is less work.
+template <typename K>
+int wave_grid(K* kfn, size_t smem, long long units, int sms) {
+  const long long want = (units + kBnThreads - 1) / kBnThreads;
+  const long long wave = (long long)sms * resident_blocks(reinterpret_cast<const void*>(kfn), smem);
+  return int(std::max<long long>(1, std::min(want, wave)));
+}
+
 int elem_grid(long long units, int sms) {
   const long long b = (units + kBnThreads - 1) / kBnThreads;
   return int(std::max<long long>(1, std::min<long long>(b, (long long)sms * 16)));
@@ -661,8 +688,15 @@ NhwcShape nhwc_shape(long long N, long long C, long long HW) {
   return s;
 }
 
+// Partial-sum blocks for the NHWC sums kernels: every active thread sums at
+// least ~16 pixels; at most one full wave (`wave`) and kMaxSumBlocks.
+long long nhwc_blocks(const NhwcShape& s, long long wave) {
+  const long long want = (s.P + (long long)s.rpb * 16 - 1) / ((long long)s.rpb * 16);
+  return std::max<long long>(1, std::min<long long>(std::min(want, wave), kMaxSumBlocks));
+}
+
+// Upper bound of nhwc_blocks over all waves (sizes the workspace).
 long long nhwc_blocks(const NhwcShape& s) {
-  // every active thread sums at least ~16 pixels
   const long long want = (s.P + (long long)s.rpb * 16 - 1) / ((long long)s.rpb * 16);
   return std::max<long long>(1, std::min<long long>(want, kMaxSumBlocks));
 }
@@ -705,10 +739,12 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
   if (layout == 1) {
     B2_TRY(check_nhwc(C, {x, y}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
-    const long long blocks = nhwc_blocks(sh);
+    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+    const long long blocks =
+        nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
+                                                              &bn_nhwc_sums_kernel<false, false>), red));
     float* pa = static_cast<float*>(workspace);
     float* pb = pa + blocks * C;
-    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
     bn_nhwc_sums_kernel<false, false><<<int(blocks), kBnThreads, red, st>>>(x, nullptr, nullptr, nullptr, nullptr,
                                                                             sh, 0.0f, 0, pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc sums launch"));
@@ -716,7 +752,7 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
                                                                           momentum, ch, mean_out, invstd_out);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc stats launch"));
     if (kBnThreads % sh.CV == 0)
-      bn_nhwc_apply_kernel<true><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out,
+      bn_nhwc_apply_kernel<true><<<wave_grid(&bn_nhwc_apply_kernel<true>, 0, sh.P * sh.CV, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out,
                                                                                       y, sh, slope);
     else
       bn_nhwc_apply_kernel<false><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 2 * C * sizeof(float), st>>>(
@@ -739,7 +775,7 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
   B2_TRY(check_cuda(cudaGetLastError(), "bn channel launch"));
   if (vec) {
     const long long units = planes * (HW / 8);
-    bn_apply_kernel<true><<<elem_grid(units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
+    bn_apply_kernel<true><<<wave_grid(&bn_apply_kernel<true>, 0, units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
                                                                        HW / 8, C, slope);
   } else {
     const long long units = planes * HW;
@@ -759,11 +795,13 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
   if (layout == 1) {
     B2_TRY(check_nhwc(C, {g, yy, xx, dx}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
-    const long long blocks = nhwc_blocks(sh);
+    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+    const long long blocks =
+        nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
+                                                              &bn_nhwc_sums_kernel<true, ACT>), red));
     float* pa = static_cast<float*>(workspace);
     float* pb = pa + blocks * C;
     float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(blocks) * C * sizeof(float)));
-    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
     bn_nhwc_sums_kernel<true, ACT><<<int(blocks), kBnThreads, red, st>>>(xx, g, yy, mean, invstd, sh, slope, relu,
                                                                          pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd sums launch"));
@@ -771,7 +809,8 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd channel launch"));
     if (!dx) return B2_OK;
     if (kBnThreads % sh.CV == 0)
-      bn_nhwc_dx_kernel<ACT, true><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 0, st>>>(
+      bn_nhwc_dx_kernel<ACT, true><<<wave_grid(&bn_nhwc_dx_kernel<ACT, true>, 0, sh.P * sh.CV, sms), kBnThreads, 0,
+                                                                                              st>>>(
           g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu);
     else
       bn_nhwc_dx_kernel<ACT, false><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 5 * C * sizeof(float), st>>>(
@@ -803,7 +842,7 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
   if (!dx) return B2_OK;
   if (vec) {
     const long long units = planes * (HW / 8);
-    bn_bwd_dx_kernel<true, ACT><<<elem_grid(units, sms), kBnThreads, 0, st>>>(g, yy, xx, w, pdtype, mean, invstd, k,
+    bn_bwd_dx_kernel<true, ACT><<<wave_grid(&bn_bwd_dx_kernel<true, ACT>, 0, units, sms), kBnThreads, 0, st>>>(g, yy, xx, w, pdtype, mean, invstd, k,
                                                                              dx, units, HW / 8, C, slope, relu);
   } else {
     const long long units = planes * HW;

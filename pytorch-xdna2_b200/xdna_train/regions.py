@@ -340,11 +340,12 @@ def fuse_perceptual_loss(loss_module, features_attr: str = "perceptual_vgg") -> 
 # fuse_norm_activation: training BatchNorm2d + ReLU / LeakyReLU as one op
 # ---------------------------------------------------------------------------
 
-#: Inputs smaller than this many bytes keep the eager pair.  The reference
-#: fuses only from 4 MB up (its host kernel loses to eager on small tensors);
-#: on the GPU the fused op saves launches and passes at every size, so the
-#: default is 0.  ``XDNA_REGION_NORM_ACT_MIN_BYTES`` overrides it.
-_NORM_ACT_MIN_BYTES = int(os.environ.get("XDNA_REGION_NORM_ACT_MIN_BYTES", "0"))
+#: Inputs smaller than this many bytes keep the eager pair (the reference's
+#: default, 4 MB).  The eager BatchNorm runs this backend's own kernels too;
+#: below this size the fused op's Python-level autograd node costs more host
+#: time than the activation pass it saves.  ``XDNA_REGION_NORM_ACT_MIN_BYTES``
+#: overrides it.
+_NORM_ACT_MIN_BYTES = int(os.environ.get("XDNA_REGION_NORM_ACT_MIN_BYTES", "4000000"))
 
 
 class _BatchNormAct(torch.autograd.Function):
