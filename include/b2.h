@@ -240,6 +240,65 @@ b2_status b2_region_maxpool2_bwd_bf16(const void* x, const void* g, void* out,
                                       int64_t planes, int64_t H, int64_t W,
                                       void* stream);
 
+/* ---- 1x1 convolutions, stride 1, no padding (the reference runs them on its
+ * CPU path, torch_xdna_device.cpp:4578-4603, 4828-4878) as tcgen05 GEMMs.
+ * layout 0 = contiguous NCHW [B][C][HW], 1 = channels-last NHWC [B*HW][C];
+ * w = [Cout][Cin] bf16; bias bf16 [Cout] or NULL.  Cin, Cout (and HW for
+ * NCHW) multiples of 8; pointers 16-byte aligned.  The weight gradient sums
+ * over all B*HW pixels with split-K fp32 partials (workspace of
+ * b2_conv1x1_wgrad_workspace_bytes bytes, queried with the target device
+ * current) reduced in a fixed order: deterministic; dw dtype B2_BF16 or
+ * B2_F32. */
+b2_status b2_conv1x1_fwd(const void* x, const void* w, const void* bias,
+                         void* y, int layout, int64_t B, int64_t Cin,
+                         int64_t HW, int64_t Cout, void* stream);
+b2_status b2_conv1x1_dgrad(const void* dy, const void* w, void* dx, int layout,
+                           int64_t B, int64_t Cin, int64_t HW, int64_t Cout,
+                           void* stream);
+size_t b2_conv1x1_wgrad_workspace_bytes(int layout, int64_t B, int64_t Cin,
+                                        int64_t HW, int64_t Cout);
+b2_status b2_conv1x1_wgrad(const void* dy, const void* x, void* dw,
+                           int dw_dtype, int layout, int64_t B, int64_t Cin,
+                           int64_t HW, int64_t Cout, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* General GEMM with split-K (deterministic, fixed-order reduction):
+ * D[M][N] (dtype d_dtype, row stride ldd) = op(A) . op(B), operands as in
+ * b2_gemm_bf16 (transA: A stored [K][M]; transB: B stored [N][K]).  Splits fill
+ * one wave of SMs; workspace: b2_gemm_splitk_workspace_bytes (0 when a dense
+ * fp32 D takes the sums directly). */
+size_t b2_gemm_splitk_workspace_bytes(int M, int N, int K, int d_dtype);
+b2_status b2_gemm_splitk_bf16(int transA, int transB, int M, int N, int K,
+                              const void* A, int64_t lda, const void* B,
+                              int64_t ldb, void* D, int d_dtype, int64_t ldd,
+                              void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ---- general convolutions (any kernel size / stride / padding / dilation,
+ * groups 1; the reference's CPU path, torch_xdna_device.cpp:4578-4605,
+ * 4828-4878) as GEMMs over an explicit column matrix:
+ *   col[P][Kp] (P = B*Ho*Wo, column (ky*kw + kx)*C + ci, zero past K = kh*kw*C,
+ *   Kp a multiple of 8 >= K), weights Wk[Cout][Kp] in the same order; the
+ *   input gradient from dcol = dY . Wk (fp32) by a gather over the taps in
+ *   (ky, kx) order (deterministic).  Tensors through element strides (sb, sc,
+ *   sh, sw), so NCHW and channels-last work alike. */
+b2_status b2_im2col_bf16(const void* x, int64_t sb, int64_t sc, int64_t sh,
+                         int64_t sw, int64_t B, int64_t C, int64_t H, int64_t W,
+                         int kh, int kw, int sy, int sx, int py, int px,
+                         int dy, int dx, int64_t Ho, int64_t Wo, int64_t Kp,
+                         void* col, void* stream);
+b2_status b2_col2im_bf16(const float* dcol, int64_t Kp, int64_t B, int64_t C,
+                         int64_t H, int64_t W, int kh, int kw, int sy, int sx,
+                         int py, int px, int dy, int dx, int64_t Ho,
+                         int64_t Wo, void* dx_out, int64_t sb, int64_t sc,
+                         int64_t sh, int64_t sw, void* stream);
+b2_status b2_pack_weight_khwc_bf16(const void* w, int64_t Cout, int64_t Cin,
+                                   int kh, int kw, int64_t Kp, void* wk,
+                                   void* stream);
+b2_status b2_unpack_weight_khwc(const float* dwk, int64_t Cout, int64_t Cin,
+                                int kh, int kw, int64_t Kp, void* dw,
+                                int dtype, void* stream);
+
 /* ---- layout ops (replace the reference's host cat / nearest-2x upsample,
  * torch_xdna_device.cpp:3796-4175; used by the xdna `cat`,
  * `upsample_nearest2d` and `upsample_nearest2d_backward` kernels) ---------- */

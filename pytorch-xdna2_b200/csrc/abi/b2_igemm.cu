@@ -55,8 +55,12 @@ struct Params {
   const void* cin;
   int cin_dtype;
   long long c_sm, c_sn, c_sb;
-  float* partial;                // wgrad partial sums [splits][9][M][N]
+  float* partial;                // wgrad partial sums [splits][9][M][N]; gemm split-K [splits][M][N]
   int* status;
+  // GEMM extensions (1x1 convolutions)
+  int a_bcast;       // A has one batch slice, shared by every batch
+  int kb_per_batch;  // > 0: the reduction runs over the batch slices too (k-block kb is in slice kb / kb_per_batch)
+  int gemm_split;    // 1: tile-space slices are split-K ranges writing fp32 partials
 };
 
 template <int BN>
@@ -89,8 +93,13 @@ __device__ __forceinline__ void decode_tile(int kind, const Params& p, int t, in
     t /= p.tiles_n;
     mt = t % p.tiles_m;
     bz = t / p.tiles_m;
-    kb0 = 0;
-    kb1 = p.num_kb;
+    if (p.gemm_split) {
+      kb0 = bz * p.kb_per_split;
+      kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+    } else {
+      kb0 = 0;
+      kb1 = p.num_kb;
+    }
   }
 }
 
@@ -229,6 +238,24 @@ __device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int co
     if (col0 + c < p.N) base[col0 + c] = cvt1(v[c]);
 }
 
+// split-K GEMM: fp32 partial sums of split `split`, [splits][M][N]
+__device__ __forceinline__ void epi_gemm_partial(const Params& p, int split, int m, int col0,
+                                                 const uint32_t (&r)[32]) {
+  if (m >= p.M) return;
+  float* dst = p.partial + ((long long)split * p.M + m) * p.N;
+  if (col0 + 32 <= p.N && (p.N % 4) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      d4[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                          __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+    return;
+  }
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (col0 + c < p.N) dst[col0 + c] = __uint_as_float(r[c]);
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -315,18 +342,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < BN / 64; ++h)
               tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK + dy * p.wp + dx, 0);
           } else {
+            // slice (z) and k offset of this k-block for A and B
+            int za = bz, zb = bz, k0 = kb * BK;
+            if (p.kb_per_batch > 0) {
+              za = zb = kb / p.kb_per_batch;
+              k0 = (kb - za * p.kb_per_batch) * BK;
+            } else if (p.gemm_split) {
+              za = zb = 0;
+            }
+            if (p.a_bcast) za = 0;
             if constexpr (A_MN) {
-              tma_load_3d(sa, &tma_a, fb, mt * BM, kb * BK, bz);
-              tma_load_3d(sa + 8192, &tma_a, fb, mt * BM + 64, kb * BK, bz);
+              tma_load_3d(sa, &tma_a, fb, mt * BM, k0, za);
+              tma_load_3d(sa + 8192, &tma_a, fb, mt * BM + 64, k0, za);
             } else {
-              tma_load_3d(sa, &tma_a, fb, kb * BK, mt * BM, bz);
+              tma_load_3d(sa, &tma_a, fb, k0, mt * BM, za);
             }
             if constexpr (B_MN) {
 #pragma unroll
               for (int h = 0; h < BN / 64; ++h)
-                tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK, bz);
+                tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, k0, zb);
             } else {
-              tma_load_3d(sb, &tma_b, fb, kb * BK, nt * BN, bz);
+              tma_load_3d(sb, &tma_b, fb, k0, nt * BN, zb);
             }
           }
           if (++stage == STAGES) {
@@ -422,6 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_conv(p, obase, col0, lane, r);
         } else if constexpr (KIND == kWgrad) {
           epi_wgrad(p, bz, tap, mt, col0, row, r);
+        } else if (p.gemm_split) {
+          epi_gemm_partial(p, bz, mt * BM + row, col0, r);
         } else {
           epi_gemm(p, bz, mt, col0, row, lane, r);
         }
@@ -683,6 +721,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
+// D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
+__global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
+                                         void* D, int d_dtype, long long ldd) {
+  const long long total = (long long)M * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += partial[k * total + i];
+    s *= alpha;
+    const long long m = i / N, n = i - m * N;
+    if (d_dtype == B2_F32)
+      static_cast<float*>(D)[m * ldd + n] = s;
+    else
+      static_cast<uint16_t*>(D)[m * ldd + n] = f2bf(s);
+  }
+}
+
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw, int dtype,
                                     int splits, int Cout, int Cin) {
   const long long total = (long long)Cout * Cin * 9;
@@ -731,6 +786,7 @@ b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   return check_cuda(cudaGetLastError(), "igemm launch");
 }
 
+constexpr int kStages64 = 8;
 constexpr int kStages128 = 6;
 constexpr int kStages256 = 4;
 constexpr int kStagesPair = 6;
@@ -857,6 +913,132 @@ WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow
   return w;
 }
 
+// One GEMM call, D[z] = alpha * op(A[z]) * op(B[z]) + beta * C[z] (bf16 in, fp32
+// accumulate), with the extensions the 1x1 convolutions need:
+//   a_bcast    A has a single slice used for every z;
+//   k_batched  the reduction also runs over the `batch` slices of A and B
+//              (one output slice): sum_z op(A[z]) op(B[z]);
+//   partial    split-K: `splits` fp32 partials [splits][M][N] in `partial`,
+//              summed in split order into D (dtype d_dtype, alpha only); also
+//              with one split, for an fp32 D.
+struct GemmCall {
+  int transA = 0, transB = 0, M = 0, N = 0, K = 0;
+  float alpha = 1.f;
+  const void* A = nullptr;
+  int64_t lda = 0, strideA = 0;
+  const void* B = nullptr;
+  int64_t ldb = 0, strideB = 0;
+  float beta = 0.f;
+  const void* C = nullptr;
+  int c_dtype = B2_BF16;
+  int64_t c_sm = 0, c_sn = 0, c_sb = 0;
+  void* D = nullptr;
+  int64_t ldd = 0, strideD = 0;
+  int batch = 1;
+  bool a_bcast = false, k_batched = false;
+  int splits = 1;
+  float* partial = nullptr;
+  int d_dtype = B2_BF16;
+  bool partial_is_d = false;  // one split, fp32 D with ldd == N: the partial is D itself
+};
+
+b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
+  // narrow outputs (1x1 convolutions with 64 channels, stems) take 64-wide
+  // tiles: no MMA or epilogue work on padding columns
+  const int BN = g.N > 128 ? 256 : g.N > 64 ? 128 : 64;
+  const uint64_t bt = uint64_t(g.batch);
+  const uint64_t bta = g.a_bcast ? 1 : bt;
+  CUtensorMap ta, tb;
+  if (!g.transA) {  // A [M][K], K contiguous -> K-major
+    const uint64_t dims[3] = {uint64_t(g.K), uint64_t(g.M), bta};
+    const uint64_t strides[2] = {uint64_t(g.lda) * 2, uint64_t(bta > 1 ? g.strideA : g.lda * g.M) * 2};
+    const uint32_t box[3] = {64, BM, 1};
+    B2_TRY(encode_tmap(&ta, g.A, 3, dims, strides, box, true));
+  } else {  // A stored [K][M], M contiguous -> MN-major
+    const uint64_t dims[3] = {uint64_t(g.M), uint64_t(g.K), bta};
+    const uint64_t strides[2] = {uint64_t(g.lda) * 2, uint64_t(bta > 1 ? g.strideA : g.lda * g.K) * 2};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&ta, g.A, 3, dims, strides, box, true));
+  }
+  if (g.transB) {  // B stored [N][K] -> K-major
+    const uint64_t dims[3] = {uint64_t(g.K), uint64_t(g.N), bt};
+    const uint64_t strides[2] = {uint64_t(g.ldb) * 2, uint64_t(bt > 1 ? g.strideB : g.ldb * g.N) * 2};
+    const uint32_t box[3] = {64, uint32_t(BN), 1};
+    B2_TRY(encode_tmap(&tb, g.B, 3, dims, strides, box, true));
+  } else {  // B [K][N], N contiguous -> MN-major
+    const uint64_t dims[3] = {uint64_t(g.N), uint64_t(g.K), bt};
+    const uint64_t strides[2] = {uint64_t(g.ldb) * 2, uint64_t(bt > 1 ? g.strideB : g.ldb * g.K) * 2};
+    const uint32_t box[3] = {64, 64, 1};
+    B2_TRY(encode_tmap(&tb, g.B, 3, dims, strides, box, true));
+  }
+  Params p{};
+  p.tiles_m = (g.M + BM - 1) / BM;
+  p.tiles_n = (g.N + BN - 1) / BN;
+  const int kb_slice = (g.K + BK - 1) / BK;
+  p.num_kb = g.k_batched ? kb_slice * g.batch : kb_slice;
+  p.kb_per_batch = g.k_batched ? kb_slice : 0;
+  p.a_bcast = g.a_bcast ? 1 : 0;
+  p.splits = 1;
+  if (g.partial) {
+    p.gemm_split = 1;
+    p.kb_per_split = (p.num_kb + std::max(1, g.splits) - 1) / std::max(1, g.splits);
+    p.batch = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;  // tile-space slices = splits
+    p.partial = g.partial;
+  } else {
+    p.kb_per_split = p.num_kb;
+    p.batch = g.k_batched ? 1 : g.batch;
+  }
+  p.M = g.M;
+  p.N = g.N;
+  p.out = g.D;
+  p.osn = g.strideD;
+  p.osh = g.ldd;
+  p.alpha = g.alpha;
+  p.beta = g.beta;
+  p.cin = g.C;
+  p.cin_dtype = g.c_dtype;
+  p.c_sm = g.c_sm;
+  p.c_sn = g.c_sn;
+  p.c_sb = g.c_sb;
+  p.status = device_status_ptr();
+  const int tiles = p.batch * p.tiles_m * p.tiles_n;
+  const bool amn = g.transA != 0, bmn = g.transB == 0;
+  b2_status rc;
+  if (BN == 256) {
+    if (!amn && !bmn) rc = launch<256, kStages256, kGemm, false, false>(ta, tb, p, tiles, st);
+    else if (!amn && bmn) rc = launch<256, kStages256, kGemm, false, true>(ta, tb, p, tiles, st);
+    else if (amn && !bmn) rc = launch<256, kStages256, kGemm, true, false>(ta, tb, p, tiles, st);
+    else rc = launch<256, kStages256, kGemm, true, true>(ta, tb, p, tiles, st);
+  } else if (BN == 128) {
+    if (!amn && !bmn) rc = launch<128, kStages128, kGemm, false, false>(ta, tb, p, tiles, st);
+    else if (!amn && bmn) rc = launch<128, kStages128, kGemm, false, true>(ta, tb, p, tiles, st);
+    else if (amn && !bmn) rc = launch<128, kStages128, kGemm, true, false>(ta, tb, p, tiles, st);
+    else rc = launch<128, kStages128, kGemm, true, true>(ta, tb, p, tiles, st);
+  } else {
+    if (!amn && !bmn) rc = launch<64, kStages64, kGemm, false, false>(ta, tb, p, tiles, st);
+    else if (!amn && bmn) rc = launch<64, kStages64, kGemm, false, true>(ta, tb, p, tiles, st);
+    else if (amn && !bmn) rc = launch<64, kStages64, kGemm, true, false>(ta, tb, p, tiles, st);
+    else rc = launch<64, kStages64, kGemm, true, true>(ta, tb, p, tiles, st);
+  }
+  if (rc != B2_OK || !p.gemm_split || g.partial_is_d) return rc;
+  const long long total = (long long)g.M * g.N;
+  const int threads = 256;
+  const int blocks = int(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads, 148LL * 8)));
+  gemm_split_reduce_kernel<<<blocks, threads, 0, st>>>(g.partial, p.batch, g.M, g.N, g.alpha, g.D, g.d_dtype, g.ldd);
+  return check_cuda(cudaGetLastError(), "gemm split reduce launch");
+}
+
+// Split-K plan for a reduction-heavy GEMM (1x1 wgrad): enough splits for one
+// wave over the SMs, at least 16 k-blocks per split.
+int gemm_splits(int M, int N, long long num_kb, int sms) {
+  const int BN = N > 128 ? 256 : N > 64 ? 128 : 64;
+  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  long long splits = tiles >= sms ? 1 : sms / tiles;
+  splits = std::max<long long>(1, std::min<long long>(splits, num_kb / 16));
+  const long long kps = (num_kb + splits - 1) / splits;
+  return int((num_kb + kps - 1) / kps);
+}
+
 }  // namespace
 }  // namespace b2
 
@@ -965,63 +1147,202 @@ b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
   if (K == 0) return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_bf16: K == 0");
   if (!aligned16(A) || !aligned16(Bm) || lda % 8 || ldb % 8 || (batch > 1 && (strideA % 8 || strideB % 8)))
     return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_bf16: operands need 16-byte aligned rows");
-  const int BN = N > 128 ? 256 : 128;
-  const uint64_t bt = uint64_t(batch);
-  CUtensorMap ta, tb;
-  if (!transA) {  // A [M][K], K contiguous -> K-major
-    const uint64_t dims[3] = {uint64_t(K), uint64_t(M), bt};
-    const uint64_t strides[2] = {uint64_t(lda) * 2, uint64_t(batch > 1 ? strideA : lda * M) * 2};
-    const uint32_t box[3] = {64, BM, 1};
-    B2_TRY(encode_tmap(&ta, A, 3, dims, strides, box, true));
-  } else {  // A stored [K][M], M contiguous -> MN-major
-    const uint64_t dims[3] = {uint64_t(M), uint64_t(K), bt};
-    const uint64_t strides[2] = {uint64_t(lda) * 2, uint64_t(batch > 1 ? strideA : lda * K) * 2};
-    const uint32_t box[3] = {64, 64, 1};
-    B2_TRY(encode_tmap(&ta, A, 3, dims, strides, box, true));
+  GemmCall g;
+  g.transA = transA;
+  g.transB = transB;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.alpha = alpha;
+  g.A = A;
+  g.lda = lda;
+  g.strideA = strideA;
+  g.B = Bm;
+  g.ldb = ldb;
+  g.strideB = strideB;
+  g.beta = beta;
+  g.C = C;
+  g.c_dtype = c_dtype;
+  g.c_sm = c_sm;
+  g.c_sn = c_sn;
+  g.c_sb = c_sb;
+  g.D = D;
+  g.ldd = ldd;
+  g.strideD = strideD;
+  g.batch = batch;
+  return gemm_core(g, st);
+}
+
+// ---- 1x1 convolutions (stride 1, no padding) as GEMMs ----------------------
+// layout 0: NCHW (per image, X[b] is [Cin][HW]); 1: NHWC (X is [B*HW][Cin]).
+// Weights [Cout][Cin] (OIHW with 1x1 kernels), bf16; every row stride must be
+// a multiple of 8 elements (16 bytes) and every pointer 16-byte aligned.
+
+size_t b2_gemm_splitk_workspace_bytes(int M, int N, int K, int d_dtype) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int splits = gemm_splits(M, N, (K + BK - 1) / BK, sm_count(dev));
+  if (splits == 1 && d_dtype == B2_F32) return 0;  // a dense fp32 D takes the sums directly
+  return size_t(splits) * size_t(M) * size_t(N) * sizeof(float);
+}
+
+b2_status b2_gemm_splitk_bf16(int transA, int transB, int M, int N, int K, const void* A, int64_t lda,
+                              const void* Bm, int64_t ldb, void* D, int d_dtype, int64_t ldd, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(B2_ERR_INVALID, "b2_gemm_splitk_bf16: negative size");
+  if (d_dtype != B2_BF16 && d_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_gemm_splitk_bf16: D dtype");
+  if (M == 0 || N == 0) return B2_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!A || !Bm || !D) return set_error(B2_ERR_INVALID, "b2_gemm_splitk_bf16: null pointer");
+  if (!aligned16(A) || !aligned16(Bm) || lda % 8 || ldb % 8)
+    return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_splitk_bf16: operands need 16-byte aligned rows");
+  if (K == 0) {
+    if (ldd != N) return set_error(B2_ERR_UNSUPPORTED, "b2_gemm_splitk_bf16: K == 0 needs a dense D");
+    return check_cuda(cudaMemsetAsync(D, 0, size_t(M) * N * (d_dtype == B2_F32 ? 4 : 2), st), "memset");
   }
-  if (transB) {  // B stored [N][K] -> K-major
-    const uint64_t dims[3] = {uint64_t(K), uint64_t(N), bt};
-    const uint64_t strides[2] = {uint64_t(ldb) * 2, uint64_t(batch > 1 ? strideB : ldb * N) * 2};
-    const uint32_t box[3] = {64, uint32_t(BN), 1};
-    B2_TRY(encode_tmap(&tb, Bm, 3, dims, strides, box, true));
-  } else {  // B [K][N], N contiguous -> MN-major
-    const uint64_t dims[3] = {uint64_t(N), uint64_t(K), bt};
-    const uint64_t strides[2] = {uint64_t(ldb) * 2, uint64_t(batch > 1 ? strideB : ldb * K) * 2};
-    const uint32_t box[3] = {64, 64, 1};
-    B2_TRY(encode_tmap(&tb, Bm, 3, dims, strides, box, true));
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const int splits = gemm_splits(M, N, (K + BK - 1) / BK, sm_count(dev));
+  GemmCall g;
+  g.transA = transA;
+  g.transB = transB;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.A = A;
+  g.lda = lda;
+  g.B = Bm;
+  g.ldb = ldb;
+  g.D = D;
+  g.ldd = ldd;
+  g.d_dtype = d_dtype;
+  g.splits = splits;
+  if (splits == 1 && d_dtype == B2_F32 && ldd == N && aligned16(D)) {
+    g.partial = static_cast<float*>(D);
+    g.partial_is_d = true;
+  } else {
+    const size_t need = size_t(splits) * size_t(M) * size_t(N) * sizeof(float);
+    if (workspace_bytes < need || !workspace || !aligned16(workspace))
+      return set_error(B2_ERR_WORKSPACE, "b2_gemm_splitk_bf16: workspace of %zu bytes needed", need);
+    g.partial = static_cast<float*>(workspace);
   }
-  Params p{};
-  p.tiles_m = (M + BM - 1) / BM;
-  p.tiles_n = (N + BN - 1) / BN;
-  p.splits = 1;
-  p.batch = batch;
-  p.num_kb = (K + BK - 1) / BK;
-  p.kb_per_split = p.num_kb;
-  p.M = M;
-  p.N = N;
-  p.out = D;
-  p.osn = strideD;
-  p.osh = ldd;
-  p.alpha = alpha;
-  p.beta = beta;
-  p.cin = C;
-  p.cin_dtype = c_dtype;
-  p.c_sm = c_sm;
-  p.c_sn = c_sn;
-  p.c_sb = c_sb;
-  p.status = device_status_ptr();
-  const int tiles = batch * p.tiles_m * p.tiles_n;
-  const bool amn = transA != 0, bmn = transB == 0;
-  if (BN == 256) {
-    if (!amn && !bmn) return launch<256, kStages256, kGemm, false, false>(ta, tb, p, tiles, st);
-    if (!amn && bmn) return launch<256, kStages256, kGemm, false, true>(ta, tb, p, tiles, st);
-    if (amn && !bmn) return launch<256, kStages256, kGemm, true, false>(ta, tb, p, tiles, st);
-    return launch<256, kStages256, kGemm, true, true>(ta, tb, p, tiles, st);
+  return gemm_core(g, st);
+}
+
+static b2_status conv1x1_check(const char* who, int layout, int64_t B, int64_t Cin, int64_t HW, int64_t Cout,
+                               std::initializer_list<const void*> ptrs) {
+  if (layout != 0 && layout != 1) return set_error(B2_ERR_INVALID, "%s: layout must be 0 (NCHW) or 1 (NHWC)", who);
+  if (B < 0 || Cin < 0 || HW < 0 || Cout < 0) return set_error(B2_ERR_INVALID, "%s: negative size", who);
+  if (B * HW > INT32_MAX || Cin > INT32_MAX || Cout > INT32_MAX)
+    return set_error(B2_ERR_UNSUPPORTED, "%s: too large", who);
+  for (const void* q : ptrs)
+    if (!q) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return set_error(B2_ERR_UNSUPPORTED, "%s: 16-byte alignment needed", who);
+  if (Cin % 8 || Cout % 8 || (layout == 0 && HW % 8))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: channel counts (and HW for NCHW) must be multiples of 8", who);
+  return B2_OK;
+}
+
+b2_status b2_conv1x1_fwd(const void* x, const void* w, const void* bias, void* y, int layout, int64_t B,
+                         int64_t Cin, int64_t HW, int64_t Cout, void* stream) {
+  B2_TRY(conv1x1_check("b2_conv1x1_fwd", layout, B, Cin, HW, Cout, {x, w, y}));
+  if (B * HW == 0 || Cout == 0) return B2_OK;
+  if (Cin == 0) return set_error(B2_ERR_UNSUPPORTED, "b2_conv1x1_fwd: Cin == 0");
+  GemmCall g;
+  if (layout == 1) {  // Y[P][Cout] = X[P][Cin] . W^T
+    g.transA = 0; g.transB = 1;
+    g.M = int(B * HW); g.N = int(Cout); g.K = int(Cin);
+    g.A = x; g.lda = Cin; g.B = w; g.ldb = Cin;
+    g.D = y; g.ldd = Cout;
+    if (bias) { g.beta = 1.f; g.C = bias; g.c_sm = 0; g.c_sn = 1; }
+  } else {  // Y[b][Cout][HW] = W[Cout][Cin] . X[b][Cin][HW]
+    g.transA = 0; g.transB = 0;
+    g.M = int(Cout); g.N = int(HW); g.K = int(Cin);
+    g.A = w; g.lda = Cin; g.a_bcast = true;
+    g.B = x; g.ldb = HW; g.strideB = Cin * HW;
+    g.D = y; g.ldd = HW; g.strideD = Cout * HW;
+    g.batch = int(B);
+    if (bias) { g.beta = 1.f; g.C = bias; g.c_sm = 1; g.c_sn = 0; }
   }
-  if (!amn && !bmn) return launch<128, kStages128, kGemm, false, false>(ta, tb, p, tiles, st);
-  if (!amn && bmn) return launch<128, kStages128, kGemm, false, true>(ta, tb, p, tiles, st);
-  if (amn && !bmn) return launch<128, kStages128, kGemm, true, false>(ta, tb, p, tiles, st);
-  return launch<128, kStages128, kGemm, true, true>(ta, tb, p, tiles, st);
+  return gemm_core(g, static_cast<cudaStream_t>(stream));
+}
+
+b2_status b2_conv1x1_dgrad(const void* dy, const void* w, void* dx, int layout, int64_t B, int64_t Cin,
+                           int64_t HW, int64_t Cout, void* stream) {
+  B2_TRY(conv1x1_check("b2_conv1x1_dgrad", layout, B, Cin, HW, Cout, {dy, w, dx}));
+  if (B * HW == 0 || Cin == 0) return B2_OK;
+  if (Cout == 0) return set_error(B2_ERR_UNSUPPORTED, "b2_conv1x1_dgrad: Cout == 0");
+  GemmCall g;
+  if (layout == 1) {  // dX[P][Cin] = dY[P][Cout] . W[Cout][Cin]
+    g.transA = 0; g.transB = 0;
+    g.M = int(B * HW); g.N = int(Cin); g.K = int(Cout);
+    g.A = dy; g.lda = Cout; g.B = w; g.ldb = Cin;
+    g.D = dx; g.ldd = Cin;
+  } else {  // dX[b][Cin][HW] = W^T[Cin][Cout] . dY[b][Cout][HW]
+    g.transA = 1; g.transB = 0;
+    g.M = int(Cin); g.N = int(HW); g.K = int(Cout);
+    g.A = w; g.lda = Cin; g.a_bcast = true;
+    g.B = dy; g.ldb = HW; g.strideB = Cout * HW;
+    g.D = dx; g.ldd = HW; g.strideD = Cin * HW;
+    g.batch = int(B);
+  }
+  return gemm_core(g, static_cast<cudaStream_t>(stream));
+}
+
+static int conv1x1_wgrad_splits(int layout, int64_t B, int64_t Cin, int64_t HW, int64_t Cout, int sms) {
+  const long long num_kb = layout == 1 ? (B * HW + BK - 1) / BK : B * ((HW + BK - 1) / BK);
+  return gemm_splits(int(Cout), int(Cin), num_kb, sms);
+}
+
+size_t b2_conv1x1_wgrad_workspace_bytes(int layout, int64_t B, int64_t Cin, int64_t HW, int64_t Cout) {
+  if (B * HW <= 0 || Cin <= 0 || Cout <= 0) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int splits = conv1x1_wgrad_splits(layout, B, Cin, HW, Cout, sm_count(dev));
+  return size_t(splits) * size_t(Cout) * size_t(Cin) * sizeof(float);
+}
+
+b2_status b2_conv1x1_wgrad(const void* dy, const void* x, void* dw, int dw_dtype, int layout, int64_t B,
+                           int64_t Cin, int64_t HW, int64_t Cout, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  B2_TRY(conv1x1_check("b2_conv1x1_wgrad", layout, B, Cin, HW, Cout, {dy, x, dw}));
+  if (dw_dtype != B2_BF16 && dw_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_conv1x1_wgrad: dw dtype");
+  if (Cin == 0 || Cout == 0) return B2_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B * HW == 0) {  // empty reduction: dW = 0
+    const size_t bytes = size_t(Cout) * size_t(Cin) * (dw_dtype == B2_F32 ? 4 : 2);
+    return check_cuda(cudaMemsetAsync(dw, 0, bytes, st), "b2_conv1x1_wgrad: memset");
+  }
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const int splits = conv1x1_wgrad_splits(layout, B, Cin, HW, Cout, sm_count(dev));
+  const size_t need = size_t(splits) * size_t(Cout) * size_t(Cin) * sizeof(float);
+  if (workspace_bytes < need || !workspace || !aligned16(workspace))
+    return set_error(B2_ERR_WORKSPACE, "b2_conv1x1_wgrad: workspace of %zu bytes needed", need);
+  GemmCall g;
+  g.M = int(Cout);
+  g.N = int(Cin);
+  if (layout == 1) {  // dW[Cout][Cin] = dY^T . X over the P pixels
+    g.transA = 1; g.transB = 0;
+    g.K = int(B * HW);
+    g.A = dy; g.lda = Cout; g.B = x; g.ldb = Cin;
+  } else {  // dW = sum_b dY[b][Cout][HW] . X[b]^T
+    g.transA = 0; g.transB = 1;
+    g.K = int(HW);
+    g.A = dy; g.lda = HW; g.strideA = Cout * HW;
+    g.B = x; g.ldb = HW; g.strideB = Cin * HW;
+    g.batch = int(B);
+    g.k_batched = true;
+  }
+  g.D = dw;
+  g.ldd = Cin;
+  g.d_dtype = dw_dtype;
+  // split-K partials (also with one split: dW may be fp32), reduced in order
+  g.splits = splits;
+  g.partial = static_cast<float*>(workspace);
+  return gemm_core(g, st);
 }
 
 }  // extern "C"

@@ -9,6 +9,12 @@
 //   dW        wgrad kernel over the dy rows and the x rows the forward kept,
 //             deferred until the gradient is first read (see deferred.cpp)
 //   dbias     sum of dy over (N, H, W)
+// BF16 1x1 / stride 1 / no padding convolutions (contiguous NCHW or
+// channels-last, channel counts -- and H*W for NCHW -- multiples of 8) run as
+// tcgen05 GEMMs (b2_conv1x1_*): forward and dX one GEMM each, dW a split-K GEMM
+// over all pixels computed with the backward.  Stems and large kernels (few
+// input channels, or >= 5x5; any stride / padding / dilation) run as GEMMs
+// over an explicit column matrix (b2_im2col_*, b2_gemm_splitk_bf16).
 // Outputs follow the input's memory format (NCHW or channels-last), written
 // directly by the kernel epilogue.  Other convolutions (and set_npu_mode(0))
 // take ATen's CUDA convolution on aliases -- the reference sends them to its
@@ -36,6 +42,225 @@ bool is3x3s1p1(const at::Tensor& input, const at::Tensor& weight, at::IntArrayRe
 }
 
 bool bf16(const at::Tensor& t) { return !t.defined() || t.scalar_type() == at::kBFloat16; }
+
+// 1x1 / stride 1 / no padding: the GEMM layout of the input (0 = NCHW,
+// 1 = channels-last), or -1 when the GEMM kernels cannot take it.
+int conv1x1_layout(const at::Tensor& input, const at::Tensor& weight, at::IntArrayRef stride,
+                   at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed, int64_t groups) {
+  if (input.dim() != 4 || weight.dim() != 4 || transposed || groups != 1) return -1;
+  if (weight.size(2) != 1 || weight.size(3) != 1 || input.size(1) != weight.size(1)) return -1;
+  auto all = [](at::IntArrayRef v, int64_t x) {
+    for (auto e : v)
+      if (e != x) return false;
+    return v.size() == 2;
+  };
+  if (!all(stride, 1) || !all(padding, 0) || !all(dilation, 1)) return -1;
+  const int64_t Cin = input.size(1), Cout = weight.size(0), HW = input.size(2) * input.size(3);
+  if (Cin % 8 || Cout % 8 || input.numel() == 0) return -1;
+  auto aligned = [](const at::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0; };
+  if (!aligned(input)) return -1;
+  if (input.suggest_memory_format() == at::MemoryFormat::ChannelsLast &&
+      input.is_contiguous(at::MemoryFormat::ChannelsLast))
+    return 1;
+  if (input.is_contiguous() && HW % 8 == 0) return 0;
+  return -1;
+}
+
+// ---- general convolutions as GEMMs over a column matrix (b2_im2col_*) -------
+// Taken for the convolutions ATen's library kernels handle worst and an
+// explicit column matrix handles well: few input channels (stems: 7x7 3->64,
+// 9x9 3->32) or large kernels (>= 5x5).  Groups 1, bf16, Cout % 8 == 0, and a
+// column matrix of at most 4 GiB.
+struct GeneralConv {
+  int64_t B, Cin, H, W, Cout, Ho, Wo, P, K, Kp;
+  int kh, kw, sy, sx, py, px, dy, dx;
+};
+
+bool general_conv(const at::Tensor& input, const at::Tensor& weight, at::IntArrayRef stride, at::IntArrayRef padding,
+                  at::IntArrayRef dilation, bool transposed, int64_t groups, GeneralConv& g) {
+  if (input.dim() != 4 || weight.dim() != 4 || transposed || groups != 1 || input.numel() == 0) return false;
+  if (stride.size() != 2 || padding.size() != 2 || dilation.size() != 2 || input.size(1) != weight.size(1))
+    return false;
+  g.B = input.size(0);
+  g.Cin = input.size(1);
+  g.H = input.size(2);
+  g.W = input.size(3);
+  g.Cout = weight.size(0);
+  g.kh = int(weight.size(2));
+  g.kw = int(weight.size(3));
+  g.sy = int(stride[0]);
+  g.sx = int(stride[1]);
+  g.py = int(padding[0]);
+  g.px = int(padding[1]);
+  g.dy = int(dilation[0]);
+  g.dx = int(dilation[1]);
+  if (g.Cout % 8 || g.sy < 1 || g.sx < 1 || g.dy < 1 || g.dx < 1) return false;
+  if (!(g.Cin <= 16 || int64_t(g.kh) * g.kw >= 25)) return false;
+  g.Ho = (g.H + 2 * g.py - int64_t(g.dy) * (g.kh - 1) - 1) / g.sy + 1;
+  g.Wo = (g.W + 2 * g.px - int64_t(g.dx) * (g.kw - 1) - 1) / g.sx + 1;
+  if (g.Ho <= 0 || g.Wo <= 0) return false;
+  g.P = g.B * g.Ho * g.Wo;
+  g.K = int64_t(g.kh) * g.kw * g.Cin;
+  g.Kp = (g.K + 7) / 8 * 8;
+  return g.P * g.Kp * 2 <= (int64_t(4) << 30) && g.P < INT32_MAX;
+}
+
+at::Tensor im2col(const at::Tensor& x, const GeneralConv& g) {
+  const auto dev = x.device().index();
+  at::Tensor col = empty({g.P, g.Kp}, at::kBFloat16, dev);
+  materialize(x);
+  XDNA_B2(b2_im2col_bf16(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), x.stride(3), g.B, g.Cin, g.H, g.W, g.kh,
+                         g.kw, g.sy, g.sx, g.py, g.px, g.dy, g.dx, g.Ho, g.Wo, g.Kp, col.data_ptr(), stream(dev)));
+  count_launch("im2col");
+  return col;
+}
+
+at::Tensor pack_weight_khwc(const at::Tensor& weight, const GeneralConv& g) {
+  at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+  materialize(w);
+  at::Tensor wk = empty({g.Cout, g.Kp}, at::kBFloat16, w.device().index());
+  XDNA_B2(b2_pack_weight_khwc_bf16(w.data_ptr(), g.Cout, g.Cin, g.kh, g.kw, g.Kp, wk.data_ptr(),
+                                   stream(w.device().index())));
+  count_launch("pack_weight_khwc");
+  return wk;
+}
+
+// op(A) . op(B) with split-K into a new fp32 [M][N] tensor.
+at::Tensor gemm_splitk_f32(int transA, int transB, int64_t M, int64_t N, int64_t K, const at::Tensor& A, int64_t lda,
+                           const at::Tensor& B, int64_t ldb, c10::DeviceIndex dev) {
+  at::Tensor d = empty({M, N}, at::kFloat, dev);
+  const size_t wsb = b2_gemm_splitk_workspace_bytes(int(M), int(N), int(K), B2_F32);
+  at::Tensor ws = empty({int64_t((wsb + 15) / 16) * 4 + 4}, at::kFloat, dev);
+  XDNA_B2(b2_gemm_splitk_bf16(transA, transB, int(M), int(N), int(K), A.data_ptr(), lda, B.data_ptr(), ldb,
+                              d.data_ptr(), B2_F32, N, ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
+  count_launch("gemm_splitk", 2);
+  return d;
+}
+
+at::Tensor general_forward(const at::Tensor& input, const at::Tensor& weight, const at::Tensor& bias,
+                           const GeneralConv& g) {
+  const auto dev = input.device().index();
+  c10::cuda::CUDAGuard guard(dev);
+  at::Tensor col = im2col(input, g);
+  at::Tensor wk = pack_weight_khwc(weight, g);
+  at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
+  if (b.defined()) materialize(b);
+  const bool cl = input.suggest_memory_format() == at::MemoryFormat::ChannelsLast;
+  // Y as [P][Cout] (channels-last); NCHW callers get a transposed copy
+  at::Tensor y = empty({g.B, g.Cout, g.Ho, g.Wo}, at::kBFloat16, dev, at::MemoryFormat::ChannelsLast);
+  XDNA_B2(b2_gemm_bf16(0, 1, int(g.P), int(g.Cout), int(g.Kp), 1.f, col.data_ptr(), g.Kp, 0, wk.data_ptr(), g.Kp, 0,
+                       b.defined() ? 1.f : 0.f, b.defined() ? b.data_ptr() : nullptr, B2_BF16, 0, 1, 0, y.data_ptr(),
+                       g.Cout, 0, 1, stream(dev)));
+  count_launch("conv.gemm");
+  if (cl) return y;
+  at::Tensor yn = empty({g.B, g.Cout, g.Ho, g.Wo}, at::kBFloat16, dev);
+  XDNA_B2(b2_nhwc_to_nchw_bf16(y.data_ptr(), yn.data_ptr(), int(g.B), int(g.Cout), int(g.Ho * g.Wo), stream(dev)));
+  count_launch("nhwc_to_nchw");
+  return yn;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> general_backward(const at::Tensor& grad_output, const at::Tensor& input,
+                                                                const at::Tensor& weight, const GeneralConv& g,
+                                                                std::array<bool, 3> mask) {
+  const auto dev = input.device().index();
+  c10::cuda::CUDAGuard guard(dev);
+  // dY as [P][Cout]
+  at::Tensor dy;
+  if (grad_output.suggest_memory_format() == at::MemoryFormat::ChannelsLast &&
+      grad_output.is_contiguous(at::MemoryFormat::ChannelsLast)) {
+    dy = grad_output;
+    materialize(dy);
+  } else {
+    at::Tensor gc = grad_output.is_contiguous() ? grad_output : grad_output.contiguous();
+    materialize(gc);
+    dy = empty({g.B, g.Cout, g.Ho, g.Wo}, at::kBFloat16, dev, at::MemoryFormat::ChannelsLast);
+    XDNA_B2(b2_nchw_to_nhwc_bf16(gc.data_ptr(), dy.data_ptr(), int(g.B), int(g.Cout), int(g.Ho * g.Wo), stream(dev)));
+    count_launch("nchw_to_nhwc");
+  }
+  at::Tensor dx, dw, db;
+  if (mask[0]) {
+    at::Tensor wk = pack_weight_khwc(weight, g);
+    // dcol[P][Kp] = dY[P][Cout] . Wk[Cout][Kp]
+    at::Tensor dcol = gemm_splitk_f32(0, 0, g.P, g.Kp, g.Cout, dy, g.Cout, wk, g.Kp, dev);
+    const auto mf = input.suggest_memory_format() == at::MemoryFormat::ChannelsLast ? at::MemoryFormat::ChannelsLast
+                                                                                     : at::MemoryFormat::Contiguous;
+    dx = empty({g.B, g.Cin, g.H, g.W}, at::kBFloat16, dev, mf);
+    XDNA_B2(b2_col2im_bf16(dcol.data_ptr<float>(), g.Kp, g.B, g.Cin, g.H, g.W, g.kh, g.kw, g.sy, g.sx, g.py, g.px,
+                           g.dy, g.dx, g.Ho, g.Wo, dx.data_ptr(), dx.stride(0), dx.stride(1), dx.stride(2),
+                           dx.stride(3), stream(dev)));
+    count_launch("col2im");
+  }
+  if (mask[1]) {
+    at::Tensor col = im2col(input, g);
+    // dWk[Cout][Kp] = dY^T . col over the P pixels
+    at::Tensor dwk = gemm_splitk_f32(1, 0, g.Cout, g.Kp, g.P, dy, g.Cout, col, g.Kp, dev);
+    dw = empty({g.Cout, g.Cin, g.kh, g.kw}, weight.scalar_type(), dev);
+    XDNA_B2(b2_unpack_weight_khwc(dwk.data_ptr<float>(), g.Cout, g.Cin, g.kh, g.kw, g.Kp, dw.data_ptr(),
+                                  weight.scalar_type() == at::kFloat ? B2_F32 : B2_BF16, stream(dev)));
+    count_launch("unpack_weight_khwc");
+  }
+  if (mask[2]) {
+    count_fallback("conv.dbias");
+    db = adopt(to_cuda(dy).sum(at::IntArrayRef{0, 2, 3}).to(grad_output.scalar_type()));
+  }
+  return {dx, dw, db};
+}
+
+at::Tensor contiguous_as(const at::Tensor& t, int layout) {
+  const auto mf = layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous;
+  return t.is_contiguous(mf) ? t : t.contiguous(mf);
+}
+
+at::Tensor conv1x1_forward(const at::Tensor& input, const at::Tensor& weight, const at::Tensor& bias, int layout) {
+  const c10::DeviceIndex dev = input.device().index();
+  c10::cuda::CUDAGuard g(dev);
+  const int64_t B = input.size(0), Cin = input.size(1), H = input.size(2), W = input.size(3), Cout = weight.size(0);
+  at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+  at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
+  materialize(input);
+  materialize(w);
+  if (b.defined()) materialize(b);
+  const auto mf = layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous;
+  at::Tensor y = empty({B, Cout, H, W}, at::kBFloat16, dev, mf);
+  XDNA_B2(b2_conv1x1_fwd(input.data_ptr(), w.data_ptr(), b.defined() ? b.data_ptr() : nullptr, y.data_ptr(), layout, B,
+                         Cin, H * W, Cout, stream(dev)));
+  count_launch("conv1x1.fwd");
+  return y;
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> conv1x1_backward(const at::Tensor& grad_output,
+                                                                const at::Tensor& input, const at::Tensor& weight,
+                                                                int layout, std::array<bool, 3> mask) {
+  const c10::DeviceIndex dev = input.device().index();
+  c10::cuda::CUDAGuard g(dev);
+  const int64_t B = input.size(0), Cin = input.size(1), H = input.size(2), W = input.size(3), Cout = weight.size(0);
+  at::Tensor dy = contiguous_as(grad_output, layout);
+  materialize(dy);
+  materialize(input);
+  at::Tensor dx, dw, db;
+  if (mask[0]) {
+    at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+    materialize(w);
+    dx = empty({B, Cin, H, W}, at::kBFloat16, dev,
+               layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous);
+    XDNA_B2(b2_conv1x1_dgrad(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), layout, B, Cin, H * W, Cout, stream(dev)));
+    count_launch("conv1x1.dgrad");
+  }
+  if (mask[1]) {
+    dw = empty({Cout, Cin, 1, 1}, weight.scalar_type(), dev);
+    const size_t ws_bytes = b2_conv1x1_wgrad_workspace_bytes(layout, B, Cin, H * W, Cout);
+    at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4 + 4}, at::kFloat, dev);
+    XDNA_B2(b2_conv1x1_wgrad(dy.data_ptr(), input.data_ptr(), dw.data_ptr(),
+                             weight.scalar_type() == at::kFloat ? B2_F32 : B2_BF16, layout, B, Cin, H * W, Cout,
+                             ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
+    count_launch("conv1x1.wgrad", 2);  // split-K GEMM + ordered reduce
+  }
+  if (mask[2]) {
+    count_fallback("conv1x1.dbias");
+    db = adopt(to_cuda(dy).sum(at::IntArrayRef{0, 2, 3}).to(grad_output.scalar_type()));
+  }
+  return {dx, dw, db};
+}
 
 at::MemoryFormat out_format(const at::Tensor& input) {
   return input.suggest_memory_format() == at::MemoryFormat::ChannelsLast ? at::MemoryFormat::ChannelsLast
@@ -82,6 +307,25 @@ void launch_wgrad(const at::Tensor& dy_rows, const at::Tensor& x_rows, void* gw,
   count_launch("conv3x3.wgrad", 2);  // igemm + split-K reduce
 }
 
+bool env_flag(const char* name, bool dflt) {
+  const char* s = std::getenv(name);
+  return s ? std::string(s) != "0" : dflt;
+}
+
+}  // namespace
+
+// Routing of the convolutions outside the 3x3 fast path (set_conv_paths).
+// Both off by default: measured on ResNet-50 (channels-last, batch 128) ATen's
+// library kernels are faster for its 1x1 convolutions and its 7x7 stem, and
+// equal on the style network's 9x9 layers.
+std::atomic<bool> g_conv1x1{env_flag("XDNA_CONV1X1", false)};
+std::atomic<bool> g_conv_general{env_flag("XDNA_CONV_GENERAL", false)};
+
+namespace {
+
+bool conv1x1_enabled() { return g_conv1x1.load(); }
+bool general_enabled() { return g_conv_general.load(); }
+
 bool deferral_enabled() {
   static const bool on = [] {
     const char* s = std::getenv("XDNA_DEFER_DW");
@@ -95,6 +339,15 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
                                     at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed,
                                     at::IntArrayRef output_padding, int64_t groups) {
   const at::Tensor bias = bias_opt.has_value() ? *bias_opt : at::Tensor();
+  if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(bias)) {
+    const int l1 =
+        conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
+    if (l1 >= 0) return conv1x1_forward(input, weight, bias, l1);
+    GeneralConv gc;
+    if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
+        general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
+      return general_forward(input, weight, bias, gc);
+  }
   const bool fast = g_mode.load() > 0 && is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
                     bf16(input) && bf16(weight) && bf16(bias) && input.numel() > 0;
   if (!fast) {
@@ -124,6 +377,15 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight, at::IntArrayRef stride,
     at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed, at::IntArrayRef output_padding, int64_t groups,
     std::array<bool, 3> output_mask) {
+  if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(grad_output)) {
+    const int l1 =
+        conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
+    if (l1 >= 0) return conv1x1_backward(grad_output, input, weight, l1, output_mask);
+    GeneralConv gc;
+    if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
+        general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
+      return general_backward(grad_output, input, weight, gc, output_mask);
+  }
   const bool fast = g_mode.load() > 0 && is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
                     bf16(input) && bf16(weight) && bf16(grad_output) && input.numel() > 0;
   c10::cuda::CUDAGuard g(input.device().index());

@@ -325,6 +325,11 @@ PYBIND11_MODULE(_C, m) {
   m.def("region_addtap", &region_addtap);
   m.def("region_relu_bwd", &region_relu_bwd);
   m.def("region_maxpool2_bwd", &region_maxpool2_bwd);
+  m.def("set_conv_paths", [](std::optional<bool> conv1x1, std::optional<bool> general) {
+    if (conv1x1) xdna::g_conv1x1.store(*conv1x1);
+    if (general) xdna::g_conv_general.store(*general);
+    return py::make_tuple(xdna::g_conv1x1.load(), xdna::g_conv_general.load());
+  }, py::arg("conv1x1") = py::none(), py::arg("general") = py::none());
   m.def("region_bn_fwd", &region_bn_fwd);
   m.def("region_bn_bwd", &region_bn_bwd);
   m.def("region_bn_forward", &region_bn_forward);

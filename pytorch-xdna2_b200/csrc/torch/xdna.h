@@ -83,6 +83,10 @@ at::Tensor find_rows(const at::Tensor& input);
 // 2: all hot-path kernels; 1: weight gradients through the CUDA-alias path;
 // 0: every hot op through the CUDA-alias path (A/B switch, set_npu_mode).
 extern std::atomic<int> g_mode;
+// Convolutions outside the 3x3 fast path: 1x1 GEMMs / column-matrix GEMMs
+// (conv_ops.cpp); off sends them to ATen's CUDA kernels.
+extern std::atomic<bool> g_conv1x1;
+extern std::atomic<bool> g_conv_general;
 void count_launch(const char* what, int64_t n = 1);
 void count_fallback(const std::string& op);
 std::map<std::string, int64_t> launch_stats();

@@ -26,6 +26,7 @@ from .device import (
     reset_fallback_stats,
     reset_mapped_cpu_stats,
     set_npu_mode,
+    set_conv_paths,
     synchronize,
     try_register_xdna_device,
     wait_for_builds,
@@ -46,6 +47,7 @@ __all__ = [
     "async_dw_stats",
     "autotune_result",
     "set_npu_mode",
+    "set_conv_paths",
     "npu_mode",
     "wait_for_builds",
     "reset_fallback_stats",

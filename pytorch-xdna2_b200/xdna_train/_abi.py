@@ -56,6 +56,18 @@ SIGNATURES = {
     "b2_region_addtap_bf16": [vp, vp, vp, vp, i64, f32, vp],
     "b2_region_relu_bwd_bf16": [vp, vp, vp, vp, vp, i64, f32, vp],
     "b2_region_maxpool2_bwd_bf16": [vp, vp, vp, i64, i64, i64, vp],
+    "b2_conv1x1_fwd": [vp, vp, vp, vp, i32, i64, i64, i64, i64, vp],
+    "b2_conv1x1_dgrad": [vp, vp, vp, i32, i64, i64, i64, i64, vp],
+    "b2_conv1x1_wgrad_workspace_bytes": [i32, i64, i64, i64, i64],
+    "b2_conv1x1_wgrad": [vp, vp, vp, i32, i32, i64, i64, i64, i64, vp, sz, vp],
+    "b2_gemm_splitk_workspace_bytes": [i32, i32, i32, i32],
+    "b2_gemm_splitk_bf16": [i32, i32, i32, i32, i32, vp, i64, vp, i64, vp, i32, i64, vp, sz, vp],
+    "b2_im2col_bf16": [vp, i64, i64, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32, i32, i64, i64,
+                       i64, vp, vp],
+    "b2_col2im_bf16": [vp, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32, i32, i64, i64, vp, i64, i64,
+                       i64, i64, vp],
+    "b2_pack_weight_khwc_bf16": [vp, i64, i64, i32, i32, i64, vp, vp],
+    "b2_unpack_weight_khwc": [vp, i64, i64, i32, i32, i64, vp, i32, vp],
     "b2_cat_blocks": [vp, vp, i32, vp, i64, i64, vp],
     "b2_upsample_nearest2x": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_upsample_nearest2x_backward": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
@@ -68,6 +80,7 @@ SIGNATURES = {
 }
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
              "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
+             "b2_conv1x1_wgrad_workspace_bytes": sz, "b2_gemm_splitk_workspace_bytes": sz,
              "b2_batch_norm_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 

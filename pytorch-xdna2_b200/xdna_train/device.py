@@ -327,6 +327,20 @@ def npu_mode() -> int:
     return int(_C.npu_mode())
 
 
+def set_conv_paths(conv1x1=None, general=None):
+    """Route the convolutions outside the 3x3 fast path (no counterpart in the
+    reference, whose other convolutions all run on its CPU path):
+    ``conv1x1`` -- 1x1 / stride 1 convolutions as tcgen05 GEMMs;
+    ``general`` -- stems and large kernels as GEMMs over a column matrix.
+    Both default off: on ResNet-50 (channels-last, batch 128) ATen's library
+    kernels are faster for these layers today, and equal on the style
+    network's 9x9 layers.  ``None`` leaves a setting as it is.  Returns the
+    settings (also ``XDNA_CONV1X1`` / ``XDNA_CONV_GENERAL`` = 0/1 at
+    start-up)."""
+    register_xdna_device()
+    return tuple(bool(v) for v in _C.set_conv_paths(conv1x1, general))
+
+
 def wait_for_builds(timeout: float | None = None) -> bool:
     """Kernels are compiled ahead of time; nothing to wait for."""
     del timeout

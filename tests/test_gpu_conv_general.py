@@ -1,0 +1,136 @@
+"""General convolutions (stems and large kernels, any stride / padding /
+dilation) as GEMMs over an explicit column matrix: im2col against a plain
+PyTorch gather, and nn.Conv2d on the xdna device against an fp32 reference of
+the reference's CPU path (the same convolution on the CPU), forward, input and
+weight gradients, NCHW and channels-last.  Tolerance
+max|err| <= 2e-2 * max|ref| (fp32 accumulation, one bf16 rounding; the input
+gradient adds the taps of an fp32 column gradient before its one rounding).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import xdna_train
+from xdna_train import _abi
+
+pytestmark = pytest.mark.gpu
+
+X = torch.device("xdna")
+
+
+def st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def close(got, ref, tol=2e-2, l2=1e-2):
+    got, ref = got.detach().float().cpu(), ref.detach().float().cpu()
+    scale = ref.abs().max().item()
+    err = (got - ref).abs().max().item()
+    assert err <= tol * scale + 1e-6, f"max abs err {err} vs scale {scale}"
+    rel = ((got - ref).norm() / ref.norm().clamp_min(1e-12)).item()
+    assert rel <= l2, f"rel-L2 {rel}"
+
+
+def col_reference(x, kh, kw, s, p, d):
+    """[P][K] columns in (ky, kx, ci) order from a padded NCHW input."""
+    B, C, H, W = x.shape
+    xp = F.pad(x, (p, p, p, p))
+    Ho = (H + 2 * p - d * (kh - 1) - 1) // s + 1
+    Wo = (W + 2 * p - d * (kw - 1) - 1) // s + 1
+    cols = []
+    for ky in range(kh):
+        for kx in range(kw):
+            patch = xp[:, :, ky * d: ky * d + s * (Ho - 1) + 1: s, kx * d: kx * d + s * (Wo - 1) + 1: s]
+            cols.append(patch.permute(0, 2, 3, 1).reshape(B * Ho * Wo, C))
+    return torch.cat(cols, 1), Ho, Wo
+
+
+@pytest.mark.parametrize("shape,k,s,p,d,cl", [((2, 3, 11, 13), 7, 2, 3, 1, False), ((2, 16, 9, 9), 3, 1, 2, 2, True),
+                                              ((1, 5, 6, 7), 5, 3, 1, 1, True)])
+def test_im2col_matches_gather(cuda, shape, k, s, p, d, cl):
+    x = torch.randn(*shape).bfloat16()
+    ref, Ho, Wo = col_reference(x, k, k, s, p, d)
+    K = ref.shape[1]
+    Kp = (K + 7) // 8 * 8
+    xd = x.to(cuda)
+    if cl:
+        xd = xd.contiguous(memory_format=torch.channels_last)
+    col = torch.full((ref.shape[0], Kp), 7.0, dtype=torch.bfloat16, device=cuda)
+    B, C, H, W = shape
+    _abi.call("b2_im2col_bf16", xd.data_ptr(), *xd.stride(), B, C, H, W, k, k, s, s, p, p, d, d, Ho, Wo, Kp,
+              col.data_ptr(), st())
+    got = col.cpu()
+    assert torch.equal(got[:, :K], ref) and bool((got[:, K:] == 0).all())
+
+
+@pytest.fixture()
+def fresh(cuda):
+    xdna_train.register_xdna_device()
+    xdna_train.set_npu_mode(2)
+    saved = xdna_train.set_conv_paths()
+    xdna_train.set_conv_paths(conv1x1=True, general=True)
+    xdna_train.reset_fallback_stats()
+    yield
+    xdna_train.set_conv_paths(*saved)
+
+
+CASES = [
+    # (B, Cin, H, W, Cout, k, stride, pad, dilation, bias, channels_last)
+    (2, 3, 64, 64, 64, 7, 2, 3, 1, False, True),   # ResNet stem
+    (2, 3, 64, 64, 64, 7, 2, 3, 1, False, False),
+    (4, 3, 36, 36, 32, 9, 1, 4, 1, True, False),   # style-net first layer
+    (2, 32, 20, 20, 16, 9, 1, 4, 1, True, False),  # large kernel, many channels
+    (2, 8, 17, 15, 16, 3, 2, 1, 1, False, True),   # strided 3x3, few channels
+    (2, 16, 21, 19, 24, 5, 1, 4, 2, True, True),   # dilated 5x5
+]
+
+
+@pytest.mark.parametrize("B,Cin,H,W,Cout,k,s,p,d,bias,cl", CASES)
+def test_general_conv_module_vs_fp32(fresh, B, Cin, H, W, Cout, k, s, p, d, bias, cl):
+    torch.manual_seed(B * Cin + k)
+    conv = nn.Conv2d(Cin, Cout, k, stride=s, padding=p, dilation=d, bias=bias).bfloat16()
+    x = torch.randn(B, Cin, H, W).bfloat16()
+    mf = torch.channels_last if cl else torch.contiguous_format
+    ref = nn.Conv2d(Cin, Cout, k, stride=s, padding=p, dilation=d, bias=bias)
+    ref.load_state_dict({n: t.float() for n, t in conv.state_dict().items()})
+    xr = x.float().contiguous(memory_format=mf).detach().requires_grad_()
+    yr = ref(xr)
+    g = torch.randn_like(yr).bfloat16()
+    yr.backward(g.float())
+    cx = nn.Conv2d(Cin, Cout, k, stride=s, padding=p, dilation=d, bias=bias).bfloat16()
+    cx.load_state_dict(conv.state_dict())
+    cx = cx.to(X)
+    xx = x.to(X).contiguous(memory_format=mf).detach().requires_grad_()
+    yx = cx(xx)
+    yx.backward(g.to(X).contiguous(memory_format=mf))
+    close(yx, yr)
+    close(xx.grad, xr.grad)
+    close(cx.weight.grad, ref.weight.grad)
+    if bias:
+        close(cx.bias.grad, ref.bias.grad)
+    kst = xdna_train.kernel_stats()
+    assert kst.get("im2col", 0) >= 2 and kst.get("conv.gemm", 0) >= 1 and kst.get("col2im", 0) >= 1
+    assert "convolution_overrideable" not in xdna_train.fallback_stats()
+
+
+def test_stem_without_input_gradient(fresh):
+    """The first layer's input needs no gradient: only dW is computed."""
+    torch.manual_seed(0)
+    conv = nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False).bfloat16()
+    x = torch.randn(2, 3, 32, 32).bfloat16()
+    ref = nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False)
+    ref.load_state_dict({n: t.float() for n, t in conv.state_dict().items()})
+    yr = ref(x.float())
+    g = torch.randn_like(yr).bfloat16()
+    yr.backward(g.float())
+    cx = nn.Conv2d(3, 64, 7, stride=2, padding=3, bias=False).bfloat16()
+    cx.load_state_dict(conv.state_dict())
+    cx = cx.to(X)
+    yx = cx(x.to(X))
+    yx.backward(g.to(X))
+    close(cx.weight.grad, ref.weight.grad)
+    assert xdna_train.kernel_stats().get("col2im", 0) == 0
