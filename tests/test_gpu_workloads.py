@@ -111,28 +111,45 @@ def test_config4_style_transfer_steps(fused):
 
 
 def test_config5_resnet50_steps():
+    """ResNet-50 (BASELINE config 5 at batch 4) against an fp32 CPU reference,
+    with the reference's own kind of gate (the fused path's error no larger
+    than 1.5x the CPU bf16 path's, tests/run_regions_bn.py): the first step's
+    loss and the whole gradient vector; then three SGD steps lower the loss.
+    In bf16 every BatchNorm output is rounded once, and 53 BatchNorms over
+    batch-4 statistics compound those roundings into gradient differences of
+    order one between any two bf16 implementations, so bf16 is compared with
+    fp32, not with another bf16 run."""
     from torchvision.models import resnet50
 
-    def run(dev):
+    def run(dev, dtype, steps=3):
         torch.manual_seed(0)
-        model = resnet50(num_classes=1000).bfloat16().to(dev).to(memory_format=torch.channels_last)
-        # single-tensor SGD on both sides: torch 2.11's CPU _fused_sgd_ leaves
+        model = resnet50(num_classes=1000).to(dtype).to(dev).to(memory_format=torch.channels_last)
+        # single-tensor SGD on every side: torch 2.11's CPU _fused_sgd_ leaves
         # bf16 parameters unchanged, so the CPU side cannot use the fused kernel
         opt = torch.optim.SGD(model.parameters(), lr=0.01, momentum=0.9, foreach=False, fused=False)
         g = torch.Generator().manual_seed(1)
-        x = torch.randn(4, 3, 224, 224, generator=g).bfloat16().to(dev).contiguous(memory_format=torch.channels_last)
+        x = torch.randn(4, 3, 224, 224, generator=g).bfloat16().to(dtype).to(dev)
+        x = x.contiguous(memory_format=torch.channels_last)
         y = torch.randint(0, 1000, (4,), generator=g).to(dev)
-        out = []
-        for _ in range(3):
+        out, grads = [], None
+        for i in range(steps):
             opt.zero_grad(set_to_none=True)
             loss = F.cross_entropy(model(x).float(), y)
             loss.backward()
+            if i == 0:
+                grads = torch.cat([p.grad.detach().float().cpu().reshape(-1) for p in model.parameters()])
             opt.step()
             out.append(loss.item())
-        return out
-    lc = run("cpu")
-    lx = run(X)
-    for a, b in zip(lx, lc):
-        assert _rel(a, b) <= 0.03, (lx, lc)
+        return out, grads
+    l32, g32 = run("cpu", torch.float32, steps=1)
+    lc, gc = run("cpu", torch.bfloat16)
+    lx, gx = run(X, torch.bfloat16)
+
+    def err(g):
+        return ((g - g32).norm() / g32.norm()).item()
+    e_cpu, e_x = err(gc), err(gx)
+    assert abs(lx[0] - l32[0]) <= 1.5 * abs(lc[0] - l32[0]) + 0.01 * abs(l32[0]), (lx[0], lc[0], l32[0])
+    assert e_x <= 1.5 * e_cpu + 0.05, (e_x, e_cpu)
+    assert lx[2] < lx[0] and lc[2] < lc[0], (lx, lc)
     ks = xdna_train.kernel_stats()
-    assert ks.get("conv3x3.fwd", 0) >= 12 and ks.get("conv3x3.wgrad", 0) > 0
+    assert ks.get("conv3x3.fwd", 0) >= 12 and ks.get("conv3x3.wgrad", 0) > 0 and ks.get("batch_norm.fwd", 0) > 0
