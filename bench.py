@@ -644,9 +644,50 @@ def kernel_probe(args):
     print(json.dumps({"probe": f"B{b} C{c} HW{hw}", **out}), flush=True)
 
 
+def bn_probe(args):
+    """Device time of training-mode BatchNorm2d forward + backward on one
+    channels-last shape (``--bn-probe --batch B --channels C --hw H``), with the
+    algorithmic bandwidth: forward 6 B/elem (x read by the sums and by the
+    apply pass, y written), backward 8 B/elem (dy and x read by the sums and
+    by the dx pass, dx written).  The ncu small case of the BatchNorm kernels."""
+    import torch.nn as nn
+
+    import xdna_train
+    xdna_train.register_xdna_device()
+    torch.cuda.set_device(0)
+    X = torch.device("xdna", 0)
+    b, c, hw = args.batch, args.channels, args.hw
+    cl = torch.channels_last
+    bn = nn.BatchNorm2d(c).bfloat16().to(X)
+    x = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X).contiguous(memory_format=cl).requires_grad_()
+    g = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X).contiguous(memory_format=cl)
+    st = torch.cuda.current_stream()
+    times = {"fwd": [], "bwd": []}
+    for i in range(args.iters + 3):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(st)
+        y = bn(x)
+        e1.record(st)
+        y.backward(g)
+        e2.record(st)
+        torch.cuda.synchronize()
+        if i >= 3:
+            times["fwd"].append(e0.elapsed_time(e1))
+            times["bwd"].append(e1.elapsed_time(e2))
+        x.grad = None
+    n = x.numel()
+    out = {}
+    for k, bpe in (("fwd", 6), ("bwd", 8)):
+        ms = sorted(times[k])[len(times[k]) // 2]
+        out[k] = {"ms": round(ms, 4), "gbs": round(bpe * n / (ms * 1e-3) / 1e9, 1)}
+    print(json.dumps({"probe": f"BatchNorm2d channels-last B{b} C{c} HW{hw}", **out,
+                      "kernels": xdna_train.kernel_stats()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
+    ap.add_argument("--bn-probe", action="store_true")
     ap.add_argument("--workload", default="conv", choices=["conv", "readme", "mlp", "style", "resnet50"],
                     help="conv (default, the headline) or another BASELINE config")
     ap.add_argument("--batch", type=int, default=B_PER_GPU)
@@ -661,6 +702,9 @@ def main():
     args = ap.parse_args()
     if args.kernel_probe:
         kernel_probe(args)
+        return
+    if args.bn_probe:
+        bn_probe(args)
         return
     if args.workload != "conv":
         line = run_workload(args)
