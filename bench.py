@@ -581,7 +581,10 @@ def run_workload(args):
             on_x = torch.device(dev).type == "xdna"
             # the CPU side keeps the single-tensor SGD: torch 2.11's CPU _fused_sgd_
             # leaves bf16 parameters unchanged
-            opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True if on_x else None)
+            if args.optimizer == "adam":  # the config's Adam variant
+                opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True if on_x else None)
+            else:
+                opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True if on_x else None)
             ar = GradAllReduce(model) if (world > 1 and torch.device(dev).type == "xdna") else None
             g = torch.Generator().manual_seed(rank)
             x = torch.randn(b, 3, 224, 224, generator=g).bfloat16().to(dev).contiguous(
@@ -598,7 +601,8 @@ def run_workload(args):
             return step
         dt = _timed(make(X, bsz), args.steps, args.warmup, sync)
         out.update(metric="ResNet-50 training images/s (BASELINE config 5)", value=round(world * bsz / dt, 1),
-                   unit="images/s", ms_per_step=round(dt * 1e3, 4), per_gpu_batch=bsz, scaling="weak")
+                   unit="images/s", ms_per_step=round(dt * 1e3, 4), per_gpu_batch=bsz, scaling="weak",
+                   optimizer="Adam lr 1e-3" if args.optimizer == "adam" else "SGD momentum 0.9")
         c = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             c = _timed(make("cpu", 4), 2, 1, cpu) / 4 * bsz  # seconds per bsz images, from a 4-image sample
@@ -684,10 +688,70 @@ def bn_probe(args):
                       "kernels": xdna_train.kernel_stats()}), flush=True)
 
 
+def adam_probe(args):
+    """Device time of one fused Adam step over ``--params`` million fp32
+    parameters (FP32 master weights, the MLP config's regime) or bf16 ones
+    (``--adam-bf16``), in 4 tensors, through torch.optim.Adam on the xdna
+    device; algorithmic bytes per element: fp32 28 (read g, p, m, v; write p,
+    m, v), bf16 14.  The ncu small case of the Adam kernel."""
+    import xdna_train
+    xdna_train.register_xdna_device()
+    torch.cuda.set_device(0)
+    X = torch.device("xdna", 0)
+    dt = torch.bfloat16 if args.adam_bf16 else torch.float32
+    n = int(args.params * 1e6) // 4
+    params = [torch.nn.Parameter(torch.randn(n, dtype=dt, device=X)) for _ in range(4)]
+    for q in params:
+        q.grad = torch.randn(n, dtype=dt, device=X)
+    opt = torch.optim.Adam(params, lr=1e-4)
+    st = torch.cuda.current_stream()
+    ts = []
+    for i in range(args.iters + 3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        opt.step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        if i >= 3:
+            ts.append(e0.elapsed_time(e1))
+    ms = sorted(ts)[len(ts) // 2]
+    # the kernel alone, through the C ABI on the optimizer's own state
+    import ctypes
+    from xdna_train import _abi
+    arr = (_abi.AdamTensor * 4)()
+    for k, q in enumerate(params):
+        stt = opt.state[q]
+        arr[k] = _abi.AdamTensor(q.data_ptr(), q.grad.data_ptr(), stt["exp_avg"].data_ptr(),
+                                 stt["exp_avg_sq"].data_ptr(), None, stt["step"].data_ptr(), n)
+    code = _abi.B2_BF16 if args.adam_bf16 else _abi.B2_F32
+    hp = _abi.AdamHparams(1e-4, 0.9, 0.999, 0.0, 1e-8, 0, 0, 0, code, code, None, None, None)
+    kts = []
+    for i in range(args.iters + 3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        _abi.check(_abi.lib().b2_fused_adam(arr, 4, ctypes.byref(hp), st.cuda_stream))
+        e1.record(st)
+        torch.cuda.synchronize()
+        if i >= 3:
+            kts.append(e0.elapsed_time(e1))
+    kms = sorted(kts)[len(kts) // 2]
+    bpe = 14 if args.adam_bf16 else 28
+    elems = 4 * n
+    print(json.dumps({"probe": f"fused Adam {elems / 1e6:.1f} M {str(dt).split('.')[-1]} parameters",
+                      "step_ms": round(ms, 4), "step_gbs": round(bpe * elems / (ms * 1e-3) / 1e9, 1),
+                      "kernel_ms": round(kms, 4), "kernel_gbs": round(bpe * elems / (kms * 1e-3) / 1e9, 1),
+                      "note": "step = torch.optim.Adam.step() incl. host-side work and step-counter updates",
+                      "kernels": xdna_train.kernel_stats()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
     ap.add_argument("--bn-probe", action="store_true")
+    ap.add_argument("--adam-probe", action="store_true")
+    ap.add_argument("--adam-bf16", action="store_true")
+    ap.add_argument("--params", type=float, default=64.0, help="--adam-probe: millions of parameters")
+    ap.add_argument("--optimizer", default="sgd", choices=["sgd", "adam"], help="--workload resnet50: optimizer")
     ap.add_argument("--workload", default="conv", choices=["conv", "readme", "mlp", "style", "resnet50"],
                     help="conv (default, the headline) or another BASELINE config")
     ap.add_argument("--batch", type=int, default=B_PER_GPU)
@@ -705,6 +769,9 @@ def main():
         return
     if args.bn_probe:
         bn_probe(args)
+        return
+    if args.adam_probe:
+        adam_probe(args)
         return
     if args.workload != "conv":
         line = run_workload(args)

@@ -39,7 +39,7 @@ struct AdamArgs {
   const float* step[kMaxTensors];
   long long numel[kMaxTensors];
   int chunk_begin[kMaxTensors + 1];  // prefix sums of chunks per tensor
-  unsigned char vec[kMaxTensors];    // all arrays aligned for 4-element vectors
+  unsigned char vec[kMaxTensors];    // all arrays 16-byte aligned (8-element vectors)
   int ntensors;
 };
 
@@ -69,32 +69,37 @@ __device__ __forceinline__ void st(void* p, long long i, float v) {
   else
     static_cast<float*>(p)[i] = v;
 }
-// 4 consecutive elements (i % 4 == 0, arrays aligned for it)
+// 8 consecutive elements (i % 8 == 0, arrays 16-byte aligned): one 16-byte
+// access for bf16, two for fp32.
 template <typename T>
-__device__ __forceinline__ void ld4(const void* p, long long i, float (&o)[4]) {
+__device__ __forceinline__ void ld8(const void* p, long long i, float (&o)[8]) {
   if constexpr (sizeof(T) == 2) {
-    const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i);
-    o[0] = __uint_as_float(u.x << 16);
-    o[1] = __uint_as_float(u.x & 0xffff0000u);
-    o[2] = __uint_as_float(u.y << 16);
-    o[3] = __uint_as_float(u.y & 0xffff0000u);
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[2 * k] = __uint_as_float(w[k] << 16);
+      o[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
   } else {
-    const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
-    o[0] = f.x;
-    o[1] = f.y;
-    o[2] = f.z;
-    o[3] = f.w;
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i + 4);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
   }
 }
 template <typename T>
-__device__ __forceinline__ void st4(void* p, long long i, const float (&v)[4]) {
+__device__ __forceinline__ void st8(void* p, long long i, const float (&v)[8]) {
   if constexpr (sizeof(T) == 2) {
-    uint2 u;
+    uint4 u;
     u.x = uint32_t(f2bf(v[0])) | (uint32_t(f2bf(v[1])) << 16);
     u.y = uint32_t(f2bf(v[2])) | (uint32_t(f2bf(v[3])) << 16);
-    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p) + i) = u;
+    u.z = uint32_t(f2bf(v[4])) | (uint32_t(f2bf(v[5])) << 16);
+    u.w = uint32_t(f2bf(v[6])) | (uint32_t(f2bf(v[7])) << 16);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = u;
   } else {
     *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i + 4) = make_float4(v[4], v[5], v[6], v[7]);
   }
 }
 
@@ -157,20 +162,20 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
     void* V_ = a.v[t];
     void* X_ = a.vmax[t];
     if (a.vec[t]) {
-      for (long long i = begin + 4 * threadIdx.x; i < end; i += 4 * kThreads) {
-        if (i + 4 <= end) {
-          float g[4], p[4], m[4], v[4], x[4] = {0.f, 0.f, 0.f, 0.f};
-          ld4<P>(G_, i, g);
-          ld4<P>(P_, i, p);
-          ld4<S>(M_, i, m);
-          ld4<S>(V_, i, v);
-          if (s.amsgrad) ld4<S>(X_, i, x);
+      for (long long i = begin + 8 * threadIdx.x; i < end; i += 8 * kThreads) {
+        if (i + 8 <= end) {
+          float g[8], p[8], m[8], v[8], x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          ld8<P>(G_, i, g);
+          ld8<P>(P_, i, p);
+          ld8<S>(M_, i, m);
+          ld8<S>(V_, i, v);
+          if (s.amsgrad) ld8<S>(X_, i, x);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) update(s, c, g[k], p[k], m[k], v[k], x[k]);
-          st4<P>(P_, i, p);
-          st4<S>(M_, i, m);
-          st4<S>(V_, i, v);
-          if (s.amsgrad) st4<S>(X_, i, x);
+          for (int k = 0; k < 8; ++k) update(s, c, g[k], p[k], m[k], v[k], x[k]);
+          st8<P>(P_, i, p);
+          st8<S>(M_, i, m);
+          st8<S>(V_, i, v);
+          if (s.amsgrad) st8<S>(X_, i, x);
         } else {
           for (long long j = i; j < end; ++j) {
             float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
@@ -256,8 +261,8 @@ extern "C" b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n, const b
     args.vmax[k] = t.max_exp_avg_sq;
     args.step[k] = t.step;
     args.numel[k] = t.numel;
-    args.vec[k] = al(t.param, 4 * psz) && al(t.grad, 4 * psz) && al(t.exp_avg, 4 * ssz) &&
-                  al(t.exp_avg_sq, 4 * ssz) && (!hp->amsgrad || al(t.max_exp_avg_sq, 4 * ssz));
+    args.vec[k] = al(t.param, 16) && al(t.grad, 16) && al(t.exp_avg, 16) && al(t.exp_avg_sq, 16) &&
+                  (!hp->amsgrad || al(t.max_exp_avg_sq, 16));
     args.chunk_begin[k + 1] = args.chunk_begin[k] + int(chunks);
     args.ntensors = k + 1;
   }
