@@ -131,11 +131,24 @@ def setup_dist(args):
 
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        # once xdna is registered PyTorch treats it as the accelerator and
+        # refuses a cuda device_id; NCCL then binds the device lazily
+        acc = torch.accelerator.current_accelerator() if hasattr(torch, "accelerator") else None
+        kw = {"device_id": torch.device("cuda", local)} if acc is None or acc.type == "cuda" else {}
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), **kw)
     else:
         torch.cuda.set_device(0)
     return world, rank, local
+
+
+def cuda_barrier():
+    """A barrier as an all-reduce of a CUDA tensor: dist.barrier() picks its
+    device from the current accelerator, which is xdna once registered, and
+    NCCL has no xdna backend."""
+    import torch.distributed as dist
+    t = torch.zeros(1, device=torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(t)
+    torch.cuda.synchronize()
 
 
 def allreduce_max(v: float, world: int) -> float:
@@ -188,7 +201,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     xdna_train.reset_mapped_cpu_stats()
     if world > 1:
-        dist.barrier()
+        cuda_barrier()
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -199,7 +212,7 @@ def run_ours(args):
         e1.record(s)
         torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        cuda_barrier()
     ms = e0.elapsed_time(e1) / args.steps
     ms = allreduce_max(ms, world)
     launches = sum(xdna_train.kernel_stats().values())
@@ -213,7 +226,7 @@ def run_ours(args):
         w_host.copy_(conv.weight.detach(), non_blocking=True)
     torch.cuda.synchronize()
     if world > 1:
-        dist.barrier()
+        cuda_barrier()
     t0 = time.perf_counter()
     e2 = torch.cuda.Event(enable_timing=True)
     e3 = torch.cuda.Event(enable_timing=True)
@@ -779,7 +792,7 @@ def main():
             print(json.dumps(line), flush=True)
         if int(os.environ.get("WORLD_SIZE", "1")) > 1:
             import torch.distributed as dist
-            dist.barrier()
+            cuda_barrier()
             dist.destroy_process_group()
         return
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup
@@ -797,7 +810,7 @@ def main():
         print(json.dumps(line), flush=True)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.impl == "ours":
         import torch.distributed as dist
-        dist.barrier()
+        cuda_barrier()
         dist.destroy_process_group()
 
 
