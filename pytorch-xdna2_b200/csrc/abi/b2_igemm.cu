@@ -836,7 +836,8 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   const int ktot = chunks * 9 * 64;
   const bool wide = Cout > 128 && (Cout % 256 == 0 || Cout % 256 > 128);
   const bool pair = wide && pair_mma_enabled();
-  const int BN = wide ? 256 : 128;
+  const bool narrow = Cout <= 64;  // 64-wide tiles: no MMA work on padding columns
+  const int BN = wide ? 256 : narrow ? 64 : 128;
   const uint32_t b_box = pair ? 128u : uint32_t(BN);  // the pair kernel loads half of B per CTA
 
   CUtensorMap ta, tb;
@@ -882,6 +883,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
     return launch_pair<kConv>(ta, tb, pp, pp.tiles_m * pp.tiles_n, st);
   }
   if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
+  if (narrow) return launch<64, kStages64, kConv, false, false>(ta, tb, p, tiles, st);
   return launch<128, kStages128, kConv, false, false>(ta, tb, p, tiles, st);
 }
 
@@ -896,7 +898,7 @@ WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow
   WgradPlan w{};
   w.m_total = (long long)B * (H + 2) * (W + 2);
   w.pair = allow_pair && Cin > 128 && Cout > 128;
-  w.BN = Cin > 128 ? 256 : 128;
+  w.BN = Cin > 128 ? 256 : Cin > 64 ? 128 : 64;
   w.ci_blocks = (Cin + w.BN - 1) / w.BN;
   w.tiles_m = (Cout + (w.pair ? 255 : BM - 1)) / (w.pair ? 256 : BM);
   w.num_kb = int((w.m_total + BK - 1) / BK);
@@ -1123,6 +1125,8 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
     B2_TRY(launch_pair<kWgrad>(ta, tb, p, tiles, st));
   else if (w.BN == 256)
     B2_TRY((launch<256, kStages256, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  else if (w.BN == 64)
+    B2_TRY((launch<64, kStages64, kWgrad, true, true>(ta, tb, p, tiles, st)));
   else
     B2_TRY((launch<128, kStages128, kWgrad, true, true>(ta, tb, p, tiles, st)));
   const long long total = (long long)Cout * Cin * 9;
@@ -1463,6 +1467,8 @@ b2_status b2_conv3x3_wgrad_noalloc(const void* dy_rows, const void* x_rows, void
   const int tiles = w.splits * w.tiles_m * 9 * w.ci_blocks;
   if (w.BN == 256)
     B2_TRY((launch<256, kStages256, kWgrad, true, true>(ta, tb, p, tiles, st)));
+  else if (w.BN == 64)
+    B2_TRY((launch<64, kStages64, kWgrad, true, true>(ta, tb, p, tiles, st)));
   else
     B2_TRY((launch<128, kStages128, kWgrad, true, true>(ta, tb, p, tiles, st)));
   const long long total = (long long)Cout * Cin * 9;
