@@ -299,6 +299,26 @@ b2_status b2_unpack_weight_khwc(const float* dwk, int64_t Cout, int64_t Cin,
                                 int kh, int kw, int64_t Kp, void* dw,
                                 int dtype, void* stream);
 
+/* ---- 2-D max pooling with indices (the reference runs it on its CPU path;
+ * the same results as ATen): windows scanned in (kh, kw) order, a value
+ * replaces the maximum when greater or NaN, index h*W + w within the plane
+ * (int64).  The backward gathers, per input element in (oh, ow) order, the
+ * gradients whose saved index is its own, in fp32, rounded once.  x/dx and
+ * y/indices/dy through element strides [n, c, h, w] (indices and dy share
+ * y_strides); dtype B2_BF16 or B2_F32. */
+b2_status b2_maxpool2d_fwd(const void* x, const int64_t* x_strides, void* y,
+                           int64_t* indices, const int64_t* y_strides,
+                           int dtype, int64_t N, int64_t C, int64_t H,
+                           int64_t W, int64_t OH, int64_t OW, int kh, int kw,
+                           int sh, int sw, int ph, int pw, int dh, int dw,
+                           void* stream);
+b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices,
+                           const int64_t* y_strides, void* dx,
+                           const int64_t* x_strides, int dtype, int64_t N,
+                           int64_t C, int64_t H, int64_t W, int64_t OH,
+                           int64_t OW, int kh, int kw, int sh, int sw, int ph,
+                           int pw, int dh, int dw, void* stream);
+
 /* ---- layout ops (replace the reference's host cat / nearest-2x upsample,
  * torch_xdna_device.cpp:3796-4175; used by the xdna `cat`,
  * `upsample_nearest2d` and `upsample_nearest2d_backward` kernels) ---------- */

@@ -1,0 +1,278 @@
+// 2-D max pooling with indices (forward) and its backward, bf16 / fp32, any
+// kernel, stride, padding, dilation and ceil mode.  Same results as ATen
+// (the reference runs these on its CPU path):
+//
+//   forward   the window is scanned in (kh, kw) order; a value replaces the
+//             running maximum when it is greater or NaN (so the last NaN
+//             wins), starting from -inf at the window's first valid position;
+//             the index is h*W + w within the plane (int64).
+//   backward  a gather: every input element adds, in (oh, ow) order, the
+//             gradients of the outputs whose saved index is its own, in fp32,
+//             and is rounded once -- no atomics, deterministic.
+//
+// Channels-last bf16 with C % 8 == 0 moves 16-byte channel vectors; every
+// other layout goes through element strides.  HBM-bound.
+#include <algorithm>
+
+#include "b2_common.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kPoolThreads = 256;
+
+struct PoolGeom {
+  long long N, C, H, W, OH, OW;
+  int kh, kw, sh, sw, ph, pw, dh, dw;
+  // element strides of x (and dx) and of y / indices / dy
+  long long xs[4], ys[4];
+};
+
+int pool_grid(long long units, int sms) {
+  const long long b = (units + kPoolThreads - 1) / kPoolThreads;
+  return int(std::max<long long>(1, std::min<long long>(b, (long long)sms * 16)));
+}
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p, long long i) {
+  if constexpr (sizeof(T) == 2) return bf2f(reinterpret_cast<const uint16_t*>(p)[i]);
+  else return p[i];
+}
+template <typename T>
+__device__ __forceinline__ void stf(T* p, long long i, float v) {
+  if constexpr (sizeof(T) == 2) reinterpret_cast<uint16_t*>(p)[i] = f2bf(v);
+  else p[i] = v;
+}
+
+// first valid tap of a window start (may be negative) and its end (exclusive)
+__device__ __forceinline__ void window(long long o, int s, int p, int k, int d, long long n, long long& beg,
+                                       long long& end) {
+  beg = o * s - p;
+  end = min(beg + (long long)(k - 1) * d + 1, n);
+  while (beg < 0) beg += d;
+}
+
+// output positions whose window can cover input position i: [lo, hi)
+__device__ __forceinline__ void covering(long long i, int s, int p, int k, int d, long long on, long long& lo,
+                                         long long& hi) {
+  const long long span = (long long)(k - 1) * d + 1;
+  lo = (i + p < span) ? 0 : (i + p - span) / s + 1;
+  hi = min((i + p) / s + 1, on);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_kernel(const T* __restrict__ x, PoolGeom g,
+                                                                   T* __restrict__ y, int64_t* __restrict__ ind) {
+  const long long total = g.N * g.C * g.OH * g.OW;
+  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
+       u += (long long)gridDim.x * kPoolThreads) {
+    const long long ow = u % g.OW, oh = (u / g.OW) % g.OH, c = (u / (g.OW * g.OH)) % g.C,
+                    n = u / (g.OW * g.OH * g.C);
+    long long h0, h1, w0, w1;
+    window(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
+    window(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
+    const T* xp = x + n * g.xs[0] + c * g.xs[1];
+    float best = -INFINITY;
+    long long bi = h0 * g.W + w0;
+    for (long long h = h0; h < h1; h += g.dh)
+      for (long long w = w0; w < w1; w += g.dw) {
+        const float v = ldf(xp, h * g.xs[2] + w * g.xs[3]);
+        if (v > best || v != v) {
+          best = v;
+          bi = h * g.W + w;
+        }
+      }
+    const long long o = n * g.ys[0] + c * g.ys[1] + oh * g.ys[2] + ow * g.ys[3];
+    stf(y, o, best);
+    ind[o] = bi;
+  }
+}
+
+// channels-last bf16, 8 channels per thread (C % 8 == 0, 16-byte aligned)
+__global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const uint16_t* __restrict__ x, PoolGeom g,
+                                                                         uint16_t* __restrict__ y,
+                                                                         int64_t* __restrict__ ind) {
+  const long long cv = g.C / 8;
+  const long long total = g.N * g.OH * g.OW * cv;
+  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
+       u += (long long)gridDim.x * kPoolThreads) {
+    const long long q = u % cv, r = u / cv;
+    const long long ow = r % g.OW, oh = (r / g.OW) % g.OH, n = r / (g.OW * g.OH);
+    long long h0, h1, w0, w1;
+    window(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
+    window(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
+    float best[8];
+    long long bi[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      best[e] = -INFINITY;
+      bi[e] = h0 * g.W + w0;
+    }
+    const uint16_t* xp = x + n * g.xs[0] + q * 8;
+    for (long long h = h0; h < h1; h += g.dh)
+      for (long long w = w0; w < w1; w += g.dw) {
+        const uint4 v4 = *reinterpret_cast<const uint4*>(xp + h * g.xs[2] + w * g.xs[3]);
+        const uint32_t wd[4] = {v4.x, v4.y, v4.z, v4.w};
+        const long long idx = h * g.W + w;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float v = __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
+          if (v > best[e] || v != v) {
+            best[e] = v;
+            bi[e] = idx;
+          }
+        }
+      }
+    const long long o = n * g.ys[0] + oh * g.ys[2] + ow * g.ys[3] + q * 8;
+    uint4 out;
+    out.x = pack_bf2(best[0], best[1]);
+    out.y = pack_bf2(best[2], best[3]);
+    out.z = pack_bf2(best[4], best[5]);
+    out.w = pack_bf2(best[6], best[7]);
+    *reinterpret_cast<uint4*>(y + o) = out;
+    longlong2* ip = reinterpret_cast<longlong2*>(ind + o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ip[e] = make_longlong2(bi[2 * e], bi[2 * e + 1]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_kernel(const T* __restrict__ dy,
+                                                                   const int64_t* __restrict__ ind, PoolGeom g,
+                                                                   T* __restrict__ dx) {
+  const long long total = g.N * g.C * g.H * g.W;
+  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
+       u += (long long)gridDim.x * kPoolThreads) {
+    const long long w = u % g.W, h = (u / g.W) % g.H, c = (u / (g.W * g.H)) % g.C, n = u / (g.W * g.H * g.C);
+    long long oh0, oh1, ow0, ow1;
+    covering(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
+    covering(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
+    const long long me = h * g.W + w;
+    const long long base = n * g.ys[0] + c * g.ys[1];
+    float s = 0.0f;
+    for (long long oh = oh0; oh < oh1; ++oh)
+      for (long long ow = ow0; ow < ow1; ++ow) {
+        const long long o = base + oh * g.ys[2] + ow * g.ys[3];
+        if (ind[o] == me) s = __fadd_rn(s, ldf(dy, o));
+      }
+    stf(dx, n * g.xs[0] + c * g.xs[1] + h * g.xs[2] + w * g.xs[3], s);
+  }
+}
+
+__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_kernel(const uint16_t* __restrict__ dy,
+                                                                         const int64_t* __restrict__ ind,
+                                                                         PoolGeom g, uint16_t* __restrict__ dx) {
+  const long long cv = g.C / 8;
+  const long long total = g.N * g.H * g.W * cv;
+  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
+       u += (long long)gridDim.x * kPoolThreads) {
+    const long long q = u % cv, r = u / cv;
+    const long long w = r % g.W, h = (r / g.W) % g.H, n = r / (g.W * g.H);
+    long long oh0, oh1, ow0, ow1;
+    covering(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
+    covering(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
+    const long long me = h * g.W + w;
+    float s[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+    for (long long oh = oh0; oh < oh1; ++oh)
+      for (long long ow = ow0; ow < ow1; ++ow) {
+        const long long o = n * g.ys[0] + oh * g.ys[2] + ow * g.ys[3] + q * 8;
+        const uint4 v4 = *reinterpret_cast<const uint4*>(dy + o);
+        const uint32_t wd[4] = {v4.x, v4.y, v4.z, v4.w};
+        const longlong2* ip = reinterpret_cast<const longlong2*>(ind + o);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const longlong2 ii = ip[e2];
+          if (ii.x == me) s[2 * e2] = __fadd_rn(s[2 * e2], __uint_as_float(wd[e2] << 16));
+          if (ii.y == me) s[2 * e2 + 1] = __fadd_rn(s[2 * e2 + 1], __uint_as_float(wd[e2] & 0xffff0000u));
+        }
+      }
+    uint4 out;
+    out.x = pack_bf2(s[0], s[1]);
+    out.y = pack_bf2(s[2], s[3]);
+    out.z = pack_bf2(s[4], s[5]);
+    out.w = pack_bf2(s[6], s[7]);
+    *reinterpret_cast<uint4*>(dx + n * g.xs[0] + h * g.xs[2] + w * g.xs[3] + q * 8) = out;
+  }
+}
+
+b2_status make_pool(PoolGeom& g, int64_t N, int64_t C, int64_t H, int64_t W, int64_t OH, int64_t OW, int kh, int kw,
+                    int sh, int sw, int ph, int pw, int dh, int dw, const int64_t* xs, const int64_t* ys,
+                    const char* who) {
+  if (N < 0 || C < 0 || H <= 0 || W <= 0 || OH < 0 || OW < 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 || ph < 0 ||
+      pw < 0 || dh <= 0 || dw <= 0 || 2 * ph > kh || 2 * pw > kw || !xs || !ys)
+    return set_error(B2_ERR_INVALID, "%s: bad geometry", who);
+  g = PoolGeom{N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, {xs[0], xs[1], xs[2], xs[3]},
+               {ys[0], ys[1], ys[2], ys[3]}};
+  return B2_OK;
+}
+
+bool nhwc8(const PoolGeom& g, const void* a, const void* b, const void* c) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return g.C % 8 == 0 && g.xs[1] == 1 && g.ys[1] == 1 && g.xs[3] % 8 == 0 && g.xs[2] % 8 == 0 && g.xs[0] % 8 == 0 &&
+         g.ys[3] % 8 == 0 && g.ys[2] % 8 == 0 && g.ys[0] % 8 == 0 && al(a) && al(b) && al(c);
+}
+
+int cur_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  return sm_count(dev);
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+b2_status b2_maxpool2d_fwd(const void* x, const int64_t* x_strides, void* y, int64_t* indices,
+                           const int64_t* y_strides, int dtype, int64_t N, int64_t C, int64_t H, int64_t W,
+                           int64_t OH, int64_t OW, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
+                           void* stream) {
+  PoolGeom g;
+  B2_TRY(make_pool(g, N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, x_strides, y_strides, "b2_maxpool2d_fwd"));
+  if (dtype != B2_BF16 && dtype != B2_F32) return set_error(B2_ERR_UNSUPPORTED, "b2_maxpool2d_fwd: dtype");
+  const long long total = N * C * OH * OW;
+  if (total == 0) return B2_OK;
+  if (!x || !y || !indices) return set_error(B2_ERR_INVALID, "b2_maxpool2d_fwd: null pointer");
+  auto st = static_cast<cudaStream_t>(stream);
+  const int sms = cur_sms();
+  if (dtype == B2_BF16 && nhwc8(g, x, y, indices))
+    maxpool_fwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else if (dtype == B2_BF16)
+    maxpool_fwd_kernel<uint16_t><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else
+    maxpool_fwd_kernel<float><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(static_cast<const float*>(x), g,
+                                                                              static_cast<float*>(y), indices);
+  return check_cuda(cudaGetLastError(), "maxpool fwd launch");
+}
+
+b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices, const int64_t* y_strides, void* dx,
+                           const int64_t* x_strides, int dtype, int64_t N, int64_t C, int64_t H, int64_t W,
+                           int64_t OH, int64_t OW, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
+                           void* stream) {
+  PoolGeom g;
+  B2_TRY(make_pool(g, N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, x_strides, y_strides, "b2_maxpool2d_bwd"));
+  if (dtype != B2_BF16 && dtype != B2_F32) return set_error(B2_ERR_UNSUPPORTED, "b2_maxpool2d_bwd: dtype");
+  const long long total = N * C * H * W;
+  if (total == 0) return B2_OK;
+  if (!dx || (N * C * OH * OW > 0 && (!dy || !indices))) return set_error(B2_ERR_INVALID, "b2_maxpool2d_bwd: null pointer");
+  auto st = static_cast<cudaStream_t>(stream);
+  const int sms = cur_sms();
+  if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices))
+    maxpool_bwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else if (dtype == B2_BF16)
+    maxpool_bwd_kernel<uint16_t><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else
+    maxpool_bwd_kernel<float><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(static_cast<const float*>(dy), indices,
+                                                                               g, static_cast<float*>(dx));
+  return check_cuda(cudaGetLastError(), "maxpool bwd launch");
+}
+
+}  // extern "C"

@@ -68,6 +68,10 @@ SIGNATURES = {
                        i64, i64, vp],
     "b2_pack_weight_khwc_bf16": [vp, i64, i64, i32, i32, i64, vp, vp],
     "b2_unpack_weight_khwc": [vp, i64, i64, i32, i32, i64, vp, i32, vp],
+    "b2_maxpool2d_fwd": [vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32,
+                         i32, vp],
+    "b2_maxpool2d_bwd": [vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32,
+                         i32, vp],
     "b2_cat_blocks": [vp, vp, i32, vp, i64, i64, vp],
     "b2_upsample_nearest2x": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_upsample_nearest2x_backward": [vp, vp, i32, i32, i64, i64, i64, i64, vp],

@@ -4,8 +4,10 @@ The reference is single-device (docs/compatibility.md:44); data parallelism
 over the batch is new here.  ``GradAllReduce`` gives each rank a replica and
 averages the gradients after every backward:
 
-* parameters are grouped into flat buckets (``bucket_cap_mb``) in reverse
-  registration order, which is roughly the order backward produces them;
+* parameters are grouped into flat buckets (``bucket_cap_mb``, 16 MB: several
+  buckets per model, so all but the last all-reduce overlap backward) in
+  reverse registration order, which is roughly the order backward produces
+  them;
 * a post-accumulate-grad hook copies a ready gradient into its bucket -- that
   copy is the gradient's first read, so a deferred conv weight gradient is
   computed (enqueued) right there -- and when a bucket is complete its
@@ -31,11 +33,13 @@ def _comm_view(t: torch.Tensor) -> torch.Tensor:
 
 
 class GradAllReduce:
-    def __init__(self, module: torch.nn.Module, process_group=None, bucket_cap_mb: float = 64.0,
+    def __init__(self, module: torch.nn.Module, process_group=None, bucket_cap_mb: float = 16.0,
                  overlap: bool = True):
         self.module = module
         self.pg = process_group
         self.world = dist.get_world_size(process_group)
+        # NCCL averages in the collective; gloo (the CPU tests) sums, then we divide
+        self._avg = dist.get_backend(process_group) == "nccl"
         params = [p for p in module.parameters() if p.requires_grad]
         self.params = params
         cap = int(bucket_cap_mb * 1024 * 1024)
@@ -72,7 +76,11 @@ class GradAllReduce:
         b["flat"][off:off + p.numel()].copy_(p.grad.reshape(-1))
         b["ready"] += 1
         if b["ready"] == len(b["params"]):
-            b["work"] = dist.all_reduce(_comm_view(b["flat"]), group=self.pg, async_op=True)
+            b["work"] = self._all_reduce(b["flat"])
+
+    def _all_reduce(self, flat: torch.Tensor):
+        op = dist.ReduceOp.AVG if self._avg else dist.ReduceOp.SUM
+        return dist.all_reduce(_comm_view(flat), op=op, group=self.pg, async_op=True)
 
     def synchronize(self) -> None:
         """Finish all bucket all-reduces and write averaged gradients back."""
@@ -87,10 +95,11 @@ class GradAllReduce:
                     else:
                         b["flat"][off:off + n].zero_()
                     off += n
-                b["work"] = dist.all_reduce(_comm_view(b["flat"]), group=self.pg, async_op=True)
+                b["work"] = self._all_reduce(b["flat"])
         for b in self.buckets:
             b["work"].wait()
-            b["flat"].div_(self.world)
+            if not self._avg:
+                b["flat"].div_(self.world)
             off = 0
             for p in b["params"]:
                 n = p.numel()
