@@ -780,9 +780,93 @@ def adam_probe(args):
                       "kernels": xdna_train.kernel_stats()}), flush=True)
 
 
+# ResNet-50's 1x1 convolutions at stride 1: (H*W, Cin, Cout) per layer kind
+RESNET50_1X1 = [(3136, 64, 64), (3136, 64, 256), (3136, 256, 64), (3136, 256, 128), (784, 128, 512),
+                (784, 512, 128), (784, 512, 256), (196, 256, 1024), (196, 1024, 256), (196, 1024, 512),
+                (49, 512, 2048), (49, 2048, 512)]
+
+
+def conv1x1_probe(args):
+    """Device times of the channels-last 1x1 convolution kernels (forward,
+    dgrad, wgrad with its ordered reduce) on ResNet-50's stride-1 shapes at
+    ``--batch``, beside ATen's CUDA library kernels for the same convolution
+    (``--conv1x1-probe``).  CUDA tensors and the C ABI only; nothing is
+    registered.  FLOPs per direction 2*P*Cin*Cout."""
+    from xdna_train import _abi
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    st = torch.cuda.current_stream()
+    b = args.batch
+    cl = torch.channels_last
+
+    reps = 20
+
+    def med(fn):
+        # `reps` calls back to back per timed region, so that the host-side
+        # cost of each call overlaps the device work of the previous ones
+        ts = []
+        for i in range(args.iters + 3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1) / reps)
+        return sorted(ts)[len(ts) // 2]
+
+    rows = []
+    shapes = RESNET50_1X1 if args.shape_index < 0 else [RESNET50_1X1[args.shape_index]]
+    for hw2, cin, cout in shapes:
+        hw = int(round(hw2 ** 0.5))
+        x = torch.randn(b, cin, hw, hw, dtype=torch.bfloat16, device=dev).contiguous(memory_format=cl)
+        w = torch.randn(cout, cin, 1, 1, dtype=torch.bfloat16, device=dev)
+        dy = torch.randn(b, cout, hw, hw, dtype=torch.bfloat16, device=dev).contiguous(memory_format=cl)
+        y = torch.empty_like(dy)
+        dx = torch.empty_like(x)
+        dw = torch.empty(cout, cin, dtype=torch.float32, device=dev)
+        wsb = _abi.lib().b2_conv1x1_wgrad_workspace_bytes(1, b, cin, hw2, cout)
+        ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev)
+        s = st.cuda_stream
+        ours = {
+            "fwd": med(lambda: _abi.call("b2_conv1x1_fwd", x.data_ptr(), w.data_ptr(), None, y.data_ptr(), 1, b, cin,
+                                         hw2, cout, s)),
+            "dgrad": med(lambda: _abi.call("b2_conv1x1_dgrad", dy.data_ptr(), w.data_ptr(), dx.data_ptr(), 1, b, cin,
+                                           hw2, cout, s)),
+            "wgrad": med(lambda: _abi.call("b2_conv1x1_wgrad", dy.data_ptr(), x.data_ptr(), dw.data_ptr(),
+                                           _abi.B2_F32, 1, b, cin, hw2, cout, ws.data_ptr(), wsb, s)),
+        }
+        ref = torch.nn.functional.conv2d(x, w)
+        yo = ref.float()
+        lib = {
+            "fwd": med(lambda: torch.nn.functional.conv2d(x, w)),
+            "dgrad": med(lambda: torch.ops.aten.convolution_backward(dy, x, w, None, [1, 1], [0, 0], [1, 1], False,
+                                                                     [0, 0], 1, [True, False, False])),
+            "wgrad": med(lambda: torch.ops.aten.convolution_backward(dy, x, w, None, [1, 1], [0, 0], [1, 1], False,
+                                                                     [0, 0], 1, [False, True, False])),
+        }
+        # the forward against the library's, as a sanity check of the timed call
+        _abi.call("b2_conv1x1_fwd", x.data_ptr(), w.data_ptr(), None, y.data_ptr(), 1, b, cin, hw2, cout, s)
+        err = ((y.float() - yo).abs().max() / yo.abs().max().clamp_min(1e-6)).item()
+        fl = 2.0 * b * hw2 * cin * cout
+        row = {"shape": f"P{b * hw2} Cin{cin} Cout{cout}", "fwd_rel_err": round(err, 5)}
+        for k in ("fwd", "dgrad", "wgrad"):
+            row[k] = {"ours_us": round(ours[k] * 1e3, 1), "lib_us": round(lib[k] * 1e3, 1),
+                      "ours_tflops": round(fl / (ours[k] * 1e-3) / 1e12, 1)}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+    tot_o = sum(r[k]["ours_us"] for r in rows for k in ("fwd", "dgrad", "wgrad"))
+    tot_l = sum(r[k]["lib_us"] for r in rows for k in ("fwd", "dgrad", "wgrad"))
+    print(json.dumps({"probe": f"conv1x1 channels-last B{b}", "ours_us_total": round(tot_o, 1),
+                      "lib_us_total": round(tot_l, 1)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
+    ap.add_argument("--conv1x1-probe", action="store_true")
+    ap.add_argument("--shape-index", type=int, default=-1, help="--conv1x1-probe: one shape of the list")
     ap.add_argument("--bn-probe", action="store_true")
     ap.add_argument("--adam-probe", action="store_true")
     ap.add_argument("--adam-bf16", action="store_true")
@@ -805,6 +889,9 @@ def main():
         return
     if args.bn_probe:
         bn_probe(args)
+        return
+    if args.conv1x1_probe:
+        conv1x1_probe(args)
         return
     if args.adam_probe:
         adam_probe(args)

@@ -61,6 +61,7 @@ struct Params {
   int a_bcast;       // A has one batch slice, shared by every batch
   int kb_per_batch;  // > 0: the reduction runs over the batch slices too (k-block kb is in slice kb / kb_per_batch)
   int gemm_split;    // 1: tile-space slices are split-K ranges writing fp32 partials
+  int tma_store;     // GEMM: bf16 D written by TMA stores of shared-memory staged boxes
 };
 
 template <int BN>
@@ -68,6 +69,23 @@ struct Smem {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
 };
+
+// GEMM output staging: per epilogue warp two 32-row bf16 boxes, one filled
+// while the TMA store of the other reads it.  Boxes are 64 columns wide
+// (128-byte rows, 128-byte swizzle) when the warp's half of the tile has 64
+// or more columns, else 32 (64-byte rows, 64-byte swizzle).
+template <int BN>
+constexpr int epi_box_cols() {
+  return BN >= 128 ? 64 : 32;
+}
+template <int BN>
+constexpr int epi_box_bytes() {
+  return 32 * epi_box_cols<BN>() * 2;
+}
+template <int KIND, int BN>
+constexpr int epi_stage_bytes() {
+  return KIND == kGemm ? kEpiWarps * 2 * epi_box_bytes<BN>() : 0;
+}
 
 __device__ __forceinline__ void decode_tile(int kind, const Params& p, int t, int& mt, int& nt,
                                             int& bz, int& tap, int& kb0, int& kb1) {
@@ -143,14 +161,22 @@ __device__ __forceinline__ uint16_t* conv_row_base(const Params& p, int mt, int 
 __device__ __forceinline__ void epi_conv(const Params& p, uint16_t* base, int col0, int lane,
                                          const uint32_t (&r)[32]) {
   const bool full = col0 + 32 <= p.N;
-  float bl = 0.f;
-  if (p.bias && col0 + lane < p.N) bl = bf2f(p.bias[col0 + lane]);
   float v[32];
+  // uniform branches outside the element loops (see gemm_values); without a
+  // bias the accumulator still gets + 0.0f, which turns a -0 sum into +0 as
+  // an accumulation that starts from zero does
+  if (p.bias) {
+    float bl = 0.f;
+    if (col0 + lane < p.N) bl = bf2f(p.bias[col0 + lane]);
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    float a = __uint_as_float(r[c]) + __shfl_sync(0xffffffffu, bl, c);
-    if (p.relu) a = fmaxf(a, 0.f);
-    v[c] = a;
+    for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]) + __shfl_sync(0xffffffffu, bl, c);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]) + 0.f;
+  }
+  if (p.relu) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) v[c] = fmaxf(v[c], 0.f);
   }
   if (!base) return;
   if (p.osc == 1 && full && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
@@ -203,26 +229,40 @@ __device__ __forceinline__ float load_c(const Params& p, long long i) {
                                : bf2f(static_cast<const uint16_t*>(p.cin)[i]);
 }
 
-__device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int col0, int row, int lane,
-                                         const uint32_t (&r)[32]) {
-  const int m = mt * BM + row;
-  float v[32];
-  if (p.beta != 0.f && p.c_sm == 0) {
+// alpha * acc + beta * C for columns [col0, col0+32) of output row m
+__device__ __forceinline__ void gemm_values(const Params& p, int bz, int m, int col0, int lane,
+                                            const uint32_t (&r)[32], float (&v)[32]) {
+  // Branch once on the uniform parameters: a per-element test would be
+  // compiled into 32 predicated address computations and loads that cost
+  // more than the rest of the epilogue even when beta is 0.
+  const float alpha = p.alpha, beta = p.beta;
+  if (beta == 0.f) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) v[c] = alpha * __uint_as_float(r[c]);
+  } else if (p.c_sm == 0) {
     // C broadcast along rows (a bias vector): one load per lane, shuffled
     float cl = 0.f;
     if (col0 + lane < p.N) cl = load_c(p, bz * p.c_sb + (long long)(col0 + lane) * p.c_sn);
 #pragma unroll
     for (int c = 0; c < 32; ++c)
-      v[c] = p.alpha * __uint_as_float(r[c]) + p.beta * __shfl_sync(0xffffffffu, cl, c);
+      v[c] = alpha * __uint_as_float(r[c]) + beta * __shfl_sync(0xffffffffu, cl, c);
   } else {
+    const bool row_ok = m < p.M;
+    const long long base = bz * p.c_sb + (long long)m * p.c_sm;
 #pragma unroll
     for (int c = 0; c < 32; ++c) {
-      float a = p.alpha * __uint_as_float(r[c]);
-      if (p.beta != 0.f && m < p.M && col0 + c < p.N)
-        a += p.beta * load_c(p, bz * p.c_sb + (long long)m * p.c_sm + (long long)(col0 + c) * p.c_sn);
+      float a = alpha * __uint_as_float(r[c]);
+      if (row_ok && col0 + c < p.N) a += beta * load_c(p, base + (long long)(col0 + c) * p.c_sn);
       v[c] = a;
     }
   }
+}
+
+__device__ __forceinline__ void epi_gemm(const Params& p, int bz, int mt, int col0, int row, int lane,
+                                         const uint32_t (&r)[32]) {
+  const int m = mt * BM + row;
+  float v[32];
+  gemm_values(p, bz, m, col0, lane, r, v);
   if (m >= p.M) return;
   uint16_t* base = static_cast<uint16_t*>(p.out) + bz * p.osn + (long long)m * p.osh;
   if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(base + col0) & 15) == 0)) {
@@ -262,7 +302,8 @@ __device__ __forceinline__ void epi_gemm_partial(const Params& p, int split, int
 template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                 const __grid_constant__ CUtensorMap tma_b, const Params p) {
+                 const __grid_constant__ CUtensorMap tma_b,
+                 const __grid_constant__ CUtensorMap tma_d, const Params p) {
   constexpr int kStageBytes = Smem<BN>::kStageBytes;
   constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, A_MN, B_MN);
   constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered accumulator
@@ -270,7 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint8_t* epi_stage = smem + STAGES * kStageBytes;  // 1024-aligned: stage sizes are KB multiples
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + epi_stage_bytes<KIND, BN>());
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -437,6 +479,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kChunks = BN / 64;  // 32-column chunks per half
     int acc = 0;
     uint32_t acc_phase = 0;
+    constexpr int kBoxCols = epi_box_cols<BN>();
+    constexpr int kBoxBytes = epi_box_bytes<BN>();
+    uint8_t* epi_buf = epi_stage + (warp - 2) * 2 * kBoxBytes;  // GEMM output staging of this warp
+    int epi_sel = 0;
+    (void)epi_buf;
+    (void)epi_sel;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
       int mt, nt, bz, tap, kb0, kb1;
       decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
@@ -448,6 +496,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
+      if (KIND == kGemm && p.tma_store) {
+        // Stage each 32-row box of the warp's columns in shared memory (the
+        // swizzle puts 16-byte chunk q of row `lane` at chunk q ^ (lane & 7)
+        // for 128-byte rows, q ^ ((lane >> 1) & 3) for 64-byte rows, so the
+        // eight rows of each store phase hit distinct banks) and let the TMA
+        // unit write it out in whole rows; rows past M / columns past N are
+        // clipped by the tensor map.
+        constexpr int kSub = kBoxCols / 32;
+#pragma unroll 1
+        for (int j = 0; j < (BN / 2) / kBoxCols; ++j) {
+          const int c0 = nt * BN + half * (BN / 2) + j * kBoxCols;
+          uint32_t r[kSub][32];
+#pragma unroll
+          for (int u = 0; u < kSub; ++u) tmem_ld32(taddr + j * kBoxCols + u * 32, r[u]);
+          tc_wait_ld();
+          uint32_t packed[kBoxCols / 2];
+#pragma unroll
+          for (int u = 0; u < kSub; ++u) {
+            float v[32];
+            gemm_values(p, bz, mt * BM + row, c0 + u * 32, lane, r[u], v);
+#pragma unroll
+            for (int c = 0; c < 16; ++c) packed[u * 16 + c] = cvt2(v[2 * c], v[2 * c + 1]);
+          }
+          if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+          __syncwarp();
+          uint8_t* buf = epi_buf + epi_sel * kBoxBytes;
+#pragma unroll
+          for (int q = 0; q < kBoxCols / 8; ++q) {
+            const int phys = kBoxCols == 64 ? (q ^ (lane & 7)) : (q ^ ((lane >> 1) & 3));
+            *reinterpret_cast<uint4*>(buf + lane * (kBoxCols * 2) + (phys << 4)) =
+                make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tma_d, smem_u32(buf), c0, mt * BM + quarter * 32, bz);
+            bulk_commit();
+          }
+          epi_sel ^= 1;
+        }
+      } else {
 #pragma unroll 1
       for (int j = 0; j < kChunks; ++j) {
         uint32_t r[32];
@@ -464,11 +553,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_gemm(p, bz, mt, col0, row, lane, r);
         }
       }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+    }
+    if constexpr (KIND == kGemm) {
+      if (lane == 0) bulk_wait_all();  // stores done before the CTA's shared memory goes away
+      __syncwarp();
     }
   }
 
@@ -761,16 +855,17 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw,
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KIND>
 constexpr size_t smem_bytes() {
-  return size_t(STAGES) * Smem<BN>::kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  return size_t(STAGES) * Smem<BN>::kStageBytes + epi_stage_bytes<KIND, BN>() + 1024 /*align*/ + 256 /*barriers*/;
 }
 
 template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
 b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles,
-                 cudaStream_t st) {
+                 cudaStream_t st, const CUtensorMap* td = nullptr) {
   auto kern = igemm_kernel<BN, STAGES, KIND, A_MN, B_MN>;
-  constexpr size_t smem = smem_bytes<BN, STAGES>();
+  constexpr size_t smem = smem_bytes<BN, STAGES, KIND>();
+  static_assert(smem <= 232448, "shared memory per block");
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   static bool configured[64] = {};
@@ -782,13 +877,18 @@ b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   }
   if (tiles <= 0) return B2_OK;
   const int grid = std::min(tiles, sm_count(dev));
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, p);
+  static const CUtensorMap kNoMap{};  // kinds without a TMA store never read it
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, td ? *td : kNoMap, p);
   return check_cuda(cudaGetLastError(), "igemm launch");
 }
 
 constexpr int kStages64 = 8;
 constexpr int kStages128 = 6;
 constexpr int kStages256 = 4;
+// the GEMM kind gives up operand stages for its output staging
+constexpr int kGemmStages64 = 8;
+constexpr int kGemmStages128 = 5;
+constexpr int kGemmStages256 = 3;
 constexpr int kStagesPair = 6;
 
 template <int KIND>
@@ -1003,24 +1103,40 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
   p.c_sn = g.c_sn;
   p.c_sb = g.c_sb;
   p.status = device_status_ptr();
+  // bf16 D through TMA stores: 32 x 32 boxes of a {N, M, batch} map (16-byte
+  // aligned base and row / slice strides; the box is clipped at M and N)
+  CUtensorMap td;
+  const CUtensorMap* tdp = nullptr;
+  if (!p.gemm_split && g.D && aligned16(g.D) && g.ldd % 8 == 0 && g.ldd >= g.N &&
+      (p.batch <= 1 || g.strideD % 8 == 0)) {
+    const uint64_t nb = uint64_t(std::max(1, p.batch));
+    const uint64_t dims[3] = {uint64_t(g.N), uint64_t(g.M), nb};
+    const uint64_t strides[2] = {uint64_t(g.ldd) * 2, uint64_t(nb > 1 ? g.strideD : g.ldd * g.M) * 2};
+    const uint32_t bc = BN >= 128 ? 64 : 32;  // epi_box_cols<BN>()
+    const uint32_t box[3] = {bc, 32, 1};
+    if (encode_tmap_sw(&td, g.D, 3, dims, strides, box, int(bc * 2)) == B2_OK) {
+      tdp = &td;
+      p.tma_store = 1;
+    }
+  }
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const bool amn = g.transA != 0, bmn = g.transB == 0;
   b2_status rc;
   if (BN == 256) {
-    if (!amn && !bmn) rc = launch<256, kStages256, kGemm, false, false>(ta, tb, p, tiles, st);
-    else if (!amn && bmn) rc = launch<256, kStages256, kGemm, false, true>(ta, tb, p, tiles, st);
-    else if (amn && !bmn) rc = launch<256, kStages256, kGemm, true, false>(ta, tb, p, tiles, st);
-    else rc = launch<256, kStages256, kGemm, true, true>(ta, tb, p, tiles, st);
+    if (!amn && !bmn) rc = launch<256, kGemmStages256, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
+    else if (!amn && bmn) rc = launch<256, kGemmStages256, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
+    else if (amn && !bmn) rc = launch<256, kGemmStages256, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
+    else rc = launch<256, kGemmStages256, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
   } else if (BN == 128) {
-    if (!amn && !bmn) rc = launch<128, kStages128, kGemm, false, false>(ta, tb, p, tiles, st);
-    else if (!amn && bmn) rc = launch<128, kStages128, kGemm, false, true>(ta, tb, p, tiles, st);
-    else if (amn && !bmn) rc = launch<128, kStages128, kGemm, true, false>(ta, tb, p, tiles, st);
-    else rc = launch<128, kStages128, kGemm, true, true>(ta, tb, p, tiles, st);
+    if (!amn && !bmn) rc = launch<128, kGemmStages128, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
+    else if (!amn && bmn) rc = launch<128, kGemmStages128, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
+    else if (amn && !bmn) rc = launch<128, kGemmStages128, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
+    else rc = launch<128, kGemmStages128, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
   } else {
-    if (!amn && !bmn) rc = launch<64, kStages64, kGemm, false, false>(ta, tb, p, tiles, st);
-    else if (!amn && bmn) rc = launch<64, kStages64, kGemm, false, true>(ta, tb, p, tiles, st);
-    else if (amn && !bmn) rc = launch<64, kStages64, kGemm, true, false>(ta, tb, p, tiles, st);
-    else rc = launch<64, kStages64, kGemm, true, true>(ta, tb, p, tiles, st);
+    if (!amn && !bmn) rc = launch<64, kGemmStages64, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
+    else if (!amn && bmn) rc = launch<64, kGemmStages64, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
+    else if (amn && !bmn) rc = launch<64, kGemmStages64, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
+    else rc = launch<64, kGemmStages64, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
   }
   if (rc != B2_OK || !p.gemm_split || g.partial_is_d) return rc;
   const long long total = (long long)g.M * g.N;

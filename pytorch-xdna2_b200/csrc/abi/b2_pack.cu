@@ -174,6 +174,144 @@ __global__ void __launch_bounds__(kVecThreads) pack_rows_nchw_vec_kernel(
   if (rsum && tid < kCh) rsum[tid] = csum;
 }
 
+// TMA variant of the NCHW packer (W % 8 == 0, W <= 256, 16-byte strides).
+// Persistent CTAs walk work items (b, y, chunk), y fastest: the TMA unit
+// loads the 64-channel x W slab of image row y (channel-major, channels past
+// C zero-filled) into one of two input buffers while the CTA transposes the
+// other into a 128-byte-swizzled [W][64] tile, which a TMA store writes to
+// padded pixels 1..W of the row.  Threads write the two border pixels of the
+// row; extra items zero the top and bottom border rows.  With `rowsum`, the
+// per-row channel sums (fp32, x order) are left as the generic kernel does.
+constexpr int kTmaPackThreads = 256;
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+
+template <bool ROWSUM>
+__global__ void __launch_bounds__(kTmaPackThreads) pack_rows_nchw_tma_kernel(
+    const __grid_constant__ CUtensorMap tin, const __grid_constant__ CUtensorMap tout, int B, int H, int W,
+    int chunks, uint16_t* __restrict__ rows, float* __restrict__ rowsum, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tile = W * 128;  // bytes of one [W][64] bf16 tile; also of one [64][W] slab
+  uint8_t* obuf = smem;                 // 2 output tiles (1024-aligned: W % 8 == 0)
+  uint8_t* ibuf = smem + 2 * tile;      // 2 input slabs
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 4 * tile);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2);
+  const int tid = threadIdx.x;
+  const int wp = W + 2;
+  const long long cpad = (long long)chunks * kCh;
+  const long long interior = (long long)B * H * chunks;
+  const long long items = interior + 2LL * B * chunks;
+  if (tid == 0) {
+    mbar_init(smem_u32(&full[0]), 1);
+    mbar_init(smem_u32(&full[1]), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int issued = 0;  // loads issued (thread 0)
+  auto issue = [&](long long it, int s) {  // thread 0: load interior item `it` into slab s
+    ++issued;
+    const int y = int(it % H);
+    const long long r = it / H;
+    const int chunk = int(r % chunks);
+    const int b = int(r / chunks);
+    const uint32_t bar = smem_u32(&full[s]);
+    mbar_arrive_expect_tx(bar, uint32_t(tile));
+    tma_load_4d(smem_u32(ibuf + s * tile), &tin, bar, 0, y, chunk * kCh, b);
+  };
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  long long it = blockIdx.x;
+  if (tid == 0 && it < interior) issue(it, 0);
+  int i = 0;      // interior items done by this CTA
+  bool ok = true;
+  for (; it < items; it += gridDim.x) {
+    if (it >= interior) {  // a top / bottom border row: zeros (and zero row sums)
+      const long long r = it - interior;
+      const int chunk = int(r % chunks);
+      const int top = int((r / chunks) % 2);
+      const int b = int(r / (2LL * chunks));
+      const int yp = top ? 0 : H + 1;
+      uint16_t* dst = rows + ((long long)(b * (H + 2) + yp) * wp) * cpad + chunk * kCh;
+      for (int e = tid; e < wp * 8; e += kTmaPackThreads)
+        *reinterpret_cast<uint4*>(dst + (long long)(e >> 3) * cpad + (e & 7) * 8) = zero;
+      if (ROWSUM && tid < kCh) rowsum[(long long)(b * (H + 2) + yp) * cpad + chunk * kCh + tid] = 0.f;
+      continue;
+    }
+    const int s = i & 1;
+    const long long nxt = it + gridDim.x;
+    // slab s^1 was last read in the previous iteration, before its closing barrier
+    if (tid == 0 && nxt < interior) issue(nxt, s ^ 1);
+    const int y = int(it % H);
+    const long long r = it / H;
+    const int chunk = int(r % chunks);
+    const int b = int(r / chunks);
+    const long long prow = (long long)b * (H + 2) + y + 1;
+    uint16_t* dst = rows + prow * wp * cpad + chunk * kCh;
+    if (tid < 16) *reinterpret_cast<uint4*>(dst + (long long)(tid < 8 ? 0 : W + 1) * cpad + (tid & 7) * 8) = zero;
+    if (tid == 0) bulk_wait_read<1>();  // the store issued two items ago has read tile s
+    ok = mbar_wait(smem_u32(&full[s]), uint32_t((i >> 1) & 1), status, abort_flag);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    const uint32_t* in32 = reinterpret_cast<const uint32_t*>(ibuf + s * tile);
+    uint8_t* out = obuf + s * tile;
+    const int half = W >> 1;  // pixel pairs
+    for (int e = tid; e < half * 8; e += kTmaPackThreads) {
+      const int pp = e % half, v = e / half;  // lanes walk pixel pairs: conflict-free slab reads
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = in32[(v * 8 + k) * half + pp];
+      uint4 lo, hi;
+      lo.x = __byte_perm(w[0], w[1], 0x5410);
+      lo.y = __byte_perm(w[2], w[3], 0x5410);
+      lo.z = __byte_perm(w[4], w[5], 0x5410);
+      lo.w = __byte_perm(w[6], w[7], 0x5410);
+      hi.x = __byte_perm(w[0], w[1], 0x7632);
+      hi.y = __byte_perm(w[2], w[3], 0x7632);
+      hi.z = __byte_perm(w[4], w[5], 0x7632);
+      hi.w = __byte_perm(w[6], w[7], 0x7632);
+      const int px = 2 * pp;  // 128-byte swizzle: chunk v of pixel px at v ^ (px & 7)
+      *reinterpret_cast<uint4*>(out + px * 128 + ((v ^ (px & 7)) << 4)) = lo;
+      *reinterpret_cast<uint4*>(out + (px + 1) * 128 + ((v ^ ((px + 1) & 7)) << 4)) = hi;
+    }
+    if (ROWSUM && tid < kCh) {  // channel tid of this row, in x order
+      const uint32_t* t = in32 + tid * half;
+      float csum = 0.f;
+      for (int q = 0; q < half; ++q) {
+        const uint32_t v = t[q];
+        csum += __uint_as_float(v << 16);
+        csum += __uint_as_float(v & 0xffff0000u);
+      }
+      rowsum[prow * cpad + chunk * kCh + tid] = csum;
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tma_store_2d(&tout, smem_u32(out), chunk * kCh, int(prow * wp + 1));
+      bulk_commit();
+    }
+    ++i;
+  }
+  if (!ok && tid == 0) {
+    // loads i .. issued-1 may still be in flight into this CTA's shared memory: let them land
+    for (int q = i; q < issued; ++q) mbar_wait(smem_u32(&full[q & 1]), uint32_t((q >> 1) & 1), status, nullptr);
+  }
+  if (tid == 0) bulk_wait_all();
+}
+
 // Channel sums, stage 1: out[g][c] = sum of rows [64g, 64g+64) of in[.][c]
 // (in = per-row sums from the packer, or the packed rows themselves).
 template <typename T>
@@ -349,6 +487,44 @@ b2_status b2_pack_rows_dbias_bf16(const void* x, int64_t sn, int64_t sc, int64_t
   return check_cuda(cudaGetLastError(), "channel-sum launch");
 }
 
+// TMA packer launch (see pack_rows_nchw_tma_kernel); B2_ERR_UNSUPPORTED when
+// the tensor maps cannot describe the operands, so the caller takes the
+// generic kernel.
+static b2_status pack_rows_nchw_tma(const void* x, int64_t sn, int64_t sc, int64_t sh, int B, int C, int H, int W,
+                                   int chunks, void* rows, float* rowsum, cudaStream_t st) {
+  if ((sh * 2) % 16 || (sc * 2) % 16 || (sn * 2) % 16 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return B2_ERR_UNSUPPORTED;
+  const long long cpad = (long long)chunks * kCh;
+  const long long npix = (long long)B * (H + 2) * (W + 2);
+  CUtensorMap tin, tout;
+  {
+    const uint64_t dims[4] = {uint64_t(W), uint64_t(H), uint64_t(C), uint64_t(B)};
+    const uint64_t strides[3] = {uint64_t(sh) * 2, uint64_t(sc) * 2, uint64_t(sn) * 2};
+    const uint32_t box[4] = {uint32_t(W), 1, uint32_t(kCh), 1};
+    if (encode_tmap_sw(&tin, x, 4, dims, strides, box, 0) != B2_OK) return B2_ERR_UNSUPPORTED;
+  }
+  {
+    const uint64_t dims[2] = {uint64_t(cpad), uint64_t(npix)};
+    const uint64_t strides[1] = {uint64_t(cpad) * 2};
+    const uint32_t box[2] = {uint32_t(kCh), uint32_t(W)};
+    if (encode_tmap_sw(&tout, rows, 2, dims, strides, box, 128) != B2_OK) return B2_ERR_UNSUPPORTED;
+  }
+  const size_t smem = size_t(4) * W * 128 + 64 + 1024;
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  auto kern = rowsum ? pack_rows_nchw_tma_kernel<true> : pack_rows_nchw_tma_kernel<false>;
+  B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                    "cudaFuncSetAttribute(pack smem)"));
+  int per_sm = 0;
+  B2_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTmaPackThreads, smem),
+                    "pack occupancy"));
+  const long long items = (long long)B * H * chunks + 2LL * B * chunks;
+  const int grid = int(std::max<long long>(1, std::min<long long>(items, (long long)std::max(1, per_sm) * sm_count(dev))));
+  kern<<<grid, kTmaPackThreads, smem, st>>>(tin, tout, B, H, W, chunks, static_cast<uint16_t*>(rows), rowsum,
+                                             device_status_ptr());
+  return check_cuda(cudaGetLastError(), "pack_rows(nchw tma) launch");
+}
+
 static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B, int C, int H,
                                 int W, int chunks, void* rows, float* rowsum, void* stream) {
   if (!x || !rows) return set_error(B2_ERR_INVALID, "b2_pack_rows_bf16: null pointer");
@@ -361,6 +537,10 @@ static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t s
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
   const int vw = nchw_vec_width(x, sn, sc, sh, sw, W);  // widest vector the strides and base allow
+  if (vw == 8 && W <= 256 && H > 0) {
+    b2_status rc = pack_rows_nchw_tma(x, sn, sc, sh, B, C, H, W, chunks, rows, rowsum, st);
+    if (rc != B2_ERR_UNSUPPORTED) return rc;
+  }
   if (vw) {
     const int seg = std::min(W, kMaxSeg);
     int pitch = seg / 2;

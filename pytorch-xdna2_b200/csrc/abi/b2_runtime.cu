@@ -70,6 +70,11 @@ int sm_count(int device) {
 
 b2_status encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                       const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  return encode_tmap_sw(map, base, rank, dims, strides_bytes, box, swizzle128 ? 128 : 0);
+}
+
+b2_status encode_tmap_sw(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_encode) {
@@ -100,7 +105,9 @@ b2_status encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64
   }
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), gdim,
                         gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(B2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return B2_OK;

@@ -64,7 +64,11 @@ def wk_of(w: torch.Tensor, dgrad=False) -> torch.Tensor:
 # --------------------------------------------------------------------- packers
 
 @pytest.mark.parametrize("shape", [(2, 70, 5, 7), (1, 3, 4, 4), (3, 64, 6, 9), (2, 130, 3, 11), (1, 64, 2, 150),
-                                   (2, 64, 5, 36), (2, 96, 3, 18), (1, 70, 3, 264), (2, 128, 4, 72)])
+                                   (2, 64, 5, 36), (2, 96, 3, 18), (1, 70, 3, 264), (2, 128, 4, 72),
+                                   # W % 8 == 0, W <= 256: the TMA packer (ragged channel chunks, one row,
+                                   # W = 256, several work items per CTA)
+                                   (2, 70, 5, 16), (3, 130, 4, 8), (2, 64, 1, 8), (1, 64, 3, 256),
+                                   (8, 200, 40, 72)])
 @pytest.mark.parametrize("channels_last", [False, True])
 def test_pack_rows_bit_exact(cuda, shape, channels_last):
     g = torch.Generator().manual_seed(0)
@@ -77,7 +81,8 @@ def test_pack_rows_bit_exact(cuda, shape, channels_last):
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("shape", [(4, 256, 9, 72), (2, 70, 5, 36), (3, 64, 6, 9), (2, 130, 7, 18)])
+@pytest.mark.parametrize("shape", [(4, 256, 9, 72), (2, 70, 5, 36), (3, 64, 6, 9), (2, 130, 7, 18), (2, 70, 5, 24),
+                                   (6, 130, 30, 64)])
 @pytest.mark.parametrize("channels_last", [False, True])
 def test_pack_rows_dbias(cuda, shape, channels_last):
     """Packed rows bit-exact, plus dbias = sum over (b, y, x) (fixed-order fp32 sums)."""
