@@ -299,6 +299,30 @@ b2_status b2_unpack_weight_khwc(const float* dwk, int64_t Cout, int64_t Cin,
                                 int kh, int kw, int64_t Kp, void* dw,
                                 int dtype, void* stream);
 
+/* ---- direct convolutions for layers with few output channels (an RGB
+ * output layer; the reference's CPU path, torch_xdna_device.cpp:4578-4605,
+ * 4828-4878), on the CUDA cores:
+ *   out[b][o][y][x] = bias[o] + sum_{i,ky,kx} in[b][i][y*sy-py+ky*dy][x*sx-px+kx*dx] * wt[i][ky][kx][o]
+ * in fp32 in (i, ky, kx) order, rounded once to bf16; at most 64 output
+ * channels.  wt comes from b2_direct_conv_weight: the forward's
+ * (wt[ci][ky][kx][co] = W[co][ci][ky][kx]) or, with dgrad = 1, the input
+ * gradient's of a stride-1 convolution (wt[co][ky][kx][ci] =
+ * W[co][ci][kh-1-ky][kw-1-kx]; run over dY with padding (k-1)*d - p), output
+ * channels padded to 4/8/16/32/64 with zeros.  Tensors through element
+ * strides [n, c, h, w]; bias (bf16, NOUT values) may be null. */
+size_t b2_direct_conv_weight_floats(int64_t Cout, int64_t Cin, int kh, int kw,
+                                    int dgrad);
+b2_status b2_direct_conv_weight(const void* w, int64_t Cout, int64_t Cin,
+                                int kh, int kw, int dgrad, float* wt,
+                                void* stream);
+b2_status b2_direct_conv_bf16(const void* in, const int64_t* in_strides,
+                              int64_t B, int64_t NIN, int64_t Hin, int64_t Win,
+                              const float* wt, int kh, int kw, int sy, int sx,
+                              int py, int px, int dy, int dx, const void* bias,
+                              void* out, const int64_t* out_strides,
+                              int64_t NOUT, int64_t Ho, int64_t Wo,
+                              void* stream);
+
 /* ---- 2-D max pooling with indices (the reference runs it on its CPU path;
  * the same results as ATen): windows scanned in (kh, kw) order, a value
  * replaces the maximum when greater or NaN, index h*W + w within the plane

@@ -199,22 +199,46 @@ __global__ void __launch_bounds__(kBnThreads) bn_plane_stats_kernel(
 
 // One thread per channel: Chan's merge of the N plane statistics in double,
 // in plane order; mean / invstd out; running statistics.
+// Channel statistics from the per-plane (mean, M2) partials: a warp per
+// channel, lane l merging planes l, l+32, ... in order (Chan's parallel
+// update, in double), then the lanes merged by a fixed shuffle tree --
+// deterministic, and N-fold shorter dependent chains than one thread per
+// channel walking all N planes.
+__device__ __forceinline__ void chan_merge(double& n, double& mean, double& m2, double nb, double mb, double m2b) {
+  if (nb == 0.0) return;
+  if (n == 0.0) {
+    n = nb;
+    mean = mb;
+    m2 = m2b;
+    return;
+  }
+  const double tot = n + nb;
+  const double delta = mb - mean;
+  mean += delta * nb / tot;
+  m2 += m2b + delta * delta * n * nb / tot;
+  n = tot;
+}
+
 __global__ void bn_channel_stats_kernel(const float* __restrict__ pm, const float* __restrict__ pq,
                                         long long N, long long C, long long hw, float eps, float momentum,
                                         BnChan ch, float* __restrict__ mean_out, float* __restrict__ invstd_out) {
-  const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long c = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
   if (c >= C) return;
   const double nb = double(hw);
   double count = 0.0, mean = 0.0, m2 = 0.0;
-  for (long long n = 0; n < N; ++n) {
-    const double tot = count + nb;
-    const double delta = double(pm[n * C + c]) - mean;
-    mean += delta * nb / tot;
-    m2 += double(pq[n * C + c]) + delta * delta * count * nb / tot;
-    count = tot;
+  for (long long n = lane; n < N; n += 32) chan_merge(count, mean, m2, nb, double(pm[n * C + c]), double(pq[n * C + c]));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const double ob = __shfl_down_sync(0xffffffffu, count, off);
+    const double om = __shfl_down_sync(0xffffffffu, mean, off);
+    const double oq = __shfl_down_sync(0xffffffffu, m2, off);
+    chan_merge(count, mean, m2, ob, om, oq);
   }
-  const double M = double(N) * nb;
-  finish_stats(c, mean, m2 / M, M, eps, momentum, ch, mean_out, invstd_out);
+  if (lane == 0) {
+    const double M = double(N) * nb;
+    finish_stats(c, mean, m2 / M, M, eps, momentum, ch, mean_out, invstd_out);
+  }
 }
 
 // y = act(x*scale + shift); one thread per 8 elements (VEC) or per element.
@@ -770,8 +794,8 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
   else if (vec) bn_plane_stats_kernel<kBnThreads, true><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
   else bn_plane_stats_kernel<kBnThreads, false><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
   B2_TRY(check_cuda(cudaGetLastError(), "bn stats launch"));
-  bn_channel_stats_kernel<<<int((C + 127) / 128), 128, 0, st>>>(pm, pq, N, C, HW, eps, momentum, ch, mean_out,
-                                                                invstd_out);
+  bn_channel_stats_kernel<<<int((C + 3) / 4), 128, 0, st>>>(pm, pq, N, C, HW, eps, momentum, ch, mean_out,
+                                                            invstd_out);
   B2_TRY(check_cuda(cudaGetLastError(), "bn channel launch"));
   if (vec) {
     const long long units = planes * (HW / 8);

@@ -13,70 +13,63 @@
 namespace b2 {
 namespace {
 
-constexpr int kPix = 64;  // pixels per tile
 constexpr int kCh = 64;   // channels per tile (one chunk)
 
-// One CTA writes one padded grid row (b, yp) for one 64-channel chunk:
-// (W+2) pixels x 64 channels, 128 bytes per pixel.
+// Generic strided packer: one thread per 16-byte output vector (8 channels of
+// one padded pixel), threads of a warp on consecutive pixels of the same
+// channel group, so each of a thread's 8 element loads is coalesced across
+// the warp whenever pixels are the contiguous axis.  No shared memory and a
+// thread per vector: small images (9 x 9 planes, ragged widths) get a full
+// grid.  Border pixels are the trailing index range.
 __global__ void __launch_bounds__(256) pack_rows_kernel(const uint16_t* __restrict__ x, long long sn,
                                                         long long sc, long long sh, long long sw,
                                                         int B, int C, int H, int W, int chunks,
                                                         uint16_t* __restrict__ rows) {
-  __shared__ uint16_t tile[kCh][kPix + 2];
-  const int chunk = blockIdx.x % chunks;
-  const int yp = (blockIdx.x / chunks) % (H + 2);
-  const int b = blockIdx.x / (chunks * (H + 2));
   const int wp = W + 2;
   const long long cpad = (long long)chunks * kCh;
-  uint16_t* dst_row = rows + ((long long)(b * (H + 2) + yp) * wp) * cpad + chunk * kCh;
-  const int tid = threadIdx.x;
-  if (yp == 0 || yp == H + 1) {
-    // border row: all zeros
-    for (int e = tid; e < wp * 8; e += 256) {
-      const int px = e >> 3, v = e & 7;
-      *reinterpret_cast<uint4*>(dst_row + px * cpad + v * 8) = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
-  const int y = yp - 1;
-  if (tid < 16) {  // left and right border pixels
-    const int px = (tid < 8) ? 0 : W + 1;
-    *reinterpret_cast<uint4*>(dst_row + px * cpad + (tid & 7) * 8) = make_uint4(0, 0, 0, 0);
-  }
-  const uint16_t* src = x + b * sn + y * sh + (long long)(chunk * kCh) * sc;
-  const bool x_fast = (sw == 1);  // NCHW-like: pixels contiguous
-  for (int x0 = 0; x0 < W; x0 += kPix) {
-    __syncthreads();
-    // load [64 ch][64 px]
-    for (int i = 0; i < (kCh * kPix) / 256; ++i) {
-      const int e = i * 256 + tid;
-      int c, px;
-      if (x_fast) {
-        c = e / kPix;
-        px = e % kPix;
-      } else {
-        px = e / kCh;
-        c = e % kCh;
+  const int hw = H * W;
+  const int groups = chunks * 8;  // 8-channel groups per pixel
+  const long long interior = (long long)B * groups * hw;
+  const int nb = 2 * wp + 2 * H;  // border pixels per image
+  const long long total = interior + (long long)B * nb * groups;
+  for (long long u = (long long)blockIdx.x * 256 + threadIdx.x; u < total; u += (long long)gridDim.x * 256) {
+    if (u < interior) {
+      const int p = int(u % hw);
+      const long long r = u / hw;
+      const int g = int(r % groups);
+      const int b = int(r / groups);
+      const int y = p / W, xx = p - y * W;
+      const int c0 = g * 8;
+      const uint16_t* src = x + b * sn + (long long)y * sh + (long long)xx * sw + (long long)c0 * sc;
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t lo = c0 + 2 * k < C ? src[(long long)(2 * k) * sc] : 0u;
+        const uint32_t hi = c0 + 2 * k + 1 < C ? src[(long long)(2 * k + 1) * sc] : 0u;
+        w[k] = lo | (hi << 16);
       }
-      const int xx = x0 + px;
-      const int cc = chunk * kCh + c;
-      uint16_t v = 0;
-      if (xx < W && cc < C) v = src[(long long)c * sc + (long long)xx * sw];
-      tile[c][px] = v;
-    }
-    __syncthreads();
-    // store: pixel-major, 8 x 16 B per pixel
-    for (int i = 0; i < (kCh * kPix / 8) / 256; ++i) {
-      const int e = i * 256 + tid;
-      const int px = e >> 3, v = e & 7;
-      const int xx = x0 + px;
-      if (xx >= W) continue;
-      uint4 w;
-      w.x = uint32_t(tile[v * 8 + 0][px]) | (uint32_t(tile[v * 8 + 1][px]) << 16);
-      w.y = uint32_t(tile[v * 8 + 2][px]) | (uint32_t(tile[v * 8 + 3][px]) << 16);
-      w.z = uint32_t(tile[v * 8 + 4][px]) | (uint32_t(tile[v * 8 + 5][px]) << 16);
-      w.w = uint32_t(tile[v * 8 + 6][px]) | (uint32_t(tile[v * 8 + 7][px]) << 16);
-      *reinterpret_cast<uint4*>(dst_row + (long long)(xx + 1) * cpad + v * 8) = w;
+      *reinterpret_cast<uint4*>(rows + (((long long)b * (H + 2) + y + 1) * wp + xx + 1) * cpad + c0) =
+          make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      const long long v = u - interior;
+      const int g = int(v % groups);
+      const long long r = v / groups;
+      const int k = int(r % nb);
+      const int b = int(r / nb);
+      int yp, xp;
+      if (k < wp) {
+        yp = 0;
+        xp = k;
+      } else if (k < 2 * wp) {
+        yp = H + 1;
+        xp = k - wp;
+      } else {
+        const int j = k - 2 * wp;
+        yp = 1 + (j >> 1);
+        xp = (j & 1) ? W + 1 : 0;
+      }
+      *reinterpret_cast<uint4*>(rows + (((long long)b * (H + 2) + yp) * wp + xp) * cpad + g * 8) =
+          make_uint4(0, 0, 0, 0);
     }
   }
 }
@@ -566,8 +559,13 @@ static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t s
                                                     static_cast<uint16_t*>(rows));
     return check_cuda(cudaGetLastError(), "pack_rows(nhwc) launch");
   }
-  pack_rows_kernel<<<unsigned(blocks), 256, 0, st>>>(
-      static_cast<const uint16_t*>(x), sn, sc, sh, sw, B, C, H, W, chunks, static_cast<uint16_t*>(rows));
+  if ((long long)H * W >= (1LL << 31)) return set_error(B2_ERR_UNSUPPORTED, "b2_pack_rows_bf16: too large");
+  const long long vecs = (long long)B * chunks * 8 * ((long long)H * W + 2LL * (W + 2) + 2LL * H);
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const int grid = int(std::max<long long>(1, std::min<long long>((vecs + 255) / 256, (long long)sm_count(dev) * 16)));
+  pack_rows_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(x), sn, sc, sh, sw, B, C, H, W, chunks,
+                                         static_cast<uint16_t*>(rows));
   return check_cuda(cudaGetLastError(), "pack_rows launch");
 }
 

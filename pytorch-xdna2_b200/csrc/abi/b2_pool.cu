@@ -45,44 +45,50 @@ __device__ __forceinline__ void stf(T* p, long long i, float v) {
 }
 
 // first valid tap of a window start (may be negative) and its end (exclusive)
-__device__ __forceinline__ void window(long long o, int s, int p, int k, int d, long long n, long long& beg,
-                                       long long& end) {
+template <typename I>
+__device__ __forceinline__ void window(I o, int s, int p, int k, int d, I n, I& beg, I& end) {
   beg = o * s - p;
-  end = min(beg + (long long)(k - 1) * d + 1, n);
+  end = min(beg + I(k - 1) * d + 1, n);
   while (beg < 0) beg += d;
 }
 
 // output positions whose window can cover input position i: [lo, hi)
-__device__ __forceinline__ void covering(long long i, int s, int p, int k, int d, long long on, long long& lo,
-                                         long long& hi) {
-  const long long span = (long long)(k - 1) * d + 1;
+template <typename I>
+__device__ __forceinline__ void covering(I i, int s, int p, int k, int d, I on, I& lo, I& hi) {
+  const I span = I(k - 1) * d + 1;
   lo = (i + p < span) ? 0 : (i + p - span) / s + 1;
   hi = min((i + p) / s + 1, on);
 }
 
-template <typename T>
+// Element-strided kernels, index type I: int when every offset fits (the
+// divisions that unflatten the thread index are then 32-bit, several times
+// cheaper than 64-bit ones), else long long.
+template <typename T, typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_kernel(const T* __restrict__ x, PoolGeom g,
                                                                    T* __restrict__ y, int64_t* __restrict__ ind) {
-  const long long total = g.N * g.C * g.OH * g.OW;
-  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
-       u += (long long)gridDim.x * kPoolThreads) {
-    const long long ow = u % g.OW, oh = (u / g.OW) % g.OH, c = (u / (g.OW * g.OH)) % g.C,
-                    n = u / (g.OW * g.OH * g.C);
-    long long h0, h1, w0, w1;
-    window(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
-    window(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
-    const T* xp = x + n * g.xs[0] + c * g.xs[1];
+  const I OW = I(g.OW), OH = I(g.OH), C = I(g.C), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * C * OH * OW;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    I r = u / OW;
+    const I ow = u - r * OW;
+    I r2 = r / OH;
+    const I oh = r - r2 * OH;
+    const I n = r2 / C, c = r2 - n * C;
+    I h0, h1, w0, w1;
+    window<I>(oh, g.sh, g.ph, g.kh, g.dh, H, h0, h1);
+    window<I>(ow, g.sw, g.pw, g.kw, g.dw, W, w0, w1);
+    const T* xp = x + n * I(g.xs[0]) + c * I(g.xs[1]);
     float best = -INFINITY;
-    long long bi = h0 * g.W + w0;
-    for (long long h = h0; h < h1; h += g.dh)
-      for (long long w = w0; w < w1; w += g.dw) {
-        const float v = ldf(xp, h * g.xs[2] + w * g.xs[3]);
+    I bi = h0 * W + w0;
+    for (I h = h0; h < h1; h += g.dh)
+      for (I w = w0; w < w1; w += g.dw) {
+        const float v = ldf(xp, h * I(g.xs[2]) + w * I(g.xs[3]));
         if (v > best || v != v) {
           best = v;
-          bi = h * g.W + w;
+          bi = h * W + w;
         }
       }
-    const long long o = n * g.ys[0] + c * g.ys[1] + oh * g.ys[2] + ow * g.ys[3];
+    const I o = n * I(g.ys[0]) + c * I(g.ys[1]) + oh * I(g.ys[2]) + ow * I(g.ys[3]);
     stf(y, o, best);
     ind[o] = bi;
   }
@@ -99,8 +105,8 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const u
     const long long q = u % cv, r = u / cv;
     const long long ow = r % g.OW, oh = (r / g.OW) % g.OH, n = r / (g.OW * g.OH);
     long long h0, h1, w0, w1;
-    window(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
-    window(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
+    window<long long>(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
+    window<long long>(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
     float best[8];
     long long bi[8];
 #pragma unroll
@@ -136,26 +142,30 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const u
   }
 }
 
-template <typename T>
+template <typename T, typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_kernel(const T* __restrict__ dy,
                                                                    const int64_t* __restrict__ ind, PoolGeom g,
                                                                    T* __restrict__ dx) {
-  const long long total = g.N * g.C * g.H * g.W;
-  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
-       u += (long long)gridDim.x * kPoolThreads) {
-    const long long w = u % g.W, h = (u / g.W) % g.H, c = (u / (g.W * g.H)) % g.C, n = u / (g.W * g.H * g.C);
-    long long oh0, oh1, ow0, ow1;
-    covering(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
-    covering(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
-    const long long me = h * g.W + w;
-    const long long base = n * g.ys[0] + c * g.ys[1];
+  const I OW = I(g.OW), OH = I(g.OH), C = I(g.C), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * C * H * W;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    I r = u / W;
+    const I w = u - r * W;
+    I r2 = r / H;
+    const I h = r - r2 * H;
+    const I n = r2 / C, c = r2 - n * C;
+    I oh0, oh1, ow0, ow1;
+    covering<I>(h, g.sh, g.ph, g.kh, g.dh, OH, oh0, oh1);
+    covering<I>(w, g.sw, g.pw, g.kw, g.dw, OW, ow0, ow1);
+    const long long me = (long long)h * W + w;
+    const I base = n * I(g.ys[0]) + c * I(g.ys[1]);
     float s = 0.0f;
-    for (long long oh = oh0; oh < oh1; ++oh)
-      for (long long ow = ow0; ow < ow1; ++ow) {
-        const long long o = base + oh * g.ys[2] + ow * g.ys[3];
+    for (I oh = oh0; oh < oh1; ++oh)
+      for (I ow = ow0; ow < ow1; ++ow) {
+        const I o = base + oh * I(g.ys[2]) + ow * I(g.ys[3]);
         if (ind[o] == me) s = __fadd_rn(s, ldf(dy, o));
       }
-    stf(dx, n * g.xs[0] + c * g.xs[1] + h * g.xs[2] + w * g.xs[3], s);
+    stf(dx, n * I(g.xs[0]) + c * I(g.xs[1]) + h * I(g.xs[2]) + w * I(g.xs[3]), s);
   }
 }
 
@@ -169,8 +179,8 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_kernel(const u
     const long long q = u % cv, r = u / cv;
     const long long w = r % g.W, h = (r / g.W) % g.H, n = r / (g.W * g.H);
     long long oh0, oh1, ow0, ow1;
-    covering(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
-    covering(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
+    covering<long long>(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
+    covering<long long>(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
     const long long me = h * g.W + w;
     float s[8];
 #pragma unroll
@@ -208,6 +218,17 @@ b2_status make_pool(PoolGeom& g, int64_t N, int64_t C, int64_t H, int64_t W, int
   return B2_OK;
 }
 
+// every element offset (of x and of y, and the thread index range) fits an int
+bool fits32(const PoolGeom& g) {
+  auto span = [](const long long* st, long long a, long long b, long long c, long long d) {
+    return (a - 1) * std::llabs(st[0]) + (b - 1) * std::llabs(st[1]) + (c - 1) * std::llabs(st[2]) +
+           (d - 1) * std::llabs(st[3]);
+  };
+  const long long lim = (1LL << 31) - (1LL << 26);  // headroom for the grid-stride step past the end
+  return g.N * g.C * g.H * g.W < lim && g.N * g.C * g.OH * g.OW < lim && span(g.xs, g.N, g.C, g.H, g.W) < lim &&
+         span(g.ys, g.N, g.C, g.OH, g.OW) < lim;
+}
+
 bool nhwc8(const PoolGeom& g, const void* a, const void* b, const void* c) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   return g.C % 8 == 0 && g.xs[1] == 1 && g.ys[1] == 1 && g.xs[3] % 8 == 0 && g.xs[2] % 8 == 0 && g.xs[0] % 8 == 0 &&
@@ -242,12 +263,18 @@ b2_status b2_maxpool2d_fwd(const void* x, const int64_t* x_strides, void* y, int
   if (dtype == B2_BF16 && nhwc8(g, x, y, indices))
     maxpool_fwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
-  else if (dtype == B2_BF16)
-    maxpool_fwd_kernel<uint16_t><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+  else if (dtype == B2_BF16 && fits32(g))
+    maxpool_fwd_kernel<uint16_t, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else if (dtype == B2_BF16)
+    maxpool_fwd_kernel<uint16_t, long long><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else if (fits32(g))
+    maxpool_fwd_kernel<float, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const float*>(x), g, static_cast<float*>(y), indices);
   else
-    maxpool_fwd_kernel<float><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(static_cast<const float*>(x), g,
-                                                                              static_cast<float*>(y), indices);
+    maxpool_fwd_kernel<float, long long><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const float*>(x), g, static_cast<float*>(y), indices);
   return check_cuda(cudaGetLastError(), "maxpool fwd launch");
 }
 
@@ -266,12 +293,18 @@ b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices, const int64_t
   if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices))
     maxpool_bwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
-  else if (dtype == B2_BF16)
-    maxpool_bwd_kernel<uint16_t><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+  else if (dtype == B2_BF16 && fits32(g))
+    maxpool_bwd_kernel<uint16_t, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else if (dtype == B2_BF16)
+    maxpool_bwd_kernel<uint16_t, long long><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else if (fits32(g))
+    maxpool_bwd_kernel<float, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const float*>(dy), indices, g, static_cast<float*>(dx));
   else
-    maxpool_bwd_kernel<float><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(static_cast<const float*>(dy), indices,
-                                                                               g, static_cast<float*>(dx));
+    maxpool_bwd_kernel<float, long long><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
+        static_cast<const float*>(dy), indices, g, static_cast<float*>(dx));
   return check_cuda(cudaGetLastError(), "maxpool bwd launch");
 }
 

@@ -115,14 +115,33 @@ at::Tensor im2col(const at::Tensor& x, const GeneralConv& g) {
   return col;
 }
 
-at::Tensor pack_weight_khwc(const at::Tensor& weight, const GeneralConv& g) {
-  at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+// Frozen weights (no gradient wanted: a perceptual loss's feature network)
+// keep their packed forms between calls; the cache drops them on any write
+// into the weight's storage.  Kinds: 0 / 1 3x3 forward / input gradient,
+// 2 column-matrix order, 3 / 4 direct forward / input gradient.
+template <typename F>
+at::Tensor cached_pack(const at::Tensor& w, int kind, F make) {
   materialize(w);
-  at::Tensor wk = empty({g.Cout, g.Kp}, at::kBFloat16, w.device().index());
-  XDNA_B2(b2_pack_weight_khwc_bf16(w.data_ptr(), g.Cout, g.Cin, g.kh, g.kw, g.Kp, wk.data_ptr(),
-                                   stream(w.device().index())));
-  count_launch("pack_weight_khwc");
-  return wk;
+  const bool frozen = !w.requires_grad();
+  if (frozen) {
+    at::Tensor hit = find_packed_weight(w, kind);
+    if (hit.defined()) return hit;
+  }
+  at::Tensor packed = make();
+  if (frozen) attach_packed_weight(w, kind, packed);
+  return packed;
+}
+
+at::Tensor pack_weight_khwc(const at::Tensor& weight, const GeneralConv& g) {
+  return cached_pack(weight, 2, [&] {
+    at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+    materialize(w);
+    at::Tensor wk = empty({g.Cout, g.Kp}, at::kBFloat16, w.device().index());
+    XDNA_B2(b2_pack_weight_khwc_bf16(w.data_ptr(), g.Cout, g.Cin, g.kh, g.kw, g.Kp, wk.data_ptr(),
+                                     stream(w.device().index())));
+    count_launch("pack_weight_khwc");
+    return wk;
+  });
 }
 
 // op(A) . op(B) with split-K into a new fp32 [M][N] tensor.
@@ -206,6 +225,99 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> general_backward(const at::Tensor
   return {dx, dw, db};
 }
 
+at::MemoryFormat out_format(const at::Tensor& input) {
+  return input.suggest_memory_format() == at::MemoryFormat::ChannelsLast ? at::MemoryFormat::ChannelsLast
+                                                                          : at::MemoryFormat::Contiguous;
+}
+
+// ---- direct convolutions for layers with <= 4 output channels (b2_direct.cu)
+// An RGB output layer (9x9 32->3 in the style network) wastes nearly all of a
+// tensor-core tile, and ATen's library answers its input gradient with a
+// direct kernel of ~0.5 ms at B40 36x36: forward and input gradient run on
+// the CUDA cores here (fp32, one rounding); the weight gradient stays on
+// ATen's library kernels.
+struct DirectConv {
+  int64_t B, Cin, H, W, Cout, Ho, Wo;
+  int kh, kw, sy, sx, py, px, dy, dx;
+};
+
+bool direct_conv(const at::Tensor& input, const at::Tensor& weight, at::IntArrayRef stride, at::IntArrayRef padding,
+                 at::IntArrayRef dilation, bool transposed, int64_t groups, DirectConv& d) {
+  if (input.dim() != 4 || weight.dim() != 4 || transposed || groups != 1 || input.numel() == 0) return false;
+  if (stride.size() != 2 || padding.size() != 2 || dilation.size() != 2 || input.size(1) != weight.size(1))
+    return false;
+  d.B = input.size(0);
+  d.Cin = input.size(1);
+  d.H = input.size(2);
+  d.W = input.size(3);
+  d.Cout = weight.size(0);
+  d.kh = int(weight.size(2));
+  d.kw = int(weight.size(3));
+  d.sy = int(stride[0]);
+  d.sx = int(stride[1]);
+  d.py = int(padding[0]);
+  d.px = int(padding[1]);
+  d.dy = int(dilation[0]);
+  d.dx = int(dilation[1]);
+  if (d.Cout > 4 || d.Cout < 1 || d.Cin > 64 || d.kh > 11 || d.kw > 11) return false;
+  if (d.sy < 1 || d.sx < 1 || d.dy < 1 || d.dx < 1 || d.py < 0 || d.px < 0) return false;
+  d.Ho = (d.H + 2 * d.py - int64_t(d.dy) * (d.kh - 1) - 1) / d.sy + 1;
+  d.Wo = (d.W + 2 * d.px - int64_t(d.dx) * (d.kw - 1) - 1) / d.sx + 1;
+  return d.Ho > 0 && d.Wo > 0;
+}
+
+at::Tensor direct_weight(const at::Tensor& weight, const DirectConv& d, int dgrad) {
+  return cached_pack(weight, dgrad ? 4 : 3, [&] {
+    at::Tensor w = weight.is_contiguous() ? weight : weight.contiguous();
+    materialize(w);
+    const size_t n = b2_direct_conv_weight_floats(d.Cout, d.Cin, d.kh, d.kw, dgrad);
+    at::Tensor wt = empty({int64_t(n)}, at::kFloat, w.device().index());
+    XDNA_B2(b2_direct_conv_weight(w.data_ptr(), d.Cout, d.Cin, d.kh, d.kw, dgrad, wt.data_ptr<float>(),
+                                  stream(w.device().index())));
+    count_launch("direct_conv.weight");
+    return wt;
+  });
+}
+
+at::Tensor direct_forward(const at::Tensor& input, const at::Tensor& weight, const at::Tensor& bias,
+                          const DirectConv& d) {
+  const auto dev = input.device().index();
+  c10::cuda::CUDAGuard guard(dev);
+  materialize(input);
+  at::Tensor wt = direct_weight(weight, d, 0);
+  at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
+  if (b.defined()) materialize(b);
+  at::Tensor y = empty({d.B, d.Cout, d.Ho, d.Wo}, at::kBFloat16, dev, out_format(input));
+  const int64_t is[4] = {input.stride(0), input.stride(1), input.stride(2), input.stride(3)};
+  const int64_t os[4] = {y.stride(0), y.stride(1), y.stride(2), y.stride(3)};
+  XDNA_B2(b2_direct_conv_bf16(input.data_ptr(), is, d.B, d.Cin, d.H, d.W, wt.data_ptr<float>(), d.kh, d.kw, d.sy,
+                              d.sx, d.py, d.px, d.dy, d.dx, b.defined() ? b.data_ptr() : nullptr, y.data_ptr(), os,
+                              d.Cout, d.Ho, d.Wo, stream(dev)));
+  count_launch("direct_conv.fwd");
+  return y;
+}
+
+// stride-1 input gradient as a direct convolution over dY
+bool direct_dgrad_ok(const DirectConv& d) {
+  return d.sy == 1 && d.sx == 1 && (d.kh - 1) * d.dy >= d.py && (d.kw - 1) * d.dx >= d.px;
+}
+
+at::Tensor direct_dgrad(const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
+                        const DirectConv& d) {
+  const auto dev = input.device().index();
+  c10::cuda::CUDAGuard guard(dev);
+  materialize(grad_output);
+  at::Tensor wt = direct_weight(weight, d, 1);
+  at::Tensor dx = empty({d.B, d.Cin, d.H, d.W}, at::kBFloat16, dev, out_format(input));
+  const int64_t is[4] = {grad_output.stride(0), grad_output.stride(1), grad_output.stride(2), grad_output.stride(3)};
+  const int64_t os[4] = {dx.stride(0), dx.stride(1), dx.stride(2), dx.stride(3)};
+  XDNA_B2(b2_direct_conv_bf16(grad_output.data_ptr(), is, d.B, d.Cout, d.Ho, d.Wo, wt.data_ptr<float>(), d.kh, d.kw,
+                              1, 1, (d.kh - 1) * d.dy - d.py, (d.kw - 1) * d.dx - d.px, d.dy, d.dx, nullptr,
+                              dx.data_ptr(), os, d.Cin, d.H, d.W, stream(dev)));
+  count_launch("direct_conv.dgrad");
+  return dx;
+}
+
 at::Tensor contiguous_as(const at::Tensor& t, int layout) {
   const auto mf = layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous;
   return t.is_contiguous(mf) ? t : t.contiguous(mf);
@@ -262,11 +374,6 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> conv1x1_backward(const at::Tensor
   return {dx, dw, db};
 }
 
-at::MemoryFormat out_format(const at::Tensor& input) {
-  return input.suggest_memory_format() == at::MemoryFormat::ChannelsLast ? at::MemoryFormat::ChannelsLast
-                                                                          : at::MemoryFormat::Contiguous;
-}
-
 int chunks_of(int64_t c) { return int((c + 63) / 64); }
 
 at::Tensor pack_rows(const at::Tensor& x) {
@@ -281,17 +388,19 @@ at::Tensor pack_rows(const at::Tensor& x) {
 }
 
 at::Tensor pack_weight(const at::Tensor& w_in, bool dgrad) {
-  at::Tensor w = w_in.is_contiguous() ? w_in : w_in.contiguous();
-  materialize(w);
-  const int Cout = int(w.size(0)), Cin = int(w.size(1));
-  const int ch = chunks_of(dgrad ? Cout : Cin);
-  at::Tensor wk = empty({dgrad ? Cin : Cout, int64_t(ch) * 576}, at::kBFloat16, w.device().index());
-  if (dgrad)
-    XDNA_B2(b2_pack_weight_dgrad_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
-  else
-    XDNA_B2(b2_pack_weight_fwd_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
-  count_launch("pack_weight");
-  return wk;
+  return cached_pack(w_in, dgrad ? 1 : 0, [&] {
+    at::Tensor w = w_in.is_contiguous() ? w_in : w_in.contiguous();
+    materialize(w);
+    const int Cout = int(w.size(0)), Cin = int(w.size(1));
+    const int ch = chunks_of(dgrad ? Cout : Cin);
+    at::Tensor wk = empty({dgrad ? Cin : Cout, int64_t(ch) * 576}, at::kBFloat16, w.device().index());
+    if (dgrad)
+      XDNA_B2(b2_pack_weight_dgrad_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
+    else
+      XDNA_B2(b2_pack_weight_fwd_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
+    count_launch("pack_weight");
+    return wk;
+  });
 }
 
 // dW into `gw` (raw pointer: a deferred job must not keep the gradient's
@@ -340,6 +449,9 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
                                     at::IntArrayRef output_padding, int64_t groups) {
   const at::Tensor bias = bias_opt.has_value() ? *bias_opt : at::Tensor();
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(bias)) {
+    DirectConv dc;
+    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc))
+      return direct_forward(input, weight, bias, dc);
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
     if (l1 >= 0) return conv1x1_forward(input, weight, bias, l1);
@@ -378,6 +490,21 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     at::IntArrayRef padding, at::IntArrayRef dilation, bool transposed, at::IntArrayRef output_padding, int64_t groups,
     std::array<bool, 3> output_mask) {
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(grad_output)) {
+    DirectConv dc;
+    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_dgrad_ok(dc)) {
+      at::Tensor dx = output_mask[0] ? direct_dgrad(grad_output, input, weight, dc) : at::Tensor();
+      at::Tensor dw, db;
+      if (output_mask[1] || output_mask[2]) {
+        count_fallback("convolution_backward_overrideable.dw");
+        c10::cuda::CUDAGuard g(input.device().index());
+        auto r = at::convolution_backward(to_cuda(grad_output), to_cuda(input), to_cuda(weight), std::nullopt,
+                                          stride, padding, dilation, transposed, output_padding, groups,
+                                          {false, output_mask[1], output_mask[2]});
+        if (output_mask[1]) dw = adopt(std::get<1>(r));
+        if (output_mask[2]) db = adopt(std::get<2>(r));
+      }
+      return {dx, dw, db};
+    }
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
     if (l1 >= 0) return conv1x1_backward(grad_output, input, weight, l1, output_mask);

@@ -39,9 +39,22 @@ struct Attachment {
   int64_t offset = 0;
 };
 
+// A packed (GEMM-operand) form of a weight, valid while the weight's version,
+// geometry and storage are unchanged and nothing wrote the storage.
+struct WeightSlot {
+  int kind = 0;
+  int64_t version = 0;
+  std::vector<int64_t> sizes, strides;
+  int64_t offset = 0;
+  at::Tensor packed;
+};
+
 std::mutex g_mu;
 std::unordered_map<void*, Job> g_jobs;               // storage data ptr -> pending job
 std::unordered_map<void*, Attachment> g_attach;      // storage data ptr -> packed rows
+std::unordered_map<void*, std::vector<WeightSlot>> g_wslots;  // storage data ptr -> packed weights
+std::atomic<int64_t> g_nwslots{0};
+int64_t g_whits = 0, g_wmisses = 0;
 int64_t g_order = 0;
 int64_t g_started = 0, g_dropped = 0, g_kicks = 0, g_deferred = 0;
 int64_t g_dx_this_step = 0, g_k_prev = -1, g_k_learned = 0;
@@ -115,8 +128,15 @@ void on_release(void* ptr) {
   if (!ptr) return;
   Job dropped;
   Attachment att;
+  std::vector<WeightSlot> slots;
   {
     std::lock_guard<std::mutex> lk(g_mu);
+    auto ws = g_wslots.find(ptr);
+    if (ws != g_wslots.end()) {
+      slots = std::move(ws->second);
+      g_wslots.erase(ws);
+      g_nwslots.store(int64_t(g_wslots.size()));
+    }
     auto it = g_jobs.find(ptr);
     if (it != g_jobs.end()) {
       dropped = std::move(it->second);
@@ -156,7 +176,50 @@ std::map<std::string, int64_t> deferred_stats() {
   std::lock_guard<std::mutex> lk(g_mu);
   return {{"pending", int64_t(g_jobs.size())}, {"deferred", g_deferred}, {"started", g_started},
           {"dropped", g_dropped},          {"kicks", g_kicks},       {"k_learned", g_k_learned},
-          {"attached_rows", int64_t(g_attach.size())}};
+          {"attached_rows", int64_t(g_attach.size())}, {"packed_weights", int64_t(g_wslots.size())},
+          {"packed_weight_hits", g_whits}, {"packed_weight_misses", g_wmisses}};
+}
+
+void note_write(const at::Tensor& t) {
+  if (g_nwslots.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
+  std::vector<WeightSlot> dropped;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_wslots.find(t.storage().mutable_data());
+  if (it == g_wslots.end()) return;
+  dropped = std::move(it->second);
+  g_wslots.erase(it);
+  g_nwslots.store(int64_t(g_wslots.size()));
+}
+
+at::Tensor find_packed_weight(const at::Tensor& w, int kind) {
+  if (!w.has_storage()) return {};
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_wslots.find(w.storage().mutable_data());
+  if (it != g_wslots.end())
+    for (const WeightSlot& ws : it->second)
+      if (ws.kind == kind && ws.version == int64_t(w._version()) && ws.sizes == w.sizes().vec() &&
+          ws.strides == w.strides().vec() && ws.offset == w.storage_offset()) {
+        ++g_whits;
+        return ws.packed;
+      }
+  ++g_wmisses;
+  return {};
+}
+
+void attach_packed_weight(const at::Tensor& w, int kind, const at::Tensor& packed) {
+  if (!w.has_storage()) return;
+  WeightSlot fresh{kind, int64_t(w._version()), w.sizes().vec(), w.strides().vec(), w.storage_offset(), packed};
+  WeightSlot old;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto& v = g_wslots[w.storage().mutable_data()];
+  for (WeightSlot& ws : v)
+    if (ws.kind == kind) {
+      old = std::move(ws);
+      ws = std::move(fresh);
+      return;
+    }
+  v.push_back(std::move(fresh));
+  g_nwslots.store(int64_t(g_wslots.size()));
 }
 
 void attach_rows(const at::Tensor& input, const at::Tensor& rows) {

@@ -135,14 +135,18 @@ void cuda_alias_fallback(const c10::OperatorHandle& op, torch::jit::Stack* stack
 
   for (auto& w : written) {
     const c10::IValue& o = originals[w.first];
-    if (o.isTensor() && o.toTensor().defined() && o.toTensor().device().type() == kXdna)
+    if (o.isTensor() && o.toTensor().defined() && o.toTensor().device().type() == kXdna) {
       sync_back(o.toTensor(), w.second.toTensor());
-    else if (o.isTensorList()) {
+      note_write(o.toTensor());
+    } else if (o.isTensorList()) {
       auto ol = o.toTensorList();
       auto al = w.second.toTensorList();
       for (size_t k = 0; k < ol.size(); ++k) {
         const at::Tensor& ot = ol[k];
-        if (ot.defined() && ot.device().type() == kXdna) sync_back(ot, al[k]);
+        if (ot.defined() && ot.device().type() == kXdna) {
+          sync_back(ot, al[k]);
+          note_write(ot);
+        }
       }
     }
   }
@@ -187,8 +191,29 @@ TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {
 // output which the kernel resizes (a deprecation warning on every call); the
 // functional form on the CUDA alias allocates its own output and needs one
 // dispatch instead of two.
+//
+// The _foreach_* ops carry a CompositeExplicitAutograd kernel that a backend
+// without its own kernels inherits ahead of the boxed fallback: a host loop of
+// one single-tensor op per list element (an optimizer's step counters alone
+// are one launch per parameter).  Routed through the CUDA aliases they reach
+// ATen's CUDA multi-tensor kernels: one launch per list.
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
-  m.impl("mse_loss", torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>());
+  const auto boxed = [] { return torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>(); };
+  m.impl("mse_loss", boxed());
+  for (const char* op :
+       {"_foreach_add_.Scalar", "_foreach_add_.List", "_foreach_add_.ScalarList", "_foreach_add_.Tensor",
+        "_foreach_mul_.Scalar", "_foreach_mul_.List", "_foreach_mul_.ScalarList", "_foreach_mul_.Tensor",
+        "_foreach_div_.Scalar", "_foreach_div_.List", "_foreach_div_.ScalarList", "_foreach_div_.Tensor",
+        "_foreach_sub_.Scalar", "_foreach_sub_.List", "_foreach_sub_.ScalarList", "_foreach_addcmul_.Scalar",
+        "_foreach_addcmul_.ScalarList", "_foreach_addcmul_.Tensor", "_foreach_addcdiv_.Scalar",
+        "_foreach_addcdiv_.ScalarList", "_foreach_addcdiv_.Tensor", "_foreach_lerp_.Scalar", "_foreach_lerp_.List",
+        "_foreach_lerp_.ScalarList", "_foreach_maximum_.Scalar", "_foreach_maximum_.List",
+        "_foreach_maximum_.ScalarList", "_foreach_sqrt_", "_foreach_zero_", "_foreach_copy_", "_foreach_add.Scalar",
+        "_foreach_add.List", "_foreach_add.ScalarList", "_foreach_add.Tensor", "_foreach_mul.Scalar",
+        "_foreach_mul.List", "_foreach_mul.ScalarList", "_foreach_mul.Tensor", "_foreach_div.Scalar",
+        "_foreach_div.List", "_foreach_div.ScalarList", "_foreach_div.Tensor", "_foreach_sqrt", "_foreach_neg",
+        "_foreach_norm.Scalar"})
+    m.impl(op, boxed());
 }
 
 }  // namespace xdna

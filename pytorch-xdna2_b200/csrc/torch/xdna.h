@@ -79,6 +79,16 @@ extern std::atomic<int64_t> g_pending_jobs;
 void attach_rows(const at::Tensor& input, const at::Tensor& rows);
 at::Tensor find_rows(const at::Tensor& input);
 
+// Packed GEMM-operand forms of frozen weights (the reference's weight-encode
+// cache keyed on pointer, version counter and write epoch,
+// torch_xdna_device.cpp:2200-2271): found while the weight's version, geometry
+// and storage are unchanged; any write into the storage through this backend
+// (note_write: the CUDA-alias fallback, copies, out= and fused optimizer ops)
+// and the storage's release drop them.
+at::Tensor find_packed_weight(const at::Tensor& w, int kind);
+void attach_packed_weight(const at::Tensor& w, int kind, const at::Tensor& packed);
+void note_write(const at::Tensor& t);
+
 // ---- modes and counters (module.cpp) --------------------------------------
 // 2: all hot-path kernels; 1: weight gradients through the CUDA-alias path;
 // 0: every hot op through the CUDA-alias path (A/B switch, set_npu_mode).

@@ -68,6 +68,10 @@ SIGNATURES = {
                        i64, i64, vp],
     "b2_pack_weight_khwc_bf16": [vp, i64, i64, i32, i32, i64, vp, vp],
     "b2_unpack_weight_khwc": [vp, i64, i64, i32, i32, i64, vp, i32, vp],
+    "b2_direct_conv_weight_floats": [i64, i64, i32, i32, i32],
+    "b2_direct_conv_weight": [vp, i64, i64, i32, i32, i32, vp, vp],
+    "b2_direct_conv_bf16": [vp, vp, i64, i64, i64, i64, vp, i32, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64,
+                            i64, i64, vp],
     "b2_maxpool2d_fwd": [vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32,
                          i32, vp],
     "b2_maxpool2d_bwd": [vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32,
@@ -84,7 +88,7 @@ SIGNATURES = {
 }
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
              "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
-             "b2_conv1x1_wgrad_workspace_bytes": sz, "b2_gemm_splitk_workspace_bytes": sz,
+             "b2_conv1x1_wgrad_workspace_bytes": sz, "b2_direct_conv_weight_floats": sz, "b2_gemm_splitk_workspace_bytes": sz,
              "b2_batch_norm_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
