@@ -233,9 +233,10 @@ at::MemoryFormat out_format(const at::Tensor& input) {
 // ---- direct convolutions for layers with <= 4 output channels (b2_direct.cu)
 // An RGB output layer (9x9 32->3 in the style network) wastes nearly all of a
 // tensor-core tile, and ATen's library answers its input gradient with a
-// direct kernel of ~0.5 ms at B40 36x36: forward and input gradient run on
-// the CUDA cores here (fp32, one rounding); the weight gradient stays on
-// ATen's library kernels.
+// direct kernel of ~0.5 ms at B40 36x36: the input gradient (a reduction over
+// only Cout*kh*kw taps) runs on the CUDA cores here (fp32, one rounding), and
+// so does the forward when its reduction is short (Cin*kh*kw <= 512); the
+// weight gradient and long forwards stay on ATen's library kernels.
 struct DirectConv {
   int64_t B, Cin, H, W, Cout, Ho, Wo;
   int kh, kw, sy, sx, py, px, dy, dx;
@@ -450,7 +451,10 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
   const at::Tensor bias = bias_opt.has_value() ? *bias_opt : at::Tensor();
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(bias)) {
     DirectConv dc;
-    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc))
+    // forward: only short reductions (a thread per pixel walks all Cin*kh*kw
+    // taps; a long walk is latency-bound and ATen's kernels win)
+    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) &&
+        dc.Cin * dc.kh * dc.kw <= 512)
       return direct_forward(input, weight, bias, dc);
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
