@@ -525,12 +525,24 @@ def run_workload(args):
             return None
         return _timed(make_step(), steps, warmup, cpu)
 
+    def graphed(make_step, key, scale):
+        """The same step captured once into a CUDA graph (xdna_train.graphs)
+        and replayed: the step's kernels without the host's per-op dispatch."""
+        if world != 1:
+            return
+        from xdna_train import graphs
+        try:
+            replay = graphs.make_graphed_step(make_step(), warmup=max(3, args.warmup))
+            out[key] = round(scale / _timed(replay, args.steps, 2, sync), 2)
+        except Exception as e:  # reported, not hidden: the eager figure stands
+            out[key + "_error"] = f"{type(e).__name__}: {e}"[:300]
+
     if w == "readme":
         # config 1: Conv2d(128,128,3,pad=1) BF16, x [16,128,36,36], target 0, Adam 1e-3
-        def make(dev):
+        def make(dev, capturable=False):
             torch.manual_seed(0)
             model = nn.Conv2d(128, 128, 3, padding=1).bfloat16().to(dev)
-            opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True)
+            opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True, capturable=capturable)
             x = torch.randn(16, 128, 36, 36, dtype=torch.bfloat16).to(dev)
             tgt = torch.zeros_like(x)
 
@@ -544,13 +556,14 @@ def run_workload(args):
         out.update(metric="README Conv2d training step it/s (BASELINE config 1)", value=round(1 / dt, 2),
                    unit="it/s", ms_per_step=round(dt * 1e3, 4),
                    tflops=round(18.35e9 / dt / 1e12, 1))
+        graphed(lambda: make(X, True), "graphed_it_s", 1.0)
         c = cpu_rate(lambda: make("cpu"), steps=5, warmup=1)
     elif w == "mlp":
         # config 3: MLP B512, autocast BF16 over FP32 params (FP32 master state), Adam 1e-4
-        def make(dev):
+        def make(dev, capturable=False):
             torch.manual_seed(0)
             model = make_mlp().to(dev)
-            opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True)
+            opt = torch.optim.Adam(model.parameters(), lr=1e-4, fused=True, capturable=capturable)
             x = torch.randn(512, 1024).to(dev)
             tgt = torch.randn(512, 1024).to(dev)
             dtype = "xdna" if torch.device(dev).type == "xdna" else "cpu"
@@ -565,6 +578,7 @@ def run_workload(args):
         dt = _timed(make(X), args.steps, args.warmup, sync)
         out.update(metric="MLP training TFLOP/s (BASELINE config 3)", value=round(128.85e9 / dt / 1e12, 2),
                    unit="TFLOP/s", ms_per_step=round(dt * 1e3, 4))
+        graphed(lambda: make(X, True), "graphed_tflops", 128.85e9 / 1e12)
         c = cpu_rate(lambda: make("cpu"))
         if c:
             c = c  # seconds per step
@@ -572,7 +586,7 @@ def run_workload(args):
         # config 4: B40 36x36 style transfer, Adam 1e-3, with and without the region
         from xdna_train import regions
 
-        def make(dev, fused, fuse_norm=False):
+        def make(dev, fused, fuse_norm=False, capturable=False):
             torch.manual_seed(0)
             gen = make_style_generator().bfloat16().to(dev)
             crit = StyleLoss().bfloat16().to(dev)
@@ -585,7 +599,7 @@ def run_workload(args):
                     for a, b in zip(mods, mods[1:]):
                         if isinstance(a, nn.BatchNorm2d) and isinstance(b, nn.ReLU):
                             assert regions.fuse_norm_activation(a, b)
-            opt = torch.optim.Adam(gen.parameters(), lr=1e-3, fused=True)
+            opt = torch.optim.Adam(gen.parameters(), lr=1e-3, fused=True, capturable=capturable)
             g = torch.Generator().manual_seed(1)
             x = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
             tgt = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
@@ -603,6 +617,8 @@ def run_workload(args):
         out.update(metric="style-transfer training it/s (BASELINE config 4)", value=round(1 / dt, 2), unit="it/s",
                    ms_per_step=round(dt * 1e3, 4), fused_perceptual_loss_it_s=round(1 / dtf, 2),
                    fused_perceptual_and_norm_act_it_s=round(1 / dtn, 2))
+        graphed(lambda: make(X, False, capturable=True), "graphed_it_s", 1.0)
+        graphed(lambda: make(X, True, True, capturable=True), "graphed_fused_perceptual_and_norm_act_it_s", 1.0)
         c = cpu_rate(lambda: make("cpu", False))
     elif w == "resnet50":
         # config 5: ResNet-50 224x224, per-GPU batch 128, SGD momentum 0.9, DP over NCCL

@@ -120,6 +120,8 @@ __global__ void direct_weight_kernel(const uint16_t* __restrict__ w, int Cout, i
   }
 }
 
+constexpr int kDirectMaxSmem = 200 * 1024;
+
 int pad_out(int n) { return n <= 4 ? 4 : n <= 8 ? 8 : n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 0; }
 
 size_t direct_smem(const DirectGeom& g, int noutp) {
@@ -144,8 +146,17 @@ b2_status launch_direct_kw(const uint16_t* in, const float* wt, const uint16_t* 
                            uint16_t* out, cudaStream_t st) {
   const size_t smem = direct_smem(g, NOUT);
   auto kern = direct_conv_kernel<NOUT, KW>;
-  B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                    "cudaFuncSetAttribute(direct conv smem)"));
+  // once per device, at the largest size accepted (no attribute calls per
+  // launch: they must not run inside a CUDA graph capture)
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[dev]) {
+    B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDirectMaxSmem),
+                      "cudaFuncSetAttribute(direct conv smem)"));
+    configured[dev] = true;
+  }
   const long long blocks = (long long)g.B * g.tiles_x * g.tiles_y;
   kern<<<unsigned(blocks), g.TH * g.TW, smem, st>>>(in, wt, bias, g, out);
   return check_cuda(cudaGetLastError(), "direct conv launch");
@@ -225,7 +236,7 @@ b2_status b2_direct_conv_bf16(const void* in, const int64_t* in_strides, int64_t
   // few output channels: small tiles, so that enough CTAs (and warps) are
   // resident to hide the shared-memory latency of the long reduction
   direct_tile(g, np <= 8 ? 64 : 256);
-  if (direct_smem(g, np) > 200 * 1024)
+  if (direct_smem(g, np) > size_t(kDirectMaxSmem))
     return set_error(B2_ERR_UNSUPPORTED, "b2_direct_conv_bf16: %zu bytes of shared memory needed",
                      direct_smem(g, np));
   if ((long long)g.B * g.tiles_x * g.tiles_y >= (1LL << 31))

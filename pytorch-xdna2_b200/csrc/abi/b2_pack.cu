@@ -506,8 +506,16 @@ static b2_status pack_rows_nchw_tma(const void* x, int64_t sn, int64_t sc, int64
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   auto kern = rowsum ? pack_rows_nchw_tma_kernel<true> : pack_rows_nchw_tma_kernel<false>;
-  B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                    "cudaFuncSetAttribute(pack smem)"));
+  // once per device and variant, at the largest size (W = 256): no attribute
+  // calls per launch, so that the packer can run inside a CUDA graph capture
+  static bool configured[2][64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[rowsum ? 1 : 0][dev]) {
+    B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(size_t(4) * 256 * 128 + 64 + 1024)),
+                      "cudaFuncSetAttribute(pack smem)"));
+    configured[rowsum ? 1 : 0][dev] = true;
+  }
   int per_sm = 0;
   B2_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTmaPackThreads, smem),
                     "pack occupancy"));

@@ -284,6 +284,11 @@ PYBIND11_MODULE(_C, m) {
     c10::cuda::CUDACachingAllocator::emptyCache();
   });
   m.def("allocator_stats", [] { return to_dict(allocator_stats()); });
+  m.def("graph_capture_begin", [](int device, uintptr_t stream, int share_pool) {
+    return graph_capture_begin(device, reinterpret_cast<cudaStream_t>(stream), share_pool);
+  });
+  m.def("graph_capture_end", [](uintptr_t stream) { graph_capture_end(reinterpret_cast<cudaStream_t>(stream)); });
+  m.def("graph_pool_release", [](int pool) { graph_pool_release(pool); });
   m.def("fallback_stats", [] {
     py::dict d;
     for (auto& kv : fallback_stats()) {

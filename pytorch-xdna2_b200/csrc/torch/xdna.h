@@ -44,6 +44,12 @@ c10::Allocator* allocator();
 void record_stream(const c10::DataPtr& ptr, cudaStream_t stream);
 void empty_cache();
 std::map<std::string, int64_t> allocator_stats();
+// CUDA graph capture: allocations on `stream` come from a private pool until
+// graph_capture_end; a pool (returned id; share_pool > 0 reuses one) stays
+// reserved for its graphs until graph_pool_release.
+int graph_capture_begin(int device, cudaStream_t stream, int share_pool);
+void graph_capture_end(cudaStream_t stream);
+void graph_pool_release(int pool);
 // Called by the allocator when a block is released; drops deferred work and
 // packed-operand attachments keyed on that address.
 void on_release(void* ptr);
