@@ -230,13 +230,13 @@ at::MemoryFormat out_format(const at::Tensor& input) {
                                                                           : at::MemoryFormat::Contiguous;
 }
 
-// ---- direct convolutions for layers with <= 4 output channels (b2_direct.cu)
+// ---- direct convolutions for RGB input / output layers (b2_direct.cu)
 // An RGB output layer (9x9 32->3 in the style network) wastes nearly all of a
 // tensor-core tile, and ATen's library answers its input gradient with a
-// direct kernel of ~0.5 ms at B40 36x36: the input gradient (a reduction over
-// only Cout*kh*kw taps) runs on the CUDA cores here (fp32, one rounding), and
-// so does the forward when its reduction is short (Cin*kh*kw <= 512); the
-// weight gradient and long forwards stay on ATen's library kernels.
+// direct kernel of ~0.5 ms at B40 36x36 (45 us here); an RGB input layer's
+// forward (9x9 3->32) is a short reduction.  Both run on the CUDA cores (fp32,
+// one rounding); the weight gradients stay on ATen's library kernels, and 3x3
+// stride-1 layers on the tensor-core path.
 struct DirectConv {
   int64_t B, Cin, H, W, Cout, Ho, Wo;
   int kh, kw, sy, sx, py, px, dy, dx;
@@ -260,7 +260,9 @@ bool direct_conv(const at::Tensor& input, const at::Tensor& weight, at::IntArray
   d.px = int(padding[1]);
   d.dy = int(dilation[0]);
   d.dx = int(dilation[1]);
-  if (d.Cout > 4 || d.Cout < 1 || d.Cin > 64 || d.kh > 11 || d.kw > 11) return false;
+  // a handful of channels on one side (an RGB input or output layer), at most
+  // 64 on the other (a thread holds one fp32 accumulator per output channel)
+  if (std::min(d.Cin, d.Cout) > 4 || d.Cout > 64 || d.Cin > 64 || d.kh > 11 || d.kw > 11) return false;
   if (d.sy < 1 || d.sx < 1 || d.dy < 1 || d.dx < 1 || d.py < 0 || d.px < 0) return false;
   d.Ho = (d.H + 2 * d.py - int64_t(d.dy) * (d.kh - 1) - 1) / d.sy + 1;
   d.Wo = (d.W + 2 * d.px - int64_t(d.dx) * (d.kw - 1) - 1) / d.sx + 1;
@@ -299,8 +301,21 @@ at::Tensor direct_forward(const at::Tensor& input, const at::Tensor& weight, con
 }
 
 // stride-1 input gradient as a direct convolution over dY
+// A thread per output pixel keeps one fp32 accumulator per output channel and
+// walks the whole reduction: efficient when many outputs share each load (>= 8
+// of them) and the walk is short; with 1-4 outputs and hundreds of taps it is
+// latency-bound.  So: the input gradient of an RGB output layer (Cout <= 4,
+// 8 <= Cin <= 64, stride 1) and the forward of an RGB input layer (Cin <= 4,
+// 16 <= Cout <= 64, Cin*kh*kw <= 512, <= 2^31 FMAs: a 224x224 batch-128 stem
+// belongs on tensor cores).
 bool direct_dgrad_ok(const DirectConv& d) {
-  return d.sy == 1 && d.sx == 1 && (d.kh - 1) * d.dy >= d.py && (d.kw - 1) * d.dx >= d.px;
+  return d.Cout <= 4 && d.Cin >= 8 && d.sy == 1 && d.sx == 1 && (d.kh - 1) * d.dy >= d.py &&
+         (d.kw - 1) * d.dx >= d.px && d.Cout * d.kh * d.kw <= 2592;
+}
+
+bool direct_fwd_ok(const DirectConv& d) {
+  return d.Cin <= 4 && d.Cout >= 16 && d.Cin * d.kh * d.kw <= 512 &&
+         d.B * d.Ho * d.Wo * d.Cin * d.kh * d.kw * d.Cout <= (int64_t(1) << 31);
 }
 
 at::Tensor direct_dgrad(const at::Tensor& grad_output, const at::Tensor& input, const at::Tensor& weight,
@@ -450,12 +465,6 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
                                     at::IntArrayRef output_padding, int64_t groups) {
   const at::Tensor bias = bias_opt.has_value() ? *bias_opt : at::Tensor();
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(bias)) {
-    DirectConv dc;
-    // forward: only short reductions (a thread per pixel walks all Cin*kh*kw
-    // taps; a long walk is latency-bound and ATen's kernels win)
-    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) &&
-        dc.Cin * dc.kh * dc.kw <= 512)
-      return direct_forward(input, weight, bias, dc);
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
     if (l1 >= 0) return conv1x1_forward(input, weight, bias, l1);
@@ -463,6 +472,10 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
     if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
         general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
       return general_forward(input, weight, bias, gc);
+    DirectConv dc;
+    if (!is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
+        direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_fwd_ok(dc))
+      return direct_forward(input, weight, bias, dc);
   }
   const bool fast = g_mode.load() > 0 && is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
                     bf16(input) && bf16(weight) && bf16(bias) && input.numel() > 0;
@@ -495,7 +508,10 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     std::array<bool, 3> output_mask) {
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(grad_output)) {
     DirectConv dc;
-    if (direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_dgrad_ok(dc)) {
+    const bool general = general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed,
+                                                         groups);
+    if (!general && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
+        direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_dgrad_ok(dc)) {
       at::Tensor dx = output_mask[0] ? direct_dgrad(grad_output, input, weight, dc) : at::Tensor();
       at::Tensor dw, db;
       if (output_mask[1] || output_mask[2]) {

@@ -27,7 +27,9 @@ def _worker(rank, world, port, mode, q):
     from xdna_train.ddp import GradAllReduce
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    # the timeout bounds both the rendezvous (a spawned rank's first torch
+    # import can take a while on a loaded machine) and the failure case's wait
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     try:
         torch.manual_seed(0)
         model = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.ReLU(), torch.nn.Linear(16, 4))

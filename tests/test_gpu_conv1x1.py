@@ -121,10 +121,11 @@ def test_conv1x1_module_vs_cpu_path(fresh, shape, cl, bias):
 
 
 def test_ineligible_1x1_takes_the_aten_path(fresh):
-    # 5 output channels: neither the 1x1 GEMM nor the column-matrix path
-    conv = nn.Conv2d(3, 5, 1).bfloat16()
-    x = torch.randn(2, 3, 5, 5).bfloat16()
-    cx = nn.Conv2d(3, 5, 1).bfloat16()
+    # 6 -> 5 channels: neither the 1x1 GEMM, the column-matrix path nor the
+    # direct kernel (more than 4 channels on both sides)
+    conv = nn.Conv2d(6, 5, 1).bfloat16()
+    x = torch.randn(2, 6, 5, 5).bfloat16()
+    cx = nn.Conv2d(6, 5, 1).bfloat16()
     cx.load_state_dict(conv.state_dict())
     close(cx.to(X)(x.to(X)), conv(x))
     assert "convolution_overrideable" in xdna_train.fallback_stats()

@@ -1,6 +1,6 @@
-"""Direct convolutions for layers with <= 4 output channels (an RGB output
-layer such as the style network's 9x9 32->3): forward and input gradient on
-the CUDA cores, weight gradient on ATen's library kernels.  Checked against
+"""Direct convolutions for RGB layers: the input gradient of an output layer
+(the style network's 9x9 32->3) and the forward of an input layer (its 9x9
+3->32 stem) on the CUDA cores, weight gradients on ATen's library kernels.  Checked against
 an fp32 reference of the reference's CPU path (the same convolution on the
 CPU) with the north-star bound max|err| <= 2e-2 * max|ref| (fp32 sums, one
 bf16 rounding), NCHW and channels-last, with and without bias, strided and
@@ -38,11 +38,13 @@ CASES = [
     # (B, Cin, H, W, Cout, k, stride, pad, dilation, bias, channels_last)
     (4, 32, 36, 36, 3, 9, 1, 4, 1, True, False),   # style network output layer
     (2, 32, 20, 17, 3, 9, 1, 4, 1, False, True),
-    (3, 16, 13, 11, 1, 3, 1, 1, 1, True, False),
+    (3, 16, 13, 11, 1, 5, 1, 2, 1, True, False),
     (2, 64, 9, 9, 4, 5, 1, 2, 1, True, True),
-    (2, 8, 15, 14, 2, 3, 2, 1, 1, True, False),    # strided: forward direct, input gradient on ATen
     (2, 12, 16, 16, 3, 3, 1, 2, 2, False, False),  # dilated
-    (2, 4, 12, 12, 3, 7, 2, 3, 1, True, True),     # short reduction, strided forward
+    (2, 3, 15, 14, 16, 3, 2, 1, 1, True, False),   # strided RGB input layer
+    (2, 4, 12, 12, 16, 7, 2, 3, 1, True, True),
+    (3, 3, 20, 18, 64, 5, 1, 2, 1, True, False),
+    (2, 3, 16, 16, 32, 9, 1, 4, 1, True, True),    # style network stem
 ]
 
 
@@ -73,10 +75,10 @@ def test_direct_conv_vs_fp32(fresh, B, Cin, H, W, Cout, k, s, p, d, bias, cl):
     if bias:
         close(cx.bias.grad, ref.bias.grad)
     kst = xdna_train.kernel_stats()
-    if Cin * k * k <= 512:  # short reductions: forward on the direct kernel too
+    if Cin <= 4 and 16 <= Cout <= 64 and Cin * k * k <= 512:  # RGB input layer: forward
         assert kst.get("direct_conv.fwd", 0) >= 1
         assert "convolution_overrideable" not in xdna_train.fallback_stats()
-    if s == 1:
+    if Cout <= 4 and Cin >= 8 and s == 1:  # RGB output layer: input gradient
         assert kst.get("direct_conv.dgrad", 0) >= 1
 
 
