@@ -385,6 +385,24 @@ b2_status b2_batch_norm_fwd_bf16(const void* x, int layout, const void* w,
                                  int64_t HW, float momentum, float eps,
                                  void* workspace, size_t workspace_bytes,
                                  void* stream);
+
+/* The forward in two calls: the statistics (save_mean / save_invstd and the
+ * running statistics, as above) and the output pass, which can also run the
+ * ops that followed the BatchNorm in the same pass: y = bf16(x*scale + shift),
+ * then, with `residual` (bf16 in x's layout, may be NULL), y = bf16(y +
+ * residual) (an fp32 add, as ATen's), then, with relu != 0, y = y > 0 ? y : 0
+ * (NaN kept).  w, b as above; mean / invstd from the statistics call. */
+b2_status b2_batch_norm_stats_bf16(const void* x, int layout, int pdtype,
+                                   void* rm, void* rv, int rdtype,
+                                   float* save_mean, float* save_invstd,
+                                   int64_t N, int64_t C, int64_t HW,
+                                   float momentum, float eps, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+b2_status b2_batch_norm_apply_bf16(const void* x, int layout, const void* w,
+                                   const void* b, int pdtype, const float* mean,
+                                   const float* invstd, const void* residual,
+                                   int relu, void* y, int64_t N, int64_t C,
+                                   int64_t HW, void* stream);
 /* Backward from the saved batch statistics: dx (may be NULL), dw = sum
  * dy*xhat, db = sum dy (dtype gdtype, each may be NULL). */
 b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout,

@@ -120,6 +120,18 @@ __device__ __forceinline__ float bn_act(float xv, float scale, float shift, floa
   return z > 0.0f ? z : __fmul_rn(z, slope);
 }
 
+// Fused tail of the plain BatchNorm forward (the ops that followed it, run in
+// the same pass with their own roundings): v = bf16(z); then, with a
+// residual, v = bf16(v + r) (an fp32 add, as ATen's bf16 add); then, with
+// relu, v = v > 0 ? v : 0 (NaN kept).
+__device__ __forceinline__ float round_bf(float v) { return bf2f(f2bf(v)); }
+__device__ __forceinline__ float bn_tail(float z, bool has_res, float res, bool relu) {
+  float v = round_bf(z);
+  if (has_res) v = round_bf(__fadd_rn(v, res));
+  if (relu && !(v > 0.0f) && v == v) v = 0.0f;
+  return v;
+}
+
 template <bool ACT>
 __device__ __forceinline__ float bn_dz(float g, float yv, float slope, int relu) {
   if constexpr (!ACT) return g;
@@ -242,10 +254,13 @@ __global__ void bn_channel_stats_kernel(const float* __restrict__ pm, const floa
 }
 
 // y = act(x*scale + shift); one thread per 8 elements (VEC) or per element.
-template <bool VEC>
+// EPI: the fused tail (bn_tail) with an optional residual `res` (x's layout)
+// and ReLU instead of the activation.
+template <bool VEC, bool EPI>
 __global__ void __launch_bounds__(kBnThreads) bn_apply_kernel(
     const uint16_t* __restrict__ x, BnChan ch, const float* __restrict__ mean, const float* __restrict__ invstd,
-    uint16_t* __restrict__ y, long long units, long long units_per_plane, long long C, float slope) {
+    uint16_t* __restrict__ y, long long units, long long units_per_plane, long long C, float slope,
+    const uint16_t* __restrict__ res, int relu) {
   for (long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x; u < units;
        u += (long long)gridDim.x * kBnThreads) {
     const long long c = (u / units_per_plane) % C;
@@ -254,9 +269,20 @@ __global__ void __launch_bounds__(kBnThreads) bn_apply_kernel(
     if constexpr (VEC) {
       float f[8], r[8];
       unpack8(__ldg(reinterpret_cast<const uint4*>(x) + u), f);
+      if constexpr (EPI) {
+        float q[8];
+        if (res) unpack8(__ldg(reinterpret_cast<const uint4*>(res) + u), q);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale, shift, slope);
+        for (int e = 0; e < 8; ++e)
+          r[e] = bn_tail(__fadd_rn(__fmul_rn(f[e], scale), shift), res != nullptr, res ? q[e] : 0.f, relu != 0);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale, shift, slope);
+      }
       reinterpret_cast<uint4*>(y)[u] = pack8(r);
+    } else if constexpr (EPI) {
+      y[u] = f2bf(bn_tail(__fadd_rn(__fmul_rn(bf2f(x[u]), scale), shift), res != nullptr, res ? bf2f(res[u]) : 0.f,
+                          relu != 0));
     } else {
       y[u] = f2bf(bn_act(bf2f(x[u]), scale, shift, slope));
     }
@@ -526,10 +552,10 @@ __global__ void __launch_bounds__(kMergeThreads) bn_nhwc_stats_kernel(
 // y = act(x*scale + shift).  FIXED: CV divides the block size, so every
 // thread keeps one channel group through the grid-stride loop and holds its 8
 // scales and shifts in registers; otherwise they are staged in shared memory.
-template <bool FIXED>
+template <bool FIXED, bool EPI>
 __global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
     const uint16_t* __restrict__ x, BnChan ch, const float* __restrict__ mean, const float* __restrict__ invstd,
-    uint16_t* __restrict__ y, NhwcShape sh, float slope) {
+    uint16_t* __restrict__ y, NhwcShape sh, float slope, const uint16_t* __restrict__ res, int relu) {
   extern __shared__ float tab[];  // scale[C], shift[C] (!FIXED)
   float scale[8], shift[8];
   if constexpr (FIXED) {
@@ -550,22 +576,36 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
   const long long units = sh.P * sh.CV;
   const long long stride = (long long)gridDim.x * kBnThreads;
   const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  const uint4* r4 = reinterpret_cast<const uint4*>(res);
   uint4* y4 = reinterpret_cast<uint4*>(y);
-  auto one = [&](const uint4 v) {
+  const bool has_res = EPI && res != nullptr;
+  auto one = [&](const uint4 v, const uint4 rv) {
     float f[8], r[8];
     unpack8(v, f);
+    if constexpr (EPI) {
+      float q[8];
+      unpack8(rv, q);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
+      for (int e = 0; e < 8; ++e)
+        r[e] = bn_tail(__fadd_rn(__fmul_rn(f[e], scale[e]), shift[e]), has_res, q[e], relu != 0);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
+    }
     return pack8(r);
   };
+  const uint4 zero4 = make_uint4(0, 0, 0, 0);
   long long u = (long long)blockIdx.x * kBnThreads + threadIdx.x;
   if constexpr (FIXED) {  // the channel group is the same for u, u + stride, ...
     for (; u + 3 * stride < units; u += 4 * stride) {
-      uint4 v[4];
+      uint4 v[4], q[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[i] = __ldg(x4 + u + i * stride);
+      for (int i = 0; i < 4; ++i) {
+        v[i] = __ldg(x4 + u + i * stride);
+        q[i] = has_res ? __ldg(r4 + u + i * stride) : zero4;
+      }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) y4[u + i * stride] = one(v[i]);
+      for (int i = 0; i < 4; ++i) y4[u + i * stride] = one(v[i], q[i]);
     }
   }
   for (; u < units; u += stride) {
@@ -577,7 +617,7 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_apply_kernel(
         shift[e] = tab[sh.C + c0 + e];
       }
     }
-    y4[u] = one(__ldg(x4 + u));
+    y4[u] = one(__ldg(x4 + u), has_res ? __ldg(r4 + u) : zero4);
   }
 }
 
@@ -756,12 +796,14 @@ int current_sms() {
   return sm_count(dev);
 }
 
-b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* y, float* mean_out,
-                     float* invstd_out, long long N, long long C, long long HW, float eps, float slope,
-                     float momentum, void* workspace, cudaStream_t st, const char* who) {
+// The statistics passes of the forward (batch mean / invstd, running
+// statistics); the output is written by bn_apply.
+b2_status bn_stats(const uint16_t* x, int layout, const BnChan& ch, float* mean_out, float* invstd_out, long long N,
+                   long long C, long long HW, float eps, float momentum, void* workspace, cudaStream_t st,
+                   const char* who) {
   const int sms = current_sms();
   if (layout == 1) {
-    B2_TRY(check_nhwc(C, {x, y}, who));
+    B2_TRY(check_nhwc(C, {x}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
     const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
     const long long blocks =
@@ -774,19 +816,12 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc sums launch"));
     bn_nhwc_stats_kernel<<<int(C), kMergeThreads, 0, st>>>(x, pa, pb, blocks, C, sh.P, eps,
                                                                           momentum, ch, mean_out, invstd_out);
-    B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc stats launch"));
-    if (kBnThreads % sh.CV == 0)
-      bn_nhwc_apply_kernel<true><<<wave_grid(&bn_nhwc_apply_kernel<true>, 0, sh.P * sh.CV, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out,
-                                                                                      y, sh, slope);
-    else
-      bn_nhwc_apply_kernel<false><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 2 * C * sizeof(float), st>>>(
-          x, ch, mean_out, invstd_out, y, sh, slope);
-    return check_cuda(cudaGetLastError(), "bn nhwc apply launch");
+    return check_cuda(cudaGetLastError(), "bn nhwc stats launch");
   }
   const long long planes = N * C;
   float* pm = static_cast<float*>(workspace);
   float* pq = pm + planes;
-  const bool vec = HW % 8 == 0 && aligned16(x) && aligned16(y);
+  const bool vec = HW % 8 == 0 && aligned16(x);
   const bool warp = warp_per_plane(planes, sms);
   const int sg = stats_grid(planes, warp, sms);
   if (warp && vec) bn_plane_stats_kernel<32, true><<<sg, kBnThreads, 0, st>>>(x, planes, HW, pm, pq);
@@ -796,17 +831,47 @@ b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* 
   B2_TRY(check_cuda(cudaGetLastError(), "bn stats launch"));
   bn_channel_stats_kernel<<<int((C + 3) / 4), 128, 0, st>>>(pm, pq, N, C, HW, eps, momentum, ch, mean_out,
                                                             invstd_out);
-  B2_TRY(check_cuda(cudaGetLastError(), "bn channel launch"));
+  return check_cuda(cudaGetLastError(), "bn channel launch");
+}
+
+// y = act(x*scale + shift) from the statistics; epi: the fused tail with an
+// optional residual (x's layout) and ReLU instead of the activation.
+template <bool EPI>
+b2_status bn_apply_launch(const uint16_t* x, int layout, const BnChan& ch, const float* mean, const float* invstd,
+                          uint16_t* y, long long N, long long C, long long HW, float slope, const uint16_t* res,
+                          int relu, cudaStream_t st, const char* who) {
+  const int sms = current_sms();
+  if (layout == 1) {
+    B2_TRY(check_nhwc(C, {x, y, res}, who));
+    const NhwcShape sh = nhwc_shape(N, C, HW);
+    if (kBnThreads % sh.CV == 0)
+      bn_nhwc_apply_kernel<true, EPI><<<wave_grid(&bn_nhwc_apply_kernel<true, EPI>, 0, sh.P * sh.CV, sms),
+                                        kBnThreads, 0, st>>>(x, ch, mean, invstd, y, sh, slope, res, relu);
+    else
+      bn_nhwc_apply_kernel<false, EPI><<<elem_grid(sh.P * sh.CV, sms), kBnThreads, 2 * C * sizeof(float), st>>>(
+          x, ch, mean, invstd, y, sh, slope, res, relu);
+    return check_cuda(cudaGetLastError(), "bn nhwc apply launch");
+  }
+  const long long planes = N * C;
+  const bool vec = HW % 8 == 0 && aligned16(x) && aligned16(y) && (!res || aligned16(res));
   if (vec) {
     const long long units = planes * (HW / 8);
-    bn_apply_kernel<true><<<wave_grid(&bn_apply_kernel<true>, 0, units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
-                                                                       HW / 8, C, slope);
+    bn_apply_kernel<true, EPI><<<wave_grid(&bn_apply_kernel<true, EPI>, 0, units, sms), kBnThreads, 0, st>>>(
+        x, ch, mean, invstd, y, units, HW / 8, C, slope, res, relu);
   } else {
     const long long units = planes * HW;
-    bn_apply_kernel<false><<<elem_grid(units, sms), kBnThreads, 0, st>>>(x, ch, mean_out, invstd_out, y, units,
-                                                                        HW, C, slope);
+    bn_apply_kernel<false, EPI><<<elem_grid(units, sms), kBnThreads, 0, st>>>(x, ch, mean, invstd, y, units, HW, C,
+                                                                              slope, res, relu);
   }
   return check_cuda(cudaGetLastError(), "bn apply launch");
+}
+
+b2_status bn_forward(const uint16_t* x, int layout, const BnChan& ch, uint16_t* y, float* mean_out,
+                     float* invstd_out, long long N, long long C, long long HW, float eps, float slope,
+                     float momentum, void* workspace, cudaStream_t st, const char* who) {
+  if (layout == 1) B2_TRY(check_nhwc(C, {x, y}, who));
+  B2_TRY(bn_stats(x, layout, ch, mean_out, invstd_out, N, C, HW, eps, momentum, workspace, st, who));
+  return bn_apply_launch<false>(x, layout, ch, mean_out, invstd_out, y, N, C, HW, slope, nullptr, 0, st, who);
 }
 
 template <bool ACT>
@@ -935,6 +1000,38 @@ b2_status b2_batch_norm_fwd_bf16(const void* x, int layout, const void* w, const
   const BnChan ch{w, b, pdtype, rm, rv, rdtype};
   return bn_forward(static_cast<const uint16_t*>(x), layout, ch, static_cast<uint16_t*>(y), save_mean, save_invstd,
                     N, C, HW, eps, 1.0f, momentum, workspace, static_cast<cudaStream_t>(stream), who);
+}
+
+b2_status b2_batch_norm_stats_bf16(const void* x, int layout, int pdtype, void* rm, void* rv, int rdtype,
+                                   float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t HW,
+                                   float momentum, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_stats_bf16";
+  B2_TRY(check_common(N, C, HW, layout, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(rdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C == 0) return B2_OK;
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!x || !save_mean || !save_invstd || (!rm) != (!rv)) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  const BnChan ch{nullptr, nullptr, pdtype, rm, rv, rdtype};
+  return bn_stats(static_cast<const uint16_t*>(x), layout, ch, save_mean, save_invstd, N, C, HW, eps, momentum,
+                  workspace, static_cast<cudaStream_t>(stream), who);
+}
+
+b2_status b2_batch_norm_apply_bf16(const void* x, int layout, const void* w, const void* b, int pdtype,
+                                   const float* mean, const float* invstd, const void* residual, int relu, void* y,
+                                   int64_t N, int64_t C, int64_t HW, void* stream) {
+  const char* who = "b2_batch_norm_apply_bf16";
+  if (layout != 0 && layout != 1) return set_error(B2_ERR_INVALID, "%s: layout", who);
+  if (N < 0 || C < 0 || HW < 0) return set_error(B2_ERR_INVALID, "%s: negative size", who);
+  if (!valid_pdtype(pdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C * HW == 0) return B2_OK;
+  if (!x || !y || !mean || !invstd) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  const BnChan ch{w, b, pdtype, nullptr, nullptr, B2_F32};
+  auto st = static_cast<cudaStream_t>(stream);
+  auto* xp = static_cast<const uint16_t*>(x);
+  auto* yp = static_cast<uint16_t*>(y);
+  auto* rp = static_cast<const uint16_t*>(residual);
+  if (!residual && !relu) return bn_apply_launch<false>(xp, layout, ch, mean, invstd, yp, N, C, HW, 1.0f, nullptr, 0, st, who);
+  return bn_apply_launch<true>(xp, layout, ch, mean, invstd, yp, N, C, HW, 1.0f, rp, relu, st, who);
 }
 
 b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout, const void* w, int pdtype,

@@ -55,6 +55,37 @@ std::unordered_map<void*, Attachment> g_attach;      // storage data ptr -> pack
 std::unordered_map<void*, std::vector<WeightSlot>> g_wslots;  // storage data ptr -> packed weights
 std::atomic<int64_t> g_nwslots{0};
 int64_t g_whits = 0, g_wmisses = 0;
+
+// pending outputs with foldable tails, and the storages their producers read
+struct EpiSlot {
+  std::shared_ptr<EpiSpec> spec;
+  std::vector<int64_t> sizes, strides;
+  int64_t offset = 0;
+  std::vector<void*> inputs;
+};
+std::unordered_map<void*, EpiSlot> g_epi;            // output storage -> slot
+std::unordered_multimap<void*, void*> g_readers;     // input storage -> pending output storage
+std::atomic<int64_t> g_nreaders{0};
+int64_t g_folded = 0;
+
+// Moves the slot of `out` out of the tables (destroyed by the caller, outside
+// the lock: it may hold the last reference to a tensor).
+EpiSlot take_epi_locked(void* out) {
+  EpiSlot slot;
+  auto it = g_epi.find(out);
+  if (it == g_epi.end()) return slot;
+  slot = std::move(it->second);
+  g_epi.erase(it);
+  for (void* in : slot.inputs) {
+    auto range = g_readers.equal_range(in);
+    for (auto r = range.first; r != range.second;) {
+      if (r->second == out) r = g_readers.erase(r);
+      else ++r;
+    }
+  }
+  g_nreaders.store(int64_t(g_readers.size()));
+  return slot;
+}
 int64_t g_order = 0;
 int64_t g_started = 0, g_dropped = 0, g_kicks = 0, g_deferred = 0;
 int64_t g_dx_this_step = 0, g_k_prev = -1, g_k_learned = 0;
@@ -89,10 +120,10 @@ void defer_write(const at::Tensor& target, std::function<void()> job) {
   }
 }
 
-void materialize(const at::Tensor& t) {
-  if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
-  void* key = t.storage().mutable_data();
+namespace {
+void materialize_key(void* key) {
   std::function<void()> fn;
+  EpiSlot slot;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_jobs.find(key);
@@ -101,8 +132,69 @@ void materialize(const at::Tensor& t) {
     g_jobs.erase(it);
     ++g_started;
     g_pending_jobs.store(int64_t(g_jobs.size()));
+    slot = take_epi_locked(key);
   }
   run_job(fn);
+}
+}  // namespace
+
+void materialize(const at::Tensor& t) {
+  if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
+  materialize_key(t.storage().mutable_data());
+}
+
+void defer_epilogue(const at::Tensor& out, const std::vector<at::Tensor>& inputs, std::shared_ptr<EpiSpec> spec,
+                    std::function<void()> job) {
+  defer_write(out, std::move(job));
+  void* key = out.storage().mutable_data();
+  std::lock_guard<std::mutex> lk(g_mu);
+  EpiSlot& slot = g_epi[key];
+  slot.spec = std::move(spec);
+  slot.sizes = out.sizes().vec();
+  slot.strides = out.strides().vec();
+  slot.offset = out.storage_offset();
+  for (const at::Tensor& in : inputs) {
+    if (!in.defined() || !in.has_storage()) continue;
+    void* ik = in.storage().mutable_data();
+    slot.inputs.push_back(ik);
+    g_readers.emplace(ik, key);
+  }
+  g_nreaders.store(int64_t(g_readers.size()));
+}
+
+std::shared_ptr<EpiSpec> find_epilogue(const at::Tensor& t) {
+  if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return nullptr;
+  void* key = t.storage().mutable_data();
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_epi.find(key);
+  if (it == g_epi.end() || !g_jobs.count(key)) return nullptr;
+  const EpiSlot& s = it->second;
+  if (s.sizes != t.sizes().vec() || s.strides != t.strides().vec() || s.offset != t.storage_offset()) return nullptr;
+  ++g_folded;
+  return s.spec;
+}
+
+void add_epilogue_input(const at::Tensor& out, const at::Tensor& input) {
+  if (!input.defined() || !input.has_storage()) return;
+  void* key = out.storage().mutable_data();
+  void* ik = input.storage().mutable_data();
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_epi.find(key);
+  if (it == g_epi.end()) return;
+  it->second.inputs.push_back(ik);
+  g_readers.emplace(ik, key);
+  g_nreaders.store(int64_t(g_readers.size()));
+}
+
+void before_write(const at::Tensor& t) {
+  if (g_nreaders.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
+  std::vector<void*> outs;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto range = g_readers.equal_range(t.storage().mutable_data());
+    for (auto r = range.first; r != range.second; ++r) outs.push_back(r->second);
+  }
+  for (void* o : outs) materialize_key(o);
 }
 
 bool has_pending(const at::Tensor& t) {
@@ -113,12 +205,16 @@ bool has_pending(const at::Tensor& t) {
 
 void materialize_all() {
   std::vector<std::pair<int64_t, std::function<void()>>> fns;
+  std::unordered_map<void*, EpiSlot> slots;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto& kv : g_jobs) fns.emplace_back(kv.second.order, std::move(kv.second.fn));
     g_started += int64_t(g_jobs.size());
     g_jobs.clear();
     g_pending_jobs.store(0);
+    slots.swap(g_epi);
+    g_readers.clear();
+    g_nreaders.store(0);
   }
   std::sort(fns.begin(), fns.end(), [](auto& a, auto& b) { return a.first < b.first; });
   for (auto& f : fns) run_job(f.second);
@@ -129,6 +225,7 @@ void on_release(void* ptr) {
   Job dropped;
   Attachment att;
   std::vector<WeightSlot> slots;
+  EpiSlot epi;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto ws = g_wslots.find(ptr);
@@ -137,6 +234,7 @@ void on_release(void* ptr) {
       g_wslots.erase(ws);
       g_nwslots.store(int64_t(g_wslots.size()));
     }
+    epi = take_epi_locked(ptr);
     auto it = g_jobs.find(ptr);
     if (it != g_jobs.end()) {
       dropped = std::move(it->second);
@@ -177,7 +275,8 @@ std::map<std::string, int64_t> deferred_stats() {
   return {{"pending", int64_t(g_jobs.size())}, {"deferred", g_deferred}, {"started", g_started},
           {"dropped", g_dropped},          {"kicks", g_kicks},       {"k_learned", g_k_learned},
           {"attached_rows", int64_t(g_attach.size())}, {"packed_weights", int64_t(g_wslots.size())},
-          {"packed_weight_hits", g_whits}, {"packed_weight_misses", g_wmisses}};
+          {"packed_weight_hits", g_whits}, {"packed_weight_misses", g_wmisses},
+          {"folded_tails", g_folded}, {"pending_tails", int64_t(g_epi.size())}};
 }
 
 void note_write(const at::Tensor& t) {

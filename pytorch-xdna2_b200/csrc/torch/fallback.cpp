@@ -120,11 +120,18 @@ void cuda_alias_fallback(const c10::OperatorHandle& op, torch::jit::Stack* stack
   auto args_begin = stack->end() - nargs;
   std::vector<c10::IValue> originals(args_begin, stack->end());
   for (size_t i = 0; i < nargs; ++i) args_begin[i] = convert_in(args_begin[i], map, dev);
-  // aliases of mutated arguments, to sync back after the call
+  // aliases of mutated arguments, to sync back after the call; deferred
+  // producers that read a mutated storage run before the write lands
   std::vector<std::pair<size_t, c10::IValue>> written;
   for (size_t i = 0; i < nargs; ++i) {
     const auto* ai = schema.arguments()[i].alias_info();
-    if (ai && ai->isWrite()) written.emplace_back(i, args_begin[i]);
+    if (ai && ai->isWrite()) {
+      written.emplace_back(i, args_begin[i]);
+      const c10::IValue& o = originals[i];
+      if (o.isTensor()) before_write(o.toTensor());
+      else if (o.isTensorList())
+        for (const at::Tensor& t : o.toTensorList()) before_write(t);
+    }
   }
 
   {
@@ -179,6 +186,44 @@ void cuda_alias_fallback(const c10::OperatorHandle& op, torch::jit::Stack* stack
   }
 }
 
+// relu_ / add_.Tensor on a pending BatchNorm output fold into its output pass
+// (the residual add first, then the ReLU, in that order only); anything else
+// takes the CUDA-alias path.
+void relu_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
+  const at::Tensor self = (*stack)[stack->size() - 1].toTensor();
+  if (g_bn_epilogue.load() && self.device().type() == kXdna) {
+    auto spec = find_epilogue(self);
+    if (spec && !spec->relu) {
+      spec->relu = true;
+      return;  // the stack holds self, the op's return
+    }
+  }
+  cuda_alias_fallback(op, stack);
+}
+
+void add_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
+  auto args = stack->end() - 3;  // self, other, alpha
+  if (g_bn_epilogue.load() && args[0].isTensor() && args[1].isTensor()) {
+    const at::Tensor self = args[0].toTensor();
+    const at::Tensor other = args[1].toTensor();
+    if (self.device().type() == kXdna && other.defined() && other.device().type() == kXdna &&
+        self.scalar_type() == at::kBFloat16 && other.scalar_type() == at::kBFloat16 && args[2].toScalar().toDouble() == 1.0 &&
+        other.sizes() == self.sizes() && other.strides() == self.strides() &&
+        other.storage().data() != self.storage().data()) {
+      auto spec = find_epilogue(self);
+      if (spec && !spec->relu && !spec->residual.defined()) {
+        materialize(other);
+        spec->residual = other;
+        add_epilogue_input(self, other);
+        torch::jit::drop(*stack, 3);
+        stack->push_back(self);
+        return;
+      }
+    }
+  }
+  cuda_alias_fallback(op, stack);
+}
+
 }  // namespace
 
 TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {
@@ -200,6 +245,8 @@ TORCH_LIBRARY_IMPL(_, PrivateUse1, m) {
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   const auto boxed = [] { return torch::CppFunction::makeFromBoxedFunction<&cuda_alias_fallback>(); };
   m.impl("mse_loss", boxed());
+  m.impl("relu_", torch::CppFunction::makeFromBoxedFunction<&relu_inplace>());
+  m.impl("add_.Tensor", torch::CppFunction::makeFromBoxedFunction<&add_inplace>());
   for (const char* op :
        {"_foreach_add_.Scalar", "_foreach_add_.List", "_foreach_add_.ScalarList", "_foreach_add_.Tensor",
         "_foreach_mul_.Scalar", "_foreach_mul_.List", "_foreach_mul_.ScalarList", "_foreach_mul_.Tensor",

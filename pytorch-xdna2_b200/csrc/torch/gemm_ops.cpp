@@ -106,6 +106,7 @@ at::Tensor mm(const at::Tensor& self, const at::Tensor& mat2) {
 }
 
 at::Tensor& mm_out(const at::Tensor& self, const at::Tensor& mat2, at::Tensor& out) {
+  before_write(out);
   note_write(out);
   c10::cuda::CUDAGuard g(self.device().index());
   if (eligible(self, mat2) && self.dim() == 2 && mat2.dim() == 2 && self.size(1) > 0) {
@@ -134,6 +135,7 @@ at::Tensor addmm(const at::Tensor& self, const at::Tensor& mat1, const at::Tenso
 
 at::Tensor& addmm_out(const at::Tensor& self, const at::Tensor& mat1, const at::Tensor& mat2, const at::Scalar& beta,
                       const at::Scalar& alpha, at::Tensor& out) {
+  before_write(out);
   note_write(out);
   c10::cuda::CUDAGuard g(mat1.device().index());
   if (eligible(mat1, mat2) && mat1.dim() == 2 && mat2.dim() == 2 && mat1.size(1) > 0 && !out.is_same(self)) {
@@ -159,6 +161,7 @@ at::Tensor bmm(const at::Tensor& self, const at::Tensor& mat2) {
 }
 
 at::Tensor& bmm_out(const at::Tensor& self, const at::Tensor& mat2, at::Tensor& out) {
+  before_write(out);
   note_write(out);
   c10::cuda::CUDAGuard g(self.device().index());
   if (eligible(self, mat2) && self.dim() == 3 && mat2.dim() == 3 && self.size(2) > 0) {

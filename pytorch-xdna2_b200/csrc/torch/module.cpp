@@ -289,6 +289,8 @@ PYBIND11_MODULE(_C, m) {
   });
   m.def("graph_capture_end", [](uintptr_t stream) { graph_capture_end(reinterpret_cast<cudaStream_t>(stream)); });
   m.def("graph_pool_release", [](int pool) { graph_pool_release(pool); });
+  m.def("set_bn_epilogue", [](bool on) { return g_bn_epilogue.exchange(on); });
+  m.def("bn_epilogue", [] { return g_bn_epilogue.load(); });
   m.def("fallback_stats", [] {
     py::dict d;
     for (auto& kv : fallback_stats()) {

@@ -13,6 +13,14 @@
 #include "xdna.h"
 
 namespace xdna {
+
+// XDNA_BN_EPILOGUE=0 turns the folding of add_ / relu_ into BatchNorm's
+// output pass off (xdna_train.set_fusion switches it at run time).
+std::atomic<bool> g_bn_epilogue{[] {
+  const char* s = std::getenv("XDNA_BN_EPILOGUE");
+  return !s || std::string(s) != "0";
+}()};
+
 namespace {
 
 int vec_dtype(const std::optional<at::Tensor>& t, int64_t C) {
@@ -79,6 +87,31 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
   materialize(input);
   const int pdt = defined(weight) ? pw : pb;
   c10::cuda::CUDAGuard g(dev);
+  if (g_bn_epilogue.load() && g_mode.load() > 1) {
+    // statistics now; the output pass waits for the first reader of `out`,
+    // so that a residual add_ and a relu_ on `out` fold into it
+    XDNA_B2(b2_batch_norm_stats_bf16(input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
+                                     const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(),
+                                     save_invstd.data_ptr<float>(), N, C, HW, float(momentum), float(eps),
+                                     ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+    count_launch("batch_norm.fwd", 2);
+    auto spec = std::make_shared<EpiSpec>();
+    const at::Tensor w = defined(weight) ? *weight : at::Tensor();
+    const at::Tensor b = defined(bias) ? *bias : at::Tensor();
+    if (w.defined()) materialize(w);
+    if (b.defined()) materialize(b);
+    void* y = out.data_ptr();  // raw: an unread output must stay free to drop its pass
+    defer_epilogue(out, {input, w, b}, spec, [input, w, b, stats, spec, y, layout, pdt, N, C, HW, dev]() {
+      c10::cuda::CUDAGuard guard(dev);
+      const at::Tensor& r = spec->residual;
+      XDNA_B2(b2_batch_norm_apply_bf16(input.data_ptr(), layout, w.defined() ? w.data_ptr() : nullptr,
+                                       b.defined() ? b.data_ptr() : nullptr, pdt, stats[0].data_ptr<float>(),
+                                       stats[1].data_ptr<float>(), r.defined() ? r.data_ptr() : nullptr,
+                                       spec->relu ? 1 : 0, y, N, C, HW, stream(dev)));
+      count_launch("batch_norm.fwd");
+    });
+    return {out, save_mean, save_invstd};
+  }
   XDNA_B2(b2_batch_norm_fwd_bf16(input.data_ptr(), layout, ptr_of(weight), ptr_of(bias), pdt,
                                  const_cast<void*>(ptr_of(running_mean)), const_cast<void*>(ptr_of(running_var)),
                                  rdm, out.data_ptr(), save_mean.data_ptr<float>(), save_invstd.data_ptr<float>(), N,

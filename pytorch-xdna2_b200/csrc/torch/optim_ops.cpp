@@ -54,7 +54,10 @@ void fused_adam_impl(at::TensorList params, at::TensorList grads, at::TensorList
                      double beta2, double wd, double eps, bool amsgrad, bool maximize,
                      const std::optional<at::Tensor>& grad_scale, const std::optional<at::Tensor>& found_inf,
                      bool adamw) {
-  for (const at::Tensor& p : params) note_write(p);
+  for (const at::Tensor& p : params) {
+    before_write(p);
+    note_write(p);
+  }
   at::ScalarType pt, st;
   if (!supported(params, grads, m, v, vmax, steps, amsgrad, pt, st)) {
     // unsupported layout/dtype mix: ATen's CUDA fused kernel on aliases

@@ -193,7 +193,10 @@ at::Tensor& set_empty(at::Tensor& self) {
 // ---- copies ----------------------------------------------------------------------------
 
 at::Tensor copy_from(const at::Tensor& self, const at::Tensor& dst, bool non_blocking) {
-  if (dst.device().type() == kXdna) note_write(dst);
+  if (dst.device().type() == kXdna) {
+    before_write(dst);
+    note_write(dst);
+  }
   // self -> dst; at least one of them is on xdna.
   const bool src_x = self.device().type() == kXdna;
   const bool dst_x = dst.device().type() == kXdna;

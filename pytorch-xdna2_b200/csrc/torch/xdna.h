@@ -85,6 +85,24 @@ extern std::atomic<int64_t> g_pending_jobs;
 void attach_rows(const at::Tensor& input, const at::Tensor& rows);
 at::Tensor find_rows(const at::Tensor& input);
 
+// Fused tails of a deferred producer (a BatchNorm whose output pass waits for
+// its first reader): the in-place ops that follow it on exactly its output
+// tensor (a residual add_, then a relu_) fold into that pass instead of
+// running as passes of their own.  Readers materialize it as any deferred
+// write; a write into a storage it reads (before_write: the CUDA-alias
+// fallback, copies, out= and fused optimizer ops call it first) runs it
+// before the write lands.
+struct EpiSpec {
+  at::Tensor residual;
+  bool relu = false;
+};
+void defer_epilogue(const at::Tensor& out, const std::vector<at::Tensor>& inputs, std::shared_ptr<EpiSpec> spec,
+                    std::function<void()> job);
+std::shared_ptr<EpiSpec> find_epilogue(const at::Tensor& t);  // t is exactly a pending output
+void add_epilogue_input(const at::Tensor& out, const at::Tensor& input);
+void before_write(const at::Tensor& t);
+extern std::atomic<bool> g_bn_epilogue;  // fold add_ / relu_ into BatchNorm's output pass
+
 // Packed GEMM-operand forms of frozen weights (the reference's weight-encode
 // cache keyed on pointer, version counter and write epoch,
 // torch_xdna_device.cpp:2200-2271): found while the weight's version, geometry

@@ -27,6 +27,7 @@ from .device import (
     reset_mapped_cpu_stats,
     set_npu_mode,
     set_conv_paths,
+    set_fusion,
     synchronize,
     try_register_xdna_device,
     wait_for_builds,
@@ -48,6 +49,7 @@ __all__ = [
     "autotune_result",
     "set_npu_mode",
     "set_conv_paths",
+    "set_fusion",
     "npu_mode",
     "wait_for_builds",
     "reset_fallback_stats",

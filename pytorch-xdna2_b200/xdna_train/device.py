@@ -341,6 +341,19 @@ def set_conv_paths(conv1x1=None, general=None):
     return tuple(bool(v) for v in _C.set_conv_paths(conv1x1, general))
 
 
+def set_fusion(bn_epilogue=None) -> bool:
+    """Fold a residual ``add_`` and a ``relu_`` that follow a training-mode
+    BatchNorm on its output tensor into BatchNorm's output pass (the pass
+    waits for the output's first reader, like a deferred weight gradient; a
+    write into a tensor it reads runs it first).  On by default
+    (``XDNA_BN_EPILOGUE=0`` at start-up turns it off); ``None`` leaves it as
+    it is.  Returns the previous setting."""
+    register_xdna_device()
+    if bn_epilogue is None:
+        return bool(_C.bn_epilogue())
+    return bool(_C.set_bn_epilogue(bool(bn_epilogue)))
+
+
 def wait_for_builds(timeout: float | None = None) -> bool:
     """Kernels are compiled ahead of time; nothing to wait for."""
     del timeout

@@ -209,3 +209,72 @@ def test_eval_mode_and_mixed_dtypes():
     ref.eval()
     assert rel(bx(x.bfloat16().to(X)), ref(x.bfloat16().float())) < 1e-2
     assert xdna_train.fallback_stats()["aten::native_batch_norm"]["calls"] == 1
+
+
+# ---- BatchNorm tails folded into the output pass ---------------------------------
+
+def _block(cl, fused, seed=0):
+    """conv -> bn -> (+ identity) -> relu_, the residual tail of a ResNet
+    bottleneck, forward and backward; fused or not."""
+    xdna_train.set_fusion(bn_epilogue=fused)
+    torch.manual_seed(seed)
+    conv = nn.Conv2d(64, 64, 3, padding=1, bias=False).bfloat16()
+    bn = nn.BatchNorm2d(64).bfloat16()
+    mf = torch.channels_last if cl else torch.contiguous_format
+    x = torch.randn(4, 64, 14, 14).bfloat16()
+    idn = torch.randn(4, 64, 14, 14).bfloat16()
+    g = torch.randn(4, 64, 14, 14).bfloat16()
+    conv, bn = conv.to(X), bn.to(X)
+    xx = x.to(X).contiguous(memory_format=mf).requires_grad_()
+    ii = idn.to(X).contiguous(memory_format=mf).requires_grad_()
+    out = bn(conv(xx))
+    out += ii
+    out.relu_()
+    out.backward(g.to(X).contiguous(memory_format=mf))
+    res = {"y": out.detach().cpu(), "dx": xx.grad.cpu(), "di": ii.grad.cpu(), "dw": conv.weight.grad.cpu(),
+           "dg": bn.weight.grad.cpu(), "db": bn.bias.grad.cpu(), "rm": bn.running_mean.cpu()}
+    return res
+
+
+@pytest.mark.parametrize("cl", [False, True])
+def test_residual_add_and_relu_fold_into_batch_norm(cl):
+    before = xdna_train.async_dw_stats()["folded_tails"]
+    try:
+        fused = _block(cl, True)
+        folded = xdna_train.async_dw_stats()["folded_tails"] - before
+        fb = xdna_train.fallback_stats()
+        xdna_train.reset_fallback_stats()
+        plain = _block(cl, False)
+        fp = xdna_train.fallback_stats()
+    finally:
+        xdna_train.set_fusion(bn_epilogue=True)
+    assert folded >= 2
+    calls = lambda d, k: d.get(k, {}).get("calls", 0)  # noqa: E731
+    # unfused: the residual add and the ReLU ran as ATen passes (BatchNorm's
+    # num_batches_tracked += 1 is an add_ in both runs)
+    assert calls(fb, "aten::relu_") == 0 and calls(fp, "aten::relu_") == 1
+    assert calls(fp, "aten::add_.Tensor") == calls(fb, "aten::add_.Tensor") + 1
+    for k in fused:
+        # the same roundings in the same order: bit-identical (zeros compared by value)
+        assert torch.equal(fused[k].float(), plain[k].float()), k
+
+
+def test_writes_into_a_pending_pass_inputs_run_it_first():
+    """The folded pass reads x, the residual and the affine parameters when its
+    output is first read: writes into any of them in between must not leak in."""
+    torch.manual_seed(1)
+    bn = nn.BatchNorm2d(32).bfloat16().to(X)
+    x = torch.randn(2, 32, 6, 6).bfloat16()
+    idn = torch.randn(2, 32, 6, 6).bfloat16()
+    with torch.no_grad():
+        ref = torch.relu(nn.functional.batch_norm(x.float(), None, None, bn.weight.float().cpu(),
+                                                  bn.bias.float().cpu(), True) + idn.float())
+        for write in (lambda xx, ii: xx.zero_(), lambda xx, ii: ii.mul_(0), lambda xx, ii: bn.weight.mul_(3),
+                      lambda xx, ii: ii.copy_(torch.zeros_like(ii))):
+            bn.weight.fill_(1.0)
+            xx, ii = x.to(X), idn.to(X)
+            y = bn(xx)
+            y += ii
+            y.relu_()
+            write(xx, ii)
+            assert (y.float().cpu() - ref).abs().max().item() <= 3e-2 * ref.abs().max().item()
