@@ -170,8 +170,12 @@ std::shared_ptr<EpiSpec> find_epilogue(const at::Tensor& t) {
   if (it == g_epi.end() || !g_jobs.count(key)) return nullptr;
   const EpiSlot& s = it->second;
   if (s.sizes != t.sizes().vec() || s.strides != t.strides().vec() || s.offset != t.storage_offset()) return nullptr;
-  ++g_folded;
   return s.spec;
+}
+
+void note_folded() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  ++g_folded;
 }
 
 void add_epilogue_input(const at::Tensor& out, const at::Tensor& input) {

@@ -195,6 +195,7 @@ void relu_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
     auto spec = find_epilogue(self);
     if (spec && !spec->relu) {
       spec->relu = true;
+      note_folded();
       return;  // the stack holds self, the op's return
     }
   }
@@ -215,6 +216,7 @@ void add_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
         materialize(other);
         spec->residual = other;
         add_epilogue_input(self, other);
+        note_folded();
         torch::jit::drop(*stack, 3);
         stack->push_back(self);
         return;

@@ -100,6 +100,7 @@ void defer_epilogue(const at::Tensor& out, const std::vector<at::Tensor>& inputs
                     std::function<void()> job);
 std::shared_ptr<EpiSpec> find_epilogue(const at::Tensor& t);  // t is exactly a pending output
 void add_epilogue_input(const at::Tensor& out, const at::Tensor& input);
+void note_folded();  // an op folded into a pending output pass (async_dw_stats "folded_tails")
 void before_write(const at::Tensor& t);
 extern std::atomic<bool> g_bn_epilogue;  // fold add_ / relu_ into BatchNorm's output pass
 
