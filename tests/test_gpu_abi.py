@@ -145,6 +145,11 @@ LARGE = [  # the reference's run_conv3x3w_torch.py shapes (:22-35) and the READM
     (1, 64, 8, 224, 64, False),
     (16, 128, 36, 36, 128, True),
     (8, 512, 18, 18, 512, False),
+    # wide convolutions on the halo kernel: windows of one and two TMA boxes,
+    # the largest window that fits, and one too wide for it (the plain pair kernel)
+    (2, 256, 10, 72, 256, True),
+    (1, 192, 4, 150, 320, False),
+    (1, 256, 3, 200, 256, False),
 ]
 
 
