@@ -63,12 +63,12 @@ def graph(g: XdnaGraph, pool: int = 0, stream: torch.cuda.Stream | None = None,
     with torch.cuda.graph(g.cuda_graph, stream=stream, capture_error_mode=capture_error_mode):
         s = torch.cuda.current_stream()
         g.pool_id = native.graph_capture_begin(s.device_index, s.cuda_stream, int(pool))
+        if g._finalizer is None:  # the pool goes back with the graph, also after a failed capture
+            g._finalizer = weakref.finalize(g, native.graph_pool_release, g.pool_id)
         try:
             yield g
         finally:
             native.graph_capture_end(s.cuda_stream)
-    if g._finalizer is None:
-        g._finalizer = weakref.finalize(g, native.graph_pool_release, g.pool_id)
 
 
 def make_graphed_step(step, warmup: int = 3):
