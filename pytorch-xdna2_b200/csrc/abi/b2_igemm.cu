@@ -63,7 +63,6 @@ struct Params {
   int gemm_split;    // 1: tile-space slices are split-K ranges writing fp32 partials
   int tma_store;     // GEMM: bf16 D written by TMA stores of shared-memory staged boxes
   int win_boxes, win_box_rows;  // conv halo kernel: the A window is win_boxes TMA boxes of win_box_rows rows
-  int ring;                     // single-CTA halo kernel: depth of the B ring (<= kMaxRing)
 };
 
 template <int BN>
@@ -1054,217 +1053,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 
-
-// The single-CTA conv kernel with the same halo reuse, for Cout <= 128.
-// Narrow tiles are bound by load latency, not L2 bandwidth: a tap's MMAs take
-// ~140 clocks at 64 output channels, and the ring of the per-tap kernel holds
-// only 8 loads of 24 KB.  With the window loaded once per chunk a tap stages
-// just its B slice (8 or 16 KB), so the same shared memory holds a ring of
-// 10-20 taps in flight (p.ring, as deep as the window leaves room for).
-constexpr int kMaxRing = 24;
-
-template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
-    igemm_halo_kernel(const __grid_constant__ CUtensorMap tma_win, const __grid_constant__ CUtensorMap tma_b,
-                      const Params p) {
-  constexpr uint32_t kBBytes = BN * BK * 2;
-  constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, false, false);
-  constexpr uint32_t kTmemCols = 2 * BN;
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  const int NB = p.ring;
-  const uint32_t box_bytes = uint32_t(p.win_box_rows) * 128u;
-  const uint32_t a_bytes = uint32_t(p.win_boxes) * box_bytes;
-  uint8_t* a_base = smem;
-  uint8_t* b_base = smem + 2 * a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + NB * kBBytes);
-  uint64_t* a_full = bars;
-  uint64_t* a_empty = bars + 2;
-  uint64_t* b_full = bars + 4;
-  uint64_t* b_empty = b_full + kMaxRing;
-  uint64_t* tfull = b_empty + kMaxRing;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  const int chunks = p.num_kb / 9;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&a_full[s]), 1);
-      mbar_init(smem_u32(&a_empty[s]), 1);
-      mbar_init(smem_u32(&tfull[s]), 1);
-      mbar_init(smem_u32(&tempty[s]), kEpiWarps);
-    }
-    for (int s = 0; s < NB; ++s) {
-      mbar_init(smem_u32(&b_full[s]), 1);
-      mbar_init(smem_u32(&b_empty[s]), 1);
-    }
-    mbar_init(smem_u32(mma_done), 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int ntiles = p.tiles_m * p.tiles_n;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------ producer ------------------------------
-      tma_prefetch_desc(&tma_win);
-      tma_prefetch_desc(&tma_b);
-      int as = 0, bs = 0;
-      uint32_t aph = 0, bph = 0;
-      int a_last[2] = {-1, -1};
-      int b_last[kMaxRing];
-      for (int s = 0; s < kMaxRing; ++s) b_last[s] = -1;
-      bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const int nt = t % p.tiles_n, mt = t / p.tiles_n;
-        for (int ch = 0; ch < chunks && ok; ++ch) {
-          if (!mbar_wait(smem_u32(&a_empty[as]), aph ^ 1, p.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t fa = smem_u32(&a_full[as]);
-          mbar_arrive_expect_tx(fa, a_bytes);
-          a_last[as] = int(aph);
-          const uint32_t sa = smem_u32(a_base + as * a_bytes);
-          for (int i = 0; i < p.win_boxes; ++i)
-            tma_load_3d(sa + i * box_bytes, &tma_win, fa, ch * BK, mt * BM + i * p.win_box_rows, 0);
-          if (++as == 2) {
-            as = 0;
-            aph ^= 1;
-          }
-          for (int tap = 0; tap < 9; ++tap) {
-            if (!mbar_wait(smem_u32(&b_empty[bs]), bph ^ 1, p.status, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t fb = smem_u32(&b_full[bs]);
-            mbar_arrive_expect_tx(fb, kBBytes);
-            b_last[bs] = int(bph);
-            tma_load_3d(smem_u32(b_base + bs * kBBytes), &tma_b, fb, (ch * 9 + tap) * BK, nt * BN, 0);
-            if (++bs == NB) {
-              bs = 0;
-              bph ^= 1;
-            }
-          }
-        }
-      }
-      if (!ok) {
-        for (int s = 0; s < 2; ++s)
-          if (a_last[s] >= 0) mbar_wait(smem_u32(&a_full[s]), uint32_t(a_last[s]), p.status, nullptr);
-        for (int s = 0; s < NB; ++s)
-          if (b_last[s] >= 0) mbar_wait(smem_u32(&b_full[s]), uint32_t(b_last[s]), p.status, nullptr);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------ MMA issuer ----------------------------
-      int as = 0, bs = 0, acc = 0;
-      uint32_t aph = 0, bph = 0, acc_phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        for (int ch = 0; ch < chunks && ok; ++ch) {
-          if (!mbar_wait(smem_u32(&a_full[as]), aph, p.status, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(a_base + as * a_bytes);
-          for (int tap = 0; tap < 9; ++tap) {
-            if (!mbar_wait(smem_u32(&b_full[bs]), bph, p.status, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const int dy = tap / 3, dx = tap - dy * 3;
-            const int shift = dy * p.wp + dx;
-            const uint32_t sb = smem_u32(b_base + bs * kBBytes);
-#pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              tc_mma_f16(d_tmem, smem_desc_sw128_row(sa, shift, uint32_t(k * 32)),
-                         smem_desc_sw128(sb + k * 32, 16, 1024), kIdesc, (ch > 0 || tap > 0 || k > 0) ? 1u : 0u);
-            tc_commit(smem_u32(&b_empty[bs]));
-            if (++bs == NB) {
-              bs = 0;
-              bph ^= 1;
-            }
-          }
-          if (!ok) break;
-          tc_commit(smem_u32(&a_empty[as]));
-          if (++as == 2) {
-            as = 0;
-            aph ^= 1;
-          }
-        }
-        if (!ok) break;
-        tc_commit(smem_u32(&tfull[acc]));
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
-      }
-      tc_commit(smem_u32(mma_done));
-      mbar_wait(smem_u32(mma_done), 0, p.status, nullptr);
-    }
-    __syncwarp();
-  } else {
-    // -------------------------------- epilogue ------------------------------
-    const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int row = quarter * 32 + lane;
-    constexpr int kChunks = BN / 64;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-      const int nt = t % p.tiles_n, mt = t / p.tiles_n;
-      uint16_t* obase = conv_row_base(p, mt, row);
-      bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t taddr =
-          tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
-#pragma unroll 1
-      for (int j = 0; j < kChunks; ++j) {
-        uint32_t r[32];
-        tmem_ld32(taddr + j * 32, r);
-        tc_wait_ld();
-        epi_conv(p, obase, nt * BN + half * (BN / 2) + j * 32, lane, r);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
-  }
-}
-
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 // D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
@@ -1364,43 +1152,18 @@ b2_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params
 constexpr int kHaloB = 6;                       // B ring depth of the halo kernel
 constexpr size_t kHaloMaxSmem = 227 * 1024;
 
-// Window geometry of the halo kernels for padded width wp: TMA boxes of at
-// most 256 rows, each a multiple of 8 rows; 0 boxes when the window and a ring
-// of `b_ring_bytes` do not fit in shared memory.
+// Window geometry of the halo kernel for padded width wp: TMA boxes of at most
+// 256 rows, each a multiple of 8 rows; 0 boxes when the window and a ring of
+// `b_ring_bytes` do not fit in shared memory.  (Single-CTA versions of the
+// kernel, with a 6-deep and with a 10-24-deep B ring, were measured 3-8 %
+// slower than the per-tap loads on 64- and 128-channel layers: there the MMA
+// issue rate of the narrow tiles binds, not L2.)
 void halo_window(int wp, size_t b_ring_bytes, int& boxes, int& box_rows) {
   const int need = 128 + 2 * wp + 2;
   boxes = (need + 255) / 256;
   box_rows = ((need + boxes - 1) / boxes + 7) / 8 * 8;
   const size_t smem = 2 * size_t(boxes) * box_rows * 128 + b_ring_bytes + 1024 + 512;
   if (smem > kHaloMaxSmem) boxes = 0;
-}
-
-// Single-CTA halo launch: the B ring as deep as the window leaves room for
-// (at least 8 taps; 0 returned in `ring` when that does not fit).
-template <int BN>
-int halo_ring_for(int win_bytes) {
-  const size_t room = kHaloMaxSmem - 2 * size_t(win_bytes) - 1024 - 640;
-  const int ring = int(std::min<size_t>(kMaxRing, room / (size_t(BN) * BK * 2)));
-  return ring >= 8 ? ring : 0;
-}
-
-template <int BN>
-b2_status launch_halo(const CUtensorMap& twin, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
-  auto kern = igemm_halo_kernel<BN>;
-  const size_t smem = 2 * size_t(p.win_boxes) * p.win_box_rows * 128 + size_t(p.ring) * BN * BK * 2 + 1024 + 640;
-  int dev = 0;
-  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  static bool configured[64] = {};
-  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
-  if (!configured[dev]) {  // once, at the largest size accepted
-    B2_TRY(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kHaloMaxSmem)),
-                      "cudaFuncSetAttribute(smem, halo)"));
-    configured[dev] = true;
-  }
-  const int tiles = p.tiles_m * p.tiles_n;
-  if (tiles <= 0) return B2_OK;
-  kern<<<std::min(tiles, sm_count(dev)), kThreads, smem, st>>>(twin, tb, p);
-  return check_cuda(cudaGetLastError(), "igemm halo launch");
 }
 
 b2_status launch_pair_halo(const CUtensorMap& twin, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
@@ -1427,15 +1190,6 @@ bool halo_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("B2_CONV_HALO");
     return !e || e[0] != '0';
-  }();
-  return on;
-}
-
-// The deep-ring halo kernel for 64 / 128-wide tiles when B2_CONV_HALO_NARROW=1.
-bool halo_narrow_enabled() {
-  static const bool on = [] {
-    const char* e = std::getenv("B2_CONV_HALO_NARROW");
-    return e && e[0] == '1' && halo_enabled();
   }();
   return on;
 }
@@ -1523,24 +1277,6 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
       return launch_pair_halo(twin, tb, pp, st);
     }
     return launch_pair<kConv>(ta, tb, pp, pp.tiles_m * pp.tiles_n, st);
-  }
-  if (!wide && halo_narrow_enabled()) {  // 64 / 128-wide tiles: the deep-ring halo kernel when it fits
-    int boxes = 0, box_rows = 0;
-    halo_window(W + 2, 0, boxes, box_rows);
-    const int win_bytes = boxes * box_rows * 128;
-    const int ring = boxes > 0 ? (narrow ? halo_ring_for<64>(win_bytes) : halo_ring_for<128>(win_bytes)) : 0;
-    if (ring > 0) {
-      CUtensorMap twin;
-      const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
-      const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
-      const uint32_t box[3] = {64, uint32_t(box_rows), 1};
-      B2_TRY(encode_tmap(&twin, rows, 3, dims, strides, box, true));
-      Params ph = p;
-      ph.win_boxes = boxes;
-      ph.win_box_rows = box_rows;
-      ph.ring = ring;
-      return narrow ? launch_halo<64>(twin, tb, ph, st) : launch_halo<128>(twin, tb, ph, st);
-    }
   }
   if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
   if (narrow) return launch<64, kStages64, kConv, false, false>(ta, tb, p, tiles, st);
