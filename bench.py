@@ -447,6 +447,128 @@ def make_style_generator():
     return nn.Sequential(*layers)
 
 
+class _ConvNormAct(torch.nn.Module):
+    """[nearest 2x upsample ->] 3x3 conv (no bias) -> BatchNorm2d -> LeakyReLU(0.2)."""
+
+    def __init__(self, ci, co, stride=1, upsample=False):
+        super().__init__()
+        import torch.nn as nn
+        self.upsample = upsample
+        self.conv = nn.Conv2d(ci, co, 3, stride=stride, padding=1, bias=False)
+        self.norm = nn.BatchNorm2d(co)
+        self.act = nn.LeakyReLU(0.2)
+
+    def forward(self, x):
+        if self.upsample:
+            x = torch.nn.functional.interpolate(x, scale_factor=2, mode="nearest")
+        return self.act(self.norm(self.conv(x)))
+
+
+class _LeakyRes(torch.nn.Module):
+    """LeakyReLU(BN(conv(ConvNormAct(x))) + x), 3x3 convs without bias."""
+
+    def __init__(self, c):
+        super().__init__()
+        import torch.nn as nn
+        self.first = _ConvNormAct(c, c)
+        self.conv = nn.Conv2d(c, c, 3, padding=1, bias=False)
+        self.norm = nn.BatchNorm2d(c)
+        self.act = nn.LeakyReLU(0.2)
+
+    def forward(self, x):
+        return self.act(self.norm(self.conv(self.first(x))) + x)
+
+
+class RefStyleNet(torch.nn.Module):
+    """The reference's own benchmark generator (`benchmarks/style_net.py:64-88`,
+    the network its perceptual-loss region was written for), built from that
+    description: encoder 3->64 (stride 1), ->128 and ->128 (stride 2) of
+    conv-BN-LeakyReLU(0.2); 5 residual blocks at 128 channels; two decoder
+    stages (nearest 2x upsample + conv-BN-LeakyReLU) fed with the encoder's
+    skip maps concatenated on the channel axis; a conv-BN-LeakyReLU over
+    [decoder, first encoder map, input] (195 -> 64 channels) and a 1x1 conv
+    with bias to 3 channels."""
+
+    def __init__(self, cin=3, cout=3, blocks=5):
+        super().__init__()
+        import torch.nn as nn
+        self.enc0 = _ConvNormAct(cin, 64)
+        self.enc1 = _ConvNormAct(64, 128, stride=2)
+        self.enc2 = _ConvNormAct(128, 128, stride=2)
+        self.blocks = nn.ModuleList(_LeakyRes(128) for _ in range(blocks))
+        self.dec2 = _ConvNormAct(256, 128, upsample=True)
+        self.dec1 = _ConvNormAct(256, 128, upsample=True)
+        self.head = _ConvNormAct(128 + 64 + cin, 64)
+        self.out = nn.Conv2d(64, cout, 1)
+
+    def forward(self, x):
+        e0 = self.enc0(x)
+        e1 = self.enc1(e0)
+        e2 = self.enc2(e1)
+        r = e2.clone()
+        for b in self.blocks:
+            r = b(r)
+        y = self.dec2(torch.cat([r, e2], dim=1))
+        y = self.dec1(torch.cat([y, e1], dim=1))
+        return self.out(self.head(torch.cat([y, e0, x], dim=1)))
+
+    def norm_act_pairs(self):
+        """(BatchNorm2d, LeakyReLU) pairs with nothing between them, for
+        `regions.fuse_norm_activation` (the residual tail has an add between)."""
+        return [(m.norm, m.act) for m in self.modules() if isinstance(m, _ConvNormAct)]
+
+
+class _ImageNetNorm(torch.nn.Module):
+    """(x - mean) / std per RGB channel, the constants cast to x's dtype."""
+
+    def __init__(self):
+        super().__init__()
+        self.mean = torch.tensor([0.485, 0.456, 0.406]).view(1, 3, 1, 1)
+        self.std = torch.tensor([0.229, 0.224, 0.225]).view(1, 3, 1, 1)
+
+    def forward(self, x):
+        return (x - self.mean.to(x.device, x.dtype)) / self.std.to(x.device, x.dtype)
+
+
+class RefStyleLoss(torch.nn.Module):
+    """The reference benchmark's loss (`benchmarks/style_net.py:90-144`), from
+    its description: l_perceptual * mean((f(x) - f(t))**2) over the
+    concatenated flattened outputs of frozen random-init VGG19 features 0, 3
+    and 5 of the ImageNet-normalised images (target side without autograd),
+    plus l_l1 * L1(x, t).  The module layout is the one
+    `regions.fuse_perceptual_loss` matches."""
+
+    def __init__(self, l_l1=4.0, l_perceptual=6.0, taps=(0, 3, 5)):
+        super().__init__()
+        from torchvision.models import vgg19
+        self.perceptual_vgg = torch.nn.Module()
+        self.perceptual_vgg.model = vgg19(weights=None).eval()
+        self.perceptual_vgg.feature_layers = tuple(taps)
+        self.perceptual_vgg.use_norm = True
+        self.perceptual_vgg.norm = _ImageNetNorm()
+        for q in self.perceptual_vgg.parameters():
+            q.requires_grad_(False)
+        self.l_l1, self.l_perceptual = l_l1, l_perceptual
+
+    def features(self, x):
+        net, maps = self.perceptual_vgg, []
+        y = net.norm(x)
+        for i in range(max(net.feature_layers) + 1):
+            y = net.model.features[i](y)
+            if i in net.feature_layers:
+                maps.append(y.clone().view(y.shape[0], -1))
+        return torch.cat(maps, dim=1)
+
+    def compute_perceptual_loss(self, x, t):
+        fx = self.features(x)
+        with torch.no_grad():
+            ft = self.features(t)
+        return ((fx - ft) ** 2).mean()
+
+    def forward(self, x, t):
+        return self.l_perceptual * self.compute_perceptual_loss(x, t) + self.l_l1 * torch.nn.functional.l1_loss(x, t)
+
+
 
 
 class StyleLoss(torch.nn.Module):
@@ -525,15 +647,17 @@ def run_workload(args):
             return None
         return _timed(make_step(), steps, warmup, cpu)
 
-    def graphed(make_step, key, scale):
+    def graphed(make_step, key, scale, read_loss=False):
         """The same step captured once into a CUDA graph (xdna_train.graphs)
-        and replayed: the step's kernels without the host's per-op dispatch."""
+        and replayed: the step's kernels without the host's per-op dispatch
+        (``read_loss``: every replay also reads the loss on the host)."""
         if world != 1:
             return
         from xdna_train import graphs
         try:
             replay = graphs.make_graphed_step(make_step(), warmup=max(3, args.warmup))
-            out[key] = round(scale / _timed(replay, args.steps, 2, sync), 2)
+            fn = (lambda: replay().item()) if read_loss else replay
+            out[key] = round(scale / _timed(fn, args.steps, 2, sync), 2)
         except Exception as e:  # reported, not hidden: the eager figure stands
             out[key + "_error"] = f"{type(e).__name__}: {e}"[:300]
 
@@ -620,6 +744,44 @@ def run_workload(args):
             out.update(fused_perceptual_loss_it_s=round(1 / dtf, 2), fused_perceptual_and_norm_act_it_s=round(1 / dtn, 2))
             graphed(lambda: make(X, False, capturable=True), "graphed_it_s", 1.0)
             graphed(lambda: make(X, True, True, capturable=True), "graphed_fused_perceptual_and_norm_act_it_s", 1.0)
+
+            # The reference's own benchmark network and loss (benchmarks/end_to_end_speed.py: BF16, B40 36x36,
+            # Adam lr 1e-4 wd 1e-5, the loss read on the host every step), eager plain / with the perceptual
+            # region / with the region and the BatchNorm+LeakyReLU pairs fused, and replayed as a CUDA graph.
+            def make_ref(dev, fused, fuse_norm=False, capturable=False):
+                torch.manual_seed(0)
+                net = RefStyleNet().bfloat16().to(dev)
+                crit = RefStyleLoss().bfloat16().to(dev)
+                if fused:
+                    assert regions.fuse_perceptual_loss(crit)
+                if fuse_norm:
+                    for bn, act in net.norm_act_pairs():
+                        assert regions.fuse_norm_activation(bn, act)
+                opt = torch.optim.Adam(net.parameters(), lr=1e-4, weight_decay=1e-5, fused=True,
+                                       capturable=capturable)
+                g = torch.Generator().manual_seed(1)
+                x = (torch.rand(40, 3, 36, 36, generator=g) * 2 - 1).bfloat16().to(dev)
+                tgt = torch.rand(40, 3, 36, 36, generator=g).bfloat16().to(dev)
+
+                def step():
+                    loss = crit(net(x), tgt)
+                    opt.zero_grad(set_to_none=True)
+                    loss.backward()
+                    opt.step()
+                    return loss
+                return step
+
+            def read(step):
+                return lambda: step().item()
+            rn = {}
+            for key, fl in (("eager_it_s", (False,)), ("fused_perceptual_loss_it_s", (True,)),
+                            ("fused_perceptual_and_norm_act_it_s", (True, True))):
+                rn[key] = round(1 / _timed(read(make_ref(X, *fl)), args.steps, args.warmup, sync), 2)
+            out["reference_stylenet"] = rn
+            graphed(lambda: make_ref(X, True, True, capturable=True), "reference_stylenet_graphed_it_s", 1.0,
+                    read_loss=True)
+            if rank == 0 and world == 1 and not args.no_cpu_baseline:
+                rn["cpu_it_s"] = round(1 / _timed(read(make_ref("cpu", False)), 2, 1, cpu), 3)
         c = cpu_rate(lambda: make("cpu", False))
     elif w == "resnet50":
         # config 5: ResNet-50 224x224, per-GPU batch 128, SGD momentum 0.9, DP over NCCL

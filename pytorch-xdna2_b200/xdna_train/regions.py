@@ -302,11 +302,37 @@ def _fused_compute_perceptual_loss(self, input, target):
         mean, std = getattr(norm, "mean", None), getattr(norm, "std", None)
         if mean is None or std is None:
             return type(self).compute_perceptual_loss(self, input, target)
-        m = torch.as_tensor(mean, dtype=x.dtype, device=x.device).view(1, -1, 1, 1)
-        s = torch.as_tensor(std, dtype=x.dtype, device=x.device).view(1, -1, 1, 1)
+        m, s = _norm_constants(self, mean, std, x)
         x = (x - m) / s
         t = (t - m) / s
     return frozen_feature_mse(chain, x, t)
+
+
+def _norm_constants(loss_module, mean, std, x):
+    """mean / std as [1, C, 1, 1] tensors of x's dtype on x's device.  The
+    reference's normalisation keeps them as CPU tensors and copies them on
+    every call; the copies are cached here per device, dtype and tensor
+    version, so that after the first call no host-to-device copy is issued
+    (a captured CUDA graph may contain none from pageable memory).  Constants
+    that are not tensors (lists, tuples) are converted on every call."""
+    m = torch.as_tensor(mean, dtype=x.dtype, device=x.device).view(1, -1, 1, 1) \
+        if not isinstance(mean, torch.Tensor) else None
+    s = torch.as_tensor(std, dtype=x.dtype, device=x.device).view(1, -1, 1, 1) \
+        if not isinstance(std, torch.Tensor) else None
+    if m is not None or s is not None:
+        if m is None:
+            m = mean.to(device=x.device, dtype=x.dtype).view(1, -1, 1, 1)
+        if s is None:
+            s = std.to(device=x.device, dtype=x.dtype).view(1, -1, 1, 1)
+        return m, s
+    key = (mean._version, std._version, x.device, x.dtype)
+    hit = loss_module.__dict__.get("_xdna_norm_consts")
+    if hit is not None and hit[0] is mean and hit[1] is std and hit[2] == key:
+        return hit[3], hit[4]
+    m = mean.to(device=x.device, dtype=x.dtype).view(1, -1, 1, 1)
+    s = std.to(device=x.device, dtype=x.dtype).view(1, -1, 1, 1)
+    loss_module.__dict__["_xdna_norm_consts"] = (mean, std, key, m, s)
+    return m, s
 
 
 def fuse_perceptual_loss(loss_module, features_attr: str = "perceptual_vgg") -> bool:

@@ -119,3 +119,33 @@ def test_graph_pool_is_released(fresh):
     gc.collect()
     torch.xdna.synchronize()
     assert xdna_train.allocator_stats()["graph_pools"] == before
+
+
+def test_fused_perceptual_loss_with_host_norm_constants_is_capturable(fresh):
+    """A loss whose normalisation keeps mean / std as CPU tensors (the
+    reference's benchmark loss) copies them to the device on every eager call;
+    the fused perceptual loss caches those copies, so a step through it can be
+    captured, and a replay gives the eager loss and input gradient."""
+    import bench
+    from xdna_train import regions
+    torch.manual_seed(0)
+    crit = bench.RefStyleLoss().bfloat16().to(X)
+    assert regions.fuse_perceptual_loss(crit)
+    g = torch.Generator().manual_seed(2)
+    x = (torch.rand(2, 3, 16, 16, generator=g) * 2 - 1).bfloat16().to(X).requires_grad_()
+    t = torch.rand(2, 3, 16, 16, generator=g).bfloat16().to(X)
+
+    def step():
+        x.grad = None
+        loss = crit(x, t)
+        loss.backward()
+        return loss
+
+    le = step().detach().float().cpu()
+    ge = x.grad.detach().float().cpu()
+    replay = graphs.make_graphed_step(step, warmup=2)
+    lr = replay()
+    torch.xdna.synchronize()
+    assert torch.allclose(lr.detach().float().cpu(), le, rtol=1e-2, atol=0)
+    assert torch.allclose(x.grad.detach().float().cpu(), ge, rtol=2e-2, atol=1e-4)
+    assert xdna_train.kernel_stats().get("region.sqdiff_sum", 0) > 0

@@ -110,6 +110,48 @@ def test_config4_style_transfer_steps(fused):
         assert ks.get("region.relu_maxpool2", 0) > 0 and ks.get("region.sqdiff_sum", 0) > 0
 
 
+@pytest.mark.parametrize("fused", [False, True])
+def test_config4_reference_stylenet_steps(fused, monkeypatch):
+    """The reference's own benchmark network and loss (LeakyReLU(0.2), skip
+    concatenations, a 195-channel 3x3 conv, a 1x1 output conv; perceptual taps
+    0, 3, 5 of ImageNet-normalised images plus L1; Adam lr 1e-4 wd 1e-5), with
+    the perceptual region and every BatchNorm+LeakyReLU pair fused or not,
+    against the same seeded steps on the CPU BF16 path."""
+    from xdna_train import regions
+    monkeypatch.setattr(regions, "_NORM_ACT_MIN_BYTES", 0)
+
+    def run(dev, fuse):
+        torch.manual_seed(0)
+        net = bench.RefStyleNet().bfloat16().to(dev)
+        crit = bench.RefStyleLoss().bfloat16().to(dev)
+        if fuse:
+            assert regions.fuse_perceptual_loss(crit)
+            for bn, act in net.norm_act_pairs():
+                assert regions.fuse_norm_activation(bn, act)
+        opt = torch.optim.Adam(net.parameters(), lr=1e-4, weight_decay=1e-5, fused=True)
+        g = torch.Generator().manual_seed(1)
+        x = (torch.rand(4, 3, 36, 36, generator=g) * 2 - 1).bfloat16().to(dev)
+        tgt = torch.rand(4, 3, 36, 36, generator=g).bfloat16().to(dev)
+        out = []
+        for _ in range(3):
+            loss = crit(net(x), tgt)
+            opt.zero_grad(set_to_none=True)
+            loss.backward()
+            opt.step()
+            out.append(loss.item())
+        return out
+    lc = run("cpu", False)
+    k0 = dict(xdna_train.kernel_stats())
+    lx = run(X, fused)
+    for a, b in zip(lx, lc):
+        assert _rel(a, b) <= 0.03, (lx, lc)
+    ks = xdna_train.kernel_stats()
+    ran = lambda k: ks.get(k, 0) - k0.get(k, 0)  # noqa: E731
+    assert ran("conv3x3.fwd") > 0 and ran("conv3x3.dgrad") > 0 and ran("fused_adam") > 0
+    if fused:
+        assert ran("region.sqdiff_sum") > 0 and ran("region.bn_fwd") > 0 and ran("region.bn_bwd") > 0
+
+
 def test_config5_resnet50_steps():
     """ResNet-50 (BASELINE config 5 at batch 4) against an fp32 CPU reference,
     with the reference's own kind of gate (the fused path's error no larger
