@@ -863,6 +863,87 @@ def kernel_probe(args):
     print(json.dumps({"probe": f"B{b} C{c} HW{hw}", **out}), flush=True)
 
 
+SWEEP_C = (32, 64, 128, 256, 512)
+SWEEP_HW = (18, 36, 72, 144)
+SWEEP_B = (8, 40, 128)
+
+
+def conv_sweep(args):
+    """BASELINE configs[1], the whole 3x3 conv sweep (``--conv-sweep``): for
+    every C_in = C_out, H = W and batch of the config, the fwd / dgrad / wgrad
+    kernels and the NCHW row packer timed separately on the device (CUDA
+    events around back-to-back launches after two warm-up calls, as many as
+    make ~30 ms per direction, 3 to 50), with TFLOP/s and the fraction of the
+    measured dense-BF16 peak (padding to 64-channel chunks not counted as
+    work).  The reference's CPU path (stock PyTorch CPU conv /
+    convolution_backward) is timed beside it on a one-image sample per
+    (C, H), for shapes up to ~1.5 GFLOP per image and direction.  One JSON
+    line per shape, then a summary line."""
+    import torch.nn as nn
+
+    import xdna_train
+    xdna_train.register_xdna_device()
+    torch.cuda.set_device(0)
+    X = torch.device("xdna", 0)
+    peak, _, kind = peaks()
+    cs = [args.channels] if args.sweep_one else SWEEP_C
+    hws = [args.hw] if args.sweep_one else SWEEP_HW
+    bs = [args.batch] if args.sweep_one else SWEEP_B
+    cpu_tf = {}
+    if not args.no_cpu_baseline:
+        from oracle import cpu_path
+        for c in cs:
+            for hw in hws:
+                if hw * hw * c * c > 1.1e8:
+                    continue
+                g = torch.Generator().manual_seed(c + hw)
+                x = torch.randn(1, c, hw, hw, generator=g).bfloat16()
+                dy = torch.randn(1, c, hw, hw, generator=g).bfloat16()
+                w = (torch.randn(c, c, 3, 3, generator=g) * 0.05).bfloat16()
+                fl = 2.0 * hw * hw * c * c * 9
+                row = {}
+                for k, fn in (("fwd", lambda: cpu_path.conv3x3_fwd(x, w)),
+                              ("dgrad", lambda: cpu_path.conv3x3_bwd(dy, x, w, (True, False, False))),
+                              ("wgrad", lambda: cpu_path.conv3x3_bwd(dy, x, w, (False, True, False)))):
+                    fn()
+                    t0 = time.perf_counter()
+                    fn()
+                    row[k] = round(fl / (time.perf_counter() - t0) / 1e12, 3)
+                cpu_tf[(c, hw)] = row
+    rows = []
+    for c in cs:
+        torch.manual_seed(c)
+        conv = nn.Conv2d(c, c, 3, padding=1).bfloat16().to(X)
+        for hw in hws:
+            for b in bs:
+                x = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
+                dy = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
+                fl = 2.0 * b * hw * hw * c * c * 9
+                iters = max(3, min(50, int(0.03 / (fl / 1.2e15))))
+                kt = kernel_times(x, dy, conv, 0, iters=iters)
+                row = {"shape": f"B{b} C{c} HW{hw}", "gflop_per_direction": round(fl / 1e9, 3), "iters": iters}
+                for k in ("fwd", "dgrad", "wgrad"):
+                    tf = fl / (kt[k] * 1e-3) / 1e12
+                    row[k] = {"us": round(kt[k] * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / peak, 4)}
+                row["pack_rows_us"] = round(kt["pack_rows"] * 1e3, 2)
+                if (c, hw) in cpu_tf:
+                    row["cpu_tflops_1img"] = cpu_tf[(c, hw)]
+                rows.append(row)
+                print(json.dumps(row), flush=True)
+                del x, dy
+            torch.xdna.empty_cache()
+    tot_fl = sum(r["gflop_per_direction"] for r in rows) * 3
+    tot_us = sum(r[k]["us"] for r in rows for k in ("fwd", "dgrad", "wgrad"))
+    big = [r[k]["frac"] for r in rows for k in ("fwd", "dgrad", "wgrad")
+           if int(r["shape"].split()[1][1:]) >= 256 and int(r["shape"].split()[2][2:]) >= 36]
+    print(json.dumps({"probe": "conv3x3 sweep (BASELINE configs[1])", "shapes": len(rows), "peak_tflops": peak,
+                      "peak_kind": kind, "sum_gflop": round(tot_fl, 1), "sum_us": round(tot_us, 1),
+                      "aggregate_tflops": round(tot_fl * 1e9 / (tot_us * 1e-6) / 1e12, 1),
+                      "large_channel_min_frac": min(big) if big else None,
+                      "large_channel_median_frac": statistics.median(big) if big else None,
+                      "cpu_threads": torch.get_num_threads() if cpu_tf else None}), flush=True)
+
+
 def bn_probe(args):
     """Device time of training-mode BatchNorm2d forward + backward on one
     channels-last shape (``--bn-probe --batch B --channels C --hw H``), with the
@@ -1045,6 +1126,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
     ap.add_argument("--conv1x1-probe", action="store_true")
+    ap.add_argument("--conv-sweep", action="store_true", help="BASELINE configs[1]: every shape of the 3x3 sweep")
+    ap.add_argument("--sweep-one", action="store_true", help="--conv-sweep: only --batch/--channels/--hw")
     ap.add_argument("--shape-index", type=int, default=-1, help="--conv1x1-probe: one shape of the list")
     ap.add_argument("--style-plain-only", action="store_true",
                     help="--workload style: the eager plain-loss variant only (launch-list captures)")
@@ -1067,6 +1150,9 @@ def main():
     args = ap.parse_args()
     if args.kernel_probe:
         kernel_probe(args)
+        return
+    if args.conv_sweep:
+        conv_sweep(args)
         return
     if args.bn_probe:
         bn_probe(args)
