@@ -63,6 +63,7 @@ struct Params {
   int gemm_split;    // 1: tile-space slices are split-K ranges writing fp32 partials
   int tma_store;     // GEMM: bf16 D written by TMA stores of shared-memory staged boxes
   int win_boxes, win_box_rows;  // conv halo kernel: the A window is win_boxes TMA boxes of win_box_rows rows
+  int win_bufs;                 // resident-weight halo kernel: window buffers in flight (<= kMaxWinBufs)
 };
 
 template <int BN>
@@ -1053,6 +1054,184 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 
+
+// Narrow convolutions (Cin <= 64, Cout <= 64) with the weights resident: a
+// 64-wide output tile needs 9 taps x 64 x 64 weights (72 KB), the same for
+// every tile, and a 128-row tile of one 64-channel chunk does only 1152
+// cycles of MMA work.  Streaming A per tap and B per tile moved 216 KB per
+// tile through L2, more than the TMA pipeline's bytes in flight can cover at
+// that MMA rate.  Here each persistent CTA loads the whole weight slice once,
+// then streams only the padded input window of each tile (128 + 2(W+2) + 2
+// rows, loaded once and read by all nine taps as row-shifted descriptors,
+// as in the SM-pair halo kernel), with as many windows in flight as shared
+// memory holds.
+constexpr int kMaxWinBufs = 6;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    igemm_halo_bres_kernel(const __grid_constant__ CUtensorMap tma_win, const __grid_constant__ CUtensorMap tma_b,
+                           const Params p) {
+  constexpr int BN = 64;
+  constexpr uint32_t kTapBytes = BN * BK * 2;  // 8 KB
+  constexpr uint32_t kWBytes = 9 * kTapBytes;  // 72 KB
+  constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, false, false);
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int NW = p.win_bufs;
+  const uint32_t box_bytes = uint32_t(p.win_box_rows) * 128u;
+  const uint32_t a_bytes = uint32_t(p.win_boxes) * box_bytes;
+  uint8_t* w_base = smem;
+  uint8_t* a_base = smem + kWBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(a_base + NW * a_bytes);
+  uint64_t* w_full = bars;
+  uint64_t* a_full = bars + 1;
+  uint64_t* a_empty = a_full + kMaxWinBufs;
+  uint64_t* tfull = a_empty + kMaxWinBufs;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(w_full), 1);
+    for (int s = 0; s < NW; ++s) {
+      mbar_init(smem_u32(&a_full[s]), 1);
+      mbar_init(smem_u32(&a_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&tfull[s]), 1);
+      mbar_init(smem_u32(&tempty[s]), kEpiWarps);
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int ntiles = p.tiles_m;  // one 64-wide column tile
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ producer ------------------------------
+      tma_prefetch_desc(&tma_win);
+      tma_prefetch_desc(&tma_b);
+      const uint32_t fw = smem_u32(w_full);
+      mbar_arrive_expect_tx(fw, kWBytes);
+      for (int tap = 0; tap < 9; ++tap) tma_load_3d(smem_u32(w_base + tap * kTapBytes), &tma_b, fw, tap * BK, 0, 0);
+      int as = 0;
+      uint32_t aph = 0;
+      int a_last[kMaxWinBufs];
+      for (int s = 0; s < kMaxWinBufs; ++s) a_last[s] = -1;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(&a_empty[as]), aph ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fa = smem_u32(&a_full[as]);
+        mbar_arrive_expect_tx(fa, a_bytes);
+        a_last[as] = int(aph);
+        const uint32_t sa = smem_u32(a_base + as * a_bytes);
+        for (int i = 0; i < p.win_boxes; ++i)
+          tma_load_3d(sa + i * box_bytes, &tma_win, fa, 0, t * BM + i * p.win_box_rows, 0);
+        if (++as == NW) {
+          as = 0;
+          aph ^= 1;
+        }
+      }
+      // the weights and every issued window land before the CTA may exit
+      mbar_wait(fw, 0, p.status, nullptr);
+      if (!ok)
+        for (int s = 0; s < NW; ++s)
+          if (a_last[s] >= 0) mbar_wait(smem_u32(&a_full[s]), uint32_t(a_last[s]), p.status, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer ----------------------------
+      int as = 0, acc = 0;
+      uint32_t aph = 0, acc_phase = 0;
+      bool ok = mbar_wait(smem_u32(w_full), 0, p.status, abort_flag);
+      tc_fence_after();
+      const uint32_t sw = smem_u32(w_base);
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(smem_u32(&a_full[as]), aph, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        const uint32_t sa = smem_u32(a_base + as * a_bytes);
+#pragma unroll 1
+        for (int tap = 0; tap < 9; ++tap) {
+          const int dy = tap / 3, dx = tap - dy * 3;
+          const int shift = dy * p.wp + dx;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_f16(d_tmem, smem_desc_sw128_row(sa, shift, uint32_t(k * 32)),
+                       smem_desc_sw128(sw + tap * kTapBytes + k * 32, 16, 1024), kIdesc, (tap > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&a_empty[as]));
+        if (++as == NW) {
+          as = 0;
+          aph ^= 1;
+        }
+        tc_commit(smem_u32(&tfull[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      tc_commit(smem_u32(mma_done));
+      mbar_wait(smem_u32(mma_done), 0, p.status, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------- epilogue ------------------------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      uint16_t* obase = conv_row_base(p, t, row);
+      bool ok = mbar_wait(smem_u32(&tfull[acc]), acc_phase, p.status, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
+      uint32_t r[32];
+      tmem_ld32(taddr, r);
+      tc_wait_ld();
+      epi_conv(p, obase, half * (BN / 2), lane, r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 // D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
@@ -1166,6 +1345,34 @@ void halo_window(int wp, size_t b_ring_bytes, int& boxes, int& box_rows) {
   if (smem > kHaloMaxSmem) boxes = 0;
 }
 
+// Resident-weight halo launch (Cin <= 64, Cout <= 64): the 72 KB weight
+// slice plus p.win_bufs windows of the geometry halo_window gave.
+constexpr size_t kBresWeightBytes = 9 * 64 * BK * 2;
+
+int bres_window_buffers(int win_bytes) {
+  if (win_bytes <= 0) return 0;
+  const size_t room = kHaloMaxSmem - kBresWeightBytes - 1024 - 256;
+  const int n = int(std::min<size_t>(kMaxWinBufs, room / size_t(win_bytes)));
+  return n >= 2 ? n : 0;
+}
+
+b2_status launch_halo_bres(const CUtensorMap& twin, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
+  const size_t smem = kBresWeightBytes + size_t(p.win_bufs) * p.win_boxes * p.win_box_rows * 128 + 1024 + 256;
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[dev]) {  // once, at the largest size accepted
+    B2_TRY(check_cuda(cudaFuncSetAttribute(igemm_halo_bres_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(kHaloMaxSmem)),
+                      "cudaFuncSetAttribute(smem, halo bres)"));
+    configured[dev] = true;
+  }
+  if (p.tiles_m <= 0) return B2_OK;
+  igemm_halo_bres_kernel<<<std::min(p.tiles_m, sm_count(dev)), kThreads, smem, st>>>(twin, tb, p);
+  return check_cuda(cudaGetLastError(), "igemm halo bres launch");
+}
+
 b2_status launch_pair_halo(const CUtensorMap& twin, const CUtensorMap& tb, const Params& p, cudaStream_t st) {
   auto kern = igemm_pair_halo_kernel<kHaloB>;
   const size_t smem = 2 * size_t(p.win_boxes) * p.win_box_rows * 128 + size_t(kHaloB) * 128 * BK * 2 + 1024 + 512;
@@ -1190,6 +1397,16 @@ bool halo_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("B2_CONV_HALO");
     return !e || e[0] != '0';
+  }();
+  return on;
+}
+
+// Resident-weight halo kernel for Cin <= 64, Cout <= 64 unless B2_CONV_BRES=0
+// (A/B switch; 1.3-1.5x the per-tap kernel on 32- and 64-channel layers).
+bool bres_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_CONV_BRES");
+    return !(e && e[0] == '0') && halo_enabled();
   }();
   return on;
 }
@@ -1277,6 +1494,23 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
       return launch_pair_halo(twin, tb, pp, st);
     }
     return launch_pair<kConv>(ta, tb, pp, pp.tiles_m * pp.tiles_n, st);
+  }
+  if (narrow && chunks == 1 && bres_enabled()) {
+    int boxes = 0, box_rows = 0;
+    halo_window(W + 2, kBresWeightBytes, boxes, box_rows);
+    const int bufs = boxes > 0 ? bres_window_buffers(boxes * box_rows * 128) : 0;
+    if (bufs > 0) {
+      CUtensorMap twin;
+      const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
+      const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
+      const uint32_t box[3] = {64, uint32_t(box_rows), 1};
+      B2_TRY(encode_tmap(&twin, rows, 3, dims, strides, box, true));
+      Params ph = p;
+      ph.win_boxes = boxes;
+      ph.win_box_rows = box_rows;
+      ph.win_bufs = bufs;
+      return launch_halo_bres(twin, tb, ph, st);
+    }
   }
   if (wide) return launch<256, kStages256, kConv, false, false>(ta, tb, p, tiles, st);
   if (narrow) return launch<64, kStages64, kConv, false, false>(ta, tb, p, tiles, st);
