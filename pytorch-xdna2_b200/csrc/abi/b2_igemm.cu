@@ -1232,6 +1232,180 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// Weight gradient of narrow convolutions (Cin <= 64, Cout <= 64).  The tiled
+// wgrad kernel runs one tile per tap, so each 64-pixel k-block reloads dY and
+// X for every tap, and a 64-channel Cout fills only half of its 128-row MMA.
+// Here a persistent CTA owns a range of 128-pixel k-blocks (split-K) and all
+// nine taps: per k-block it loads the dY block once (128 pixels x 64 output
+// channels) and the input window once (128 + 2(W+2) + 2 padded rows x 64
+// input channels).  The MMA's M rows are two taps' input channels: rows 0-63
+// read the window `s1` rows in, rows 64-127 `s2` rows in (the two 64-element
+// halves of an M-major operand sit the descriptor's leading byte offset
+// apart, here (s2 - s1) rows).  Taps pair as (0,1) (2,3) (4,5) (6,7) (7,8);
+// the last accumulator keeps only its tap-8 half.  Five 128 x 64 fp32
+// accumulators (320 TMEM columns) hold the CTA's sums until its last k-block;
+// the epilogue writes them as this split's partials [split][tap][co][ci],
+// which wgrad_reduce_kernel adds in split order.
+constexpr int kNarrowWgradPix = 128;  // pixels (padded rows) per k-block
+
+__device__ __forceinline__ int tap_shift(int tap, int wp) {
+  const int dy = tap / 3;
+  return dy * wp + (tap - dy * 3);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    igemm_wgrad_narrow_kernel(const __grid_constant__ CUtensorMap tma_dy, const __grid_constant__ CUtensorMap tma_x,
+                              const Params p) {
+  constexpr int BN = 64;
+  constexpr uint32_t kDyBytes = kNarrowWgradPix * 128;  // 16 KB
+  constexpr uint32_t kIdesc = idesc_bf16_f32(BM, BN, true, true);
+  constexpr uint32_t kTmemCols = 512;  // 5 x 64 used
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int NS = p.win_bufs;
+  const uint32_t box_bytes = uint32_t(p.win_box_rows) * 128u;
+  const uint32_t stage_bytes = kDyBytes + uint32_t(p.win_boxes) * box_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NS * stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = full + kMaxWinBufs;
+  uint64_t* tfull = empty + kMaxWinBufs;
+  uint64_t* mma_done = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int split = blockIdx.x;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    mbar_init(smem_u32(tfull), 1);
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------ producer ------------------------------
+      tma_prefetch_desc(&tma_dy);
+      tma_prefetch_desc(&tma_x);
+      int st = 0;
+      uint32_t ph = 0;
+      int last[kMaxWinBufs];
+      for (int s = 0; s < kMaxWinBufs; ++s) last[s] = -1;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&empty[st]), ph ^ 1, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t f = smem_u32(&full[st]);
+        mbar_arrive_expect_tx(f, stage_bytes);
+        last[st] = int(ph);
+        const uint32_t sd = smem_u32(smem + st * stage_bytes);
+        const int row0 = kb * kNarrowWgradPix;
+        tma_load_3d(sd, &tma_dy, f, 0, row0 + p.a_row_shift, 0);
+        for (int i = 0; i < p.win_boxes; ++i)
+          tma_load_3d(sd + kDyBytes + i * box_bytes, &tma_x, f, 0, row0 + i * p.win_box_rows, 0);
+        if (++st == NS) {
+          st = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok)
+        for (int s = 0; s < NS; ++s)
+          if (last[s] >= 0) mbar_wait(smem_u32(&full[s]), uint32_t(last[s]), p.status, nullptr);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------ MMA issuer ----------------------------
+      int st = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&full[st]), ph, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sd = smem_u32(smem + st * stage_bytes);
+        const uint32_t sw = sd + kDyBytes;
+#pragma unroll 1
+        for (int a = 0; a < 5; ++a) {
+          const int s1 = tap_shift(a < 4 ? 2 * a : 7, p.wp);
+          const int s2 = tap_shift(a < 4 ? 2 * a + 1 : 8, p.wp);
+          const uint32_t lbo = uint32_t(s2 - s1) * 128u;
+#pragma unroll
+          for (int k = 0; k < kNarrowWgradPix / 16; ++k)
+            tc_mma_f16(tmem_base + uint32_t(a * BN), smem_desc_sw128(sw + uint32_t(s1 + 16 * k) * 128u, lbo, 1024),
+                       smem_desc_sw128(sd + k * 2048, 8192, 1024), kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&empty[st]));
+        if (++st == NS) {
+          st = 0;
+          ph ^= 1;
+        }
+      }
+      if (ok) tc_commit(smem_u32(tfull));
+      tc_commit(smem_u32(mma_done));
+      mbar_wait(smem_u32(mma_done), 0, p.status, nullptr);
+      if (!ok) *abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    // -------------------------------- epilogue ------------------------------
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int ci = row & 63;
+    bool ok = kb1 > kb0 && mbar_wait(smem_u32(tfull), 0, p.status, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll 1
+      for (int a = 0; a < 5; ++a) {
+        if (a == 4 && row < 64) continue;  // the duplicate tap-7 half (warp-uniform)
+        const int tap = a < 4 ? 2 * a + (row >> 6) : 8;
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(a * BN + half * 32), r);
+        tc_wait_ld();
+        if (ci < p.N) {
+          float* dst = p.partial + ((long long)split * 9 + tap) * p.M * p.N + ci;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int co = half * 32 + c;
+            if (co < p.M) dst[(long long)co * p.N] = __uint_as_float(r[c]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 // D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
@@ -1411,6 +1585,15 @@ bool bres_enabled() {
   return on;
 }
 
+// All-taps weight-gradient kernel for Cin, Cout <= 64 unless B2_WGRAD_NARROW=0.
+bool narrow_wgrad_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_WGRAD_NARROW");
+    return !(e && e[0] == '0') && halo_enabled();
+  }();
+  return on;
+}
+
 // SM-pair MMA for wide convolutions unless B2_PAIR_MMA=0 (A/B switch).
 bool pair_mma_enabled() {
   static const bool on = [] {
@@ -1543,6 +1726,55 @@ WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow
   w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
   w.workspace = size_t(w.splits) * 9 * size_t(Cout) * size_t(Cin) * sizeof(float);
   return w;
+}
+
+// Plan of the narrow wgrad kernel (Cin <= 64, Cout <= 64): 128-pixel
+// k-blocks split over the SMs (at least 2 per CTA), the input window of
+// halo_window's geometry, as many stages (dY block + window) as fit.  ok =
+// false when the shape is not narrow or the window does not fit.
+struct NarrowWgradPlan {
+  bool ok = false;
+  int num_kb = 0, splits = 0, kb_per_split = 0, boxes = 0, box_rows = 0, stages = 0;
+  long long m_total = 0;
+  size_t workspace = 0, smem = 0;
+};
+
+NarrowWgradPlan narrow_wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms) {
+  NarrowWgradPlan w;
+  if (Cin > 64 || Cout > 64 || !narrow_wgrad_enabled()) return w;
+  w.m_total = (long long)B * (H + 2) * (W + 2);
+  const size_t dy_bytes = size_t(kNarrowWgradPix) * 128;
+  halo_window(W + 2, 2 * dy_bytes, w.boxes, w.box_rows);
+  if (w.boxes <= 0) return w;
+  const size_t stage = dy_bytes + size_t(w.boxes) * w.box_rows * 128;
+  w.stages = int(std::min<size_t>(kMaxWinBufs, (kHaloMaxSmem - 1024 - 256) / stage));
+  if (w.stages < 2) return w;
+  w.smem = size_t(w.stages) * stage + 1024 + 256;
+  w.num_kb = int((w.m_total + kNarrowWgradPix - 1) / kNarrowWgradPix);
+  // fewer k-blocks than SMs: the tiled kernel's 9 x tiles parallelism wins
+  if (w.num_kb < sms) return w;
+  int splits = std::max(1, std::min(sms, w.num_kb / 2));
+  w.kb_per_split = (w.num_kb + splits - 1) / splits;
+  w.splits = (w.num_kb + w.kb_per_split - 1) / w.kb_per_split;
+  w.workspace = size_t(w.splits) * 9 * size_t(Cout) * size_t(Cin) * sizeof(float);
+  w.ok = true;
+  return w;
+}
+
+b2_status launch_wgrad_narrow(const CUtensorMap& tdy, const CUtensorMap& tx, const Params& p, size_t smem,
+                              int splits, cudaStream_t st) {
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  if (!configured[dev]) {  // once, at the largest size accepted
+    B2_TRY(check_cuda(cudaFuncSetAttribute(igemm_wgrad_narrow_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(kHaloMaxSmem)),
+                      "cudaFuncSetAttribute(smem, narrow wgrad)"));
+    configured[dev] = true;
+  }
+  igemm_wgrad_narrow_kernel<<<splits, kThreads, smem, st>>>(tdy, tx, p);
+  return check_cuda(cudaGetLastError(), "narrow wgrad launch");
 }
 
 // One GEMM call, D[z] = alpha * op(A[z]) * op(B[z]) + beta * C[z] (bf16 in, fp32
@@ -1712,6 +1944,8 @@ size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout) 
   if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return 16;
   int dev = 0;
   cudaGetDevice(&dev);
+  const NarrowWgradPlan nw = narrow_wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  if (nw.ok) return std::max<size_t>(16, nw.workspace);
   return std::max<size_t>(16, wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled()).workspace);
 }
 
@@ -1727,6 +1961,47 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
     return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: operands must be 16-byte aligned");
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const NarrowWgradPlan nw = narrow_wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
+  if (nw.ok) {
+    if (nw.m_total + 2LL * (W + 2) + 2 + W + 3 + kNarrowWgradPix >= (1LL << 31))
+      return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
+    if (workspace_bytes < nw.workspace)
+      return set_error(B2_ERR_WORKSPACE, "b2_conv3x3_wgrad: workspace %zu < %zu bytes", workspace_bytes,
+                       nw.workspace);
+    CUtensorMap tdy, tx;
+    {
+      const uint64_t dims[3] = {64, uint64_t(nw.m_total), 1};
+      const uint64_t strides[2] = {128, uint64_t(128) * nw.m_total};
+      const uint32_t box[3] = {64, uint32_t(kNarrowWgradPix), 1};
+      B2_TRY(encode_tmap(&tdy, dy_rows, 3, dims, strides, box, true));
+      const uint32_t wbox[3] = {64, uint32_t(nw.box_rows), 1};
+      B2_TRY(encode_tmap(&tx, x_rows, 3, dims, strides, wbox, true));
+    }
+    Params p{};
+    p.splits = nw.splits;
+    p.num_kb = nw.num_kb;
+    p.kb_per_split = nw.kb_per_split;
+    p.wp = W + 2;
+    p.hp = H + 2;
+    p.H = H;
+    p.W = W;
+    p.m_total = int(nw.m_total);
+    p.a_row_shift = W + 3;
+    p.M = Cout;
+    p.N = Cin;
+    p.win_boxes = nw.boxes;
+    p.win_box_rows = nw.box_rows;
+    p.win_bufs = nw.stages;
+    p.partial = static_cast<float*>(workspace);
+    p.alpha = 1.f;
+    p.status = device_status_ptr();
+    B2_TRY(launch_wgrad_narrow(tdy, tx, p, nw.smem, nw.splits, st));
+    const long long total = (long long)Cout * Cin * 9;
+    const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 16));
+    wgrad_reduce_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(workspace), dw, dw_dtype, nw.splits,
+                                                Cout, Cin);
+    return check_cuda(cudaGetLastError(), "wgrad reduce launch");
+  }
   const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled());
   if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
     return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
