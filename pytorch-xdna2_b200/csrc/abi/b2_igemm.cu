@@ -430,6 +430,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      // stage-0 descriptors, stepped by offsets in 16-byte units (shared
+      // addresses stay below 2^18: no carry out of the start-address field)
+      const uint64_t a_desc0 = A_MN ? smem_desc_sw128(smem_u32(smem), 8192, 1024)
+                                    : smem_desc_sw128(smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = B_MN ? smem_desc_sw128(smem_u32(smem) + kABytes, 8192, 1024)
+                                    : smem_desc_sw128(smem_u32(smem) + kABytes, 16, 1024);
+      constexpr uint32_t kAStep = A_MN ? 128u : 2u;  // one 16-deep k step: 16 rows or 32 bytes
+      constexpr uint32_t kBStep = B_MN ? 128u : 2u;
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         int mt, nt, bz, tap, kb0, kb1;
         decode_tile(KIND, p, t, mt, nt, bz, tap, kb0, kb1);
@@ -445,16 +453,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * kStageBytes);
-          const uint32_t sb = sa + kABytes;
+          const uint32_t soff = (uint32_t(stage) * uint32_t(kStageBytes)) >> 4;
+          const uint32_t first = kb > kb0 ? 1u : 0u;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024)
-                                     : smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024)
-                                     : smem_desc_sw128(sb + k * 32, 16, 1024);
-            tc_mma_f16(d_tmem, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            tc_mma_f16(d_tmem, a_desc0 + soff + kAStep * k, b_desc0 + soff + kBStep * k, kIdesc,
+                       (first | uint32_t(k)) ? 1u : 0u);
           tc_commit(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
@@ -1067,6 +1071,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // memory holds.
 constexpr int kMaxWinBufs = 6;
 
+// Row offset of tap (dy, dx) = (tap / 3, tap % 3) in a padded grid of row pitch wp.
+__device__ __forceinline__ int tap_shift(int tap, int wp) {
+  const int dy = tap / 3;
+  return dy * wp + (tap - dy * 3);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_halo_bres_kernel(const __grid_constant__ CUtensorMap tma_win, const __grid_constant__ CUtensorMap tma_b,
                            const Params p) {
@@ -1163,7 +1173,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t aph = 0, acc_phase = 0;
       bool ok = mbar_wait(smem_u32(w_full), 0, p.status, abort_flag);
       tc_fence_after();
-      const uint32_t sw = smem_u32(w_base);
+      // At 64 output columns an MMA is ~32 cycles of tensor work, so the
+      // issuing thread must not rebuild descriptors per instruction: build
+      // them once and step them by offsets (the start-address field counts 16
+      // bytes; every shared-memory address here is below 2^18, so additions
+      // never carry out of the field).
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(a_base), 16, 1024);
+      const uint64_t w_desc0 = smem_desc_sw128(smem_u32(w_base), 16, 1024);
+      uint32_t a_off[9];
+#pragma unroll
+      for (int tap = 0; tap < 9; ++tap) a_off[tap] = uint32_t(tap_shift(tap, p.wp)) * 8u;  // rows of 128 B
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
           ok = false;
@@ -1175,15 +1194,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
-        const uint32_t sa = smem_u32(a_base + as * a_bytes);
-#pragma unroll 1
+        const uint64_t a_desc = a_desc0 + uint64_t((uint32_t(as) * a_bytes) >> 4);
+#pragma unroll
         for (int tap = 0; tap < 9; ++tap) {
-          const int dy = tap / 3, dx = tap - dy * 3;
-          const int shift = dy * p.wp + dx;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            tc_mma_f16(d_tmem, smem_desc_sw128_row(sa, shift, uint32_t(k * 32)),
-                       smem_desc_sw128(sw + tap * kTapBytes + k * 32, 16, 1024), kIdesc, (tap > 0 || k > 0) ? 1u : 0u);
+            tc_mma_f16(d_tmem, a_desc + a_off[tap] + uint32_t(2 * k), w_desc0 + uint32_t((tap * kTapBytes + k * 32) >> 4),
+                       kIdesc, (tap > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(smem_u32(&a_empty[as]));
         if (++as == NW) {
@@ -1248,11 +1265,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the epilogue writes them as this split's partials [split][tap][co][ci],
 // which wgrad_reduce_kernel adds in split order.
 constexpr int kNarrowWgradPix = 128;  // pixels (padded rows) per k-block
-
-__device__ __forceinline__ int tap_shift(int tap, int wp) {
-  const int dy = tap / 3;
-  return dy * wp + (tap - dy * 3);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_wgrad_narrow_kernel(const __grid_constant__ CUtensorMap tma_dy, const __grid_constant__ CUtensorMap tma_x,
@@ -1339,23 +1351,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
+      // descriptors built once for stage 0 and stepped by offsets (see the
+      // resident-weight kernel): per tap pair its window start s1 and the
+      // leading byte offset (s2 - s1) rows to the second tap's half
+      uint64_t a_desc0[5];
+#pragma unroll
+      for (int a = 0; a < 5; ++a) {
+        const int s1 = tap_shift(a < 4 ? 2 * a : 7, p.wp);
+        const int s2 = tap_shift(a < 4 ? 2 * a + 1 : 8, p.wp);
+        a_desc0[a] = smem_desc_sw128(smem_u32(smem) + kDyBytes + uint32_t(s1) * 128u, uint32_t(s2 - s1) * 128u, 1024);
+      }
+      const uint64_t d_desc0 = smem_desc_sw128(smem_u32(smem), 8192, 1024);
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(smem_u32(&full[st]), ph, p.status, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sd = smem_u32(smem + st * stage_bytes);
-        const uint32_t sw = sd + kDyBytes;
-#pragma unroll 1
+        const uint32_t soff = (uint32_t(st) * stage_bytes) >> 4;
+        const uint32_t first = kb > kb0 ? 1u : 0u;
+#pragma unroll
         for (int a = 0; a < 5; ++a) {
-          const int s1 = tap_shift(a < 4 ? 2 * a : 7, p.wp);
-          const int s2 = tap_shift(a < 4 ? 2 * a + 1 : 8, p.wp);
-          const uint32_t lbo = uint32_t(s2 - s1) * 128u;
 #pragma unroll
           for (int k = 0; k < kNarrowWgradPix / 16; ++k)
-            tc_mma_f16(tmem_base + uint32_t(a * BN), smem_desc_sw128(sw + uint32_t(s1 + 16 * k) * 128u, lbo, 1024),
-                       smem_desc_sw128(sd + k * 2048, 8192, 1024), kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            tc_mma_f16(tmem_base + uint32_t(a * BN), a_desc0[a] + soff + uint32_t(128 * k),
+                       d_desc0 + soff + uint32_t(128 * k), kIdesc, (first | uint32_t(k)) ? 1u : 0u);
         }
         tc_commit(smem_u32(&empty[st]));
         if (++st == NS) {
