@@ -308,15 +308,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo,
   return d;
 }
 
-// The same for an operand that starts `row` 128-byte rows into a 1024-byte
-// aligned block written by a 128-byte-swizzled TMA load (any row, also
-// row % 8 != 0): the swizzle phase of each row follows the shared-memory
-// address bits on both sides, so the start address alone selects the rows and
-// the matrix base offset field stays 0 (checked against the unshifted loads:
-// tests/test_gpu_abi.py conv cases on the halo kernel).
-__device__ __forceinline__ uint64_t smem_desc_sw128_row(uint32_t block, int row, uint32_t kbytes) {
-  return smem_desc_sw128(block + uint32_t(row) * 128u + kbytes, 16, 1024);
-}
+// An operand that starts `row` 128-byte rows into a 1024-byte aligned block
+// written by a 128-byte-swizzled TMA load (any row, also row % 8 != 0) takes
+// the block's descriptor with row * 8 added to the start-address field (16-byte
+// units): the swizzle phase of each row follows the shared-memory address bits
+// on both sides, so the start address alone selects the rows and the matrix
+// base offset field stays 0 (checked against the unshifted loads:
+// tests/test_gpu_abi.py conv cases on the halo kernels).  The kernels step
+// descriptors this way; every shared address is below 2^18, so the 14-bit
+// field never carries.
 
 // Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M x N, operand majors.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, bool b_mn) {

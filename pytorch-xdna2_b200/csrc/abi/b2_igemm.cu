@@ -821,6 +821,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 
+// Row offset of tap (dy, dx) = (tap / 3, tap % 3) in a padded grid of row pitch wp.
+__device__ __forceinline__ int tap_shift(int tap, int wp) {
+  const int dy = tap / 3;
+  return dy * wp + (tap - dy * 3);
+}
+
 // ---------------------------------------------------------------------------
 // The SM-pair conv kernel with the A halo loaded once per 64-channel chunk.
 // The nine taps of a chunk read the same padded rows shifted by dy*(W+2)+dx,
@@ -832,7 +838,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // Per k-block an SM stages 16 KB instead of 32 KB, cutting the L2-to-SM
 // traffic of the wide convolutions (3.23 GB per launch at B64 C256 72x72).
 // Barriers, bounded waits, TMEM handling and the epilogue are those of
-// igemm_pair_kernel.
+// igemm_pair_kernel.  (A 128-wide version for 65-128 output channels, M=256
+// x N=128 pair MMAs, measured 3-7 % slower than the single-CTA kernel there.)
 // ---------------------------------------------------------------------------
 template <int NB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -959,6 +966,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int as = 0, bs = 0, acc = 0;
       uint32_t aph = 0, bph = 0, acc_phase = 0;
       bool ok = true;
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(a_base), 16, 1024);
+      const uint64_t b_desc0 = smem_desc_sw128(smem_u32(b_base), 16, 1024);
       for (int t = cluster; t < ntiles && ok; t += nclusters) {
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1, p.status, abort_flag)) {
           ok = false;
@@ -972,22 +981,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(a_base + as * a_bytes);
+          // descriptors stepped by offsets in 16-byte units (window row =
+          // 8 units); shared addresses stay below 2^18
+          const uint64_t a_desc = a_desc0 + uint64_t((uint32_t(as) * a_bytes) >> 4);
           for (int tap = 0; tap < 9; ++tap) {
             if (!mbar_wait(smem_u32(&b_full[bs]), bph, p.status, abort_flag)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const int dy = tap / 3, dx = tap - dy * 3;
-            const int shift = dy * p.wp + dx;
-            const uint32_t sb = smem_u32(b_base + bs * kBBytes);
+            const uint64_t ad = a_desc + uint32_t(tap_shift(tap, p.wp)) * 8u;
+            const uint64_t bd = b_desc0 + (uint32_t(bs) * kBBytes >> 4);
+            const uint32_t first = (ch > 0 || tap > 0) ? 1u : 0u;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t ad = smem_desc_sw128_row(sa, shift, uint32_t(k * 32));
-              const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
-              tc_mma_pair(d_tmem, ad, bd, kIdesc, (ch > 0 || tap > 0 || k > 0) ? 1u : 0u);
-            }
+            for (int k = 0; k < BK / 16; ++k)
+              tc_mma_pair(d_tmem, ad + uint32_t(2 * k), bd + uint32_t(2 * k), kIdesc, (first | uint32_t(k)) ? 1u : 0u);
             tc_commit_pair_mc(smem_u32(&b_empty[bs]), uint16_t(0x3));
             if (++bs == NB) {
               bs = 0;
@@ -1070,12 +1078,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 // as in the SM-pair halo kernel), with as many windows in flight as shared
 // memory holds.
 constexpr int kMaxWinBufs = 6;
-
-// Row offset of tap (dy, dx) = (tap / 3, tap % 3) in a padded grid of row pitch wp.
-__device__ __forceinline__ int tap_shift(int tap, int wp) {
-  const int dy = tap / 3;
-  return dy * wp + (tap - dy * 3);
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_halo_bres_kernel(const __grid_constant__ CUtensorMap tma_win, const __grid_constant__ CUtensorMap tma_b,
