@@ -150,6 +150,11 @@ LARGE = [  # the reference's run_conv3x3w_torch.py shapes (:22-35) and the READM
     (2, 256, 10, 72, 256, True),
     (1, 192, 4, 150, 320, False),
     (1, 256, 3, 200, 256, False),
+    # narrow layers with enough padded rows for the all-taps weight-gradient
+    # kernel: a three-box input window (W = 224) with 3 -> 10 channels, and odd
+    # channel counts below one 64-channel chunk
+    (8, 3, 40, 224, 10, True),
+    (16, 37, 40, 40, 45, False),
 ]
 
 
