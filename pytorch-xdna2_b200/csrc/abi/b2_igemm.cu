@@ -839,7 +839,8 @@ __device__ __forceinline__ int tap_shift(int tap, int wp) {
 // traffic of the wide convolutions (3.23 GB per launch at B64 C256 72x72).
 // Barriers, bounded waits, TMEM handling and the epilogue are those of
 // igemm_pair_kernel.  (A 128-wide version for 65-128 output channels, M=256
-// x N=128 pair MMAs, measured 3-7 % slower than the single-CTA kernel there.)
+// x N=128 pair MMAs with a 6- or a 12-deep B ring, measured 3-7 % slower than
+// the single-CTA kernel there, although it moves 2.7x fewer bytes from L2.)
 // ---------------------------------------------------------------------------
 template <int NB>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
