@@ -1,0 +1,89 @@
+"""CPU checks of the benchmark models and of the host logic around them (no
+GPU): the reference's own style-transfer network and loss as rebuilt in
+bench.py (structure, a BF16 training step on the CPU path, the module pattern
+``regions.fuse_perceptual_loss`` matches, and that a fused loss module falls
+back to its own method on CPU tensors), and the fused loss's cache of its
+normalisation constants."""
+import torch
+
+import bench
+from xdna_train import regions
+
+
+def _tiny_batch(b=2, hw=16):
+    g = torch.Generator().manual_seed(0)
+    x = (torch.rand(b, 3, hw, hw, generator=g) * 2 - 1).bfloat16()
+    t = torch.rand(b, 3, hw, hw, generator=g).bfloat16()
+    return x, t
+
+
+def test_ref_stylenet_shapes_and_pairs():
+    torch.manual_seed(0)
+    net = bench.RefStyleNet().bfloat16()
+    x, _ = _tiny_batch()
+    y = net(x)
+    assert y.shape == x.shape and y.dtype == torch.bfloat16
+    # encoder (3) + first halves of the 5 residual blocks + decoder (2) + head
+    pairs = net.norm_act_pairs()
+    assert len(pairs) == 11
+    assert all(isinstance(bn, torch.nn.BatchNorm2d) and isinstance(act, torch.nn.LeakyReLU) and act.negative_slope == 0.2
+               for bn, act in pairs)
+    # the head sees the decoder output, the first encoder map and the input: 128 + 64 + 3 channels
+    assert net.head.conv.in_channels == 195 and net.out.kernel_size == (1, 1) and net.out.bias is not None
+
+
+def test_ref_style_loss_training_step_on_cpu():
+    torch.manual_seed(0)
+    net = bench.RefStyleNet().bfloat16()
+    crit = bench.RefStyleLoss().bfloat16()
+    assert not any(p.requires_grad for p in crit.parameters())
+    opt = torch.optim.Adam(net.parameters(), lr=1e-4, weight_decay=1e-5)
+    x, t = _tiny_batch()
+    losses = []
+    for _ in range(2):
+        loss = crit(net(x), t)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+        losses.append(loss.item())
+    assert all(v == v and v > 0 for v in losses)
+    assert all(p.grad is not None for p in net.parameters())
+
+
+def test_ref_style_loss_matches_region_pattern_and_falls_back_on_cpu():
+    torch.manual_seed(0)
+    crit = bench.RefStyleLoss().bfloat16()
+    x, t = _tiny_batch()
+    x = x.requires_grad_()
+    plain = crit.compute_perceptual_loss(x, t)
+    (gx,) = torch.autograd.grad(plain, x)
+    assert regions.fuse_perceptual_loss(crit)
+    # CPU tensors are not eligible for the fused region: the module's own method runs, bit for bit
+    fused = crit.compute_perceptual_loss(x, t)
+    (gf,) = torch.autograd.grad(fused, x)
+    assert torch.equal(fused, plain) and torch.equal(gf, gx)
+
+
+def test_norm_constants_are_cached_per_tensor_version():
+    mod = torch.nn.Module()
+    mean = torch.tensor([0.485, 0.456, 0.406])
+    std = torch.tensor([0.229, 0.224, 0.225])
+    x = torch.zeros(1, 3, 2, 2, dtype=torch.bfloat16)
+    m1, s1 = regions._norm_constants(mod, mean, std, x)
+    assert m1.shape == (1, 3, 1, 1) and m1.dtype == torch.bfloat16
+    assert torch.equal(m1.flatten(), mean.bfloat16()) and torch.equal(s1.flatten(), std.bfloat16())
+    m2, s2 = regions._norm_constants(mod, mean, std, x)
+    assert m2 is m1 and s2 is s1  # no second conversion
+    mean.mul_(2.0)  # an in-place write bumps the version: converted again
+    m3, _ = regions._norm_constants(mod, mean, std, x)
+    assert m3 is not m1 and torch.equal(m3.flatten(), mean.bfloat16())
+    other = mean.clone()  # another tensor object with the same values is not the cached one
+    m4, _ = regions._norm_constants(mod, other, std, x)
+    assert m4 is not m3
+    # a float32 input gets float32 constants (the key includes the dtype)
+    m5, _ = regions._norm_constants(mod, other, std, x.float())
+    assert m5.dtype == torch.float32
+    # constants that are not tensors are converted on every call
+    la, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
+    lb, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
+    assert la is not lb and torch.equal(la, lb)
