@@ -39,3 +39,21 @@ def test_argument_errors_need_no_gpu():
     assert st == 1 and b"bad shape" in L.b2_last_error()
     with pytest.raises(_abi.B2Error):
         _abi.call("b2_region_relu_bf16", None, None, 5, None)
+
+
+def _declared_arity():
+    """Parameter count of every b2_* function declared in include/b2.h."""
+    text = re.sub(r"/\*.*?\*/|//[^\n]*", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"(?:const char\*|b2_status|int|size_t)\s+(b2_\w+)\(([^;]*?)\)\s*;", text, re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_bindings_match_the_header_arity():
+    arity = _declared_arity()
+    assert set(arity) == set(declared())
+    for name, n in arity.items():
+        assert len(_abi.SIGNATURES[name]) == n, f"{name}: header declares {n} parameters, ctypes binds " \
+                                                f"{len(_abi.SIGNATURES[name])}"
