@@ -921,7 +921,8 @@ def conv_sweep(args):
                 fl = 2.0 * b * hw * hw * c * c * 9
                 iters = max(3, min(50, int(0.03 / (fl / 1.2e15))))
                 kt = kernel_times(x, dy, conv, 0, iters=iters)
-                row = {"shape": f"B{b} C{c} HW{hw}", "gflop_per_direction": round(fl / 1e9, 3), "iters": iters}
+                row = {"shape": f"B{b} C{c} HW{hw}", "batch": b, "channels": c, "hw": hw,
+                       "gflop_per_direction": round(fl / 1e9, 3), "iters": iters}
                 for k in ("fwd", "dgrad", "wgrad"):
                     tf = fl / (kt[k] * 1e-3) / 1e12
                     row[k] = {"us": round(kt[k] * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / peak, 4)}
@@ -932,16 +933,23 @@ def conv_sweep(args):
                 print(json.dumps(row), flush=True)
                 del x, dy
             torch.xdna.empty_cache()
-    tot_fl = sum(r["gflop_per_direction"] for r in rows) * 3
-    tot_us = sum(r[k]["us"] for r in rows for k in ("fwd", "dgrad", "wgrad"))
-    big = [r[k]["frac"] for r in rows for k in ("fwd", "dgrad", "wgrad")
-           if int(r["shape"].split()[1][1:]) >= 256 and int(r["shape"].split()[2][2:]) >= 36]
-    print(json.dumps({"probe": "conv3x3 sweep (BASELINE configs[1])", "shapes": len(rows), "peak_tflops": peak,
-                      "peak_kind": kind, "sum_gflop": round(tot_fl, 1), "sum_us": round(tot_us, 1),
-                      "aggregate_tflops": round(tot_fl * 1e9 / (tot_us * 1e-6) / 1e12, 1),
-                      "large_channel_min_frac": min(big) if big else None,
-                      "large_channel_median_frac": statistics.median(big) if big else None,
-                      "cpu_threads": torch.get_num_threads() if cpu_tf else None}), flush=True)
+    summary = sweep_summary(rows)
+    summary.update(peak_tflops=peak, peak_kind=kind, cpu_threads=torch.get_num_threads() if cpu_tf else None)
+    print(json.dumps({"probe": "conv3x3 sweep (BASELINE configs[1])", **summary}), flush=True)
+
+
+def sweep_summary(rows):
+    """Totals of ``--conv-sweep`` rows: work and kernel time summed over the
+    three directions, the aggregate rate, and the fraction of peak over the
+    large-channel shapes (C >= 256, H = W >= 36; the sweep's >= 60 % target)."""
+    dirs = ("fwd", "dgrad", "wgrad")
+    tot_fl = sum(r["gflop_per_direction"] for r in rows) * len(dirs)
+    tot_us = sum(r[k]["us"] for r in rows for k in dirs)
+    big = [r[k]["frac"] for r in rows for k in dirs if r["channels"] >= 256 and r["hw"] >= 36]
+    return {"shapes": len(rows), "sum_gflop": round(tot_fl, 1), "sum_us": round(tot_us, 1),
+            "aggregate_tflops": round(tot_fl * 1e9 / (tot_us * 1e-6) / 1e12, 1) if tot_us > 0 else None,
+            "large_channel_min_frac": min(big) if big else None,
+            "large_channel_median_frac": statistics.median(big) if big else None}
 
 
 def bn_probe(args):

@@ -87,3 +87,20 @@ def test_norm_constants_are_cached_per_tensor_version():
     la, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
     lb, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
     assert la is not lb and torch.equal(la, lb)
+
+
+def test_conv_sweep_summary():
+    """`bench.py --conv-sweep` totals: FLOPs and kernel time over the three
+    directions; the large-channel fraction counts only C >= 256, H >= 36."""
+    def row(b, c, hw, us, frac):
+        fl = 2.0 * b * hw * hw * c * c * 9 / 1e9
+        return {"shape": f"B{b} C{c} HW{hw}", "batch": b, "channels": c, "hw": hw, "gflop_per_direction": fl,
+                **{k: {"us": us, "tflops": 0.0, "frac": frac} for k in ("fwd", "dgrad", "wgrad")}}
+    rows = [row(8, 64, 18, 10.0, 0.1), row(128, 256, 36, 100.0, 0.8), row(128, 512, 18, 50.0, 0.5),
+            row(40, 512, 72, 200.0, 0.9)]
+    s = bench.sweep_summary(rows)
+    gflop = sum(r["gflop_per_direction"] for r in rows) * 3
+    assert s["shapes"] == 4 and abs(s["sum_gflop"] - round(gflop, 1)) < 1e-9 and s["sum_us"] == 1080.0
+    assert abs(s["aggregate_tflops"] - round(gflop * 1e9 / 1080e-6 / 1e12, 1)) < 1e-9
+    assert s["large_channel_min_frac"] == 0.8 and abs(s["large_channel_median_frac"] - 0.85) < 1e-12
+    assert bench.sweep_summary([])["aggregate_tflops"] is None
