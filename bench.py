@@ -1,15 +1,22 @@
-"""Benchmark: BF16 3x3-conv training step on the `xdna` device (B200).
+"""Benchmark of the `xdna` device on B200: BF16 training, one process per GPU.
 
-Workload (the 3x3 conv sweep, at a large-channel
-point): per GPU a batch of 128 NCHW BF16 images 256 x 72 x 72, one
-Conv2d(256, 256, 3, padding=1, bias) trained with a synthetic upstream gradient
-dY ~ N(0,1): forward, dgrad, wgrad (deferred, materialized by the optimizer),
-bias grad and a fused Adam step; with N GPUs the gradients are averaged with
-NCCL all-reduce over NVLink (data parallel, weak scaling).  Metric: training
-images/s for the whole job, plus the conv's fwd+bwd TFLOP/s against the
-measured dense-BF16 peak in "roofline".
+Headline (the default; BASELINE.json's metric "train images/s at 1/2/4/8
+B200; 3x3 conv fwd+bwd TFLOP/s vs BF16 peak" on its configs[4], ResNet-50):
+per GPU a batch of 128 synthetic 224x224 images ~ N(0,1) (channels-last
+BF16) with uniform random labels over 1000 classes, a random-init
+torchvision ResNet-50 on ``torch.device("xdna")``, cross-entropy, backward
+(deferred conv weight gradients materialized by the optimizer or the
+all-reduce), SGD momentum 0.9 (``--optimizer adam``: the config's Adam
+variant); with N GPUs the gradients are averaged by bucketed NCCL
+all-reduces overlapped with backward (``xdna_train.ddp``; data parallel, weak
+scaling).  ``value`` = images/s of the whole job; ``roofline`` = the 3x3
+convolution kernels' FLOPs over their device time inside the step (CUDA
+event pairs around each launch, on its stream); ``e2e`` = the same step fed
+from pinned host memory (images and labels copied every step, the loss read
+back every step).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload conv|readme|mlp|style     (the other configs)
 
 ``--impl reference`` times the reference's CPU BF16 path for the same step
 (stock PyTorch CPU kernels -- what the reference runs for these ops,
@@ -34,8 +41,10 @@ sys.path.insert(0, str(REPO))
 import torch  # noqa: E402
 
 METRIC = "train images/s at 1/2/4/8 B200; 3x3 conv fwd+bwd TFLOP/s vs BF16 peak"
-B_PER_GPU, C, HW = 128, 256, 72
+B_PER_GPU, C, HW = 128, 256, 72  # --workload conv: the 3x3 conv layer step
 CPU_SAMPLE = 4  # images per CPU step (bounded sample of the same workload)
+RESNET_BATCH, RESNET_HW = 128, 224  # the headline: ResNet-50 per-GPU batch
+RESNET_CPU_SAMPLE = 16  # images per CPU step of the ResNet-50 reference path
 
 
 def conv_flops(b: int) -> float:
@@ -53,12 +62,17 @@ def conv_traffic_bytes():
     return int(m.group(1)) if m else None
 
 
-def peaks():
+def peaks(sustained: bool = False):
+    """(bf16 TFLOP/s, HBM GB/s, kind): the pool's measured peaks (the burst
+    GEMM figure, or with ``sustained`` the figure of a seconds-long GEMM loop
+    under the power cap, for kernels timed inside a long step), else the
+    recipe's fallback."""
     p = REPO / "MEASURED_PEAKS.json"
     if p.is_file():
         d = json.loads(p.read_text())
-        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
-    return 1590.0, 6650.0, "fallback"
+        tf = d.get("bf16_tflops_sustained") if sustained else None
+        return float(tf or d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return (1400.0 if sustained else 1590.0), 6650.0, "fallback"
 
 
 # --------------------------------------------------------------------- clocks
@@ -160,7 +174,7 @@ def allreduce_max(v: float, world: int) -> float:
     return float(t.item())
 
 
-def run_ours(args):
+def run_conv_layer(args):
     world, rank, local = setup_dist(args)
     import torch.nn as nn
 
@@ -389,7 +403,7 @@ def cpu_reference_step_rate(steps: int, warmup: int, sample: int = CPU_SAMPLE):
     return sample / dt, dt
 
 
-def run_reference(args):
+def run_conv_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
@@ -408,6 +422,286 @@ def run_reference(args):
                          "sample": f"{CPU_SAMPLE} images of {C}x{HW}x{HW} per step (of the {B_PER_GPU}-image "
                                    "GPU batch), stock PyTorch CPU conv/convolution_backward/_fused_adam_ = the "
                                    f"reference's CPU path; torch {torch.__version__} (reference pins 2.14)"},
+        "e2e": {"value": round(rate, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------- headline: ResNet-50
+
+def resnet50_model(dev):
+    """torchvision ResNet-50 (random init, seed 0) in bf16, channels-last."""
+    from torchvision.models import resnet50
+    torch.manual_seed(0)
+    return resnet50(num_classes=1000).bfloat16().to(dev).to(memory_format=torch.channels_last)
+
+
+def resnet50_train_flops(batch: int, hw: int = RESNET_HW):
+    """Algorithmic FLOPs of one ResNet-50 training step (2 per multiply-add),
+    counted from the layer shapes: every convolution and the classifier
+    forward, input gradient (all but the stem, whose input needs none) and
+    weight gradient.  Returns (total, of which the 3x3 stride-1 convolutions)."""
+    import torch.nn as nn
+    from torchvision.models import resnet50
+    m = resnet50(num_classes=1000).to("meta")
+    tot, c33 = [0.0], [0.0]
+    stem = m.conv1
+
+    def conv_hook(mod, inp, out):
+        macs = out.numel() * mod.in_channels * mod.kernel_size[0] * mod.kernel_size[1] / mod.groups
+        f = 2.0 * macs * (2 if mod is stem else 3)
+        tot[0] += f
+        if mod.kernel_size == (3, 3) and mod.stride == (1, 1):
+            c33[0] += f
+
+    def fc_hook(mod, inp, out):
+        tot[0] += 3 * 2.0 * out.numel() * mod.in_features
+
+    hs = [mm.register_forward_hook(conv_hook) for mm in m.modules() if isinstance(mm, nn.Conv2d)]
+    hs.append(m.fc.register_forward_hook(fc_hook))
+    with torch.no_grad():
+        m(torch.empty(batch, 3, hw, hw, device="meta"))
+    for h in hs:
+        h.remove()
+    return tot[0], c33[0]
+
+
+def _sgd_or_adam(model, optimizer, on_device):
+    # the CPU side keeps the foreach implementations: torch 2.11's CPU
+    # _fused_sgd_ leaves bf16 parameters unchanged
+    fused = True if on_device else None
+    if optimizer == "adam":
+        return torch.optim.Adam(model.parameters(), lr=1e-3, fused=fused)
+    return torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=fused)
+
+
+def run_resnet50(args):
+    """The headline line (see the module docstring)."""
+    import torch.nn.functional as F
+    world, rank, local = setup_dist(args)
+    import xdna_train
+    from xdna_train.ddp import GradAllReduce
+    xdna_train.register_xdna_device()
+    X = torch.device("xdna", local)
+    cl = torch.channels_last
+    B = args.batch if args.batch != B_PER_GPU else RESNET_BATCH
+    model = resnet50_model(X)
+    opt = _sgd_or_adam(model, args.optimizer, True)
+    ar = GradAllReduce(model) if world > 1 else None
+    g = torch.Generator().manual_seed(1000 + rank)
+    x_host = torch.empty((B, 3, RESNET_HW, RESNET_HW), dtype=torch.bfloat16, pin_memory=True)
+    x_host.copy_(torch.randn(B, 3, RESNET_HW, RESNET_HW, generator=g))
+    y_host = torch.randint(0, 1000, (B,), generator=g).pin_memory()
+    x = x_host.to(X).contiguous(memory_format=cl)
+    y = y_host.to(X)
+
+    def step(xin, yin):
+        opt.zero_grad(set_to_none=True)
+        loss = F.cross_entropy(model(xin).float(), yin)
+        loss.backward()
+        if ar is not None:
+            ar.synchronize()
+        opt.step()
+        return loss
+
+    s = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step(x, y)
+    torch.cuda.synchronize()
+    xdna_train.reset_mapped_cpu_stats()
+    if world > 1:
+        cuda_barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(s)
+        for _ in range(args.steps):
+            loss = step(x, y)
+        e1.record(s)
+        torch.cuda.synchronize()
+    if world > 1:
+        cuda_barrier()
+    ms = allreduce_max(e0.elapsed_time(e1) / args.steps, world)
+    launches = sum(xdna_train.kernel_stats().values())
+    fallbacks = xdna_train.fallback_stats()
+    final_loss = float(loss.item())
+
+    # ---- e2e: every step copies its images and labels from pinned host
+    # memory (on a copy stream, one step ahead, through two device buffers --
+    # what a prefetching loader does) and reads its loss back to the host
+    copy_s = torch.cuda.Stream()
+    bx = [torch.empty_like(x) for _ in range(2)]
+    by = [torch.empty_like(y) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
+    loss_host = torch.empty(max(1, args.steps), dtype=torch.float32, pin_memory=True)
+
+    def prefetch(i):
+        with torch.cuda.stream(copy_s):
+            copy_s.wait_event(used[i])
+            bx[i].copy_(x_host, non_blocking=True)
+            by[i].copy_(y_host, non_blocking=True)
+            copied[i].record(copy_s)
+
+    for i in range(2):
+        used[i].record(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        cuda_barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(s)
+    copy_s.wait_stream(s)
+    prefetch(0)
+    for k in range(args.steps):
+        i = k % 2
+        s.wait_event(copied[i])
+        if k + 1 < args.steps:
+            prefetch(1 - i)
+        loss = step(bx[i], by[i])
+        used[i].record(s)
+        loss_host[k:k + 1].copy_(loss.detach().reshape(1), non_blocking=True)
+    e3.record(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        cuda_barrier()
+    e2e_ms = allreduce_max(e2.elapsed_time(e3) / args.steps, world)
+    assert torch.isfinite(loss_host[:args.steps]).all(), "non-finite loss"
+
+    # ---- the 3x3 convolution kernels (and the other timed launch sites)
+    # inside the same step: CUDA event pairs around each launch on its stream,
+    # over a few more steps of the same workload
+    xdna_train.kernel_timer(True)
+    for _ in range(3):
+        step(x, y)
+    torch.cuda.synchronize()
+    xdna_train.kernel_timer(False)
+    kt = xdna_train.kernel_times()
+
+    # ---- the gradient all-reduce alone, per step (N > 1): every bucket's
+    # collective, events on the launching stream
+    ar_ms = None
+    if ar is not None:
+        import torch.distributed as dist
+        cuda_barrier()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(s)
+        for _ in range(5):
+            for bkt in ar.buckets:
+                dist.all_reduce(xdna_train.as_cuda(bkt["flat"]), op=dist.ReduceOp.AVG)
+        eb.record(s)
+        torch.cuda.synchronize()
+        ar_ms = allreduce_max(ea.elapsed_time(eb) / 5, world)
+
+    if rank != 0:
+        return None
+    total_fl, c33_fl = resnet50_train_flops(B)
+    peak_s, hbm, peak_kind = peaks(sustained=True)
+    conv = {k: v for k, v in kt.items() if k.startswith("conv3x3.")}
+    c_ms = sum(v["ms"] for v in conv.values())
+    c_work = sum(v["work"] for v in conv.values())
+    c_launch = sum(v["launches"] for v in conv.values())
+    achieved = c_work / (c_ms * 1e-3) / 1e12 if c_ms > 0 else None
+    images = B * world
+    line = {
+        "metric": METRIC,
+        "value": round(images / (ms * 1e-3), 2),
+        "unit": "images/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (images ~ N(0,1), uniform labels over 1000 classes; random-init ResNet-50)",
+        "config": {"workload": f"ResNet-50 training step (BASELINE configs[4]), {RESNET_HW}x{RESNET_HW}, "
+                               f"per-GPU batch {B}, channels-last bf16, cross-entropy, "
+                               + ("Adam lr 1e-3" if args.optimizer == "adam" else "SGD momentum 0.9")
+                               + (", NCCL all-reduce of bucketed gradients overlapped with backward"
+                                  if world > 1 else ""),
+                   "model": "resnet50", "global_batch": images, "per_gpu_batch": B, "image_hw": RESNET_HW,
+                   "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (the step's activations are tens of GB)",
+                   "train_gflop_per_step_per_gpu": round(total_fl / 1e9, 1),
+                   "conv3x3_s1_gflop_per_step_per_gpu": round(c33_fl / 1e9, 1)},
+        "e2e": {"value": round(images / (e2e_ms * 1e-3), 2), "unit": "images/s",
+                "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size() + y_host.numel() * 8),
+                "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None, "peak": peak_s,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_s, 4) if achieved else None,
+                     "traffic": conv_step_traffic_bytes(),
+                     "kernel": "3x3 stride-1 convolutions of the step (tcgen05 implicit GEMM: fwd, dgrad, wgrad)",
+                     "launches_per_step": round(c_launch / 3, 1),
+                     "gflop_per_launch": round(c_work / max(1, c_launch) / 1e9, 3),
+                     "ms_per_launch": round(c_ms / max(1, c_launch), 5),
+                     "peak_kind": f"{peak_kind}, sustained (kernels timed inside a long step)"},
+        "kernel_times_per_step": {k: {"launches": round(v["launches"] / 3, 1), "ms": round(v["ms"] / 3, 4),
+                                      "tflops": round(v["work"] / (v["ms"] * 1e-3) / 1e12, 1) if v["ms"] else None}
+                                  for k, v in sorted(kt.items())},
+        "step_tflops": round(total_fl / (ms * 1e-3) / 1e12, 1),
+        "final_loss": round(final_loss, 4),
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+        "fallback_ops": dict(sorted(((k, v["calls"]) for k, v in fallbacks.items()), key=lambda kv: -kv[1])[:10]),
+    }
+    if ar_ms is not None:
+        line["allreduce_ms_per_step"] = round(ar_ms, 4)
+        line["allreduce_buckets"] = len(ar.buckets)
+    return line
+
+
+def cpu_resnet50_rate(steps: int, warmup: int, sample: int = RESNET_CPU_SAMPLE, optimizer: str = "sgd"):
+    """images/s of the reference's CPU BF16 path (stock PyTorch CPU ops) on
+    a bounded sample of the ResNet-50 step: ``sample`` images per step."""
+    import torch.nn.functional as F
+    model = resnet50_model("cpu")
+    opt = _sgd_or_adam(model, optimizer, False)
+    g = torch.Generator().manual_seed(1000)
+    x = torch.randn(sample, 3, RESNET_HW, RESNET_HW, generator=g).bfloat16().contiguous(
+        memory_format=torch.channels_last)
+    y = torch.randint(0, 1000, (sample,), generator=g)
+
+    def one():
+        opt.zero_grad(set_to_none=True)
+        F.cross_entropy(model(x).float(), y).backward()
+        opt.step()
+
+    dt = _timed(one, steps, warmup, lambda: None)
+    return sample / dt, dt
+
+
+def conv_step_traffic_bytes():
+    """DRAM bytes per launch of the 3x3 conv kernels in the ResNet-50 step,
+    from the committed ncu summary (None until one is committed)."""
+    import re
+    f = REPO / "profiles" / "conv3x3_resnet50_step_traffic.md"
+    if not f.is_file():
+        return None
+    m = re.search(r"traffic_bytes_per_launch_B128:\s*(\d+)", f.read_text())
+    return int(m.group(1)) if m else None
+
+
+def run_resnet50_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    steps, warmup = max(1, args.steps), max(1, min(args.warmup, 3))
+    rate, dt = cpu_resnet50_rate(steps, warmup, optimizer=args.optimizer)
+    cores = torch.get_num_threads()
+    return {
+        "metric": METRIC, "value": round(rate, 3), "unit": "images/s", "impl": "reference",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": steps, "warmup": warmup,
+        "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (images ~ N(0,1), uniform labels over 1000 classes)",
+        "config": {"workload": f"ResNet-50 training step (BASELINE configs[4]), {RESNET_HW}x{RESNET_HW}, "
+                               "channels-last bf16, cross-entropy, "
+                               + ("Adam lr 1e-3" if args.optimizer == "adam" else "SGD momentum 0.9")
+                               + ", on the reference's CPU BF16 path",
+                   "model": "resnet50", "per_step_sample_images": RESNET_CPU_SAMPLE, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(rate, 3), "unit": "images/s", "cores": cores, "kind": "reference",
+                         "sample": f"{RESNET_CPU_SAMPLE} images of 3x{RESNET_HW}x{RESNET_HW} per step (of the "
+                                   f"{RESNET_BATCH}-image GPU batch); stock PyTorch CPU ops = the reference's CPU "
+                                   f"path; torch {torch.__version__} (reference pins 2.14)"},
         "e2e": {"value": round(rate, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -628,7 +922,7 @@ def _timed(fn, steps, warmup, device_sync):
 
 
 def run_workload(args):
-    """One JSON line for a non-headline BASELINE config (1, 3, 4 or 5)."""
+    """One JSON line for a non-headline BASELINE config (1, 3 or 4)."""
     import torch.nn as nn
     import torch.nn.functional as F
 
@@ -783,44 +1077,6 @@ def run_workload(args):
             if rank == 0 and world == 1 and not args.no_cpu_baseline:
                 rn["cpu_it_s"] = round(1 / _timed(read(make_ref("cpu", False)), 2, 1, cpu), 3)
         c = cpu_rate(lambda: make("cpu", False))
-    elif w == "resnet50":
-        # config 5: ResNet-50 224x224, per-GPU batch 128, SGD momentum 0.9, DP over NCCL
-        from torchvision.models import resnet50
-
-        from xdna_train.ddp import GradAllReduce
-        bsz = args.batch if args.batch != B_PER_GPU else 128
-
-        def make(dev, b):
-            torch.manual_seed(0)
-            model = resnet50(num_classes=1000).bfloat16().to(dev).to(memory_format=torch.channels_last)
-            on_x = torch.device(dev).type == "xdna"
-            # the CPU side keeps the single-tensor SGD: torch 2.11's CPU _fused_sgd_
-            # leaves bf16 parameters unchanged
-            if args.optimizer == "adam":  # the config's Adam variant
-                opt = torch.optim.Adam(model.parameters(), lr=1e-3, fused=True if on_x else None)
-            else:
-                opt = torch.optim.SGD(model.parameters(), lr=0.1, momentum=0.9, fused=True if on_x else None)
-            ar = GradAllReduce(model) if (world > 1 and torch.device(dev).type == "xdna") else None
-            g = torch.Generator().manual_seed(rank)
-            x = torch.randn(b, 3, 224, 224, generator=g).bfloat16().to(dev).contiguous(
-                memory_format=torch.channels_last)
-            y = torch.randint(0, 1000, (b,), generator=g).to(dev)
-
-            def step():
-                opt.zero_grad(set_to_none=True)
-                loss = F.cross_entropy(model(x).float(), y)
-                loss.backward()
-                if ar is not None:
-                    ar.synchronize()
-                opt.step()
-            return step
-        dt = _timed(make(X, bsz), args.steps, args.warmup, sync)
-        out.update(metric="ResNet-50 training images/s (BASELINE config 5)", value=round(world * bsz / dt, 1),
-                   unit="images/s", ms_per_step=round(dt * 1e3, 4), per_gpu_batch=bsz, scaling="weak",
-                   optimizer="Adam lr 1e-3" if args.optimizer == "adam" else "SGD momentum 0.9")
-        c = None
-        if rank == 0 and world == 1 and not args.no_cpu_baseline:
-            c = _timed(make("cpu", 4), 2, 1, cpu) / 4 * bsz  # seconds per bsz images, from a 4-image sample
     else:
         raise SystemExit(f"unknown workload {w}")
     if c:
@@ -828,10 +1084,8 @@ def run_workload(args):
             unit_scale = 1 / c
         elif w == "mlp":
             unit_scale = 128.85e9 / c / 1e12
-        elif w == "style":
-            unit_scale = 1 / c
         else:
-            unit_scale = bsz / c
+            unit_scale = 1 / c
         out["cpu_baseline"] = {"value": round(unit_scale, 3), "unit": out["unit"], "cores": torch.get_num_threads(),
                                "kind": "reference", "sample": "same step on the reference's CPU BF16 path "
                                                               "(stock PyTorch CPU ops), few steps"}
@@ -1144,18 +1398,22 @@ def main():
     ap.add_argument("--adam-bf16", action="store_true")
     ap.add_argument("--params", type=float, default=64.0, help="--adam-probe: millions of parameters")
     ap.add_argument("--optimizer", default="sgd", choices=["sgd", "adam"], help="--workload resnet50: optimizer")
-    ap.add_argument("--workload", default="conv", choices=["conv", "readme", "mlp", "style", "resnet50"],
-                    help="conv (default, the headline) or another BASELINE config")
+    ap.add_argument("--workload", default="resnet50", choices=["resnet50", "conv", "readme", "mlp", "style"],
+                    help="resnet50 (default, the headline) or another BASELINE config")
     ap.add_argument("--batch", type=int, default=B_PER_GPU)
     ap.add_argument("--channels", type=int, default=C)
     ap.add_argument("--hw", type=int, default=HW)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (resnet50: 100, conv: 200, others: 200)")
+    ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (resnet50: 20, others: 5)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 100 if args.workload == "resnet50" else 200
+    if args.warmup is None:
+        args.warmup = 20 if args.workload == "resnet50" else 5
     if args.kernel_probe:
         kernel_probe(args)
         return
@@ -1171,20 +1429,29 @@ def main():
     if args.adam_probe:
         adam_probe(args)
         return
-    if args.workload != "conv":
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.workload not in ("conv", "resnet50"):
         line = run_workload(args)
         if line is not None:
             print(json.dumps(line), flush=True)
-        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if world > 1:
             import torch.distributed as dist
             cuda_barrier()
             dist.destroy_process_group()
         return
     args.warmup = max(3, args.warmup) if args.impl == "ours" else args.warmup
     if args.impl == "reference":
-        line = run_reference(args)
+        line = run_resnet50_reference(args) if args.workload == "resnet50" else run_conv_reference(args)
+    elif args.workload == "resnet50":
+        line = run_resnet50(args)
+        if line is not None and not args.no_cpu_baseline and line["n_gpus"] == 1:
+            rate, dt = cpu_resnet50_rate(steps=3, warmup=1, optimizer=args.optimizer)
+            line["cpu_baseline"] = {
+                "value": round(rate, 3), "unit": "images/s", "cores": torch.get_num_threads(), "kind": "reference",
+                "sample": f"{RESNET_CPU_SAMPLE} images per step, 3 timed steps after 1 warm-up; the same ResNet-50 "
+                          "step on stock PyTorch CPU BF16 ops (the reference's CPU path)"}
     else:
-        line = run_ours(args)
+        line = run_conv_layer(args)
         if line is not None and not args.no_cpu_baseline and line["n_gpus"] == 1:
             rate, dt = cpu_reference_step_rate(steps=3, warmup=1)
             line["cpu_baseline"] = {
@@ -1193,7 +1460,7 @@ def main():
                           "conv/convolution_backward/_fused_adam_ (the reference's CPU path)"}
     if line is not None:
         print(json.dumps(line), flush=True)
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.impl == "ours":
+    if world > 1 and args.impl == "ours":
         import torch.distributed as dist
         cuda_barrier()
         dist.destroy_process_group()

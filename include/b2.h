@@ -157,7 +157,9 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw,
  * that loads the library, until exit.  If the usual split plan needs more,
  * fewer splits are used; shapes with 9*Cout*Cin*4 bytes above the limit fail
  * with B2_ERR_WORKSPACE.  The first call on a device looks the array's
- * address up (make it before any stream capture).  Calls share the array:
+ * address up (make it before any stream capture); the address is kept for the
+ * lifetime of that device's primary context (not valid after a
+ * cudaDeviceReset in the same process).  Calls share the array:
  * calls that overlap on the GPU race and must be serialized by the caller.
  * Calls no cudaMalloc / cudaFree. */
 b2_status b2_conv3x3_wgrad_noalloc(const void* dy_rows, const void* x_rows,

@@ -2309,7 +2309,9 @@ b2_status b2_conv1x1_wgrad(const void* dy, const void* x, void* dw, int dw_dtype
 //     not fit, the call fails with B2_ERR_WORKSPACE.
 //   * The array's device address is looked up once per device, on the first
 //     call made with that device current (cudaGetSymbolAddress); make that
-//     first call before any stream capture.
+//     first call before any stream capture.  The cached address is valid for
+//     the lifetime of the device's primary context: a cudaDeviceReset in the
+//     same process invalidates it.
 //   * Every call reuses the same array.  Each call overwrites every partial
 //     sum it later reads, so nothing has to be cleared between calls, but two
 //     calls that overlap on the GPU (different streams, or different host

@@ -350,6 +350,7 @@ at::Tensor conv1x1_forward(const at::Tensor& input, const at::Tensor& weight, co
   if (b.defined()) materialize(b);
   const auto mf = layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous;
   at::Tensor y = empty({B, Cout, H, W}, at::kBFloat16, dev, mf);
+  KernelTimer kt("conv1x1.fwd", 2.0 * B * H * W * Cin * Cout, stream(dev));
   XDNA_B2(b2_conv1x1_fwd(input.data_ptr(), w.data_ptr(), b.defined() ? b.data_ptr() : nullptr, y.data_ptr(), layout, B,
                          Cin, H * W, Cout, stream(dev)));
   count_launch("conv1x1.fwd");
@@ -371,6 +372,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> conv1x1_backward(const at::Tensor
     materialize(w);
     dx = empty({B, Cin, H, W}, at::kBFloat16, dev,
                layout == 1 ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous);
+    KernelTimer kt("conv1x1.dgrad", 2.0 * B * H * W * Cin * Cout, stream(dev));
     XDNA_B2(b2_conv1x1_dgrad(dy.data_ptr(), w.data_ptr(), dx.data_ptr(), layout, B, Cin, H * W, Cout, stream(dev)));
     count_launch("conv1x1.dgrad");
   }
@@ -378,6 +380,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> conv1x1_backward(const at::Tensor
     dw = empty({Cout, Cin, 1, 1}, weight.scalar_type(), dev);
     const size_t ws_bytes = b2_conv1x1_wgrad_workspace_bytes(layout, B, Cin, H * W, Cout);
     at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4 + 4}, at::kFloat, dev);
+    KernelTimer kt("conv1x1.wgrad", 2.0 * B * H * W * Cin * Cout, stream(dev));
     XDNA_B2(b2_conv1x1_wgrad(dy.data_ptr(), input.data_ptr(), dw.data_ptr(),
                              weight.scalar_type() == at::kFloat ? B2_F32 : B2_BF16, layout, B, Cin, H * W, Cout,
                              ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
@@ -397,6 +400,7 @@ at::Tensor pack_rows(const at::Tensor& x) {
   const int ch = chunks_of(C);
   at::Tensor rows = empty({int64_t(B) * (H + 2) * (W + 2), int64_t(ch) * 64}, at::kBFloat16, x.device().index());
   materialize(x);
+  KernelTimer kt("pack_rows", 2.0 * B * C * H * W + 2.0 * B * (H + 2) * (W + 2) * ch * 64, stream(x.device().index()));
   XDNA_B2(b2_pack_rows_bf16(x.data_ptr(), x.stride(0), x.stride(1), x.stride(2), x.stride(3), B, C, H, W, ch,
                             rows.data_ptr(), stream(x.device().index())));
   count_launch("pack_rows");
@@ -427,6 +431,7 @@ void launch_wgrad(const at::Tensor& dy_rows, const at::Tensor& x_rows, void* gw,
   const size_t ws_bytes = b2_conv3x3_wgrad_workspace_bytes(B, Cin, H, W, Cout);
   at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
   const int dt = dtype == at::kFloat ? B2_F32 : B2_BF16;
+  KernelTimer kt("conv3x3.wgrad", 18.0 * B * H * W * Cin * Cout, stream(dev));
   XDNA_B2(b2_conv3x3_wgrad(dy_rows.data_ptr(), x_rows.data_ptr(), gw, dt, B, Cin, H, W, Cout, ws.data_ptr(),
                            size_t(ws.numel()) * 4, stream(dev)));
   count_launch("conv3x3.wgrad", 2);  // igemm + split-K reduce
@@ -493,6 +498,7 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
   at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
   if (b.defined()) materialize(b);
   at::Tensor y = empty({B, Cout, H, W}, at::kBFloat16, input.device().index(), out_format(input));
+  KernelTimer kt("conv3x3.fwd", 18.0 * B * H * W * Cin * Cout, stream(input.device().index()));
   XDNA_B2(b2_conv3x3_fwd(rows.data_ptr(), wk.data_ptr(), b.defined() ? b.data_ptr() : nullptr, y.data_ptr(),
                          y.stride(0), y.stride(1), y.stride(2), y.stride(3), B, Cin, H, W, Cout, 0,
                          stream(input.device().index())));
@@ -565,6 +571,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
   if (output_mask[0]) {
     at::Tensor wkd = pack_weight(weight, true);
     dx = empty({B, Cin, H, W}, at::kBFloat16, dev, out_format(input));
+    KernelTimer kt("conv3x3.dgrad", 18.0 * B * H * W * Cin * Cout, stream(dev));
     XDNA_B2(b2_conv3x3_dgrad(dy_rows.data_ptr(), wkd.data_ptr(), dx.data_ptr(), dx.stride(0), dx.stride(1),
                              dx.stride(2), dx.stride(3), B, Cout, H, W, Cin, stream(dev)));
     count_launch("conv3x3.dgrad");

@@ -87,6 +87,7 @@ bool run_gemm(const at::Tensor& A, const at::Tensor& Bm, const at::Tensor& out, 
     beta = 0.f;
   }
   const c10::DeviceIndex dev = out.device().index();
+  KernelTimer kt("gemm", 2.0 * double(M) * double(N) * double(K) * double(batch), stream(dev));
   XDNA_B2(b2_gemm_bf16(a.trans, b.trans, int(M), int(N), int(K), alpha, a.ptr, a.ld, a.bstride, b.ptr, b.ld,
                        b.bstride, beta, cptr, c_dtype, c_sm, c_sn, c_sb, out.data_ptr(), N, M * N, int(batch),
                        stream(dev)));

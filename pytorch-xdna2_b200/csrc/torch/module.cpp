@@ -48,6 +48,83 @@ void reset_stats() {
 }
 
 namespace {
+std::atomic<bool> g_timer_on{false};
+struct TimedLaunch {
+  std::string label;
+  double work;
+  int device;
+  cudaEvent_t start, end;
+};
+std::mutex g_timer_mu;
+std::vector<TimedLaunch> g_timed;
+std::map<int, std::vector<cudaEvent_t>> g_event_pool;  // per device, for reuse
+
+cudaEvent_t timer_event(int device) {
+  {
+    std::lock_guard<std::mutex> lk(g_timer_mu);
+    auto& pool = g_event_pool[device];
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+  }
+  cudaEvent_t e = nullptr;
+  XDNA_CUDA(cudaEventCreate(&e));
+  return e;
+}
+
+bool capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  return cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+}
+}  // namespace
+
+void kernel_timer_enable(bool on) { g_timer_on.store(on); }
+bool kernel_timer_enabled() { return g_timer_on.load(); }
+
+KernelTimer::KernelTimer(const char* label, double work, cudaStream_t stream)
+    : label_(label), work_(work), stream_(stream) {
+  if (!g_timer_on.load(std::memory_order_relaxed) || capturing(stream)) return;
+  int dev = 0;
+  XDNA_CUDA(cudaGetDevice(&dev));
+  start_ = timer_event(dev);
+  XDNA_CUDA(cudaEventRecord(start_, stream_));
+}
+
+KernelTimer::~KernelTimer() {
+  if (!start_) return;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return;
+  cudaEvent_t end = timer_event(dev);
+  if (cudaEventRecord(end, stream_) != cudaSuccess) return;
+  std::lock_guard<std::mutex> lk(g_timer_mu);
+  g_timed.push_back({label_, work_, dev, start_, end});
+}
+
+std::map<std::string, KernelTimerRead> kernel_timer_read() {
+  std::vector<TimedLaunch> recs;
+  {
+    std::lock_guard<std::mutex> lk(g_timer_mu);
+    recs.swap(g_timed);
+  }
+  std::map<std::string, KernelTimerRead> out;
+  for (auto& r : recs) {
+    XDNA_CUDA(cudaEventSynchronize(r.end));
+    float ms = 0.f;
+    XDNA_CUDA(cudaEventElapsedTime(&ms, r.start, r.end));
+    auto& o = out[r.label];
+    o.launches += 1;
+    o.ms += ms;
+    o.work += r.work;
+    std::lock_guard<std::mutex> lk(g_timer_mu);
+    g_event_pool[r.device].push_back(r.start);
+    g_event_pool[r.device].push_back(r.end);
+  }
+  return out;
+}
+
+namespace {
 
 void check_bf16(const at::Tensor& t, const char* what) {
   TORCH_CHECK(t.device().type() == kXdna && t.scalar_type() == at::kBFloat16 && t.is_contiguous(),
@@ -301,6 +378,23 @@ PYBIND11_MODULE(_C, m) {
     return d;
   });
   m.def("launch_stats", [] { return to_dict(launch_stats()); });
+  m.def("kernel_timer_enable", [](bool on) { kernel_timer_enable(on); });
+  m.def("kernel_timer_read", [] {
+    std::map<std::string, KernelTimerRead> r;
+    {
+      py::gil_scoped_release nogil;
+      r = kernel_timer_read();
+    }
+    py::dict d;
+    for (auto& kv : r) {
+      py::dict e;
+      e["launches"] = kv.second.launches;
+      e["ms"] = kv.second.ms;
+      e["work"] = kv.second.work;
+      d[py::str(kv.first)] = e;
+    }
+    return d;
+  });
   m.def("reset_stats", [] { reset_stats(); });
   m.def("set_npu_mode", [](int mode) {
     TORCH_CHECK(mode >= 0 && mode <= 2, "npu mode must be 0, 1 or 2");

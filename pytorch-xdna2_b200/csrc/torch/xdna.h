@@ -123,6 +123,34 @@ extern std::atomic<int> g_mode;
 extern std::atomic<bool> g_conv1x1;
 extern std::atomic<bool> g_conv_general;
 void count_launch(const char* what, int64_t n = 1);
+
+// Per-launch device timing for measurements (the bench's roofline): while
+// enabled, a KernelTimer placed around a launch records a CUDA event before
+// and after it on the launching stream, with the launch's algorithmic work
+// (FLOPs or bytes).  kernel_timer_read() waits for the recorded events and
+// returns, per label, the launches, the summed device milliseconds and the
+// summed work.  Off by default (one atomic load per launch site); launches on
+// a capturing stream are not timed.
+void kernel_timer_enable(bool on);
+bool kernel_timer_enabled();
+struct KernelTimerRead {
+  int64_t launches = 0;
+  double ms = 0, work = 0;
+};
+std::map<std::string, KernelTimerRead> kernel_timer_read();
+class KernelTimer {
+ public:
+  KernelTimer(const char* label, double work, cudaStream_t stream);
+  ~KernelTimer();
+  KernelTimer(const KernelTimer&) = delete;
+  KernelTimer& operator=(const KernelTimer&) = delete;
+
+ private:
+  const char* label_;
+  double work_;
+  cudaStream_t stream_;
+  cudaEvent_t start_ = nullptr;
+};
 void count_fallback(const std::string& op);
 std::map<std::string, int64_t> launch_stats();
 std::map<std::string, int64_t> fallback_stats();

@@ -18,6 +18,8 @@ from .device import (
     is_xrt_backed,
     kernel_library_path,
     kernel_stats,
+    kernel_timer,
+    kernel_times,
     mapped_cpu_stats,
     materialize,
     native_library_path,
@@ -57,6 +59,8 @@ __all__ = [
     "mapped_cpu_stats",
     "reset_mapped_cpu_stats",
     "kernel_stats",
+    "kernel_timer",
+    "kernel_times",
     "native_library_path",
     "kernel_library_path",
     "is_xrt_backed",

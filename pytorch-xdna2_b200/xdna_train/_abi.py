@@ -1,8 +1,8 @@
 """ctypes view of the C ABI in ``include/b2.h`` (``libxdna_b200.so``).
 
 The PyTorch extension calls the library directly from C++; this module is the
-binding a Python host without the extension (or a test) uses, and it is the
-model for the cgo / JNI / N-API stubs in INTEGRATION.md.  Every function takes
+binding a Python host without the extension (or a test) uses, and the model
+for a cgo / JNI / N-API binding of the same library.  Every function takes
 plain integers for device pointers and the CUDA stream.
 """
 from __future__ import annotations

@@ -15,11 +15,21 @@ averages the gradients after every backward:
 * ``synchronize()`` (called by the optimizer pre-hook, or by hand) waits for
   the buckets and writes the averages back into ``p.grad``.
 
+Every backward must be followed by ``synchronize()`` before the next backward
+starts.  To accumulate gradients over several micro-batches, run all but the
+last backward inside ``with ar.no_sync():`` (the hooks then leave the buckets
+alone and the gradients accumulate in ``p.grad``); the last backward fills the
+buckets from the accumulated ``p.grad``.  A hook that fires for a bucket whose
+all-reduce is still in flight raises instead of overwriting the buffer NCCL is
+reading.
+
 Collectives run through ``torch.distributed``: NCCL on NVLink/NVSwitch for xdna
 tensors (handed over as zero-copy CUDA aliases, so NCCL reads and writes the
 xdna memory in place), gloo for CPU tensors (the CPU tests).
 """
 from __future__ import annotations
+
+import contextlib
 
 import torch
 import torch.distributed as dist
@@ -65,14 +75,33 @@ class GradAllReduce:
             self.buckets.append({"params": ps, "flat": flat, "ready": 0, "work": None})
         self._hooks = []
         self.overlap = overlap
+        self._hooks_on = True
         if overlap:
             for p in params:
                 self._hooks.append(p.register_post_accumulate_grad_hook(self._on_grad))
 
     # -- overlap path --------------------------------------------------------
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside this context only accumulate into ``p.grad``;
+        the next backward outside it launches the all-reduces."""
+        prev = self._hooks_on
+        self._hooks_on = False
+        try:
+            yield
+        finally:
+            self._hooks_on = prev
+
     def _on_grad(self, p: torch.Tensor) -> None:
+        if not self._hooks_on:
+            return
         bi, off = self._slot[p]
         b = self.buckets[bi]
+        if b["work"] is not None:
+            raise RuntimeError(
+                "GradAllReduce: a gradient arrived for a bucket whose all-reduce is still in flight; call "
+                "synchronize() after every backward, or run the earlier backward passes of an accumulation "
+                "inside no_sync()")
         b["flat"][off:off + p.numel()].copy_(p.grad.reshape(-1))
         b["ready"] += 1
         if b["ready"] == len(b["params"]):

@@ -291,6 +291,21 @@ def kernel_stats() -> dict[str, int]:
     return dict(_C.launch_stats())
 
 
+def kernel_timer(on: bool = True) -> None:
+    """Turn per-launch device timing on or off: while on, the timed launch
+    sites (3x3 / 1x1 convolutions, GEMMs) record a CUDA event pair around each
+    launch on its stream, with the launch's algorithmic FLOPs."""
+    register_xdna_device()
+    _C.kernel_timer_enable(bool(on))
+
+
+def kernel_times() -> dict[str, dict[str, float]]:
+    """Per label: launches, summed device milliseconds and summed algorithmic
+    work (FLOPs) of the launches timed since the last read (waits for them)."""
+    register_xdna_device()
+    return {str(k): dict(v) for k, v in dict(_C.kernel_timer_read()).items()}
+
+
 def reset_mapped_cpu_stats() -> None:
     register_xdna_device()
     _C.reset_stats()

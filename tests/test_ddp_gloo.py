@@ -2,6 +2,10 @@
 world_size-2 gloo process groups on the CPU, plus a rank-failure case made on
 the host (a rank that raises before joining the collective): the survivor's
 collective ends with an error within the process-group timeout, nothing hangs.
+Gradient accumulation: two backward passes, the first inside no_sync(), give
+the average of the accumulated gradients; two backward passes without
+synchronize() between them raise instead of overwriting a bucket whose
+all-reduce is in flight.
 """
 import os
 import socket
@@ -33,11 +37,19 @@ def _worker(rank, world, port, mode, q):
     try:
         torch.manual_seed(0)
         model = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.ReLU(), torch.nn.Linear(16, 4))
-        ar = GradAllReduce(model, bucket_cap_mb=0.0001, overlap=(mode == "overlap"))
+        ar = GradAllReduce(model, bucket_cap_mb=0.0001, overlap=(mode != "after"))
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected rank failure before the collective")
         x = torch.randn(5, 8, generator=torch.Generator().manual_seed(100 + rank))
-        model(x).square().sum().backward()
+        if mode == "accumulate":
+            with ar.no_sync():
+                model(x).square().sum().backward()
+            model(x * 0.5).square().sum().backward()
+        elif mode == "double":
+            model(x).square().sum().backward()
+            model(x).square().sum().backward()  # no synchronize() between: must raise
+        else:
+            model(x).square().sum().backward()
         local = [p.grad.clone() for p in model.parameters()]
         ar.synchronize()
         q.put((rank, "ok", [p.grad.clone() for p in model.parameters()], local, len(ar.buckets)))
@@ -68,7 +80,7 @@ def _run(mode):
     return out
 
 
-@pytest.mark.parametrize("mode", ["overlap", "after"])
+@pytest.mark.parametrize("mode", ["overlap", "after", "accumulate"])
 def test_grads_are_averaged(mode):
     out = _run(mode)
     assert out[0][1] == "ok" and out[1][1] == "ok"
@@ -84,3 +96,9 @@ def test_rank_failure_surfaces_as_error():
     out = _run("fail")
     assert out[1][1] == "error" and "injected" in out[1][2]
     assert out[0][1] == "error"  # the survivor's collective failed instead of hanging
+
+
+def test_second_backward_before_synchronize_raises():
+    out = _run("double")
+    for r in (0, 1):
+        assert out[r][1] == "error" and "in flight" in out[r][2]

@@ -42,8 +42,12 @@ def _close(got, ref, tol=2e-2, l2=5e-3):
     assert ((got - ref).norm() / ref.norm().clamp_min(1e-30)).item() <= l2
 
 
-# (B, Cin, H, W, Cout); the 512x512 case needs fewer splits than the usual plan
-SHAPES = [(4, 128, 18, 18, 128), (1, 512, 8, 8, 512), (2, 64, 9, 13, 96)]
+# (B, Cin, H, W, Cout).  The usual split-K plan of the fourth shape (2048 padded
+# rows = 32 k-blocks, 72 tiles of 148 SMs -> 2 splits) needs 2 * 9 * 512 * 512 *
+# 4 B = 18.9 MB of partial sums, more than the 16 MiB array: the call cuts it to
+# one split.  The others keep the usual plan (one split each for the first
+# three, which all fit).
+SHAPES = [(4, 128, 18, 18, 128), (1, 512, 8, 8, 512), (2, 64, 9, 13, 96), (8, 512, 14, 14, 512)]
 
 
 def test_noalloc_wgrad_matches_workspace_entry_point_on_consecutive_calls(cuda):
