@@ -215,6 +215,35 @@ typedef struct b2_adam_hparams {
 b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n,
                         const b2_adam_hparams* hp, void* stream);
 
+/* ---- multi-tensor fused SGD ------------------------------------------- */
+
+/* One parameter tensor of a fused SGD step (device pointers; host struct). */
+typedef struct b2_sgd_tensor {
+  void* param;            /* param_dtype */
+  void* grad;             /* param_dtype; rewritten unscaled when grad_scale is set */
+  void* momentum_buffer;  /* param_dtype; may be NULL when momentum == 0 */
+  int64_t numel;
+} b2_sgd_tensor;
+
+typedef struct b2_sgd_hparams {
+  double lr, weight_decay, momentum, dampening;
+  int nesterov, maximize, is_first_step; /* first step: the buffer becomes the gradient */
+  int param_dtype;        /* B2_BF16 or B2_F32 */
+  const float* lr_tensor; /* device fp32 scalar overriding lr, or NULL */
+  const float* grad_scale;/* device fp32 scalar, or NULL */
+  const float* found_inf; /* device fp32 scalar, or NULL (nonzero skips) */
+} b2_sgd_hparams;
+
+/* In-place fused SGD over n tensors in one pass per element, fp32 operands
+ * with the hyper-parameters in double (PyTorch's fused-SGD arithmetic):
+ * g = grad [/ grad_scale] [negated if maximize] [+ wd * p]; with momentum
+ * buf = first ? g : momentum * buf + (1 - dampening) * g and g = nesterov ?
+ * g + momentum * buf : buf; p -= lr * g.  Replaces the reference's CPU
+ * _fused_sgd_ reached through the boxed fallback and _prefer_fused_optimizer
+ * (torch_xdna_device.cpp:5124-5260, xdna_train/device.py:408-436). */
+b2_status b2_fused_sgd(const b2_sgd_tensor* tensors, int n,
+                       const b2_sgd_hparams* hp, void* stream);
+
 /* ---- fused region kernels (replace xdna_train/_native/region_kernels.cpp) */
 
 /* *out (device double) = sum (a[i]-b[i])^2 over n bf16 elements.

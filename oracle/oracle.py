@@ -205,6 +205,37 @@ def adam_f32(p, g, m, v, vmax, step, lr, beta1, beta2, wd, eps, amsgrad=False, m
                              int(maximize), int(adamw))
 
 
+def sgd_step(p, g, buf, lr, weight_decay=0.0, momentum=0.0, dampening=0.0, nesterov=False, maximize=False,
+             first_step=False, grad_scale=None, bf16=False):
+    """One fused-SGD step, the update torch.optim.SGD(fused=True) issues as
+    aten::_fused_sgd_ (the op the reference's _prefer_fused_optimizer selects,
+    xdna_train/device.py:408-436, and runs on its CPU through the boxed
+    fallback, torch_xdna_device.cpp:5124-5260), restated in numpy: fp32
+    operands, hyper-parameters in double, each intermediate rounded where the
+    fused definition stores it.  Arrays hold float32 values, or bf16 bit
+    patterns (np.uint16) with ``bf16``; returns new (p, g, buf) in the same
+    form (g changes only with ``grad_scale``; buf is None without momentum)."""
+    dec = (lambda a: bf16_value(a)) if bf16 else (lambda a: np.asarray(a, dtype=np.float32))
+    enc = (lambda a: bf16_bits(a.astype(np.float32))) if bf16 else (lambda a: a.astype(np.float32))
+    pf, gf = dec(p), dec(g)
+    if grad_scale is not None:
+        gf = (gf.astype(np.float64) / np.float64(np.float32(grad_scale))).astype(np.float32)
+    g_out = enc(gf) if grad_scale is not None else g
+    gg = -gf if maximize else gf
+    if weight_decay != 0.0:
+        gg = (gg.astype(np.float64) + weight_decay * pf.astype(np.float64)).astype(np.float32)
+    b_out = None
+    if momentum != 0.0:
+        if first_step:
+            bd = gg.astype(np.float64)
+        else:
+            bd = momentum * dec(buf).astype(np.float64) + (1.0 - dampening) * gg.astype(np.float64)
+        b_out = enc(bd.astype(np.float32))
+        gg = (gg.astype(np.float64) + momentum * bd).astype(np.float32) if nesterov else bd.astype(np.float32)
+    pn = (pf.astype(np.float64) - lr * gg.astype(np.float64)).astype(np.float32)
+    return enc(pn), g_out, b_out
+
+
 # ---- training BatchNorm2d + activation (region_kernels.cpp:309-460) ----------
 
 def _bn_call(fn, x, w, b, rm, rv, eps, slope, factor, update, extra=()):

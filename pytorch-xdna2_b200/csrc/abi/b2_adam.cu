@@ -2,9 +2,9 @@
 // exp_avg, exp_avg_sq (and max_exp_avg_sq), write param and the moments, all
 // arithmetic in fp32.  Tensor metadata travels in the kernel parameter block
 // (no device allocation); a launch covers up to kMaxTensors tensors, split into
-// kChunk-element chunks that a grid of at most 4 CTAs per SM walks with a
-// grid stride (each thread updates 4 consecutive elements per step, with
-// vector loads when the tensor's arrays are aligned).
+// kChunk-element chunks that one wave of resident CTAs walks with a grid
+// stride (each thread updates two 8-element vectors per step, with 16-byte
+// loads when the tensor's arrays are aligned).
 //
 // The update follows PyTorch's Adam/AdamW definition that the reference's
 // `_fused_adam_` CPU path runs (reached through the boxed fallback,
@@ -69,34 +69,39 @@ __device__ __forceinline__ void st(void* p, long long i, float v) {
   else
     static_cast<float*>(p)[i] = v;
 }
-// 8 consecutive elements (i % 8 == 0, arrays 16-byte aligned): one 16-byte
-// access for bf16, two for fp32.
+// 8 consecutive elements (i % 8 == 0, arrays 16-byte aligned) kept as raw
+// 16-byte words until used: one word for bf16, two for fp32.
 template <typename T>
-__device__ __forceinline__ void ld8(const void* p, long long i, float (&o)[8]) {
-  if constexpr (sizeof(T) == 2) {
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+struct Raw8 {
+  uint4 w[sizeof(T) == 2 ? 1 : 2];
+};
+template <typename T>
+__device__ __forceinline__ void ld8(const void* p, long long i, Raw8<T>& r) {
+  const uint4* q = reinterpret_cast<const uint4*>(static_cast<const T*>(p) + i);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      o[2 * k] = __uint_as_float(w[k] << 16);
-      o[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
-    }
-  } else {
-    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
-    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i + 4);
-    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
-    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
-  }
+  for (int k = 0; k < int(sizeof(T)) / 2; ++k) r.w[k] = q[k];
 }
+template <typename T>
+__device__ __forceinline__ float elem(const Raw8<T>& r, int e) {
+  const uint32_t* u = reinterpret_cast<const uint32_t*>(r.w);
+  if constexpr (sizeof(T) == 2)
+    return __uint_as_float((e & 1) ? (u[e >> 1] & 0xffff0000u) : (u[e >> 1] << 16));
+  else
+    return __uint_as_float(u[e]);
+}
+// Stores 8 values; bf16 through the hardware round-to-nearest-even pair
+// conversion (cvt.rn.bf16x2.f32: the same result as f2bf for every non-NaN
+// value, one instruction per pair).
 template <typename T>
 __device__ __forceinline__ void st8(void* p, long long i, const float (&v)[8]) {
   if constexpr (sizeof(T) == 2) {
-    uint4 u;
-    u.x = uint32_t(f2bf(v[0])) | (uint32_t(f2bf(v[1])) << 16);
-    u.y = uint32_t(f2bf(v[2])) | (uint32_t(f2bf(v[3])) << 16);
-    u.z = uint32_t(f2bf(v[4])) | (uint32_t(f2bf(v[5])) << 16);
-    u.w = uint32_t(f2bf(v[6])) | (uint32_t(f2bf(v[7])) << 16);
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = u;
+    uint32_t u[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+      u[k] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p) + i) = make_uint4(u[0], u[1], u[2], u[3]);
   } else {
     *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4*>(static_cast<float*>(p) + i + 4) = make_float4(v[4], v[5], v[6], v[7]);
@@ -125,7 +130,18 @@ __device__ __forceinline__ void update(const AdamScalars& s, const Coef& c, floa
 }
 
 template <typename P, typename S>
-__global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ AdamArgs a, const AdamScalars s) {
+__device__ __forceinline__ void scalar_update(const AdamScalars& s, const Coef& c, void* P_, const void* G_, void* M_,
+                                              void* V_, void* X_, long long j) {
+  float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
+  update(s, c, ld<P>(G_, j), p, m, v, x);
+  st<P>(P_, j, p);
+  st<S>(M_, j, m);
+  st<S>(V_, j, v);
+  if (s.amsgrad) st<S>(X_, j, x);
+}
+
+template <typename P, typename S>
+__global__ void __launch_bounds__(kThreads, 3) adam_kernel(const __grid_constant__ AdamArgs a, const AdamScalars s) {
   if (s.found_inf && *s.found_inf != 0.f) return;
   __shared__ Coef sc;
   const int total = a.chunk_begin[a.ntensors];
@@ -162,40 +178,52 @@ __global__ void __launch_bounds__(kThreads) adam_kernel(const __grid_constant__ 
     void* V_ = a.v[t];
     void* X_ = a.vmax[t];
     if (a.vec[t]) {
-      for (long long i = begin + 8 * threadIdx.x; i < end; i += 8 * kThreads) {
-        if (i + 8 <= end) {
-          float g[8], p[8], m[8], v[8], x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          ld8<P>(G_, i, g);
-          ld8<P>(P_, i, p);
-          ld8<S>(M_, i, m);
-          ld8<S>(V_, i, v);
-          if (s.amsgrad) ld8<S>(X_, i, x);
+      // two 8-element vectors per thread, all their loads issued before the
+      // math, so a warp keeps 8-10 independent 16-byte loads in flight while
+      // the correctly rounded divisions and square roots of the update run
+      for (long long i0 = begin + 8 * threadIdx.x; i0 < end; i0 += 16 * kThreads) {
+        const long long i1 = i0 + 8 * kThreads;
+        if (i0 + 8 > end || (i1 < end && i1 + 8 > end)) {  // ragged tail of the tensor
+          for (long long j = i0; j < end && j < i0 + 8; ++j) scalar_update<P, S>(s, c, P_, G_, M_, V_, X_, j);
+          for (long long j = i1; j < end && j < i1 + 8; ++j) scalar_update<P, S>(s, c, P_, G_, M_, V_, X_, j);
+          continue;
+        }
+        const int nv = i1 < end ? 2 : 1;
+        Raw8<P> rg[2], rp[2];
+        Raw8<S> rm[2], rv[2], rx[2];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) update(s, c, g[k], p[k], m[k], v[k], x[k]);
-          st8<P>(P_, i, p);
-          st8<S>(M_, i, m);
-          st8<S>(V_, i, v);
-          if (s.amsgrad) st8<S>(X_, i, x);
-        } else {
-          for (long long j = i; j < end; ++j) {
-            float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
-            update(s, c, ld<P>(G_, j), p, m, v, x);
-            st<P>(P_, j, p);
-            st<S>(M_, j, m);
-            st<S>(V_, j, v);
-            if (s.amsgrad) st<S>(X_, j, x);
+        for (int k = 0; k < 2; ++k) {
+          if (k < nv) {
+            const long long i = k ? i1 : i0;
+            ld8<P>(G_, i, rg[k]);
+            ld8<P>(P_, i, rp[k]);
+            ld8<S>(M_, i, rm[k]);
+            ld8<S>(V_, i, rv[k]);
+            if (s.amsgrad) ld8<S>(X_, i, rx[k]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (k < nv) {
+            const long long i = k ? i1 : i0;
+            float p[8], m[8], v[8], x[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              p[e] = elem<P>(rp[k], e);
+              m[e] = elem<S>(rm[k], e);
+              v[e] = elem<S>(rv[k], e);
+              x[e] = s.amsgrad ? elem<S>(rx[k], e) : 0.f;
+              update(s, c, elem<P>(rg[k], e), p[e], m[e], v[e], x[e]);
+            }
+            st8<P>(P_, i, p);
+            st8<S>(M_, i, m);
+            st8<S>(V_, i, v);
+            if (s.amsgrad) st8<S>(X_, i, x);
           }
         }
       }
     } else {
-      for (long long j = begin + threadIdx.x; j < end; j += kThreads) {
-        float p = ld<P>(P_, j), m = ld<S>(M_, j), v = ld<S>(V_, j), x = s.amsgrad ? ld<S>(X_, j) : 0.f;
-        update(s, c, ld<P>(G_, j), p, m, v, x);
-        st<P>(P_, j, p);
-        st<S>(M_, j, m);
-        st<S>(V_, j, v);
-        if (s.amsgrad) st<S>(X_, j, x);
-      }
+      for (long long j = begin + threadIdx.x; j < end; j += kThreads) scalar_update<P, S>(s, c, P_, G_, M_, V_, X_, j);
     }
   }
 }
@@ -230,7 +258,16 @@ extern "C" b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n, const b
   const int psz = hp->param_dtype == B2_F32 ? 4 : 2, ssz = hp->state_dtype == B2_F32 ? 4 : 2;
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  const int max_grid = 4 * sm_count(dev);
+  // one wave of resident blocks (occupancy of this instantiation, per device)
+  static int occ[64][4] = {};
+  if (dev < 0 || dev >= 64) return set_error(B2_ERR_INVALID, "device index %d", dev);
+  int& o = occ[dev][(hp->param_dtype == B2_F32 ? 2 : 0) + (hp->state_dtype == B2_F32 ? 1 : 0)];
+  if (!o) {
+    int b = 0;
+    B2_TRY(check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kern, kThreads, 0), "occupancy"));
+    o = std::max(1, b);
+  }
+  const int max_grid = o * sm_count(dev);
   AdamArgs args;
   args.ntensors = 0;
   args.chunk_begin[0] = 0;

@@ -29,6 +29,16 @@ class AdamHparams(C.Structure):
                 ("state_dtype", i32), ("lr_tensor", vp), ("grad_scale", vp), ("found_inf", vp)]
 
 
+class SgdTensor(C.Structure):
+    _fields_ = [("param", vp), ("grad", vp), ("momentum_buffer", vp), ("numel", i64)]
+
+
+class SgdHparams(C.Structure):
+    _fields_ = [("lr", f64), ("weight_decay", f64), ("momentum", f64), ("dampening", f64),
+                ("nesterov", i32), ("maximize", i32), ("is_first_step", i32), ("param_dtype", i32),
+                ("lr_tensor", vp), ("grad_scale", vp), ("found_inf", vp)]
+
+
 # name -> argument types (restype is int unless listed in _RESTYPES)
 SIGNATURES = {
     "b2_last_error": [],
@@ -50,6 +60,7 @@ SIGNATURES = {
     "b2_gemm_bf16": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
                      i64, i64, i64, vp, i64, i64, i32, vp],
     "b2_fused_adam": [C.POINTER(AdamTensor), i32, C.POINTER(AdamHparams), vp],
+    "b2_fused_sgd": [C.POINTER(SgdTensor), i32, C.POINTER(SgdHparams), vp],
     "b2_region_sqdiff_sum_bf16": [vp, vp, i64, vp, vp],
     "b2_region_relu_bf16": [vp, vp, i64, vp],
     "b2_region_relu_maxpool2_bf16": [vp, vp, vp, i64, i64, i64, vp],

@@ -168,3 +168,36 @@ def test_bn_norm_activation_matches_reference(bn):
         _bf_close(dx, bn[f"c{i}_dx"], 1e-5 * np.abs(oracle.bf16_value(bn[f"c{i}_dx"])).max())
         _bf_close(dw, bn[f"c{i}_dw"], 2e-6 * N * H * W, exact=0.9)
         _bf_close(db, bn[f"c{i}_db"], 2e-6 * N * H * W, exact=0.9)
+
+
+@pytest.mark.parametrize("opts", [dict(momentum=0.9), dict(momentum=0.9, weight_decay=1e-4, nesterov=True),
+                                  dict(momentum=0.8, dampening=0.1, maximize=True), dict(weight_decay=1e-2)])
+def test_oracle_sgd_matches_reference_cpu_fused_sgd_fp32(opts):
+    """The oracle's fused-SGD restatement against the reference's CPU path
+    for fp32 parameters (torch's CPU _fused_sgd_, reached by the reference
+    through its boxed fallback): within a few fp32 rounding steps of the
+    operands' magnitude (the CPU kernel forms its products in fp32, the
+    definition here in double; under cancellation the fp32 rounding of a
+    product shows at the product's scale).  torch 2.11's CPU _fused_sgd_ leaves
+    most bf16 parameters unchanged, so bf16 is pinned on the GPU against
+    ATen's CUDA kernel instead (tests/test_gpu_sgd.py)."""
+    g = torch.Generator().manual_seed(5)
+    p = torch.randn(4099, generator=g)
+    gr = torch.randn(4099, generator=g)
+    b = torch.randn(4099, generator=g)
+    has_buf = opts.get("momentum", 0.0) != 0.0
+    p0, g0, b0 = p.numpy().copy(), gr.numpy().copy(), b.numpy().copy()
+    want_p, _, want_b = oracle.sgd_step(p.numpy().copy(), gr.numpy().copy(), b.numpy().copy() if has_buf else None,
+                                        0.1, opts.get("weight_decay", 0.0), opts.get("momentum", 0.0),
+                                        opts.get("dampening", 0.0), opts.get("nesterov", False),
+                                        opts.get("maximize", False), False)
+    torch._fused_sgd_([p], [gr], [b] if has_buf else [], weight_decay=opts.get("weight_decay", 0.0),
+                      momentum=opts.get("momentum", 0.0), lr=0.1, dampening=opts.get("dampening", 0.0),
+                      nesterov=opts.get("nesterov", False), maximize=opts.get("maximize", False), is_first_step=False)
+    # magnitudes of the operands each result is formed from: cancellation
+    # leaves the fp32 roundings of the products at that scale
+    mb = opts.get("momentum", 0.0) * np.abs(b0) + np.abs(g0) + opts.get("weight_decay", 0.0) * np.abs(p0)
+    mp = np.abs(p0) + 0.1 * (mb if has_buf else np.abs(g0) + opts.get("weight_decay", 0.0) * np.abs(p0))
+    assert np.all(np.abs(p.numpy() - want_p) <= 4 * np.spacing(mp.astype(np.float32)))
+    if has_buf:
+        assert np.all(np.abs(b.numpy() - want_b) <= 4 * np.spacing(mb.astype(np.float32)))
