@@ -185,8 +185,11 @@ def run_conv_layer(args):
     conv = nn.Conv2d(C, C, 3, padding=1).bfloat16().to(X)
     opt = torch.optim.Adam(conv.parameters(), lr=1e-3)
     g = torch.Generator().manual_seed(1 + rank)
-    x_host = torch.randn(B_PER_GPU, C, HW, HW, generator=g).bfloat16().pin_memory()
-    dy_host = torch.randn(B_PER_GPU, C, HW, HW, generator=g).bfloat16().pin_memory()
+    mf = torch.channels_last if args.channels_last else torch.contiguous_format
+    if args.channels_last:
+        conv = conv.to(memory_format=mf)
+    x_host = torch.randn(B_PER_GPU, C, HW, HW, generator=g).bfloat16().contiguous(memory_format=mf).pin_memory()
+    dy_host = torch.randn(B_PER_GPU, C, HW, HW, generator=g).bfloat16().contiguous(memory_format=mf).pin_memory()
     x = x_host.to(X)
     dy = dy_host.to(X)
 
@@ -245,8 +248,8 @@ def run_conv_layer(args):
     # copy of step k+1 runs on a copy stream while step k computes (what a
     # prefetching data loader does); every step still copies its own inputs.
     copy_s = torch.cuda.Stream()
-    bx = [torch.empty(x_host.shape, dtype=x_host.dtype, device=X) for _ in range(2)]
-    bd = [torch.empty(dy_host.shape, dtype=dy_host.dtype, device=X) for _ in range(2)]
+    bx = [torch.empty_like(x) for _ in range(2)]
+    bd = [torch.empty_like(dy) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
 
@@ -276,15 +279,24 @@ def run_conv_layer(args):
     torch.cuda.synchronize()
     e2e_ms = allreduce_max(e2.elapsed_time(e3) / args.steps, world)
 
+    # ---- the step's own launches timed in place (event pairs on their stream)
+    xdna_train.kernel_timer(True)
+    for _ in range(3):
+        step(x.detach(), dy)
+    torch.cuda.synchronize()
+    xdna_train.kernel_timer(False)
+    in_step = {k: round(v["ms"] / 3, 4) for k, v in xdna_train.kernel_times().items()}
+
     # ---- per-kernel device time of the conv directions (CUDA events on the
     # launching stream, same operands), for the roofline
-    kt = kernel_times(x, dy, conv, local)
+    kt = kernel_times(x.contiguous(), dy.contiguous(), conv, local, nhwc=args.channels_last)
+    sfx = "_nhwc" if args.channels_last else ""
 
     if rank != 0:
         return None
     bf16_peak, _, peak_kind = peaks()
     flops_dir = conv_flops(B_PER_GPU)
-    achieved = 3 * flops_dir / ((kt["fwd"] + kt["dgrad"] + kt["wgrad"]) * 1e-3) / 1e12
+    achieved = 3 * flops_dir / ((kt["fwd" + sfx] + kt["dgrad" + sfx] + kt["wgrad" + sfx]) * 1e-3) / 1e12
     images = B_PER_GPU * world
     line = {
         "metric": METRIC,
@@ -300,7 +312,8 @@ def run_conv_layer(args):
         "dtype": "bf16",
         "data": "synthetic (x, dY ~ N(0,1); random-init Conv2d weights)",
         "config": {"workload": f"conv3x3 train step: Conv2d({C},{C},3,pad=1,bias) on B{B_PER_GPU}x{C}x{HW}x{HW} "
-                               "per GPU (BASELINE configs[1] sweep point), fwd+dgrad+wgrad+Adam",
+                               "per GPU (BASELINE configs[1] sweep point), fwd+dgrad+wgrad+Adam"
+                               + (", channels-last activations" if args.channels_last else ", NCHW activations"),
                    "global_batch": images, "per_gpu_batch": B_PER_GPU, "channels": C, "hw": HW,
                    "parallelism": f"dp{world}", "l2": "inputs larger than L2 (340 MB activations per tensor)"},
         "e2e": {"value": round(images / (e2e_ms * 1e-3), 2), "unit": "images/s",
@@ -313,15 +326,17 @@ def run_conv_layer(args):
                      "per_launch_ms": {k: round(v, 4) for k, v in kt.items()},
                      "flops_per_launch": flops_dir, "peak_kind": peak_kind},
         "gpu_launches": launches,
+        "kernel_ms_per_step": in_step,
         "clocks": clk.summary(),
         "fallback_ops": {k: v["calls"] for k, v in fallbacks.items()},
     }
     return line
 
 
-def kernel_times(x, dy, conv, local, iters=10):
+def kernel_times(x, dy, conv, local, iters=10, nhwc=False):
     """Average device time per launch of the fwd / dgrad / wgrad kernels, each
-    timed alone with CUDA events on the stream they run on."""
+    timed alone with CUDA events on the stream they run on (``nhwc``: also
+    the channels-last in-place entry points)."""
     import ctypes
 
     from xdna_train import _abi
@@ -332,7 +347,7 @@ def kernel_times(x, dy, conv, local, iters=10):
     ch = (C + 63) // 64
     rows = torch.empty(B * (HW + 2) * (HW + 2), ch * 64, dtype=torch.bfloat16, device=X)
     drows = torch.empty_like(rows)
-    w = conv.weight.detach()
+    w = conv.weight.detach().contiguous()
     wk = torch.empty(C, ch * 576, dtype=torch.bfloat16, device=X)
     wkd = torch.empty_like(wk)
     y = torch.empty_like(x)
@@ -353,6 +368,24 @@ def kernel_times(x, dy, conv, local, iters=10):
                                             ws.data_ptr(), wsb, st),
         "pack_rows": lambda: L.b2_pack_rows_bf16(x.data_ptr(), *x.stride(), B, C, HW, HW, ch, rows.data_ptr(), st),
     }
+    if nhwc:
+        # the same three directions reading channels-last x / dY in place
+        xc = x.contiguous(memory_format=torch.channels_last)
+        dyc = dy.contiguous(memory_format=torch.channels_last)
+        yc = torch.empty_like(xc)
+        dxc = torch.empty_like(xc)
+        fns.update({
+            "fwd_nhwc": lambda: L.b2_conv3x3_fwd_nhwc(xc.data_ptr(), xc.stride(0), xc.stride(2), xc.stride(3),
+                                                      wk.data_ptr(), conv.bias.data_ptr(), yc.data_ptr(),
+                                                      *yc.stride(), B, C, HW, HW, C, 0, st),
+            "dgrad_nhwc": lambda: L.b2_conv3x3_dgrad_nhwc(dyc.data_ptr(), dyc.stride(0), dyc.stride(2),
+                                                          dyc.stride(3), wkd.data_ptr(), dxc.data_ptr(),
+                                                          *dxc.stride(), B, C, HW, HW, C, st),
+            "wgrad_nhwc": lambda: L.b2_conv3x3_wgrad_nhwc(dyc.data_ptr(), dyc.stride(0), dyc.stride(2),
+                                                          dyc.stride(3), xc.data_ptr(), xc.stride(0), xc.stride(2),
+                                                          xc.stride(3), dw.data_ptr(), 0, B, C, HW, HW, C,
+                                                          ws.data_ptr(), wsb, st),
+        })
     out = {}
     for name, fn in fns.items():
         for _ in range(2):
@@ -1108,11 +1141,12 @@ def kernel_probe(args):
     conv = nn.Conv2d(c, c, 3, padding=1).bfloat16().to(X)
     x = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
     dy = torch.randn(b, c, hw, hw, dtype=torch.bfloat16, device=X)
-    kt = kernel_times(x, dy, conv, 0, iters=args.iters)
+    kt = kernel_times(x, dy, conv, 0, iters=args.iters, nhwc=args.channels % 8 == 0)
     fl = 2.0 * b * hw * hw * c * c * 9
     out = {k: {"ms": round(v, 4)} for k, v in kt.items()}
-    for k in ("fwd", "dgrad", "wgrad"):
-        out[k]["tflops"] = round(fl / (kt[k] * 1e-3) / 1e12, 1)
+    for k in kt:
+        if k != "pack_rows":
+            out[k]["tflops"] = round(fl / (kt[k] * 1e-3) / 1e12, 1)
     out["pack_rows"]["gbs"] = round(2 * (x.numel() + b * (hw + 2) ** 2 * ((c + 63) // 64) * 64) / (kt["pack_rows"] * 1e-3) / 1e9, 1)
     print(json.dumps({"probe": f"B{b} C{c} HW{hw}", **out}), flush=True)
 
@@ -1409,6 +1443,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (resnet50: 20, others: 5)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--channels-last", action="store_true", help="--workload conv: channels-last activations")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 100 if args.workload == "resnet50" else 200

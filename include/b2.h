@@ -91,6 +91,19 @@ b2_status b2_pack_rows_dbias_bf16(const void* x, int64_t sn, int64_t sc,
                                   int dbias_dtype, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* dbias of a channels-last dY read in place (the conv bias gradient when no
+ * padded-row copy of dY is made): out[c] = sum over (b, y, x) of
+ * x[b][y][x][c] (pixels dense: sh == W*sw, sn == H*sh, sw >= C), fp32 sums
+ * over fixed 64-pixel groups added in group order (deterministic), rounded
+ * once to out_dtype (B2_BF16 or B2_F32).  Workspace:
+ * b2_channel_sum_nhwc_workspace_bytes().  Replaces the reference's CPU dbias
+ * (mask[2] of convolution_backward, torch_xdna_device.cpp:4828-4878). */
+size_t b2_channel_sum_nhwc_workspace_bytes(int B, int C, int H, int W);
+b2_status b2_channel_sum_nhwc_bf16(const void* x, int64_t sn, int64_t sh,
+                                   int64_t sw, int B, int C, int H, int W,
+                                   void* out, int out_dtype, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* OIHW bf16 weight [Cout][Cin][3][3] -> Wk[Cout][chunks*9*64], K order
  * (chunk, dy, dx, c), zero for c >= Cin.  chunks >= ceil(Cin/64).
  * Replaces the K ordering of xdna_conv3x3w_pack_weights_bfp16
@@ -147,6 +160,33 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw,
                            int dw_dtype, int B, int Cin, int H, int W, int Cout,
                            void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* The three directions with channels-last activations read in place: x / dy
+ * are bf16 [B][H][W][C] views with channel stride 1 and element strides
+ * (sn, sh, sw), C and the strides multiples of 8, 16-byte aligned base.  The
+ * kernels fetch them through an im2col TMA map whose pixel box is the
+ * zero-padded grid, so they read exactly the rows b2_pack_rows_bf16 would
+ * have written, without that pass over the activation (same results, bit for
+ * bit).  Weights and outputs as in the padded-row entry points; wgrad's
+ * workspace size is b2_conv3x3_wgrad_workspace_bytes.  Replace the same
+ * reference functions as b2_conv3x3_fwd / _dgrad / _wgrad together with its
+ * channels-last strip packer (conv_pack.cpp:632-700). */
+b2_status b2_conv3x3_fwd_nhwc(const void* x, int64_t xsn, int64_t xsh,
+                              int64_t xsw, const void* wk, const void* bias,
+                              void* y, int64_t ysn, int64_t ysc, int64_t ysh,
+                              int64_t ysw, int B, int Cin, int H, int W,
+                              int Cout, int relu, void* stream);
+b2_status b2_conv3x3_dgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh,
+                                int64_t dsw, const void* wk_dgrad, void* dx,
+                                int64_t sn, int64_t sc, int64_t sh, int64_t sw,
+                                int B, int Cout, int H, int W, int Cin,
+                                void* stream);
+b2_status b2_conv3x3_wgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh,
+                                int64_t dsw, const void* x, int64_t xsn,
+                                int64_t xsh, int64_t xsw, void* dw,
+                                int dw_dtype, int B, int Cin, int H, int W,
+                                int Cout, void* workspace,
+                                size_t workspace_bytes, void* stream);
 
 /* Weight gradient that allocates nothing (no counterpart in the reference).
  * Same result as b2_conv3x3_wgrad, but the split-K partial sums live in one

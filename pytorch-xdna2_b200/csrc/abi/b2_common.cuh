@@ -25,6 +25,16 @@ b2_status encode_tmap(CUtensorMap* map, const void* base, int rank,
 // Same, with the shared-memory swizzle given in bytes (0, 64 or 128).
 b2_status encode_tmap_sw(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, int swizzle_bytes);
+// Encodes an im2col TMA descriptor over a channels-last bf16 activation
+// [B][H][W][C] (element strides sn, sh, sw; channel stride 1) whose pixel
+// box is the zero-padded grid: traversal runs over h in [-1, H] and w in
+// [-1, W] of each image in turn, so `box_rows` consecutive "pixels" from a
+// start (w, h, n) are exactly the padded-grid rows of b2_pack_rows_bf16,
+// padding positions and channels >= C filled with zeros.  64 channels per
+// pixel, 128-byte swizzle (the same shared-memory image as a tiled load of
+// the packed rows).
+b2_status encode_tmap_padded_nhwc(CUtensorMap* map, const void* base, int B, int C, int H, int W, int64_t sn,
+                                  int64_t sh, int64_t sw, uint32_t box_rows);
 int sm_count(int device);
 int* device_status_ptr();  // address of the device status word (current device)
 
@@ -135,6 +145,27 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Tiled load of a 4-D map (channels-last activation: c, w, h, n); any of w,
+// h may be negative or past the end (zero fill).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// im2col-mode load of a 4-D channels-last map: 64 channels from c of the
+// pixels the map's box traverses from (w, h, n); zero im2col offsets.
+__device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c, int w,
+                                                   int h, int n) {
+  const uint16_t z = 0;
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(z), "h"(z)
       : "memory");
 }
 // Tiled store shared -> global (bulk async-group of the issuing thread).  The
@@ -254,6 +285,50 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+// The 4-D tiled form of tma_load_3d_pair (no multicast).
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+// The im2col form of tma_load_3d_pair (no multicast).
+__device__ __forceinline__ void tma_load_im2col_4d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster,
+                                                        int c, int w, int h, int n) {
+  const uint16_t z = 0;
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c), "r"(w), "r"(h), "r"(n), "h"(z), "h"(z)
+      : "memory");
+}
+// `nrows` (the map's box) consecutive padded-grid rows of 64 channels from
+// channel c0, starting at padded row r, from either packed rows (a tiled 2-D
+// map) or a channels-last tensor (an encode_tmap_padded_nhwc map): the same
+// shared-memory image either way.  Row r of a grid of pitch wp and plane
+// rows per image is pixel (r / plane, (r % plane) / wp - 1, r % wp - 1); rows
+// past the last image start at n = B and read zeros.
+template <bool PAIR>
+__device__ __forceinline__ void load_rows(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int r,
+                                          bool im2col, int wp, int plane) {
+  if (!im2col) {
+    if constexpr (PAIR)
+      tma_load_3d_pair(dst, map, bar, c0, r, 0);
+    else
+      tma_load_3d(dst, map, bar, c0, r, 0);
+    return;
+  }
+  const int n = r / plane;
+  const int rem = r - n * plane;
+  const int yy = rem / wp;
+  const int xx = rem - yy * wp;
+  if constexpr (PAIR)
+    tma_load_im2col_4d_pair(dst, map, bar, c0, xx - 1, yy - 1, n);
+  else
+    tma_load_im2col_4d(dst, map, bar, c0, xx - 1, yy - 1, n);
 }
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)

@@ -1,5 +1,8 @@
 // tcgen05 implicit-GEMM kernels for sm_100a: 3x3/s1/p1 convolution forward
-// and dgrad, convolution wgrad, and dense (batched) bf16 GEMM.
+// and dgrad, convolution wgrad, and dense (batched) bf16 GEMM.  Activations
+// come as padded-grid rows (b2_pack_rows_bf16) or, channels-last, straight
+// from the caller's tensor through an im2col TMA map whose pixel box is the
+// padded grid (the *_nhwc entry points: no packing pass).
 //
 // One persistent, warp-specialized kernel template serves all of them:
 //   warp 0      TMA producer: fills a STAGES-deep ring of shared-memory
@@ -64,7 +67,27 @@ struct Params {
   int tma_store;     // GEMM: bf16 D written by TMA stores of shared-memory staged boxes
   int win_boxes, win_box_rows;  // conv halo kernel: the A window is win_boxes TMA boxes of win_box_rows rows
   int win_bufs;                 // resident-weight halo kernel: window buffers in flight (<= kMaxWinBufs)
+  // activation operands read as padded-grid rows: bit 0 for the first map
+  // (A, the halo window, wgrad's dY), bit 1 for the second (wgrad's X);
+  // set = an im2col map over a channels-last tensor, clear = packed rows
+  int src_im2col;
+  // weight gradient over channels-last dY and X with tiled 4-D loads: k-block
+  // kb is the patch_wb x patch_hb pixel patch (kb % patch_nx, kb / patch_nx %
+  // patch_ny) of image kb / (patch_nx * patch_ny) (patch_wb * patch_hb == 64);
+  // X for tap (dy, dx) is the same patch moved by (dx - 1, dy - 1), the image
+  // border and the patch's overhang read as zeros.  0 = padded-row k-blocks.
+  int patch_wb, patch_hb, patch_nx, patch_ny;
 };
+
+// Origin (x0, y0, n) of the pixel patch of k-block kb (Params::patch_*).
+__device__ __forceinline__ void patch_origin(const Params& p, int kb, int& x0, int& y0, int& n) {
+  const int bx = kb % p.patch_nx;
+  const int t = kb / p.patch_nx;
+  const int by = t % p.patch_ny;
+  n = t / p.patch_ny;
+  x0 = bx * p.patch_wb;
+  y0 = by * p.patch_hb;
+}
 
 template <int BN>
 struct Smem {
@@ -376,15 +399,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (KIND == kConv) {
             const int chunk = kb / 9, tp = kb - chunk * 9;
             const int dy = tp / 3, dx = tp - dy * 3;
-            tma_load_3d(sa, &tma_a, fb, chunk * BK, mt * BM + dy * p.wp + dx, 0);
+            load_rows<false>(sa, &tma_a, fb, chunk * BK, mt * BM + dy * p.wp + dx, p.src_im2col & 1, p.wp,
+                             p.wp * p.hp);
             tma_load_3d(sb, &tma_b, fb, kb * BK, nt * BN, 0);
           } else if constexpr (KIND == kWgrad) {
             const int dy = tap / 3, dx = tap - dy * 3;
-            tma_load_3d(sa, &tma_a, fb, mt * BM, kb * BK + p.a_row_shift, 0);
-            tma_load_3d(sa + 8192, &tma_a, fb, mt * BM + 64, kb * BK + p.a_row_shift, 0);
+            if (p.patch_wb) {
+              int x0, y0, n;
+              patch_origin(p, kb, x0, y0, n);
+              tma_load_4d(sa, &tma_a, fb, mt * BM, x0, y0, n);
+              tma_load_4d(sa + 8192, &tma_a, fb, mt * BM + 64, x0, y0, n);
 #pragma unroll
-            for (int h = 0; h < BN / 64; ++h)
-              tma_load_3d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK + dy * p.wp + dx, 0);
+              for (int h = 0; h < BN / 64; ++h)
+                tma_load_4d(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, x0 + dx - 1, y0 + dy - 1, n);
+            } else {
+              const int plane = p.wp * p.hp;
+              load_rows<false>(sa, &tma_a, fb, mt * BM, kb * BK + p.a_row_shift, p.src_im2col & 1, p.wp, plane);
+              load_rows<false>(sa + 8192, &tma_a, fb, mt * BM + 64, kb * BK + p.a_row_shift, p.src_im2col & 1,
+                               p.wp, plane);
+#pragma unroll
+              for (int h = 0; h < BN / 64; ++h)
+                load_rows<false>(sb + h * 8192, &tma_b, fb, nt * BN + h * 64, kb * BK + dy * p.wp + dx,
+                                 p.src_im2col & 2, p.wp, plane);
+            }
           } else {
             // slice (z) and k offset of this k-block for A and B
             int za = bz, zb = bz, k0 = kb * BK;
@@ -697,16 +734,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if constexpr (KIND == kConv) {
             const int chunk = kb / 9, tp = kb - chunk * 9;
             const int dy = tp / 3, dx = tp - dy * 3;
-            tma_load_3d_pair(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, 0);
+            load_rows<true>(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, p.src_im2col & 1, p.wp,
+                            p.wp * p.hp);
             tma_load_3d_pair(sb, &tma_b, fb, kb * BK, nt * BN + int(rank) * kBHalf, 0);
           } else {
             // A = dY rows (co contiguous), this CTA's 128 co; B = X rows shifted by the tap
             const int dy = tap / 3, dx = tap - dy * 3;
             const int ci0 = nt * BN + int(rank) * kBHalf;
-            tma_load_3d_pair(sa, &tma_a, fb, row0, kb * BK + p.a_row_shift, 0);
-            tma_load_3d_pair(sa + 8192, &tma_a, fb, row0 + 64, kb * BK + p.a_row_shift, 0);
-            tma_load_3d_pair(sb, &tma_b, fb, ci0, kb * BK + dy * p.wp + dx, 0);
-            tma_load_3d_pair(sb + 8192, &tma_b, fb, ci0 + 64, kb * BK + dy * p.wp + dx, 0);
+            if (p.patch_wb) {
+              int x0, y0, n;
+              patch_origin(p, kb, x0, y0, n);
+              tma_load_4d_pair(sa, &tma_a, fb, row0, x0, y0, n);
+              tma_load_4d_pair(sa + 8192, &tma_a, fb, row0 + 64, x0, y0, n);
+              tma_load_4d_pair(sb, &tma_b, fb, ci0, x0 + dx - 1, y0 + dy - 1, n);
+              tma_load_4d_pair(sb + 8192, &tma_b, fb, ci0 + 64, x0 + dx - 1, y0 + dy - 1, n);
+            } else {
+              const int plane = p.wp * p.hp;
+              const bool ia = p.src_im2col & 1, ib = p.src_im2col & 2;
+              load_rows<true>(sa, &tma_a, fb, row0, kb * BK + p.a_row_shift, ia, p.wp, plane);
+              load_rows<true>(sa + 8192, &tma_a, fb, row0 + 64, kb * BK + p.a_row_shift, ia, p.wp, plane);
+              load_rows<true>(sb, &tma_b, fb, ci0, kb * BK + dy * p.wp + dx, ib, p.wp, plane);
+              load_rows<true>(sb + 8192, &tma_b, fb, ci0 + 64, kb * BK + dy * p.wp + dx, ib, p.wp, plane);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -930,7 +979,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t fa = mapa_shared(fa_local, 0);
           const uint32_t sa = smem_u32(a_base + as * a_bytes);
           for (int i = 0; i < p.win_boxes; ++i)
-            tma_load_3d_pair(sa + i * box_bytes, &tma_win, fa, ch * BK, row0 + i * p.win_box_rows, 0);
+            load_rows<true>(sa + i * box_bytes, &tma_win, fa, ch * BK, row0 + i * p.win_box_rows, p.src_im2col & 1,
+                            p.wp, p.wp * p.hp);
           if (++as == 2) {
             as = 0;
             aph ^= 1;
@@ -1156,7 +1206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         a_last[as] = int(aph);
         const uint32_t sa = smem_u32(a_base + as * a_bytes);
         for (int i = 0; i < p.win_boxes; ++i)
-          tma_load_3d(sa + i * box_bytes, &tma_win, fa, 0, t * BM + i * p.win_box_rows, 0);
+          load_rows<false>(sa + i * box_bytes, &tma_win, fa, 0, t * BM + i * p.win_box_rows, p.src_im2col & 1, p.wp,
+                           p.wp * p.hp);
         if (++as == NW) {
           as = 0;
           aph ^= 1;
@@ -1335,9 +1386,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         last[st] = int(ph);
         const uint32_t sd = smem_u32(smem + st * stage_bytes);
         const int row0 = kb * kNarrowWgradPix;
-        tma_load_3d(sd, &tma_dy, f, 0, row0 + p.a_row_shift, 0);
+        load_rows<false>(sd, &tma_dy, f, 0, row0 + p.a_row_shift, p.src_im2col & 1, p.wp, p.wp * p.hp);
         for (int i = 0; i < p.win_boxes; ++i)
-          tma_load_3d(sd + kDyBytes + i * box_bytes, &tma_x, f, 0, row0 + i * p.win_box_rows, 0);
+          load_rows<false>(sd + kDyBytes + i * box_bytes, &tma_x, f, 0, row0 + i * p.win_box_rows, p.src_im2col & 2,
+                           p.wp, p.wp * p.hp);
         if (++st == NS) {
           st = 0;
           ph ^= 1;
@@ -1617,6 +1669,16 @@ bool narrow_wgrad_enabled() {
   return on;
 }
 
+// Pixel-patch k-blocks for the weight gradient of channels-last operands
+// unless B2_WGRAD_PATCH=0 (A/B switch: the im2col padded-row k-blocks).
+bool patch_wgrad_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_WGRAD_PATCH");
+    return !e || e[0] != '0';
+  }();
+  return on;
+}
+
 // SM-pair MMA for wide convolutions unless B2_PAIR_MMA=0 (A/B switch).
 bool pair_mma_enabled() {
   static const bool on = [] {
@@ -1628,13 +1690,62 @@ bool pair_mma_enabled() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, void* y, int64_t sn,
+// An activation operand of the conv kernels: padded-grid rows written by
+// b2_pack_rows_bf16, or a channels-last tensor (channel stride 1, element
+// strides sn / sh / sw) read through an im2col map whose pixel box is the
+// padded grid -- the kernels see the same rows either way.
+struct ActSrc {
+  const void* ptr = nullptr;
+  bool nhwc = false;
+  int64_t sn = 0, sh = 0, sw = 0;
+};
+
+ActSrc rows_src(const void* rows) {
+  ActSrc a;
+  a.ptr = rows;
+  return a;
+}
+
+// The stride of a dimension of size 1 is never used to address an element
+// (frameworks leave any value there, e.g. 1): give such dimensions the
+// dense stride so they pass the TMA stride rules.
+void normalize_act(ActSrc& a, int B, int C, int H, int W) {
+  if (!a.nhwc) return;
+  if (W == 1) a.sw = C;
+  if (H == 1) a.sh = int64_t(W) * a.sw;
+  if (B == 1) a.sn = int64_t(H) * a.sh;
+}
+
+b2_status check_act(const ActSrc& a, int C, const char* name, const char* what) {
+  if (!a.ptr) return set_error(B2_ERR_INVALID, "%s: null %s", name, what);
+  if (!aligned16(a.ptr)) return set_error(B2_ERR_INVALID, "%s: %s must be 16-byte aligned", name, what);
+  if (a.nhwc && (C % 8 || a.sn % 8 || a.sh % 8 || a.sw % 8 || a.sn <= 0 || a.sh <= 0 || a.sw < C))
+    return set_error(B2_ERR_UNSUPPORTED,
+                     "%s: channels-last %s needs C %% 8 == 0 and pixel strides that are multiples of 8 elements",
+                     name, what);
+  return B2_OK;
+}
+
+// A map of `box_rows` padded-grid rows x 64 channels over operand `a`.
+b2_status rows_map(CUtensorMap* m, const ActSrc& a, int B, int C, int H, int W, uint32_t box_rows) {
+  if (a.nhwc) return encode_tmap_padded_nhwc(m, a.ptr, B, C, H, W, a.sn, a.sh, a.sw, box_rows);
+  const uint64_t cpad = uint64_t((C + 63) / 64) * 64;
+  const uint64_t m_total = uint64_t(B) * uint64_t(H + 2) * uint64_t(W + 2);
+  const uint64_t dims[3] = {cpad, m_total, 1};
+  const uint64_t strides[2] = {cpad * 2, cpad * 2 * m_total};
+  const uint32_t box[3] = {64, box_rows, 1};
+  return encode_tmap(m, a.ptr, 3, dims, strides, box, true);
+}
+
+b2_status conv_common(ActSrc xs, const void* wk, const uint16_t* bias, void* y, int64_t sn,
                       int64_t sc, int64_t sh, int64_t sw, int B, int Cin, int H, int W, int Cout,
                       int relu, cudaStream_t st, const char* name) {
-  if (!rows || !wk || !y) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
+  if (!wk || !y) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
   if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
     return set_error(B2_ERR_INVALID, "%s: bad shape B=%d C=%d H=%d W=%d Cout=%d", name, B, Cin, H, W, Cout);
-  if (!aligned16(rows) || !aligned16(wk)) return set_error(B2_ERR_INVALID, "%s: operands must be 16-byte aligned", name);
+  normalize_act(xs, B, Cin, H, W);
+  B2_TRY(check_act(xs, Cin, name, "input"));
+  if (!aligned16(wk)) return set_error(B2_ERR_INVALID, "%s: operands must be 16-byte aligned", name);
   const long long m_total = (long long)B * (H + 2) * (W + 2);
   if (m_total + 2LL * (W + 2) + 2 + BM >= (1LL << 31))
     return set_error(B2_ERR_UNSUPPORTED, "%s: %lld padded rows exceed the 32-bit TMA coordinate range", name, m_total);
@@ -1647,13 +1758,9 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   const int BN = wide ? 256 : narrow ? 64 : 128;
   const uint32_t b_box = pair ? 128u : uint32_t(BN);  // the pair kernel loads half of B per CTA
 
+  (void)cpad;
   CUtensorMap ta, tb;
-  {
-    const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
-    const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
-    const uint32_t box[3] = {64, BM, 1};
-    B2_TRY(encode_tmap(&ta, rows, 3, dims, strides, box, true));
-  }
+  B2_TRY(rows_map(&ta, xs, B, Cin, H, W, BM));
   {
     const uint64_t dims[3] = {uint64_t(ktot), uint64_t(Cout), 1};
     const uint64_t strides[2] = {uint64_t(ktot) * 2, uint64_t(ktot) * 2 * Cout};
@@ -1683,6 +1790,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
   p.relu = relu;
   p.alpha = 1.f;
   p.status = device_status_ptr();
+  p.src_im2col = xs.nhwc ? 1 : 0;
   const int tiles = p.tiles_m * p.tiles_n;
   if (pair) {
     Params pp = p;
@@ -1691,10 +1799,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
     if (halo_enabled()) halo_window(W + 2, size_t(kHaloB) * 128 * BK * 2, boxes, box_rows);
     if (boxes > 0) {
       CUtensorMap twin;
-      const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
-      const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
-      const uint32_t box[3] = {64, uint32_t(box_rows), 1};
-      B2_TRY(encode_tmap(&twin, rows, 3, dims, strides, box, true));
+      B2_TRY(rows_map(&twin, xs, B, Cin, H, W, uint32_t(box_rows)));
       pp.win_boxes = boxes;
       pp.win_box_rows = box_rows;
       return launch_pair_halo(twin, tb, pp, st);
@@ -1707,10 +1812,7 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
     const int bufs = boxes > 0 ? bres_window_buffers(boxes * box_rows * 128) : 0;
     if (bufs > 0) {
       CUtensorMap twin;
-      const uint64_t dims[3] = {uint64_t(cpad), uint64_t(m_total), 1};
-      const uint64_t strides[2] = {uint64_t(cpad) * 2, uint64_t(cpad) * 2 * m_total};
-      const uint32_t box[3] = {64, uint32_t(box_rows), 1};
-      B2_TRY(encode_tmap(&twin, rows, 3, dims, strides, box, true));
+      B2_TRY(rows_map(&twin, xs, B, Cin, H, W, uint32_t(box_rows)));
       Params ph = p;
       ph.win_boxes = boxes;
       ph.win_box_rows = box_rows;
@@ -1725,12 +1827,28 @@ b2_status conv_common(const void* rows, const void* wk, const uint16_t* bias, vo
 
 struct WgradPlan {
   int BN, ci_blocks, tiles_m, num_kb, splits, kb_per_split;
+  int wb = 0, hb = 0, nx = 0, ny = 0;  // pixel patches of channels-last operands (0: padded rows)
   bool pair;  // SM-pair kernel: 256-co x 256-ci tiles per cluster of two CTAs
   long long m_total;
   size_t workspace;
 };
 
-WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow_pair) {
+// The 64-pixel patch (wb x hb, powers of two) that covers an H x W image
+// with the fewest padded pixels; ties go to the wider patch.
+void choose_patch(int H, int W, int& wb, int& hb) {
+  long long best = -1;
+  for (int e = 6; e >= 0; --e) {
+    const int cw = 1 << e, chh = BK / cw;
+    const long long area = (long long)((W + cw - 1) / cw) * cw * (long long)((H + chh - 1) / chh) * chh;
+    if (best < 0 || area < best) {
+      best = area;
+      wb = cw;
+      hb = chh;
+    }
+  }
+}
+
+WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow_pair, bool patches = false) {
   WgradPlan w{};
   w.m_total = (long long)B * (H + 2) * (W + 2);
   w.pair = allow_pair && Cin > 128 && Cout > 128;
@@ -1738,6 +1856,12 @@ WgradPlan wgrad_plan(int B, int Cin, int H, int W, int Cout, int sms, bool allow
   w.ci_blocks = (Cin + w.BN - 1) / w.BN;
   w.tiles_m = (Cout + (w.pair ? 255 : BM - 1)) / (w.pair ? 256 : BM);
   w.num_kb = int((w.m_total + BK - 1) / BK);
+  if (patches) {
+    choose_patch(H, W, w.wb, w.hb);
+    w.nx = (W + w.wb - 1) / w.wb;
+    w.ny = (H + w.hb - 1) / w.hb;
+    w.num_kb = B * w.nx * w.ny;
+  }
   // Split-K so that the tiles fill the SMs (pairs of SMs for the pair kernel)
   // in whole waves: tiles are long (thousands of k-blocks), so a partial last
   // wave would idle SMs for a whole tile's duration.
@@ -1952,14 +2076,14 @@ extern "C" {
 b2_status b2_conv3x3_fwd(const void* x_rows, const void* wk, const void* bias, void* y, int64_t ysn,
                          int64_t ysc, int64_t ysh, int64_t ysw, int B, int Cin, int H, int W,
                          int Cout, int relu, void* stream) {
-  return conv_common(x_rows, wk, static_cast<const uint16_t*>(bias), y, ysn, ysc, ysh, ysw, B, Cin,
+  return conv_common(rows_src(x_rows), wk, static_cast<const uint16_t*>(bias), y, ysn, ysc, ysh, ysw, B, Cin,
                      H, W, Cout, relu, static_cast<cudaStream_t>(stream), "b2_conv3x3_fwd");
 }
 
 b2_status b2_conv3x3_dgrad(const void* dy_rows, const void* wk_dgrad, void* dx, int64_t sn,
                            int64_t sc, int64_t sh, int64_t sw, int B, int Cout, int H, int W,
                            int Cin, void* stream) {
-  return conv_common(dy_rows, wk_dgrad, nullptr, dx, sn, sc, sh, sw, B, Cout, H, W, Cin, 0,
+  return conv_common(rows_src(dy_rows), wk_dgrad, nullptr, dx, sn, sc, sh, sw, B, Cout, H, W, Cin, 0,
                      static_cast<cudaStream_t>(stream), "b2_conv3x3_dgrad");
 }
 
@@ -1969,37 +2093,34 @@ size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout) 
   cudaGetDevice(&dev);
   const NarrowWgradPlan nw = narrow_wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
   if (nw.ok) return std::max<size_t>(16, nw.workspace);
-  return std::max<size_t>(16, wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled()).workspace);
+  // the larger of the padded-row and the pixel-patch plans (channels-last operands)
+  return std::max<size_t>({size_t(16), wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled()).workspace,
+                           wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled(), true).workspace});
 }
 
-b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, int dw_dtype, int B,
-                           int Cin, int H, int W, int Cout, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+static b2_status wgrad_common(ActSrc dys, ActSrc xs, void* dw, int dw_dtype, int B, int Cin, int H,
+                              int W, int Cout, void* workspace, size_t workspace_bytes, void* stream,
+                              const char* name) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (!dy_rows || !x_rows || !dw || !workspace) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: null pointer");
-  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0)
-    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: bad shape");
-  if (dw_dtype != B2_BF16 && dw_dtype != B2_F32) return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: dtype");
-  if (!aligned16(dy_rows) || !aligned16(x_rows) || !aligned16(workspace))
-    return set_error(B2_ERR_INVALID, "b2_conv3x3_wgrad: operands must be 16-byte aligned");
+  if (!dw || !workspace) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
+  if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
+  if (dw_dtype != B2_BF16 && dw_dtype != B2_F32) return set_error(B2_ERR_INVALID, "%s: dtype", name);
+  normalize_act(dys, B, Cout, H, W);
+  normalize_act(xs, B, Cin, H, W);
+  B2_TRY(check_act(dys, Cout, name, "dY"));
+  B2_TRY(check_act(xs, Cin, name, "input"));
+  if (!aligned16(workspace)) return set_error(B2_ERR_INVALID, "%s: workspace must be 16-byte aligned", name);
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   const NarrowWgradPlan nw = narrow_wgrad_plan(B, Cin, H, W, Cout, sm_count(dev));
   if (nw.ok) {
     if (nw.m_total + 2LL * (W + 2) + 2 + W + 3 + kNarrowWgradPix >= (1LL << 31))
-      return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
+      return set_error(B2_ERR_UNSUPPORTED, "%s: too many padded rows", name);
     if (workspace_bytes < nw.workspace)
-      return set_error(B2_ERR_WORKSPACE, "b2_conv3x3_wgrad: workspace %zu < %zu bytes", workspace_bytes,
-                       nw.workspace);
+      return set_error(B2_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", name, workspace_bytes, nw.workspace);
     CUtensorMap tdy, tx;
-    {
-      const uint64_t dims[3] = {64, uint64_t(nw.m_total), 1};
-      const uint64_t strides[2] = {128, uint64_t(128) * nw.m_total};
-      const uint32_t box[3] = {64, uint32_t(kNarrowWgradPix), 1};
-      B2_TRY(encode_tmap(&tdy, dy_rows, 3, dims, strides, box, true));
-      const uint32_t wbox[3] = {64, uint32_t(nw.box_rows), 1};
-      B2_TRY(encode_tmap(&tx, x_rows, 3, dims, strides, wbox, true));
-    }
+    B2_TRY(rows_map(&tdy, dys, B, Cout, H, W, uint32_t(kNarrowWgradPix)));
+    B2_TRY(rows_map(&tx, xs, B, Cin, H, W, uint32_t(nw.box_rows)));
     Params p{};
     p.splits = nw.splits;
     p.num_kb = nw.num_kb;
@@ -2018,6 +2139,7 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
     p.partial = static_cast<float*>(workspace);
     p.alpha = 1.f;
     p.status = device_status_ptr();
+    p.src_im2col = (dys.nhwc ? 1 : 0) | (xs.nhwc ? 2 : 0);
     B2_TRY(launch_wgrad_narrow(tdy, tx, p, nw.smem, nw.splits, st));
     const long long total = (long long)Cout * Cin * 9;
     const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 16));
@@ -2025,25 +2147,26 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
                                                 Cout, Cin);
     return check_cuda(cudaGetLastError(), "wgrad reduce launch");
   }
-  const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled());
-  if (w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
-    return set_error(B2_ERR_UNSUPPORTED, "b2_conv3x3_wgrad: too many padded rows");
+  // Channels-last dY and X: k-blocks are 64-pixel patches fetched by tiled
+  // 4-D loads (an im2col load of 64 pixels costs about twice a tiled one).
+  const bool patches = dys.nhwc && xs.nhwc && patch_wgrad_enabled();
+  const WgradPlan w = wgrad_plan(B, Cin, H, W, Cout, sm_count(dev), pair_mma_enabled(), patches);
+  if (!patches && w.m_total + 2LL * (W + 2) + 2 + W + 3 + BK >= (1LL << 31))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: too many padded rows", name);
   if (workspace_bytes < w.workspace)
-    return set_error(B2_ERR_WORKSPACE, "b2_conv3x3_wgrad: workspace %zu < %zu bytes", workspace_bytes, w.workspace);
-  const int cpo = ((Cout + 63) / 64) * 64;
-  const int cpi = ((Cin + 63) / 64) * 64;
+    return set_error(B2_ERR_WORKSPACE, "%s: workspace %zu < %zu bytes", name, workspace_bytes, w.workspace);
   CUtensorMap ta, tb;
-  {
-    const uint64_t dims[3] = {uint64_t(cpo), uint64_t(w.m_total), 1};
-    const uint64_t strides[2] = {uint64_t(cpo) * 2, uint64_t(cpo) * 2 * w.m_total};
-    const uint32_t box[3] = {64, 64, 1};
-    B2_TRY(encode_tmap(&ta, dy_rows, 3, dims, strides, box, true));
-  }
-  {
-    const uint64_t dims[3] = {uint64_t(cpi), uint64_t(w.m_total), 1};
-    const uint64_t strides[2] = {uint64_t(cpi) * 2, uint64_t(cpi) * 2 * w.m_total};
-    const uint32_t box[3] = {64, 64, 1};
-    B2_TRY(encode_tmap(&tb, x_rows, 3, dims, strides, box, true));
+  if (patches) {
+    const uint32_t box[4] = {64, uint32_t(w.wb), uint32_t(w.hb), 1};
+    const uint64_t dd[4] = {uint64_t(Cout), uint64_t(W), uint64_t(H), uint64_t(B)};
+    const uint64_t ds[3] = {uint64_t(dys.sw) * 2, uint64_t(dys.sh) * 2, uint64_t(dys.sn) * 2};
+    B2_TRY(encode_tmap(&ta, dys.ptr, 4, dd, ds, box, true));
+    const uint64_t xd[4] = {uint64_t(Cin), uint64_t(W), uint64_t(H), uint64_t(B)};
+    const uint64_t xst[3] = {uint64_t(xs.sw) * 2, uint64_t(xs.sh) * 2, uint64_t(xs.sn) * 2};
+    B2_TRY(encode_tmap(&tb, xs.ptr, 4, xd, xst, box, true));
+  } else {
+    B2_TRY(rows_map(&ta, dys, B, Cout, H, W, 64));
+    B2_TRY(rows_map(&tb, xs, B, Cin, H, W, 64));
   }
   Params p{};
   p.tiles_m = w.tiles_m;
@@ -2064,6 +2187,11 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
   p.partial = static_cast<float*>(workspace);
   p.alpha = 1.f;
   p.status = device_status_ptr();
+  p.src_im2col = (dys.nhwc ? 1 : 0) | (xs.nhwc ? 2 : 0);
+  p.patch_wb = w.wb;
+  p.patch_hb = w.hb;
+  p.patch_nx = w.nx;
+  p.patch_ny = w.ny;
   const int tiles = w.splits * w.tiles_m * 9 * w.ci_blocks;
   if (w.pair)
     B2_TRY(launch_pair<kWgrad>(ta, tb, p, tiles, st));
@@ -2079,6 +2207,44 @@ b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, in
   wgrad_reduce_kernel<<<blocks, threads, 0, st>>>(static_cast<const float*>(workspace), dw, dw_dtype,
                                                   w.splits, Cout, Cin);
   return check_cuda(cudaGetLastError(), "wgrad reduce launch");
+}
+
+b2_status b2_conv3x3_wgrad(const void* dy_rows, const void* x_rows, void* dw, int dw_dtype, int B, int Cin, int H,
+                           int W, int Cout, void* workspace, size_t workspace_bytes, void* stream) {
+  return wgrad_common(rows_src(dy_rows), rows_src(x_rows), dw, dw_dtype, B, Cin, H, W, Cout, workspace,
+                      workspace_bytes, stream, "b2_conv3x3_wgrad");
+}
+
+// ---- channels-last operands read in place (no padded-row copy) ------------
+static ActSrc nhwc_src(const void* t, int64_t sn, int64_t sh, int64_t sw) {
+  ActSrc a;
+  a.ptr = t;
+  a.nhwc = true;
+  a.sn = sn;
+  a.sh = sh;
+  a.sw = sw;
+  return a;
+}
+
+b2_status b2_conv3x3_fwd_nhwc(const void* x, int64_t xsn, int64_t xsh, int64_t xsw, const void* wk,
+                              const void* bias, void* y, int64_t ysn, int64_t ysc, int64_t ysh, int64_t ysw, int B,
+                              int Cin, int H, int W, int Cout, int relu, void* stream) {
+  return conv_common(nhwc_src(x, xsn, xsh, xsw), wk, static_cast<const uint16_t*>(bias), y, ysn, ysc, ysh, ysw, B,
+                     Cin, H, W, Cout, relu, static_cast<cudaStream_t>(stream), "b2_conv3x3_fwd_nhwc");
+}
+
+b2_status b2_conv3x3_dgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh, int64_t dsw, const void* wk_dgrad,
+                                void* dx, int64_t sn, int64_t sc, int64_t sh, int64_t sw, int B, int Cout, int H,
+                                int W, int Cin, void* stream) {
+  return conv_common(nhwc_src(dy, dsn, dsh, dsw), wk_dgrad, nullptr, dx, sn, sc, sh, sw, B, Cout, H, W, Cin, 0,
+                     static_cast<cudaStream_t>(stream), "b2_conv3x3_dgrad_nhwc");
+}
+
+b2_status b2_conv3x3_wgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh, int64_t dsw, const void* x, int64_t xsn,
+                                int64_t xsh, int64_t xsw, void* dw, int dw_dtype, int B, int Cin, int H, int W,
+                                int Cout, void* workspace, size_t workspace_bytes, void* stream) {
+  return wgrad_common(nhwc_src(dy, dsn, dsh, dsw), nhwc_src(x, xsn, xsh, xsw), dw, dw_dtype, B, Cin, H, W, Cout,
+                      workspace, workspace_bytes, stream, "b2_conv3x3_wgrad_nhwc");
 }
 
 b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha, const void* A,

@@ -324,6 +324,77 @@ __global__ void chsum_stage1_kernel(const T* __restrict__ in, long long nrows, i
   out[(long long)blockIdx.x * C + c] = s;
 }
 
+// Channel sums of dense channels-last pixel rows (C % 8 == 0, C <= 2048,
+// 16-byte aligned rows), stage 1: block g sums rows [g*rpb, (g+1)*rpb) into
+// out[g][c].  A thread owns 8 channels (16-byte loads) of every
+// rows_per_iter-th row of the range, four loads in flight; the block's row
+// lanes are then added in lane order: a fixed order, deterministic.
+__global__ void __launch_bounds__(256) chsum_nhwc_vec_kernel(const uint16_t* __restrict__ x, long long P,
+                                                              long long sw, int C, long long rpb,
+                                                              float* __restrict__ out) {
+  extern __shared__ float part[];  // [rows_per_iter][C]
+  const int lanes = C / 8;
+  const int rows_per_iter = 256 / lanes;
+  const int t = threadIdx.x;
+  const int rl = t / lanes, cl = t - (t / lanes) * lanes;
+  const long long r0 = (long long)blockIdx.x * rpb;
+  const long long r1 = r0 + rpb < P ? r0 + rpb : P;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (rl < rows_per_iter) {
+    long long r = r0 + rl;
+    for (; r + 3LL * rows_per_iter < r1; r += 4LL * rows_per_iter) {
+      uint4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = *reinterpret_cast<const uint4*>(x + (r + (long long)u * rows_per_iter) * sw + cl * 8);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          acc[2 * k] += __uint_as_float(w[k] << 16);
+          acc[2 * k + 1] += __uint_as_float(w[k] & 0xffff0000u);
+        }
+      }
+    }
+    for (; r < r1; r += rows_per_iter) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + r * sw + cl * 8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[2 * k] += __uint_as_float(w[k] << 16);
+        acc[2 * k + 1] += __uint_as_float(w[k] & 0xffff0000u);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) part[rl * C + cl * 8 + k] = acc[k];
+  }
+  __syncthreads();
+  for (int c = t; c < C; c += 256) {
+    float s = 0.f;
+    for (int l = 0; l < rows_per_iter; ++l) s += part[l * C + c];
+    out[(long long)blockIdx.x * C + c] = s;
+  }
+}
+
+// Stage 2 for many groups: a warp per channel, lane l adding groups l, l+32,
+// ... in order, then a fixed shuffle tree (deterministic), rounded once.
+__global__ void chsum_stage2_warp_kernel(const float* __restrict__ in, int ngroups, int C, void* out, int dtype) {
+  const int c = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (c >= C) return;
+  double s = 0.0;
+  for (int g = lane; g < ngroups; g += 32) s += in[(long long)g * C + c];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    if (dtype == B2_F32)
+      static_cast<float*>(out)[c] = float(s);
+    else
+      static_cast<uint16_t*>(out)[c] = f2bf(float(s));
+  }
+}
+
 // Stage 2: dbias[c] = sum over groups, fixed order, rounded once.
 __global__ void chsum_stage2_kernel(const float* __restrict__ in, int ngroups, int C, void* out, int dtype) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -477,6 +548,50 @@ b2_status b2_pack_rows_dbias_bf16(const void* x, int64_t sn, int64_t sc, int64_t
         static_cast<const uint16_t*>(rows), m_total, int(cpad), C, ws);
     chsum_stage2_kernel<<<(C + 255) / 256, 256, 0, st>>>(ws, int(ng), C, dbias, dbias_dtype);
   }
+  return check_cuda(cudaGetLastError(), "channel-sum launch");
+}
+
+size_t b2_channel_sum_nhwc_workspace_bytes(int B, int C, int H, int W) {
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0) return 256;
+  const long long ng = ((long long)B * H * W + 63) / 64;
+  return size_t((ng * C * 4 + 255) / 256 * 256);
+}
+
+b2_status b2_channel_sum_nhwc_bf16(const void* x, int64_t sn, int64_t sh, int64_t sw, int B, int C, int H, int W,
+                                   void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  if (!x || !out || !workspace) return set_error(B2_ERR_INVALID, "b2_channel_sum_nhwc_bf16: null pointer");
+  if (B <= 0 || C <= 0 || H <= 0 || W <= 0) return set_error(B2_ERR_INVALID, "b2_channel_sum_nhwc_bf16: bad shape");
+  if (out_dtype != B2_BF16 && out_dtype != B2_F32)
+    return set_error(B2_ERR_INVALID, "b2_channel_sum_nhwc_bf16: dtype");
+  if (W == 1) sw = C;  // strides of size-1 dimensions address nothing
+  if (H == 1) sh = (int64_t)W * sw;
+  if (B == 1) sn = (int64_t)H * sh;
+  if (sw < C || sh != (int64_t)W * sw || sn != (int64_t)H * sh)
+    return set_error(B2_ERR_UNSUPPORTED, "b2_channel_sum_nhwc_bf16: pixels must be dense rows of sw >= C elements");
+  if (workspace_bytes < b2_channel_sum_nhwc_workspace_bytes(B, C, H, W) || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return set_error(B2_ERR_WORKSPACE, "b2_channel_sum_nhwc_bf16: workspace of %zu bytes needed",
+                     b2_channel_sum_nhwc_workspace_bytes(B, C, H, W));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long P = (long long)B * H * W;
+  const long long ng = (P + 63) / 64;
+  if (ng > 0x7fffffffLL) return set_error(B2_ERR_UNSUPPORTED, "b2_channel_sum_nhwc_bf16: too many pixels");
+  float* ws = static_cast<float*>(workspace);
+  if (C % 8 == 0 && C <= 2048 && sw % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // 16-byte loads over ranges of rows: up to 592 blocks (4 per SM), at most
+    // ng groups, so the workspace bound above holds
+    const long long rows_per_iter = 256 / (C / 8);
+    const long long groups = std::min<long long>(std::min<long long>(592, ng), (P + rows_per_iter - 1) / rows_per_iter);
+    const long long rpb = (P + groups - 1) / groups;
+    const long long g = (P + rpb - 1) / rpb;
+    const size_t smem = size_t(rows_per_iter) * C * sizeof(float);
+    chsum_nhwc_vec_kernel<<<unsigned(g), 256, smem, st>>>(static_cast<const uint16_t*>(x), P, sw, C, rpb, ws);
+    chsum_stage2_warp_kernel<<<(C + 7) / 8, 256, 0, st>>>(ws, int(g), C, out, out_dtype);
+    return check_cuda(cudaGetLastError(), "channel-sum launch");
+  }
+  chsum_stage1_kernel<uint16_t><<<dim3(unsigned(ng), unsigned((C + 255) / 256)), 256, 0, st>>>(
+      static_cast<const uint16_t*>(x), P, int(sw), C, ws);
+  chsum_stage2_kernel<<<(C + 255) / 256, 256, 0, st>>>(ws, int(ng), C, out, out_dtype);
   return check_cuda(cudaGetLastError(), "channel-sum launch");
 }
 

@@ -25,6 +25,7 @@ int g_sm_count[kMaxDevices] = {};
 std::mutex g_mu;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
 
 }  // namespace
 
@@ -110,6 +111,36 @@ b2_status encode_tmap_sw(CUtensorMap* map, const void* base, int rank, const uin
                                               : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(B2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return B2_OK;
+}
+
+b2_status encode_tmap_padded_nhwc(CUtensorMap* map, const void* base, int B, int C, int H, int W, int64_t sn,
+                                  int64_t sh, int64_t sw, uint32_t box_rows) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_encode_im2col) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q{};
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return set_error(B2_ERR_CUDA, "cuTensorMapEncodeIm2col entry point unavailable");
+      g_encode_im2col = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(fn);
+    }
+  }
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(B2_ERR_UNSUPPORTED, "TMA base address %p not 16-byte aligned", base);
+  if (C % 8 || sw % 8 || sh % 8 || sn % 8 || sw < C || box_rows < 1 || box_rows > 256)
+    return set_error(B2_ERR_UNSUPPORTED, "channels-last operand: C and the pixel strides must be multiples of 8");
+  cuuint64_t gdim[4] = {cuuint64_t(C), cuuint64_t(W), cuuint64_t(H), cuuint64_t(B)};
+  cuuint64_t gstride[3] = {cuuint64_t(sw) * 2, cuuint64_t(sh) * 2, cuuint64_t(sn) * 2};
+  const int lower[2] = {-1, -1};  // the padded grid: one zero row / column before ...
+  const int upper[2] = {1, 1};    // ... and after the image
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  CUresult r = g_encode_im2col(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), gdim, gstride,
+                               lower, upper, 64, box_rows, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(B2_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d)", int(r));
   return B2_OK;
 }
 

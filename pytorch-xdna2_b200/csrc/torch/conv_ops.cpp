@@ -9,6 +9,9 @@
 //   dW        wgrad kernel over the dy rows and the x rows the forward kept,
 //             deferred until the gradient is first read (see deferred.cpp)
 //   dbias     sum of dy over (N, H, W)
+// Channels-last x and dy (C % 8 == 0) skip the padded-row copies: the kernels
+// read them in place through im2col TMA maps over the padded grid (the
+// *_nhwc entry points), and dbias is a channel sum of dy.
 // BF16 1x1 / stride 1 / no padding convolutions (contiguous NCHW or
 // channels-last, channel counts -- and H*W for NCHW -- multiples of 8) run as
 // tcgen05 GEMMs (b2_conv1x1_*): forward and dX one GEMM each, dW a split-K GEMM
@@ -442,6 +445,46 @@ bool env_flag(const char* name, bool dflt) {
   return s ? std::string(s) != "0" : dflt;
 }
 
+// Channels-last activations that the 3x3 kernels read in place through an
+// im2col TMA map (no padded-row copy): channel stride 1, C and the pixel
+// strides multiples of 8 elements, 16-byte aligned data.  XDNA_CONV_NHWC=0
+// packs them as NCHW inputs are packed (A/B switch).
+bool nhwc_enabled() {
+  static const bool on = env_flag("XDNA_CONV_NHWC", true);
+  return on;
+}
+
+// Every 3x3 layer reads channels-last activations in place (measured on
+// B200, all three directions together beat packing at every ResNet-50 and
+// sweep shape tried: B128 C64 56x56 to C512 7x7, B40 C128 36x36, B128 C256
+// 72x72); XDNA_CONV_NHWC=0 restores the padded-row copies.
+bool nhwc_layer(int64_t, int64_t) { return true; }
+
+bool nhwc_ok(const at::Tensor& t) {
+  if (!nhwc_enabled() || t.dim() != 4 || t.numel() == 0) return false;
+  if (!t.is_contiguous(at::MemoryFormat::ChannelsLast)) return false;
+  // channels-last contiguous: dense pixels of C channels (the library
+  // replaces the strides of size-1 dimensions by the dense ones)
+  if (t.size(1) % 8) return false;
+  return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
+}
+
+// dW from channels-last dY and x read in place (see launch_wgrad).
+void launch_wgrad_nhwc(const at::Tensor& dy, const at::Tensor& x, void* gw, at::ScalarType dtype,
+                       c10::DeviceIndex dev, int B, int Cin, int H, int W, int Cout) {
+  c10::cuda::CUDAGuard g(dev);
+  materialize(dy);
+  materialize(x);
+  const size_t ws_bytes = b2_conv3x3_wgrad_workspace_bytes(B, Cin, H, W, Cout);
+  at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
+  const int dt = dtype == at::kFloat ? B2_F32 : B2_BF16;
+  KernelTimer kt("conv3x3.wgrad", 18.0 * B * H * W * Cin * Cout, stream(dev));
+  XDNA_B2(b2_conv3x3_wgrad_nhwc(dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(), x.stride(0),
+                                x.stride(2), x.stride(3), gw, dt, B, Cin, H, W, Cout, ws.data_ptr(),
+                                size_t(ws.numel()) * 4, stream(dev)));
+  count_launch("conv3x3.wgrad", 2);  // igemm + split-K reduce
+}
+
 }  // namespace
 
 // Routing of the convolutions outside the 3x3 fast path (set_conv_paths).
@@ -493,18 +536,28 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
   c10::cuda::CUDAGuard g(input.device().index());
   const int B = int(input.size(0)), Cin = int(input.size(1)), H = int(input.size(2)), W = int(input.size(3));
   const int Cout = int(weight.size(0));
-  at::Tensor rows = pack_rows(input);
+  const bool in_place = nhwc_layer(Cin, Cout) && nhwc_ok(input);
+  at::Tensor rows;
+  if (in_place)
+    materialize(input);
+  else
+    rows = pack_rows(input);
   at::Tensor wk = pack_weight(weight, false);
   at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
   if (b.defined()) materialize(b);
   at::Tensor y = empty({B, Cout, H, W}, at::kBFloat16, input.device().index(), out_format(input));
   KernelTimer kt("conv3x3.fwd", 18.0 * B * H * W * Cin * Cout, stream(input.device().index()));
-  XDNA_B2(b2_conv3x3_fwd(rows.data_ptr(), wk.data_ptr(), b.defined() ? b.data_ptr() : nullptr, y.data_ptr(),
-                         y.stride(0), y.stride(1), y.stride(2), y.stride(3), B, Cin, H, W, Cout, 0,
-                         stream(input.device().index())));
+  if (in_place)
+    XDNA_B2(b2_conv3x3_fwd_nhwc(input.data_ptr(), input.stride(0), input.stride(2), input.stride(3), wk.data_ptr(),
+                                b.defined() ? b.data_ptr() : nullptr, y.data_ptr(), y.stride(0), y.stride(1),
+                                y.stride(2), y.stride(3), B, Cin, H, W, Cout, 0, stream(input.device().index())));
+  else
+    XDNA_B2(b2_conv3x3_fwd(rows.data_ptr(), wk.data_ptr(), b.defined() ? b.data_ptr() : nullptr, y.data_ptr(),
+                           y.stride(0), y.stride(1), y.stride(2), y.stride(3), B, Cin, H, W, Cout, 0,
+                           stream(input.device().index())));
   count_launch("conv3x3.fwd");
   // keep the packed input for the weight gradient when one will be needed
-  if (at::GradMode::is_enabled() && weight.requires_grad() && g_mode.load() > 1) attach_rows(input, rows);
+  if (!in_place && at::GradMode::is_enabled() && weight.requires_grad() && g_mode.load() > 1) attach_rows(input, rows);
   return y;
 }
 
@@ -552,8 +605,21 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
   const int Cout = int(weight.size(0));
   const c10::DeviceIndex dev = input.device().index();
   at::Tensor dx, dw, db;
+  // channels-last dY (and x, for dW) are read in place; otherwise packed rows
+  const bool dy_cl = nhwc_layer(Cin, Cout) && nhwc_ok(grad_output);
+  const bool both_cl = dy_cl && nhwc_ok(input);
   at::Tensor dy_rows;
-  if (output_mask[2]) {
+  if (dy_cl) materialize(grad_output);
+  if (output_mask[2] && dy_cl) {
+    db = empty({Cout}, grad_output.scalar_type(), dev);
+    const size_t ws_bytes = b2_channel_sum_nhwc_workspace_bytes(B, Cout, H, W);
+    at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
+    KernelTimer kt("channel_sum", 2.0 * B * H * W * Cout, stream(dev));
+    XDNA_B2(b2_channel_sum_nhwc_bf16(grad_output.data_ptr(), grad_output.stride(0), grad_output.stride(2),
+                                     grad_output.stride(3), B, Cout, H, W, db.data_ptr(), B2_BF16, ws.data_ptr(),
+                                     size_t(ws.numel()) * 4, stream(dev)));
+    count_launch("channel_sum", 2);
+  } else if (output_mask[2]) {
     // the dY packer also reduces dbias (one pass over dY, deterministic order)
     const int ch = chunks_of(Cout);
     dy_rows = empty({int64_t(B) * (H + 2) * (W + 2), int64_t(ch) * 64}, at::kBFloat16, dev);
@@ -565,20 +631,35 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
                                     grad_output.stride(2), grad_output.stride(3), B, Cout, H, W, ch, dy_rows.data_ptr(),
                                     db.data_ptr(), B2_BF16, ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
     count_launch("pack_rows_dbias", 3);  // pack + two channel-sum stages
-  } else {
+  } else if (!dy_cl) {
     dy_rows = pack_rows(grad_output);
   }
   if (output_mask[0]) {
     at::Tensor wkd = pack_weight(weight, true);
     dx = empty({B, Cin, H, W}, at::kBFloat16, dev, out_format(input));
     KernelTimer kt("conv3x3.dgrad", 18.0 * B * H * W * Cin * Cout, stream(dev));
-    XDNA_B2(b2_conv3x3_dgrad(dy_rows.data_ptr(), wkd.data_ptr(), dx.data_ptr(), dx.stride(0), dx.stride(1),
-                             dx.stride(2), dx.stride(3), B, Cout, H, W, Cin, stream(dev)));
+    if (dy_cl)
+      XDNA_B2(b2_conv3x3_dgrad_nhwc(grad_output.data_ptr(), grad_output.stride(0), grad_output.stride(2),
+                                    grad_output.stride(3), wkd.data_ptr(), dx.data_ptr(), dx.stride(0), dx.stride(1),
+                                    dx.stride(2), dx.stride(3), B, Cout, H, W, Cin, stream(dev)));
+    else
+      XDNA_B2(b2_conv3x3_dgrad(dy_rows.data_ptr(), wkd.data_ptr(), dx.data_ptr(), dx.stride(0), dx.stride(1),
+                               dx.stride(2), dx.stride(3), B, Cout, H, W, Cin, stream(dev)));
     count_launch("conv3x3.dgrad");
   }
   if (output_mask[1]) {
     dw = empty({Cout, Cin, 3, 3}, weight.scalar_type(), dev);
-    if (g_mode.load() > 1) {
+    if (g_mode.load() > 1 && both_cl) {
+      // dY and x themselves are the operands: the job keeps them alive, and a
+      // write into either (before_write) runs it first
+      auto job = [dy = grad_output, x = input, gw = dw.data_ptr(), dtype = dw.scalar_type(), dev, B, Cin, H, W,
+                  Cout]() { launch_wgrad_nhwc(dy, x, gw, dtype, dev, B, Cin, H, W, Cout); };
+      if (deferral_enabled())
+        defer_epilogue(dw, {grad_output, input}, nullptr, std::move(job));
+      else
+        job();
+    } else if (g_mode.load() > 1) {
+      if (!dy_rows.defined()) dy_rows = pack_rows(grad_output);
       at::Tensor x_rows = find_rows(input);
       if (!x_rows.defined()) x_rows = pack_rows(input);
       if (deferral_enabled()) {

@@ -47,6 +47,8 @@ SIGNATURES = {
     "b2_pack_rows_bf16": [vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp, vp],
     "b2_pack_rows_dbias_workspace_bytes": [i32, i32, i32, i32],
     "b2_pack_rows_dbias_bf16": [vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp, vp, i32, vp, sz, vp],
+    "b2_channel_sum_nhwc_workspace_bytes": [i32, i32, i32, i32],
+    "b2_channel_sum_nhwc_bf16": [vp, i64, i64, i64, i32, i32, i32, i32, vp, i32, vp, sz, vp],
     "b2_pack_weight_fwd_bf16": [vp, i32, i32, i32, vp, vp],
     "b2_pack_weight_dgrad_bf16": [vp, i32, i32, i32, vp, vp],
     "b2_nchw_to_nhwc_bf16": [vp, vp, i32, i32, i32, vp],
@@ -56,6 +58,9 @@ SIGNATURES = {
     "b2_conv3x3_wgrad_workspace_bytes": [i32, i32, i32, i32, i32],
     "b2_conv3x3_wgrad": [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, sz, vp],
     "b2_conv3x3_wgrad_noalloc": [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp],
+    "b2_conv3x3_fwd_nhwc": [vp, i64, i64, i64, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp],
+    "b2_conv3x3_dgrad_nhwc": [vp, i64, i64, i64, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp],
+    "b2_conv3x3_wgrad_nhwc": [vp, i64, i64, i64, vp, i64, i64, i64, vp, i32, i32, i32, i32, i32, i32, vp, sz, vp],
     "b2_conv3x3_wgrad_noalloc_max_bytes": [],
     "b2_gemm_bf16": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
                      i64, i64, i64, vp, i64, i64, i32, vp],
@@ -102,7 +107,7 @@ SIGNATURES = {
 _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz,
              "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
              "b2_conv1x1_wgrad_workspace_bytes": sz, "b2_direct_conv_weight_floats": sz, "b2_gemm_splitk_workspace_bytes": sz,
-             "b2_batch_norm_workspace_bytes": sz,
+             "b2_batch_norm_workspace_bytes": sz, "b2_channel_sum_nhwc_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 

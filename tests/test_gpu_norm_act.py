@@ -25,7 +25,7 @@ def _fresh(cuda, monkeypatch):
     xdna_train.register_xdna_device()
     xdna_train.set_npu_mode(2)
     xdna_train.reset_fallback_stats()
-    monkeypatch.setattr(regions, "_NORM_ACT_MIN_BYTES", 0)
+    monkeypatch.setattr(regions, "NORM_ACT_MIN_BYTES", 0)
     yield
 
 
@@ -111,7 +111,7 @@ def test_pairing_guard_and_fallbacks():
     bn_e.train()
     xt = torch.randn(4, 6, 6, 8).bfloat16().to(X).transpose(1, 3)
     yt = bn(xt)
-    assert getattr(yt, "_xdna_act_for", None) is None        # non-contiguous: eager
+    assert not regions.activation_pending(yt)                # non-contiguous: eager
     assert rel(act(yt), act_e(bn_e(xt))) < 0.01
     other = nn.BatchNorm2d(4, affine=False).to(X, torch.bfloat16)
     assert regions.fuse_norm_activation(other, nn.ReLU())
@@ -127,7 +127,7 @@ def test_pairing_guard_and_fallbacks():
     neg = nn.BatchNorm2d(8).to(X, torch.bfloat16)
     leak = nn.LeakyReLU(-0.1)
     regions.fuse_norm_activation(neg, leak)
-    assert getattr(neg(x), "_xdna_act_for", None) is None    # negative slope: eager
+    assert not regions.activation_pending(neg(x))            # negative slope: eager
 
 
 def test_inplace_change_of_saved_input_detected():
@@ -143,15 +143,15 @@ def test_inplace_change_of_saved_input_detected():
 
 
 def test_size_threshold(monkeypatch):
-    monkeypatch.setattr(regions, "_NORM_ACT_MIN_BYTES", 4_000_000)
+    monkeypatch.setattr(regions, "NORM_ACT_MIN_BYTES", 4_000_000)
     bs, a_s = make_pair(8, 0.2, 3)
     bs = bs.to(X, torch.bfloat16)
     regions.fuse_norm_activation(bs, a_s)
-    assert getattr(bs(torch.randn(2, 8, 4, 4).bfloat16().to(X)), "_xdna_act_for", None) is None
+    assert not regions.activation_pending(bs(torch.randn(2, 8, 4, 4).bfloat16().to(X)))
     bb, ab = make_pair(64, 0.2, 4)
     bb = bb.to(X, torch.bfloat16)
     regions.fuse_norm_activation(bb, ab)
-    assert getattr(bb(torch.randn(40, 64, 36, 36).bfloat16().to(X)), "_xdna_act_for", None) is not None
+    assert regions.activation_pending(bb(torch.randn(40, 64, 36, 36).bfloat16().to(X)))
 
 
 def test_deepcopy_keeps_a_working_pair():
@@ -162,4 +162,4 @@ def test_deepcopy_keeps_a_working_pair():
     x = torch.randn(4, 16, 10, 10).bfloat16().to(X)
     y = twin(x)
     assert rel(y, model(x)) < 1e-2
-    assert twin[0].__dict__["_xdna_pair"] is twin[1]
+    assert regions.paired_activation(twin[0]) is twin[1]

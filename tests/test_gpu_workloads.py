@@ -118,7 +118,7 @@ def test_config4_reference_stylenet_steps(fused, monkeypatch):
     the perceptual region and every BatchNorm+LeakyReLU pair fused or not,
     against the same seeded steps on the CPU BF16 path."""
     from xdna_train import regions
-    monkeypatch.setattr(regions, "_NORM_ACT_MIN_BYTES", 0)
+    monkeypatch.setattr(regions, "NORM_ACT_MIN_BYTES", 0)
 
     def run(dev, fuse):
         torch.manual_seed(0)

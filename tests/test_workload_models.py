@@ -65,28 +65,35 @@ def test_ref_style_loss_matches_region_pattern_and_falls_back_on_cpu():
 
 
 def test_norm_constants_are_cached_per_tensor_version():
-    mod = torch.nn.Module()
+    """The fused perceptual loss converts the normalisation's CPU mean / std
+    once per device, dtype and tensor version, not on every call."""
+    import types
+    fp = regions._FusedPerceptual(torch.nn.Module(), "perceptual_vgg")
     mean = torch.tensor([0.485, 0.456, 0.406])
     std = torch.tensor([0.229, 0.224, 0.225])
-    x = torch.zeros(1, 3, 2, 2, dtype=torch.bfloat16)
-    m1, s1 = regions._norm_constants(mod, mean, std, x)
+    norm = types.SimpleNamespace(mean=mean, std=std)
+    x = torch.ones(1, 3, 2, 2, dtype=torch.bfloat16)
+    xn, tn = fp._normalised(norm, x, x)
+    m1, s1 = fp.consts[3], fp.consts[4]
     assert m1.shape == (1, 3, 1, 1) and m1.dtype == torch.bfloat16
     assert torch.equal(m1.flatten(), mean.bfloat16()) and torch.equal(s1.flatten(), std.bfloat16())
-    m2, s2 = regions._norm_constants(mod, mean, std, x)
-    assert m2 is m1 and s2 is s1  # no second conversion
+    assert torch.equal(xn, (x - m1) / s1) and torch.equal(tn, xn)
+    fp._normalised(norm, x, x)
+    assert fp.consts[3] is m1 and fp.consts[4] is s1  # no second conversion
     mean.mul_(2.0)  # an in-place write bumps the version: converted again
-    m3, _ = regions._norm_constants(mod, mean, std, x)
-    assert m3 is not m1 and torch.equal(m3.flatten(), mean.bfloat16())
-    other = mean.clone()  # another tensor object with the same values is not the cached one
-    m4, _ = regions._norm_constants(mod, other, std, x)
-    assert m4 is not m3
-    # a float32 input gets float32 constants (the key includes the dtype)
-    m5, _ = regions._norm_constants(mod, other, std, x.float())
-    assert m5.dtype == torch.float32
-    # constants that are not tensors are converted on every call
-    la, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
-    lb, _ = regions._norm_constants(mod, [0.5, 0.5, 0.5], [0.2, 0.2, 0.2], x)
-    assert la is not lb and torch.equal(la, lb)
+    fp._normalised(norm, x, x)
+    assert fp.consts[3] is not m1 and torch.equal(fp.consts[3].flatten(), mean.bfloat16())
+    m3 = fp.consts[3]
+    other = types.SimpleNamespace(mean=mean.clone(), std=std)  # another tensor object: not the cached one
+    fp._normalised(other, x, x)
+    assert fp.consts[3] is not m3
+    fp._normalised(other, x.float(), x.float())  # the key includes the dtype
+    assert fp.consts[3].dtype == torch.float32
+    # constants that are not tensors are converted on every call (nothing cached)
+    lists = types.SimpleNamespace(mean=[0.5, 0.5, 0.5], std=[0.2, 0.2, 0.2])
+    keep = fp.consts
+    a, _ = fp._normalised(lists, x, x)
+    assert fp.consts is keep and torch.equal(a, (x - 0.5) / 0.2)
 
 
 def test_conv_sweep_summary():
