@@ -1336,6 +1336,82 @@ def adam_probe(args):
                       "kernels": xdna_train.kernel_stats()}), flush=True)
 
 
+# The MLP's GEMMs at batch 512: (M, N, K, transA, transB)
+# for each layer's forward (x . W^T), input gradient (dY . W) and weight
+# gradient (dY^T . x), as nn.Linear's autograd issues them.
+def mlp_gemm_shapes(batch=512, dims=(1024, 4096, 4096, 4096, 1024)):
+    out = []
+    for fi, fo in zip(dims[:-1], dims[1:]):
+        out.append((f"fwd {fi}->{fo}", batch, fo, fi, 0, 1))
+        out.append((f"dX {fo}->{fi}", batch, fi, fo, 0, 0))
+        out.append((f"dW {fo}x{fi}", fo, fi, batch, 1, 0))
+    return out
+
+
+def gemm_probe(args):
+    """Device time of b2_gemm_bf16 on the MLP's GEMM shapes (``--gemm-probe``),
+    beside cuBLAS (torch.matmul on CUDA tensors) for the same product: CUDA
+    events around 20 back-to-back calls after warm-up, the median of
+    ``--iters`` timings; TFLOP/s = 2*M*N*K / time against the measured burst
+    peak.  The ncu small case of the GEMM kernel."""
+    from xdna_train import _abi
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    st = torch.cuda.current_stream()
+    peak, _, kind = peaks()
+    reps = 20
+
+    def med(fn):
+        ts = []
+        for i in range(args.iters + 3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                fn()
+            e1.record(st)
+            torch.cuda.synchronize()
+            if i >= 3:
+                ts.append(e0.elapsed_time(e1) / reps)
+        return sorted(ts)[len(ts) // 2]
+
+    rows, tot_o, tot_l, tot_f = [], 0.0, 0.0, 0.0
+    shapes = mlp_gemm_shapes(args.batch if args.batch != B_PER_GPU else 512)
+    if args.shape_index >= 0:
+        shapes = [shapes[args.shape_index]]
+    for name, M, N, K, ta, tb in shapes:
+        g = torch.Generator(device=dev).manual_seed(M + N + K)
+        A = torch.randn(K if ta else M, M if ta else K, generator=g, device=dev).bfloat16()
+        Bm = torch.randn(N if tb else K, K if tb else N, generator=g, device=dev).bfloat16()
+        D = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+        lda, ldb = A.shape[1], Bm.shape[1]
+        s = st.cuda_stream
+        wsb = _abi.lib().b2_gemm_bf16_workspace_bytes(M, N, K, 1)
+        ws = torch.empty(max(16, wsb), dtype=torch.uint8, device=dev)
+        ours = med(lambda: _abi.call("b2_gemm_bf16_ws", ta, tb, M, N, K, 1.0, A.data_ptr(), lda, 0, Bm.data_ptr(),
+                                     ldb, 0, 0.0, None, _abi.B2_BF16, 0, 0, 0, D.data_ptr(), N, 0, 1, ws.data_ptr(),
+                                     wsb, s))
+        opA = A.t() if ta else A
+        opB = Bm.t() if tb else Bm
+        lib = med(lambda: torch.matmul(opA, opB))
+        ref = torch.matmul(opA.float(), opB.float())
+        err = ((D.float() - ref).abs().max() / ref.abs().max()).item()
+        fl = 2.0 * M * N * K
+        tot_o += ours
+        tot_l += lib
+        tot_f += fl
+        row = {"shape": name, "M": M, "N": N, "K": K, "split_k_workspace": wsb,
+               "ours_us": round(ours * 1e3, 2), "cublas_us": round(lib * 1e3, 2),
+               "ours_tflops": round(fl / (ours * 1e-3) / 1e12, 1), "frac": round(fl / (ours * 1e-3) / 1e12 / peak, 4),
+               "max_rel_err": round(err, 5)}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+    print(json.dumps({"probe": "MLP GEMMs (BASELINE configs[2])", "ours_us_total": round(tot_o * 1e3, 1),
+                      "cublas_us_total": round(tot_l * 1e3, 1),
+                      "ours_tflops": round(tot_f / (tot_o * 1e-3) / 1e12, 1),
+                      "cublas_tflops": round(tot_f / (tot_l * 1e-3) / 1e12, 1), "peak_tflops": peak,
+                      "peak_kind": kind}), flush=True)
+
+
 # ResNet-50's 1x1 convolutions at stride 1: (H*W, Cin, Cout) per layer kind
 RESNET50_1X1 = [(3136, 64, 64), (3136, 64, 256), (3136, 256, 64), (3136, 256, 128), (784, 128, 512),
                 (784, 512, 128), (784, 512, 256), (196, 256, 1024), (196, 1024, 256), (196, 1024, 512),
@@ -1422,9 +1498,10 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--kernel-probe", action="store_true")
     ap.add_argument("--conv1x1-probe", action="store_true")
+    ap.add_argument("--gemm-probe", action="store_true", help="b2_gemm_bf16 on the MLP's GEMM shapes vs cuBLAS")
     ap.add_argument("--conv-sweep", action="store_true", help="BASELINE configs[1]: every shape of the 3x3 sweep")
     ap.add_argument("--sweep-one", action="store_true", help="--conv-sweep: only --batch/--channels/--hw")
-    ap.add_argument("--shape-index", type=int, default=-1, help="--conv1x1-probe: one shape of the list")
+    ap.add_argument("--shape-index", type=int, default=-1, help="--conv1x1-probe / --gemm-probe: one shape of the list")
     ap.add_argument("--style-plain-only", action="store_true",
                     help="--workload style: the eager plain-loss variant only (launch-list captures)")
     ap.add_argument("--bn-probe", action="store_true")
@@ -1460,6 +1537,9 @@ def main():
         return
     if args.conv1x1_probe:
         conv1x1_probe(args)
+        return
+    if args.gemm_probe:
+        gemm_probe(args)
         return
     if args.adam_probe:
         adam_probe(args)

@@ -226,6 +226,23 @@ b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
                        int64_t c_sb, void* D, int64_t ldd, int64_t strideD,
                        int batch, void* stream);
 
+/* b2_gemm_bf16 with room for split-K partial sums: when the output has too
+ * few 128-row tiles to occupy the SMs (a 512-row activation GEMM with 1024
+ * output columns has 32), the reduction is split and the fp32 partials,
+ * summed in split order (deterministic), get alpha and beta * C in a second
+ * pass.  Workspace bytes: b2_gemm_bf16_workspace_bytes (0: no split for this
+ * shape; a smaller or NULL workspace runs unsplit).  Same results as
+ * b2_gemm_bf16 up to the fp32 summation order. */
+size_t b2_gemm_bf16_workspace_bytes(int M, int N, int K, int batch);
+b2_status b2_gemm_bf16_ws(int transA, int transB, int M, int N, int K,
+                          float alpha, const void* A, int64_t lda,
+                          int64_t strideA, const void* B, int64_t ldb,
+                          int64_t strideB, float beta, const void* C,
+                          int c_dtype, int64_t c_sm, int64_t c_sn,
+                          int64_t c_sb, void* D, int64_t ldd, int64_t strideD,
+                          int batch, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
 /* ---- multi-tensor fused Adam / AdamW ---------------------------------- */
 
 /* One parameter tensor of a fused step (device pointers; host struct). */

@@ -629,16 +629,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (all 256 columns) and releases the accumulator buffer through the leader's
 // "tmem empty" barrier.  Same bounded waits as the single-CTA kernel.
 // ---------------------------------------------------------------------------
-template <int STAGES, int KIND>
+template <int STAGES, int KIND, int PBN = 256, bool A_MN = (KIND == kWgrad), bool B_MN = (KIND == kWgrad)>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     igemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                       const Params p) {
-  static_assert(KIND == kConv || KIND == kWgrad, "pair kernel: conv or wgrad");
-  constexpr bool MN = KIND == kWgrad;  // wgrad: both operands M/N-major
-  constexpr int BN = 256;        // N per pair tile
-  constexpr int kBHalf = 128;    // B rows each CTA loads
+  static_assert(PBN == 256 || PBN == 128, "pair tile width");
+  constexpr int BN = PBN;            // N per pair tile
+  constexpr int kBHalf = PBN / 2;    // B rows each CTA loads
   constexpr int kStageBytes = kABytes + kBHalf * BK * 2;
-  constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, MN, MN);
+  constexpr uint32_t kIdesc = idesc_bf16_f32(256, BN, A_MN, B_MN);
   constexpr uint32_t kTmemCols = 2 * BN;
 
   extern __shared__ uint8_t smem_raw[];
@@ -683,10 +682,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // conv: tiles (256-pixel block, 256-channel block); wgrad: (split, 256-co
-  // block, tap, 256-ci block), as in decode_tile with M tiles of 256
-  const int ntiles = KIND == kConv ? p.tiles_m * p.tiles_n : p.splits * p.tiles_m * 9 * p.ci_blocks;
+  // block, tap, 256-ci block); GEMM: (slice or split, 256-row block, PBN-column
+  // block) -- as in decode_tile with M tiles of 256
+  const int ntiles = KIND == kConv   ? p.tiles_m * p.tiles_n
+                     : KIND == kGemm ? p.batch * p.tiles_m * p.tiles_n
+                                     : p.splits * p.tiles_m * 9 * p.ci_blocks;
   auto decode = [&](int t, int& mt, int& nt, int& split, int& tap, int& kb0, int& kb1) {
-    if (KIND == kConv) {
+    if (KIND == kGemm) {
+      nt = t % p.tiles_n;
+      t /= p.tiles_n;
+      mt = t % p.tiles_m;
+      split = t / p.tiles_m;  // batch slice, or split-K range
+      tap = 0;
+      kb0 = p.gemm_split ? split * p.kb_per_split : 0;
+      kb1 = p.gemm_split ? min(p.num_kb, kb0 + p.kb_per_split) : p.num_kb;
+    } else if (KIND == kConv) {
       nt = t % p.tiles_n;
       mt = t / p.tiles_n;
       split = 0;
@@ -737,6 +747,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             load_rows<true>(sa, &tma_a, fb, chunk * BK, row0 + dy * p.wp + dx, p.src_im2col & 1, p.wp,
                             p.wp * p.hp);
             tma_load_3d_pair(sb, &tma_b, fb, kb * BK, nt * BN + int(rank) * kBHalf, 0);
+          } else if constexpr (KIND == kGemm) {
+            // this CTA's 128 rows of A and its half of the tile's B columns
+            const int za = (p.gemm_split || p.a_bcast) ? 0 : split, zb = p.gemm_split ? 0 : split;
+            const int k0 = kb * BK;
+            const int n0 = nt * BN + int(rank) * kBHalf;
+            if constexpr (A_MN) {
+              tma_load_3d_pair(sa, &tma_a, fb, row0, k0, za);
+              tma_load_3d_pair(sa + 8192, &tma_a, fb, row0 + 64, k0, za);
+            } else {
+              tma_load_3d_pair(sa, &tma_a, fb, k0, row0, za);
+            }
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int h = 0; h < kBHalf / 64; ++h) tma_load_3d_pair(sb + h * 8192, &tma_b, fb, n0 + h * 64, k0, zb);
+            } else {
+              tma_load_3d_pair(sb, &tma_b, fb, k0, n0, zb);
+            }
           } else {
             // A = dY rows (co contiguous), this CTA's 128 co; B = X rows shifted by the tap
             const int dy = tap / 3, dx = tap - dy * 3;
@@ -796,8 +823,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + kABytes;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024) : smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024) : smem_desc_sw128(sb + k * 32, 16, 1024);
+            const uint64_t ad = A_MN ? smem_desc_sw128(sa + k * 2048, 8192, 1024) : smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(sb + k * 2048, 8192, 1024) : smem_desc_sw128(sb + k * 32, 16, 1024);
             tc_mma_pair(d_tmem, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(smem_u32(&empty[stage]), uint16_t(0x3));
@@ -844,7 +871,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int col0 = nt * BN + half * (BN / 2) + j * 32;
         if constexpr (KIND == kConv)
           epi_conv(p, obase, col0, lane, r);
-        else
+        else if constexpr (KIND == kGemm) {
+          if (p.gemm_split)
+            epi_gemm_partial(p, split, grow, col0, r);
+          else
+            epi_gemm(p, split, mt * 2 + int(rank), col0, row, lane, r);
+        } else
           epi_wgrad_co(p, split, tap, grow, col0, r);
       }
       tc_fence_before();
@@ -1484,7 +1516,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 // D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
-                                         void* D, int d_dtype, long long ldd) {
+                                         void* D, int d_dtype, long long ldd, float beta = 0.f,
+                                         const void* C = nullptr, int c_dtype = B2_BF16, long long c_sm = 0,
+                                         long long c_sn = 0) {
   const long long total = (long long)M * N;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -1492,6 +1526,10 @@ __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int 
     for (int k = 0; k < splits; ++k) s += partial[k * total + i];
     s *= alpha;
     const long long m = i / N, n = i - m * N;
+    if (beta != 0.f) {
+      const long long ci = m * c_sm + n * c_sn;
+      s += beta * (c_dtype == B2_F32 ? static_cast<const float*>(C)[ci] : bf2f(static_cast<const uint16_t*>(C)[ci]));
+    }
     if (d_dtype == B2_F32)
       static_cast<float*>(D)[m * ldd + n] = s;
     else
@@ -1558,10 +1596,12 @@ constexpr int kGemmStages128 = 5;
 constexpr int kGemmStages256 = 3;
 constexpr int kStagesPair = 6;
 
-template <int KIND>
+template <int KIND, int PBN = 256, bool A_MN = (KIND == kWgrad), bool B_MN = (KIND == kWgrad)>
 b2_status launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles, cudaStream_t st) {
-  auto kern = igemm_pair_kernel<kStagesPair, KIND>;
-  constexpr size_t smem = size_t(kStagesPair) * (kABytes + 128 * BK * 2) + 1024 + 256;
+  // 128-wide pair tiles stage 24 KB per k-block: two more stages fit
+  constexpr int kSt = PBN == 256 ? kStagesPair : kStagesPair + 2;
+  auto kern = igemm_pair_kernel<kSt, KIND, PBN, A_MN, B_MN>;
+  constexpr size_t smem = size_t(kSt) * (kABytes + (PBN / 2) * BK * 2) + 1024 + 256;
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   static bool configured[64] = {};
@@ -1675,6 +1715,19 @@ bool patch_wgrad_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("B2_WGRAD_PATCH");
     return !e || e[0] != '0';
+  }();
+  return on;
+}
+
+// SM-pair tiles for GEMMs only with B2_GEMM_PAIR=1: measured on B200 they
+// run no faster than the single-CTA tiles on the MLP's shapes (M = 512:
+// 27 us for 512 x 4096 x 4096 either way, 12.4 against 10.6 us for the
+// weight gradients; ncu: both latency-bound, tensor pipe ~47 % of active
+// cycles with L2 at 23-27 % of peak), so they are off by default.
+bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_GEMM_PAIR");
+    return e && e[0] == '1';
   }();
   return on;
 }
@@ -1953,10 +2006,31 @@ struct GemmCall {
   bool partial_is_d = false;  // one split, fp32 D with ldd == N: the partial is D itself
 };
 
+// Output tile width: the widest that still hands most SMs a tile (a 512-row
+// GEMM with 256-wide tiles would leave over half of 148 SMs idle); narrow
+// outputs (1x1 convolutions with 64 channels, stems) take 64-wide tiles, so
+// no MMA or epilogue work falls on padding columns.
+int gemm_tile_n(int M, int N, int batch, int sms) {
+  const long long tm = (M + BM - 1) / BM;
+  int bn = N > 128 ? 256 : N > 64 ? 128 : 64;
+  while (bn > 64 && tm * ((N + bn - 1) / bn) * batch < (long long)sms * 3 / 4) bn /= 2;
+  return bn;
+}
+
+// Split-K of a plain GEMM whose tiles occupy under half of the SMs: enough
+// splits for about one wave, at least 4 k-blocks each, at most 8.
+int gemm_plain_splits(int M, int N, int K, int batch, int sms) {
+  if (batch != 1) return 1;
+  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + gemm_tile_n(M, N, 1, sms) - 1) / gemm_tile_n(M, N, 1, sms));
+  const long long kb = (K + BK - 1) / BK;
+  if (tiles * 2 > sms || kb < 8) return 1;
+  return int(std::max<long long>(1, std::min<long long>({(long long)sms / tiles, kb / 4, 8})));
+}
+
 b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
-  // narrow outputs (1x1 convolutions with 64 channels, stems) take 64-wide
-  // tiles: no MMA or epilogue work on padding columns
-  const int BN = g.N > 128 ? 256 : g.N > 64 ? 128 : 64;
+  int dev = 0;
+  B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+  const int BN = gemm_tile_n(g.M, g.N, g.partial ? 1 : g.batch, sm_count(dev));
   const uint64_t bt = uint64_t(g.batch);
   const uint64_t bta = g.a_bcast ? 1 : bt;
   CUtensorMap ta, tb;
@@ -1991,6 +2065,7 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
   p.a_bcast = g.a_bcast ? 1 : 0;
   p.splits = 1;
   if (g.partial) {
+    // alpha and beta * C are applied by the reduction
     p.gemm_split = 1;
     p.kb_per_split = (p.num_kb + std::max(1, g.splits) - 1) / std::max(1, g.splits);
     p.batch = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;  // tile-space slices = splits
@@ -2028,9 +2103,49 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
       p.tma_store = 1;
     }
   }
-  const int tiles = p.batch * p.tiles_m * p.tiles_n;
   const bool amn = g.transA != 0, bmn = g.transB == 0;
   b2_status rc;
+  // SM-pair tiles (256 rows x PBN columns, tcgen05.mma.cta_group::2): each SM
+  // stages its own 128 A rows and half of the tile's B columns, so per MMA it
+  // moves a quarter (PBN 256) to an eighth less from L2 than a single-CTA
+  // tile.  Taken when the pair tiles still give most SMs work.
+  int pbn = 0;
+  if (gemm_pair_enabled() && !g.k_batched && g.M > 128 && g.N > 64) {
+    const long long tm2 = (g.M + 255) / 256;
+    for (int c : {256, 128}) {
+      if (c == 256 && g.N <= 128) continue;
+      if (2 * tm2 * ((g.N + c - 1) / c) * p.batch >= (long long)sm_count(dev) * 3 / 4) {
+        pbn = c;
+        break;
+      }
+    }
+  }
+  if (pbn) {
+    Params pp = p;
+    pp.tiles_m = (g.M + 255) / 256;
+    pp.tiles_n = (g.N + pbn - 1) / pbn;
+    pp.tma_store = 0;
+    if (g.transB) {  // re-encode B (K-major, stored [N][K]): a box is this CTA's half of the tile's columns
+      const uint64_t bt2 = uint64_t(g.batch);
+      const uint64_t dims[3] = {uint64_t(g.K), uint64_t(g.N), bt2};
+      const uint64_t strides[2] = {uint64_t(g.ldb) * 2, uint64_t(bt2 > 1 ? g.strideB : g.ldb * g.N) * 2};
+      const uint32_t box[3] = {64, uint32_t(pbn / 2), 1};
+      B2_TRY(encode_tmap(&tb, g.B, 3, dims, strides, box, true));
+    }
+    const int ptiles = pp.batch * pp.tiles_m * pp.tiles_n;
+    if (pbn == 256) {
+      if (!amn && !bmn) rc = launch_pair<kGemm, 256, false, false>(ta, tb, pp, ptiles, st);
+      else if (!amn && bmn) rc = launch_pair<kGemm, 256, false, true>(ta, tb, pp, ptiles, st);
+      else if (amn && !bmn) rc = launch_pair<kGemm, 256, true, false>(ta, tb, pp, ptiles, st);
+      else rc = launch_pair<kGemm, 256, true, true>(ta, tb, pp, ptiles, st);
+    } else {
+      if (!amn && !bmn) rc = launch_pair<kGemm, 128, false, false>(ta, tb, pp, ptiles, st);
+      else if (!amn && bmn) rc = launch_pair<kGemm, 128, false, true>(ta, tb, pp, ptiles, st);
+      else if (amn && !bmn) rc = launch_pair<kGemm, 128, true, false>(ta, tb, pp, ptiles, st);
+      else rc = launch_pair<kGemm, 128, true, true>(ta, tb, pp, ptiles, st);
+    }
+  } else {
+  const int tiles = p.batch * p.tiles_m * p.tiles_n;
   if (BN == 256) {
     if (!amn && !bmn) rc = launch<256, kGemmStages256, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
     else if (!amn && bmn) rc = launch<256, kGemmStages256, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
@@ -2047,18 +2162,20 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
     else if (amn && !bmn) rc = launch<64, kGemmStages64, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
     else rc = launch<64, kGemmStages64, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
   }
+  }
   if (rc != B2_OK || !p.gemm_split || g.partial_is_d) return rc;
   const long long total = (long long)g.M * g.N;
   const int threads = 256;
   const int blocks = int(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads, 148LL * 8)));
-  gemm_split_reduce_kernel<<<blocks, threads, 0, st>>>(g.partial, p.batch, g.M, g.N, g.alpha, g.D, g.d_dtype, g.ldd);
+  gemm_split_reduce_kernel<<<blocks, threads, 0, st>>>(g.partial, p.batch, g.M, g.N, g.alpha, g.D, g.d_dtype, g.ldd,
+                                                       g.beta, g.C, g.c_dtype, g.c_sm, g.c_sn);
   return check_cuda(cudaGetLastError(), "gemm split reduce launch");
 }
 
 // Split-K plan for a reduction-heavy GEMM (1x1 wgrad): enough splits for one
 // wave over the SMs, at least 16 k-blocks per split.
 int gemm_splits(int M, int N, long long num_kb, int sms) {
-  const int BN = N > 128 ? 256 : N > 64 ? 128 : 64;
+  const int BN = gemm_tile_n(M, N, 1, sms);
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   long long splits = tiles >= sms ? 1 : sms / tiles;
   splits = std::max<long long>(1, std::min<long long>(splits, num_kb / 16));
@@ -2252,6 +2369,22 @@ b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
                        float beta, const void* C, int c_dtype, int64_t c_sm, int64_t c_sn,
                        int64_t c_sb, void* D, int64_t ldd, int64_t strideD, int batch,
                        void* stream) {
+  return b2_gemm_bf16_ws(transA, transB, M, N, K, alpha, A, lda, strideA, Bm, ldb, strideB, beta, C, c_dtype, c_sm,
+                         c_sn, c_sb, D, ldd, strideD, batch, nullptr, 0, stream);
+}
+
+size_t b2_gemm_bf16_workspace_bytes(int M, int N, int K, int batch) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch != 1) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  const int sp = gemm_plain_splits(M, N, K, batch, sm_count(dev));
+  return sp > 1 ? size_t(sp) * size_t(M) * size_t(N) * sizeof(float) : 0;
+}
+
+b2_status b2_gemm_bf16_ws(int transA, int transB, int M, int N, int K, float alpha, const void* A, int64_t lda,
+                          int64_t strideA, const void* Bm, int64_t ldb, int64_t strideB, float beta, const void* C,
+                          int c_dtype, int64_t c_sm, int64_t c_sn, int64_t c_sb, void* D, int64_t ldd,
+                          int64_t strideD, int batch, void* workspace, size_t workspace_bytes, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (M < 0 || N < 0 || K < 0 || batch < 0) return set_error(B2_ERR_INVALID, "b2_gemm_bf16: negative size");
   if (M == 0 || N == 0 || batch == 0) return B2_OK;
@@ -2284,6 +2417,16 @@ b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha,
   g.ldd = ldd;
   g.strideD = strideD;
   g.batch = batch;
+  // too few output tiles for the SMs: split the reduction when the caller
+  // gave room for the fp32 partial sums (added in split order: deterministic)
+  const size_t need = b2_gemm_bf16_workspace_bytes(M, N, K, batch);
+  if (need > 0 && workspace && workspace_bytes >= need && aligned16(workspace)) {
+    int dev = 0;
+    B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
+    g.splits = gemm_plain_splits(M, N, K, batch, sm_count(dev));
+    g.partial = static_cast<float*>(workspace);
+    g.d_dtype = B2_BF16;
+  }
   return gemm_core(g, st);
 }
 

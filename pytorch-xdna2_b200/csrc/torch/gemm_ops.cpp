@@ -87,10 +87,14 @@ bool run_gemm(const at::Tensor& A, const at::Tensor& Bm, const at::Tensor& out, 
     beta = 0.f;
   }
   const c10::DeviceIndex dev = out.device().index();
+  // split-K room for GEMMs with too few output tiles (from the caching allocator)
+  const size_t ws_bytes = b2_gemm_bf16_workspace_bytes(int(M), int(N), int(K), int(batch));
+  at::Tensor ws;
+  if (ws_bytes) ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
   KernelTimer kt("gemm", 2.0 * double(M) * double(N) * double(K) * double(batch), stream(dev));
-  XDNA_B2(b2_gemm_bf16(a.trans, b.trans, int(M), int(N), int(K), alpha, a.ptr, a.ld, a.bstride, b.ptr, b.ld,
-                       b.bstride, beta, cptr, c_dtype, c_sm, c_sn, c_sb, out.data_ptr(), N, M * N, int(batch),
-                       stream(dev)));
+  XDNA_B2(b2_gemm_bf16_ws(a.trans, b.trans, int(M), int(N), int(K), alpha, a.ptr, a.ld, a.bstride, b.ptr, b.ld,
+                          b.bstride, beta, cptr, c_dtype, c_sm, c_sn, c_sb, out.data_ptr(), N, M * N, int(batch),
+                          ws_bytes ? ws.data_ptr() : nullptr, ws_bytes ? size_t(ws.numel()) * 4 : 0, stream(dev)));
   count_launch("gemm");
   return true;
 }

@@ -64,6 +64,9 @@ SIGNATURES = {
     "b2_conv3x3_wgrad_noalloc_max_bytes": [],
     "b2_gemm_bf16": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
                      i64, i64, i64, vp, i64, i64, i32, vp],
+    "b2_gemm_bf16_workspace_bytes": [i32, i32, i32, i32],
+    "b2_gemm_bf16_ws": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
+                        i64, i64, i64, vp, i64, i64, i32, vp, sz, vp],
     "b2_fused_adam": [C.POINTER(AdamTensor), i32, C.POINTER(AdamHparams), vp],
     "b2_fused_sgd": [C.POINTER(SgdTensor), i32, C.POINTER(SgdHparams), vp],
     "b2_region_sqdiff_sum_bf16": [vp, vp, i64, vp, vp],
@@ -108,6 +111,7 @@ _RESTYPES = {"b2_last_error": C.c_char_p, "b2_conv3x3_wgrad_workspace_bytes": sz
              "b2_pack_rows_dbias_workspace_bytes": sz, "b2_region_bn_workspace_bytes": sz,
              "b2_conv1x1_wgrad_workspace_bytes": sz, "b2_direct_conv_weight_floats": sz, "b2_gemm_splitk_workspace_bytes": sz,
              "b2_batch_norm_workspace_bytes": sz, "b2_channel_sum_nhwc_workspace_bytes": sz,
+             "b2_gemm_bf16_workspace_bytes": sz,
              "b2_conv3x3_wgrad_noalloc_max_bytes": sz}
 
 

@@ -294,6 +294,74 @@ def test_gemm_batched_bias_alpha_beta(cuda):
     close(D[1], torch.from_numpy(o))
 
 
+@pytest.mark.parametrize("mnk", [(512, 1024, 4096), (512, 4096, 4096), (300, 200, 1024)])
+def test_gemm_split_k_with_workspace(cuda, mnk):
+    """b2_gemm_bf16_ws: split-K where the output has too few tiles for the SMs,
+    alpha and a broadcast bias (beta * C) applied by the ordered reduction;
+    within the GEMM bound of the unsplit kernel against fp32."""
+    M, N, K = mnk
+    g = torch.Generator().manual_seed(M * 7 + N)
+    A = torch.randn(M, K, generator=g).bfloat16()
+    Bt = torch.randn(N, K, generator=g).bfloat16()  # transB storage, as nn.Linear's weight
+    bias = torch.randn(N, generator=g).bfloat16()
+    Ad, Bd, bd = A.to(cuda), Bt.to(cuda), bias.to(cuda)
+    L = _abi.lib()
+    wsb = L.b2_gemm_bf16_workspace_bytes(M, N, K, 1)
+    if mnk[:2] == (512, 1024):
+        assert wsb > 0  # 32 output tiles of 148 SMs: split
+    ws = torch.empty(max(16, wsb), dtype=torch.uint8, device=cuda)
+    D = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    D0 = torch.empty_like(D)
+    for out, w, wb in ((D, ws.data_ptr(), wsb), (D0, None, 0)):
+        _abi.call("b2_gemm_bf16_ws", 0, 1, M, N, K, 0.5, Ad.data_ptr(), K, 0, Bd.data_ptr(), K, 0, 1.0, bd.data_ptr(),
+                  _abi.B2_BF16, 0, 1, 0, out.data_ptr(), N, 0, 1, w, wb, st())
+    torch.cuda.synchronize()
+    ref = 0.5 * (A.float() @ Bt.float().t()) + bias.float()
+    close(D, ref)
+    close(D0, ref)
+
+
+def test_gemm_sm_pair_tiles_in_a_subprocess(cuda):
+    """The SM-pair GEMM tiles (B2_GEMM_PAIR=1, read once per process): every
+    transpose combination, 256- and 128-wide pair tiles, a bias epilogue and
+    split-K partials, against fp32 -- run in a child process with the switch
+    set."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import sys, torch
+sys.path[:0] = [sys.argv[1], sys.argv[2]]
+from xdna_train import _abi
+d = torch.device("cuda", 0)
+st = torch.cuda.current_stream().cuda_stream
+L = _abi.lib()
+for (M, N, K) in [(512, 4096, 1024), (1024, 2048, 512), (2048, 4096, 256), (512, 1024, 4096)]:
+    for ta in (0, 1):
+        for tb in (0, 1):
+            g = torch.Generator().manual_seed(M + N + K + 2 * ta + tb)
+            A = torch.randn(M, K, generator=g).bfloat16(); Bm = torch.randn(K, N, generator=g).bfloat16()
+            bias = torch.randn(N, generator=g).bfloat16()
+            a = (A.t().contiguous() if ta else A).to(d); b = (Bm.t().contiguous() if tb else Bm).to(d)
+            D = torch.empty(M, N, dtype=torch.bfloat16, device=d)
+            wsb = L.b2_gemm_bf16_workspace_bytes(M, N, K, 1)
+            ws = torch.empty(max(16, wsb), dtype=torch.uint8, device=d)
+            _abi.call("b2_gemm_bf16_ws", ta, tb, M, N, K, 1.0, a.data_ptr(), a.shape[1], 0, b.data_ptr(), b.shape[1],
+                      0, 1.0, bias.to(d).data_ptr(), _abi.B2_BF16, 0, 1, 0, D.data_ptr(), N, 0, 1, ws.data_ptr(),
+                      wsb, st)
+            torch.cuda.synchronize()
+            ref = A.float() @ Bm.float() + bias.float()
+            err = (D.float().cpu() - ref).abs().max().item()
+            assert err <= 2e-2 * ref.abs().max().item(), (M, N, K, ta, tb, err)
+print("ok")
+'''
+    repo = Path(__file__).resolve().parent.parent
+    env = dict(os.environ, B2_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", code, str(repo / "pytorch-xdna2_b200"), str(repo)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
 # ------------------------------------------------------------------------ Adam
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
