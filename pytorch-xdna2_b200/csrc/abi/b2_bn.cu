@@ -33,6 +33,8 @@
 // written; the second reads of tensors smaller than L2 hit L2), 12 B/elem with
 // the activation (y read twice too).  NHWC forward: x once for the sums.
 #include <algorithm>
+#include <climits>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -698,6 +700,285 @@ __global__ void __launch_bounds__(kBnThreads) bn_nhwc_dx_kernel(
   }
 }
 
+// ============================ NHWC streaming ================================
+// The channels-last passes fed through shared memory.  Each CTA streams 8 KB
+// chunks of its inputs (chunks b, b + G, b + 2G, ... of the 16-byte-unit
+// array, u = pixel * CV + channel group) through a ring of stages that one
+// producer warp fills with 1-D bulk copies (no multicast): ~96 KB per CTA in
+// flight, two CTAs per SM, where the register kernels above keep at most four
+// loads per thread outstanding.  256 consumer threads take units t and t + 256
+// of every chunk; with CV dividing 256 a thread's channel group is t % CV in
+// every chunk, so its per-channel coefficients stay in registers.  Element for
+// element the same arithmetic as the register kernels (the sums kernel adds in
+// another, still fixed, order).  Rounding to bf16 uses the hardware's
+// round-to-nearest-even conversion, with NaNs sent through f2bf so that their
+// bits stay the reference's.
+constexpr int kStreamConsumers = 256;
+constexpr int kStreamThreads = kStreamConsumers + 32;
+constexpr int kChunkUnits = 512;
+constexpr int kChunkBytes = kChunkUnits * 16;
+constexpr int kRingBytes = 96 * 1024;
+
+template <int NIN>
+__host__ __device__ constexpr int ring_stages() {
+  return kRingBytes / (NIN * kChunkBytes);
+}
+template <int NIN>
+__host__ __device__ constexpr size_t ring_smem_bytes() {
+  return size_t(kRingBytes) + 2 * sizeof(uint64_t) * ring_stages<NIN>() + 16;
+}
+
+__device__ __forceinline__ uint32_t pack_bf2_fast(float lo, float hi) {
+  if (lo != lo || hi != hi) return pack_bf2(lo, hi);
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint4 pack8_fast(const float* r) {
+  return make_uint4(pack_bf2_fast(r[0], r[1]), pack_bf2_fast(r[2], r[3]), pack_bf2_fast(r[4], r[5]),
+                    pack_bf2_fast(r[6], r[7]));
+}
+__device__ __forceinline__ float round_bf_fast(float v) {
+  return v != v ? round_bf(v) : __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ float bn_tail_fast(float z, bool has_res, float res, bool relu) {
+  float v = round_bf_fast(z);
+  if (has_res) v = round_bf_fast(__fadd_rn(v, res));
+  if (relu && !(v > 0.0f) && v == v) v = 0.0f;
+  return v;
+}
+
+// Named barrier over the consumer threads (the producer warp has returned).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kStreamConsumers) : "memory");
+}
+
+// Calls f(u, v) on the consumer threads for every unit u of this CTA's chunks,
+// v[i] = src[i][u].  Returns false on a consumer whose wait gave up (status
+// recorded, the other roles told through the CTA's abort flag), and on the
+// producer warp, which returns once its last copy is issued.
+template <int NIN, class F>
+__device__ __forceinline__ bool stream_units(const uint4* const (&src)[NIN], long long units, F&& f, int* status) {
+  constexpr int S = ring_stages<NIN>();
+  extern __shared__ __align__(128) uint8_t ring[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kRingBytes);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kStreamConsumers / 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const long long nchunks = (units + kChunkUnits - 1) / kChunkUnits;
+  if (warp == kStreamConsumers / 32) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int last[S];
+#pragma unroll
+      for (int i = 0; i < S; ++i) last[i] = -1;
+      bool ok = true;
+      for (long long j = blockIdx.x; j < nchunks; j += gridDim.x) {
+        if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const long long u0 = j * kChunkUnits;
+        const uint32_t bytes = uint32_t(units - u0 < kChunkUnits ? units - u0 : kChunkUnits) * 16u;
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_arrive_expect_tx(fb, uint32_t(NIN) * bytes);
+        last[s] = int(ph);
+#pragma unroll
+        for (int i = 0; i < NIN; ++i)
+          bulk_load_1d(smem_u32(ring + (s * NIN + i) * kChunkBytes), src[i] + u0, bytes, fb);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok)  // let the copies already issued land before the CTA can exit
+        for (int i = 0; i < S; ++i)
+          if (last[i] >= 0) mbar_wait(smem_u32(&full[i]), uint32_t(last[i]), status, nullptr);
+    }
+    return false;
+  }
+  int s = 0;
+  uint32_t ph = 0;
+  for (long long j = blockIdx.x; j < nchunks; j += gridDim.x) {
+    if (!mbar_wait(smem_u32(&full[s]), ph, status, abort_flag)) return false;
+    const long long u0 = j * kChunkUnits;
+    const int n = int(units - u0 < kChunkUnits ? units - u0 : kChunkUnits);
+    const uint4* stg = reinterpret_cast<const uint4*>(ring + s * NIN * kChunkBytes);
+    for (int k = threadIdx.x; k < n; k += kStreamConsumers) {
+      uint4 v[NIN];
+#pragma unroll
+      for (int i = 0; i < NIN; ++i) v[i] = stg[i * kChunkUnits + k];
+      f(u0 + k, v);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
+    if (++s == S) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+  return true;
+}
+
+// Sums per CTA and channel (as bn_nhwc_sums_kernel): forward a = sum(x - K),
+// b = sum((x - K)^2), K the first pixel; backward a = sum(dz), b = sum(dz *
+// xhat).  Inputs in ring order x, dy, y.
+template <bool BWD, bool ACT>
+__global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_sums_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y,
+    const float* __restrict__ mean, const float* __restrict__ invstd, NhwcShape sh, float slope, int relu,
+    float* __restrict__ part_a, float* __restrict__ part_b, int* status) {
+  constexpr int NIN = BWD ? (ACT ? 3 : 2) : 1;
+  const bool consumer = threadIdx.x < kStreamConsumers;
+  const int cg = threadIdx.x % sh.CV;
+  float a[8], b[8], k0[8], k1[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) a[e] = b[e] = k0[e] = k1[e] = 0.0f;
+  if (consumer) {
+    if constexpr (BWD) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        k0[e] = mean[cg * 8 + e];
+        k1[e] = invstd[cg * 8 + e];
+      }
+    } else {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(x) + cg), k0);  // shift K: the first pixel
+    }
+  }
+  const uint4* src[NIN];
+  src[0] = reinterpret_cast<const uint4*>(x);
+  if constexpr (BWD) src[1] = reinterpret_cast<const uint4*>(dy);
+  if constexpr (ACT) src[NIN - 1] = reinterpret_cast<const uint4*>(y);
+  const bool ok = stream_units<NIN>(src, sh.P * sh.CV, [&](long long, const uint4(&v)[NIN]) {
+    float fx[8];
+    unpack8(v[0], fx);
+    if constexpr (BWD) {
+      float fg[8], fy[8];
+      unpack8(v[1], fg);
+      if constexpr (ACT) unpack8(v[NIN - 1], fy);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float dz = bn_dz<ACT>(fg[e], ACT ? fy[e] : 0.0f, slope, relu);
+        a[e] = __fadd_rn(a[e], dz);
+        b[e] = __fadd_rn(b[e], __fmul_rn(dz, __fmul_rn(__fsub_rn(fx[e], k0[e]), k1[e])));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = __fsub_rn(fx[e], k0[e]);
+        a[e] = __fadd_rn(a[e], d);
+        b[e] = __fadd_rn(b[e], __fmul_rn(d, d));
+      }
+    }
+  }, status);
+  if (!consumer) return;
+  // the rows R = 256 / CV of each channel group, reduced in row order through
+  // the ring's memory (every copy into it has landed)
+  extern __shared__ __align__(128) uint8_t ring[];
+  float* red = reinterpret_cast<float*>(ring);  // [2][R][C]
+  const int R = kStreamConsumers / sh.CV, r = threadIdx.x / sh.CV;
+  consumers_sync();
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red[r * sh.C + cg * 8 + e] = a[e];
+    red[(R + r) * sh.C + cg * 8 + e] = b[e];
+  }
+  consumers_sync();
+  if (!ok) return;
+  for (int c = threadIdx.x; c < sh.C; c += kStreamConsumers) {
+    float sa = 0.0f, sb = 0.0f;
+    for (int q = 0; q < R; ++q) {
+      sa = __fadd_rn(sa, red[q * sh.C + c]);
+      sb = __fadd_rn(sb, red[(R + q) * sh.C + c]);
+    }
+    part_a[(long long)c * gridDim.x + blockIdx.x] = sa;  // channel-major
+    part_b[(long long)c * gridDim.x + blockIdx.x] = sb;
+  }
+}
+
+// y = act(x*scale + shift), or the fused tail (residual, ReLU) with EPI.
+template <bool EPI, bool RES>
+__global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_apply_kernel(
+    const uint16_t* __restrict__ x, BnChan ch, const float* __restrict__ mean, const float* __restrict__ invstd,
+    uint16_t* __restrict__ y, NhwcShape sh, float slope, const uint16_t* __restrict__ res, int relu, int* status) {
+  constexpr int NIN = RES ? 2 : 1;
+  float scale[8], shift[8];
+  if (threadIdx.x < kStreamConsumers) {
+    const int c0 = int(threadIdx.x % sh.CV) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      scale[e] = __fmul_rn(ld_par(ch.w, ch.pdtype, c0 + e, 1.0f), invstd[c0 + e]);
+      shift[e] = __fsub_rn(ld_par(ch.b, ch.pdtype, c0 + e, 0.0f), __fmul_rn(mean[c0 + e], scale[e]));
+    }
+  }
+  const uint4* src[NIN];
+  src[0] = reinterpret_cast<const uint4*>(x);
+  if constexpr (RES) src[1] = reinterpret_cast<const uint4*>(res);
+  uint4* y4 = reinterpret_cast<uint4*>(y);
+  const bool rl = relu != 0;
+  stream_units<NIN>(src, sh.P * sh.CV, [&](long long u, const uint4(&v)[NIN]) {
+    float f[8], r[8];
+    unpack8(v[0], f);
+    if constexpr (EPI) {
+      float q[8];
+      if constexpr (RES) unpack8(v[1], q);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        r[e] = bn_tail_fast(__fadd_rn(__fmul_rn(f[e], scale[e]), shift[e]), RES, RES ? q[e] : 0.0f, rl);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = bn_act(f[e], scale[e], shift[e], slope);
+    }
+    y4[u] = pack8_fast(r);
+  }, status);
+}
+
+// dx = w*invstd*(dz - k1 - xhat*k2); inputs in ring order dy, x, y.
+template <bool ACT>
+__global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_dx_kernel(
+    const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y, const uint16_t* __restrict__ x, const void* w,
+    int pdtype, const float* __restrict__ mean, const float* __restrict__ invstd, const float* __restrict__ k,
+    uint16_t* __restrict__ dx, NhwcShape sh, float slope, int relu, int* status) {
+  constexpr int NIN = ACT ? 3 : 2;
+  float ws[8], mc[8], is[8], k1[8], k2[8];
+  if (threadIdx.x < kStreamConsumers) {
+    const int c0 = int(threadIdx.x % sh.CV) * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = c0 + e;
+      ws[e] = __fmul_rn(ld_par(w, pdtype, c, 1.0f), invstd[c]);
+      mc[e] = mean[c];
+      is[e] = invstd[c];
+      k1[e] = k[c];
+      k2[e] = k[sh.C + c];
+    }
+  }
+  const uint4* src[NIN];
+  src[0] = reinterpret_cast<const uint4*>(dy);
+  src[1] = reinterpret_cast<const uint4*>(x);
+  if constexpr (ACT) src[2] = reinterpret_cast<const uint4*>(y);
+  uint4* d4 = reinterpret_cast<uint4*>(dx);
+  stream_units<NIN>(src, sh.P * sh.CV, [&](long long u, const uint4(&v)[NIN]) {
+    float fg[8], fy[8], fx[8], r[8];
+    unpack8(v[0], fg);
+    unpack8(v[1], fx);
+    if constexpr (ACT) unpack8(v[NIN - 1], fy);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
+    d4[u] = pack8_fast(r);
+  }, status);
+}
+
 // ============================ launchers =====================================
 
 // Warp-per-plane when there are enough planes to fill the GPU with warps,
@@ -710,19 +991,52 @@ int stats_grid(long long planes, bool warp, int sms) {
 }
 
 // Blocks of `kfn` resident per SM (cached per kernel and shared-memory size).
-int resident_blocks(const void* kfn, size_t smem) {
+int resident_blocks(const void* kfn, size_t smem, int threads = kBnThreads) {
   static std::mutex mu;
   static std::map<std::pair<const void*, size_t>, int> cache;
   std::lock_guard<std::mutex> lk(mu);
   auto it = cache.find({kfn, smem});
   if (it != cache.end()) return it->second;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, kBnThreads, smem) != cudaSuccess || n < 1) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, threads, smem) != cudaSuccess || n < 1) {
     cudaGetLastError();
     n = 1;
   }
   cache[{kfn, smem}] = n;
   return n;
+}
+
+// The shared-memory streaming kernels run unless B2_BN_STREAM=0 (A/B switch),
+// for channel counts whose groups divide the consumer threads.
+bool stream_ok(const NhwcShape& sh) {
+  static const bool on = [] {
+    const char* e = std::getenv("B2_BN_STREAM");
+    return !e || e[0] != '0';
+  }();
+  return on && kStreamConsumers % sh.CV == 0;
+}
+
+// Grid of a streaming kernel: one wave of resident CTAs, at most one per
+// chunk and at most `cap`; raises the kernel's shared-memory limit first
+// (once per device).
+template <typename K>
+int stream_grid(K* kfn, size_t smem, long long units, int sms, long long cap) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, bool> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto key = std::make_pair(reinterpret_cast<const void*>(kfn), dev);
+    if (!done.count(key)) {
+      if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+        cudaGetLastError();
+      done[key] = true;
+    }
+  }
+  const long long chunks = (units + kChunkUnits - 1) / kChunkUnits;
+  const long long wave = (long long)sms * resident_blocks(reinterpret_cast<const void*>(kfn), smem, kStreamThreads);
+  return int(std::max<long long>(1, std::min({chunks, wave, cap})));
 }
 
 // Grid-stride kernels: one full wave of resident blocks (no partial last
@@ -805,14 +1119,22 @@ b2_status bn_stats(const uint16_t* x, int layout, const BnChan& ch, float* mean_
   if (layout == 1) {
     B2_TRY(check_nhwc(C, {x}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
-    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
-    const long long blocks =
-        nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
-                                                              &bn_nhwc_sums_kernel<false, false>), red));
     float* pa = static_cast<float*>(workspace);
+    long long blocks;
+    if (stream_ok(sh)) {
+      auto kfn = &bn_nhwc_stream_sums_kernel<false, false>;
+      constexpr size_t smem = ring_smem_bytes<1>();
+      blocks = stream_grid(kfn, smem, sh.P * sh.CV, sms, nhwc_blocks(sh));
+      kfn<<<int(blocks), kStreamThreads, smem, st>>>(x, nullptr, nullptr, nullptr, nullptr, sh, 0.0f, 0, pa,
+                                                      pa + blocks * C, device_status_ptr());
+    } else {
+      const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+      blocks = nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
+                                                                    &bn_nhwc_sums_kernel<false, false>), red));
+      bn_nhwc_sums_kernel<false, false><<<int(blocks), kBnThreads, red, st>>>(x, nullptr, nullptr, nullptr, nullptr,
+                                                                              sh, 0.0f, 0, pa, pa + blocks * C);
+    }
     float* pb = pa + blocks * C;
-    bn_nhwc_sums_kernel<false, false><<<int(blocks), kBnThreads, red, st>>>(x, nullptr, nullptr, nullptr, nullptr,
-                                                                            sh, 0.0f, 0, pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc sums launch"));
     bn_nhwc_stats_kernel<<<int(C), kMergeThreads, 0, st>>>(x, pa, pb, blocks, C, sh.P, eps,
                                                                           momentum, ch, mean_out, invstd_out);
@@ -844,7 +1166,19 @@ b2_status bn_apply_launch(const uint16_t* x, int layout, const BnChan& ch, const
   if (layout == 1) {
     B2_TRY(check_nhwc(C, {x, y, res}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
-    if (kBnThreads % sh.CV == 0)
+    if (stream_ok(sh)) {
+      if (EPI && res) {
+        auto kfn = &bn_nhwc_stream_apply_kernel<EPI, true>;
+        constexpr size_t smem = ring_smem_bytes<2>();
+        kfn<<<stream_grid(kfn, smem, sh.P * sh.CV, sms, LLONG_MAX), kStreamThreads, smem, st>>>(
+            x, ch, mean, invstd, y, sh, slope, res, relu, device_status_ptr());
+      } else {
+        auto kfn = &bn_nhwc_stream_apply_kernel<EPI, false>;
+        constexpr size_t smem = ring_smem_bytes<1>();
+        kfn<<<stream_grid(kfn, smem, sh.P * sh.CV, sms, LLONG_MAX), kStreamThreads, smem, st>>>(
+            x, ch, mean, invstd, y, sh, slope, nullptr, relu, device_status_ptr());
+      }
+    } else if (kBnThreads % sh.CV == 0)
       bn_nhwc_apply_kernel<true, EPI><<<wave_grid(&bn_nhwc_apply_kernel<true, EPI>, 0, sh.P * sh.CV, sms),
                                         kBnThreads, 0, st>>>(x, ch, mean, invstd, y, sh, slope, res, relu);
     else
@@ -884,20 +1218,34 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
   if (layout == 1) {
     B2_TRY(check_nhwc(C, {g, yy, xx, dx}, who));
     const NhwcShape sh = nhwc_shape(N, C, HW);
-    const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
-    const long long blocks =
-        nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
-                                                              &bn_nhwc_sums_kernel<true, ACT>), red));
+    const bool stream = stream_ok(sh);
     float* pa = static_cast<float*>(workspace);
+    long long blocks;
+    if (stream) {
+      auto kfn = &bn_nhwc_stream_sums_kernel<true, ACT>;
+      constexpr size_t smem = ring_smem_bytes<ACT ? 3 : 2>();
+      blocks = stream_grid(kfn, smem, sh.P * sh.CV, sms, nhwc_blocks(sh));
+      kfn<<<int(blocks), kStreamThreads, smem, st>>>(xx, g, yy, mean, invstd, sh, slope, relu, pa, pa + blocks * C,
+                                                      device_status_ptr());
+    } else {
+      const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
+      blocks = nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
+                                                                    &bn_nhwc_sums_kernel<true, ACT>), red));
+      bn_nhwc_sums_kernel<true, ACT><<<int(blocks), kBnThreads, red, st>>>(xx, g, yy, mean, invstd, sh, slope, relu,
+                                                                           pa, pa + blocks * C);
+    }
     float* pb = pa + blocks * C;
     float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(blocks) * C * sizeof(float)));
-    bn_nhwc_sums_kernel<true, ACT><<<int(blocks), kBnThreads, red, st>>>(xx, g, yy, mean, invstd, sh, slope, relu,
-                                                                         pa, pb);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd sums launch"));
     bn_bwd_channel_kernel<<<int(C), kMergeThreads, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
     B2_TRY(check_cuda(cudaGetLastError(), "bn nhwc bwd channel launch"));
     if (!dx) return B2_OK;
-    if (kBnThreads % sh.CV == 0)
+    if (stream) {
+      auto kfn = &bn_nhwc_stream_dx_kernel<ACT>;
+      constexpr size_t smem = ring_smem_bytes<ACT ? 3 : 2>();
+      kfn<<<stream_grid(kfn, smem, sh.P * sh.CV, sms, LLONG_MAX), kStreamThreads, smem, st>>>(
+          g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu, device_status_ptr());
+    } else if (kBnThreads % sh.CV == 0)
       bn_nhwc_dx_kernel<ACT, true><<<wave_grid(&bn_nhwc_dx_kernel<ACT, true>, 0, sh.P * sh.CV, sms), kBnThreads, 0,
                                                                                               st>>>(
           g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu);

@@ -107,9 +107,12 @@ template <int BN>
 constexpr int epi_box_bytes() {
   return 32 * epi_box_cols<BN>() * 2;
 }
-template <int KIND, int BN>
+// TS: the GEMM writes bf16 D through TMA stores of staged boxes (short
+// reductions, where the epilogue is the bottleneck); long reductions drop
+// the staging for a deeper operand ring and store directly.
+template <int KIND, int BN, bool TS = (KIND == kGemm)>
 constexpr int epi_stage_bytes() {
-  return KIND == kGemm ? kEpiWarps * 2 * epi_box_bytes<BN>() : 0;
+  return (KIND == kGemm && TS) ? kEpiWarps * 2 * epi_box_bytes<BN>() : 0;
 }
 
 __device__ __forceinline__ void decode_tile(int kind, const Params& p, int t, int& mt, int& nt,
@@ -324,7 +327,7 @@ __device__ __forceinline__ void epi_gemm_partial(const Params& p, int split, int
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
+template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN, bool TS = (KIND == kGemm)>
 __global__ void __launch_bounds__(kThreads, 1)
     igemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                  const __grid_constant__ CUtensorMap tma_b,
@@ -337,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* epi_stage = smem + STAGES * kStageBytes;  // 1024-aligned: stage sizes are KB multiples
-  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + epi_stage_bytes<KIND, BN>());
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_stage + epi_stage_bytes<KIND, BN, TS>());
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -539,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * (BN / 2));
-      if (KIND == kGemm && p.tma_store) {
+      if (KIND == kGemm && TS && p.tma_store) {
         // Stage each 32-row box of the warp's columns in shared memory (the
         // swizzle puts 16-byte chunk q of row `lane` at chunk q ^ (lane & 7)
         // for 128-byte rows, q ^ ((lane >> 1) & 3) for 64-byte rows, so the
@@ -1560,16 +1563,16 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw,
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, int KIND>
+template <int BN, int STAGES, int KIND, bool TS = (KIND == kGemm)>
 constexpr size_t smem_bytes() {
-  return size_t(STAGES) * Smem<BN>::kStageBytes + epi_stage_bytes<KIND, BN>() + 1024 /*align*/ + 256 /*barriers*/;
+  return size_t(STAGES) * Smem<BN>::kStageBytes + epi_stage_bytes<KIND, BN, TS>() + 1024 /*align*/ + 256 /*barriers*/;
 }
 
-template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN>
+template <int BN, int STAGES, int KIND, bool A_MN, bool B_MN, bool TS = (KIND == kGemm)>
 b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles,
                  cudaStream_t st, const CUtensorMap* td = nullptr) {
-  auto kern = igemm_kernel<BN, STAGES, KIND, A_MN, B_MN>;
-  constexpr size_t smem = smem_bytes<BN, STAGES, KIND>();
+  auto kern = igemm_kernel<BN, STAGES, KIND, A_MN, B_MN, TS>;
+  constexpr size_t smem = smem_bytes<BN, STAGES, KIND, TS>();
   static_assert(smem <= 232448, "shared memory per block");
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
@@ -1583,7 +1586,9 @@ b2_status launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, 
   if (tiles <= 0) return B2_OK;
   const int grid = std::min(tiles, sm_count(dev));
   static const CUtensorMap kNoMap{};  // kinds without a TMA store never read it
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, td ? *td : kNoMap, p);
+  Params q = p;
+  if (!TS) q.tma_store = 0;
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, td ? *td : kNoMap, q);
   return check_cuda(cudaGetLastError(), "igemm launch");
 }
 
@@ -1594,6 +1599,9 @@ constexpr int kStages256 = 4;
 constexpr int kGemmStages64 = 8;
 constexpr int kGemmStages128 = 5;
 constexpr int kGemmStages256 = 3;
+constexpr int kGemmDeep64 = 9;  // without the store staging
+constexpr int kGemmDeep128 = 7;
+constexpr int kGemmDeep256 = 4;
 constexpr int kStagesPair = 6;
 
 template <int KIND, int PBN = 256, bool A_MN = (KIND == kWgrad), bool B_MN = (KIND == kWgrad)>
@@ -1730,6 +1738,15 @@ bool gemm_pair_enabled() {
     return e && e[0] == '1';
   }();
   return on;
+}
+
+template <int BN, int STAGES, bool TS>
+b2_status launch_gemm(bool amn, bool bmn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int tiles,
+                      cudaStream_t st, const CUtensorMap* td) {
+  if (!amn && !bmn) return launch<BN, STAGES, kGemm, false, false, TS>(ta, tb, p, tiles, st, td);
+  if (!amn && bmn) return launch<BN, STAGES, kGemm, false, true, TS>(ta, tb, p, tiles, st, td);
+  if (amn && !bmn) return launch<BN, STAGES, kGemm, true, false, TS>(ta, tb, p, tiles, st, td);
+  return launch<BN, STAGES, kGemm, true, true, TS>(ta, tb, p, tiles, st, td);
 }
 
 // SM-pair MMA for wide convolutions unless B2_PAIR_MMA=0 (A/B switch).
@@ -2004,15 +2021,18 @@ struct GemmCall {
   float* partial = nullptr;
   int d_dtype = B2_BF16;
   bool partial_is_d = false;  // one split, fp32 D with ldd == N: the partial is D itself
+  int bn = 0;                 // output tile width; 0: gemm_tile_n's choice
 };
 
 // Output tile width: the widest that still hands most SMs a tile (a 512-row
 // GEMM with 256-wide tiles would leave over half of 148 SMs idle); narrow
 // outputs (1x1 convolutions with 64 channels, stems) take 64-wide tiles, so
 // no MMA or epilogue work falls on padding columns.
+int gemm_widest_tile(int N) { return N > 128 ? 256 : N > 64 ? 128 : 64; }
+
 int gemm_tile_n(int M, int N, int batch, int sms) {
   const long long tm = (M + BM - 1) / BM;
-  int bn = N > 128 ? 256 : N > 64 ? 128 : 64;
+  int bn = gemm_widest_tile(N);
   while (bn > 64 && tm * ((N + bn - 1) / bn) * batch < (long long)sms * 3 / 4) bn /= 2;
   return bn;
 }
@@ -2030,7 +2050,7 @@ int gemm_plain_splits(int M, int N, int K, int batch, int sms) {
 b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
-  const int BN = gemm_tile_n(g.M, g.N, g.partial ? 1 : g.batch, sm_count(dev));
+  const int BN = g.bn ? g.bn : gemm_tile_n(g.M, g.N, g.partial ? 1 : g.batch, sm_count(dev));
   const uint64_t bt = uint64_t(g.batch);
   const uint64_t bta = g.a_bcast ? 1 : bt;
   CUtensorMap ta, tb;
@@ -2146,21 +2166,22 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
     }
   } else {
   const int tiles = p.batch * p.tiles_m * p.tiles_n;
-  if (BN == 256) {
-    if (!amn && !bmn) rc = launch<256, kGemmStages256, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
-    else if (!amn && bmn) rc = launch<256, kGemmStages256, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
-    else if (amn && !bmn) rc = launch<256, kGemmStages256, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
-    else rc = launch<256, kGemmStages256, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
+  // split-K partials are fp32 and never go through the TMA-store staging:
+  // its shared memory buys more operand stages instead.  (Plain GEMMs keep
+  // the staging even for long reductions: without it the direct stores of
+  // a one-tile-per-SM grid cost more than the deeper ring gains -- measured
+  // on B200, 512 x 4096 x 4096 26.2 against 26.8 us, 4096 x 4096 x 512 23.6
+  // against 28.1 us.)
+  if (p.gemm_split) {
+    if (BN == 256) rc = launch_gemm<256, kGemmDeep256, false>(amn, bmn, ta, tb, p, tiles, st, nullptr);
+    else if (BN == 128) rc = launch_gemm<128, kGemmDeep128, false>(amn, bmn, ta, tb, p, tiles, st, nullptr);
+    else rc = launch_gemm<64, kGemmDeep64, false>(amn, bmn, ta, tb, p, tiles, st, nullptr);
+  } else if (BN == 256) {
+    rc = launch_gemm<256, kGemmStages256, true>(amn, bmn, ta, tb, p, tiles, st, tdp);
   } else if (BN == 128) {
-    if (!amn && !bmn) rc = launch<128, kGemmStages128, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
-    else if (!amn && bmn) rc = launch<128, kGemmStages128, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
-    else if (amn && !bmn) rc = launch<128, kGemmStages128, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
-    else rc = launch<128, kGemmStages128, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
+    rc = launch_gemm<128, kGemmStages128, true>(amn, bmn, ta, tb, p, tiles, st, tdp);
   } else {
-    if (!amn && !bmn) rc = launch<64, kGemmStages64, kGemm, false, false>(ta, tb, p, tiles, st, tdp);
-    else if (!amn && bmn) rc = launch<64, kGemmStages64, kGemm, false, true>(ta, tb, p, tiles, st, tdp);
-    else if (amn && !bmn) rc = launch<64, kGemmStages64, kGemm, true, false>(ta, tb, p, tiles, st, tdp);
-    else rc = launch<64, kGemmStages64, kGemm, true, true>(ta, tb, p, tiles, st, tdp);
+    rc = launch_gemm<64, kGemmStages64, true>(amn, bmn, ta, tb, p, tiles, st, tdp);
   }
   }
   if (rc != B2_OK || !p.gemm_split || g.partial_is_d) return rc;
@@ -2175,7 +2196,7 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
 // Split-K plan for a reduction-heavy GEMM (1x1 wgrad): enough splits for one
 // wave over the SMs, at least 16 k-blocks per split.
 int gemm_splits(int M, int N, long long num_kb, int sms) {
-  const int BN = gemm_tile_n(M, N, 1, sms);
+  const int BN = gemm_widest_tile(N);
   const long long tiles = (long long)((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   long long splits = tiles >= sms ? 1 : sms / tiles;
   splits = std::max<long long>(1, std::min<long long>(splits, num_kb / 16));
@@ -2475,6 +2496,7 @@ b2_status b2_gemm_splitk_bf16(int transA, int transB, int M, int N, int K, const
   g.ldd = ldd;
   g.d_dtype = d_dtype;
   g.splits = splits;
+  g.bn = gemm_widest_tile(N);  // the tile width gemm_splits planned for
   if (splits == 1 && d_dtype == B2_F32 && ldd == N && aligned16(D)) {
     g.partial = static_cast<float*>(D);
     g.partial_is_d = true;
@@ -2599,6 +2621,7 @@ b2_status b2_conv1x1_wgrad(const void* dy, const void* x, void* dw, int dw_dtype
   // split-K partials (also with one split: dW may be fp32), reduced in order
   g.splits = splits;
   g.partial = static_cast<float*>(workspace);
+  g.bn = gemm_widest_tile(int(Cin));  // the tile width gemm_splits planned for
   return gemm_core(g, st);
 }
 

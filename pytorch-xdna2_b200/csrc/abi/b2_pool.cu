@@ -94,32 +94,34 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_kernel(const T* __re
   }
 }
 
-// channels-last bf16, 8 channels per thread (C % 8 == 0, 16-byte aligned)
+// channels-last bf16, 8 channels per thread (C % 8 == 0, 16-byte aligned);
+// index type I as for the element-strided kernels
+template <typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const uint16_t* __restrict__ x, PoolGeom g,
                                                                          uint16_t* __restrict__ y,
                                                                          int64_t* __restrict__ ind) {
-  const long long cv = g.C / 8;
-  const long long total = g.N * g.OH * g.OW * cv;
-  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
-       u += (long long)gridDim.x * kPoolThreads) {
-    const long long q = u % cv, r = u / cv;
-    const long long ow = r % g.OW, oh = (r / g.OW) % g.OH, n = r / (g.OW * g.OH);
-    long long h0, h1, w0, w1;
-    window<long long>(oh, g.sh, g.ph, g.kh, g.dh, g.H, h0, h1);
-    window<long long>(ow, g.sw, g.pw, g.kw, g.dw, g.W, w0, w1);
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * OH * OW * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / OW, ow = r - r2 * OW;
+    const I n = r2 / OH, oh = r2 - n * OH;
+    I h0, h1, w0, w1;
+    window<I>(oh, g.sh, g.ph, g.kh, g.dh, H, h0, h1);
+    window<I>(ow, g.sw, g.pw, g.kw, g.dw, W, w0, w1);
     float best[8];
     long long bi[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       best[e] = -INFINITY;
-      bi[e] = h0 * g.W + w0;
+      bi[e] = (long long)(h0 * W + w0);
     }
-    const uint16_t* xp = x + n * g.xs[0] + q * 8;
-    for (long long h = h0; h < h1; h += g.dh)
-      for (long long w = w0; w < w1; w += g.dw) {
-        const uint4 v4 = *reinterpret_cast<const uint4*>(xp + h * g.xs[2] + w * g.xs[3]);
+    const uint16_t* xp = x + n * I(g.xs[0]) + q * 8;
+    for (I h = h0; h < h1; h += g.dh)
+      for (I w = w0; w < w1; w += g.dw) {
+        const uint4 v4 = *reinterpret_cast<const uint4*>(xp + h * I(g.xs[2]) + w * I(g.xs[3]));
         const uint32_t wd[4] = {v4.x, v4.y, v4.z, v4.w};
-        const long long idx = h * g.W + w;
+        const long long idx = (long long)(h * W + w);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const float v = __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const u
           }
         }
       }
-    const long long o = n * g.ys[0] + oh * g.ys[2] + ow * g.ys[3] + q * 8;
+    const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
     uint4 out;
     out.x = pack_bf2(best[0], best[1]);
     out.y = pack_bf2(best[2], best[3]);
@@ -169,25 +171,26 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_kernel(const T* __re
   }
 }
 
+template <typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_kernel(const uint16_t* __restrict__ dy,
                                                                          const int64_t* __restrict__ ind,
                                                                          PoolGeom g, uint16_t* __restrict__ dx) {
-  const long long cv = g.C / 8;
-  const long long total = g.N * g.H * g.W * cv;
-  for (long long u = (long long)blockIdx.x * kPoolThreads + threadIdx.x; u < total;
-       u += (long long)gridDim.x * kPoolThreads) {
-    const long long q = u % cv, r = u / cv;
-    const long long w = r % g.W, h = (r / g.W) % g.H, n = r / (g.W * g.H);
-    long long oh0, oh1, ow0, ow1;
-    covering<long long>(h, g.sh, g.ph, g.kh, g.dh, g.OH, oh0, oh1);
-    covering<long long>(w, g.sw, g.pw, g.kw, g.dw, g.OW, ow0, ow1);
-    const long long me = h * g.W + w;
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * H * W * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / W, w = r - r2 * W;
+    const I n = r2 / H, h = r2 - n * H;
+    I oh0, oh1, ow0, ow1;
+    covering<I>(h, g.sh, g.ph, g.kh, g.dh, OH, oh0, oh1);
+    covering<I>(w, g.sw, g.pw, g.kw, g.dw, OW, ow0, ow1);
+    const long long me = (long long)(h * W + w);
     float s[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) s[e] = 0.0f;
-    for (long long oh = oh0; oh < oh1; ++oh)
-      for (long long ow = ow0; ow < ow1; ++ow) {
-        const long long o = n * g.ys[0] + oh * g.ys[2] + ow * g.ys[3] + q * 8;
+    for (I oh = oh0; oh < oh1; ++oh)
+      for (I ow = ow0; ow < ow1; ++ow) {
+        const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
         const uint4 v4 = *reinterpret_cast<const uint4*>(dy + o);
         const uint32_t wd[4] = {v4.x, v4.y, v4.z, v4.w};
         const longlong2* ip = reinterpret_cast<const longlong2*>(ind + o);
@@ -203,7 +206,7 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_kernel(const u
     out.y = pack_bf2(s[2], s[3]);
     out.z = pack_bf2(s[4], s[5]);
     out.w = pack_bf2(s[6], s[7]);
-    *reinterpret_cast<uint4*>(dx + n * g.xs[0] + h * g.xs[2] + w * g.xs[3] + q * 8) = out;
+    *reinterpret_cast<uint4*>(dx + n * I(g.xs[0]) + h * I(g.xs[2]) + w * I(g.xs[3]) + q * 8) = out;
   }
 }
 
@@ -260,8 +263,11 @@ b2_status b2_maxpool2d_fwd(const void* x, const int64_t* x_strides, void* y, int
   if (!x || !y || !indices) return set_error(B2_ERR_INVALID, "b2_maxpool2d_fwd: null pointer");
   auto st = static_cast<cudaStream_t>(stream);
   const int sms = cur_sms();
-  if (dtype == B2_BF16 && nhwc8(g, x, y, indices))
-    maxpool_fwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+  if (dtype == B2_BF16 && nhwc8(g, x, y, indices) && fits32(g))
+    maxpool_fwd_nhwc8_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else if (dtype == B2_BF16 && nhwc8(g, x, y, indices))
+    maxpool_fwd_nhwc8_kernel<long long><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
   else if (dtype == B2_BF16 && fits32(g))
     maxpool_fwd_kernel<uint16_t, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(
@@ -290,8 +296,11 @@ b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices, const int64_t
   if (!dx || (N * C * OH * OW > 0 && (!dy || !indices))) return set_error(B2_ERR_INVALID, "b2_maxpool2d_bwd: null pointer");
   auto st = static_cast<cudaStream_t>(stream);
   const int sms = cur_sms();
-  if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices))
-    maxpool_bwd_nhwc8_kernel<<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+  if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices) && fits32(g))
+    maxpool_bwd_nhwc8_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices))
+    maxpool_bwd_nhwc8_kernel<long long><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
   else if (dtype == B2_BF16 && fits32(g))
     maxpool_bwd_kernel<uint16_t, int><<<pool_grid(total, sms), kPoolThreads, 0, st>>>(

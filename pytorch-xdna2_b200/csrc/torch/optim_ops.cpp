@@ -20,8 +20,10 @@ namespace {
 // works as long as all arrays of a parameter share it (channels-last conv
 // weights and their gradients and states are dense, not contiguous).
 bool dense_like(const at::Tensor& t, const at::Tensor& ref) {
-  return t.device().type() == kXdna && t.is_non_overlapping_and_dense() && t.sizes().equals(ref.sizes()) &&
-         t.strides().equals(ref.strides());
+  if (t.device().type() != kXdna || !t.is_non_overlapping_and_dense() || !t.sizes().equals(ref.sizes())) return false;
+  for (int64_t d = 0; d < t.dim(); ++d)  // the stride of a size-1 dimension addresses nothing
+    if (t.size(d) > 1 && t.stride(d) != ref.stride(d)) return false;
+  return true;
 }
 
 bool supported(at::TensorList params, at::TensorList grads, at::TensorList m, at::TensorList v,
