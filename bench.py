@@ -9,7 +9,11 @@ torchvision ResNet-50 on ``torch.device("xdna")``, cross-entropy, backward
 all-reduce), SGD momentum 0.9 (``--optimizer adam``: the config's Adam
 variant); with N GPUs the gradients are averaged by bucketed NCCL
 all-reduces overlapped with backward (``xdna_train.ddp``; data parallel, weak
-scaling).  ``value`` = images/s of the whole job; ``roofline`` = the 3x3
+scaling).  At one GPU the step is captured into a CUDA graph
+(``xdna_train.graphs.make_graphed_step``) and replayed, so the host's per-op
+dispatch (about as long as the step's kernels) is out of the timed region;
+``--eager`` times the step op by op, and the line carries the eager rate
+beside the replayed one.  ``value`` = images/s of the whole job; ``roofline`` = the 3x3
 convolution kernels' FLOPs over their device time inside the step (CUDA
 event pairs around each launch, on its stream); ``e2e`` = the same step fed
 from pinned host memory (images and labels copied every step, the loss read
@@ -536,9 +540,21 @@ def run_resnet50(args):
         opt.step()
         return loss
 
+    # two input buffers (the e2e loop fills one while the other is in use);
+    # with CUDA graphs (the default at one GPU: xdna_train.graphs, the step's
+    # kernels replayed without the host's per-op dispatch) one capture each
+    bx = [x.clone(memory_format=cl) for _ in range(2)]
+    by = [y.clone() for _ in range(2)]
+    graphed = world == 1 and not args.eager
     s = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        step(x, y)
+    if graphed:
+        from xdna_train import graphs
+        replays = [graphs.make_graphed_step(lambda i=i: step(bx[i], by[i]), warmup=args.warmup) for i in range(2)]
+        run = lambda i: replays[i]()  # noqa: E731
+    else:
+        for _ in range(args.warmup):
+            step(x, y)
+        run = lambda i: step(bx[i], by[i])  # noqa: E731
     torch.cuda.synchronize()
     xdna_train.reset_mapped_cpu_stats()
     if world > 1:
@@ -548,7 +564,7 @@ def run_resnet50(args):
     with Clocks(local) as clk:
         e0.record(s)
         for _ in range(args.steps):
-            loss = step(x, y)
+            loss = run(0)
         e1.record(s)
         torch.cuda.synchronize()
     if world > 1:
@@ -559,11 +575,9 @@ def run_resnet50(args):
     final_loss = float(loss.item())
 
     # ---- e2e: every step copies its images and labels from pinned host
-    # memory (on a copy stream, one step ahead, through two device buffers --
-    # what a prefetching loader does) and reads its loss back to the host
+    # memory (on a copy stream, one step ahead, through the two device buffers
+    # -- what a prefetching loader does) and reads its loss back to the host
     copy_s = torch.cuda.Stream()
-    bx = [torch.empty_like(x) for _ in range(2)]
-    by = [torch.empty_like(y) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     used = [torch.cuda.Event() for _ in range(2)]
     loss_host = torch.empty(max(1, args.steps), dtype=torch.float32, pin_memory=True)
@@ -589,7 +603,7 @@ def run_resnet50(args):
         s.wait_event(copied[i])
         if k + 1 < args.steps:
             prefetch(1 - i)
-        loss = step(bx[i], by[i])
+        loss = run(i)
         used[i].record(s)
         loss_host[k:k + 1].copy_(loss.detach().reshape(1), non_blocking=True)
     e3.record(s)
@@ -602,12 +616,29 @@ def run_resnet50(args):
     # ---- the 3x3 convolution kernels (and the other timed launch sites)
     # inside the same step: CUDA event pairs around each launch on its stream,
     # over a few more steps of the same workload
+    xdna_train.reset_mapped_cpu_stats()
     xdna_train.kernel_timer(True)
     for _ in range(3):
         step(x, y)
     torch.cuda.synchronize()
     xdna_train.kernel_timer(False)
     kt = xdna_train.kernel_times()
+    if graphed:  # a replay launches what the captured step launched
+        launches = sum(xdna_train.kernel_stats().values()) * args.steps // 3
+        fallbacks = {k: {**v, "calls": v["calls"] * args.steps // 3} for k, v in xdna_train.fallback_stats().items()}
+
+    # ---- the same step eagerly (host dispatch per op), for comparison
+    eager_ms = None
+    if graphed:
+        torch.cuda.synchronize()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ne = min(args.steps, 30)
+        ea.record(s)
+        for _ in range(ne):
+            step(x, y)
+        eb.record(s)
+        torch.cuda.synchronize()
+        eager_ms = ea.elapsed_time(eb) / ne
 
     # ---- the gradient all-reduce alone, per step (N > 1): every bucket's
     # collective, events on the launching stream
@@ -654,6 +685,8 @@ def run_resnet50(args):
                                   if world > 1 else ""),
                    "model": "resnet50", "global_batch": images, "per_gpu_batch": B, "image_hw": RESNET_HW,
                    "parallelism": f"dp{world}",
+                   "execution": ("CUDA graph replay of the captured step (xdna_train.graphs)" if graphed
+                                 else "eager"),
                    "l2": "inputs larger than L2 (the step's activations are tens of GB)",
                    "train_gflop_per_step_per_gpu": round(total_fl / 1e9, 1),
                    "conv3x3_s1_gflop_per_step_per_gpu": round(c33_fl / 1e9, 1)},
@@ -668,10 +701,15 @@ def run_resnet50(args):
                      "gflop_per_launch": round(c_work / max(1, c_launch) / 1e9, 3),
                      "ms_per_launch": round(c_ms / max(1, c_launch), 5),
                      "peak_kind": f"{peak_kind}, sustained (kernels timed inside a long step)"},
+        # work is FLOPs for the convolutions and GEMMs, algorithmic bytes for
+        # the BatchNorm passes ("bn.*", reported as GB/s)
         "kernel_times_per_step": {k: {"launches": round(v["launches"] / 3, 1), "ms": round(v["ms"] / 3, 4),
-                                      "tflops": round(v["work"] / (v["ms"] * 1e-3) / 1e12, 1) if v["ms"] else None}
+                                      ("gbs" if k.startswith("bn.") else "tflops"):
+                                      (round(v["work"] / (v["ms"] * 1e-3) / (1e9 if k.startswith("bn.") else 1e12), 1)
+                                       if v["ms"] else None)}
                                   for k, v in sorted(kt.items())},
         "step_tflops": round(total_fl / (ms * 1e-3) / 1e12, 1),
+        "eager_images_per_s": round(images / (eager_ms * 1e-3), 2) if eager_ms else None,
         "final_loss": round(final_loss, 4),
         "gpu_launches": launches,
         "clocks": clk.summary(),
@@ -1244,7 +1282,7 @@ def bn_probe(args):
     """Device time of training-mode BatchNorm2d forward + backward on one
     channels-last shape (``--bn-probe --batch B --channels C --hw H``), with the
     algorithmic bandwidth: forward 6 B/elem (x read by the sums and by the
-    apply pass, y written), backward 8 B/elem (dy and x read by the sums and
+    apply pass, y written), backward 10 B/elem (dy and x read by the sums and
     by the dx pass, dx written).  The ncu small case of the BatchNorm kernels."""
     import torch.nn as nn
 
@@ -1273,7 +1311,7 @@ def bn_probe(args):
         x.grad = None
     n = x.numel()
     out = {}
-    for k, bpe in (("fwd", 6), ("bwd", 8)):
+    for k, bpe in (("fwd", 6), ("bwd", 10)):
         ms = sorted(times[k])[len(times[k]) // 2]
         out[k] = {"ms": round(ms, 4), "gbs": round(bpe * n / (ms * 1e-3) / 1e9, 1)}
     print(json.dumps({"probe": f"BatchNorm2d channels-last B{b} C{c} HW{hw}", **out,
@@ -1520,6 +1558,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=None, help="warm-up steps (resnet50: 20, others: 5)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="resnet50: time the eager step, not its CUDA-graph replay")
     ap.add_argument("--channels-last", action="store_true", help="--workload conv: channels-last activations")
     args = ap.parse_args()
     if args.steps is None:

@@ -255,7 +255,7 @@ extern "C" b2_status b2_fused_adam(const b2_adam_tensor* tensors, int n, const b
   auto kern = hp->param_dtype == B2_F32
                   ? (hp->state_dtype == B2_F32 ? adam_kernel<float, float> : adam_kernel<float, uint16_t>)
                   : (hp->state_dtype == B2_F32 ? adam_kernel<uint16_t, float> : adam_kernel<uint16_t, uint16_t>);
-  const int psz = hp->param_dtype == B2_F32 ? 4 : 2, ssz = hp->state_dtype == B2_F32 ? 4 : 2;
+  const int psz = hp->param_dtype == B2_F32 ? 4 : 2;
   int dev = 0;
   B2_TRY(check_cuda(cudaGetDevice(&dev), "cudaGetDevice"));
   // one wave of resident blocks (occupancy of this instantiation, per device)

@@ -1518,6 +1518,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Deterministic split-K reduction: dw[co][ci][tap] = sum_s partial[s][tap][co][ci].
 // D[m][n] = alpha * (partial[0][m][n] + partial[1][m][n] + ...), in split order.
+// The same sum four columns at a time (N % 4 == 0, 16-byte aligned partials;
+// D rows aligned for 8-byte bf16 or 16-byte fp32 stores): a 2-D grid of
+// column groups x rows, no 64-bit index division, every split's load of a
+// group issued before the additions, which run in split order from +0.
+__global__ void __launch_bounds__(256) gemm_split_reduce_vec_kernel(const float4* __restrict__ partial, int splits,
+                                                                    int M, int N4, float alpha, void* D, int d_dtype,
+                                                                    long long ldd, float beta, const void* C,
+                                                                    int c_dtype, long long c_sm, long long c_sn) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= N4) return;
+  const long long plane4 = (long long)M * N4;
+  for (int m = blockIdx.y; m < M; m += gridDim.y) {
+    const long long i = (long long)m * N4 + q;
+    float4 v[8];
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < splits; k0 += 8) {
+      const int nk = splits - k0 < 8 ? splits - k0 : 8;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nk) v[k] = __ldg(partial + (long long)(k0 + k) * plane4 + i);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nk) {
+          acc.x += v[k].x;
+          acc.y += v[k].y;
+          acc.z += v[k].z;
+          acc.w += v[k].w;
+        }
+    }
+    float r[4] = {acc.x * alpha, acc.y * alpha, acc.z * alpha, acc.w * alpha};
+    const long long n0 = 4LL * q;
+    if (beta != 0.f) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const long long ci = m * c_sm + (n0 + e) * c_sn;
+        r[e] += beta * (c_dtype == B2_F32 ? static_cast<const float*>(C)[ci]
+                                          : bf2f(static_cast<const uint16_t*>(C)[ci]));
+      }
+    }
+    if (d_dtype == B2_F32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(D) + m * ldd + n0) = make_float4(r[0], r[1], r[2], r[3]);
+    } else {
+      *reinterpret_cast<uint2*>(static_cast<uint16_t*>(D) + m * ldd + n0) =
+          make_uint2(pack_bf2(r[0], r[1]), pack_bf2(r[2], r[3]));
+    }
+  }
+}
+
 __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, float alpha,
                                          void* D, int d_dtype, long long ldd, float beta = 0.f,
                                          const void* C = nullptr, int c_dtype = B2_BF16, long long c_sm = 0,
@@ -2024,27 +2072,29 @@ struct GemmCall {
   int bn = 0;                 // output tile width; 0: gemm_tile_n's choice
 };
 
-// Output tile width: the widest that still hands most SMs a tile (a 512-row
-// GEMM with 256-wide tiles would leave over half of 148 SMs idle); narrow
-// outputs (1x1 convolutions with 64 channels, stems) take 64-wide tiles, so
-// no MMA or epilogue work falls on padding columns.
+// Output tile width: the widest the output allows.  A tcgen05.mma of M = 128
+// and K = 16 occupies the tensor pipe for the same time whatever its N (up to
+// 256): measured on B200, back-to-back MMAs with operands resident in shared
+// memory take 138 cycles each at N = 64, 128 and 256, so a 128-wide tile runs
+// the pipe at half the rate of a 256-wide one.  Few output tiles are made up
+// for by splitting the reduction (gemm_plain_splits), not by narrower tiles.
 int gemm_widest_tile(int N) { return N > 128 ? 256 : N > 64 ? 128 : 64; }
 
-int gemm_tile_n(int M, int N, int batch, int sms) {
-  const long long tm = (M + BM - 1) / BM;
-  int bn = gemm_widest_tile(N);
-  while (bn > 64 && tm * ((N + bn - 1) / bn) * batch < (long long)sms * 3 / 4) bn /= 2;
-  return bn;
-}
+int gemm_tile_n(int /*M*/, int N, int /*batch*/, int /*sms*/) { return gemm_widest_tile(N); }
 
-// Split-K of a plain GEMM whose tiles occupy under half of the SMs: enough
-// splits for about one wave, at least 4 k-blocks each, at most 8.
+// Split-K of a plain GEMM whose tiles occupy under three quarters of the SMs:
+// enough splits for about one wave, at most 8, and at least 16 k-blocks per
+// split -- the fp32 partials and their ordered reduction cost a few
+// microseconds (measured on B200: 512 x 4096 x 1024 ran 10.4 us in 64 tiles
+// unsplit, 17 us in two splits of 8 k-blocks; 512 x 4096 x 4096 25 us either
+// as 128 narrow tiles or as 2 x 64 wide ones).
 int gemm_plain_splits(int M, int N, int K, int batch, int sms) {
   if (batch != 1) return 1;
-  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + gemm_tile_n(M, N, 1, sms) - 1) / gemm_tile_n(M, N, 1, sms));
+  const int bn = gemm_widest_tile(N);
+  const long long tiles = (long long)((M + BM - 1) / BM) * ((N + bn - 1) / bn);
   const long long kb = (K + BK - 1) / BK;
-  if (tiles * 2 > sms || kb < 8) return 1;
-  return int(std::max<long long>(1, std::min<long long>({(long long)sms / tiles, kb / 4, 8})));
+  if (tiles * 4 >= (long long)sms * 3) return 1;
+  return int(std::max<long long>(1, std::min<long long>({(long long)sms / tiles, kb / 16, 8})));
 }
 
 b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
@@ -2130,16 +2180,7 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
   // moves a quarter (PBN 256) to an eighth less from L2 than a single-CTA
   // tile.  Taken when the pair tiles still give most SMs work.
   int pbn = 0;
-  if (gemm_pair_enabled() && !g.k_batched && g.M > 128 && g.N > 64) {
-    const long long tm2 = (g.M + 255) / 256;
-    for (int c : {256, 128}) {
-      if (c == 256 && g.N <= 128) continue;
-      if (2 * tm2 * ((g.N + c - 1) / c) * p.batch >= (long long)sm_count(dev) * 3 / 4) {
-        pbn = c;
-        break;
-      }
-    }
-  }
+  if (gemm_pair_enabled() && !g.k_batched && g.M > 128 && BN == 256) pbn = 256;
   if (pbn) {
     Params pp = p;
     pp.tiles_m = (g.M + 255) / 256;
@@ -2187,6 +2228,16 @@ b2_status gemm_core(const GemmCall& g, cudaStream_t st) {
   if (rc != B2_OK || !p.gemm_split || g.partial_is_d) return rc;
   const long long total = (long long)g.M * g.N;
   const int threads = 256;
+  const bool dvec = g.d_dtype == B2_F32 ? (aligned16(g.D) && g.ldd % 4 == 0)
+                                        : ((reinterpret_cast<uintptr_t>(g.D) & 7) == 0 && g.ldd % 4 == 0);
+  if (g.N % 4 == 0 && aligned16(g.partial) && dvec) {
+    const int n4 = g.N / 4;
+    const dim3 grid(unsigned((n4 + threads - 1) / threads), unsigned(std::min(g.M, 65535)));
+    gemm_split_reduce_vec_kernel<<<grid, threads, 0, st>>>(reinterpret_cast<const float4*>(g.partial), p.batch, g.M,
+                                                            n4, g.alpha, g.D, g.d_dtype, g.ldd, g.beta, g.C,
+                                                            g.c_dtype, g.c_sm, g.c_sn);
+    return check_cuda(cudaGetLastError(), "gemm split reduce launch");
+  }
   const int blocks = int(std::max<long long>(1, std::min<long long>((total + threads - 1) / threads, 148LL * 8)));
   gemm_split_reduce_kernel<<<blocks, threads, 0, st>>>(g.partial, p.batch, g.M, g.N, g.alpha, g.D, g.d_dtype, g.ldd,
                                                        g.beta, g.C, g.c_dtype, g.c_sm, g.c_sn);

@@ -90,10 +90,13 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
   if (g_bn_epilogue.load() && g_mode.load() > 1) {
     // statistics now; the output pass waits for the first reader of `out`,
     // so that a residual add_ and a relu_ on `out` fold into it
-    XDNA_B2(b2_batch_norm_stats_bf16(input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
-                                     const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(),
-                                     save_invstd.data_ptr<float>(), N, C, HW, float(momentum), float(eps),
-                                     ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+    {
+      KernelTimer kt("bn.stats", 2.0 * double(input.numel()), stream(dev));  // work: algorithmic bytes
+      XDNA_B2(b2_batch_norm_stats_bf16(input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
+                                       const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(),
+                                       save_invstd.data_ptr<float>(), N, C, HW, float(momentum), float(eps),
+                                       ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+    }
     count_launch("batch_norm.fwd", 2);
     auto spec = std::make_shared<EpiSpec>();
     const at::Tensor w = defined(weight) ? *weight : at::Tensor();
@@ -104,6 +107,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
     defer_epilogue(out, {input, w, b}, spec, [input, w, b, stats, spec, y, layout, pdt, N, C, HW, dev]() {
       c10::cuda::CUDAGuard guard(dev);
       const at::Tensor& r = spec->residual;
+      KernelTimer kt(r.defined() ? "bn.apply_res" : "bn.apply", (r.defined() ? 6.0 : 4.0) * double(input.numel()),
+                     stream(dev));
       XDNA_B2(b2_batch_norm_apply_bf16(input.data_ptr(), layout, w.defined() ? w.data_ptr() : nullptr,
                                        b.defined() ? b.data_ptr() : nullptr, pdt, stats[0].data_ptr<float>(),
                                        stats[1].data_ptr<float>(), r.defined() ? r.data_ptr() : nullptr,
@@ -158,6 +163,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
   materialize(g);
   materialize(input);
   c10::cuda::CUDAGuard guard(dev);
+  KernelTimer kt("bn.bwd", (mask[0] ? 10.0 : 4.0) * double(input.numel()), stream(dev));
   XDNA_B2(b2_batch_norm_bwd_bf16(g.data_ptr(), input.data_ptr(), layout, ptr_of(weight), pw,
                                  save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(),
                                  mask[0] ? gi.data_ptr() : nullptr, mask[1] ? gw.data_ptr() : nullptr,

@@ -71,10 +71,20 @@ def graph(g: XdnaGraph, pool: int = 0, stream: torch.cuda.Stream | None = None,
             native.graph_capture_end(s.cuda_stream)
 
 
+def _detached(out):
+    if isinstance(out, torch.Tensor):
+        return out.detach()
+    if isinstance(out, (list, tuple)):
+        return type(out)(_detached(o) for o in out)
+    if isinstance(out, dict):
+        return {k: _detached(v) for k, v in out.items()}
+    return out
+
+
 def make_graphed_step(step, warmup: int = 3):
     """Warm ``step`` up on a side stream, capture one call of it, and return a
     function that replays the capture and returns what the captured call
-    returned (the same tensors, refreshed by every replay).
+    returned (the same tensors, detached, refreshed by every replay).
 
     Warm-up runs real steps (an optimizer inside ``step`` updates the weights
     ``warmup`` times before the first replay; the capture itself runs
@@ -89,6 +99,10 @@ def make_graphed_step(step, warmup: int = 3):
     g = XdnaGraph()
     with graph(g):
         out = step()
+    # the captured call's outputs are returned detached: a loss that kept its
+    # autograd graph would keep that step's AccumulateGrad nodes (and the
+    # stream they were created on) alive into later captures and steps
+    out = _detached(out)
 
     def replay():
         g.replay()
