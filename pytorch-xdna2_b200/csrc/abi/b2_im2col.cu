@@ -75,6 +75,54 @@ __global__ void __launch_bounds__(kColThreads) im2col_kernel(const uint16_t* __r
 }
 
 // Fallback for K > kMaxTabK: one thread per column element.
+// Column copy in 16-byte chunks: thread u writes columns 8j..8j+7 of pixel
+// row p (u = p * Kp/8 + j), so a warp's stores cover consecutive chunks of
+// consecutive rows; its eight elements are gathered one by one through the
+// packed offset table (any channel count: the stems' 3 input channels leave no
+// wider unit to copy).  Needs P * Kp / 8 < 2^31.
+__global__ void __launch_bounds__(kColThreads) im2col_chunk8_kernel(const uint16_t* __restrict__ x, ConvGeom g,
+                                                                    uint16_t* __restrict__ col) {
+  __shared__ uint32_t tab[kMaxTabK];
+  const int K = int(g.K), Kp = int(g.Kp);
+  for (int k = threadIdx.x; k < Kp; k += kColThreads) {
+    if (k < K) {
+      const int ci = k % int(g.C), tap = k / int(g.C);
+      tab[k] = uint32_t((tap / g.kw) * g.dy) | (uint32_t((tap % g.kw) * g.dx) << 8) | (uint32_t(ci) << 16);
+    } else {
+      tab[k] = 0xffffffffu;  // padding column: zero
+    }
+  }
+  __syncthreads();
+  const uint32_t J = uint32_t(Kp / 8), Wo = uint32_t(g.Wo), Ho = uint32_t(g.Ho);
+  const uint32_t total = uint32_t(g.B * g.Ho * g.Wo) * J;
+  const int H = int(g.H), W = int(g.W);
+  for (uint32_t u = blockIdx.x * kColThreads + threadIdx.x; u < total; u += gridDim.x * kColThreads) {
+    const uint32_t p = u / J, j = u - p * J;
+    const uint32_t q = p / Wo;
+    const uint32_t ox = p - q * Wo, oy = q % Ho, b = q / Ho;
+    const int y0 = int(oy) * g.sy - g.py, x0 = int(ox) * g.sx - g.px;
+    const uint16_t* xb = x + (long long)b * g.sb;
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      uint32_t lo = 0, hi = 0;
+      const uint32_t t0 = tab[j * 8 + 2 * h], t1 = tab[j * 8 + 2 * h + 1];
+      if (t0 != 0xffffffffu) {
+        const int iy = y0 + int(t0 & 0xffu), ix = x0 + int((t0 >> 8) & 0xffu);
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+          lo = __ldg(xb + (long long)(t0 >> 16) * g.sc + (long long)iy * g.sh + (long long)ix * g.sw);
+      }
+      if (t1 != 0xffffffffu) {
+        const int iy = y0 + int(t1 & 0xffu), ix = x0 + int((t1 >> 8) & 0xffu);
+        if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+          hi = __ldg(xb + (long long)(t1 >> 16) * g.sc + (long long)iy * g.sh + (long long)ix * g.sw);
+      }
+      w[h] = lo | (hi << 16);
+    }
+    *reinterpret_cast<uint4*>(col + (long long)p * Kp + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 __global__ void __launch_bounds__(kColThreads) im2col_flat_kernel(const uint16_t* __restrict__ x, ConvGeom g,
                                                                   uint16_t* __restrict__ col) {
   const long long total = g.B * g.Ho * g.Wo * g.Kp;
@@ -223,6 +271,11 @@ b2_status b2_im2col_bf16(const void* x, int64_t sb, int64_t sc, int64_t sh, int6
     const long long units = P * kh * kw * (C / 8);
     im2col_nhwc8_kernel<<<col_grid(units, sms), kColThreads, 0, st>>>(static_cast<const uint16_t*>(x), g,
                                                                       static_cast<uint16_t*>(col));
+  } else if (g.Kp <= kMaxTabK && g.Kp % 8 == 0 && g.C < 65536 && (long long)(g.kh - 1) * g.dy < 256 &&
+             (long long)(g.kw - 1) * g.dx < 256 && P * (g.Kp / 8) < (1LL << 31) && H + 2 * py < (1LL << 30) &&
+             W + 2 * px < (1LL << 30) && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {
+    im2col_chunk8_kernel<<<col_grid(P * (g.Kp / 8), sms), kColThreads, 0, st>>>(static_cast<const uint16_t*>(x), g,
+                                                                                static_cast<uint16_t*>(col));
   } else if (g.K <= kMaxTabK && g.C < 65536 && (long long)(g.kh - 1) * g.dy < 256 &&
              (long long)(g.kw - 1) * g.dx < 256 && P < (1LL << 31) && H + 2 * py < (1LL << 30) &&
              W + 2 * px < (1LL << 30)) {

@@ -488,11 +488,14 @@ void launch_wgrad_nhwc(const at::Tensor& dy, const at::Tensor& x, void* gw, at::
 }  // namespace
 
 // Routing of the convolutions outside the 3x3 fast path (set_conv_paths).
-// Both off by default: measured on ResNet-50 (channels-last, batch 128) ATen's
-// library kernels are faster for its 1x1 convolutions and its 7x7 stem, and
-// equal on the style network's 9x9 layers.
+// Stems and large kernels take the column-matrix GEMMs by default: on
+// ResNet-50 (channels-last, batch 128, one B200) the 7x7 stem costs 0.95 ms a
+// step that way against 1.17 ms in ATen's library kernels (the step: 8825
+// against 8693 images/s).  The 1x1 GEMMs stay off by default: ATen's library
+// kernels are still faster for ResNet-50's 1x1 layers (8621 against 8999
+// images/s with them on).
 std::atomic<bool> g_conv1x1{env_flag("XDNA_CONV1X1", false)};
-std::atomic<bool> g_conv_general{env_flag("XDNA_CONV_GENERAL", false)};
+std::atomic<bool> g_conv_general{env_flag("XDNA_CONV_GENERAL", true)};
 
 namespace {
 
@@ -516,14 +519,16 @@ at::Tensor convolution_overrideable(const at::Tensor& input, const at::Tensor& w
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
     if (l1 >= 0) return conv1x1_forward(input, weight, bias, l1);
-    GeneralConv gc;
-    if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
-        general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
-      return general_forward(input, weight, bias, gc);
+    // an RGB input layer small enough for the direct kernel takes it; other
+    // stems and large kernels the column GEMMs
     DirectConv dc;
     if (!is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
         direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_fwd_ok(dc))
       return direct_forward(input, weight, bias, dc);
+    GeneralConv gc;
+    if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
+        general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
+      return general_forward(input, weight, bias, gc);
   }
   const bool fast = g_mode.load() > 0 && is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
                     bf16(input) && bf16(weight) && bf16(bias) && input.numel() > 0;
@@ -567,13 +572,21 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     std::array<bool, 3> output_mask) {
   if (g_mode.load() > 0 && bf16(input) && bf16(weight) && bf16(grad_output)) {
     DirectConv dc;
-    const bool general = general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed,
-                                                         groups);
-    if (!general && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
-        direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) && direct_dgrad_ok(dc)) {
+    GeneralConv gc;
+    const bool not3x3 = !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups);
+    const bool general =
+        general_enabled() && not3x3 && general_conv(input, weight, stride, padding, dilation, transposed, groups, gc);
+    // an RGB output layer's input gradient: the direct kernel; its weight
+    // gradient from the column GEMMs (or ATen's library kernels without them)
+    if (not3x3 && direct_conv(input, weight, stride, padding, dilation, transposed, groups, dc) &&
+        direct_dgrad_ok(dc)) {
       at::Tensor dx = output_mask[0] ? direct_dgrad(grad_output, input, weight, dc) : at::Tensor();
       at::Tensor dw, db;
-      if (output_mask[1] || output_mask[2]) {
+      if ((output_mask[1] || output_mask[2]) && general) {
+        auto r = general_backward(grad_output, input, weight, gc, {false, output_mask[1], output_mask[2]});
+        dw = std::get<1>(r);
+        db = std::get<2>(r);
+      } else if (output_mask[1] || output_mask[2]) {
         count_fallback("convolution_backward_overrideable.dw");
         c10::cuda::CUDAGuard g(input.device().index());
         auto r = at::convolution_backward(to_cuda(grad_output), to_cuda(input), to_cuda(weight), std::nullopt,
@@ -587,10 +600,7 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     const int l1 =
         conv1x1_enabled() ? conv1x1_layout(input, weight, stride, padding, dilation, transposed, groups) : -1;
     if (l1 >= 0) return conv1x1_backward(grad_output, input, weight, l1, output_mask);
-    GeneralConv gc;
-    if (general_enabled() && !is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
-        general_conv(input, weight, stride, padding, dilation, transposed, groups, gc))
-      return general_backward(grad_output, input, weight, gc, output_mask);
+    if (general) return general_backward(grad_output, input, weight, gc, output_mask);
   }
   const bool fast = g_mode.load() > 0 && is3x3s1p1(input, weight, stride, padding, dilation, transposed, groups) &&
                     bf16(input) && bf16(weight) && bf16(grad_output) && input.numel() > 0;

@@ -132,13 +132,26 @@ def test_conv_fwd_bwd_vs_reference_cpu_path(shape, channels_last):
     no_fallback("convolution_overrideable", "convolution_backward_overrideable")
 
 
-def test_non3x3_conv_takes_cuda_path():
+def test_non3x3_conv_routes():
+    """A 1x1 convolution with both non-3x3 routes off takes ATen's CUDA path
+    (counted as a fallback); with the column-matrix route on it runs on the
+    im2col kernel and the tcgen05 GEMM, with no fallback."""
     conv = nn.Conv2d(8, 16, 1).bfloat16().to(X)
     x = torch.randn(2, 8, 5, 5, dtype=torch.bfloat16, device=X)
-    y = conv(x)
     ref = F.conv2d(x.cpu().float(), conv.weight.cpu().float(), conv.bias.cpu().float())
-    close(y, ref)
-    assert "convolution_overrideable" in xdna_train.fallback_stats()
+    saved = xdna_train.set_conv_paths()
+    try:
+        xdna_train.set_conv_paths(conv1x1=False, general=False)
+        close(conv(x), ref)
+        assert "convolution_overrideable" in xdna_train.fallback_stats()
+        xdna_train.reset_fallback_stats()
+        xdna_train.set_conv_paths(conv1x1=False, general=True)
+        before = launched("conv.gemm")
+        close(conv(x), ref)
+        assert launched("conv.gemm") > before
+        no_fallback("convolution_overrideable")
+    finally:
+        xdna_train.set_conv_paths(*saved)
 
 
 def test_readme_training_step_matches_cpu():
@@ -166,6 +179,46 @@ def test_readme_training_step_matches_cpu():
     close(mx.weight, mc.weight, tol=2e-2)
     assert launched("fused_adam") >= 1
     no_fallback("convolution_overrideable", "convolution_backward_overrideable", "_fused_adam_")
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_npu_mode_ab_switch(mode):
+    """set_npu_mode (reference device.py:654-660): the same 3x3 conv training
+    step in each mode matches the CPU BF16 path, and the launch counters show
+    which kernels ran -- 0: none of this backend's conv kernels (every conv on
+    ATen's CUDA library kernels, the B200 counterpart of the reference's
+    "no offload" mode), 1: forward and input gradient native, the weight
+    gradient on ATen's CUDA path, 2: all native."""
+    x, conv, dy = _conv_case(4, 64, 12, 12, 64, True, seed=11)
+    xc = x.clone().requires_grad_()
+    yc = conv(xc)
+    yc.backward(dy)
+    cx = copy.deepcopy(conv).to(X)
+    xx = x.to(X).requires_grad_()
+    try:
+        xdna_train.set_npu_mode(mode)
+        assert xdna_train.npu_mode() == mode
+        xdna_train.reset_fallback_stats()
+        y = cx(xx)
+        y.backward(dy.to(X))
+        close(y, yc)
+        close(xx.grad, xc.grad)
+        close(cx.weight.grad, conv.weight.grad)
+        close(cx.bias.grad, conv.bias.grad)
+        fb = xdna_train.fallback_stats()
+        n = {k: launched(f"conv3x3.{k}") for k in ("fwd", "dgrad", "wgrad")}
+    finally:
+        xdna_train.set_npu_mode(2)
+    if mode == 0:
+        assert n == {"fwd": 0, "dgrad": 0, "wgrad": 0}, n
+        assert "convolution_overrideable" in fb and "convolution_backward_overrideable" in fb
+    elif mode == 1:
+        assert n["fwd"] >= 1 and n["dgrad"] >= 1 and n["wgrad"] == 0, n
+        assert "convolution_backward_overrideable.dw" in fb and "convolution_overrideable" not in fb
+    else:
+        assert min(n.values()) >= 1, n
+        no_fallback("convolution_overrideable", "convolution_backward_overrideable",
+                    "convolution_backward_overrideable.dw")
 
 
 # ------------------------------------------------------- deferred weight gradient
