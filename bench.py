@@ -639,6 +639,9 @@ def run_resnet50(args):
         eb.record(s)
         torch.cuda.synchronize()
         eager_ms = ea.elapsed_time(eb) / ne
+        for r in replays:
+            r.graph.reset()
+        del replays, run
 
     # ---- the gradient all-reduce alone, per step (N > 1): every bucket's
     # collective, events on the launching stream

@@ -117,6 +117,15 @@ b2_status b2_pack_weight_fwd_bf16(const void* w, int Cout, int Cin, int chunks,
 b2_status b2_pack_weight_dgrad_bf16(const void* w, int Cout, int Cin,
                                     int chunks_o, void* wk, void* stream);
 
+/* Either packing (dgrad != 0: the dgrad form) from a weight read through its
+ * element strides {co, ci, ky, kx} -- OIHW is {9*Cin, 9, 3, 1}, a
+ * channels-last OHWI weight {9*Cin, 1, 3*Cin, Cin} -- so a channels-last
+ * model's weights need no contiguous copy first.  Same output as the two
+ * calls above (conv_pack.cpp:398-443, 474-519). */
+b2_status b2_pack_weight_strided_bf16(const void* w, const int64_t* strides,
+                                      int Cout, int Cin, int chunks, int dgrad,
+                                      void* wk, void* stream);
+
 /* Dense bf16 NCHW [B][C][H*W] <-> NHWC [B][H*W][C] transposes.
  * Replace xdna_pack_conv3x3_halo_padded_bf16 / xdna_yxbc_to_channels_last_bf16
  * (conv_pack.cpp:19-112) for the channels-last boundary. */
@@ -500,6 +509,23 @@ b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout,
                                  void* db, int gdtype, int64_t N, int64_t C,
                                  int64_t HW, void* workspace,
                                  size_t workspace_bytes, void* stream);
+/* Backward of a BatchNorm whose output pass folded a ReLU (no residual): dy is
+ * the gradient of y = relu(bf16(x*scale + shift)); the ReLU's gate (y > 0 or
+ * NaN, as ATen's threshold_backward) is recomputed from x, w, b and the saved
+ * statistics, so neither y nor the gated gradient is read.  Results are bit
+ * for bit those of threshold_backward(dy, y, 0) followed by
+ * b2_batch_norm_bwd_bf16 (replaces the reference's two CPU-alias ops,
+ * threshold_backward and native_batch_norm_backward,
+ * torch_xdna_device.cpp:4214-4358, 5124-5260, for this pair).  Channels-last
+ * only, C a power of two in [8, 2048]; workspace as b2_batch_norm_bwd_bf16
+ * (layout 1). */
+b2_status b2_batch_norm_relu_bwd_bf16(const void* dy, const void* x,
+                                      const void* w, const void* b, int pdtype,
+                                      const float* save_mean,
+                                      const float* save_invstd, void* dx,
+                                      void* dw, void* db, int gdtype, int64_t N,
+                                      int64_t C, int64_t HW, void* workspace,
+                                      size_t workspace_bytes, void* stream);
 
 /* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
  * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,

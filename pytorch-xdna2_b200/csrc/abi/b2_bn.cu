@@ -829,26 +829,47 @@ __device__ __forceinline__ bool stream_units(const uint4* const (&src)[NIN], lon
   return true;
 }
 
+// The ReLU that followed a BatchNorm, recomputed from its input: the forward
+// wrote y = relu(bf16(z)), z = x*scale + shift (bn_tail_fast without a
+// residual), and ATen's threshold_backward passes dy where y > 0 or y is NaN,
+// elsewhere the gradient is exactly +0.  bf16(z) > 0 exactly when z > 2^-134:
+// the smallest positive bf16 is 2^-133, and round-to-nearest-even sends z in
+// (0, 2^-134] -- the tie included -- to zero.  So the gate is !(z <= 2^-134),
+// NaN passing, with no rounding.
+__device__ __forceinline__ float relu_gate(float g, float xv, float scale, float shift) {
+  const float z = __fadd_rn(__fmul_rn(xv, scale), shift);
+  return !(z <= 0x1p-134f) ? g : 0.0f;
+}
+
 // Sums per CTA and channel (as bn_nhwc_sums_kernel): forward a = sum(x - K),
 // b = sum((x - K)^2), K the first pixel; backward a = sum(dz), b = sum(dz *
-// xhat).  Inputs in ring order x, dy, y.
-template <bool BWD, bool ACT>
+// xhat).  Inputs in ring order x, dy, y.  RC (backward): dz = relu_gate(dy)
+// with scale and shift from rc's w, b and the saved statistics (no y read).
+template <bool BWD, bool ACT, bool RC = false>
 __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_sums_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y,
     const float* __restrict__ mean, const float* __restrict__ invstd, NhwcShape sh, float slope, int relu,
-    float* __restrict__ part_a, float* __restrict__ part_b, int* status) {
+    float* __restrict__ part_a, float* __restrict__ part_b, int* status, BnChan rc = BnChan{}) {
+  static_assert(!RC || (BWD && !ACT), "the recomputed ReLU gate is a backward of plain BatchNorm");
   constexpr int NIN = BWD ? (ACT ? 3 : 2) : 1;
   const bool consumer = threadIdx.x < kStreamConsumers;
   const int cg = threadIdx.x % sh.CV;
-  float a[8], b[8], k0[8], k1[8];
+  float a[8], b[8], k0[8], k1[8], gsc[8], gsh[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) a[e] = b[e] = k0[e] = k1[e] = 0.0f;
+  for (int e = 0; e < 8; ++e) a[e] = b[e] = k0[e] = k1[e] = gsc[e] = gsh[e] = 0.0f;
   if (consumer) {
     if constexpr (BWD) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         k0[e] = mean[cg * 8 + e];
         k1[e] = invstd[cg * 8 + e];
+      }
+      if constexpr (RC) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          gsc[e] = __fmul_rn(ld_par(rc.w, rc.pdtype, cg * 8 + e, 1.0f), k1[e]);
+          gsh[e] = __fsub_rn(ld_par(rc.b, rc.pdtype, cg * 8 + e, 0.0f), __fmul_rn(k0[e], gsc[e]));
+        }
       }
     } else {
       unpack8(__ldg(reinterpret_cast<const uint4*>(x) + cg), k0);  // shift K: the first pixel
@@ -867,7 +888,7 @@ __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_sums_kernel(
       if constexpr (ACT) unpack8(v[NIN - 1], fy);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float dz = bn_dz<ACT>(fg[e], ACT ? fy[e] : 0.0f, slope, relu);
+        const float dz = RC ? relu_gate(fg[e], fx[e], gsc[e], gsh[e]) : bn_dz<ACT>(fg[e], ACT ? fy[e] : 0.0f, slope, relu);
         a[e] = __fadd_rn(a[e], dz);
         b[e] = __fadd_rn(b[e], __fmul_rn(dz, __fmul_rn(__fsub_rn(fx[e], k0[e]), k1[e])));
       }
@@ -942,14 +963,16 @@ __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_apply_kernel(
   }, status);
 }
 
-// dx = w*invstd*(dz - k1 - xhat*k2); inputs in ring order dy, x, y.
-template <bool ACT>
+// dx = w*invstd*(dz - k1 - xhat*k2); inputs in ring order dy, x, y.  RC: dz =
+// relu_gate(dy) as in the sums kernel (w, b from rc).
+template <bool ACT, bool RC = false>
 __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_dx_kernel(
     const uint16_t* __restrict__ dy, const uint16_t* __restrict__ y, const uint16_t* __restrict__ x, const void* w,
     int pdtype, const float* __restrict__ mean, const float* __restrict__ invstd, const float* __restrict__ k,
-    uint16_t* __restrict__ dx, NhwcShape sh, float slope, int relu, int* status) {
+    uint16_t* __restrict__ dx, NhwcShape sh, float slope, int relu, int* status, BnChan rc = BnChan{}) {
+  static_assert(!RC || !ACT, "the recomputed ReLU gate is a backward of plain BatchNorm");
   constexpr int NIN = ACT ? 3 : 2;
-  float ws[8], mc[8], is[8], k1[8], k2[8];
+  float ws[8], mc[8], is[8], k1[8], k2[8], gsc[8], gsh[8];
   if (threadIdx.x < kStreamConsumers) {
     const int c0 = int(threadIdx.x % sh.CV) * 8;
 #pragma unroll
@@ -960,6 +983,11 @@ __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_dx_kernel(
       is[e] = invstd[c];
       k1[e] = k[c];
       k2[e] = k[sh.C + c];
+      gsc[e] = gsh[e] = 0.0f;
+      if constexpr (RC) {
+        gsc[e] = __fmul_rn(ld_par(rc.w, rc.pdtype, c, 1.0f), invstd[c]);
+        gsh[e] = __fsub_rn(ld_par(rc.b, rc.pdtype, c, 0.0f), __fmul_rn(mean[c], gsc[e]));
+      }
     }
   }
   const uint4* src[NIN];
@@ -973,8 +1001,13 @@ __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_dx_kernel(
     unpack8(v[1], fx);
     if constexpr (ACT) unpack8(v[NIN - 1], fy);
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
+    for (int e = 0; e < 8; ++e) {
+      if constexpr (RC)
+        r[e] = bn_dx<false>(relu_gate(fg[e], fx[e], gsc[e], gsh[e]), 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e],
+                            slope, relu);
+      else
+        r[e] = bn_dx<ACT>(fg[e], ACT ? fy[e] : 0.0f, fx[e], mc[e], is[e], ws[e], k1[e], k2[e], slope, relu);
+    }
     d4[u] = pack8_fast(r);
   }, status);
 }
@@ -1016,24 +1049,27 @@ bool stream_ok(const NhwcShape& sh) {
   return on && kStreamConsumers % sh.CV == 0;
 }
 
-// Grid of a streaming kernel: one wave of resident CTAs, at most one per
-// chunk and at most `cap`; raises the kernel's shared-memory limit first
-// (once per device).
+// Raises a streaming kernel's shared-memory limit to `smem` (once per device).
 template <typename K>
-int stream_grid(K* kfn, size_t smem, long long units, int sms, long long cap) {
+void allow_smem(K* kfn, size_t smem) {
   static std::mutex mu;
   static std::map<std::pair<const void*, int>, bool> done;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    auto key = std::make_pair(reinterpret_cast<const void*>(kfn), dev);
-    if (!done.count(key)) {
-      if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-        cudaGetLastError();
-      done[key] = true;
-    }
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(reinterpret_cast<const void*>(kfn), dev);
+  if (!done.count(key)) {
+    if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+      cudaGetLastError();
+    done[key] = true;
   }
+}
+
+// Grid of a streaming kernel: one wave of resident CTAs, at most one per
+// chunk and at most `cap`; raises the kernel's shared-memory limit first.
+template <typename K>
+int stream_grid(K* kfn, size_t smem, long long units, int sms, long long cap) {
+  allow_smem(kfn, smem);
   const long long chunks = (units + kChunkUnits - 1) / kChunkUnits;
   const long long wave = (long long)sms * resident_blocks(reinterpret_cast<const void*>(kfn), smem, kStreamThreads);
   return int(std::max<long long>(1, std::min({chunks, wave, cap})));
@@ -1126,7 +1162,7 @@ b2_status bn_stats(const uint16_t* x, int layout, const BnChan& ch, float* mean_
       constexpr size_t smem = ring_smem_bytes<1>();
       blocks = stream_grid(kfn, smem, sh.P * sh.CV, sms, nhwc_blocks(sh));
       kfn<<<int(blocks), kStreamThreads, smem, st>>>(x, nullptr, nullptr, nullptr, nullptr, sh, 0.0f, 0, pa,
-                                                      pa + blocks * C, device_status_ptr());
+                                                      pa + blocks * C, device_status_ptr(), BnChan{});
     } else {
       const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
       blocks = nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
@@ -1226,7 +1262,7 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
       constexpr size_t smem = ring_smem_bytes<ACT ? 3 : 2>();
       blocks = stream_grid(kfn, smem, sh.P * sh.CV, sms, nhwc_blocks(sh));
       kfn<<<int(blocks), kStreamThreads, smem, st>>>(xx, g, yy, mean, invstd, sh, slope, relu, pa, pa + blocks * C,
-                                                      device_status_ptr());
+                                                      device_status_ptr(), BnChan{});
     } else {
       const size_t red = 2 * size_t(sh.rpb) * size_t(C) * sizeof(float);
       blocks = nhwc_blocks(sh, (long long)sms * resident_blocks(reinterpret_cast<const void*>(
@@ -1244,7 +1280,7 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
       auto kfn = &bn_nhwc_stream_dx_kernel<ACT>;
       constexpr size_t smem = ring_smem_bytes<ACT ? 3 : 2>();
       kfn<<<stream_grid(kfn, smem, sh.P * sh.CV, sms, LLONG_MAX), kStreamThreads, smem, st>>>(
-          g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu, device_status_ptr());
+          g, yy, xx, w, pdtype, mean, invstd, k, dx, sh, slope, relu, device_status_ptr(), BnChan{});
     } else if (kBnThreads % sh.CV == 0)
       bn_nhwc_dx_kernel<ACT, true><<<wave_grid(&bn_nhwc_dx_kernel<ACT, true>, 0, sh.P * sh.CV, sms), kBnThreads, 0,
                                                                                               st>>>(
@@ -1287,6 +1323,41 @@ b2_status bn_backward(const uint16_t* g, const uint16_t* yy, const uint16_t* xx,
                                                                               k, dx, units, HW, C, slope, relu);
   }
   return check_cuda(cudaGetLastError(), "bn dx launch");
+}
+
+// Backward of y = relu(bf16(BatchNorm(x))) from dL/dy, channels-last, with
+// the ReLU's gate recomputed from x (no y read, no gated-gradient pass).  The
+// grid is the plain backward's, so the partial sums -- and dw, db, dx -- are
+// bit for bit those of ATen's threshold_backward followed by
+// b2_batch_norm_bwd_bf16.
+b2_status bn_relu_backward(const uint16_t* g, const uint16_t* xx, const void* w, const void* b, int pdtype,
+                           const float* mean, const float* invstd, uint16_t* dx, void* dw, void* db, int gdtype,
+                           long long N, long long C, long long HW, void* workspace, cudaStream_t st, const char* who) {
+  B2_TRY(check_nhwc(C, {g, xx, dx}, who));
+  const NhwcShape sh = nhwc_shape(N, C, HW);
+  if (!stream_ok(sh))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: needs the streaming kernels (C/8 dividing 256, B2_BN_STREAM on)", who);
+  const int sms = current_sms();
+  const double M = double(N) * double(HW);
+  const BnChan rc{w, b, pdtype, nullptr, nullptr, B2_F32};
+  constexpr size_t smem = ring_smem_bytes<2>();
+  const long long units = sh.P * sh.CV;
+  const long long blocks = stream_grid(&bn_nhwc_stream_sums_kernel<true, false>, smem, units, sms, nhwc_blocks(sh));
+  auto sums = &bn_nhwc_stream_sums_kernel<true, false, true>;
+  allow_smem(sums, smem);
+  float* pa = static_cast<float*>(workspace);
+  float* pb = pa + blocks * C;
+  sums<<<int(blocks), kStreamThreads, smem, st>>>(xx, g, nullptr, mean, invstd, sh, 0.0f, 0, pa, pb,
+                                                  device_status_ptr(), rc);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn relu bwd sums launch"));
+  float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(blocks) * C * sizeof(float)));
+  bn_bwd_channel_kernel<<<int(C), kMergeThreads, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn relu bwd channel launch"));
+  if (!dx) return B2_OK;
+  auto dxk = &bn_nhwc_stream_dx_kernel<false, true>;
+  dxk<<<stream_grid(dxk, smem, units, sms, LLONG_MAX), kStreamThreads, smem, st>>>(
+      g, nullptr, xx, w, pdtype, mean, invstd, k, dx, sh, 0.0f, 0, device_status_ptr(), rc);
+  return check_cuda(cudaGetLastError(), "bn relu dx launch");
 }
 
 bool valid_pdtype(int dt) { return dt == B2_BF16 || dt == B2_F32; }
@@ -1398,3 +1469,18 @@ b2_status b2_batch_norm_bwd_bf16(const void* dy, const void* x, int layout, cons
 }
 
 }  // extern "C"
+
+extern "C" b2_status b2_batch_norm_relu_bwd_bf16(const void* dy, const void* x, const void* w, const void* b,
+                                                 int pdtype, const float* save_mean, const float* save_invstd,
+                                                 void* dx, void* dw, void* db, int gdtype, int64_t N, int64_t C,
+                                                 int64_t HW, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_relu_bwd_bf16";
+  B2_TRY(check_common(N, C, HW, 1, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(gdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C == 0) return B2_OK;
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!dy || !x || !save_mean || !save_invstd) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  return bn_relu_backward(static_cast<const uint16_t*>(dy), static_cast<const uint16_t*>(x), w, b, pdtype, save_mean,
+                          save_invstd, static_cast<uint16_t*>(dx), dw, db, gdtype, N, C, HW, workspace,
+                          static_cast<cudaStream_t>(stream), who);
+}

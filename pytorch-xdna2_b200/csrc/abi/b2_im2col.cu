@@ -74,6 +74,72 @@ __global__ void __launch_bounds__(kColThreads) im2col_kernel(const uint16_t* __r
   }
 }
 
+// Column copy by output rows through shared memory: a CTA takes one output
+// row (b, oy) at a time, stages the kh input rows its windows read -- zero
+// padded left and right, zero rows outside the image -- as [kh][Wpad][C]
+// (Wpad = W + 2*px), then writes the row's Wo*Kp columns in 16-byte chunks,
+// consecutive chunks to consecutive addresses, each of the chunk's 8 columns
+// one shared-memory read at a per-column offset (a table) plus the pixel's
+// window origin ox*sx*C.  For stems (3 channels, 7x7): the input is read
+// once per output row instead of once per column element, and the stores are
+// full 16-byte lines.
+constexpr int kRowTileMaxBytes = 40 * 1024;
+
+__global__ void __launch_bounds__(kColThreads) im2col_rowtile_kernel(const uint16_t* __restrict__ x, ConvGeom g,
+                                                                     uint16_t* __restrict__ col) {
+  extern __shared__ __align__(16) uint8_t rt_smem[];
+  const int K = int(g.K), Kp = int(g.Kp), C = int(g.C), kh = g.kh;
+  const int Wpad = int(g.W) + 2 * g.px;
+  const int rowlen = Wpad * C;  // elements of one staged input row
+  int* off = reinterpret_cast<int*>(rt_smem);
+  uint16_t* stage = reinterpret_cast<uint16_t*>(rt_smem + ((size_t(Kp) * 4 + 15) & ~size_t(15)));
+  for (int k = threadIdx.x; k < Kp; k += kColThreads) {
+    if (k < K) {
+      const int ci = k % C, tap = k / C;
+      off[k] = (tap / g.kw) * rowlen + (tap % g.kw) * g.dx * C + ci;
+    } else {
+      off[k] = -1;  // padding column: zero
+    }
+  }
+  const int Wo = int(g.Wo), J = Kp / 8;
+  const long long rows = g.B * g.Ho;
+  const int staged = kh * rowlen;
+  for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int oy = int(r % g.Ho);
+    const long long b = r / g.Ho;
+    const uint16_t* xb = x + b * g.sb;
+    __syncthreads();  // the previous row's reads of the stage (and the table) are done
+    for (int e = threadIdx.x; e < staged; e += kColThreads) {
+      const int ky = e / rowlen, rem = e - ky * rowlen;
+      const int ixp = rem / C, ci = rem - ixp * C;
+      const int iy = oy * g.sy - g.py + ky * g.dy, ix = ixp - g.px;
+      uint16_t v = 0;
+      if (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W)
+        v = __ldg(xb + (long long)ci * g.sc + (long long)iy * g.sh + (long long)ix * g.sw);
+      stage[e] = v;
+    }
+    __syncthreads();
+    uint16_t* dst = col + r * (long long)Wo * Kp;
+    for (int u = threadIdx.x; u < Wo * J; u += kColThreads) {
+      const int ox = u / J, j = u - ox * J;
+      const int base = ox * g.sx * C;
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int o0 = off[j * 8 + 2 * h], o1 = off[j * 8 + 2 * h + 1];
+        const uint32_t lo = o0 >= 0 ? stage[base + o0] : 0u;
+        const uint32_t hi = o1 >= 0 ? stage[base + o1] : 0u;
+        w[h] = lo | (hi << 16);
+      }
+      *reinterpret_cast<uint4*>(dst + (long long)ox * Kp + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+size_t rowtile_smem(const ConvGeom& g) {
+  return ((size_t(g.Kp) * 4 + 15) & ~size_t(15)) + size_t(g.kh) * size_t(g.W + 2 * g.px) * size_t(g.C) * 2;
+}
+
 // Fallback for K > kMaxTabK: one thread per column element.
 // Column copy in 16-byte chunks: thread u writes columns 8j..8j+7 of pixel
 // row p (u = p * Kp/8 + j), so a warp's stores cover consecutive chunks of
@@ -271,6 +337,13 @@ b2_status b2_im2col_bf16(const void* x, int64_t sb, int64_t sc, int64_t sh, int6
     const long long units = P * kh * kw * (C / 8);
     im2col_nhwc8_kernel<<<col_grid(units, sms), kColThreads, 0, st>>>(static_cast<const uint16_t*>(x), g,
                                                                       static_cast<uint16_t*>(col));
+  } else if (g.Kp % 8 == 0 && (reinterpret_cast<uintptr_t>(col) & 15) == 0 && g.Kp <= kMaxTabK &&
+             rowtile_smem(g) <= size_t(kRowTileMaxBytes) && g.Wo * (g.Kp / 8) < (1LL << 31)) {
+    const size_t smem = rowtile_smem(g);
+    const long long rows = B * Ho;
+    const int grid = int(std::max<long long>(1, std::min<long long>(rows, (long long)sms * 8)));
+    im2col_rowtile_kernel<<<grid, kColThreads, smem, st>>>(static_cast<const uint16_t*>(x), g,
+                                                           static_cast<uint16_t*>(col));
   } else if (g.Kp <= kMaxTabK && g.Kp % 8 == 0 && g.C < 65536 && (long long)(g.kh - 1) * g.dy < 256 &&
              (long long)(g.kw - 1) * g.dx < 256 && P * (g.Kp / 8) < (1LL << 31) && H + 2 * py < (1LL << 30) &&
              W + 2 * px < (1LL << 30) && (reinterpret_cast<uintptr_t>(col) & 15) == 0) {

@@ -431,7 +431,12 @@ __global__ void pack_rows_nhwc_vec_kernel(const uint16_t* __restrict__ x, long l
 
 // Wk[n][chunk*576 + tap*64 + c]; forward: n = co, source w[co][chunk*64+c][tap];
 // dgrad: n = ci, source w[chunk*64+c][ci][8-tap] (spatial flip + in/out swap).
-__global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int Cout, int Cin, int chunks,
+// The source is read through its element strides (co, ci, ky, kx): OIHW, or
+// the channels-last OHWI form of a channels-last model, without a copy.
+struct WStrides {
+  long long co, ci, ky, kx;
+};
+__global__ void pack_weight_kernel(const uint16_t* __restrict__ w, WStrides ws, int Cout, int Cin, int chunks,
                                    int dgrad, uint16_t* __restrict__ wk) {
   const int ktot = chunks * 576;
   const int nrows = dgrad ? Cin : Cout;
@@ -446,10 +451,9 @@ __global__ void pack_weight_kernel(const uint16_t* __restrict__ w, int Cout, int
     const int c = chunk * 64 + (k % 64);
     uint16_t v = 0;
     if (c < kred) {
-      if (!dgrad)
-        v = w[((long long)n * Cin + c) * 9 + tap];
-      else
-        v = w[((long long)c * Cin + n) * 9 + (8 - tap)];
+      const int t = dgrad ? 8 - tap : tap;
+      const long long co = dgrad ? c : n, ci = dgrad ? n : c;
+      v = w[co * ws.co + ci * ws.ci + (t / 3) * ws.ky + (t % 3) * ws.kx];
     }
     wk[i] = v;
   }
@@ -692,25 +696,34 @@ static b2_status pack_rows_impl(const void* x, int64_t sn, int64_t sc, int64_t s
   return check_cuda(cudaGetLastError(), "pack_rows launch");
 }
 
-static b2_status pack_weight(const void* w, int Cout, int Cin, int chunks, int dgrad, void* wk,
+static b2_status pack_weight(const void* w, WStrides ws, int Cout, int Cin, int chunks, int dgrad, void* wk,
                              void* stream, const char* name) {
   if (!w || !wk) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
   const int kred = dgrad ? Cout : Cin;
   if (Cout <= 0 || Cin <= 0 || chunks < (kred + 63) / 64) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
+  if (ws.co < 0 || ws.ci < 0 || ws.ky < 0 || ws.kx < 0) return set_error(B2_ERR_INVALID, "%s: negative stride", name);
   const long long total = (long long)(dgrad ? Cin : Cout) * chunks * 576;
   const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 8));
   pack_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(w), Cout, Cin, chunks, dgrad, static_cast<uint16_t*>(wk));
+      static_cast<const uint16_t*>(w), ws, Cout, Cin, chunks, dgrad, static_cast<uint16_t*>(wk));
   return check_cuda(cudaGetLastError(), "pack_weight launch");
 }
 
 b2_status b2_pack_weight_fwd_bf16(const void* w, int Cout, int Cin, int chunks, void* wk, void* stream) {
-  return pack_weight(w, Cout, Cin, chunks, 0, wk, stream, "b2_pack_weight_fwd_bf16");
+  return pack_weight(w, WStrides{9LL * Cin, 9, 3, 1}, Cout, Cin, chunks, 0, wk, stream, "b2_pack_weight_fwd_bf16");
 }
 
 b2_status b2_pack_weight_dgrad_bf16(const void* w, int Cout, int Cin, int chunks_o, void* wk,
                                     void* stream) {
-  return pack_weight(w, Cout, Cin, chunks_o, 1, wk, stream, "b2_pack_weight_dgrad_bf16");
+  return pack_weight(w, WStrides{9LL * Cin, 9, 3, 1}, Cout, Cin, chunks_o, 1, wk, stream,
+                     "b2_pack_weight_dgrad_bf16");
+}
+
+b2_status b2_pack_weight_strided_bf16(const void* w, const int64_t* strides, int Cout, int Cin, int chunks,
+                                      int dgrad, void* wk, void* stream) {
+  if (!strides) return set_error(B2_ERR_INVALID, "b2_pack_weight_strided_bf16: null strides");
+  return pack_weight(w, WStrides{strides[0], strides[1], strides[2], strides[3]}, Cout, Cin, chunks, dgrad ? 1 : 0,
+                     wk, stream, "b2_pack_weight_strided_bf16");
 }
 
 static b2_status transpose(const void* src, void* dst, int B, int R, int S, void* stream, const char* name) {

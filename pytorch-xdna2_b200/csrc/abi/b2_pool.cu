@@ -210,6 +210,69 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_kernel(const u
   }
 }
 
+// As maxpool_bwd_nhwc8_kernel when every input position is covered by at
+// most two outputs per dimension (window span <= 2 * stride: ResNet's 3x3 /
+// stride 2 pool): the up to four covering outputs' gradients and indices are
+// all loaded before any is compared -- four independent 80-byte loads in
+// flight per thread instead of a dependent chain -- then added in the same
+// (oh, ow) order, so the results are those of the general kernel.
+template <typename I>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_two_kernel(const uint16_t* __restrict__ dy,
+                                                                             const int64_t* __restrict__ ind,
+                                                                             PoolGeom g, uint16_t* __restrict__ dx) {
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * H * W * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / W, w = r - r2 * W;
+    const I n = r2 / H, h = r2 - n * H;
+    I oh0, oh1, ow0, ow1;
+    covering<I>(h, g.sh, g.ph, g.kh, g.dh, OH, oh0, oh1);
+    covering<I>(w, g.sw, g.pw, g.kw, g.dw, OW, ow0, ow1);
+    const long long me = (long long)(h * W + w);
+    uint4 v[4];
+    longlong2 ii[4][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const I oh = oh0 + (t >> 1), ow = ow0 + (t & 1);
+      if (oh < oh1 && ow < ow1) {
+        const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
+        v[t] = __ldg(reinterpret_cast<const uint4*>(dy + o));
+        const longlong2* ip = reinterpret_cast<const longlong2*>(ind + o);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) ii[t][e2] = __ldg(ip + e2);
+      } else {
+        v[t] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) ii[t][e2] = make_longlong2(-1, -1);  // never an input position
+      }
+    }
+    float s[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        if (ii[t][e2].x == me) s[2 * e2] = __fadd_rn(s[2 * e2], __uint_as_float(wd[e2] << 16));
+        if (ii[t][e2].y == me) s[2 * e2 + 1] = __fadd_rn(s[2 * e2 + 1], __uint_as_float(wd[e2] & 0xffff0000u));
+      }
+    }
+    uint4 out;
+    out.x = pack_bf2(s[0], s[1]);
+    out.y = pack_bf2(s[2], s[3]);
+    out.z = pack_bf2(s[4], s[5]);
+    out.w = pack_bf2(s[6], s[7]);
+    *reinterpret_cast<uint4*>(dx + n * I(g.xs[0]) + h * I(g.xs[2]) + w * I(g.xs[3]) + q * 8) = out;
+  }
+}
+
+// every input position covered by at most two outputs per dimension
+bool two_cover(const PoolGeom& g) {
+  return (long long)(g.kh - 1) * g.dh + 1 <= 2LL * g.sh && (long long)(g.kw - 1) * g.dw + 1 <= 2LL * g.sw;
+}
+
 b2_status make_pool(PoolGeom& g, int64_t N, int64_t C, int64_t H, int64_t W, int64_t OH, int64_t OW, int kh, int kw,
                     int sh, int sw, int ph, int pw, int dh, int dw, const int64_t* xs, const int64_t* ys,
                     const char* who) {
@@ -296,7 +359,10 @@ b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices, const int64_t
   if (!dx || (N * C * OH * OW > 0 && (!dy || !indices))) return set_error(B2_ERR_INVALID, "b2_maxpool2d_bwd: null pointer");
   auto st = static_cast<cudaStream_t>(stream);
   const int sms = cur_sms();
-  if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices) && fits32(g))
+  if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices) && fits32(g) && two_cover(g))
+    maxpool_bwd_nhwc8_two_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
+  else if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices) && fits32(g))
     maxpool_bwd_nhwc8_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(dy), indices, g, static_cast<uint16_t*>(dx));
   else if (dtype == B2_BF16 && nhwc8(g, dx, dy, indices))

@@ -108,6 +108,15 @@ bool general_conv(const at::Tensor& input, const at::Tensor& weight, at::IntArra
   return g.P * g.Kp * 2 <= (int64_t(4) << 30) && g.P < INT32_MAX;
 }
 
+// Slot kind of a column matrix kept on its input's storage: a tag of the
+// window geometry (kinds 0-4 are packed weights), so two convolutions of one
+// input never share one.
+int col_kind(const GeneralConv& g) {
+  uint32_t h = 2166136261u;
+  for (int v : {g.kh, g.kw, g.sy, g.sx, g.py, g.px, g.dy, g.dx}) h = (h ^ uint32_t(v)) * 16777619u;
+  return int(16 + (h & 0x3fffffffu));
+}
+
 at::Tensor im2col(const at::Tensor& x, const GeneralConv& g) {
   const auto dev = x.device().index();
   at::Tensor col = empty({g.P, g.Kp}, at::kBFloat16, dev);
@@ -164,6 +173,11 @@ at::Tensor general_forward(const at::Tensor& input, const at::Tensor& weight, co
   const auto dev = input.device().index();
   c10::cuda::CUDAGuard guard(dev);
   at::Tensor col = im2col(input, g);
+  // the weight gradient multiplies the same column matrix: kept on the
+  // input's storage under its geometry (dropped when the input is written or
+  // freed)
+  if (at::GradMode::is_enabled() && weight.requires_grad() && g_mode.load() > 1)
+    attach_packed_weight(input, col_kind(g), col);
   at::Tensor wk = pack_weight_khwc(weight, g);
   at::Tensor b = bias.defined() ? (bias.is_contiguous() ? bias : bias.contiguous()) : at::Tensor();
   if (b.defined()) materialize(b);
@@ -213,7 +227,8 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> general_backward(const at::Tensor
     count_launch("col2im");
   }
   if (mask[1]) {
-    at::Tensor col = im2col(input, g);
+    at::Tensor col = find_packed_weight(input, col_kind(g));
+    if (!col.defined() || col.dim() != 2 || col.size(0) != g.P || col.size(1) != g.Kp) col = im2col(input, g);
     // dWk[Cout][Kp] = dY^T . col over the P pixels
     at::Tensor dwk = gemm_splitk_f32(1, 0, g.Cout, g.Kp, g.P, dy, g.Cout, col, g.Kp, dev);
     dw = empty({g.Cout, g.Cin, g.kh, g.kw}, weight.scalar_type(), dev);
@@ -412,15 +427,18 @@ at::Tensor pack_rows(const at::Tensor& x) {
 
 at::Tensor pack_weight(const at::Tensor& w_in, bool dgrad) {
   return cached_pack(w_in, dgrad ? 1 : 0, [&] {
-    at::Tensor w = w_in.is_contiguous() ? w_in : w_in.contiguous();
+    // read in place through its strides (a channels-last model's OHWI
+    // weights included); only a weight with negative strides is copied
+    bool strided_ok = true;
+    for (int d = 0; d < 4; ++d) strided_ok = strided_ok && w_in.stride(d) >= 0;
+    at::Tensor w = strided_ok ? w_in : w_in.contiguous();
     materialize(w);
     const int Cout = int(w.size(0)), Cin = int(w.size(1));
     const int ch = chunks_of(dgrad ? Cout : Cin);
     at::Tensor wk = empty({dgrad ? Cin : Cout, int64_t(ch) * 576}, at::kBFloat16, w.device().index());
-    if (dgrad)
-      XDNA_B2(b2_pack_weight_dgrad_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
-    else
-      XDNA_B2(b2_pack_weight_fwd_bf16(w.data_ptr(), Cout, Cin, ch, wk.data_ptr(), stream(w.device().index())));
+    const int64_t st[4] = {w.stride(0), w.stride(1), w.stride(2), w.stride(3)};
+    XDNA_B2(b2_pack_weight_strided_bf16(w.data_ptr(), st, Cout, Cin, ch, dgrad ? 1 : 0, wk.data_ptr(),
+                                        stream(w.device().index())));
     count_launch("pack_weight");
     return wk;
   });
@@ -671,7 +689,9 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     } else if (g_mode.load() > 1) {
       if (!dy_rows.defined()) dy_rows = pack_rows(grad_output);
       at::Tensor x_rows = find_rows(input);
-      if (!x_rows.defined()) x_rows = pack_rows(input);
+      if (!x_rows.defined() || x_rows.dim() != 2 || x_rows.size(0) != int64_t(B) * (H + 2) * (W + 2) ||
+          x_rows.size(1) != int64_t(chunks_of(Cin)) * 64)
+        x_rows = pack_rows(input);
       if (deferral_enabled()) {
         defer_write(dw, [dy_rows, x_rows, gw = dw.data_ptr(), dtype = dw.scalar_type(), dev, B, Cin, H, W, Cout]() {
           launch_wgrad(dy_rows, x_rows, gw, dtype, dev, B, Cin, H, W, Cout);

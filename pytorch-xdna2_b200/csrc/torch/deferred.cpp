@@ -64,6 +64,14 @@ struct EpiSlot {
   std::vector<void*> inputs;
 };
 std::unordered_map<void*, EpiSlot> g_epi;            // output storage -> slot
+// gated BatchNorm outputs (storage -> source and the output's geometry)
+struct GateSlot {
+  std::shared_ptr<GateSource> src;
+  std::vector<int64_t> sizes, strides;
+  int64_t offset = 0;
+};
+std::unordered_map<void*, GateSlot> g_gates;
+std::atomic<int64_t> g_ngates{0};
 std::unordered_multimap<void*, void*> g_readers;     // input storage -> pending output storage
 std::atomic<int64_t> g_nreaders{0};
 int64_t g_folded = 0;
@@ -230,8 +238,15 @@ void on_release(void* ptr) {
   Attachment att;
   std::vector<WeightSlot> slots;
   EpiSlot epi;
+  GateSlot gate;
   {
     std::lock_guard<std::mutex> lk(g_mu);
+    auto gs = g_gates.find(ptr);
+    if (gs != g_gates.end()) {
+      gate = std::move(gs->second);
+      g_gates.erase(gs);
+      g_ngates.store(int64_t(g_gates.size()));
+    }
     auto ws = g_wslots.find(ptr);
     if (ws != g_wslots.end()) {
       slots = std::move(ws->second);
@@ -252,6 +267,28 @@ void on_release(void* ptr) {
       g_attach.erase(at);
     }
   }
+}
+
+void note_gate_source(void* storage_data, std::vector<int64_t> sizes, std::vector<int64_t> strides, int64_t offset,
+                      std::shared_ptr<GateSource> src) {
+  if (!storage_data) return;
+  GateSlot fresh{std::move(src), std::move(sizes), std::move(strides), offset};
+  GateSlot old;
+  std::lock_guard<std::mutex> lk(g_mu);
+  GateSlot& slot = g_gates[storage_data];
+  old = std::move(slot);
+  slot = std::move(fresh);
+  g_ngates.store(int64_t(g_gates.size()));
+}
+
+std::shared_ptr<GateSource> find_gate_source(const at::Tensor& y) {
+  if (g_ngates.load(std::memory_order_relaxed) == 0 || !y.defined() || !y.has_storage()) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_gates.find(y.storage().mutable_data());
+  if (it == g_gates.end()) return nullptr;
+  const GateSlot& s = it->second;
+  if (s.sizes != y.sizes().vec() || s.strides != y.strides().vec() || s.offset != y.storage_offset()) return nullptr;
+  return s.src;
 }
 
 void note_dgrad() {
@@ -280,7 +317,8 @@ std::map<std::string, int64_t> deferred_stats() {
           {"dropped", g_dropped},          {"kicks", g_kicks},       {"k_learned", g_k_learned},
           {"attached_rows", int64_t(g_attach.size())}, {"packed_weights", int64_t(g_wslots.size())},
           {"packed_weight_hits", g_whits}, {"packed_weight_misses", g_wmisses},
-          {"folded_tails", g_folded}, {"pending_tails", int64_t(g_epi.size())}};
+          {"folded_tails", g_folded}, {"pending_tails", int64_t(g_epi.size())},
+          {"gated_outputs", int64_t(g_gates.size())}};
 }
 
 void note_write(const at::Tensor& t) {

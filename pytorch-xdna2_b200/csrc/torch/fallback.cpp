@@ -193,7 +193,7 @@ void relu_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
   const at::Tensor self = (*stack)[stack->size() - 1].toTensor();
   if (g_bn_epilogue.load() && self.device().type() == kXdna) {
     auto spec = find_epilogue(self);
-    if (spec && !spec->relu) {
+    if (spec && !spec->relu && !spec->gate) {
       spec->relu = true;
       note_folded();
       return;  // the stack holds self, the op's return
@@ -212,7 +212,7 @@ void add_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
         other.sizes() == self.sizes() && other.strides() == self.strides() &&
         other.storage().data() != self.storage().data()) {
       auto spec = find_epilogue(self);
-      if (spec && !spec->relu && !spec->residual.defined()) {
+      if (spec && !spec->relu && !spec->residual.defined() && !spec->gate) {
         materialize(other);
         spec->residual = other;
         add_epilogue_input(self, other);

@@ -7,6 +7,7 @@
 // weight, bias, running statistics absent or bf16 / fp32 xdna vectors of C
 // elements.  save_mean / save_invstd are fp32.  Evaluation mode and every
 // other case run ATen's CUDA kernels on zero-copy CUDA aliases.
+#include <ATen/ops/threshold_backward.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
@@ -104,9 +105,25 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
     if (w.defined()) materialize(w);
     if (b.defined()) materialize(b);
     void* y = out.data_ptr();  // raw: an unread output must stay free to drop its pass
-    defer_epilogue(out, {input, w, b}, spec, [input, w, b, stats, spec, y, layout, pdt, N, C, HW, dev]() {
+    // the output's geometry, to register it as a gated output when its pass
+    // folded a relu_ and no residual (the pass runs while the output lives)
+    auto geo = std::make_shared<std::pair<std::vector<int64_t>, std::vector<int64_t>>>(out.sizes().vec(),
+                                                                                      out.strides().vec());
+    defer_epilogue(out, {input, w, b}, spec, [input, w, b, stats, spec, y, layout, pdt, N, C, HW, dev, geo]() {
       c10::cuda::CUDAGuard guard(dev);
       const at::Tensor& r = spec->residual;
+      if (spec->relu && !r.defined() && layout == 1) {
+        auto src = std::make_shared<GateSource>();
+        src->x = input;
+        src->w = w;
+        src->b = b;
+        src->stats = stats;
+        src->x_version = int64_t(input._version());
+        src->w_version = w.defined() ? int64_t(w._version()) : 0;
+        src->b_version = b.defined() ? int64_t(b._version()) : 0;
+        src->pdtype = pdt;
+        note_gate_source(y, geo->first, geo->second, 0, std::move(src));
+      }
       KernelTimer kt(r.defined() ? "bn.apply_res" : "bn.apply", (r.defined() ? 6.0 : 4.0) * double(input.numel()),
                      stream(dev));
       XDNA_B2(b2_batch_norm_apply_bf16(input.data_ptr(), layout, w.defined() ? w.data_ptr() : nullptr,
@@ -150,10 +167,47 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
   }
   const auto dev = input.device().index();
   const auto mf = layout == 1 ? c10::MemoryFormat::ChannelsLast : c10::MemoryFormat::Contiguous;
-  // the gradient in the input's memory order (a copy only when they differ)
-  at::Tensor g = grad_out.is_contiguous(mf) ? grad_out : grad_out.contiguous(mf);
   const int64_t N = input.size(0), HW = input.numel() / (N * C);
   const auto gdt = defined(weight) ? weight->scalar_type() : at::kFloat;
+  // grad_out still pending as threshold_backward(grad, y, 0) of this
+  // BatchNorm's own gated output: one backward from `grad`, the ReLU's gate
+  // recomputed from x (the pending pass is never run unless read elsewhere)
+  if (auto spec = layout == 1 ? find_epilogue(grad_out) : nullptr; spec && spec->gate) {
+    const GateSource& src = *spec->gate;
+    const at::Tensor& gg = spec->gate_grad;
+    const bool same_bn =
+        src.x.is_same(input) && int64_t(input._version()) == src.x_version &&
+        save_mean->data_ptr() == src.stats[0].data_ptr() && save_invstd->data_ptr() == src.stats[1].data_ptr() &&
+        (defined(weight) ? (src.w.defined() && weight->is_same(src.w) && int64_t(src.w._version()) == src.w_version)
+                         : !src.w.defined()) &&
+        (!src.b.defined() || int64_t(src.b._version()) == src.b_version) && gg.is_contiguous(mf);
+    if (same_bn) {
+      at::Tensor gi, gw, gb;
+      if (mask[0]) gi = empty(input.sizes(), at::kBFloat16, dev, mf);
+      if (mask[1]) gw = empty({C}, gdt, dev);
+      if (mask[2]) gb = empty({C}, gdt, dev);
+      const int64_t wsb = int64_t(b2_batch_norm_workspace_bytes(N, C, HW, 1));
+      at::Tensor ws = empty({std::max<int64_t>(wsb, 16)}, at::kByte, dev);
+      materialize(gg);
+      materialize(input);
+      c10::cuda::CUDAGuard guard(dev);
+      KernelTimer kt("bn.bwd_relu", (mask[0] ? 10.0 : 4.0) * double(input.numel()), stream(dev));
+      const b2_status st = b2_batch_norm_relu_bwd_bf16(
+          gg.data_ptr(), input.data_ptr(), src.w.defined() ? src.w.data_ptr() : nullptr,
+          src.b.defined() ? src.b.data_ptr() : nullptr, src.pdtype, save_mean->data_ptr<float>(),
+          save_invstd->data_ptr<float>(), mask[0] ? gi.data_ptr() : nullptr, mask[1] ? gw.data_ptr() : nullptr,
+          mask[2] ? gb.data_ptr() : nullptr, gdt == at::kFloat ? B2_F32 : B2_BF16, N, C, HW, ws.data_ptr(),
+          size_t(ws.numel()), stream(dev));
+      if (st == B2_OK) {
+        count_launch("batch_norm.bwd_relu", mask[0] ? 3 : 2);
+        return {gi, gw, gb};
+      }
+      TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_batch_norm_relu_bwd_bf16 failed (", st, "): ",
+                  b2_last_error());
+    }
+  }
+  // the gradient in the input's memory order (a copy only when they differ)
+  at::Tensor g = grad_out.is_contiguous(mf) ? grad_out : grad_out.contiguous(mf);
   at::Tensor gi, gw, gb;
   if (mask[0]) gi = empty(input.sizes(), at::kBFloat16, dev, mf);
   if (mask[1]) gw = empty({C}, gdt, dev);
@@ -173,11 +227,49 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
   return {gi, gw, gb};
 }
 
+// ReLU backward (autograd's ReluBackward: threshold_backward(grad, result,
+// 0)).  On a gated BatchNorm output the result is left pending: that
+// BatchNorm's backward, its only reader, takes `grad` instead and recomputes
+// the gate (b2_batch_norm_relu_bwd_bf16), so this pass never runs; any other
+// reader runs it first.  Everything else takes ATen's CUDA kernel on aliases.
+at::Tensor threshold_backward(const at::Tensor& grad, const at::Tensor& self, const at::Scalar& threshold) {
+  const auto cl = c10::MemoryFormat::ChannelsLast;
+  std::shared_ptr<GateSource> src;
+  if (g_bn_epilogue.load() && g_mode.load() > 1 && threshold.toDouble() == 0.0 &&
+      grad.scalar_type() == at::kBFloat16 && self.scalar_type() == at::kBFloat16 && grad.dim() == 4 &&
+      grad.sizes() == self.sizes() && grad.is_contiguous(cl) && self.is_contiguous(cl) &&
+      grad.device() == self.device()) {
+    materialize(self);  // a pending output pass registers its gate when it runs
+    src = find_gate_source(self);
+  }
+  if (src) {
+    const auto dev = self.device().index();
+    at::Tensor dz = empty(self.sizes(), at::kBFloat16, dev, cl);
+    auto spec = std::make_shared<EpiSpec>();
+    spec->gate_grad = grad;
+    spec->gate = std::move(src);
+    // raw: an unread gradient must stay free to drop its pass
+    defer_epilogue(dz, {grad, self}, spec,
+                   [grad, self, ptr = dz.data_ptr(), sizes = dz.sizes().vec(), strides = dz.strides().vec(), dev]() {
+                     c10::cuda::CUDAGuard guard(dev);
+                     count_fallback("aten::threshold_backward");
+                     at::Tensor out = at::from_blob(ptr, sizes, strides,
+                                                    at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, dev));
+                     at::threshold_backward_out(out, to_cuda(grad), to_cuda(self), 0);
+                   });
+    return dz;
+  }
+  count_fallback("aten::threshold_backward");
+  c10::cuda::CUDAGuard g(self.device().index());
+  return adopt(at::threshold_backward(to_cuda(grad), to_cuda(self), threshold));
+}
+
 }  // namespace
 
 TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("native_batch_norm", native_batch_norm);
   m.impl("native_batch_norm_backward", native_batch_norm_backward);
+  m.impl("threshold_backward", threshold_backward);
 }
 
 }  // namespace xdna

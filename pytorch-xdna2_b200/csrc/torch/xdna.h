@@ -85,6 +85,14 @@ extern std::atomic<int64_t> g_pending_jobs;
 void attach_rows(const at::Tensor& input, const at::Tensor& rows);
 at::Tensor find_rows(const at::Tensor& input);
 
+// A BatchNorm output pass that folded a relu_ and no residual: its output y
+// is relu(bf16(x*scale + shift)), so the ReLU's gate can be recomputed from
+// the BatchNorm's input and parameters (b2_batch_norm_relu_bwd_bf16).
+struct GateSource {
+  at::Tensor x, w, b, stats;  // stats: [2][C] fp32 (save_mean, save_invstd)
+  int64_t x_version = 0, w_version = 0, b_version = 0;
+  int pdtype = 0;
+};
 // Fused tails of a deferred producer (a BatchNorm whose output pass waits for
 // its first reader): the in-place ops that follow it on exactly its output
 // tensor (a residual add_, then a relu_) fold into that pass instead of
@@ -95,7 +103,17 @@ at::Tensor find_rows(const at::Tensor& input);
 struct EpiSpec {
   at::Tensor residual;
   bool relu = false;
+  // a pending ReLU input gradient (threshold_backward(grad, y, 0) with y a
+  // gated BatchNorm output): its BatchNorm's backward reads `grad` and
+  // recomputes the gate instead of running the pass; nothing folds into it
+  at::Tensor gate_grad;
+  std::shared_ptr<GateSource> gate;
 };
+// The gated BatchNorm output y (registered when its output pass is enqueued;
+// dropped when y's storage is released) and its lookup by exact geometry.
+void note_gate_source(void* storage_data, std::vector<int64_t> sizes, std::vector<int64_t> strides, int64_t offset,
+                      std::shared_ptr<GateSource> src);
+std::shared_ptr<GateSource> find_gate_source(const at::Tensor& y);
 void defer_epilogue(const at::Tensor& out, const std::vector<at::Tensor>& inputs, std::shared_ptr<EpiSpec> spec,
                     std::function<void()> job);
 std::shared_ptr<EpiSpec> find_epilogue(const at::Tensor& t);  // t is exactly a pending output

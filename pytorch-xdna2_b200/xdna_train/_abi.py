@@ -51,6 +51,7 @@ SIGNATURES = {
     "b2_channel_sum_nhwc_bf16": [vp, i64, i64, i64, i32, i32, i32, i32, vp, i32, vp, sz, vp],
     "b2_pack_weight_fwd_bf16": [vp, i32, i32, i32, vp, vp],
     "b2_pack_weight_dgrad_bf16": [vp, i32, i32, i32, vp, vp],
+    "b2_pack_weight_strided_bf16": [vp, vp, i32, i32, i32, i32, vp, vp],
     "b2_nchw_to_nhwc_bf16": [vp, vp, i32, i32, i32, vp],
     "b2_nhwc_to_nchw_bf16": [vp, vp, i32, i32, i32, vp],
     "b2_conv3x3_fwd": [vp, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp],
@@ -104,6 +105,7 @@ SIGNATURES = {
     "b2_batch_norm_workspace_bytes": [i64, i64, i64, i32],
     "b2_batch_norm_fwd_bf16": [vp, i32, vp, vp, i32, vp, vp, i32, vp, vp, vp, i64, i64, i64, f32, f32, vp, sz, vp],
     "b2_batch_norm_bwd_bf16": [vp, vp, i32, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
+    "b2_batch_norm_relu_bwd_bf16": [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
     "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
     "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
 }

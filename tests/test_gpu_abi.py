@@ -117,6 +117,26 @@ def test_pack_weights_bit_exact(cuda, co_ci):
     assert np.array_equal(bits(wk_of(wd, dgrad=True)), oracle.pack_weight(bits(w), dgrad=True))
 
 
+@pytest.mark.parametrize("co_ci", [(128, 70), (64, 64), (3, 10), (256, 130)])
+def test_pack_weights_strided_bit_exact(cuda, co_ci):
+    """Packing read through the weight's strides: a channels-last (OHWI)
+    weight and a transposed view give the oracle's packed forms."""
+    import ctypes
+    Cout, Cin = co_ci
+    w = torch.randn(Cout, Cin, 3, 3).bfloat16()
+    views = [w.to(cuda).contiguous(memory_format=torch.channels_last),
+             w.transpose(2, 3).contiguous().to(cuda).transpose(2, 3)]
+    for wd in views:
+        assert wd.shape == w.shape and not wd.is_contiguous()
+        for dgrad in (0, 1):
+            chunks = -(-(Cout if dgrad else Cin) // 64)
+            wk = torch.empty((Cin if dgrad else Cout), chunks * 576, dtype=torch.bfloat16, device=cuda)
+            strides = (ctypes.c_int64 * 4)(*wd.stride())
+            _abi.call("b2_pack_weight_strided_bf16", wd.data_ptr(), strides, Cout, Cin, chunks, dgrad,
+                      wk.data_ptr(), st())
+            assert np.array_equal(bits(wk), oracle.pack_weight(bits(w), dgrad=bool(dgrad)))
+
+
 def test_nchw_nhwc_roundtrip_bit_exact(cuda):
     x = torch.randn(3, 70, 9, 13, device=cuda).bfloat16()
     y = torch.empty(3, 9 * 13, 70, dtype=torch.bfloat16, device=cuda)

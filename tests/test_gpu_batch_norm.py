@@ -278,3 +278,136 @@ def test_writes_into_a_pending_pass_inputs_run_it_first():
             y.relu_()
             write(xx, ii)
             assert (y.float().cpu() - ref).abs().max().item() <= 3e-2 * ref.abs().max().item()
+
+
+# ---- the ReLU after a BatchNorm, recomputed in its backward -------------------
+
+@pytest.mark.parametrize("shape", [(8, 64, 14, 14), (4, 256, 7, 7), (2, 2048, 3, 3), (16, 8, 5, 5)])
+@pytest.mark.parametrize("pdtype", [0, 1])
+def test_batch_norm_relu_bwd_abi_bit_exact(cuda, shape, pdtype):
+    """b2_batch_norm_relu_bwd_bf16 (gate recomputed from x) against the two
+    passes it replaces: ATen's threshold_backward(dy, y, 0) on the forward's
+    ReLU output, then b2_batch_norm_bwd_bf16 -- bit for bit.  x carries exact
+    zeros of the affine output, a NaN and an inf, so every branch of the gate
+    is taken."""
+    N, C, H, W = shape
+    rng = np.random.default_rng(N + C + H)
+    xn = rng.standard_normal(shape).astype(np.float32) * 1.3 + 0.2
+    xn[0, 0, 0, 0] = np.nan
+    xn[-1, -1, -1, -1] = np.inf
+    x = torch.from_numpy(xn).bfloat16()
+    dy = torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).bfloat16()
+    pt = torch.float32 if pdtype == 1 else torch.bfloat16
+    w = torch.from_numpy(rng.uniform(0.5, 1.5, C).astype(np.float32)).to(pt)
+    b = torch.from_numpy(rng.standard_normal(C).astype(np.float32) * 0.3).to(pt)
+    if pdtype == 1:
+        # channel 1: affine outputs z straddling 2^-134, where bf16(z) turns
+        # from zero (the tie included) to the smallest positive bf16
+        w[1] = 2.0 ** -140
+        b[1] = 2.0 ** -134
+    cl = torch.channels_last
+    xd, dyd = x.to(cuda).contiguous(memory_format=cl), dy.to(cuda).contiguous(memory_format=cl)
+    wd, bd = w.to(cuda), b.to(cuda)
+    y = torch.empty_like(xd)
+    sm = torch.empty(C, dtype=torch.float32, device=cuda)
+    si = torch.empty_like(sm)
+    nws = _abi.lib().b2_batch_norm_workspace_bytes(N, C, H * W, 1)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=cuda)
+    _abi.call("b2_batch_norm_stats_bf16", xd.data_ptr(), 1, pdtype, None, None, pdtype, sm.data_ptr(), si.data_ptr(),
+              N, C, H * W, ctypes.c_float(0.1), ctypes.c_float(1e-5), ws.data_ptr(), nws, st())
+    _abi.call("b2_batch_norm_apply_bf16", xd.data_ptr(), 1, wd.data_ptr(), bd.data_ptr(), pdtype, sm.data_ptr(),
+              si.data_ptr(), None, 1, y.data_ptr(), N, C, H * W, st())
+    dz = torch.ops.aten.threshold_backward(dyd, y, 0)
+    outs = {}
+    for name, fn, g in (("plain", "b2_batch_norm_bwd_bf16", dz), ("fused", "b2_batch_norm_relu_bwd_bf16", dyd)):
+        dx = torch.empty_like(xd)
+        dw = torch.empty(C, dtype=pt, device=cuda)
+        db = torch.empty_like(dw)
+        if name == "plain":
+            _abi.call(fn, g.data_ptr(), xd.data_ptr(), 1, wd.data_ptr(), pdtype, sm.data_ptr(), si.data_ptr(),
+                      dx.data_ptr(), dw.data_ptr(), db.data_ptr(), pdtype, N, C, H * W, ws.data_ptr(), nws, st())
+        else:
+            _abi.call(fn, g.data_ptr(), xd.data_ptr(), wd.data_ptr(), bd.data_ptr(), pdtype, sm.data_ptr(),
+                      si.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), pdtype, N, C, H * W, ws.data_ptr(),
+                      nws, st())
+        torch.cuda.synchronize()
+        outs[name] = (dx, dw, db)
+    for a, b_ in zip(outs["plain"], outs["fused"]):
+        assert torch.equal(a.view(torch.int16 if a.dtype == torch.bfloat16 else torch.int32),
+                           b_.view(torch.int16 if b_.dtype == torch.bfloat16 else torch.int32))
+
+
+def _relu_block(cl, gated, seed=3):
+    """conv -> BatchNorm -> relu_ -> conv -> BatchNorm -> relu_ (torchvision's
+    Bottleneck pattern), forward and backward on xdna; returns every gradient."""
+    torch.manual_seed(seed)
+    c1 = nn.Conv2d(32, 64, 3, padding=1, bias=False).bfloat16()
+    b1 = nn.BatchNorm2d(64).bfloat16()
+    c2 = nn.Conv2d(64, 64, 1, bias=False).bfloat16()
+    b2 = nn.BatchNorm2d(64).bfloat16()
+    with torch.no_grad():
+        b1.weight.uniform_(0.5, 1.5)
+        b1.bias.normal_(0, 0.3)
+    x = torch.randn(4, 32, 12, 12).bfloat16()
+    g = torch.randn(4, 64, 12, 12).bfloat16()
+    mods = [m.to(X) for m in (c1, b1, c2, b2)]
+    mf = torch.channels_last if cl else torch.contiguous_format
+    for m in mods:
+        m.to(memory_format=mf)
+    xx = x.to(X).contiguous(memory_format=mf).requires_grad_()
+    xdna_train.set_fusion(bn_epilogue=gated)
+    out = mods[0](xx)
+    out = mods[1](out)
+    out.relu_()
+    out = mods[2](out)
+    out = mods[3](out)
+    out.relu_()
+    out.backward(g.to(X).contiguous(memory_format=mf))
+    res = {"dx": xx.grad.cpu(), "dc1": mods[0].weight.grad.cpu(), "dg1": mods[1].weight.grad.cpu(),
+           "db1": mods[1].bias.grad.cpu(), "dc2": mods[2].weight.grad.cpu(), "dg2": mods[3].weight.grad.cpu(),
+           "db2": mods[3].bias.grad.cpu(), "y": out.detach().cpu()}
+    return res
+
+
+@pytest.mark.parametrize("cl", [False, True])
+def test_relu_backward_folds_into_batch_norm_backward(cl):
+    """threshold_backward of a BatchNorm output that folded the relu_ stays
+    pending; the BatchNorm's backward recomputes the gate from x and never
+    runs that pass (channels-last); the results equal the unfused run's bit
+    for bit."""
+    try:
+        xdna_train.reset_fallback_stats()
+        fused = _relu_block(cl, True)
+        fb = xdna_train.fallback_stats()
+        n_relu = launched("batch_norm.bwd_relu")
+        xdna_train.reset_fallback_stats()
+        plain = _relu_block(cl, False)
+        fp = xdna_train.fallback_stats()
+    finally:
+        xdna_train.set_fusion(bn_epilogue=True)
+    calls = lambda d, k: d.get(k, {}).get("calls", 0)  # noqa: E731
+    if cl:
+        assert n_relu > 0 and calls(fb, "aten::threshold_backward") == 0
+    assert calls(fp, "aten::threshold_backward") + calls(fp, "aten::threshold_backward.grad_input") == 2
+    for k in fused:
+        assert torch.equal(fused[k].float(), plain[k].float()), k
+
+
+def test_gated_gradient_read_elsewhere_runs_its_pass():
+    """A hook that reads the pending ReLU input gradient runs its pass, and
+    the BatchNorm backward then takes the plain path on it: same results."""
+    torch.manual_seed(5)
+    bn = nn.BatchNorm2d(16).bfloat16().to(X).to(memory_format=torch.channels_last)
+    x = torch.randn(2, 16, 6, 6).bfloat16()
+    g = torch.randn(2, 16, 6, 6).bfloat16()
+    seen = []
+    grads = []
+    for hook in (False, True):
+        xx = x.to(X).contiguous(memory_format=torch.channels_last).requires_grad_()
+        y = bn(xx)
+        if hook:
+            y.register_hook(lambda t: seen.append(t.float().cpu()))
+        y.relu_()
+        y.backward(g.to(X).contiguous(memory_format=torch.channels_last))
+        grads.append(xx.grad.cpu())
+    assert seen and torch.equal(grads[0].float(), grads[1].float())
