@@ -465,6 +465,10 @@ def run_conv_reference(args):
 
 # ------------------------------------------------------- headline: ResNet-50
 
+# in-step timer labels whose work is algorithmic bytes (HBM-bound passes)
+MEM_LABELS = ("bn.", "relu_bwd_sum")
+
+
 def resnet50_model(dev):
     """torchvision ResNet-50 (random init, seed 0) in bf16, channels-last."""
     from torchvision.models import resnet50
@@ -705,10 +709,10 @@ def run_resnet50(args):
                      "ms_per_launch": round(c_ms / max(1, c_launch), 5),
                      "peak_kind": f"{peak_kind}, sustained (kernels timed inside a long step)"},
         # work is FLOPs for the convolutions and GEMMs, algorithmic bytes for
-        # the BatchNorm passes ("bn.*", reported as GB/s)
+        # the BatchNorm and gradient passes (MEM_LABELS, reported as GB/s)
         "kernel_times_per_step": {k: {"launches": round(v["launches"] / 3, 1), "ms": round(v["ms"] / 3, 4),
-                                      ("gbs" if k.startswith("bn.") else "tflops"):
-                                      (round(v["work"] / (v["ms"] * 1e-3) / (1e9 if k.startswith("bn.") else 1e12), 1)
+                                      ("gbs" if k.startswith(MEM_LABELS) else "tflops"):
+                                      (round(v["work"] / (v["ms"] * 1e-3) / (1e9 if k.startswith(MEM_LABELS) else 1e12), 1)
                                        if v["ms"] else None)}
                                   for k, v in sorted(kt.items())},
         "step_tflops": round(total_fl / (ms * 1e-3) / 1e12, 1),

@@ -527,6 +527,17 @@ b2_status b2_batch_norm_relu_bwd_bf16(const void* dy, const void* x,
                                       int64_t C, int64_t HW, void* workspace,
                                       size_t workspace_bytes, void* stream);
 
+/* A ReLU's backward on the sum of two gradients, in one pass over n bf16
+ * elements of four dense tensors with the same layout (16-byte aligned, n a
+ * multiple of 8):  dz = (y > 0 or y is NaN) ? bf16(float(a) + float(b)) : +0
+ * -- bit for bit ATen's in-place add a += b (fp32 add, hardware round to
+ * nearest even) followed by threshold_backward(a, y, 0).  Autograd sums the
+ * two gradients of a residual block's output this way before the block's
+ * ReLU backward; the reference runs both ops on its CPU-alias fallback
+ * (torch_xdna_device.cpp:5124-5260). */
+b2_status b2_relu_bwd_sum_bf16(const void* a, const void* b, const void* y,
+                               void* dz, int64_t n, void* stream);
+
 /* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
  * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,
  * region_kernels.cpp:309-460; used by regions.fuse_norm_activation,

@@ -193,7 +193,7 @@ void relu_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
   const at::Tensor self = (*stack)[stack->size() - 1].toTensor();
   if (g_bn_epilogue.load() && self.device().type() == kXdna) {
     auto spec = find_epilogue(self);
-    if (spec && !spec->relu && !spec->gate) {
+    if (spec && spec->foldable() && !spec->relu) {
       spec->relu = true;
       note_folded();
       return;  // the stack holds self, the op's return
@@ -212,11 +212,37 @@ void add_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
         other.sizes() == self.sizes() && other.strides() == self.strides() &&
         other.storage().data() != self.storage().data()) {
       auto spec = find_epilogue(self);
-      if (spec && !spec->relu && !spec->residual.defined() && !spec->gate) {
+      if (spec && spec->foldable() && !spec->relu && !spec->residual.defined()) {
         materialize(other);
         spec->residual = other;
         add_epilogue_input(self, other);
         note_folded();
+        torch::jit::drop(*stack, 3);
+        stack->push_back(self);
+        return;
+      }
+      // a gradient sum inside backward (autograd adds the two gradients of a
+      // tensor used twice, e.g. a residual block's output): left pending on
+      // self, so that a ReLU backward reading it sums both terms in its own
+      // pass; any other reader runs the add first
+      if (!spec && g_mode.load() > 1 && !at::GradMode::is_enabled() && self.dim() == 4 &&
+          self.is_contiguous(at::MemoryFormat::ChannelsLast) && self.numel() >= (int64_t(1) << 20) &&
+          self.numel() % 8 == 0 && (reinterpret_cast<uintptr_t>(self.data_ptr()) & 15) == 0 &&
+          (reinterpret_cast<uintptr_t>(other.data_ptr()) & 15) == 0 && self.device() == other.device() &&
+          !has_pending(self)) {
+        materialize(other);
+        auto sum = std::make_shared<EpiSpec>();
+        sum->pending_sum = other;
+        const auto dev = self.device().index();
+        defer_epilogue(self, {other}, sum,
+                       [ptr = self.data_ptr(), sizes = self.sizes().vec(), strides = self.strides().vec(), other,
+                        dev]() {
+                         c10::cuda::CUDAGuard guard(dev);
+                         count_fallback("aten::add_.Tensor");
+                         at::Tensor s = at::from_blob(ptr, sizes, strides,
+                                                      at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, dev));
+                         s.add_(to_cuda(other));
+                       });
         torch::jit::drop(*stack, 3);
         stack->push_back(self);
         return;

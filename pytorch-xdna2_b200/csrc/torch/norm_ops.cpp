@@ -234,6 +234,26 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
 // reader runs it first.  Everything else takes ATen's CUDA kernel on aliases.
 at::Tensor threshold_backward(const at::Tensor& grad, const at::Tensor& self, const at::Scalar& threshold) {
   const auto cl = c10::MemoryFormat::ChannelsLast;
+  // the gradient is a pending sum (grad += other, left by add_): both terms
+  // summed and gated in one pass; grad's own pass is never run unless read
+  if (g_mode.load() > 1 && threshold.toDouble() == 0.0 && grad.scalar_type() == at::kBFloat16 &&
+      self.scalar_type() == at::kBFloat16 && grad.dim() == 4 && grad.sizes() == self.sizes() &&
+      grad.strides() == self.strides() && grad.is_contiguous(cl) && grad.device() == self.device()) {
+    if (auto sum = find_epilogue(grad); sum && sum->pending_sum.defined()) {
+      const auto dev = self.device().index();
+      materialize(self);
+      at::Tensor dz = empty(self.sizes(), at::kBFloat16, dev, cl);
+      c10::cuda::CUDAGuard guard(dev);
+      KernelTimer kt("relu_bwd_sum", 8.0 * double(self.numel()), stream(dev));
+      const b2_status st = b2_relu_bwd_sum_bf16(grad.data_ptr(), sum->pending_sum.data_ptr(), self.data_ptr(),
+                                                dz.data_ptr(), self.numel(), stream(dev));
+      if (st == B2_OK) {
+        count_launch("relu_bwd_sum");
+        return dz;
+      }
+      TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_relu_bwd_sum_bf16 failed (", st, "): ", b2_last_error());
+    }
+  }
   std::shared_ptr<GateSource> src;
   if (g_bn_epilogue.load() && g_mode.load() > 1 && threshold.toDouble() == 0.0 &&
       grad.scalar_type() == at::kBFloat16 && self.scalar_type() == at::kBFloat16 && grad.dim() == 4 &&

@@ -108,6 +108,12 @@ struct EpiSpec {
   // recomputes the gate instead of running the pass; nothing folds into it
   at::Tensor gate_grad;
   std::shared_ptr<GateSource> gate;
+  // a pending in-place sum (self += pending_sum, both bf16, same layout):
+  // a ReLU backward on it reads both terms and sums them in its own pass
+  // (b2_relu_bwd_sum_bf16); nothing folds into it
+  at::Tensor pending_sum;
+  // add_ / relu_ may fold into this pending output: only a BatchNorm's pass
+  bool foldable() const { return !gate && !pending_sum.defined(); }
 };
 // The gated BatchNorm output y (registered when its output pass is enqueued;
 // dropped when y's storage is released) and its lookup by exact geometry.

@@ -106,6 +106,7 @@ SIGNATURES = {
     "b2_batch_norm_fwd_bf16": [vp, i32, vp, vp, i32, vp, vp, i32, vp, vp, vp, i64, i64, i64, f32, f32, vp, sz, vp],
     "b2_batch_norm_bwd_bf16": [vp, vp, i32, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
     "b2_batch_norm_relu_bwd_bf16": [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
+    "b2_relu_bwd_sum_bf16": [vp, vp, vp, vp, i64, vp],
     "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
     "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
 }

@@ -411,3 +411,78 @@ def test_gated_gradient_read_elsewhere_runs_its_pass():
         y.backward(g.to(X).contiguous(memory_format=torch.channels_last))
         grads.append(xx.grad.cpu())
     assert seen and torch.equal(grads[0].float(), grads[1].float())
+
+
+# ---- a residual block's gradient sum, fused with its ReLU backward ------------
+
+@pytest.mark.parametrize("n", [8, 4096, 1 << 20])
+def test_relu_bwd_sum_abi_bit_exact(cuda, n):
+    """b2_relu_bwd_sum_bf16 against ATen's own two ops on the GPU -- a += b,
+    then threshold_backward(a, y, 0) -- bit for bit, with y holding NaN, +0,
+    -0 and negatives and a + b overflowing to inf and producing NaN."""
+    g = torch.Generator().manual_seed(n)
+    a = torch.randn(n, generator=g).bfloat16()
+    b = torch.randn(n, generator=g).bfloat16()
+    y = torch.randn(n, generator=g).bfloat16()
+    y[:4] = torch.tensor([float("nan"), 0.0, -0.0, -1.0]).bfloat16()
+    a[4:8] = torch.tensor([3e38, float("inf"), float("nan"), -3e38]).bfloat16()
+    b[4:8] = torch.tensor([3e38, float("-inf"), 1.0, -3e38]).bfloat16()
+    y[4:8] = 1.0
+    ad, bd, yd = a.to(cuda), b.to(cuda), y.to(cuda)
+    ref = torch.ops.aten.threshold_backward(ad.clone().add_(bd), yd, 0)
+    dz = torch.empty_like(yd)
+    _abi.call("b2_relu_bwd_sum_bf16", ad.data_ptr(), bd.data_ptr(), yd.data_ptr(), dz.data_ptr(), n, st())
+    torch.cuda.synchronize()
+    assert torch.equal(dz.view(torch.int16).cpu(), ref.view(torch.int16).cpu())
+
+
+def _residual_stack(fused, seed=7):
+    """stem conv -> BatchNorm -> relu_, then two residual blocks
+    (conv -> BatchNorm -> += identity -> relu_) on channels-last xdna tensors:
+    the blocks' inputs are used twice, so backward sums two gradients for each
+    before the ReLU backward of the layer that made it."""
+    torch.manual_seed(seed)
+    convs = [nn.Conv2d(64, 64, 3, padding=1, bias=False).bfloat16() for _ in range(3)]
+    bns = [nn.BatchNorm2d(64).bfloat16() for _ in range(3)]
+    x = torch.randn(8, 64, 48, 48).bfloat16()
+    g = torch.randn(8, 64, 48, 48).bfloat16()
+    cl = torch.channels_last
+    convs = [c.to(X).to(memory_format=cl) for c in convs]
+    bns = [b.to(X) for b in bns]
+    xx = x.to(X).contiguous(memory_format=cl).requires_grad_()
+    xdna_train.set_fusion(bn_epilogue=fused)
+    h = bns[0](convs[0](xx))
+    h.relu_()
+    for i in (1, 2):
+        out = bns[i](convs[i](h))
+        out += h
+        out.relu_()
+        h = out
+    h.backward(g.to(X).contiguous(memory_format=cl))
+    res = {"dx": xx.grad.cpu()}
+    for i in range(3):
+        res[f"dc{i}"] = convs[i].weight.grad.cpu()
+        res[f"dg{i}"] = bns[i].weight.grad.cpu()
+        res[f"db{i}"] = bns[i].bias.grad.cpu()
+    return res
+
+
+def test_gradient_sums_fold_into_relu_backward():
+    """The block inputs' gradient sums stay pending and the ReLU backward that
+    reads them adds and gates in one pass: every gradient equals the unfused
+    run's bit for bit, and the separate add passes are gone."""
+    try:
+        xdna_train.reset_fallback_stats()
+        fused = _residual_stack(True)
+        fb = xdna_train.fallback_stats()
+        n_sum = launched("relu_bwd_sum")
+        xdna_train.reset_fallback_stats()
+        plain = _residual_stack(False)
+        fp = xdna_train.fallback_stats()
+    finally:
+        xdna_train.set_fusion(bn_epilogue=True)
+    calls = lambda d, k: d.get(k, {}).get("calls", 0)  # noqa: E731
+    assert n_sum == 2
+    assert calls(fp, "aten::add_.Tensor") - calls(fb, "aten::add_.Tensor") >= 2
+    for k in fused:
+        assert torch.equal(fused[k].float(), plain[k].float()), k
