@@ -144,6 +144,66 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const u
   }
 }
 
+// As maxpool_fwd_nhwc8_kernel for 3x3 windows (ResNet's stem pool): the up to
+// nine window loads are all issued before the scan, which then visits the
+// valid taps in the same (h, w) order -- the same maxima and indices.
+template <typename I>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_k3_kernel(const uint16_t* __restrict__ x,
+                                                                            PoolGeom g, uint16_t* __restrict__ y,
+                                                                            int64_t* __restrict__ ind) {
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * OH * OW * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / OW, ow = r - r2 * OW;
+    const I n = r2 / OH, oh = r2 - n * OH;
+    I h0, h1, w0, w1;
+    window<I>(oh, g.sh, g.ph, 3, g.dh, H, h0, h1);
+    window<I>(ow, g.sw, g.pw, 3, g.dw, W, w0, w1);
+    const uint16_t* xp = x + n * I(g.xs[0]) + q * 8;
+    uint4 v[9];
+    bool ok[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+      const I h = h0 + I(t / 3) * g.dh, w = w0 + I(t % 3) * g.dw;
+      ok[t] = h < h1 && w < w1;
+      v[t] = ok[t] ? __ldg(reinterpret_cast<const uint4*>(xp + h * I(g.xs[2]) + w * I(g.xs[3])))
+                   : make_uint4(0, 0, 0, 0);
+    }
+    float best[8];
+    long long bi[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      best[e] = -INFINITY;
+      bi[e] = (long long)(h0 * W + w0);
+    }
+#pragma unroll
+    for (int t = 0; t < 9; ++t) {
+      if (!ok[t]) continue;
+      const long long idx = (long long)((h0 + I(t / 3) * g.dh) * W + w0 + I(t % 3) * g.dw);
+      const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
+        if (f > best[e] || f != f) {
+          best[e] = f;
+          bi[e] = idx;
+        }
+      }
+    }
+    const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
+    uint4 out;
+    out.x = pack_bf2(best[0], best[1]);
+    out.y = pack_bf2(best[2], best[3]);
+    out.z = pack_bf2(best[4], best[5]);
+    out.w = pack_bf2(best[6], best[7]);
+    *reinterpret_cast<uint4*>(y + o) = out;
+    longlong2* ip = reinterpret_cast<longlong2*>(ind + o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ip[e] = make_longlong2(bi[2 * e], bi[2 * e + 1]);
+  }
+}
+
 template <typename T, typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_kernel(const T* __restrict__ dy,
                                                                    const int64_t* __restrict__ ind, PoolGeom g,
@@ -326,7 +386,10 @@ b2_status b2_maxpool2d_fwd(const void* x, const int64_t* x_strides, void* y, int
   if (!x || !y || !indices) return set_error(B2_ERR_INVALID, "b2_maxpool2d_fwd: null pointer");
   auto st = static_cast<cudaStream_t>(stream);
   const int sms = cur_sms();
-  if (dtype == B2_BF16 && nhwc8(g, x, y, indices) && fits32(g))
+  if (dtype == B2_BF16 && nhwc8(g, x, y, indices) && fits32(g) && g.kh == 3 && g.kw == 3)
+    maxpool_fwd_nhwc8_k3_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
+        static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
+  else if (dtype == B2_BF16 && nhwc8(g, x, y, indices) && fits32(g))
     maxpool_fwd_nhwc8_kernel<int><<<pool_grid(total / 8, sms), kPoolThreads, 0, st>>>(
         static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), indices);
   else if (dtype == B2_BF16 && nhwc8(g, x, y, indices))
