@@ -9,8 +9,8 @@ torchvision ResNet-50 on ``torch.device("xdna")``, cross-entropy, backward
 all-reduce), SGD momentum 0.9 (``--optimizer adam``: the config's Adam
 variant); with N GPUs the gradients are averaged by bucketed NCCL
 all-reduces overlapped with backward (``xdna_train.ddp``; data parallel, weak
-scaling).  At one GPU the step is captured into a CUDA graph
-(``xdna_train.graphs.make_graphed_step``) and replayed, so the host's per-op
+scaling).  The step (at N > 1 with its NCCL all-reduces) is captured into a
+CUDA graph (``xdna_train.graphs.make_graphed_step``) and replayed, so the host's per-op
 dispatch (about as long as the step's kernels) is out of the timed region;
 ``--eager`` times the step op by op, and the line carries the eager rate
 beside the replayed one.  ``value`` = images/s of the whole job; ``roofline`` = the 3x3
@@ -545,11 +545,12 @@ def run_resnet50(args):
         return loss
 
     # two input buffers (the e2e loop fills one while the other is in use);
-    # with CUDA graphs (the default at one GPU: xdna_train.graphs, the step's
-    # kernels replayed without the host's per-op dispatch) one capture each
+    # with CUDA graphs (the default: xdna_train.graphs, the step's kernels --
+    # and at N > 1 its bucketed NCCL all-reduces -- replayed without the
+    # host's per-op dispatch) one capture each
     bx = [x.clone(memory_format=cl) for _ in range(2)]
     by = [y.clone() for _ in range(2)]
-    graphed = world == 1 and not args.eager
+    graphed = not args.eager
     s = torch.cuda.current_stream()
     if graphed:
         from xdna_train import graphs
@@ -643,6 +644,7 @@ def run_resnet50(args):
         eb.record(s)
         torch.cuda.synchronize()
         eager_ms = ea.elapsed_time(eb) / ne
+        # graphs holding NCCL calls are released before the process group
         for r in replays:
             r.graph.reset()
         del replays, run
@@ -1468,7 +1470,8 @@ def conv1x1_probe(args):
     dgrad, wgrad with its ordered reduce) on ResNet-50's stride-1 shapes at
     ``--batch``, beside ATen's CUDA library kernels for the same convolution
     (``--conv1x1-probe``).  CUDA tensors and the C ABI only; nothing is
-    registered.  FLOPs per direction 2*P*Cin*Cout."""
+    registered.  Each timing replays 20 calls captured into one CUDA graph:
+    device time for both sides.  FLOPs per direction 2*P*Cin*Cout."""
     from xdna_train import _abi
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(0)
@@ -1479,18 +1482,25 @@ def conv1x1_probe(args):
     reps = 20
 
     def med(fn):
-        # `reps` calls back to back per timed region, so that the host-side
-        # cost of each call overlaps the device work of the previous ones
+        # `reps` calls captured into one CUDA graph and replayed, so that both
+        # sides are timed on the device only (no host dispatch between calls)
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(reps):
+                fn()
         ts = []
         for i in range(args.iters + 3):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
-            for _ in range(reps):
-                fn()
+            g.replay()
             e1.record(st)
             torch.cuda.synchronize()
             if i >= 3:
                 ts.append(e0.elapsed_time(e1) / reps)
+        g.reset()
         return sorted(ts)[len(ts) // 2]
 
     rows = []
@@ -1506,13 +1516,17 @@ def conv1x1_probe(args):
         wsb = _abi.lib().b2_conv1x1_wgrad_workspace_bytes(1, b, cin, hw2, cout)
         ws = torch.empty(max(1, wsb), dtype=torch.uint8, device=dev)
         s = st.cuda_stream
+
+        def cs():  # the stream a call is made on (the capture stream inside med)
+            return torch.cuda.current_stream().cuda_stream
+
         ours = {
             "fwd": med(lambda: _abi.call("b2_conv1x1_fwd", x.data_ptr(), w.data_ptr(), None, y.data_ptr(), 1, b, cin,
-                                         hw2, cout, s)),
+                                         hw2, cout, cs())),
             "dgrad": med(lambda: _abi.call("b2_conv1x1_dgrad", dy.data_ptr(), w.data_ptr(), dx.data_ptr(), 1, b, cin,
-                                           hw2, cout, s)),
+                                           hw2, cout, cs())),
             "wgrad": med(lambda: _abi.call("b2_conv1x1_wgrad", dy.data_ptr(), x.data_ptr(), dw.data_ptr(),
-                                           _abi.B2_F32, 1, b, cin, hw2, cout, ws.data_ptr(), wsb, s)),
+                                           _abi.B2_F32, 1, b, cin, hw2, cout, ws.data_ptr(), wsb, cs())),
         }
         ref = torch.nn.functional.conv2d(x, w)
         yo = ref.float()
