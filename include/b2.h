@@ -439,6 +439,36 @@ b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices,
                            int64_t C, int64_t H, int64_t W, int64_t OH,
                            int64_t OW, int kh, int kw, int sh, int sw, int ph,
                            int pw, int dh, int dw, void* stream);
+/* The same pooling with the argmax kept as one byte per output element --
+ * its tap i*kw + j inside the window that starts at (oh*sh - ph, ow*sw - pw)
+ * -- instead of ATen's int64 index: the forward writes y and `taps` (uint8,
+ * y's element strides); b2_maxpool2d_taps_to_indices expands them to exactly
+ * the int64 indices b2_maxpool2d_fwd writes; b2_maxpool2d_bwd_taps is
+ * b2_maxpool2d_bwd reading the taps (same sums in the same order).  The
+ * backward of a ResNet stem reads 1 byte of index per element instead of 8.
+ * Channels-last bf16 (C % 8 == 0, 16-byte aligned tensors, 8-byte aligned
+ * taps), 3x3 windows for the forward, windows spanning at most two strides
+ * for the backward.  Replaces the reference's CPU max_pool2d_with_indices and
+ * its backward (torch_xdna_device.cpp:5124-5260) like the two calls above. */
+b2_status b2_maxpool2d_fwd_taps(const void* x, const int64_t* x_strides,
+                                void* y, void* taps, const int64_t* y_strides,
+                                int64_t N, int64_t C, int64_t H, int64_t W,
+                                int64_t OH, int64_t OW, int kh, int kw, int sh,
+                                int sw, int ph, int pw, int dh, int dw,
+                                void* stream);
+b2_status b2_maxpool2d_taps_to_indices(const void* taps,
+                                       const int64_t* y_strides,
+                                       int64_t* indices, int64_t N, int64_t C,
+                                       int64_t H, int64_t W, int64_t OH,
+                                       int64_t OW, int kh, int kw, int sh,
+                                       int sw, int ph, int pw, int dh, int dw,
+                                       void* stream);
+b2_status b2_maxpool2d_bwd_taps(const void* dy, const void* taps,
+                                const int64_t* y_strides, void* dx,
+                                const int64_t* x_strides, int64_t N, int64_t C,
+                                int64_t H, int64_t W, int64_t OH, int64_t OW,
+                                int kh, int kw, int sh, int sw, int ph, int pw,
+                                int dh, int dw, void* stream);
 
 /* ---- layout ops (replace the reference's host cat / nearest-2x upsample,
  * torch_xdna_device.cpp:3796-4175; used by the xdna `cat`,
@@ -537,6 +567,24 @@ b2_status b2_batch_norm_relu_bwd_bf16(const void* dy, const void* x,
  * (torch_xdna_device.cpp:5124-5260). */
 b2_status b2_relu_bwd_sum_bf16(const void* a, const void* b, const void* y,
                                void* dz, int64_t n, void* stream);
+/* The same gated sum feeding a BatchNorm's backward (the residual block's
+ * last BatchNorm): dz = (y > 0 or NaN) ? bf16(a + b) : +0 is made, written to
+ * dz (its other readers need it) and reduced in one pass, then dx, dw, db as
+ * b2_batch_norm_bwd_bf16 from dy = dz.  Bit for bit b2_relu_bwd_sum_bf16
+ * followed by b2_batch_norm_bwd_bf16 (replaces the reference's CPU add,
+ * threshold_backward and native_batch_norm_backward for this chain,
+ * torch_xdna_device.cpp:4214-4358, 5124-5260).  Channels-last, C a power of
+ * two in [8, 2048]; x, w, statistics and workspace as b2_batch_norm_bwd_bf16
+ * (layout 1); dx may be NULL. */
+b2_status b2_batch_norm_bwd_relu_sum_bf16(const void* a, const void* b,
+                                          const void* y, const void* x,
+                                          const void* w, int pdtype,
+                                          const float* save_mean,
+                                          const float* save_invstd, void* dz,
+                                          void* dx, void* dw, void* db,
+                                          int gdtype, int64_t N, int64_t C,
+                                          int64_t HW, void* workspace,
+                                          size_t workspace_bytes, void* stream);
 
 /* Training BatchNorm2d + LeakyReLU/ReLU on contiguous NCHW bf16 [N, C, HW]
  * (replaces xdna_region_bn_fwd_bf16 / xdna_region_bn_bwd_bf16,

@@ -829,6 +829,33 @@ __device__ __forceinline__ bool stream_units(const uint4* const (&src)[NIN], lon
   return true;
 }
 
+// End of a sums kernel (consumer threads): the rows R = 256 / CV of each
+// channel group reduced in row order through the ring's memory (every copy
+// into it has landed), one partial per channel written channel-major.
+__device__ __forceinline__ void sums_tail(const float (&a)[8], const float (&b)[8], const NhwcShape& sh, int cg,
+                                          bool ok, float* __restrict__ part_a, float* __restrict__ part_b) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  float* red = reinterpret_cast<float*>(ring);  // [2][R][C]
+  const int R = kStreamConsumers / sh.CV, r = threadIdx.x / sh.CV;
+  consumers_sync();
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red[r * sh.C + cg * 8 + e] = a[e];
+    red[(R + r) * sh.C + cg * 8 + e] = b[e];
+  }
+  consumers_sync();
+  if (!ok) return;
+  for (int c = threadIdx.x; c < sh.C; c += kStreamConsumers) {
+    float sa = 0.0f, sb = 0.0f;
+    for (int q = 0; q < R; ++q) {
+      sa = __fadd_rn(sa, red[q * sh.C + c]);
+      sb = __fadd_rn(sb, red[(R + q) * sh.C + c]);
+    }
+    part_a[(long long)c * gridDim.x + blockIdx.x] = sa;  // channel-major
+    part_b[(long long)c * gridDim.x + blockIdx.x] = sb;
+  }
+}
+
 // The ReLU that followed a BatchNorm, recomputed from its input: the forward
 // wrote y = relu(bf16(z)), z = x*scale + shift (bn_tail_fast without a
 // residual), and ATen's threshold_backward passes dy where y > 0 or y is NaN,
@@ -902,28 +929,58 @@ __global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_sums_kernel(
     }
   }, status);
   if (!consumer) return;
-  // the rows R = 256 / CV of each channel group, reduced in row order through
-  // the ring's memory (every copy into it has landed)
-  extern __shared__ __align__(128) uint8_t ring[];
-  float* red = reinterpret_cast<float*>(ring);  // [2][R][C]
-  const int R = kStreamConsumers / sh.CV, r = threadIdx.x / sh.CV;
-  consumers_sync();
+  sums_tail(a, b, sh, cg, ok, part_a, part_b);
+}
+
+// Backward sums of a BatchNorm whose output feeds a ReLU through a residual
+// sum: the gradient at the BatchNorm's output is dz = (y > 0 or NaN) ?
+// bf16(a + b) : +0 (a ReLU backward on the sum of two gradients, as
+// b2_relu_bwd_sum_bf16), made here in the same pass that sums it: dz is
+// written out (its other readers need it) and summed as the plain backward
+// sums its dy.  Inputs in ring order x, a, b, y.
+__global__ void __launch_bounds__(kStreamThreads) bn_nhwc_stream_sums_gsum_kernel(
+    const uint16_t* __restrict__ x, const uint16_t* __restrict__ ga, const uint16_t* __restrict__ gb,
+    const uint16_t* __restrict__ y, const float* __restrict__ mean, const float* __restrict__ invstd, NhwcShape sh,
+    uint16_t* __restrict__ dz_out, float* __restrict__ part_a, float* __restrict__ part_b, int* status) {
+  constexpr int NIN = 4;
+  const bool consumer = threadIdx.x < kStreamConsumers;
+  const int cg = threadIdx.x % sh.CV;
+  float a[8], b[8], k0[8], k1[8];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    red[r * sh.C + cg * 8 + e] = a[e];
-    red[(R + r) * sh.C + cg * 8 + e] = b[e];
-  }
-  consumers_sync();
-  if (!ok) return;
-  for (int c = threadIdx.x; c < sh.C; c += kStreamConsumers) {
-    float sa = 0.0f, sb = 0.0f;
-    for (int q = 0; q < R; ++q) {
-      sa = __fadd_rn(sa, red[q * sh.C + c]);
-      sb = __fadd_rn(sb, red[(R + q) * sh.C + c]);
+  for (int e = 0; e < 8; ++e) a[e] = b[e] = k0[e] = k1[e] = 0.0f;
+  if (consumer) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      k0[e] = mean[cg * 8 + e];
+      k1[e] = invstd[cg * 8 + e];
     }
-    part_a[(long long)c * gridDim.x + blockIdx.x] = sa;  // channel-major
-    part_b[(long long)c * gridDim.x + blockIdx.x] = sb;
   }
+  const uint4* src[NIN] = {reinterpret_cast<const uint4*>(x), reinterpret_cast<const uint4*>(ga),
+                           reinterpret_cast<const uint4*>(gb), reinterpret_cast<const uint4*>(y)};
+  uint4* d4 = reinterpret_cast<uint4*>(dz_out);
+  const bool ok = stream_units<NIN>(src, sh.P * sh.CV, [&](long long u, const uint4(&v)[NIN]) {
+    float fx[8], fa[8], fb[8], fy[8], dz[8];
+    unpack8(v[0], fx);
+    unpack8(v[1], fa);
+    unpack8(v[2], fb);
+    unpack8(v[3], fy);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t hb = !(fy[e] <= 0.0f) ? uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(__fadd_rn(fa[e], fb[e]))))
+                                           : 0u;
+      w[e >> 1] |= hb << (16 * (e & 1));
+      dz[e] = __uint_as_float(hb << 16);
+    }
+    d4[u] = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      a[e] = __fadd_rn(a[e], dz[e]);
+      b[e] = __fadd_rn(b[e], __fmul_rn(dz[e], __fmul_rn(__fsub_rn(fx[e], k0[e]), k1[e])));
+    }
+  }, status);
+  if (!consumer) return;
+  sums_tail(a, b, sh, cg, ok, part_a, part_b);
 }
 
 // y = act(x*scale + shift), or the fused tail (residual, ReLU) with EPI.
@@ -1360,6 +1417,42 @@ b2_status bn_relu_backward(const uint16_t* g, const uint16_t* xx, const void* w,
   return check_cuda(cudaGetLastError(), "bn relu dx launch");
 }
 
+// Backward of a BatchNorm (channels-last) whose output gradient is the ReLU
+// backward of a residual sum: dz = gate(y) ? bf16(a + b) : 0 made, written to
+// dz_out and summed in one pass, then the plain merge and dx passes (dx reads
+// the dz just written).  The plain backward's grid, so every result is bit for
+// bit b2_relu_bwd_sum_bf16 followed by b2_batch_norm_bwd_bf16.
+b2_status bn_gsum_backward(const uint16_t* ga, const uint16_t* gb, const uint16_t* yy, const uint16_t* xx,
+                           const void* w, int pdtype, const float* mean, const float* invstd, uint16_t* dz_out,
+                           uint16_t* dx, void* dw, void* db, int gdtype, long long N, long long C, long long HW,
+                           void* workspace, cudaStream_t st, const char* who) {
+  B2_TRY(check_nhwc(C, {ga, gb, yy, xx, dz_out, dx}, who));
+  const NhwcShape sh = nhwc_shape(N, C, HW);
+  if (!stream_ok(sh))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: needs the streaming kernels (C/8 dividing 256, B2_BN_STREAM on)", who);
+  const int sms = current_sms();
+  const double M = double(N) * double(HW);
+  const long long units = sh.P * sh.CV;
+  constexpr size_t smem2 = ring_smem_bytes<2>();
+  const long long blocks = stream_grid(&bn_nhwc_stream_sums_kernel<true, false>, smem2, units, sms, nhwc_blocks(sh));
+  auto sums = &bn_nhwc_stream_sums_gsum_kernel;
+  constexpr size_t smem4 = ring_smem_bytes<4>();
+  allow_smem(sums, smem4);
+  float* pa = static_cast<float*>(workspace);
+  float* pb = pa + blocks * C;
+  sums<<<int(blocks), kStreamThreads, smem4, st>>>(xx, ga, gb, yy, mean, invstd, sh, dz_out, pa, pb,
+                                                   device_status_ptr());
+  B2_TRY(check_cuda(cudaGetLastError(), "bn gsum sums launch"));
+  float* k = reinterpret_cast<float*>(static_cast<char*>(workspace) + align16(2 * size_t(blocks) * C * sizeof(float)));
+  bn_bwd_channel_kernel<<<int(C), kMergeThreads, 0, st>>>(pa, pb, blocks, C, M, dw, db, gdtype, k);
+  B2_TRY(check_cuda(cudaGetLastError(), "bn gsum channel launch"));
+  if (!dx) return B2_OK;
+  auto dxk = &bn_nhwc_stream_dx_kernel<false>;
+  dxk<<<stream_grid(dxk, smem2, units, sms, LLONG_MAX), kStreamThreads, smem2, st>>>(
+      dz_out, nullptr, xx, w, pdtype, mean, invstd, k, dx, sh, 1.0f, 0, device_status_ptr(), BnChan{});
+  return check_cuda(cudaGetLastError(), "bn gsum dx launch");
+}
+
 bool valid_pdtype(int dt) { return dt == B2_BF16 || dt == B2_F32; }
 
 }  // namespace
@@ -1483,4 +1576,21 @@ extern "C" b2_status b2_batch_norm_relu_bwd_bf16(const void* dy, const void* x, 
   return bn_relu_backward(static_cast<const uint16_t*>(dy), static_cast<const uint16_t*>(x), w, b, pdtype, save_mean,
                           save_invstd, static_cast<uint16_t*>(dx), dw, db, gdtype, N, C, HW, workspace,
                           static_cast<cudaStream_t>(stream), who);
+}
+
+extern "C" b2_status b2_batch_norm_bwd_relu_sum_bf16(const void* a, const void* b, const void* y, const void* x,
+                                                     const void* w, int pdtype, const float* save_mean,
+                                                     const float* save_invstd, void* dz, void* dx, void* dw, void* db,
+                                                     int gdtype, int64_t N, int64_t C, int64_t HW, void* workspace,
+                                                     size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_bwd_relu_sum_bf16";
+  B2_TRY(check_common(N, C, HW, 1, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(gdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (N * C == 0) return B2_OK;
+  if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
+  if (!a || !b || !y || !x || !dz || !save_mean || !save_invstd) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  return bn_gsum_backward(static_cast<const uint16_t*>(a), static_cast<const uint16_t*>(b),
+                          static_cast<const uint16_t*>(y), static_cast<const uint16_t*>(x), w, pdtype, save_mean,
+                          save_invstd, static_cast<uint16_t*>(dz), static_cast<uint16_t*>(dx), dw, db, gdtype, N, C,
+                          HW, workspace, static_cast<cudaStream_t>(stream), who);
 }

@@ -147,10 +147,17 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_kernel(const u
 // As maxpool_fwd_nhwc8_kernel for 3x3 windows (ResNet's stem pool): the up to
 // nine window loads are all issued before the scan, which then visits the
 // valid taps in the same (h, w) order -- the same maxima and indices.
-template <typename I>
+//
+// TAPS: instead of int64 indices, one byte per output element -- the argmax's
+// position inside its window, i * kw + j for tap (hs + i*dh, ws + j*dw) of the
+// window that starts at (hs, ws) = (oh*sh - ph, ow*sw - pw).  ATen's int64
+// indices follow from it (maxpool_taps_to_indices_kernel), and the backward
+// reads 1 byte per element instead of 8.
+template <typename I, bool TAPS = false>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_k3_kernel(const uint16_t* __restrict__ x,
                                                                             PoolGeom g, uint16_t* __restrict__ y,
-                                                                            int64_t* __restrict__ ind) {
+                                                                            int64_t* __restrict__ ind,
+                                                                            uint8_t* __restrict__ taps = nullptr) {
   const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
   const I total = I(g.N) * OH * OW * cv;
   for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
@@ -170,17 +177,20 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_k3_kernel(cons
       v[t] = ok[t] ? __ldg(reinterpret_cast<const uint4*>(xp + h * I(g.xs[2]) + w * I(g.xs[3])))
                    : make_uint4(0, 0, 0, 0);
     }
+    // window-relative position of the first valid tap (h0, w0)
+    const int i0 = int((h0 - (oh * g.sh - g.ph)) / g.dh), j0 = int((w0 - (ow * g.sw - g.pw)) / g.dw);
     float best[8];
     long long bi[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       best[e] = -INFINITY;
-      bi[e] = (long long)(h0 * W + w0);
+      bi[e] = TAPS ? (long long)(i0 * 3 + j0) : (long long)(h0 * W + w0);
     }
 #pragma unroll
     for (int t = 0; t < 9; ++t) {
       if (!ok[t]) continue;
-      const long long idx = (long long)((h0 + I(t / 3) * g.dh) * W + w0 + I(t % 3) * g.dw);
+      const long long idx = TAPS ? (long long)((i0 + t / 3) * 3 + j0 + t % 3)
+                                 : (long long)((h0 + I(t / 3) * g.dh) * W + w0 + I(t % 3) * g.dw);
       const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -198,9 +208,45 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_k3_kernel(cons
     out.z = pack_bf2(best[4], best[5]);
     out.w = pack_bf2(best[6], best[7]);
     *reinterpret_cast<uint4*>(y + o) = out;
+    if constexpr (TAPS) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        lo |= uint32_t(bi[e]) << (8 * e);
+        hi |= uint32_t(bi[4 + e]) << (8 * e);
+      }
+      *reinterpret_cast<uint2*>(taps + o) = make_uint2(lo, hi);
+    } else {
+      longlong2* ip = reinterpret_cast<longlong2*>(ind + o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ip[e] = make_longlong2(bi[2 * e], bi[2 * e + 1]);
+    }
+  }
+}
+
+// ATen's int64 indices (h*W + w within the plane) from the window taps.
+template <typename I>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_taps_to_indices_kernel(const uint8_t* __restrict__ taps,
+                                                                               PoolGeom g,
+                                                                               int64_t* __restrict__ ind) {
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), W = I(g.W);
+  const I total = I(g.N) * OH * OW * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / OW, ow = r - r2 * OW;
+    const I n = r2 / OH, oh = r2 - n * OH;
+    const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
+    const uint2 tv = *reinterpret_cast<const uint2*>(taps + o);
+    const long long hs = (long long)oh * g.sh - g.ph, ws = (long long)ow * g.sw - g.pw;
+    long long idx[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = int(((e < 4 ? tv.x : tv.y) >> (8 * (e & 3))) & 0xffu);
+      idx[e] = (hs + (long long)(t / g.kw) * g.dh) * (long long)W + ws + (long long)(t % g.kw) * g.dw;
+    }
     longlong2* ip = reinterpret_cast<longlong2*>(ind + o);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ip[e] = make_longlong2(bi[2 * e], bi[2 * e + 1]);
+    for (int e = 0; e < 4; ++e) ip[e] = make_longlong2(idx[2 * e], idx[2 * e + 1]);
   }
 }
 
@@ -317,6 +363,62 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_two_kernel(con
       for (int e2 = 0; e2 < 4; ++e2) {
         if (ii[t][e2].x == me) s[2 * e2] = __fadd_rn(s[2 * e2], __uint_as_float(wd[e2] << 16));
         if (ii[t][e2].y == me) s[2 * e2 + 1] = __fadd_rn(s[2 * e2 + 1], __uint_as_float(wd[e2] & 0xffff0000u));
+      }
+    }
+    uint4 out;
+    out.x = pack_bf2(s[0], s[1]);
+    out.y = pack_bf2(s[2], s[3]);
+    out.z = pack_bf2(s[4], s[5]);
+    out.w = pack_bf2(s[6], s[7]);
+    *reinterpret_cast<uint4*>(dx + n * I(g.xs[0]) + h * I(g.xs[2]) + w * I(g.xs[3]) + q * 8) = out;
+  }
+}
+
+// maxpool_bwd_nhwc8_two_kernel reading the forward's window taps (1 byte per
+// element) instead of int64 indices: input (h, w) matches output (oh, ow)'s
+// tap when it is that window's tap ((h - hs) / dh) * kw + (w - ws) / dw.
+template <typename I>
+__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_taps_kernel(const uint16_t* __restrict__ dy,
+                                                                              const uint8_t* __restrict__ taps,
+                                                                              PoolGeom g, uint16_t* __restrict__ dx) {
+  const I cv = I(g.C / 8), OW = I(g.OW), OH = I(g.OH), H = I(g.H), W = I(g.W);
+  const I total = I(g.N) * H * W * cv;
+  for (I u = I(blockIdx.x) * kPoolThreads + I(threadIdx.x); u < total; u += I(gridDim.x) * kPoolThreads) {
+    const I r = u / cv, q = u - r * cv;
+    const I r2 = r / W, w = r - r2 * W;
+    const I n = r2 / H, h = r2 - n * H;
+    I oh0, oh1, ow0, ow1;
+    covering<I>(h, g.sh, g.ph, g.kh, g.dh, OH, oh0, oh1);
+    covering<I>(w, g.sw, g.pw, g.kw, g.dw, OW, ow0, ow1);
+    uint4 v[4];
+    uint2 tv[4];
+    uint32_t want[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const I oh = oh0 + (t >> 1), ow = ow0 + (t & 1);
+      want[t] = 0xffffffffu;  // matches no tap byte
+      if (oh < oh1 && ow < ow1) {
+        const I o = n * I(g.ys[0]) + oh * I(g.ys[2]) + ow * I(g.ys[3]) + q * 8;
+        v[t] = __ldg(reinterpret_cast<const uint4*>(dy + o));
+        tv[t] = __ldg(reinterpret_cast<const uint2*>(taps + o));
+        const I di = h - (oh * g.sh - g.ph), dj = w - (ow * g.sw - g.pw);
+        if (di % g.dh == 0 && dj % g.dw == 0) want[t] = uint32_t((di / g.dh) * g.kw + dj / g.dw);
+      } else {
+        v[t] = make_uint4(0, 0, 0, 0);
+        tv[t] = make_uint2(0, 0);
+      }
+    }
+    float s[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t tap = ((e < 4 ? tv[t].x : tv[t].y) >> (8 * (e & 3))) & 0xffu;
+        if (tap == want[t])
+          s[e] = __fadd_rn(s[e], __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16)));
       }
     }
     uint4 out;
@@ -447,3 +549,60 @@ b2_status b2_maxpool2d_bwd(const void* dy, const int64_t* indices, const int64_t
 }
 
 }  // extern "C"
+
+// ---- max pooling with window taps (channels-last bf16, 3x3 windows) ---------
+
+extern "C" b2_status b2_maxpool2d_fwd_taps(const void* x, const int64_t* x_strides, void* y, void* taps,
+                                           const int64_t* y_strides, int64_t N, int64_t C, int64_t H, int64_t W,
+                                           int64_t OH, int64_t OW, int kh, int kw, int sh, int sw, int ph, int pw,
+                                           int dh, int dw, void* stream) {
+  const char* who = "b2_maxpool2d_fwd_taps";
+  PoolGeom g;
+  B2_TRY(make_pool(g, N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, x_strides, y_strides, who));
+  const long long total = N * C * OH * OW;
+  if (total == 0) return B2_OK;
+  if (!x || !y || !taps) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  if (kh != 3 || kw != 3 || !nhwc8(g, x, y, y) || (reinterpret_cast<uintptr_t>(taps) & 7) || !fits32(g))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: needs 3x3 windows over channels-last bf16 (C %% 8 == 0)", who);
+  maxpool_fwd_nhwc8_k3_kernel<int, true><<<pool_grid(total / 8, cur_sms()), kPoolThreads, 0,
+                                           static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), nullptr, static_cast<uint8_t*>(taps));
+  return check_cuda(cudaGetLastError(), "maxpool fwd taps launch");
+}
+
+extern "C" b2_status b2_maxpool2d_taps_to_indices(const void* taps, const int64_t* y_strides, int64_t* indices,
+                                                  int64_t N, int64_t C, int64_t H, int64_t W, int64_t OH, int64_t OW,
+                                                  int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
+                                                  void* stream) {
+  const char* who = "b2_maxpool2d_taps_to_indices";
+  PoolGeom g;
+  B2_TRY(make_pool(g, N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, y_strides, y_strides, who));
+  const long long total = N * C * OH * OW;
+  if (total == 0) return B2_OK;
+  if (!taps || !indices) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  if (kh * kw > 256 || !nhwc8(g, indices, indices, indices) || (reinterpret_cast<uintptr_t>(taps) & 7) || !fits32(g))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: needs the channels-last layout of b2_maxpool2d_fwd_taps", who);
+  maxpool_taps_to_indices_kernel<int><<<pool_grid(total / 8, cur_sms()), kPoolThreads, 0,
+                                        static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(taps), g,
+                                                                             indices);
+  return check_cuda(cudaGetLastError(), "maxpool taps to indices launch");
+}
+
+extern "C" b2_status b2_maxpool2d_bwd_taps(const void* dy, const void* taps, const int64_t* y_strides, void* dx,
+                                           const int64_t* x_strides, int64_t N, int64_t C, int64_t H, int64_t W,
+                                           int64_t OH, int64_t OW, int kh, int kw, int sh, int sw, int ph, int pw,
+                                           int dh, int dw, void* stream) {
+  const char* who = "b2_maxpool2d_bwd_taps";
+  PoolGeom g;
+  B2_TRY(make_pool(g, N, C, H, W, OH, OW, kh, kw, sh, sw, ph, pw, dh, dw, x_strides, y_strides, who));
+  const long long total = N * C * H * W;
+  if (total == 0) return B2_OK;
+  if (!dx || (N * C * OH * OW > 0 && (!dy || !taps))) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  if (kh * kw > 256 || !nhwc8(g, dx, dy, dy) || (reinterpret_cast<uintptr_t>(taps) & 7) || !fits32(g) ||
+      !two_cover(g))
+    return set_error(B2_ERR_UNSUPPORTED, "%s: needs channels-last bf16 and windows spanning <= 2 strides", who);
+  maxpool_bwd_nhwc8_taps_kernel<int><<<pool_grid(total / 8, cur_sms()), kPoolThreads, 0,
+                                       static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(dy), static_cast<const uint8_t*>(taps), g, static_cast<uint16_t*>(dx));
+  return check_cuda(cudaGetLastError(), "maxpool bwd taps launch");
+}

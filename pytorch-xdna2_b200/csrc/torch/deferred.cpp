@@ -30,6 +30,7 @@ namespace {
 struct Job {
   std::function<void()> fn;
   int64_t order = 0;
+  bool kick = true;  // launched early by the async policy (weight gradients)
 };
 
 struct Attachment {
@@ -115,14 +116,14 @@ void run_job(std::function<void()>& fn) {
 // Entries are always moved out of the tables before they are destroyed:
 // destroying a job or an attachment frees tensors, and the allocator's release
 // hook (on_release) takes g_mu again.
-void defer_write(const at::Tensor& target, std::function<void()> job) {
+void defer_write(const at::Tensor& target, std::function<void()> job, bool kick) {
   void* key = target.storage().mutable_data();
   Job old;
   {
     std::lock_guard<std::mutex> lk(g_mu);
     auto it = g_jobs.find(key);
     if (it != g_jobs.end()) old = std::move(it->second);
-    g_jobs[key] = Job{std::move(job), g_order++};
+    g_jobs[key] = Job{std::move(job), g_order++, kick};
     ++g_deferred;
     g_pending_jobs.store(int64_t(g_jobs.size()));
   }
@@ -146,6 +147,23 @@ void materialize_key(void* key) {
 }
 }  // namespace
 
+void drop_pending(const at::Tensor& t) {
+  if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
+  void* key = t.storage().mutable_data();
+  Job done;
+  EpiSlot slot;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_jobs.find(key);
+    if (it == g_jobs.end()) return;
+    done = std::move(it->second);
+    g_jobs.erase(it);
+    ++g_started;
+    g_pending_jobs.store(int64_t(g_jobs.size()));
+    slot = take_epi_locked(key);
+  }
+}
+
 void materialize(const at::Tensor& t) {
   if (g_pending_jobs.load(std::memory_order_relaxed) == 0 || !t.defined() || !t.has_storage()) return;
   materialize_key(t.storage().mutable_data());
@@ -153,7 +171,10 @@ void materialize(const at::Tensor& t) {
 
 void defer_epilogue(const at::Tensor& out, const std::vector<at::Tensor>& inputs, std::shared_ptr<EpiSpec> spec,
                     std::function<void()> job) {
-  defer_write(out, std::move(job));
+  // a producer with a spec waits for its reader (that is its point); only the
+  // weight-gradient jobs (no spec) go with the async policy's early launch
+  const bool kick = spec == nullptr;
+  defer_write(out, std::move(job), kick);
   void* key = out.storage().mutable_data();
   std::lock_guard<std::mutex> lk(g_mu);
   EpiSlot& slot = g_epi[key];
@@ -299,7 +320,26 @@ void note_dgrad() {
     kick = async_enabled() && g_k_learned > 0 && g_dx_this_step == g_k_learned && !g_jobs.empty();
     if (kick) ++g_kicks;
   }
-  if (kick) materialize_all();
+  if (!kick) return;
+  // the pending weight gradients, in the order they were deferred
+  std::vector<std::pair<int64_t, std::function<void()>>> fns;
+  std::vector<EpiSlot> slots;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto it = g_jobs.begin(); it != g_jobs.end();) {
+      if (!it->second.kick) {
+        ++it;
+        continue;
+      }
+      fns.emplace_back(it->second.order, std::move(it->second.fn));
+      slots.push_back(take_epi_locked(it->first));
+      ++g_started;
+      it = g_jobs.erase(it);
+    }
+    g_pending_jobs.store(int64_t(g_jobs.size()));
+  }
+  std::sort(fns.begin(), fns.end(), [](auto& a, auto& b) { return a.first < b.first; });
+  for (auto& f : fns) run_job(f.second);
 }
 
 void note_optimizer_step() {

@@ -169,6 +169,36 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm_backward(
   const auto mf = layout == 1 ? c10::MemoryFormat::ChannelsLast : c10::MemoryFormat::Contiguous;
   const int64_t N = input.size(0), HW = input.numel() / (N * C);
   const auto gdt = defined(weight) ? weight->scalar_type() : at::kFloat;
+  // grad_out still pending as the ReLU backward of a pending gradient sum
+  // (a residual block's last BatchNorm): dz made, written and reduced in one
+  // pass from the sum's two terms and the ReLU's output
+  if (auto rs = layout == 1 ? find_epilogue(grad_out) : nullptr;
+      rs && rs->relu_sum_a.defined() && has_pending(rs->relu_sum_a) && grad_out.is_contiguous(mf) &&
+      grad_out.strides() == input.strides()) {
+    at::Tensor gi, gw, gb;
+    if (mask[0]) gi = empty(input.sizes(), at::kBFloat16, dev, mf);
+    if (mask[1]) gw = empty({C}, gdt, dev);
+    if (mask[2]) gb = empty({C}, gdt, dev);
+    const int64_t wsb = int64_t(b2_batch_norm_workspace_bytes(N, C, HW, 1));
+    at::Tensor ws = empty({std::max<int64_t>(wsb, 16)}, at::kByte, dev);
+    materialize(rs->relu_sum_b);
+    materialize(rs->relu_sum_y);
+    materialize(input);
+    c10::cuda::CUDAGuard guard(dev);
+    KernelTimer kt("bn.bwd_relu_sum", (mask[0] ? 16.0 : 10.0) * double(input.numel()), stream(dev));
+    const b2_status st = b2_batch_norm_bwd_relu_sum_bf16(
+        rs->relu_sum_a.data_ptr(), rs->relu_sum_b.data_ptr(), rs->relu_sum_y.data_ptr(), input.data_ptr(),
+        ptr_of(weight), pw, save_mean->data_ptr<float>(), save_invstd->data_ptr<float>(), grad_out.data_ptr(),
+        mask[0] ? gi.data_ptr() : nullptr, mask[1] ? gw.data_ptr() : nullptr, mask[2] ? gb.data_ptr() : nullptr,
+        gdt == at::kFloat ? B2_F32 : B2_BF16, N, C, HW, ws.data_ptr(), size_t(ws.numel()), stream(dev));
+    if (st == B2_OK) {
+      drop_pending(grad_out);  // dz written by the fused pass
+      count_launch("batch_norm.bwd_relu_sum", mask[0] ? 3 : 2);
+      return {gi, gw, gb};
+    }
+    TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_batch_norm_bwd_relu_sum_bf16 failed (", st, "): ",
+                b2_last_error());
+  }
   // grad_out still pending as threshold_backward(grad, y, 0) of this
   // BatchNorm's own gated output: one backward from `grad`, the ReLU's gate
   // recomputed from x (the pending pass is never run unless read elsewhere)
@@ -239,19 +269,34 @@ at::Tensor threshold_backward(const at::Tensor& grad, const at::Tensor& self, co
   if (g_mode.load() > 1 && threshold.toDouble() == 0.0 && grad.scalar_type() == at::kBFloat16 &&
       self.scalar_type() == at::kBFloat16 && grad.dim() == 4 && grad.sizes() == self.sizes() &&
       grad.strides() == self.strides() && grad.is_contiguous(cl) && grad.device() == self.device()) {
-    if (auto sum = find_epilogue(grad); sum && sum->pending_sum.defined()) {
+    if (auto sum = find_epilogue(grad); sum && sum->pending_sum.defined() && (self.numel() % 8 == 0) &&
+                                        (reinterpret_cast<uintptr_t>(self.data_ptr()) & 15) == 0) {
       const auto dev = self.device().index();
       materialize(self);
       at::Tensor dz = empty(self.sizes(), at::kBFloat16, dev, cl);
-      c10::cuda::CUDAGuard guard(dev);
-      KernelTimer kt("relu_bwd_sum", 8.0 * double(self.numel()), stream(dev));
-      const b2_status st = b2_relu_bwd_sum_bf16(grad.data_ptr(), sum->pending_sum.data_ptr(), self.data_ptr(),
-                                                dz.data_ptr(), self.numel(), stream(dev));
-      if (st == B2_OK) {
-        count_launch("relu_bwd_sum");
-        return dz;
-      }
-      TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_relu_bwd_sum_bf16 failed (", st, "): ", b2_last_error());
+      // dz itself is left pending too: a BatchNorm backward reading it makes
+      // it in its own reduction pass; any other reader runs this job
+      auto rs = std::make_shared<EpiSpec>();
+      rs->relu_sum_a = grad;
+      rs->relu_sum_b = sum->pending_sum;
+      rs->relu_sum_y = self;
+      defer_epilogue(dz, {grad, sum->pending_sum, self}, rs,
+                     [grad, other = sum->pending_sum, self, ptr = dz.data_ptr(), sizes = dz.sizes().vec(),
+                      strides = dz.strides().vec(), dev]() {
+                       c10::cuda::CUDAGuard guard(dev);
+                       if (has_pending(grad)) {  // grad still holds a, its sum with `other` pending
+                         KernelTimer kt("relu_bwd_sum", 8.0 * double(self.numel()), stream(dev));
+                         XDNA_B2(b2_relu_bwd_sum_bf16(grad.data_ptr(), other.data_ptr(), self.data_ptr(), ptr,
+                                                      self.numel(), stream(dev)));
+                         count_launch("relu_bwd_sum");
+                       } else {  // the sum has run in place: a plain ReLU backward of it
+                         count_fallback("aten::threshold_backward");
+                         at::Tensor out = at::from_blob(
+                             ptr, sizes, strides, at::TensorOptions().dtype(at::kBFloat16).device(at::kCUDA, dev));
+                         at::threshold_backward_out(out, to_cuda(grad), to_cuda(self), 0);
+                       }
+                     });
+      return dz;
     }
   }
   std::shared_ptr<GateSource> src;

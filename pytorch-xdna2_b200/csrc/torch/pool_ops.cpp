@@ -48,6 +48,20 @@ bool parse(const at::Tensor& x, at::IntArrayRef k, at::IntArrayRef s, at::IntArr
 
 int dtype_code(at::ScalarType t) { return t == at::kBFloat16 ? B2_BF16 : t == at::kFloat ? B2_F32 : -1; }
 
+// Slot kind of the window taps kept on the int64 indices' storage (kinds
+// below 16 are packed weights, from 16 the column matrices' geometry tags).
+constexpr int kTapsSlot = 15;
+
+// The window-tap kernels' case: channels-last bf16, C % 8 == 0, 3x3 windows
+// spanning at most two strides (the backward's covering bound).
+bool taps_pool(const at::Tensor& x, const Pool2d& g) {
+  return x.scalar_type() == at::kBFloat16 && x.dim() == 4 &&
+         x.suggest_memory_format() == at::MemoryFormat::ChannelsLast &&
+         x.is_contiguous(at::MemoryFormat::ChannelsLast) && x.size(1) % 8 == 0 && g.kh == 3 && g.kw == 3 &&
+         2 * (g.kh - 1) * g.dh + 2 <= 4 * g.sh && 2 * (g.kw - 1) * g.dw + 2 <= 4 * g.sw &&
+         (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0;
+}
+
 std::tuple<at::Tensor, at::Tensor> max_pool2d_with_indices(const at::Tensor& self, at::IntArrayRef k,
                                                            at::IntArrayRef s, at::IntArrayRef p, at::IntArrayRef d,
                                                            bool ceil_mode) {
@@ -67,6 +81,30 @@ std::tuple<at::Tensor, at::Tensor> max_pool2d_with_indices(const at::Tensor& sel
   c10::cuda::CUDAGuard guard(dev);
   const int64_t xs[4] = {self.stride(0), self.stride(1), self.stride(2), self.stride(3)};
   const int64_t ys[4] = {y.stride(0), y.stride(1), y.stride(2), y.stride(3)};
+  // channels-last bf16 3x3 windows: the argmax kept as window taps (1 byte an
+  // element); ATen's int64 indices are written only when something reads
+  // them -- the backward reads the taps (attached to the indices' storage)
+  if (g_mode.load() > 1 && taps_pool(self, g)) {
+    at::Tensor taps = empty({self.size(0), self.size(1), g.OH, g.OW}, at::kByte, dev, mf);
+    const b2_status st =
+        b2_maxpool2d_fwd_taps(self.data_ptr(), xs, y.data_ptr(), taps.data_ptr(), ys, self.size(0), self.size(1),
+                              self.size(2), self.size(3), g.OH, g.OW, g.kh, g.kw, g.sh, g.sw, g.ph, g.pw, g.dh, g.dw,
+                              stream(dev));
+    if (st == B2_OK) {
+      count_launch("maxpool2d.fwd");
+      const int64_t N = self.size(0), C = self.size(1), H = self.size(2), W = self.size(3);
+      defer_write(ind, [taps, ptr = ind.data_ptr<int64_t>(), ys4 = std::vector<int64_t>(ys, ys + 4), N, C, H, W, g,
+                        dev]() {
+        c10::cuda::CUDAGuard guard(dev);
+        XDNA_B2(b2_maxpool2d_taps_to_indices(taps.data_ptr(), ys4.data(), ptr, N, C, H, W, g.OH, g.OW, g.kh, g.kw,
+                                             g.sh, g.sw, g.ph, g.pw, g.dh, g.dw, stream(dev)));
+        count_launch("maxpool2d.indices");
+      }, /*kick=*/false);
+      attach_packed_weight(ind, kTapsSlot, taps);
+      return {y, ind};
+    }
+    TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_maxpool2d_fwd_taps failed (", st, "): ", b2_last_error());
+  }
   XDNA_B2(b2_maxpool2d_fwd(self.data_ptr(), xs, y.data_ptr(), ind.data_ptr<int64_t>(), ys,
                            dtype_code(self.scalar_type()), self.size(0), self.size(1), self.size(2), self.size(3), g.OH,
                            g.OW, g.kh, g.kw, g.sh, g.sw, g.ph, g.pw, g.dh, g.dw, stream(dev)));
@@ -88,6 +126,26 @@ at::Tensor max_pool2d_with_indices_backward(const at::Tensor& grad, const at::Te
                                                       to_cuda(indices)));
   }
   const auto dev = self.device().index();
+  // the forward's window taps, when the indices are still the forward's
+  if (g_mode.load() > 1 && taps_pool(self, g) && grad.strides() == indices.strides() &&
+      grad.is_contiguous(at::MemoryFormat::ChannelsLast)) {
+    at::Tensor taps = find_packed_weight(indices, kTapsSlot);
+    if (taps.defined() && taps.sizes() == indices.sizes() && taps.strides() == indices.strides()) {
+      at::Tensor dx = empty(self.sizes(), self.scalar_type(), dev, at::MemoryFormat::ChannelsLast);
+      materialize(grad);
+      c10::cuda::CUDAGuard guard(dev);
+      const int64_t xs[4] = {dx.stride(0), dx.stride(1), dx.stride(2), dx.stride(3)};
+      const int64_t ys[4] = {grad.stride(0), grad.stride(1), grad.stride(2), grad.stride(3)};
+      const b2_status st = b2_maxpool2d_bwd_taps(grad.data_ptr(), taps.data_ptr(), ys, dx.data_ptr(), xs,
+                                                 self.size(0), self.size(1), self.size(2), self.size(3), g.OH, g.OW,
+                                                 g.kh, g.kw, g.sh, g.sw, g.ph, g.pw, g.dh, g.dw, stream(dev));
+      if (st == B2_OK) {
+        count_launch("maxpool2d.bwd");
+        return dx;
+      }
+      TORCH_CHECK(st == B2_ERR_UNSUPPORTED, "xdna: b2_maxpool2d_bwd_taps failed (", st, "): ", b2_last_error());
+    }
+  }
   // dy read with the indices' strides
   at::Tensor gy = grad.strides() == indices.strides() ? grad : grad.contiguous(indices.suggest_memory_format());
   at::Tensor ind = indices;

@@ -70,8 +70,13 @@ at::Tensor adopt(const at::Tensor& cuda_tensor);
 // A job produces the contents of one storage.  Readers run it first; freeing
 // the storage before anyone read it drops it unrun (reference semantics,
 // torch_xdna_device.cpp:299-482, 550-656).
-void defer_write(const at::Tensor& target, std::function<void()> job);
+// kick = false keeps the job out of the async policy's early launch (a
+// producer whose whole point is to wait for a reader that may never come).
+void defer_write(const at::Tensor& target, std::function<void()> job, bool kick = true);
 void materialize(const at::Tensor& t);  // no-op unless t's storage has a pending job
+// t's pending job and tails dropped unrun: its contents were written by a
+// kernel that fused the job's work into its own pass
+void drop_pending(const at::Tensor& t);
 void materialize_all();
 bool has_pending(const at::Tensor& t);
 void note_dgrad();           // one dX computed (async policy bookkeeping)
@@ -112,8 +117,14 @@ struct EpiSpec {
   // a ReLU backward on it reads both terms and sums them in its own pass
   // (b2_relu_bwd_sum_bf16); nothing folds into it
   at::Tensor pending_sum;
+  // a pending ReLU backward of a pending sum: dz = gate(relu_sum_y) ?
+  // bf16(relu_sum_a + relu_sum_b) : 0, relu_sum_a still holding its pre-add
+  // values while its own sum is pending; the BatchNorm backward that reads dz
+  // makes, writes and reduces it in one pass
+  // (b2_batch_norm_bwd_relu_sum_bf16)
+  at::Tensor relu_sum_a, relu_sum_b, relu_sum_y;
   // add_ / relu_ may fold into this pending output: only a BatchNorm's pass
-  bool foldable() const { return !gate && !pending_sum.defined(); }
+  bool foldable() const { return !gate && !pending_sum.defined() && !relu_sum_a.defined(); }
 };
 // The gated BatchNorm output y (registered when its output pass is enqueued;
 // dropped when y's storage is released) and its lookup by exact geometry.

@@ -98,6 +98,9 @@ SIGNATURES = {
                          i32, vp],
     "b2_maxpool2d_bwd": [vp, vp, vp, vp, vp, i32, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32,
                          i32, vp],
+    "b2_maxpool2d_fwd_taps": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32, i32, vp],
+    "b2_maxpool2d_taps_to_indices": [vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32, i32, vp],
+    "b2_maxpool2d_bwd_taps": [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, i32, i32, vp],
     "b2_cat_blocks": [vp, vp, i32, vp, i64, i64, vp],
     "b2_upsample_nearest2x": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
     "b2_upsample_nearest2x_backward": [vp, vp, i32, i32, i64, i64, i64, i64, vp],
@@ -107,6 +110,8 @@ SIGNATURES = {
     "b2_batch_norm_bwd_bf16": [vp, vp, i32, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
     "b2_batch_norm_relu_bwd_bf16": [vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz, vp],
     "b2_relu_bwd_sum_bf16": [vp, vp, vp, vp, i64, vp],
+    "b2_batch_norm_bwd_relu_sum_bf16": [vp, vp, vp, vp, vp, i32, vp, vp, vp, vp, vp, vp, i32, i64, i64, i64, vp, sz,
+                                        vp],
     "b2_region_bn_fwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, f32, f32, i32, vp, sz, vp],
     "b2_region_bn_bwd_bf16": [vp, vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, f32, i32, vp, sz, vp],
 }

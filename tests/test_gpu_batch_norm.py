@@ -468,21 +468,67 @@ def _residual_stack(fused, seed=7):
 
 
 def test_gradient_sums_fold_into_relu_backward():
-    """The block inputs' gradient sums stay pending and the ReLU backward that
-    reads them adds and gates in one pass: every gradient equals the unfused
-    run's bit for bit, and the separate add passes are gone."""
+    """The block inputs' gradient sums stay pending, so does the ReLU backward
+    that reads them, and the BatchNorm backward reading that adds, gates and
+    reduces in one pass: every gradient equals the unfused run's bit for bit,
+    and the separate add and ReLU-backward passes are gone."""
     try:
         xdna_train.reset_fallback_stats()
         fused = _residual_stack(True)
         fb = xdna_train.fallback_stats()
         n_sum = launched("relu_bwd_sum")
+        n_bn_sum = launched("batch_norm.bwd_relu_sum")
         xdna_train.reset_fallback_stats()
         plain = _residual_stack(False)
         fp = xdna_train.fallback_stats()
     finally:
         xdna_train.set_fusion(bn_epilogue=True)
     calls = lambda d, k: d.get(k, {}).get("calls", 0)  # noqa: E731
-    assert n_sum == 2
+    # both sums are made inside the BatchNorm backward that reads them
+    assert n_sum == 0 and n_bn_sum == 2 * 3
     assert calls(fp, "aten::add_.Tensor") - calls(fb, "aten::add_.Tensor") >= 2
     for k in fused:
         assert torch.equal(fused[k].float(), plain[k].float()), k
+
+
+@pytest.mark.parametrize("shape", [(8, 64, 14, 14), (4, 256, 7, 7), (2, 2048, 3, 3)])
+@pytest.mark.parametrize("pdtype", [0, 1])
+def test_batch_norm_bwd_relu_sum_abi_bit_exact(cuda, shape, pdtype):
+    """b2_batch_norm_bwd_relu_sum_bf16 against b2_relu_bwd_sum_bf16 followed
+    by b2_batch_norm_bwd_bf16: dz, dx, dw and db bit for bit (y with NaN and
+    zeros, a + b overflowing)."""
+    N, C, H, W = shape
+    g = torch.Generator().manual_seed(N * C + H)
+    # NHWC storage, viewed as channels-last NCHW
+    flat = [torch.randn(N * H * W * C, generator=g).bfloat16() for _ in range(4)]
+    flat[3][:3] = torch.tensor([float("nan"), 0.0, -0.0]).bfloat16()
+    flat[1][5] = flat[2][5] = 3e38
+    x, a, b, y = (f.to(cuda).view(N, H, W, C).permute(0, 3, 1, 2) for f in flat)
+    assert x.is_contiguous(memory_format=torch.channels_last)
+    pt = torch.float32 if pdtype == 1 else torch.bfloat16
+    w = (torch.rand(C, generator=g) + 0.5).to(pt).to(cuda)
+    sm = torch.randn(C, generator=g).to(cuda) * 0.1
+    si = (torch.rand(C, generator=g) + 0.5).to(cuda)
+    nws = _abi.lib().b2_batch_norm_workspace_bytes(N, C, H * W, 1)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=cuda)
+    outs = {}
+    for name in ("plain", "fused"):
+        dz = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        assert dz.stride() == x.stride()
+        dw = torch.empty(C, dtype=pt, device=cuda)
+        db = torch.empty_like(dw)
+        if name == "plain":
+            _abi.call("b2_relu_bwd_sum_bf16", a.data_ptr(), b.data_ptr(), y.data_ptr(), dz.data_ptr(), x.numel(), st())
+            _abi.call("b2_batch_norm_bwd_bf16", dz.data_ptr(), x.data_ptr(), 1, w.data_ptr(), pdtype, sm.data_ptr(),
+                      si.data_ptr(), dx.data_ptr(), dw.data_ptr(), db.data_ptr(), pdtype, N, C, H * W, ws.data_ptr(),
+                      nws, st())
+        else:
+            _abi.call("b2_batch_norm_bwd_relu_sum_bf16", a.data_ptr(), b.data_ptr(), y.data_ptr(), x.data_ptr(),
+                      w.data_ptr(), pdtype, sm.data_ptr(), si.data_ptr(), dz.data_ptr(), dx.data_ptr(), dw.data_ptr(),
+                      db.data_ptr(), pdtype, N, C, H * W, ws.data_ptr(), nws, st())
+        torch.cuda.synchronize()
+        outs[name] = (dz, dx, dw, db)
+    for p_, f_ in zip(outs["plain"], outs["fused"]):
+        iv = torch.int16 if p_.dtype == torch.bfloat16 else torch.int32
+        assert torch.equal(p_.contiguous().view(iv).cpu(), f_.contiguous().view(iv).cpu())

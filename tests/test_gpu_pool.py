@@ -91,3 +91,59 @@ def test_maxpool_module_in_a_model():
     nx.load_state_dict(net.state_dict())
     got = nx.to(X)(x.to(X))
     assert torch.allclose(got.cpu(), ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("shape,s,p,d", [((2, 64, 56, 56), 2, 1, 1), ((3, 16, 21, 19), 2, 1, 1),
+                                         ((2, 8, 17, 15), 3, 1, 1), ((2, 24, 13, 13), 2, 0, 1)])
+def test_window_taps_abi_match_int64_path(shape, s, p, d):
+    """b2_maxpool2d_fwd_taps / taps_to_indices / bwd_taps against the int64
+    path on the same inputs (NaNs and ties included): y, the expanded
+    indices and dx are bit-identical."""
+    import ctypes
+    from xdna_train import _abi
+    cuda = torch.device("cuda", 0)
+    N, C, H, W = shape
+    g = torch.Generator().manual_seed(sum(shape) + s)
+    x = torch.randn(*shape, generator=g).bfloat16()
+    flat = x.view(-1)
+    flat[torch.randperm(flat.numel(), generator=g)[: max(2, flat.numel() // 300)]] = float("nan")
+    x[0, :, 0, :3] = 1.0  # ties
+    cl = torch.channels_last
+    xd = x.to(cuda).contiguous(memory_format=cl)
+    OH = (H + 2 * p - d * 2 - 1) // s + 1
+    OW = (W + 2 * p - d * 2 - 1) // s + 1
+    y0 = torch.empty(N, C, OH, OW, dtype=torch.bfloat16, device=cuda).contiguous(memory_format=cl)
+    y1 = torch.empty_like(y0)
+    ind0 = torch.empty(N, C, OH, OW, dtype=torch.int64, device=cuda).contiguous(memory_format=cl)
+    ind1 = torch.empty_like(ind0)
+    taps = torch.empty(N, C, OH, OW, dtype=torch.uint8, device=cuda).contiguous(memory_format=cl)
+    arr = lambda t: (ctypes.c_int64 * 4)(*t.stride())  # noqa: E731
+    st = torch.cuda.current_stream().cuda_stream
+    geo = (N, C, H, W, OH, OW, 3, 3, s, s, p, p, d, d)
+    _abi.call("b2_maxpool2d_fwd", xd.data_ptr(), arr(xd), y0.data_ptr(), ind0.data_ptr(), arr(y0), 0, *geo, st)
+    _abi.call("b2_maxpool2d_fwd_taps", xd.data_ptr(), arr(xd), y1.data_ptr(), taps.data_ptr(), arr(y1), *geo, st)
+    _abi.call("b2_maxpool2d_taps_to_indices", taps.data_ptr(), arr(y1), ind1.data_ptr(), *geo, st)
+    dy = torch.randn(N, C, OH, OW, generator=g).bfloat16().to(cuda).contiguous(memory_format=cl)
+    dx0 = torch.empty_like(xd)
+    dx1 = torch.empty_like(xd)
+    _abi.call("b2_maxpool2d_bwd", dy.data_ptr(), ind0.data_ptr(), arr(dy), dx0.data_ptr(), arr(dx0), 0, *geo, st)
+    _abi.call("b2_maxpool2d_bwd_taps", dy.data_ptr(), taps.data_ptr(), arr(dy), dx1.data_ptr(), arr(dx1), *geo, st)
+    torch.cuda.synchronize()
+    assert torch.equal(bits(y0), bits(y1))
+    assert torch.equal(ind0.cpu(), ind1.cpu())
+    assert torch.equal(bits(dx0), bits(dx1))
+
+
+def test_indices_written_only_when_read():
+    """With the window taps the forward leaves ATen's int64 indices pending:
+    a training step never writes them, and reading them runs the expansion
+    and gives the CPU's indices."""
+    x = torch.randn(2, 64, 20, 20).bfloat16()
+    xx = x.to(X).contiguous(memory_format=torch.channels_last).requires_grad_()
+    xdna_train.reset_fallback_stats()
+    y, ind = F.max_pool2d(xx, 3, 2, 1, return_indices=True)
+    y.backward(torch.ones_like(y))
+    assert xdna_train.kernel_stats().get("maxpool2d.indices", 0) == 0
+    _, ic = F.max_pool2d(x.contiguous(memory_format=torch.channels_last), 3, 2, 1, return_indices=True)
+    assert torch.equal(ind.cpu(), ic)
+    assert xdna_train.kernel_stats().get("maxpool2d.indices", 0) == 1
