@@ -75,15 +75,18 @@ __global__ void __launch_bounds__(kColThreads) im2col_kernel(const uint16_t* __r
 }
 
 // Column copy by output rows through shared memory: a CTA takes one output
-// row (b, oy) at a time, stages the kh input rows its windows read -- zero
+// row (b, oy) at a time and stages the kh input rows its windows read -- zero
 // padded left and right, zero rows outside the image -- as [kh][Wpad][C]
-// (Wpad = W + 2*px), then writes the row's Wo*Kp columns in 16-byte chunks,
-// consecutive chunks to consecutive addresses, each of the chunk's 8 columns
-// one shared-memory read at a per-column offset (a table) plus the pixel's
-// window origin ox*sx*C.  For stems (3 channels, 7x7): the input is read
-// once per output row instead of once per column element, and the stores are
-// full 16-byte lines.
-constexpr int kRowTileMaxBytes = 40 * 1024;
+// (Wpad = W + 2*px), twice: as bf16 elements and as 32-bit pairs (element e
+// and e + 1), so that two adjacent columns that read adjacent elements (the
+// same window row) cost one 4-byte shared load.  Thread t keeps column
+// chunk j = t % J (8 columns, J = Kp / 8) for the whole kernel -- its eight
+// element offsets and which of its four column pairs are adjacent sit in
+// registers -- and writes that chunk for pixels ox = t / J, t / J + 256 / J,
+// ... of each row as one 16-byte store.  For a stem (3 channels, 7x7) the
+// input is read once per output row and a 16-byte chunk costs about four
+// shared loads.
+constexpr int kRowTileMaxBytes = 48 * 1024;
 
 __global__ void __launch_bounds__(kColThreads) im2col_rowtile_kernel(const uint16_t* __restrict__ x, ConvGeom g,
                                                                      uint16_t* __restrict__ col) {
@@ -91,53 +94,93 @@ __global__ void __launch_bounds__(kColThreads) im2col_rowtile_kernel(const uint1
   const int K = int(g.K), Kp = int(g.Kp), C = int(g.C), kh = g.kh;
   const int Wpad = int(g.W) + 2 * g.px;
   const int rowlen = Wpad * C;  // elements of one staged input row
-  int* off = reinterpret_cast<int*>(rt_smem);
-  uint16_t* stage = reinterpret_cast<uint16_t*>(rt_smem + ((size_t(Kp) * 4 + 15) & ~size_t(15)));
-  for (int k = threadIdx.x; k < Kp; k += kColThreads) {
+  const int staged = kh * rowlen;
+  uint32_t* pairs = reinterpret_cast<uint32_t*>(rt_smem);
+  uint16_t* stage = reinterpret_cast<uint16_t*>(rt_smem + size_t(staged) * 4);
+  const int Wo = int(g.Wo), J = Kp / 8, L = kColThreads / J;
+  const int j = int(threadIdx.x) % J, lane = int(threadIdx.x) / J;
+  // this thread's eight columns: element offsets in the stage (-1: zero)
+  int o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int k = j * 8 + e;
     if (k < K) {
       const int ci = k % C, tap = k / C;
-      off[k] = (tap / g.kw) * rowlen + (tap % g.kw) * g.dx * C + ci;
+      o[e] = (tap / g.kw) * rowlen + (tap % g.kw) * g.dx * C + ci;
     } else {
-      off[k] = -1;  // padding column: zero
+      o[e] = -1;
     }
   }
-  const int Wo = int(g.Wo), J = Kp / 8;
+  bool adj[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) adj[h] = o[2 * h] >= 0 && o[2 * h + 1] == o[2 * h] + 1;
+  // channels-last input rows dense and 16-byte aligned: vector staging
+  const bool dense = g.sc == 1 && g.sw == g.C && (g.W * g.C) % 8 == 0 && g.sh % 8 == 0 && g.sb % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   const long long rows = g.B * g.Ho;
-  const int staged = kh * rowlen;
   for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
     const int oy = int(r % g.Ho);
     const long long b = r / g.Ho;
     const uint16_t* xb = x + b * g.sb;
-    __syncthreads();  // the previous row's reads of the stage (and the table) are done
-    for (int e = threadIdx.x; e < staged; e += kColThreads) {
-      const int ky = e / rowlen, rem = e - ky * rowlen;
-      const int ixp = rem / C, ci = rem - ixp * C;
-      const int iy = oy * g.sy - g.py + ky * g.dy, ix = ixp - g.px;
-      uint16_t v = 0;
-      if (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W)
-        v = __ldg(xb + (long long)ci * g.sc + (long long)iy * g.sh + (long long)ix * g.sw);
-      stage[e] = v;
+    __syncthreads();  // the previous row's reads of the stage are done
+    if (dense) {
+      // each input row is W*C contiguous elements: 16-byte loads, the zero
+      // padding columns and the rows outside the image written as zeros
+      const int pad = g.px * C, vr = int(g.W) * C / 8;
+      for (int e = threadIdx.x; e < kh * vr; e += kColThreads) {
+        const int ky = e / vr, q = e - ky * vr;
+        const int iy = oy * g.sy - g.py + ky * g.dy;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (iy >= 0 && iy < g.H) v = __ldg(reinterpret_cast<const uint4*>(xb + (long long)iy * g.sh) + q);
+        uint16_t* d = stage + ky * rowlen + pad + q * 8;
+        const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          d[2 * h] = uint16_t(wd[h] & 0xffffu);
+          d[2 * h + 1] = uint16_t(wd[h] >> 16);
+        }
+      }
+      for (int e = threadIdx.x; e < kh * 2 * pad; e += kColThreads) {
+        const int ky = e / (2 * pad), t = e - ky * 2 * pad;
+        stage[ky * rowlen + (t < pad ? t : rowlen - 2 * pad + t)] = 0;
+      }
+    } else {
+      for (int e = threadIdx.x; e < staged; e += kColThreads) {
+        const int ky = e / rowlen, rem = e - ky * rowlen;
+        const int ixp = rem / C, ci = rem - ixp * C;
+        const int iy = oy * g.sy - g.py + ky * g.dy, ix = ixp - g.px;
+        uint16_t v = 0;
+        if (iy >= 0 && iy < g.H && ix >= 0 && ix < g.W)
+          v = __ldg(xb + (long long)ci * g.sc + (long long)iy * g.sh + (long long)ix * g.sw);
+        stage[e] = v;
+      }
     }
     __syncthreads();
-    uint16_t* dst = col + r * (long long)Wo * Kp;
-    for (int u = threadIdx.x; u < Wo * J; u += kColThreads) {
-      const int ox = u / J, j = u - ox * J;
+    for (int e = threadIdx.x; e < staged; e += kColThreads)
+      pairs[e] = uint32_t(stage[e]) | (e + 1 < staged ? uint32_t(stage[e + 1]) << 16 : 0u);
+    __syncthreads();
+    if (lane >= L) continue;
+    uint16_t* dst = col + r * (long long)Wo * Kp + j * 8;
+    for (int ox = lane; ox < Wo; ox += L) {
       const int base = ox * g.sx * C;
       uint32_t w[4];
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const int o0 = off[j * 8 + 2 * h], o1 = off[j * 8 + 2 * h + 1];
-        const uint32_t lo = o0 >= 0 ? stage[base + o0] : 0u;
-        const uint32_t hi = o1 >= 0 ? stage[base + o1] : 0u;
-        w[h] = lo | (hi << 16);
+        if (adj[h]) {
+          w[h] = pairs[base + o[2 * h]];
+        } else {
+          const uint32_t lo = o[2 * h] >= 0 ? stage[base + o[2 * h]] : 0u;
+          const uint32_t hi = o[2 * h + 1] >= 0 ? stage[base + o[2 * h + 1]] : 0u;
+          w[h] = lo | (hi << 16);
+        }
       }
-      *reinterpret_cast<uint4*>(dst + (long long)ox * Kp + j * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(dst + (long long)ox * Kp) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
 size_t rowtile_smem(const ConvGeom& g) {
-  return ((size_t(g.Kp) * 4 + 15) & ~size_t(15)) + size_t(g.kh) * size_t(g.W + 2 * g.px) * size_t(g.C) * 2;
+  return size_t(g.kh) * size_t(g.W + 2 * g.px) * size_t(g.C) * 6;  // pairs (4 B) and elements (2 B)
 }
 
 // Fallback for K > kMaxTabK: one thread per column element.
@@ -337,7 +380,7 @@ b2_status b2_im2col_bf16(const void* x, int64_t sb, int64_t sc, int64_t sh, int6
     const long long units = P * kh * kw * (C / 8);
     im2col_nhwc8_kernel<<<col_grid(units, sms), kColThreads, 0, st>>>(static_cast<const uint16_t*>(x), g,
                                                                       static_cast<uint16_t*>(col));
-  } else if (g.Kp % 8 == 0 && (reinterpret_cast<uintptr_t>(col) & 15) == 0 && g.Kp <= kMaxTabK &&
+  } else if (g.Kp % 8 == 0 && (reinterpret_cast<uintptr_t>(col) & 15) == 0 && g.Kp / 8 <= kColThreads &&
              rowtile_smem(g) <= size_t(kRowTileMaxBytes) && g.Wo * (g.Kp / 8) < (1LL << 31)) {
     const size_t smem = rowtile_smem(g);
     const long long rows = B * Ho;

@@ -50,7 +50,9 @@ def col_reference(x, kh, kw, s, p, d):
 
 
 @pytest.mark.parametrize("shape,k,s,p,d,cl", [((2, 3, 11, 13), 7, 2, 3, 1, False), ((2, 16, 9, 9), 3, 1, 2, 2, True),
-                                              ((1, 5, 6, 7), 5, 3, 1, 1, True)])
+                                              ((1, 5, 6, 7), 5, 3, 1, 1, True),
+                                              # dense channels-last rows: 16-byte row staging
+                                              ((2, 3, 16, 24), 7, 2, 3, 1, True), ((1, 3, 9, 16), 9, 1, 4, 1, True)])
 def test_im2col_matches_gather(cuda, shape, k, s, p, d, cl):
     x = torch.randn(*shape).bfloat16()
     ref, Ho, Wo = col_reference(x, k, k, s, p, d)
