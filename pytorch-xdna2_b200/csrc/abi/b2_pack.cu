@@ -459,6 +459,46 @@ __global__ void pack_weight_kernel(const uint16_t* __restrict__ w, WStrides ws, 
   }
 }
 
+// The same packing, 8 consecutive K entries (one 16-byte store) per thread:
+// unit u = (n, k8) with k = chunk*576 + tap*64 + c8*8.  Forward: the 8
+// channels ci = chunk*64 + c8*8 + e of w[co][ci][tap] -- one 16-byte load
+// when the channel stride is 1 (channels-last weights), else 8 loads; dgrad:
+// the 8 output channels co = chunk*64 + c8*8 + e of w[co][ci][8 - tap].
+// Needs the reduced channel count (Cin forward, Cout dgrad) % 8 == 0.
+__global__ void pack_weight_vec_kernel(const uint16_t* __restrict__ w, WStrides ws, int Cout, int Cin, int chunks,
+                                       int dgrad, uint16_t* __restrict__ wk) {
+  const int k8tot = chunks * 72;  // 576 / 8
+  const int nrows = dgrad ? Cin : Cout;
+  const int kred = dgrad ? Cout : Cin;
+  const long long total = (long long)nrows * k8tot;
+  const bool vec = !dgrad && ws.ci == 1 && (ws.co % 8) == 0 && (ws.ky % 8) == 0 && (ws.kx % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int n = int(i / k8tot);
+    const int k8 = int(i % k8tot);
+    const int chunk = k8 / 72, rem = k8 % 72;
+    const int tap = rem / 8, c0 = chunk * 64 + (rem % 8) * 8;
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (c0 < kred) {
+      const int t = dgrad ? 8 - tap : tap;
+      const long long tapoff = (t / 3) * ws.ky + (t % 3) * ws.kx;
+      if (vec) {
+        out = __ldg(reinterpret_cast<const uint4*>(w + n * ws.co + c0 + tapoff));
+      } else {
+        uint32_t v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const long long co = dgrad ? c0 + e : n, ci = dgrad ? n : c0 + e;
+          v[e] = __ldg(w + co * ws.co + ci * ws.ci + tapoff);
+        }
+        out = make_uint4(v[0] | (v[1] << 16), v[2] | (v[3] << 16), v[4] | (v[5] << 16), v[6] | (v[7] << 16));
+      }
+    }
+    reinterpret_cast<uint4*>(wk)[i] = out;
+  }
+}
+
 // [B][R][S] -> [B][S][R] bf16 tile transpose (R, S arbitrary).
 __global__ void __launch_bounds__(256) transpose_kernel(const uint16_t* __restrict__ src,
                                                         uint16_t* __restrict__ dst, int R, int S) {
@@ -703,6 +743,12 @@ static b2_status pack_weight(const void* w, WStrides ws, int Cout, int Cin, int 
   if (Cout <= 0 || Cin <= 0 || chunks < (kred + 63) / 64) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
   if (ws.co < 0 || ws.ci < 0 || ws.ky < 0 || ws.kx < 0) return set_error(B2_ERR_INVALID, "%s: negative stride", name);
   const long long total = (long long)(dgrad ? Cin : Cout) * chunks * 576;
+  if (kred % 8 == 0 && (reinterpret_cast<uintptr_t>(wk) & 15) == 0) {
+    const int blocks = int(std::min<long long>((total / 8 + 255) / 256, 148LL * 8));
+    pack_weight_vec_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(w), ws, Cout, Cin, chunks, dgrad, static_cast<uint16_t*>(wk));
+    return check_cuda(cudaGetLastError(), "pack_weight launch");
+  }
   const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 8));
   pack_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(w), ws, Cout, Cin, chunks, dgrad, static_cast<uint16_t*>(wk));
