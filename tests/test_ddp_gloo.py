@@ -50,9 +50,12 @@ def _worker(rank, world, port, mode, q):
             model(x).square().sum().backward()  # no synchronize() between: must raise
         else:
             model(x).square().sum().backward()
-        local = [p.grad.clone() for p in model.parameters()]
+        # numpy copies travel by value: a tensor put on the queue is shared
+        # through a handle that dies with this process, which may exit before
+        # the parent reads it
+        local = [p.grad.numpy().copy() for p in model.parameters()]
         ar.synchronize()
-        q.put((rank, "ok", [p.grad.clone() for p in model.parameters()], local, len(ar.buckets)))
+        q.put((rank, "ok", [p.grad.numpy().copy() for p in model.parameters()], local, len(ar.buckets)))
     except Exception as e:  # noqa: BLE001
         q.put((rank, "error", repr(e), None, None))
     finally:
@@ -88,6 +91,7 @@ def test_grads_are_averaged(mode):
     g1, l1 = out[1][2], out[1][3]
     assert nb > 1  # tiny cap: several buckets
     for a, b, x, y in zip(g0, g1, l0, l1):
+        a, b, x, y = (torch.from_numpy(t) for t in (a, b, x, y))
         assert torch.allclose(a, b)
         assert torch.allclose(a, (x + y) / 2, atol=1e-6)
 
