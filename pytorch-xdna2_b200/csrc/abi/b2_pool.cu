@@ -224,6 +224,68 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_nhwc8_k3_kernel(cons
   }
 }
 
+// The taps forward for ResNet's stem pool (3x3 windows, stride 2, padding 1,
+// no dilation): a CTA row per output row (b, oh) (grid.y), threads over its
+// (ow, channel group) units, window bounds from shifts -- the same scan, the
+// same maxima and taps as maxpool_fwd_nhwc8_k3_kernel<.., true>.
+__global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_s2k3_taps_kernel(const uint16_t* __restrict__ x,
+                                                                             PoolGeom g, int cv_shift,
+                                                                             uint16_t* __restrict__ y,
+                                                                             uint8_t* __restrict__ taps) {
+  const int H = int(g.H), W = int(g.W), OH = int(g.OH), OW = int(g.OW);
+  const int row = blockIdx.y, n = row / OH, oh = row - n * OH;
+  const int u = blockIdx.x * kPoolThreads + threadIdx.x;
+  const int ow = u >> cv_shift, q = u & ((1 << cv_shift) - 1);
+  if (ow >= OW) return;
+  const int hs = 2 * oh - 1, ws = 2 * ow - 1;  // window start (may be -1)
+  const uint16_t* xp = x + (long long)n * g.xs[0] + q * 8;
+  uint4 v[9];
+  bool ok[9];
+#pragma unroll
+  for (int t = 0; t < 9; ++t) {
+    const int h = hs + t / 3, w = ws + t % 3;
+    ok[t] = h >= 0 && h < H && w >= 0 && w < W;
+    v[t] = ok[t] ? __ldg(reinterpret_cast<const uint4*>(xp + (long long)h * g.xs[2] + (long long)w * g.xs[3]))
+                 : make_uint4(0, 0, 0, 0);
+  }
+  // the first valid tap (the general kernel's starting index)
+  const int i0 = hs < 0 ? 1 : 0, j0 = ws < 0 ? 1 : 0;
+  float best[8];
+  int bt[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    best[e] = -INFINITY;
+    bt[e] = i0 * 3 + j0;
+  }
+#pragma unroll
+  for (int t = 0; t < 9; ++t) {
+    if (!ok[t]) continue;
+    const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
+      if (f > best[e] || f != f) {
+        best[e] = f;
+        bt[e] = t;
+      }
+    }
+  }
+  const long long o = (long long)n * g.ys[0] + (long long)oh * g.ys[2] + (long long)ow * g.ys[3] + q * 8;
+  uint4 out;
+  out.x = pack_bf2(best[0], best[1]);
+  out.y = pack_bf2(best[2], best[3]);
+  out.z = pack_bf2(best[4], best[5]);
+  out.w = pack_bf2(best[6], best[7]);
+  *reinterpret_cast<uint4*>(y + o) = out;
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    lo |= uint32_t(bt[e]) << (8 * e);
+    hi |= uint32_t(bt[4 + e]) << (8 * e);
+  }
+  *reinterpret_cast<uint2*>(taps + o) = make_uint2(lo, hi);
+}
+
 // ATen's int64 indices (h*W + w within the plane) from the window taps.
 template <typename I>
 __global__ void __launch_bounds__(kPoolThreads) maxpool_taps_to_indices_kernel(const uint8_t* __restrict__ taps,
@@ -430,6 +492,65 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_taps_kernel(co
   }
 }
 
+// maxpool_bwd_nhwc8_taps_kernel for ResNet's stem pool (3x3 windows, stride
+// 2, padding 1, no dilation): a CTA row per input row (b, h) (grid.y), threads
+// over that row's (w, channel group) units; the covering outputs and the
+// expected taps come from shifts instead of divisions (the general kernel's
+// index arithmetic is most of its instructions), and the adds run in the
+// same (oh, ow) order -- the same sums.
+__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_s2k3_taps_kernel(const uint16_t* __restrict__ dy,
+                                                                             const uint8_t* __restrict__ taps,
+                                                                             PoolGeom g, int cv_shift,
+                                                                             uint16_t* __restrict__ dx) {
+  const int H = int(g.H), W = int(g.W), OH = int(g.OH), OW = int(g.OW);
+  const int row = blockIdx.y, n = row / H, h = row - n * H;
+  const int u = blockIdx.x * kPoolThreads + threadIdx.x;
+  const int w = u >> cv_shift, q = u & ((1 << cv_shift) - 1);
+  if (w >= W) return;
+  // outputs whose window covers h: oh in [lo, hi), window start 2*oh - 1
+  const int ohl = h >= 2 ? ((h - 2) >> 1) + 1 : 0, ohh = min(((h + 1) >> 1) + 1, OH);
+  const int owl = w >= 2 ? ((w - 2) >> 1) + 1 : 0, owh = min(((w + 1) >> 1) + 1, OW);
+  const uint16_t* dyn = dy + (long long)n * g.ys[0] + q * 8;
+  const uint8_t* tn = taps + (long long)n * g.ys[0] + q * 8;
+  uint4 v[4];
+  uint2 tv[4];
+  uint32_t want[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const int oh = ohl + (t >> 1), ow = owl + (t & 1);
+    if (oh < ohh && ow < owh) {
+      const long long o = (long long)oh * g.ys[2] + (long long)ow * g.ys[3];
+      v[t] = __ldg(reinterpret_cast<const uint4*>(dyn + o));
+      tv[t] = __ldg(reinterpret_cast<const uint2*>(tn + o));
+      want[t] = uint32_t((h + 1 - 2 * oh) * 3 + (w + 1 - 2 * ow));
+    } else {
+      v[t] = make_uint4(0, 0, 0, 0);
+      tv[t] = make_uint2(0, 0);
+      want[t] = 0xffffffffu;
+    }
+  }
+  float s[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t tap = ((e < 4 ? tv[t].x : tv[t].y) >> (8 * (e & 3))) & 0xffu;
+      if (tap == want[t])
+        s[e] = __fadd_rn(s[e], __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16)));
+    }
+  }
+  uint4 out;
+  out.x = pack_bf2(s[0], s[1]);
+  out.y = pack_bf2(s[2], s[3]);
+  out.z = pack_bf2(s[4], s[5]);
+  out.w = pack_bf2(s[6], s[7]);
+  *reinterpret_cast<uint4*>(dx + (long long)n * g.xs[0] + (long long)h * g.xs[2] + (long long)w * g.xs[3] + q * 8) =
+      out;
+}
+
 // every input position covered by at most two outputs per dimension
 bool two_cover(const PoolGeom& g) {
   return (long long)(g.kh - 1) * g.dh + 1 <= 2LL * g.sh && (long long)(g.kw - 1) * g.dw + 1 <= 2LL * g.sw;
@@ -564,6 +685,16 @@ extern "C" b2_status b2_maxpool2d_fwd_taps(const void* x, const int64_t* x_strid
   if (!x || !y || !taps) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
   if (kh != 3 || kw != 3 || !nhwc8(g, x, y, y) || (reinterpret_cast<uintptr_t>(taps) & 7) || !fits32(g))
     return set_error(B2_ERR_UNSUPPORTED, "%s: needs 3x3 windows over channels-last bf16 (C %% 8 == 0)", who);
+  const long long cv = C / 8;
+  int cv_shift = 0;
+  while ((1LL << cv_shift) < cv) ++cv_shift;
+  if (sh == 2 && sw == 2 && ph == 1 && pw == 1 && dh == 1 && dw == 1 && (1LL << cv_shift) == cv &&
+      OW * cv < (1LL << 30) && N * OH <= 65535) {
+    const dim3 grid(unsigned((OW * cv + kPoolThreads - 1) / kPoolThreads), unsigned(N * OH));
+    maxpool_fwd_s2k3_taps_kernel<<<grid, kPoolThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(x), g, cv_shift, static_cast<uint16_t*>(y), static_cast<uint8_t*>(taps));
+    return check_cuda(cudaGetLastError(), "maxpool fwd taps launch");
+  }
   maxpool_fwd_nhwc8_k3_kernel<int, true><<<pool_grid(total / 8, cur_sms()), kPoolThreads, 0,
                                            static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(x), g, static_cast<uint16_t*>(y), nullptr, static_cast<uint8_t*>(taps));
@@ -601,6 +732,16 @@ extern "C" b2_status b2_maxpool2d_bwd_taps(const void* dy, const void* taps, con
   if (kh * kw > 256 || !nhwc8(g, dx, dy, dy) || (reinterpret_cast<uintptr_t>(taps) & 7) || !fits32(g) ||
       !two_cover(g))
     return set_error(B2_ERR_UNSUPPORTED, "%s: needs channels-last bf16 and windows spanning <= 2 strides", who);
+  const long long cv = C / 8;
+  int cv_shift = 0;
+  while ((1LL << cv_shift) < cv) ++cv_shift;
+  if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && ph == 1 && pw == 1 && dh == 1 && dw == 1 &&
+      (1LL << cv_shift) == cv && W * cv < (1LL << 30) && N * H <= 65535) {
+    const dim3 grid(unsigned((W * cv + kPoolThreads - 1) / kPoolThreads), unsigned(N * H));
+    maxpool_bwd_s2k3_taps_kernel<<<grid, kPoolThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(dy), static_cast<const uint8_t*>(taps), g, cv_shift, static_cast<uint16_t*>(dx));
+    return check_cuda(cudaGetLastError(), "maxpool bwd taps launch");
+  }
   maxpool_bwd_nhwc8_taps_kernel<int><<<pool_grid(total / 8, cur_sms()), kPoolThreads, 0,
                                        static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(dy), static_cast<const uint8_t*>(taps), g, static_cast<uint16_t*>(dx));
