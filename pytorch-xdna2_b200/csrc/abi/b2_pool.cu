@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_fwd_s2k3_taps_kernel(con
                                                                              uint8_t* __restrict__ taps) {
   const int H = int(g.H), W = int(g.W), OH = int(g.OH), OW = int(g.OW);
   const int row = blockIdx.y, n = row / OH, oh = row - n * OH;
-  const int u = blockIdx.x * kPoolThreads + threadIdx.x;
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
   const int ow = u >> cv_shift, q = u & ((1 << cv_shift) - 1);
   if (ow >= OW) return;
   const int hs = 2 * oh - 1, ws = 2 * ow - 1;  // window start (may be -1)
@@ -493,65 +493,79 @@ __global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_nhwc8_taps_kernel(co
 }
 
 // maxpool_bwd_nhwc8_taps_kernel for ResNet's stem pool (3x3 windows, stride
-// 2, padding 1, no dilation): a CTA row per input row (b, h) (grid.y), threads
-// over that row's (w, channel group) units; the covering outputs and the
-// expected taps come from shifts instead of divisions (the general kernel's
-// index arithmetic is most of its instructions), and the adds run in the
-// same (oh, ow) order -- the same sums.
-__global__ void __launch_bounds__(kPoolThreads) maxpool_bwd_s2k3_taps_kernel(const uint16_t* __restrict__ dy,
-                                                                             const uint8_t* __restrict__ taps,
-                                                                             PoolGeom g, int cv_shift,
-                                                                             uint16_t* __restrict__ dx) {
+// 2, padding 1, no dilation; 2*OH >= H and 2*OW >= W).  A thread per output
+// window (b, oh, ow, channel group) owns the 2x2 input block (2oh + a,
+// 2ow + b), a, b in {0, 1}: the windows covering those inputs are (oh, ow),
+// (oh, ow + 1), (oh + 1, ow) and (oh + 1, ow + 1), so four dy/taps reads make
+// four dx groups (the per-input form reads 2.25 windows per input).  Window
+// (oh, ow) sends taps 4/5/7/8 to (0,0)/(0,1)/(1,0)/(1,1); (oh, ow + 1) taps 3/6
+// to (0,1)/(1,1); (oh + 1, ow) taps 1/2 to (1,0)/(1,1); (oh + 1, ow + 1) tap 0
+// to (1,1).  Each input's adds run in the same (oh, ow) order from 0.0f as
+// the general kernel's -- the same sums.  CTA row (grid.y) = (b, oh).
+__global__ void __launch_bounds__(512) maxpool_bwd_s2k3_quad_kernel(const uint16_t* __restrict__ dy,
+                                                                    const uint8_t* __restrict__ taps, PoolGeom g,
+                                                                    int cv_shift, uint16_t* __restrict__ dx) {
   const int H = int(g.H), W = int(g.W), OH = int(g.OH), OW = int(g.OW);
-  const int row = blockIdx.y, n = row / H, h = row - n * H;
-  const int u = blockIdx.x * kPoolThreads + threadIdx.x;
-  const int w = u >> cv_shift, q = u & ((1 << cv_shift) - 1);
-  if (w >= W) return;
-  // outputs whose window covers h: oh in [lo, hi), window start 2*oh - 1
-  const int ohl = h >= 2 ? ((h - 2) >> 1) + 1 : 0, ohh = min(((h + 1) >> 1) + 1, OH);
-  const int owl = w >= 2 ? ((w - 2) >> 1) + 1 : 0, owh = min(((w + 1) >> 1) + 1, OW);
+  const int row = blockIdx.y, n = row / OH, oh = row - n * OH;
+  const int u = blockIdx.x * blockDim.x + threadIdx.x;
+  const int ow = u >> cv_shift, q = u & ((1 << cv_shift) - 1);
+  if (ow >= OW) return;
   const uint16_t* dyn = dy + (long long)n * g.ys[0] + q * 8;
   const uint8_t* tn = taps + (long long)n * g.ys[0] + q * 8;
   uint4 v[4];
   uint2 tv[4];
-  uint32_t want[4];
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
-    const int oh = ohl + (t >> 1), ow = owl + (t & 1);
-    if (oh < ohh && ow < owh) {
-      const long long o = (long long)oh * g.ys[2] + (long long)ow * g.ys[3];
+    const int wh = oh + (t >> 1), ww = ow + (t & 1);
+    if (wh < OH && ww < OW) {
+      const long long o = (long long)wh * g.ys[2] + (long long)ww * g.ys[3];
       v[t] = __ldg(reinterpret_cast<const uint4*>(dyn + o));
       tv[t] = __ldg(reinterpret_cast<const uint2*>(tn + o));
-      want[t] = uint32_t((h + 1 - 2 * oh) * 3 + (w + 1 - 2 * ow));
     } else {
       v[t] = make_uint4(0, 0, 0, 0);
-      tv[t] = make_uint2(0, 0);
-      want[t] = 0xffffffffu;
+      tv[t] = make_uint2(0xffffffffu, 0xffffffffu);  // no tap matches 255
     }
   }
-  float s[8];
+  float s[4][8];  // [a * 2 + b][channel]
 #pragma unroll
-  for (int e = 0; e < 8; ++e) s[e] = 0.0f;
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[k][e] = 0.0f;
+  // tap -> owned input (a * 2 + b) for each window, -1 where the tap lies outside the block
+  constexpr int kDst[4][9] = {{-1, -1, -1, -1, 0, 1, -1, 2, 3},
+                              {-1, -1, -1, 1, -1, -1, 3, -1, -1},
+                              {-1, 2, 3, -1, -1, -1, -1, -1, -1},
+                              {3, -1, -1, -1, -1, -1, -1, -1, -1}};
 #pragma unroll
   for (int t = 0; t < 4; ++t) {
     const uint32_t wd[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const uint32_t tap = ((e < 4 ? tv[t].x : tv[t].y) >> (8 * (e & 3))) & 0xffu;
-      if (tap == want[t])
-        s[e] = __fadd_rn(s[e], __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16)));
+      const float f = __uint_as_float((e & 1) ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
+#pragma unroll
+      for (int k = 0; k < 9; ++k)
+        if (kDst[t][k] >= 0 && tap == uint32_t(k)) s[kDst[t][k]][e] = __fadd_rn(s[kDst[t][k]][e], f);
     }
   }
-  uint4 out;
-  out.x = pack_bf2(s[0], s[1]);
-  out.y = pack_bf2(s[2], s[3]);
-  out.z = pack_bf2(s[4], s[5]);
-  out.w = pack_bf2(s[6], s[7]);
-  *reinterpret_cast<uint4*>(dx + (long long)n * g.xs[0] + (long long)h * g.xs[2] + (long long)w * g.xs[3] + q * 8) =
-      out;
+  uint16_t* dxn = dx + (long long)n * g.xs[0] + q * 8;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int h = 2 * oh + (k >> 1), w = 2 * ow + (k & 1);
+    if (h >= H || w >= W) continue;
+    uint4 out;
+    out.x = pack_bf2(s[k][0], s[k][1]);
+    out.y = pack_bf2(s[k][2], s[k][3]);
+    out.z = pack_bf2(s[k][4], s[k][5]);
+    out.w = pack_bf2(s[k][6], s[k][7]);
+    *reinterpret_cast<uint4*>(dxn + (long long)h * g.xs[2] + (long long)w * g.xs[3]) = out;
+  }
 }
 
-// every input position covered by at most two outputs per dimension
+// Threads per CTA for a row of `units` (channel group) units: the row rounded
+// up to whole warps, at most 512 (no idle tail of a fixed 256-thread CTA).
+inline int row_threads(long long units) { return int(std::min<long long>(512, (units + 31) / 32 * 32)); }
+
 bool two_cover(const PoolGeom& g) {
   return (long long)(g.kh - 1) * g.dh + 1 <= 2LL * g.sh && (long long)(g.kw - 1) * g.dw + 1 <= 2LL * g.sw;
 }
@@ -736,9 +750,10 @@ extern "C" b2_status b2_maxpool2d_bwd_taps(const void* dy, const void* taps, con
   int cv_shift = 0;
   while ((1LL << cv_shift) < cv) ++cv_shift;
   if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && ph == 1 && pw == 1 && dh == 1 && dw == 1 &&
-      (1LL << cv_shift) == cv && W * cv < (1LL << 30) && N * H <= 65535) {
-    const dim3 grid(unsigned((W * cv + kPoolThreads - 1) / kPoolThreads), unsigned(N * H));
-    maxpool_bwd_s2k3_taps_kernel<<<grid, kPoolThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      (1LL << cv_shift) == cv && 2 * OH >= H && 2 * OW >= W && OW * cv < (1LL << 30) && N * OH <= 65535) {
+    const int bs = row_threads(OW * cv);
+    const dim3 grid(unsigned((OW * cv + bs - 1) / bs), unsigned(N * OH));
+    maxpool_bwd_s2k3_quad_kernel<<<grid, bs, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t*>(dy), static_cast<const uint8_t*>(taps), g, cv_shift, static_cast<uint16_t*>(dx));
     return check_cuda(cudaGetLastError(), "maxpool bwd taps launch");
   }

@@ -94,6 +94,9 @@ def test_maxpool_module_in_a_model():
 
 
 @pytest.mark.parametrize("shape,s,p,d", [((2, 64, 56, 56), 2, 1, 1), ((3, 16, 21, 19), 2, 1, 1),
+                                         ((1, 64, 112, 112), 2, 1, 1),  # the stem: 448-thread rows
+                                         ((1, 64, 150, 149), 2, 1, 1),  # rows over 512 units, odd W
+                                         ((2, 128, 15, 16), 2, 1, 1),
                                          ((2, 8, 17, 15), 3, 1, 1), ((2, 24, 13, 13), 2, 0, 1)])
 def test_window_taps_abi_match_int64_path(shape, s, p, d):
     """b2_maxpool2d_fwd_taps / taps_to_indices / bwd_taps against the int64
