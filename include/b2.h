@@ -197,6 +197,20 @@ b2_status b2_conv3x3_wgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh,
                                 int Cout, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* b2_conv3x3_wgrad_nhwc with dw written in [Cout][3][3][Cin] order, the
+ * storage order of a channels-last weight (OHWI), so that a channels-last
+ * model's gradient lands in its parameter's layout without a re-layout copy.
+ * Same values, bit for bit.  Replaces the same reference function as
+ * b2_conv3x3_wgrad (torch_xdna_device.cpp:2683-2751); the reference allocates
+ * that gradient in OIHW order (torch_xdna_device.cpp:4690), which autograd
+ * then copies into a channels-last parameter's layout. */
+b2_status b2_conv3x3_wgrad_nhwc_ohwi(const void* dy, int64_t dsn, int64_t dsh,
+                                     int64_t dsw, const void* x, int64_t xsn,
+                                     int64_t xsh, int64_t xsw, void* dw,
+                                     int dw_dtype, int B, int Cin, int H,
+                                     int W, int Cout, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* Weight gradient that allocates nothing (no counterpart in the reference).
  * Same result as b2_conv3x3_wgrad, but the split-K partial sums live in one
  * fixed device array inside this library instead of a caller workspace, for

@@ -1588,16 +1588,27 @@ __global__ void gemm_split_reduce_kernel(const float* __restrict__ partial, int 
   }
 }
 
+// ohwi: dw in [Cout][3][3][Cin] order (a channels-last weight's layout),
+// which also reads the [tap][Cout][Cin] partials contiguously; otherwise OIHW.
+// Same sums, in the same split order, either way.
 __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw, int dtype,
-                                    int splits, int Cout, int Cin) {
+                                    int splits, int Cout, int Cin, bool ohwi = false) {
   const long long total = (long long)Cout * Cin * 9;
   const long long plane = (long long)9 * Cout * Cin;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
-    const int tap = int(i % 9);
-    const long long oc = i / 9;
-    const int ci = int(oc % Cin);
-    const int co = int(oc / Cin);
+    int tap, ci, co;
+    if (ohwi) {
+      ci = int(i % Cin);
+      const long long ct = i / Cin;
+      tap = int(ct % 9);
+      co = int(ct / 9);
+    } else {
+      tap = int(i % 9);
+      const long long oc = i / 9;
+      ci = int(oc % Cin);
+      co = int(oc / Cin);
+    }
     const float* src = partial + ((long long)tap * Cout + co) * Cin + ci;
     float s = 0.f;
     for (int k = 0; k < splits; ++k) s += src[k * plane];
@@ -2289,7 +2300,7 @@ size_t b2_conv3x3_wgrad_workspace_bytes(int B, int Cin, int H, int W, int Cout) 
 
 static b2_status wgrad_common(ActSrc dys, ActSrc xs, void* dw, int dw_dtype, int B, int Cin, int H,
                               int W, int Cout, void* workspace, size_t workspace_bytes, void* stream,
-                              const char* name) {
+                              const char* name, bool ohwi = false) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!dw || !workspace) return set_error(B2_ERR_INVALID, "%s: null pointer", name);
   if (B <= 0 || Cin <= 0 || H <= 0 || W <= 0 || Cout <= 0) return set_error(B2_ERR_INVALID, "%s: bad shape", name);
@@ -2333,7 +2344,7 @@ static b2_status wgrad_common(ActSrc dys, ActSrc xs, void* dw, int dw_dtype, int
     const long long total = (long long)Cout * Cin * 9;
     const int blocks = int(std::min<long long>((total + 255) / 256, 148LL * 16));
     wgrad_reduce_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(workspace), dw, dw_dtype, nw.splits,
-                                                Cout, Cin);
+                                                Cout, Cin, ohwi);
     return check_cuda(cudaGetLastError(), "wgrad reduce launch");
   }
   // Channels-last dY and X: k-blocks are 64-pixel patches fetched by tiled
@@ -2394,7 +2405,7 @@ static b2_status wgrad_common(ActSrc dys, ActSrc xs, void* dw, int dw_dtype, int
   const int threads = 256;
   const int blocks = int(std::min<long long>((total + threads - 1) / threads, 148LL * 16));
   wgrad_reduce_kernel<<<blocks, threads, 0, st>>>(static_cast<const float*>(workspace), dw, dw_dtype,
-                                                  w.splits, Cout, Cin);
+                                                  w.splits, Cout, Cin, ohwi);
   return check_cuda(cudaGetLastError(), "wgrad reduce launch");
 }
 
@@ -2434,6 +2445,13 @@ b2_status b2_conv3x3_wgrad_nhwc(const void* dy, int64_t dsn, int64_t dsh, int64_
                                 int Cout, void* workspace, size_t workspace_bytes, void* stream) {
   return wgrad_common(nhwc_src(dy, dsn, dsh, dsw), nhwc_src(x, xsn, xsh, xsw), dw, dw_dtype, B, Cin, H, W, Cout,
                       workspace, workspace_bytes, stream, "b2_conv3x3_wgrad_nhwc");
+}
+
+b2_status b2_conv3x3_wgrad_nhwc_ohwi(const void* dy, int64_t dsn, int64_t dsh, int64_t dsw, const void* x,
+                                     int64_t xsn, int64_t xsh, int64_t xsw, void* dw, int dw_dtype, int B, int Cin,
+                                     int H, int W, int Cout, void* workspace, size_t workspace_bytes, void* stream) {
+  return wgrad_common(nhwc_src(dy, dsn, dsh, dsw), nhwc_src(x, xsn, xsh, xsw), dw, dw_dtype, B, Cin, H, W, Cout,
+                      workspace, workspace_bytes, stream, "b2_conv3x3_wgrad_nhwc_ohwi", true);
 }
 
 b2_status b2_gemm_bf16(int transA, int transB, int M, int N, int K, float alpha, const void* A,

@@ -487,9 +487,10 @@ bool nhwc_ok(const at::Tensor& t) {
   return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
 }
 
-// dW from channels-last dY and x read in place (see launch_wgrad).
+// dW from channels-last dY and x read in place (see launch_wgrad); ohwi:
+// written in a channels-last weight's [Cout][3][3][Cin] order.
 void launch_wgrad_nhwc(const at::Tensor& dy, const at::Tensor& x, void* gw, at::ScalarType dtype,
-                       c10::DeviceIndex dev, int B, int Cin, int H, int W, int Cout) {
+                       c10::DeviceIndex dev, int B, int Cin, int H, int W, int Cout, bool ohwi) {
   c10::cuda::CUDAGuard g(dev);
   materialize(dy);
   materialize(x);
@@ -497,9 +498,9 @@ void launch_wgrad_nhwc(const at::Tensor& dy, const at::Tensor& x, void* gw, at::
   at::Tensor ws = empty({int64_t((ws_bytes + 15) / 16) * 4}, at::kFloat, dev);
   const int dt = dtype == at::kFloat ? B2_F32 : B2_BF16;
   KernelTimer kt("conv3x3.wgrad", 18.0 * B * H * W * Cin * Cout, stream(dev));
-  XDNA_B2(b2_conv3x3_wgrad_nhwc(dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(), x.stride(0),
-                                x.stride(2), x.stride(3), gw, dt, B, Cin, H, W, Cout, ws.data_ptr(),
-                                size_t(ws.numel()) * 4, stream(dev)));
+  auto* fn = ohwi ? b2_conv3x3_wgrad_nhwc_ohwi : b2_conv3x3_wgrad_nhwc;
+  XDNA_B2(fn(dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(), x.stride(0), x.stride(2),
+             x.stride(3), gw, dt, B, Cin, H, W, Cout, ws.data_ptr(), size_t(ws.numel()) * 4, stream(dev)));
   count_launch("conv3x3.wgrad", 2);  // igemm + split-K reduce
 }
 
@@ -676,12 +677,17 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> convolution_backward_overrideable
     count_launch("conv3x3.dgrad");
   }
   if (output_mask[1]) {
-    dw = empty({Cout, Cin, 3, 3}, weight.scalar_type(), dev);
+    // a channels-last weight gets its gradient in its own layout (autograd
+    // would otherwise copy an OIHW gradient into the parameter's strides)
+    const bool ohwi = g_mode.load() > 1 && both_cl && weight.is_contiguous(at::MemoryFormat::ChannelsLast) &&
+                      !weight.is_contiguous();
+    dw = empty({Cout, Cin, 3, 3}, weight.scalar_type(), dev,
+               ohwi ? at::MemoryFormat::ChannelsLast : at::MemoryFormat::Contiguous);
     if (g_mode.load() > 1 && both_cl) {
       // dY and x themselves are the operands: the job keeps them alive, and a
       // write into either (before_write) runs it first
       auto job = [dy = grad_output, x = input, gw = dw.data_ptr(), dtype = dw.scalar_type(), dev, B, Cin, H, W,
-                  Cout]() { launch_wgrad_nhwc(dy, x, gw, dtype, dev, B, Cin, H, W, Cout); };
+                  Cout, ohwi]() { launch_wgrad_nhwc(dy, x, gw, dtype, dev, B, Cin, H, W, Cout, ohwi); };
       if (deferral_enabled())
         defer_epilogue(dw, {grad_output, input}, nullptr, std::move(job));
       else

@@ -62,6 +62,8 @@ SIGNATURES = {
     "b2_conv3x3_fwd_nhwc": [vp, i64, i64, i64, vp, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, i32, vp],
     "b2_conv3x3_dgrad_nhwc": [vp, i64, i64, i64, vp, vp, i64, i64, i64, i64, i32, i32, i32, i32, i32, vp],
     "b2_conv3x3_wgrad_nhwc": [vp, i64, i64, i64, vp, i64, i64, i64, vp, i32, i32, i32, i32, i32, i32, vp, sz, vp],
+    "b2_conv3x3_wgrad_nhwc_ohwi": [vp, i64, i64, i64, vp, i64, i64, i64, vp, i32, i32, i32, i32, i32, i32, vp, sz,
+                                   vp],
     "b2_conv3x3_wgrad_noalloc_max_bytes": [],
     "b2_gemm_bf16": [i32, i32, i32, i32, i32, f32, vp, i64, i64, vp, i64, i64, f32, vp, i32,
                      i64, i64, i64, vp, i64, i64, i32, vp],

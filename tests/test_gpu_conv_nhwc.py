@@ -101,7 +101,23 @@ def test_nhwc_entry_points_bit_exact_vs_padded_rows(cuda, shape):
     _abi.call("b2_conv3x3_wgrad_nhwc", dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(),
               x.stride(0), x.stride(2), x.stride(3), dw1.data_ptr(), _abi.B2_F32, B, Cin, H, W, Cout, ws.data_ptr(),
               wsb, _st())
+    # the same weight gradient written in a channels-last weight's OHWI order,
+    # fp32 and bf16: the same sums, bit for bit
+    dw2 = torch.full((Cout, 3, 3, Cin), float("nan"), dtype=torch.float32, device=cuda)
+    _abi.call("b2_conv3x3_wgrad_nhwc_ohwi", dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(),
+              x.stride(0), x.stride(2), x.stride(3), dw2.data_ptr(), _abi.B2_F32, B, Cin, H, W, Cout, ws.data_ptr(),
+              wsb, _st())
+    dw3 = torch.empty(Cout, Cin, 3, 3, dtype=torch.bfloat16, device=cuda)
+    dw4 = torch.empty(Cout, 3, 3, Cin, dtype=torch.bfloat16, device=cuda)
+    _abi.call("b2_conv3x3_wgrad_nhwc", dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(),
+              x.stride(0), x.stride(2), x.stride(3), dw3.data_ptr(), _abi.B2_BF16, B, Cin, H, W, Cout, ws.data_ptr(),
+              wsb, _st())
+    _abi.call("b2_conv3x3_wgrad_nhwc_ohwi", dy.data_ptr(), dy.stride(0), dy.stride(2), dy.stride(3), x.data_ptr(),
+              x.stride(0), x.stride(2), x.stride(3), dw4.data_ptr(), _abi.B2_BF16, B, Cin, H, W, Cout, ws.data_ptr(),
+              wsb, _st())
     torch.cuda.synchronize()
+    assert torch.equal(dw2.permute(0, 3, 1, 2).view(torch.int32), dw1.view(torch.int32))
+    assert torch.equal(dw4.permute(0, 3, 1, 2).view(torch.int16), dw3.view(torch.int16))
     assert torch.equal(y0, y1)
     assert torch.equal(dx0, dx1)
     # dW: the all-taps narrow kernel reads the same padded-grid k-blocks either
@@ -170,6 +186,10 @@ def test_channels_last_training_step_makes_no_padded_copies(cuda):
         xdna_train.reset_mapped_cpu_stats()
         y = m(xx)
         y.backward(gy.to(X).contiguous(memory_format=mf))
+        # each weight's gradient arrives in its parameter's own layout (no
+        # re-layout copy by autograd): OHWI for a channels-last weight
+        for p in m.parameters():
+            assert p.grad.stride() == p.stride(), (p.shape, p.grad.stride(), p.stride())
         out = [y.detach().cpu(), xx.grad.cpu()] + [p.grad.cpu() for p in m.parameters()]
         return out, dict(xdna_train.kernel_stats())
     cl, ks_cl = run(torch.channels_last)
