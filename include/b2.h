@@ -539,6 +539,22 @@ b2_status b2_batch_norm_stats_bf16(const void* x, int layout, int pdtype,
                                    int64_t N, int64_t C, int64_t HW,
                                    float momentum, float eps, void* workspace,
                                    size_t workspace_bytes, void* stream);
+/* b2_batch_norm_stats_bf16 that also advances a module's step counter:
+ * *count += count_inc (count: an int64 scalar in device memory, 8-byte
+ * aligned) in the same launch, once.  A training BatchNorm2d runs
+ * `num_batches_tracked.add_(1)` right before its forward; done here, that
+ * increment costs no kernel of its own.  Replaces the pair of that add_
+ * (through the CPU-alias fallback, torch_xdna_device.cpp:5124-5260) and
+ * native_batch_norm_xdna's statistics (torch_xdna_device.cpp:4214-4358).
+ * Empty inputs are refused (nothing would run the increment). */
+b2_status b2_batch_norm_stats_count_bf16(const void* x, int layout, int pdtype,
+                                         void* rm, void* rv, int rdtype,
+                                         float* save_mean, float* save_invstd,
+                                         int64_t N, int64_t C, int64_t HW,
+                                         float momentum, float eps,
+                                         int64_t* count, int64_t count_inc,
+                                         void* workspace,
+                                         size_t workspace_bytes, void* stream);
 b2_status b2_batch_norm_apply_bf16(const void* x, int layout, const void* w,
                                    const void* b, int pdtype, const float* mean,
                                    const float* invstd, const void* residual,

@@ -102,6 +102,10 @@ struct BnChan {
   void* rm;
   void* rv;
   int rdtype;  // dtype of rm, rv; statistics updated when both are non-null
+  // a module's step counter (int64 scalar) advanced by `count_inc` in the
+  // same launch (b2_batch_norm_stats_count_bf16); none when null
+  long long* count = nullptr;
+  long long count_inc = 0;
 };
 
 __device__ __forceinline__ void finish_stats(long long c, double mean, double var, double M, float eps,
@@ -109,6 +113,7 @@ __device__ __forceinline__ void finish_stats(long long c, double mean, double va
                                              float* invstd_out) {
   mean_out[c] = float(mean);
   invstd_out[c] = float(1.0 / sqrt(var + double(eps)));
+  if (c == 0 && ch.count) *ch.count += ch.count_inc;  // one thread finishes channel 0
   if (ch.rm && ch.rv) {
     const double unbiased = M > 1.0 ? var * M / (M - 1.0) : var;
     const double f = double(momentum);
@@ -1524,6 +1529,23 @@ b2_status b2_batch_norm_stats_bf16(const void* x, int layout, int pdtype, void* 
   if (HW == 0) return set_error(B2_ERR_INVALID, "%s: empty planes", who);
   if (!x || !save_mean || !save_invstd || (!rm) != (!rv)) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
   const BnChan ch{nullptr, nullptr, pdtype, rm, rv, rdtype};
+  return bn_stats(static_cast<const uint16_t*>(x), layout, ch, save_mean, save_invstd, N, C, HW, eps, momentum,
+                  workspace, static_cast<cudaStream_t>(stream), who);
+}
+
+b2_status b2_batch_norm_stats_count_bf16(const void* x, int layout, int pdtype, void* rm, void* rv, int rdtype,
+                                         float* save_mean, float* save_invstd, int64_t N, int64_t C, int64_t HW,
+                                         float momentum, float eps, int64_t* count, int64_t count_inc,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  const char* who = "b2_batch_norm_stats_count_bf16";
+  B2_TRY(check_common(N, C, HW, layout, workspace, workspace_bytes, who));
+  if (!valid_pdtype(pdtype) || !valid_pdtype(rdtype)) return set_error(B2_ERR_UNSUPPORTED, "%s: parameter dtype", who);
+  if (!count || (reinterpret_cast<uintptr_t>(count) & 7)) return set_error(B2_ERR_INVALID, "%s: counter", who);
+  if (N * C == 0 || HW == 0) return set_error(B2_ERR_INVALID, "%s: empty input (nothing would advance the counter)", who);
+  if (!x || !save_mean || !save_invstd || (!rm) != (!rv)) return set_error(B2_ERR_INVALID, "%s: null pointer", who);
+  BnChan ch{nullptr, nullptr, pdtype, rm, rv, rdtype};
+  ch.count = reinterpret_cast<long long*>(count);
+  ch.count_inc = count_inc;
   return bn_stats(static_cast<const uint16_t*>(x), layout, ch, save_mean, save_invstd, N, C, HW, eps, momentum,
                   workspace, static_cast<cudaStream_t>(stream), who);
 }

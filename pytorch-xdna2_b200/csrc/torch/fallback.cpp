@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <mutex>
 #include <unordered_map>
 
 #include "xdna.h"
@@ -202,8 +203,72 @@ void relu_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
   cuda_alias_fallback(op, stack);
 }
 
+std::mutex g_count_mu;
+PendingCount g_count;  // at most one: a new increment runs the previous first
+
+bool host_integer(const at::Tensor& t) {
+  return t.defined() && t.device().is_cpu() && t.dim() == 0 && at::isIntegralType(t.scalar_type(), false);
+}
+
+}  // namespace
+
+PendingCount take_pending_count(c10::DeviceIndex dev) {
+  PendingCount pc;
+  {
+    std::lock_guard<std::mutex> lk(g_count_mu);
+    if (!g_count.counter.defined() || g_count.counter.device().index() != dev) return {};
+    pc = std::move(g_count);
+    g_count = PendingCount{};
+  }
+  if (!has_pending(pc.counter)) return {};  // read (and so run) since
+  drop_pending(pc.counter);
+  return pc;
+}
+
+void flush_pending_count() {
+  at::Tensor t;
+  {
+    std::lock_guard<std::mutex> lk(g_count_mu);
+    t = std::move(g_count.counter);
+    g_count = PendingCount{};
+  }
+  if (t.defined()) materialize(t);
+}
+
+namespace {
+
 void add_inplace(const c10::OperatorHandle& op, torch::jit::Stack* stack) {
   auto args = stack->end() - 3;  // self, other, alpha
+  // a module's step counter: counter.add_(k), an xdna int64 scalar and a host
+  // integer -- left pending for the next training BatchNorm forward to
+  // advance inside its statistics launch (no kernel of its own)
+  if (g_bn_epilogue.load() && g_mode.load() > 1 && args[0].isTensor() && args[1].isTensor() &&
+      args[2].isScalar() && args[2].toScalar().isIntegral(false)) {
+    const at::Tensor self = args[0].toTensor();
+    const at::Tensor other = args[1].toTensor();
+    if (self.device().type() == kXdna && self.scalar_type() == at::kLong && self.numel() == 1 && self.dim() <= 1 &&
+        self.storage().nbytes() == sizeof(int64_t) && !self.requires_grad() && host_integer(other) &&
+        (reinterpret_cast<uintptr_t>(self.data_ptr()) & 7) == 0) {
+      const int64_t inc = other.item<int64_t>() * args[2].toScalar().toLong();
+      flush_pending_count();
+      materialize(self);
+      const auto dev = self.device().index();
+      defer_write(self,
+                  [ptr = self.data_ptr(), dev, inc]() {
+                    c10::cuda::CUDAGuard guard(dev);
+                    count_fallback("aten::add_.Tensor");
+                    at::from_blob(ptr, {1}, at::TensorOptions().dtype(at::kLong).device(at::kCUDA, dev)).add_(inc);
+                  },
+                  /*kick=*/false);
+      {
+        std::lock_guard<std::mutex> lk(g_count_mu);
+        g_count = PendingCount{self, inc};
+      }
+      torch::jit::drop(*stack, 3);
+      stack->push_back(self);
+      return;
+    }
+  }
   if (g_bn_epilogue.load() && args[0].isTensor() && args[1].isTensor()) {
     const at::Tensor self = args[0].toTensor();
     const at::Tensor other = args[1].toTensor();

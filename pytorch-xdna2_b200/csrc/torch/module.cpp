@@ -364,7 +364,15 @@ PYBIND11_MODULE(_C, m) {
   m.def("graph_capture_begin", [](int device, uintptr_t stream, int share_pool) {
     return graph_capture_begin(device, reinterpret_cast<cudaStream_t>(stream), share_pool);
   });
-  m.def("graph_capture_end", [](uintptr_t stream) { graph_capture_end(reinterpret_cast<cudaStream_t>(stream)); });
+  m.def("graph_capture_end", [](uintptr_t stream) {
+    // a step counter still pending advances inside the capture, so that each
+    // replay advances it; after a failed capture there is nothing to keep
+    try {
+      flush_pending_count();
+    } catch (const std::exception&) {
+    }
+    graph_capture_end(reinterpret_cast<cudaStream_t>(stream));
+  });
   m.def("graph_pool_release", [](int pool) { graph_pool_release(pool); });
   m.def("set_bn_epilogue", [](bool on) { return g_bn_epilogue.exchange(on); });
   m.def("bn_epilogue", [] { return g_bn_epilogue.load(); });

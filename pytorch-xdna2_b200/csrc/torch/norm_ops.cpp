@@ -92,11 +92,21 @@ std::tuple<at::Tensor, at::Tensor, at::Tensor> native_batch_norm(
     // statistics now; the output pass waits for the first reader of `out`,
     // so that a residual add_ and a relu_ on `out` fold into it
     {
+      // the module's num_batches_tracked.add_(1) just before this forward,
+      // if still pending, advances inside the statistics launch
+      const PendingCount pc = take_pending_count(dev);
       KernelTimer kt("bn.stats", 2.0 * double(input.numel()), stream(dev));  // work: algorithmic bytes
-      XDNA_B2(b2_batch_norm_stats_bf16(input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
-                                       const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(),
-                                       save_invstd.data_ptr<float>(), N, C, HW, float(momentum), float(eps),
-                                       ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+      if (pc.counter.defined())
+        XDNA_B2(b2_batch_norm_stats_count_bf16(
+            input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
+            const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(), save_invstd.data_ptr<float>(),
+            N, C, HW, float(momentum), float(eps), static_cast<int64_t*>(pc.counter.data_ptr()), pc.inc,
+            ws.data_ptr(), size_t(ws.numel()), stream(dev)));
+      else
+        XDNA_B2(b2_batch_norm_stats_bf16(input.data_ptr(), layout, pdt, const_cast<void*>(ptr_of(running_mean)),
+                                         const_cast<void*>(ptr_of(running_var)), rdm, save_mean.data_ptr<float>(),
+                                         save_invstd.data_ptr<float>(), N, C, HW, float(momentum), float(eps),
+                                         ws.data_ptr(), size_t(ws.numel()), stream(dev)));
     }
     count_launch("batch_norm.fwd", 2);
     auto spec = std::make_shared<EpiSpec>();

@@ -187,6 +187,20 @@ class KernelTimer {
   cudaEvent_t start_ = nullptr;
 };
 void count_fallback(const std::string& op);
+
+// ---- a module's step counter left pending (fallback.cpp) -------------------
+// `counter.add_(k)` on an xdna int64 scalar with a host integer k (a training
+// BatchNorm's num_batches_tracked.add_(1)) is deferred like any write: a reader
+// runs it first.  The next training BatchNorm forward on that device takes it
+// (take_pending_count: the job dropped, the counter and k handed over) and
+// advances the counter inside its statistics launch.  flush_pending_count
+// runs a pending one now (the end of a graph capture).
+struct PendingCount {
+  at::Tensor counter;
+  int64_t inc = 0;
+};
+PendingCount take_pending_count(c10::DeviceIndex dev);
+void flush_pending_count();
 std::map<std::string, int64_t> launch_stats();
 std::map<std::string, int64_t> fallback_stats();
 void reset_stats();

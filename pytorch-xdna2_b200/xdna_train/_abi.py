@@ -91,6 +91,8 @@ SIGNATURES = {
     "b2_pack_weight_khwc_bf16": [vp, i64, i64, i32, i32, i64, vp, vp],
     "b2_unpack_weight_khwc": [vp, i64, i64, i32, i32, i64, vp, i32, vp],
     "b2_batch_norm_stats_bf16": [vp, i32, i32, vp, vp, i32, vp, vp, i64, i64, i64, f32, f32, vp, sz, vp],
+    "b2_batch_norm_stats_count_bf16": [vp, i32, i32, vp, vp, i32, vp, vp, i64, i64, i64, f32, f32, vp, i64, vp, sz,
+                                       vp],
     "b2_batch_norm_apply_bf16": [vp, i32, vp, vp, i32, vp, vp, vp, i32, vp, i64, i64, i64, vp],
     "b2_direct_conv_weight_floats": [i64, i64, i32, i32, i32],
     "b2_direct_conv_weight": [vp, i64, i64, i32, i32, i32, vp, vp],

@@ -250,10 +250,11 @@ def test_residual_add_and_relu_fold_into_batch_norm(cl):
         xdna_train.set_fusion(bn_epilogue=True)
     assert folded >= 2
     calls = lambda d, k: d.get(k, {}).get("calls", 0)  # noqa: E731
-    # unfused: the residual add and the ReLU ran as ATen passes (BatchNorm's
-    # num_batches_tracked += 1 is an add_ in both runs)
+    # unfused: the residual add and the ReLU ran as ATen passes, and so did
+    # BatchNorm's num_batches_tracked += 1, which the fused run advances
+    # inside its statistics launch
     assert calls(fb, "aten::relu_") == 0 and calls(fp, "aten::relu_") == 1
-    assert calls(fp, "aten::add_.Tensor") == calls(fb, "aten::add_.Tensor") + 1
+    assert calls(fb, "aten::add_.Tensor") == 0 and calls(fp, "aten::add_.Tensor") == 2
     for k in fused:
         # the same roundings in the same order: bit-identical (zeros compared by value)
         assert torch.equal(fused[k].float(), plain[k].float()), k
@@ -532,3 +533,75 @@ def test_batch_norm_bwd_relu_sum_abi_bit_exact(cuda, shape, pdtype):
     for p_, f_ in zip(outs["plain"], outs["fused"]):
         iv = torch.int16 if p_.dtype == torch.bfloat16 else torch.int32
         assert torch.equal(p_.contiguous().view(iv).cpu(), f_.contiguous().view(iv).cpu())
+
+
+# ---- the step counter advanced inside the statistics launch ------------------
+
+@pytest.mark.parametrize("shape,layout", [((8, 64, 14, 14), 1), ((4, 24, 5, 7), 0), ((2, 2048, 3, 3), 1)])
+def test_batch_norm_stats_count_abi(cuda, shape, layout):
+    """b2_batch_norm_stats_count_bf16: the statistics and running statistics
+    of b2_batch_norm_stats_bf16 bit for bit, and the counter advanced by the
+    increment once per call (two calls in a row)."""
+    N, C, H, W = shape
+    rng = np.random.default_rng(C + H)
+    x = torch.from_numpy(rng.standard_normal(shape).astype(np.float32) * 2 + 0.5).bfloat16().to(cuda)
+    if layout == 1:
+        x = x.contiguous(memory_format=torch.channels_last)
+    nws = _abi.lib().b2_batch_norm_workspace_bytes(N, C, H * W, layout)
+    ws = torch.empty(max(nws, 16), dtype=torch.uint8, device=cuda)
+    outs = []
+    count = torch.tensor([41], dtype=torch.int64, device=cuda)
+    for fn in ("b2_batch_norm_stats_bf16", "b2_batch_norm_stats_count_bf16"):
+        rm = torch.full((C,), 0.25, dtype=torch.float32, device=cuda)
+        rv = torch.full((C,), 2.0, dtype=torch.float32, device=cuda)
+        sm, si = torch.empty_like(rm), torch.empty_like(rm)
+        for _ in range(2):
+            extra = (count.data_ptr(), 3) if fn.endswith("count_bf16") else ()
+            _abi.call(fn, x.data_ptr(), layout, 1, rm.data_ptr(), rv.data_ptr(), 1, sm.data_ptr(), si.data_ptr(), N, C,
+                      H * W, ctypes.c_float(0.1), ctypes.c_float(1e-5), *extra, ws.data_ptr(), nws, st())
+        torch.cuda.synchronize()
+        outs.append([t.cpu() for t in (sm, si, rm, rv)])
+    for a, b in zip(*outs):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    assert int(count.item()) == 41 + 2 * 3
+    L = _abi.lib()
+    status = L.b2_batch_norm_stats_count_bf16(x.data_ptr(), layout, 1, None, None, 1, sm.data_ptr(), si.data_ptr(),
+                                              N, C, H * W, ctypes.c_float(0.1), ctypes.c_float(1e-5), None, 1,
+                                              ws.data_ptr(), nws, st())
+    assert status != 0 and b"counter" in L.b2_last_error()
+
+
+def test_num_batches_tracked_advances_inside_the_statistics_launch():
+    """A training BatchNorm2d's num_batches_tracked.add_(1) takes no kernel of
+    its own: the forward's statistics launch advances it (no add_ fallback);
+    the count reads right after every step, after a read taken between the
+    add_ and the forward (which runs the add first), and with momentum=None,
+    whose forward reads the count itself."""
+    torch.manual_seed(0)
+    for momentum in (0.1, None):
+        bn = nn.BatchNorm2d(32, momentum=momentum).bfloat16().to(X)
+        ref = nn.BatchNorm2d(32, momentum=momentum).bfloat16()
+        ref.load_state_dict({k: v.cpu() for k, v in bn.state_dict().items()})
+        g = torch.Generator().manual_seed(3)
+        xdna_train.reset_fallback_stats()
+        for step in range(4):
+            x = torch.randn(4, 32, 6, 6, generator=g).bfloat16()
+            y = bn(x.to(X).contiguous(memory_format=torch.channels_last))
+            ref(x)
+            if momentum is not None and step < 3:
+                assert "aten::add_.Tensor" not in xdna_train.fallback_stats(), xdna_train.fallback_stats()
+            assert int(bn.num_batches_tracked.item()) == step + 1
+            y.float().sum().item()
+        torch.testing.assert_close(bn.running_mean.cpu(), ref.running_mean, rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(bn.running_var.cpu(), ref.running_var, rtol=2e-2, atol=2e-2)
+    # a read between the increment and the forward runs the pending add
+    bn = nn.BatchNorm2d(16).bfloat16().to(X)
+    bn.num_batches_tracked.add_(5)
+    assert int(bn.num_batches_tracked.item()) == 5
+    bn(torch.randn(2, 16, 4, 4).bfloat16().to(X).contiguous(memory_format=torch.channels_last))
+    assert int(bn.num_batches_tracked.item()) == 6
+    # two increments with no forward between: both land
+    bn.num_batches_tracked.add_(1)
+    bn.num_batches_tracked.add_(2)
+    bn(torch.randn(2, 16, 4, 4).bfloat16().to(X).contiguous(memory_format=torch.channels_last))
+    assert int(bn.num_batches_tracked.item()) == 10
