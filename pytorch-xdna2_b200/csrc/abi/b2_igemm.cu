@@ -1610,8 +1610,18 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ partial, void* dw,
       co = int(oc / Cin);
     }
     const float* src = partial + ((long long)tap * Cout + co) * Cin + ci;
+    // eight splits' loads issued together, then added in split order (the
+    // same sums as one load per add, without a load latency per split)
     float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += src[k * plane];
+    for (int k0 = 0; k0 < splits; k0 += 8) {
+      const int nk = splits - k0 < 8 ? splits - k0 : 8;
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = k < nk ? __ldg(src + (long long)(k0 + k) * plane) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k < nk) s += v[k];
+    }
     if (dtype == B2_F32)
       static_cast<float*>(dw)[i] = s;
     else
